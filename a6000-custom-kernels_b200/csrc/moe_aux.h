@@ -1,0 +1,25 @@
+// moe_aux.h -- launchers of the small kernels around the GEMV (moe_aux.cu)
+// and of the GEMV itself (moe_gemv.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace moe {
+
+struct GemvArgs;
+
+cudaError_t launch_quantize_act(int act_type, const float *x, void *y, int64_t n_rows, int64_t n_cols,
+                                cudaStream_t st);
+cudaError_t launch_topk_softmax(const float *logits, int64_t n_tok, int64_t n_experts, int64_t k, int norm_w,
+                                int32_t *ids, float *weights, cudaStream_t st);
+cudaError_t launch_combine(const float *y, const float *w, const float *ys, float *out, int64_t n_tok, int64_t H,
+                           int64_t k, cudaStream_t st);
+cudaError_t launch_fill_quantized(int type, void *dst, int64_t n_rows, int64_t n_cols, uint64_t seed, float sigma,
+                                  cudaStream_t st);
+
+// Plans the launch geometry into `a` and launches the GEMV for weight type
+// `type` with activation semantics `act`. Returns 0, or a negative MOE_ERR_*
+// with *why set, or MOE_ERR_CUDA with *cuda_err set.
+int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
+
+}  // namespace moe

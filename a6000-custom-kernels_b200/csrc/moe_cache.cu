@@ -1,0 +1,840 @@
+// moe_cache.cu -- host side of the hot-expert cache and the C ABI.
+//
+// Restates the reference's host code (kernels/moe-cache.cu of
+// Zapdev-labs/a6000-custom-kernels) for B200:
+//   registry / slot sizing / seeding  -> moe_get_or_create      (:525-622)
+//   promotion + LRU eviction          -> ggml_cuda_moe_cache_step, moe_acquire_slot (:628-775)
+//   eligibility / env / pinning       -> :345-469
+// Differences, each deliberate:
+//   * every entry point returns a status instead of aborting;
+//   * one step's misses are processed in sorted (tensor << 12 | expert) order,
+//     so the cache state does not depend on the GPU's block scheduling (the
+//     reference uses atomicAdd arrival order, :168-172);
+//   * HBM-resident expert tensors are claimed too: their table points straight
+//     at the weights (no pool), so the step has nothing to do for them and
+//     returns without a device sync when no tensor is host-tiered;
+//   * a gate tensor without a table is read at its expert's offset (the
+//     reference reads expert 0 there, :200).
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "moe_aux.h"
+#include "moe_cache_b200.h"
+#include "moe_gemv.cuh"
+
+namespace {
+
+constexpr int kMaxPromotions = 48;             // reference :37
+constexpr uint32_t kLogCap = 16382;            // miss-log entries (reference: 8190)
+constexpr int kStatsWords = 2 + static_cast<int>(kLogCap);
+constexpr size_t kAdmissionGc = 8192;          // reference :766
+constexpr size_t kVramMargin = 2ull << 30;     // reference :553
+
+struct Entry {
+    int32_t id = -1;
+    int type = 0;
+    const char *data = nullptr;
+    size_t expert_bytes = 0;
+    int n_experts = 0;
+    int n_slots = 0;
+    bool host = false;            // tiered (pinned host) vs HBM-resident
+    std::string name;
+    char *pool = nullptr;
+    char **d_tbl = nullptr;
+    std::vector<char *> h_tbl;
+    uint32_t *d_stamps = nullptr;
+    std::vector<int32_t> slot_of, expert_of;
+    std::vector<uint32_t> h_stamps;
+    uint32_t stamps_clock = 0xFFFFFFFFu;
+    bool tbl_dirty = false;
+};
+
+struct State {
+    bool enabled = false, env_read = false, configured = false;
+    int slots = 320;
+    size_t budget = 30ull << 30;
+    size_t used = 0;
+    bool claim_device = true;
+    bool debug = false;
+    std::string seed_path;
+    std::unordered_map<const char *, Entry *> by_data;
+    std::vector<Entry *> all;
+    uint32_t *d_stats = nullptr, *h_stats = nullptr, *d_clock = nullptr;
+    int *d_err = nullptr;
+    uint32_t h_clock = 0;
+    int device = -1;
+    std::unordered_map<uint32_t, int> admission;
+    std::unordered_map<std::string, std::vector<int>> seed;
+    bool seed_loaded = false;
+    std::unordered_map<const void *, int> ptr_kind;   // 1 host, 2 device, 0 other
+    uint64_t steps = 0, hits = 0, misses = 0, promotions = 0, evictions = 0, overflow = 0;
+};
+
+State g;
+std::recursive_mutex g_mu;
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) return fail(MOE_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+int type_size(int t) {
+    switch (t) {
+        case MOE_TYPE_Q4_0: return 18;
+        case MOE_TYPE_Q5_0: return 22;
+        case MOE_TYPE_Q8_0: return 34;
+        case MOE_TYPE_Q2_K: return 84;
+        case MOE_TYPE_Q3_K: return 110;
+        case MOE_TYPE_Q4_K: return 144;
+        case MOE_TYPE_Q5_K: return 176;
+        case MOE_TYPE_Q6_K: return 210;
+        default: return 0;
+    }
+}
+int blck_size(int t) { return (t >= MOE_TYPE_Q2_K && t <= MOE_TYPE_Q6_K) ? 256 : 32; }
+
+// reference moe_type_supported (:407-421)
+bool type_supported(int t) { return type_size(t) != 0; }
+
+int env_int(const char *n, int fb) { const char *s = getenv(n); return s ? atoi(s) : fb; }
+double env_double(const char *n, double fb) { const char *s = getenv(n); return s ? atof(s) : fb; }
+
+// reference ggml_cuda_moe_cache_enabled (:345-363)
+void read_env() {
+    if (g.env_read) return;
+    const char *env = getenv("GGML_CUDA_MOE_CACHE");
+    g.enabled = env && env[0] && env[0] != '0';
+    g.slots = env_int("GGML_CUDA_MOE_CACHE_SLOTS", g.slots);
+    if (g.slots < 0) g.slots = 0;
+    const double gb = env_double("GGML_CUDA_MOE_CACHE_BUDGET_GB", 0.0);
+    if (gb > 0) g.budget = static_cast<size_t>(gb * 1024.0 * 1024.0 * 1024.0);
+    const char *seed = getenv("GGML_CUDA_MOE_CACHE_SEED");
+    g.seed_path = seed ? seed : "";
+    g.claim_device = env_int("GGML_CUDA_MOE_CACHE_DEVICE", 1) != 0;
+    g.debug = getenv("GGML_CUDA_MOE_CACHE_DEBUG") != nullptr;
+    g.env_read = true;
+    if (g.enabled && g.debug)
+        fprintf(stderr, "moe-cache: enabled, slots=%d budget=%.1f GB\n", g.slots,
+                static_cast<double>(g.budget) / (1024.0 * 1024.0 * 1024.0));
+}
+
+// 1 = pinned host, 2 = device memory of the current device, 0 = neither
+int ptr_kind(const void *p) {
+    auto it = g.ptr_kind.find(p);
+    if (it != g.ptr_kind.end()) return it->second;
+    cudaPointerAttributes attrs;
+    int kind = 0;
+    if (cudaPointerGetAttributes(&attrs, p) == cudaSuccess) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (attrs.type == cudaMemoryTypeHost) kind = 1;
+        else if (attrs.type == cudaMemoryTypeDevice && attrs.device == dev) kind = 2;
+    } else {
+        cudaGetLastError();
+    }
+    g.ptr_kind[p] = kind;
+    return kind;
+}
+
+bool contiguous(const moe_tensor *t) {
+    const uint64_t ts = static_cast<uint64_t>(type_size(t->type));
+    const int64_t bs = blck_size(t->type);
+    if (t->ne[0] % bs) return false;
+    return t->nb[0] == ts && t->nb[1] == ts * static_cast<uint64_t>(t->ne[0] / bs) &&
+           t->nb[2] == t->nb[1] * static_cast<uint64_t>(t->ne[1]) && t->nb[3] == t->nb[2] * static_cast<uint64_t>(t->ne[2]);
+}
+
+// reference ggml_cuda_moe_cache_wants (:442-469), widened to HBM-resident tensors
+int wants_locked(const moe_tensor *src0) {
+    read_env();
+    if (!g.enabled || !src0 || !src0->data) return 0;
+    if (src0->flags & MOE_TENSOR_NO_BUFFER) return 0;
+    const int kind = ptr_kind(src0->data);
+    if (kind == 0 || (kind == 2 && !g.claim_device)) return 0;
+    if (!type_supported(src0->type)) return 0;
+    if (src0->ne[2] < 2 || src0->ne[3] != 1 || (src0->flags & MOE_TENSOR_VIEW)) return 0;
+    if (!contiguous(src0)) return 0;
+    return 1;
+}
+
+int init_device_globals() {
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (g.d_stats) {
+        if (dev != g.device) return fail(MOE_ERR_STATE, "moe-cache state belongs to device %d, called on %d", g.device, dev);
+        return MOE_OK;
+    }
+    CK(cudaMalloc(&g.d_stats, sizeof(uint32_t) * kStatsWords));
+    CK(cudaMallocHost(&g.h_stats, sizeof(uint32_t) * kStatsWords));
+    CK(cudaMemset(g.d_stats, 0, sizeof(uint32_t) * kStatsWords));
+    CK(cudaMalloc(&g.d_clock, sizeof(uint32_t)));
+    CK(cudaMemset(g.d_clock, 0, sizeof(uint32_t)));
+    CK(cudaMalloc(&g.d_err, sizeof(int)));
+    CK(cudaMemset(g.d_err, 0, sizeof(int)));
+    g.h_clock = 0;
+    g.device = dev;
+    return MOE_OK;
+}
+
+// reference moe_load_seed (:487-523): lines of "tensorname id1,id2,..."
+void load_seed() {
+    if (g.seed_loaded) return;
+    g.seed_loaded = true;
+    if (g.seed_path.empty()) return;
+    FILE *f = fopen(g.seed_path.c_str(), "r");
+    if (!f) {
+        fprintf(stderr, "moe-cache: seed file %s not found, starting cold\n", g.seed_path.c_str());
+        return;
+    }
+    std::vector<char> line(1 << 16);
+    while (fgets(line.data(), static_cast<int>(line.size()), f)) {
+        char *sp = strchr(line.data(), ' ');
+        if (!sp) continue;
+        *sp = 0;
+        std::vector<int> ids;
+        char *p = sp + 1;
+        while (*p) {
+            char *end = nullptr;
+            const long v = strtol(p, &end, 10);
+            if (end == p) break;
+            ids.push_back(static_cast<int>(v));
+            p = (*end == ',') ? end + 1 : end;
+        }
+        g.seed[line.data()] = std::move(ids);
+    }
+    fclose(f);
+    if (g.debug) fprintf(stderr, "moe-cache: loaded seed for %zu tensors from %s\n", g.seed.size(), g.seed_path.c_str());
+}
+
+char *host_tag(const char *p) { return reinterpret_cast<char *>(reinterpret_cast<uintptr_t>(p) | 1u); }
+
+// reference moe_get_or_create (:525-622)
+int get_or_create(const moe_tensor *src0, cudaStream_t stream, Entry **out) {
+    int rc = init_device_globals();
+    if (rc) return rc;
+    auto it = g.by_data.find(static_cast<const char *>(src0->data));
+    if (it != g.by_data.end()) { *out = it->second; return MOE_OK; }
+
+    Entry *e = new Entry();
+    e->id = static_cast<int32_t>(g.all.size());
+    e->type = src0->type;
+    e->data = static_cast<const char *>(src0->data);
+    e->expert_bytes = src0->nb[2];
+    e->n_experts = static_cast<int>(src0->ne[2]);
+    e->host = ptr_kind(src0->data) == 1;
+    e->name = src0->name ? src0->name : "";
+    if (e->n_experts > 4096) { delete e; return fail(MOE_ERR_UNSUPPORTED, "more than 4096 experts"); }
+
+    int slots = 0;
+    size_t free_vram = 0, total_vram = 0;
+    if (e->host) {
+        slots = g.slots;
+        const size_t free_budget = g.budget > g.used ? g.budget - g.used : 0;
+        if (static_cast<size_t>(slots) * e->expert_bytes > free_budget) slots = static_cast<int>(free_budget / e->expert_bytes);
+        if (cudaMemGetInfo(&free_vram, &total_vram) != cudaSuccess) { delete e; return fail(MOE_ERR_CUDA, "cudaMemGetInfo failed"); }
+        const size_t usable = free_vram > kVramMargin ? free_vram - kVramMargin : 0;
+        if (static_cast<size_t>(slots) * e->expert_bytes > usable) slots = static_cast<int>(usable / e->expert_bytes);
+        if (slots > e->n_experts) slots = e->n_experts;
+    }
+    e->n_slots = slots;
+    e->h_tbl.resize(e->n_experts);
+    for (int i = 0; i < e->n_experts; ++i) {
+        const char *p = e->data + static_cast<size_t>(i) * e->expert_bytes;
+        e->h_tbl[i] = e->host ? host_tag(p) : const_cast<char *>(p);
+    }
+    if (cudaMalloc(&e->d_tbl, sizeof(char *) * e->n_experts) != cudaSuccess ||
+        cudaMalloc(&e->d_stamps, sizeof(uint32_t) * e->n_experts) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(e->d_tbl);
+        delete e;
+        return fail(MOE_ERR_OOM, "table allocation failed");
+    }
+    CK(cudaMemsetAsync(e->d_stamps, 0, sizeof(uint32_t) * e->n_experts, stream));
+    e->h_stamps.assign(e->n_experts, 0);
+    e->slot_of.assign(e->n_experts, -1);
+    e->expert_of.assign(slots, -1);
+    if (slots > 0) {
+        if (cudaMalloc(&e->pool, static_cast<size_t>(slots) * e->expert_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(e->d_tbl);
+            cudaFree(e->d_stamps);
+            delete e;
+            return fail(MOE_ERR_OOM, "pool allocation failed");
+        }
+        g.used += static_cast<size_t>(slots) * e->expert_bytes;
+    }
+    g.by_data[e->data] = e;
+    g.all.push_back(e);
+
+    // seeding: all slots free, seeded experts take slots 0..seeded-1 (:584-609)
+    load_seed();
+    auto sit = g.seed.find(e->name);
+    if (sit != g.seed.end() && e->n_slots > 0) {
+        int seeded = 0;
+        for (const int expert : sit->second) {
+            if (seeded >= e->n_slots) break;
+            if (expert < 0 || expert >= e->n_experts || e->slot_of[expert] >= 0) continue;
+            const int slot = seeded;
+            CK(cudaMemcpyAsync(e->pool + static_cast<size_t>(slot) * e->expert_bytes,
+                               e->data + static_cast<size_t>(expert) * e->expert_bytes, e->expert_bytes,
+                               cudaMemcpyHostToDevice, stream));
+            e->h_tbl[expert] = e->pool + static_cast<size_t>(slot) * e->expert_bytes;
+            e->slot_of[expert] = slot;
+            e->expert_of[slot] = expert;
+            seeded++;
+        }
+        if (seeded > 0 && g.debug) fprintf(stderr, "moe-cache: seeded %d/%d experts for %s\n", seeded, e->n_slots, e->name.c_str());
+    }
+    // one table upload, ordered after the seed copies on the same stream (:611-613)
+    CK(cudaMemcpyAsync(e->d_tbl, e->h_tbl.data(), sizeof(char *) * e->n_experts, cudaMemcpyHostToDevice, stream));
+    if (g.debug)
+        fprintf(stderr, "moe-cache: registered %s type=%d experts=%d slot_bytes=%zu slots=%d %s\n", e->name.c_str(),
+                e->type, e->n_experts, e->expert_bytes, e->n_slots, e->host ? "(host-tiered)" : "(HBM-resident)");
+    *out = e;
+    return MOE_OK;
+}
+
+// reference moe_acquire_slot (:628-667)
+int acquire_slot(Entry *e, cudaStream_t stream, int *slot_out) {
+    *slot_out = -1;
+    if (e->n_slots == 0) return MOE_OK;
+    for (int s = 0; s < e->n_slots; ++s)
+        if (e->expert_of[s] < 0) { *slot_out = s; return MOE_OK; }
+    if (e->stamps_clock != g.h_clock) {
+        CK(cudaMemcpyAsync(e->h_stamps.data(), e->d_stamps, sizeof(uint32_t) * e->n_experts, cudaMemcpyDeviceToHost, stream));
+        CK(cudaStreamSynchronize(stream));
+        e->stamps_clock = g.h_clock;
+    }
+    int victim_slot = -1;
+    uint32_t best = UINT32_MAX;
+    for (int s = 0; s < e->n_slots; ++s) {
+        const int expert = e->expert_of[s];
+        const uint32_t stamp = expert >= 0 ? e->h_stamps[expert] : 0;
+        if (stamp < best) { best = stamp; victim_slot = s; }
+    }
+    if (victim_slot < 0) return MOE_OK;
+    const int victim = e->expert_of[victim_slot];
+    if (victim >= 0) {
+        e->slot_of[victim] = -1;
+        e->h_tbl[victim] = host_tag(e->data + static_cast<size_t>(victim) * e->expert_bytes);
+        e->tbl_dirty = true;
+        g.evictions++;
+    }
+    e->expert_of[victim_slot] = -1;
+    *slot_out = victim_slot;
+    return MOE_OK;
+}
+
+// reference ggml_cuda_moe_cache_step (:669-775)
+int step_locked(cudaStream_t stream) {
+    if (!g.enabled || g.all.empty()) return MOE_OK;
+    bool any_host = false;
+    for (const Entry *e : g.all) any_host |= e->host;
+    if (!any_host) { g.steps++; return MOE_OK; }
+
+    CK(cudaMemcpyAsync(g.h_stats, g.d_stats, sizeof(uint32_t) * kStatsWords, cudaMemcpyDeviceToHost, stream));
+    CK(cudaStreamSynchronize(stream));
+    uint32_t n = g.h_stats[0];
+    if (n > kLogCap) { g.overflow += n - kLogCap; n = kLogCap; }
+    const uint32_t step_hits = g.h_stats[1];
+
+    g.h_clock += 1;
+    CK(cudaMemcpyAsync(g.d_clock, &g.h_clock, sizeof(uint32_t), cudaMemcpyHostToDevice, stream));
+    CK(cudaMemsetAsync(g.d_stats, 0, 2 * sizeof(uint32_t), stream));
+    g.steps++;
+    g.hits += step_hits;
+    g.misses += g.h_stats[0];
+    if (g.debug && g.steps % 64 == 0) {
+        size_t resident = 0;
+        for (const Entry *e : g.all)
+            for (int s = 0; s < e->n_slots; ++s) resident += e->expert_of[s] >= 0;
+        fprintf(stderr, "moe-cache: step %llu: hits=%u misses=%u (totals: hits %llu, misses %llu, promos %llu), resident %zu\n",
+                static_cast<unsigned long long>(g.steps), step_hits, n, static_cast<unsigned long long>(g.hits),
+                static_cast<unsigned long long>(g.misses), static_cast<unsigned long long>(g.promotions), resident);
+    }
+    if (n == 0) return MOE_OK;
+
+    // order-independent processing: sort this step's log
+    uint32_t *log = g.h_stats + moe::GEMV_LOG_BASE;
+    std::sort(log, log + n);
+    int promoted = 0;
+    for (uint32_t i = 0; i < n && promoted < kMaxPromotions; ++i) {
+        const uint32_t packed = log[i];
+        const int32_t cid = static_cast<int32_t>(packed >> 12);
+        const int32_t expert = static_cast<int32_t>(packed & 0xFFF);
+        int &count = g.admission[packed];
+        count += 1;
+        if (count < 2) continue;
+        count = 0;
+        if (cid < 0 || cid >= static_cast<int>(g.all.size())) continue;
+        Entry *e = g.all[cid];
+        if (expert < 0 || expert >= e->n_experts || e->slot_of[expert] >= 0) continue;
+        int slot = -1;
+        const int rc = acquire_slot(e, stream, &slot);
+        if (rc) return rc;
+        if (slot < 0) continue;
+        CK(cudaMemcpyAsync(e->pool + static_cast<size_t>(slot) * e->expert_bytes,
+                           e->data + static_cast<size_t>(expert) * e->expert_bytes, e->expert_bytes,
+                           cudaMemcpyHostToDevice, stream));
+        e->h_tbl[expert] = e->pool + static_cast<size_t>(slot) * e->expert_bytes;
+        e->tbl_dirty = true;
+        e->slot_of[expert] = slot;
+        e->expert_of[slot] = expert;
+        promoted++;
+        g.promotions++;
+    }
+    for (Entry *e : g.all) {
+        if (!e->tbl_dirty) continue;
+        CK(cudaMemcpyAsync(e->d_tbl, e->h_tbl.data(), sizeof(char *) * e->n_experts, cudaMemcpyHostToDevice, stream));
+        e->tbl_dirty = false;
+    }
+    if (g.admission.size() > kAdmissionGc) {
+        for (auto it = g.admission.begin(); it != g.admission.end();) {
+            if (it->second == 0) it = g.admission.erase(it);
+            else ++it;
+        }
+    }
+    return MOE_OK;
+}
+
+void free_all() {
+    for (Entry *e : g.all) {
+        cudaFree(e->pool);
+        cudaFree(e->d_tbl);
+        cudaFree(e->d_stamps);
+        delete e;
+    }
+    g.all.clear();
+    g.by_data.clear();
+    if (g.d_stats) cudaFree(g.d_stats);
+    if (g.h_stats) cudaFreeHost(g.h_stats);
+    if (g.d_clock) cudaFree(g.d_clock);
+    if (g.d_err) cudaFree(g.d_err);
+    g.d_stats = g.h_stats = g.d_clock = nullptr;
+    g.d_err = nullptr;
+    g.h_clock = 0;
+    g.used = 0;
+    g.device = -1;
+    g.admission.clear();
+    g.seed.clear();
+    g.seed_loaded = false;
+    g.ptr_kind.clear();
+    g.steps = g.hits = g.misses = g.promotions = g.evictions = g.overflow = 0;
+}
+
+// common GEMV argument setup for the boundary call and the layer path
+struct MmvqCall {
+    const moe_tensor *src0 = nullptr;
+    const moe_tensor *gate = nullptr;            // fusion host gate tensor
+    const moe_fusion_device *fd = nullptr;
+    const void *src1 = nullptr;
+    int src1_type = MOE_TYPE_Q8_1;
+    const int32_t *ids = nullptr;
+    float *dst = nullptr;
+    int64_t ne00 = 0, ne01 = 0, ncols_dst = 0, s01 = 0;
+    int64_t nchannels_y = 1, nchannels_dst = 0, stride_col_y = 0, stride_col_dst = 0;
+    int64_t stride_channel_y = 0, stride_channel_dst = 0, ids_stride = 0;
+    const void *shared_y = nullptr;               // layer path: shared-block activations
+    int64_t shared_y_stride_col = 0;
+};
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
+    const moe_tensor *src0 = c.src0;
+    if (!src0 || !src0->data || !c.src1 || !c.ids || !c.dst) return fail(MOE_ERR_INVALID, "null argument");
+    if (!type_supported(src0->type)) return fail(MOE_ERR_UNSUPPORTED, "moe-cache: unsupported expert type %d", src0->type);
+    if (!contiguous(src0)) return fail(MOE_ERR_UNSUPPORTED, "expert tensor is not contiguous");
+    if (c.src1_type != MOE_TYPE_Q8_1 && c.src1_type != MOE_TYPE_F32) return fail(MOE_ERR_UNSUPPORTED, "src1 must be Q8_1 or F32");
+    if (c.ne00 != src0->ne[0] || c.ne01 != src0->ne[1]) return fail(MOE_ERR_INVALID, "ne00/ne01 do not match src0");
+    if (c.nchannels_y < 1) return fail(MOE_ERR_INVALID, "nchannels_y < 1");
+    // 16-byte aligned bases (ggml aligns tensor data to 32 bytes) keep every
+    // shared-memory word load of the GEMV aligned
+    if (!aligned16(src0->data)) return fail(MOE_ERR_UNSUPPORTED, "expert tensor data must be 16-byte aligned");
+    if (c.fd && ((c.fd->gate && !aligned16(c.fd->gate)) || (c.fd->shared_up && !aligned16(c.fd->shared_up)) ||
+                 (c.fd->shared_gate && !aligned16(c.fd->shared_gate))))
+        return fail(MOE_ERR_UNSUPPORTED, "gate / shared expert data must be 16-byte aligned");
+    Entry *e = nullptr;
+    int rc = get_or_create(src0, stream, &e);
+    if (rc) return rc;
+    const moe_fusion_device *fd = c.fd;
+    const bool use_gate = fd && fd->gate;
+    Entry *ge = nullptr;
+    if (use_gate && c.gate && wants_locked(c.gate)) {
+        if (c.gate->type != src0->type || c.gate->ne[0] != src0->ne[0] || c.gate->ne[1] != src0->ne[1])
+            return fail(MOE_ERR_UNSUPPORTED, "fused gate must match the up tensor's type and shape");
+        rc = get_or_create(c.gate, stream, &ge);
+        if (rc) return rc;
+    }
+    moe::GemvArgs a{};
+    a.tbl = e->d_tbl;
+    a.stamps = e->d_stamps;
+    a.cache_id = e->id;
+    a.use_gate = use_gate ? 1 : 0;
+    a.has_fusion = fd && (fd->gate || fd->x_bias || fd->gate_bias || fd->x_scale || fd->gate_scale) ? 1 : 0;
+    const bool tma_main = (src0->nb[2] % 16) == 0;
+    a.tma_main = tma_main;
+    if (use_gate) {
+        if (ge) {
+            a.tbl_gate = ge->d_tbl;
+            a.stamps_gate = ge->d_stamps;
+            a.cache_id_gate = ge->id;
+            a.tma_gate = aligned16(ge->data) && (ge->expert_bytes % 16) == 0;
+        } else {
+            a.gate_dense = static_cast<const char *>(fd->gate);
+            a.gate_expert_bytes = src0->nb[2];
+            a.tma_gate = aligned16(fd->gate) && (src0->nb[2] % 16) == 0 && ptr_kind(fd->gate) == 2;
+        }
+        a.x_bias = fd->x_bias;
+        a.gate_bias = fd->gate_bias;
+    } else if (fd) {
+        a.x_bias = fd->x_bias;
+    }
+    if (fd) {
+        a.glu_op = fd->glu_op;
+        a.glu_limit = fd->glu_limit;
+        if (fd->shared_up) {
+            if (use_gate && !fd->shared_gate) return fail(MOE_ERR_INVALID, "shared expert needs shared_gate with a fused gate");
+            a.shared_up = static_cast<const char *>(fd->shared_up);
+            a.shared_gate = use_gate ? static_cast<const char *>(fd->shared_gate) : nullptr;
+            a.shared_dst = fd->shared_dst;
+            a.shared_stride_col_dst = fd->shared_stride_col_dst;
+            const uint64_t mat = src0->nb[2];
+            a.tma_shared = aligned16(fd->shared_up) && (!use_gate || aligned16(fd->shared_gate)) && (mat % 16) == 0 &&
+                           ptr_kind(fd->shared_up) == 2 && (!use_gate || ptr_kind(fd->shared_gate) == 2);
+        }
+    }
+    a.shared_y = c.shared_y;
+    a.shared_y_stride_col = c.shared_y_stride_col;
+    a.stats = g.d_stats;
+    a.clock = g.d_clock;
+    a.log_cap = kLogCap;
+    a.y = c.src1;
+    a.stride_col_y = c.stride_col_y;
+    a.stride_channel_y = c.stride_channel_y;
+    a.nchannels_y = static_cast<int32_t>(c.nchannels_y);
+    a.ids = c.ids;
+    a.ids_stride = c.ids_stride;
+    a.ncols_dst = static_cast<int32_t>(c.ncols_dst);
+    a.nchannels_dst = static_cast<int32_t>(c.nchannels_dst);
+    a.n_experts = e->n_experts;
+    a.dst = c.dst;
+    a.stride_col_dst = c.stride_col_dst;
+    a.stride_channel_dst = c.stride_channel_dst;
+    a.K = static_cast<int32_t>(c.ne00);
+    a.nrows = static_cast<int32_t>(c.ne01);
+    a.row_bytes = static_cast<uint32_t>(c.s01 * type_size(src0->type));
+    if (a.row_bytes != src0->nb[1]) return fail(MOE_ERR_INVALID, "s01 does not match src0->nb[1]");
+    a.err = g.d_err;
+    const char *why = "";
+    cudaError_t ce = cudaSuccess;
+    const int act = c.src1_type == MOE_TYPE_Q8_1 ? moe::ACT_Q8_1 : moe::ACT_CPU;
+    rc = moe::launch_gemv(src0->type, act, a, stream, &why, &ce);
+    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+    if (rc) return fail(rc, "%s", why);
+    return MOE_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct LayerWs {
+    int32_t *ids;
+    float *w, *h, *hs, *y, *ys;
+    size_t bytes;
+};
+
+LayerWs layer_ws(const moe_layer_desc *L, int64_t n_tok, char *base) {
+    LayerWs w{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
+    const int64_t k = L->k, F = L->F, H = L->H;
+    w.ids = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * n_tok * k));
+    w.w = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k));
+    w.h = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k * F));
+    w.hs = reinterpret_cast<float *>(take(sizeof(float) * n_tok * F));
+    w.y = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k * H));
+    w.ys = reinterpret_cast<float *>(take(sizeof(float) * n_tok * H));
+    w.bytes = off;
+    return w;
+}
+
+}  // namespace
+
+// ============================================================================
+// C ABI
+// ============================================================================
+extern "C" {
+
+int ggml_cuda_moe_cache_enabled(void) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    return g.enabled ? 1 : 0;
+}
+
+int ggml_cuda_moe_cache_wants(const moe_tensor *src0) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    return wants_locked(src0);
+}
+
+int ggml_cuda_moe_cache_mul_mat_vec_q(const moe_tensor *src0, const moe_fusion_host *fusion,
+                                      const moe_fusion_device *fusion_dev, const void *src1, int32_t src1_type,
+                                      const int32_t *ids_d, float *dst_d, int64_t ne00, int64_t ne01, int64_t ne02,
+                                      int64_t ne03, int64_t ncols_dst, int64_t s01, int64_t s02, int64_t s03,
+                                      int64_t nchannels_y, int64_t nchannels_dst, int64_t stride_col_y,
+                                      int64_t stride_col_dst, int64_t stride_channel_y, int64_t stride_channel_dst,
+                                      int64_t ids_stride, moe_stream_t stream) {
+    (void)ne02; (void)ne03; (void)s02; (void)s03;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    MmvqCall c;
+    c.src0 = src0;
+    c.gate = fusion ? fusion->gate : nullptr;
+    c.fd = fusion_dev;
+    c.src1 = src1;
+    c.src1_type = src1_type;
+    c.ids = ids_d;
+    c.dst = dst_d;
+    c.ne00 = ne00; c.ne01 = ne01; c.ncols_dst = ncols_dst; c.s01 = s01;
+    c.nchannels_y = nchannels_y; c.nchannels_dst = nchannels_dst;
+    c.stride_col_y = stride_col_y; c.stride_col_dst = stride_col_dst;
+    c.stride_channel_y = stride_channel_y; c.stride_channel_dst = stride_channel_dst;
+    c.ids_stride = ids_stride;
+    return run_mmvq(c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ggml_cuda_moe_cache_step(moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    return step_locked(reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ggml_cuda_moe_cache_active(void) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    return g.all.empty() ? 0 : 1;
+}
+
+// reference ggml_cuda_moe_cache_pin_host (:372-405)
+int ggml_cuda_moe_cache_pin_host(const moe_tensor *t) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!g.enabled || !t || (t->flags & MOE_TENSOR_NO_BUFFER) || !t->data) return 0;
+    cudaPointerAttributes attrs;
+    cudaError_t err = cudaPointerGetAttributes(&attrs, t->data);
+    if (err != cudaSuccess) { cudaGetLastError(); return 0; }
+    if (attrs.type == cudaMemoryTypeHost || attrs.type == cudaMemoryTypeManaged) return 1;
+    if (attrs.type == cudaMemoryTypeDevice) return 0;
+    const int64_t bs = blck_size(t->type);
+    uint64_t nbytes = static_cast<uint64_t>(t->ne[0] / bs) * t->nb[0];
+    for (int i = 1; i < 4; ++i) nbytes += static_cast<uint64_t>(t->ne[i] - 1) * t->nb[i];
+    const uintptr_t page = 4096;
+    const uintptr_t base = reinterpret_cast<uintptr_t>(t->data) & ~(page - 1);
+    const uintptr_t end = (reinterpret_cast<uintptr_t>(t->data) + nbytes + page - 1) & ~(page - 1);
+    err = cudaHostRegister(reinterpret_cast<void *>(base), end - base, cudaHostRegisterPortable | cudaHostRegisterReadOnly);
+    if (err == cudaSuccess) {
+        g.ptr_kind.erase(t->data);
+        return 1;
+    }
+    cudaGetLastError();
+    fail(MOE_ERR_CUDA, "moe-cache: failed to pin %s: %s", t->name ? t->name : "<tensor>", cudaGetErrorString(err));
+    return 0;
+}
+
+int moe_b200_configure(const moe_cache_config *cfg) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!cfg) return fail(MOE_ERR_INVALID, "null config");
+    free_all();
+    g.enabled = cfg->enabled != 0;
+    g.slots = cfg->slots < 0 ? 0 : cfg->slots;
+    g.budget = cfg->budget_gb > 0 ? static_cast<size_t>(cfg->budget_gb * 1024.0 * 1024.0 * 1024.0) : (30ull << 30);
+    g.seed_path = cfg->seed_path ? cfg->seed_path : "";
+    g.claim_device = cfg->claim_device != 0;
+    g.debug = cfg->debug != 0;
+    g.env_read = true;
+    g.configured = true;
+    return MOE_OK;
+}
+
+int moe_b200_reset(void) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    free_all();
+    g.env_read = false;
+    g.configured = false;
+    g.enabled = false;
+    g.slots = 320;
+    g.budget = 30ull << 30;
+    g.claim_device = true;
+    g.debug = false;
+    g.seed_path.clear();
+    return MOE_OK;
+}
+
+int moe_b200_stats(moe_cache_stats *out) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!out) return fail(MOE_ERR_INVALID, "null stats");
+    uint64_t resident = 0;
+    for (const Entry *e : g.all)
+        for (int s = 0; s < e->n_slots; ++s) resident += e->expert_of[s] >= 0;
+    out->steps = g.steps;
+    out->hits = g.hits;
+    out->misses = g.misses;
+    out->promotions = g.promotions;
+    out->evictions = g.evictions;
+    out->resident = resident;
+    out->registered = g.all.size();
+    out->log_overflow = g.overflow;
+    out->pool_bytes = g.used;
+    return MOE_OK;
+}
+
+int moe_b200_table(const void *data, int32_t *slot_of, int32_t n_experts, int32_t *n_slots, int32_t *tensor_id) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    auto it = g.by_data.find(static_cast<const char *>(data));
+    if (it == g.by_data.end()) return fail(MOE_ERR_INVALID, "tensor is not registered");
+    Entry *e = it->second;
+    if (n_experts < e->n_experts) return fail(MOE_ERR_INVALID, "slot_of too small");
+    std::vector<char *> tbl(e->n_experts);
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(tbl.data(), e->d_tbl, sizeof(char *) * e->n_experts, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < e->n_experts; ++i) {
+        const uintptr_t p = reinterpret_cast<uintptr_t>(tbl[i]);
+        if (p & 1u) slot_of[i] = -1;
+        else if (e->pool && p >= reinterpret_cast<uintptr_t>(e->pool) &&
+                 p < reinterpret_cast<uintptr_t>(e->pool) + static_cast<uintptr_t>(e->n_slots) * e->expert_bytes)
+            slot_of[i] = static_cast<int32_t>((p - reinterpret_cast<uintptr_t>(e->pool)) / e->expert_bytes);
+        else slot_of[i] = -2;
+    }
+    if (n_slots) *n_slots = e->n_slots;
+    if (tensor_id) *tensor_id = e->id;
+    return MOE_OK;
+}
+
+int moe_b200_device_error(moe_stream_t stream, int32_t *code) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (code) *code = 0;
+    CK(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+    if (!g.d_err) return MOE_OK;
+    int v = 0;
+    CK(cudaMemcpy(&v, g.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    CK(cudaMemset(g.d_err, 0, sizeof(int)));
+    if (code) *code = v;
+    return MOE_OK;
+}
+
+const char *moe_b200_last_error(void) { return g_err.c_str(); }
+
+int moe_b200_quantize_act(int32_t act_type, const float *x, void *y, int64_t n_rows, int64_t n_cols, moe_stream_t stream) {
+    if (act_type != MOE_TYPE_Q8_0 && act_type != MOE_TYPE_Q8_1 && act_type != MOE_TYPE_Q8_K)
+        return fail(MOE_ERR_UNSUPPORTED, "act_type must be Q8_0, Q8_1 or Q8_K");
+    const int64_t qk = act_type == MOE_TYPE_Q8_K ? 256 : 32;
+    if (n_cols % qk || n_rows < 0) return fail(MOE_ERR_INVALID, "n_cols must be a multiple of %lld", static_cast<long long>(qk));
+    CK(moe::launch_quantize_act(act_type, x, y, n_rows, n_cols, reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+int moe_b200_topk_softmax(const float *logits, int64_t n_tok, int64_t n_experts, int64_t k, int32_t norm_w, int32_t *ids,
+                          float *weights, moe_stream_t stream) {
+    if (k < 1 || k > 32 || k > n_experts || n_experts > 65536) return fail(MOE_ERR_INVALID, "need 1 <= k <= min(32, n_experts)");
+    CK(moe::launch_topk_softmax(logits, n_tok, n_experts, k, norm_w, ids, weights, reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+size_t moe_b200_layer_workspace_size(const moe_layer_desc *L, int64_t n_tok) {
+    if (!L) return 0;
+    return layer_ws(L, n_tok, nullptr).bytes;
+}
+
+int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *logits, float *out, int64_t n_tok,
+                          void *workspace, size_t workspace_bytes, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || !x || !logits || !out) return fail(MOE_ERR_INVALID, "null argument");
+    if (n_tok < 1 || n_tok > 8) return fail(MOE_ERR_UNSUPPORTED, "layer decode handles 1..8 tokens");
+    const LayerWs w = layer_ws(L, n_tok, static_cast<char *>(workspace));
+    if (!workspace || workspace_bytes < w.bytes) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, w.bytes);
+    if (L->gate.type != L->up.type) return fail(MOE_ERR_UNSUPPORTED, "gate and up must share a type for the fused GEMV");
+    const bool shared = L->shared_type >= 0;   // shared gate/up take up's type, shared down takes down's
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t k = L->k, F = L->F, H = L->H;
+    if (L->up.ne[0] != H || L->up.ne[1] != F || L->down.ne[0] != F || L->down.ne[1] != H)
+        return fail(MOE_ERR_INVALID, "expert tensor shapes do not match H/F");
+    CK(moe::launch_topk_softmax(logits, n_tok, L->n_experts, k, L->norm_w, w.ids, w.w, st));
+
+    moe_fusion_device fd{};
+    fd.gate = L->gate.data;
+    fd.glu_op = L->glu_op;
+    fd.glu_limit = L->glu_limit;
+    if (shared) {
+        fd.shared_up = L->shared_up;
+        fd.shared_gate = L->shared_gate;
+        fd.shared_dst = w.hs;
+        fd.shared_stride_col_dst = F;
+    }
+    MmvqCall c;
+    c.src0 = &L->up;
+    c.gate = &L->gate;
+    c.fd = &fd;
+    c.src1 = x;
+    c.src1_type = MOE_TYPE_F32;
+    c.ids = w.ids;
+    c.dst = w.h;
+    c.ne00 = H; c.ne01 = F; c.ncols_dst = n_tok; c.s01 = static_cast<int64_t>(L->up.nb[1]) / type_size(L->up.type);
+    c.nchannels_y = 1; c.nchannels_dst = k;
+    c.stride_col_y = H; c.stride_channel_y = 0;
+    c.stride_col_dst = k * F; c.stride_channel_dst = F;
+    c.ids_stride = k;
+    int rc = run_mmvq(c, st);
+    if (rc) return rc;
+
+    moe_fusion_device fd2{};
+    if (shared) {
+        fd2.shared_up = L->shared_down;
+        fd2.shared_dst = w.ys;
+        fd2.shared_stride_col_dst = H;
+    }
+    MmvqCall d;
+    d.src0 = &L->down;
+    d.fd = &fd2;
+    d.src1 = w.h;
+    d.src1_type = MOE_TYPE_F32;
+    d.ids = w.ids;
+    d.dst = w.y;
+    d.ne00 = F; d.ne01 = H; d.ncols_dst = n_tok; d.s01 = static_cast<int64_t>(L->down.nb[1]) / type_size(L->down.type);
+    d.nchannels_y = k; d.nchannels_dst = k;
+    d.stride_col_y = k * F; d.stride_channel_y = F;
+    d.stride_col_dst = k * H; d.stride_channel_dst = H;
+    d.ids_stride = k;
+    d.shared_y = shared ? w.hs : nullptr;
+    d.shared_y_stride_col = F;
+    rc = run_mmvq(d, st);
+    if (rc) return rc;
+    CK(moe::launch_combine(w.y, w.w, shared ? w.ys : nullptr, out, n_tok, H, k, st));
+    return MOE_OK;
+}
+
+int moe_b200_fill_quantized(int32_t type, void *dst, int64_t n_rows, int64_t n_cols, uint64_t seed, float sigma,
+                            moe_stream_t stream) {
+    if (!type_supported(type)) return fail(MOE_ERR_UNSUPPORTED, "unsupported type %d", type);
+    if (n_cols % blck_size(type)) return fail(MOE_ERR_INVALID, "n_cols not a multiple of the block size");
+    CK(moe::launch_fill_quantized(type, dst, n_rows, n_cols, seed, sigma, reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,207 @@
+// moe_common.cuh -- device helpers shared by the sm_100a kernels of the MoE
+// expert path: block-format constants, PTX wrappers (mbarrier, 1-D bulk copy,
+// mixed-sign dp4a/dp2a), and bounded waits.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace moe {
+
+// ggml_type ids of the path
+enum : int {
+    T_F32 = 0, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_Q8_1 = 9,
+    T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_Q8_K = 15,
+};
+
+// activation semantics
+enum : int { ACT_Q8_1 = 0, ACT_CPU = 1 };
+
+// device error codes (first writer wins)
+enum : int {
+    DERR_NONE = 0, DERR_BAD_ID = 1, DERR_TOO_MANY_KEYS = 2, DERR_TIMEOUT_FULL = 3,
+    DERR_TIMEOUT_EMPTY = 4, DERR_TOO_MANY_SEGMENTS = 5, DERR_DRAIN = 6,
+};
+
+template <int T> struct fmt;
+template <> struct fmt<T_Q4_0> { static constexpr int qk = 32,  bytes = 18,  tasks = 1; static constexpr bool a4 = false; };
+template <> struct fmt<T_Q5_0> { static constexpr int qk = 32,  bytes = 22,  tasks = 1; static constexpr bool a4 = false; };
+template <> struct fmt<T_Q8_0> { static constexpr int qk = 32,  bytes = 34,  tasks = 1; static constexpr bool a4 = false; };
+template <> struct fmt<T_Q2_K> { static constexpr int qk = 256, bytes = 84,  tasks = 2; static constexpr bool a4 = true;  };
+template <> struct fmt<T_Q3_K> { static constexpr int qk = 256, bytes = 110, tasks = 2; static constexpr bool a4 = false; };
+template <> struct fmt<T_Q4_K> { static constexpr int qk = 256, bytes = 144, tasks = 4; static constexpr bool a4 = true;  };
+template <> struct fmt<T_Q5_K> { static constexpr int qk = 256, bytes = 176, tasks = 4; static constexpr bool a4 = true;  };
+template <> struct fmt<T_Q6_K> { static constexpr int qk = 256, bytes = 210, tasks = 2; static constexpr bool a4 = false; };
+
+__host__ __device__ constexpr bool is_kquant(int t) { return t >= T_Q2_K && t <= T_Q6_K; }
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase with the given parity; gives up after ~timeout_ns.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && global_timer_ns() - t0 > timeout_ns) return false;
+    }
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (tx bytes).
+// dst, src 16-byte aligned; bytes a multiple of 16. Never used on host memory.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// sum of 4 (unsigned byte of a) * (signed byte of b) + c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// signed x signed
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// a: two signed 16-bit, b: four unsigned bytes; lo uses bytes 0,1 of b, hi bytes 2,3
+__device__ __forceinline__ int dp2a_lo_su(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_su(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// a: two signed 16-bit, b: four signed bytes
+__device__ __forceinline__ int dp2a_lo_ss(int a, int b, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_ss(int a, int b, int c) {
+    int d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t ld_u32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+__device__ __forceinline__ float ld_half(const uint8_t *p) {
+    return __half2float(*reinterpret_cast<const __half *>(p));
+}
+
+// N consecutive 32-bit words from a 2-byte aligned shared-memory address
+// (reads one word past the run; callers keep 16 bytes of slack).
+template <int N>
+__device__ __forceinline__ void ld_words_a2(const uint8_t *p, uint32_t (&w)[N]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *base = reinterpret_cast<const uint32_t *>(a & ~static_cast<uintptr_t>(3));
+    const uint32_t sh = static_cast<uint32_t>(a & 2u) * 8u;
+    uint32_t x[N + 1];
+#pragma unroll
+    for (int i = 0; i <= N; ++i) x[i] = base[i];
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(x[i], x[i + 1], sh);
+}
+
+template <int N>
+__device__ __forceinline__ void ld_words_a4(const uint8_t *p, uint32_t (&w)[N]) {
+    const uint32_t *b = reinterpret_cast<const uint32_t *>(p);
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = b[i];
+}
+
+// 4 bits -> bit 4 of each of the 4 bytes
+__device__ __forceinline__ uint32_t spread4_bit4(uint32_t nib) { return ((nib & 0xFu) * 0x02040810u) & 0x10101010u; }
+
+// ggml's nearest_int (1.5*2^23 magic rounding), with explicit non-contracted ops
+__device__ __forceinline__ int nearest_int_dev(float prod) {
+    const float val = __fadd_rn(prod, 12582912.f);
+    return (__float_as_int(val) & 0x007fffff) - 0x00400000;
+}
+
+__device__ __forceinline__ void set_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// GLU epilogue (reference kernels/moe-cache.cu:264-280): result = up, g = gate
+__device__ __forceinline__ float glu_apply(int op, float g, float up, float limit) {
+    switch (op) {
+        case 0: return up * (g / (1.0f + expf(-g)));
+        case 1: {
+            const float c = 0.79788456080286535587989211986876f, a = 0.044715f;
+            return up * (0.5f * g * (1.0f + tanhf(c * g * (1.0f + a * g * g))));
+        }
+        case 2: {
+            const float x = fminf(g, 7.0f);
+            const float u = fmaxf(fminf(up, 7.0f), -7.0f);
+            return (x / (1.0f + expf(-x * 1.702f))) * (u + 1.0f);
+        }
+        case 3: {
+            const float x = fminf(g, limit);
+            const float u = fmaxf(fminf(up, limit), -limit);
+            return (x / (1.0f + expf(-x))) * u;
+        }
+        default: return up * g;
+    }
+}
+
+}  // namespace moe

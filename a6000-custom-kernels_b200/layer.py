@@ -1,0 +1,94 @@
+"""One MoE FFN layer on the B200 path: the graph around two MUL_MAT_ID calls.
+
+Routing (top-k + softmax), the fused gate/up GEMV with the GLU and the shared
+expert, the down GEMV and the weighted combine run as four sm_100a launches of
+libmoe_b200.so (moe_b200_layer_decode). This mirrors what llama.cpp's graph does
+around the reference's intercepted MUL_MAT_ID calls (build_moe_ffn order:
+route, gate/up, GLU, down, weight, sum over picks, add the shared expert).
+"""
+import ctypes
+
+import torch
+
+from ._lib import MoeLayerDesc, check, lib
+from .moe_cache import GLU_SWIGLU, _ptr, _stream, expert_tensor, fill_quantized, row_size
+
+
+class MoELayer:
+    """Expert weights live in `device` memory (HBM-resident) unless `host=True`,
+    in which case they live in pinned host memory behind the tiered cache."""
+
+    def __init__(self, H, F, n_experts, k, types, shared=True, glu_op=GLU_SWIGLU, glu_limit=0.0, norm_w=False,
+                 device="cuda", host=False, name="blk.0", seed=0, weights=None):
+        self.H, self.F, self.E, self.k = H, F, n_experts, k
+        self.types = dict(types)          # {"gate": t, "up": t, "down": t}
+        self.glu_op, self.glu_limit, self.norm_w = glu_op, glu_limit, norm_w
+        self.device = torch.device(device)
+        shapes = {"gate": (F, H), "up": (F, H), "down": (H, F)}
+        self.w = {}
+        for i, role in enumerate(("gate", "up", "down")):
+            t = self.types[role]
+            rows, K = shapes[role]
+            if weights is not None:
+                src = torch.as_tensor(weights[role])
+                buf = src.pin_memory() if host else src.to(self.device)
+            else:
+                buf = torch.empty((n_experts, rows, row_size(t, K)), dtype=torch.uint8, device=self.device)
+                fill_quantized(t, buf, n_experts * rows, K, seed * 1000003 + i)
+                if host:
+                    buf = buf.cpu().pin_memory()
+            self.w[role] = buf
+        self.desc_t = {r: expert_tensor(self.w[r], self.types[r], shapes[r][1], shapes[r][0],
+                                        name=f"{name}.ffn_{r}_exps.weight") for r in ("gate", "up", "down")}
+        self.shared = {}
+        if shared:
+            for i, role in enumerate(("gate", "up", "down")):
+                t = self.types[role]
+                rows, K = shapes[role]
+                if weights is not None and weights.get(f"shared_{role}") is not None:
+                    buf = torch.as_tensor(weights[f"shared_{role}"]).to(self.device)
+                else:
+                    buf = torch.empty((rows, row_size(t, K)), dtype=torch.uint8, device=self.device)
+                    fill_quantized(t, buf, rows, K, seed * 1000003 + 7 + i)
+                self.shared[role] = buf
+        d = MoeLayerDesc()
+        d.gate, d.up, d.down = self.desc_t["gate"], self.desc_t["up"], self.desc_t["down"]
+        d.shared_type = self.types["up"] if shared else -1
+        d.shared_gate = _ptr(self.shared.get("gate"))
+        d.shared_up = _ptr(self.shared.get("up"))
+        d.shared_down = _ptr(self.shared.get("down"))
+        d.H, d.F, d.n_experts, d.k = H, F, n_experts, k
+        d.glu_op, d.glu_limit, d.norm_w = glu_op, glu_limit, int(norm_w)
+        self.desc = d
+        self._ws = {}
+
+    def weight_bytes_per_token(self):
+        """Expert bytes one batch-1 token streams: k routed + shared experts x 3 matrices."""
+        per = sum(self.w[r][0].numel() for r in ("gate", "up", "down"))
+        return per * (self.k + (1 if self.shared else 0))
+
+    def workspace(self, n_tok):
+        ws = self._ws.get(n_tok)
+        if ws is None:
+            nbytes = lib().moe_b200_layer_workspace_size(ctypes.byref(self.desc), n_tok)
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self._ws[n_tok] = ws
+        return ws
+
+    def decode(self, x, logits, out=None, stream=None):
+        """x f32 [n_tok, H], logits f32 [n_tok, E] (device) -> out f32 [n_tok, H]."""
+        n_tok = x.shape[0]
+        if out is None:
+            out = torch.empty((n_tok, self.H), dtype=torch.float32, device=self.device)
+        ws = self.workspace(n_tok)
+        check(lib().moe_b200_layer_decode(ctypes.byref(self.desc), _ptr(x), _ptr(logits), _ptr(out), n_tok,
+                                          _ptr(ws), ws.numel(), _stream(stream)))
+        return out
+
+    def routing_of(self, n_tok):
+        """(ids, weights) views of the last decode's routing in the workspace."""
+        ws = self._ws[n_tok]
+        ids = ws[: n_tok * self.k * 4].view(torch.int32).view(n_tok, self.k)
+        off = (n_tok * self.k * 4 + 255) // 256 * 256
+        w = ws[off: off + n_tok * self.k * 4].view(torch.float32).view(n_tok, self.k)
+        return ids, w

@@ -1,0 +1,468 @@
+#!/usr/bin/env python
+"""MoE decode benchmark of the B200 expert path (BASELINE.json metric:
+"MoE decode tokens/s; expert-GEMV HBM GB/s (% of 8 TB/s)").
+
+Workload (N=1 line): BASELINE config 2 -- one full-width MoE layer at batch-1
+decode: hidden 3072, 512 experts, expert FFN 768, top-8 routing over
+Zipf(1.1)-skewed router logits, one always-on shared expert, gate/up/down Q2_K
+from N(0, 0.02) weights, f32 activations ~ N(0, 1), all experts HBM-resident.
+A step = one token through the layer: route, fused gate/up GEMV + SwiGLU +
+shared expert, down GEMV, weighted combine (4 launches). The timed loop cycles
+through 32 independently generated copies of the layer (38 GB), so every step
+reads expert weights that the L2 (126 MB) no longer holds.
+
+  python bench.py [--gpus N --steps K --warmup W]       # this implementation
+  python bench.py --impl reference [...]                 # CPU reference arm
+
+N > 1 (under torchrun): replicas -- every rank runs the same workload on its
+own GPU with its own layers; value = all ranks' tokens / max-over-ranks time.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+H, F, E, K_TOP = 3072, 768, 512, 8
+Q2_K = 10
+EXPERT_BYTES = 768 * (3072 // 256) * 84          # one Q2_K expert matrix: 774,144 B
+GATEUP_BYTES = (K_TOP + 1) * 2 * EXPERT_BYTES     # per gate/up launch (8 routed + shared)
+DOWN_BYTES = (K_TOP + 1) * EXPERT_BYTES
+STEP_BYTES = GATEUP_BYTES + DOWN_BYTES            # 20,901,888 B per token
+METRIC = "MoE decode tokens/s; expert-GEMV HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+WORKLOAD = "config2: full-width MoE layer (H=3072, E=512, F=768, top-8 Zipf(1.1) + shared expert, Q2_K), batch-1 decode"
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
+    ap.add_argument("--layers", type=int, default=32, help="independent layer copies cycled by the timed loop")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
+    ap.add_argument("--e2e-steps", type=int, default=2000)
+    return ap.parse_args()
+
+
+def zipf_logits(n_tok, seed, alpha=1.1):
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(E)
+    base = -alpha * np.log(perm + 1.0)
+    return (base[None, :] + rng.normal(0.0, 1.0, size=(n_tok, E))).astype(np.float32)
+
+
+def token_pool(n, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.normal(0.0, 1.0, size=(n, H)).astype(np.float32)
+    return x, zipf_logits(n, seed + 1)
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle's llama.cpp-semantics layer on the host cores
+# ---------------------------------------------------------------------------
+def cpu_layer_sample(seconds, n_threads, layer_seed=0, pool_seed=1234):
+    """Time the CPU restatement of llama.cpp's MoE layer (Q8_K activations,
+    generic vec_dot) on config 2, weights generated for the experts the sampled
+    tokens route to. Returns (tokens/s, steps, seconds)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    n_pool = 16
+    x, logits = token_pool(n_pool, pool_seed)
+    ids, _ = O.topk_softmax(logits, K_TOP)
+    used = sorted(set(ids.reshape(-1).tolist()))
+    rb_h, rb_f = O.row_size(Q2_K, H), O.row_size(Q2_K, F)
+    W = {r: np.zeros((E, F if r != "down" else H, rb_h if r != "down" else rb_f), np.uint8) for r in ("gate", "up", "down")}
+    for i, r in enumerate(("gate", "up", "down")):
+        rows, cols = (F, H) if r != "down" else (H, F)
+        for e in used:
+            O.fill_quantized(Q2_K, W[r][e], e * rows, rows, cols, seed=layer_seed * 1000003 + i, n_threads=n_threads)
+    shared = {}
+    for i, r in enumerate(("gate", "up", "down")):
+        rows, cols = (F, H) if r != "down" else (H, F)
+        buf = np.zeros((rows, O.row_size(Q2_K, cols)), np.uint8)
+        O.fill_quantized(Q2_K, buf, 0, rows, cols, seed=layer_seed * 1000003 + 7 + i, n_threads=n_threads)
+        shared[r] = buf
+    L = dict(H=H, F=F, E=E, k=K_TOP, type_gate=Q2_K, type_up=Q2_K, type_down=Q2_K, gate=W["gate"], up=W["up"],
+             down=W["down"], shared_type=Q2_K, shared_gate=shared["gate"], shared_up=shared["up"],
+             shared_down=shared["down"])
+    O.moe_layer(L, x[:1], logits[:1], n_threads=n_threads)       # warm
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        i = steps % n_pool
+        O.moe_layer(L, x[i:i + 1], logits[i:i + 1], n_threads=n_threads)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and steps >= 3:
+            break
+    return steps / el, steps, el
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    per_step_s = None
+    tps, steps, el = cpu_layer_sample(min(args.cpu_seconds, 20.0), cores)
+    per_step_s = 1.0 / tps
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": 1, "ms_per_step": round(per_step_s * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": 1, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps} decode tokens of one config-2 layer ({el:.1f} s), CPU restatement of "
+                                   "llama.cpp's MUL_MAT_ID (oracle/, Q8_K activations), not llama.cpp itself"},
+        "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "llama.cpp is not present on this machine; the reference arm times this repo's CPU restatement "
+                "of its MUL_MAT_ID path",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        rows = [l for (t, l) in self.lines if t0 <= t <= t1] or [l for (_, l) in self.lines]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            f = [c.strip() for c in r.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_mine(args):
+    import torch
+    import torch.distributed as dist
+    import importlib
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    mc = pkg.moe_cache
+    mc.configure(enabled=True)
+    R = args.layers
+    layers = [pkg.MoELayer(H, F, E, K_TOP, {"gate": Q2_K, "up": Q2_K, "down": Q2_K}, shared=True, device=dev,
+                           seed=rank * 1000 + l, name=f"blk.{l}") for l in range(R)]
+    P = 64
+    xs_np, lg_np = token_pool(P, 1234 + rank)
+    xs = torch.from_numpy(xs_np).to(dev).view(P, 1, H)
+    lgs = torch.from_numpy(lg_np).to(dev).view(P, 1, E)
+    outs = torch.empty((P, 1, H), device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+
+    def step(i):
+        layers[i % R].decode(xs[i % P], lgs[i % P], outs[i % P], stream=stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, R)):
+            step(i)
+    torch.cuda.synchronize()
+    assert mc.device_error(stream) == 0
+
+    # CUDA graphs of the timed sequence: G-step chunks plus a remainder, so the
+    # timed region is exactly K steps
+    G = 512
+    K = args.steps
+    graphs = {}
+
+    def graph_for(n, start):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for j in range(n):
+                step(start + j)
+        return g
+
+    full = graph_for(G, 0) if K >= G else None
+    rem = graph_for(K % G, 0) if K % G else None
+    # warm the graphs (W warm-up steps already ran eagerly)
+    with torch.cuda.stream(stream):
+        if full is not None:
+            full.replay()
+        if rem is not None:
+            rem.replay()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    clocks.start()
+    # keep the GPU busy while the sampler starts
+    t_end = time.time() + 0.5
+    with torch.cuda.stream(stream):
+        while time.time() < t_end:
+            (full or rem).replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(K // G):
+            full.replay()
+        if rem is not None:
+            rem.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert mc.device_error(stream) == 0
+    value = world * K / (ms / 1e3)
+
+    # ---- dominant kernel: the fused gate/up GEMV, timed per launch -------------
+    kern = time_gateup_kernel(pkg, layers, xs, dev, stream, n=min(max(K, 256), 4096))
+
+    # ---- end to end through the public API with host buffers ------------------
+    e2e = run_e2e(pkg, layers, xs_np, lg_np, dev, stream, args.e2e_steps)
+    if world > 1:
+        t = torch.tensor([e2e["seconds"]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["seconds"] = float(t.item())
+    e2e_value = world * e2e["steps"] / e2e["seconds"]
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs")
+    peak_src = "of measured" if peak else "of fallback"
+    peak = peak or 6650.0
+    achieved = GATEUP_BYTES / (kern["us"] * 1e-6) / 1e9
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "gemv_gateup_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("bytes_per_launch")
+        except (OSError, ValueError):
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        cores = os.cpu_count() or 1
+        tps, steps, el = cpu_layer_sample(args.cpu_seconds, cores)
+        cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{steps} batch-1 decode tokens of one config-2 layer ({el:.1f} s) through the CPU "
+                         "restatement of llama.cpp's MUL_MAT_ID (oracle/), all host threads"}
+
+    if rank == 0:
+        ck = clocks.summary(wall0, wall1)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(ms / K, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "layers_cycled": R, "l2": f"inputs larger than L2: {R} layer copies "
+                                                 f"({R * 3 * E * EXPERT_BYTES / 1e9:.1f} GB) cycled",
+                       "graph": "CUDA graphs of 512-step chunks"},
+            "layer_gbs": round(STEP_BYTES * value / world / 1e9, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "frac_of_8TBs": round(achieved / 8000.0, 4), "traffic": traffic,
+                         "kernel": "moe_gemv_kernel<Q2_K> fused gate/up+SwiGLU+shared",
+                         "bytes_per_launch": GATEUP_BYTES, "us_per_launch": round(kern["us"], 3),
+                         "timing": kern["how"], "down_us_per_launch": round(kern.get("down_us", 0.0), 3)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"]},
+            "gpu_launches": 4 * K,
+            "clocks": ck,
+        }
+        print(json.dumps(line), flush=True)
+    for L in layers:
+        L._ws.clear()
+    del full, rem
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def time_gateup_kernel(pkg, layers, xs, dev, stream, n):
+    """Per-launch duration of the fused gate/up GEMV and of the down GEMV on the
+    benchmark's own layers and tokens: graphs of n launches each, bracketed by
+    external CUDA events per launch; mean of the per-launch intervals."""
+    import torch
+    mc = pkg.moe_cache
+    R = len(layers)
+    P = xs.shape[0]
+    bufs = []
+    for L in layers:
+        ids, _ = L.routing_of(1)
+        h = torch.empty((1, K_TOP, F), device=dev)
+        hs = torch.empty((1, F), device=dev)
+        y = torch.empty((1, K_TOP, H), device=dev)
+        ys = torch.empty((1, H), device=dev)
+        fd = mc.fusion_device(gate=L.w["gate"], glu_op=0, shared_up=L.shared["up"], shared_gate=L.shared["gate"],
+                              shared_dst=hs, shared_stride_col_dst=F)
+        fd2 = mc.fusion_device(shared_up=L.shared["down"], shared_dst=ys, shared_stride_col_dst=H)
+        bufs.append((ids, h, hs, y, ys, fd, fd2))
+
+    def gateup(i):
+        L = layers[i % R]
+        ids, h, hs, y, ys, fd, fd2 = bufs[i % R]
+        mc.mul_mat_vec_q(L.desc_t["up"], xs[i % P], mc.F32, ids, h, ncols_dst=1, nchannels_y=1, nchannels_dst=K_TOP,
+                         stride_col_y=H, stride_col_dst=K_TOP * F, stride_channel_y=0, stride_channel_dst=F,
+                         ids_stride=K_TOP, fusion_gate=L.desc_t["gate"], fusion_dev=fd, stream=stream)
+
+    def down(i):
+        L = layers[i % R]
+        ids, h, hs, y, ys, fd, fd2 = bufs[i % R]
+        mc.mul_mat_vec_q(L.desc_t["down"], h, mc.F32, ids, y, ncols_dst=1, nchannels_y=K_TOP, nchannels_dst=K_TOP,
+                         stride_col_y=K_TOP * F, stride_channel_y=F, stride_col_dst=K_TOP * H, stride_channel_dst=H,
+                         ids_stride=K_TOP, fusion_dev=fd2, stream=stream)
+
+    out = {}
+    for name, fn in (("gateup", gateup), ("down", down)):
+        with torch.cuda.stream(stream):
+            for i in range(R):
+                fn(i)
+        torch.cuda.synchronize()
+        try:
+            evs = [(torch.cuda.Event(enable_timing=True, external=True),
+                    torch.cuda.Event(enable_timing=True, external=True)) for _ in range(n)]
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(n):
+                    evs[i][0].record(stream)
+                    fn(i)
+                    evs[i][1].record(stream)
+            with torch.cuda.stream(stream):
+                g.replay()
+            torch.cuda.synchronize()
+            per = [a.elapsed_time(b) for a, b in evs]
+            us = 1e3 * statistics.mean(per)
+            how = (f"CUDA events around each of {n} launches (external event nodes in one CUDA graph), "
+                   f"{R} layer copies cycled")
+            del g
+        except (TypeError, RuntimeError):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(n):
+                    fn(i)
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                g.replay()
+                ev0.record(stream)
+                g.replay()
+                ev1.record(stream)
+            torch.cuda.synchronize()
+            us = 1e3 * ev0.elapsed_time(ev1) / n
+            how = f"CUDA events around a graph of {n} back-to-back launches (includes launch gaps)"
+            del g
+        out[name] = (us, how)
+    assert mc.device_error(stream) == 0
+    return {"us": out["gateup"][0], "how": out["gateup"][1], "down_us": out["down"][0]}
+
+
+def run_e2e(pkg, layers, xs_np, lg_np, dev, stream, steps):
+    """Public API end to end: per step, H2D of the token's activations and router
+    logits from pinned host memory, MoELayer.decode, D2H of the layer output."""
+    import torch
+    R = len(layers)
+    P = xs_np.shape[0]
+    hx = torch.from_numpy(xs_np).pin_memory()
+    hl = torch.from_numpy(lg_np).pin_memory()
+    hout = torch.empty((P, H), dtype=torch.float32).pin_memory()
+    dx = torch.empty((1, H), device=dev)
+    dl = torch.empty((1, E), device=dev)
+    dout = torch.empty((1, H), device=dev)
+
+    def one(i):
+        with torch.cuda.stream(stream):
+            dx.copy_(hx[i % P:i % P + 1], non_blocking=True)
+            dl.copy_(hl[i % P:i % P + 1], non_blocking=True)
+            layers[i % R].decode(dx, dl, dout, stream=stream)
+            hout[i % P:i % P + 1].copy_(dout, non_blocking=True)
+        stream.synchronize()
+
+    for i in range(20):
+        one(i)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(steps):
+        one(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    return {"seconds": ev0.elapsed_time(ev1) / 1e3, "steps": steps, "h2d": (H + E) * 4, "d2h": H * 4}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mine(args)
+
+
+if __name__ == "__main__":
+    main()

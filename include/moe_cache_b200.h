@@ -1,0 +1,219 @@
+/*
+ * moe_cache_b200.h -- C ABI of the B200 (sm_100a) MoE expert hot path.
+ *
+ * The entry points named ggml_cuda_moe_cache_* are the reference's boundary
+ * (kernels/moe-cache.cuh:15-40 of Zapdev-labs/a6000-custom-kernels) restated as
+ * a C ABI: plain pointers and sizes instead of ggml_tensor / C++ references,
+ * and an int status instead of aborting. Entry points prefixed moe_b200_ are
+ * additions with no reference counterpart; each says so.
+ *
+ * Status: 0 = MOE_OK, negative = error (moe_b200_last_error() describes it).
+ * Threading: all entry points are serialised by one library mutex, as the
+ * reference serialises its registry and step (moe-cache.cu:321,526,674).
+ * Streams: all work is enqueued on the caller's stream, as in the reference.
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *moe_stream_t;   /* same type as cudaStream_t */
+
+#define MOE_OK               0
+#define MOE_ERR_INVALID     -1   /* bad argument or shape */
+#define MOE_ERR_UNSUPPORTED -2   /* type / layout the path does not handle */
+#define MOE_ERR_CUDA        -3   /* a CUDA runtime call failed */
+#define MOE_ERR_OOM         -4   /* allocation failed */
+#define MOE_ERR_DEVICE      -5   /* a kernel reported a device-side check failure */
+#define MOE_ERR_STATE       -6   /* called in the wrong state (e.g. wrong device) */
+
+/* ggml_type numbering (ggml.h) for the formats of the path */
+enum {
+    MOE_TYPE_F32 = 0, MOE_TYPE_Q4_0 = 2, MOE_TYPE_Q5_0 = 6, MOE_TYPE_Q8_0 = 8, MOE_TYPE_Q8_1 = 9,
+    MOE_TYPE_Q2_K = 10, MOE_TYPE_Q3_K = 11, MOE_TYPE_Q4_K = 12, MOE_TYPE_Q5_K = 13,
+    MOE_TYPE_Q6_K = 14, MOE_TYPE_Q8_K = 15,
+};
+
+/* GLU ops of the fused gate/up epilogue (moe-cache.cu:264-280). The shim maps
+ * ggml_glu_op by name: SWIGLU, GEGLU, SWIGLU_OAI, SWIGLU_CLAMP; every other op
+ * maps to MOE_GLU_PRODUCT, which is the reference's default branch. */
+enum { MOE_GLU_SWIGLU = 0, MOE_GLU_GEGLU = 1, MOE_GLU_SWIGLU_OAI = 2, MOE_GLU_SWIGLU_CLAMP = 3,
+       MOE_GLU_PRODUCT = 4 };
+
+#define MOE_TENSOR_VIEW      1   /* ggml_tensor::view_src != NULL */
+#define MOE_TENSOR_NO_BUFFER 2   /* ggml_tensor::buffer == NULL   */
+
+/* The fields of a ggml_tensor that the path reads. */
+typedef struct {
+    const void *data;
+    int32_t     type;      /* MOE_TYPE_* */
+    int32_t     flags;     /* MOE_TENSOR_* */
+    int64_t     ne[4];
+    uint64_t    nb[4];
+    const char *name;      /* NUL-terminated; matched against seed-file lines */
+} moe_tensor;
+
+/* Mirror of upstream ggml_cuda_mm_fusion_args_host: the gate tensor, which
+ * gets its own table when it is itself cached (moe-cache.cu:840-844). */
+typedef struct {
+    const moe_tensor *gate;   /* may be NULL */
+} moe_fusion_host;
+
+/* Mirror of upstream ggml_cuda_mm_fusion_args_device (fields read at
+ * moe-cache.cu:103-129,797-798). All pointers are device pointers. */
+typedef struct {
+    const void  *gate;        /* gate weights, used when the gate has no table  */
+    const float *x_bias;      /* [n_experts][rows], added to the up/main result */
+    const float *gate_bias;   /* [n_experts][rows], added to the gate result    */
+    const float *x_scale;     /* NVFP4-only upstream: accepted and ignored      */
+    const float *gate_scale;  /* NVFP4-only upstream: accepted and ignored      */
+    int32_t      glu_op;      /* MOE_GLU_*                                      */
+    float        glu_limit;
+    const void  *shared_up;   /* shared expert ([rows][row bytes], same type)   */
+    const void  *shared_gate;
+    float       *shared_dst;
+    int64_t      shared_stride_col_dst;
+} moe_fusion_device;
+
+/* Replaces: bool ggml_cuda_moe_cache_enabled()  (moe-cache.cuh:15,
+ * moe-cache.cu:345-363). Reads GGML_CUDA_MOE_CACHE, _SLOTS, _BUDGET_GB,
+ * _SEED, _DEBUG and _DEVICE once. Returns 1 when enabled, 0 otherwise. */
+int ggml_cuda_moe_cache_enabled(void);
+
+/* Replaces: bool ggml_cuda_moe_cache_wants(const ggml_tensor*)  (moe-cache.cuh:18,
+ * moe-cache.cu:442-469). 1 when src0 should take this path: enabled, supported
+ * type, ne[2] >= 2, ne[3] == 1, not a view, contiguous, and either pinned host
+ * memory (tiered cache, as in the reference) or device memory (HBM-resident
+ * experts, new on B200; off with GGML_CUDA_MOE_CACHE_DEVICE=0). */
+int ggml_cuda_moe_cache_wants(const moe_tensor *src0);
+
+/* Replaces: void ggml_cuda_moe_cache_mul_mat_vec_q(ctx, src0, ids, dst, fusion,
+ * fusion_dev, src1_q8_1, ids_d, dst_d, ne00..ne03, ncols_dst, s01..s03,
+ * nchannels_y, nchannels_dst, stride_col_y, stride_col_dst, stride_channel_y,
+ * stride_channel_dst, ids_stride, stream)  (moe-cache.cuh:21-30,
+ * moe-cache.cu:821-868). The unused ctx/ids/dst tensor arguments are dropped.
+ *
+ * dst_d[ch*stride_channel_dst + tok*stride_col_dst + row] =
+ *     dot(expert ids_d[ch + tok*ids_stride] row `row`, src1[(ch % nchannels_y), tok])
+ * for ch < nchannels_dst, tok < ncols_dst, row < ne01, with the fused gate /
+ * GLU / bias / shared-expert epilogue when fusion_dev enables it.
+ *
+ * src1_type selects the activation semantics:
+ *   MOE_TYPE_Q8_1: src1 is Q8_1 blocks (36 B) as produced by llama.cpp's CUDA
+ *                  quantize_q8_1 (the reference's input); strides in blocks.
+ *   MOE_TYPE_F32:  src1 is f32; the kernel quantizes it exactly as llama.cpp's
+ *                  CPU path does (Q8_K for K-quants, Q8_0 for Q4_0/Q5_0/Q8_0);
+ *                  strides in floats.
+ * ncols_dst <= 8 (the MMVQ batch limit the reference runs at). */
+int ggml_cuda_moe_cache_mul_mat_vec_q(
+        const moe_tensor *src0, const moe_fusion_host *fusion, const moe_fusion_device *fusion_dev,
+        const void *src1, int32_t src1_type, const int32_t *ids_d, float *dst_d,
+        int64_t ne00, int64_t ne01, int64_t ne02, int64_t ne03,
+        int64_t ncols_dst, int64_t s01, int64_t s02, int64_t s03,
+        int64_t nchannels_y, int64_t nchannels_dst,
+        int64_t stride_col_y, int64_t stride_col_dst,
+        int64_t stride_channel_y, int64_t stride_channel_dst,
+        int64_t ids_stride, moe_stream_t stream);
+
+/* Replaces: void ggml_cuda_moe_cache_step(cudaStream_t)  (moe-cache.cuh:33,
+ * moe-cache.cu:669-775). Between graphs, never during stream capture. Returns
+ * at once (no device sync) when no registered tensor is host-tiered. */
+int ggml_cuda_moe_cache_step(moe_stream_t stream);
+
+/* Replaces: bool ggml_cuda_moe_cache_active()  (moe-cache.cuh:36, :365-368). */
+int ggml_cuda_moe_cache_active(void);
+
+/* Replaces: bool ggml_cuda_moe_cache_pin_host(const ggml_tensor*)
+ * (moe-cache.cuh:39, :372-405). 1 when t->data is GPU-readable host memory
+ * after the call (registers a plain host range with cudaHostRegister). */
+int ggml_cuda_moe_cache_pin_host(const moe_tensor *t);
+
+/* ---- additions (no counterpart in the reference) ------------------------ */
+
+typedef struct {
+    int32_t     enabled;        /* GGML_CUDA_MOE_CACHE            */
+    int32_t     slots;          /* GGML_CUDA_MOE_CACHE_SLOTS      (default 320) */
+    double      budget_gb;      /* GGML_CUDA_MOE_CACHE_BUDGET_GB  (default 30, <=0 keeps default) */
+    const char *seed_path;      /* GGML_CUDA_MOE_CACHE_SEED       (NULL: none)  */
+    int32_t     claim_device;   /* GGML_CUDA_MOE_CACHE_DEVICE     (default 1)   */
+    int32_t     debug;          /* GGML_CUDA_MOE_CACHE_DEBUG                    */
+} moe_cache_config;
+
+/* No counterpart in the reference: set the configuration programmatically
+ * instead of from the environment (forgets earlier registrations first). */
+int moe_b200_configure(const moe_cache_config *cfg);
+
+/* No counterpart in the reference (its state lives for the process): free all
+ * pools, tables and stamps and forget every registration. The next call
+ * re-reads the environment unless moe_b200_configure is called. */
+int moe_b200_reset(void);
+
+typedef struct {
+    uint64_t steps, hits, misses, promotions, evictions, resident, registered, log_overflow;
+    uint64_t pool_bytes;
+} moe_cache_stats;
+
+/* No counterpart in the reference (it prints every 64 steps): totals. */
+int moe_b200_stats(moe_cache_stats *out);
+
+/* No counterpart in the reference: read the DEVICE pointer table of the
+ * registered tensor whose data pointer is `data` back to the host and decode
+ * it: slot_of[e] = pool slot, -1 = host-tagged (cold), -2 = direct device
+ * pointer (HBM-resident tensor). Synchronises the device. */
+int moe_b200_table(const void *data, int32_t *slot_of, int32_t n_experts, int32_t *n_slots, int32_t *tensor_id);
+
+/* No counterpart in the reference: synchronise `stream`, then read and clear
+ * the kernels' device-side error word (0 = none). */
+int moe_b200_device_error(moe_stream_t stream, int32_t *code);
+
+/* No counterpart in the reference: message of the last failed call. */
+const char *moe_b200_last_error(void);
+
+/* No counterpart in the reference (upstream quantize_q8_1 / CPU quantizers):
+ * quantize n_rows rows of n_cols f32 into act_type blocks (MOE_TYPE_Q8_0,
+ * MOE_TYPE_Q8_1 or MOE_TYPE_Q8_K), bit-exact with llama.cpp's quantizers. */
+int moe_b200_quantize_act(int32_t act_type, const float *x, void *y, int64_t n_rows, int64_t n_cols,
+                          moe_stream_t stream);
+
+/* No counterpart in the reference (upstream graph ops): top-k over logits
+ * (descending, ties to the lower expert id) and softmax gating weights. */
+int moe_b200_topk_softmax(const float *logits, int64_t n_tok, int64_t n_experts, int64_t k, int32_t norm_w,
+                          int32_t *ids, float *weights, moe_stream_t stream);
+
+/* One MoE FFN layer (gate/up/down expert tensors + optional shared expert). */
+typedef struct {
+    moe_tensor  gate, up, down;        /* expert tensors: [E][F][H], [E][F][H], [E][H][F] */
+    int32_t     shared_type;           /* -1: no shared expert; otherwise the shared gate/up
+                                          have up.type and the shared down has down.type */
+    const void *shared_gate, *shared_up, *shared_down;
+    int64_t     H, F, n_experts, k;
+    int32_t     glu_op;
+    float       glu_limit;
+    int32_t     norm_w;
+} moe_layer_desc;
+
+/* No counterpart in the reference: bytes of caller-owned device workspace
+ * moe_b200_layer_decode needs for n_tok tokens. */
+size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok);
+
+/* No counterpart in the reference (the upstream graph around two
+ * MUL_MAT_ID calls): one MoE layer for n_tok <= 8 decode tokens, f32 in/out on
+ * device: route, fused gate/up GEMV + GLU, down GEMV, weighted combine plus the
+ * shared expert. Activations use llama.cpp CPU semantics (see src1_type F32).
+ * Allocates nothing: `workspace` is caller-owned device memory. */
+int moe_b200_layer_decode(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
+                          int64_t n_tok, void *workspace, size_t workspace_bytes, moe_stream_t stream);
+
+/* No counterpart in the reference: synthetic weights for tests and benches:
+ * n_rows rows of n_cols values ~ N(0, sigma) from a counter-based hash of
+ * (seed, element index), quantized on the device with this project's min/max
+ * quantizer (the same algorithm as the CPU oracle's). */
+int moe_b200_fill_quantized(int32_t type, void *dst, int64_t n_rows, int64_t n_cols, uint64_t seed,
+                            float sigma, moe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,109 @@
+"""The tiered hot-expert cache on the GPU: experts in pinned host memory read
+zero-copy through tagged table entries, a capped HBM pool, seeding, and the
+promotion step. After every step the DEVICE pointer tables are read back and
+compared bit-exactly with the policy model (oracle/cache_model.py), and the
+layer outputs are checked against the CPU oracle while experts move."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from cache_model import CacheModel, parse_seed
+from moe_data import activations, experts, rel_err, zipf_logits
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def _layer_np(t, H, F, E, seed):
+    return dict(H=H, F=F, E=E, type_gate=t, type_up=t, type_down=t,
+                gate=experts(t, E, F, H, seed), up=experts(t, E, F, H, seed + 1), down=experts(t, E, H, F, seed + 2),
+                shared_type=t, shared_gate=experts(t, 1, F, H, seed + 3)[0],
+                shared_up=experts(t, 1, F, H, seed + 4)[0], shared_down=experts(t, 1, H, F, seed + 5)[0])
+
+
+@pytest.mark.parametrize("n_tok,slots", [(1, 5), (4, 3)])
+def test_tiered_cache_matches_policy_model(pkg, cuda, tmp_path, n_tok, slots):
+    mc = pkg.moe_cache
+    t, H, F, E, k = O.Q4_K, 512, 256, 16, 4
+    L = _layer_np(t, H, F, E, seed=11)
+    L["k"] = k
+    seed_text = "blk.0.ffn_up_exps.weight 3,1,4,1,77\nblk.0.ffn_down_exps.weight 0,9\n"
+    seed_file = tmp_path / "seed.txt"
+    seed_file.write_text(seed_text)
+    mc.configure(enabled=True, slots=slots, budget_gb=1.0, seed_path=str(seed_file))
+    try:
+        layer = pkg.MoELayer(H, F, E, k, {"gate": t, "up": t, "down": t}, shared=True, host=True,
+                             weights={r: L[r] for r in ("gate", "up", "down", "shared_gate", "shared_up", "shared_down")})
+        assert all(mc.wants(layer.desc_t[r]) for r in ("gate", "up", "down"))
+        model = CacheModel(slots=slots, budget_bytes=1 << 30, seed=parse_seed(seed_text))
+        names = {r: f"blk.0.ffn_{r}_exps.weight" for r in ("gate", "up", "down")}
+        eb = {r: layer.w[r][0].numel() for r in ("gate", "up", "down")}
+        mt = {}
+        for step in range(24):
+            x = activations((n_tok, H), seed=100 + step)
+            logits = zipf_logits(n_tok, E, seed=7) + 0.3 * activations((n_tok, E), seed=200 + step)
+            out = layer.decode(torch.from_numpy(x).to(cuda), torch.from_numpy(logits).to(cuda))
+            ref, rid, _ = O.moe_layer(L, x, logits)
+            ids = layer.routing_of(n_tok)[0].cpu().numpy()
+            np.testing.assert_array_equal(ids, rid)
+            assert rel_err(out.cpu().numpy(), ref) < TOL
+            if step == 0:
+                for r in ("up", "gate", "down"):          # registration order of the library
+                    mt[r] = model.register(r, names[r], E, eb[r])
+            entries = ids.reshape(-1).tolist()
+            for r in ("up", "gate", "down"):
+                model.launch(mt[r], entries)
+            mc.step()
+            model.step()
+            for r in ("up", "gate", "down"):
+                tbl, n_slots, tid = mc.table(layer.desc_t[r])
+                assert n_slots == mt[r].n_slots and tid == mt[r].id
+                assert tbl == mt[r].slot_of, (step, r)
+        s = mc.stats()
+        assert s["promotions"] == model.promotions and s["hits"] == model.hits
+        assert s["promotions"] > 0 and s["evictions"] > 0
+        assert mc.device_error() == 0
+    finally:
+        mc.reset()
+
+
+def test_pin_host_and_wants(pkg, cuda):
+    mc = pkg.moe_cache
+    mc.configure(enabled=True)
+    try:
+        t, E, rows, K = O.Q8_0, 4, 8, 64
+        arr = np.ascontiguousarray(experts(t, E, rows, K, seed=1))
+        buf = torch.from_numpy(arr)                 # plain (unregistered) host memory
+        d = mc.expert_tensor(buf, t, K, rows, name="plain")
+        assert not mc.wants(d)
+        assert mc.pin_host(d)
+        assert mc.wants(d)
+        dev = buf.to(cuda)
+        assert mc.wants(mc.expert_tensor(dev, t, K, rows))
+        assert not mc.pin_host(mc.expert_tensor(dev, t, K, rows))
+        one = mc.expert_tensor(dev[:1].clone(), t, K, rows)
+        assert not mc.wants(one)                     # ne[2] < 2
+        view = mc.expert_tensor(dev, t, K, rows, flags=mc.TENSOR_VIEW)
+        assert not mc.wants(view)
+        torch.cuda.cudart().cudaHostUnregister(ctypes.c_void_p(buf.data_ptr() & ~4095))
+    finally:
+        mc.reset()
+
+
+def test_device_resident_tables_are_direct(pkg, cuda):
+    mc = pkg.moe_cache
+    mc.configure(enabled=True)
+    try:
+        t, H, F, E, k = O.Q2_K, 512, 256, 8, 2
+        layer = pkg.MoELayer(H, F, E, k, {"gate": t, "up": t, "down": t}, shared=False, seed=1)
+        layer.decode(torch.randn(1, H, device=cuda), torch.randn(1, E, device=cuda))
+        mc.step()                                     # no host tensors: no sync, nothing to promote
+        for r in ("gate", "up", "down"):
+            tbl, n_slots, _ = mc.table(layer.desc_t[r])
+            assert n_slots == 0 and tbl == [-2] * E
+        assert mc.stats()["misses"] == 0
+    finally:
+        mc.reset()

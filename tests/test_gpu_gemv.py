@@ -1,0 +1,247 @@
+"""Parity of the sm_100a pointer-table GEMV (ggml_cuda_moe_cache_mul_mat_vec_q)
+against the CPU oracle, through the C ABI.
+
+Tolerances (max |gpu - ref| / max |ref| per output vector):
+  TIGHT  = 1e-4  same activation quantization on both sides (F32 input: the
+                 kernel's in-kernel Q8_K/Q8_0 vs llama.cpp's CPU path; Q8_1
+                 input: exact dots on the same Q8_1 blocks). Only float
+                 summation order differs.
+  CROSS  = 3e-2  Q8_1-semantics GPU result vs llama.cpp CPU semantics
+                 (Q8_K / Q8_0 activations): the activation quantizers differ.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from moe_data import activations, distinct_ids, experts, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TIGHT = 1e-4
+CROSS = 3e-2
+
+
+def _dev(a, cuda):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def _run(pkg, cuda, t, W, K, rows, ids, src1_np, act, nchannels_y, gate=None, shared=None, x_bias=None,
+         gate_bias=None, glu_op=0, claim_gate_table=True):
+    """Run one MUL_MAT_ID through the C ABI. src1_np f32 [n_tok][nchannels_y][K]."""
+    mc = pkg.moe_cache
+    n_tok, n_used = ids.shape
+    Wd = _dev(W, cuda)
+    src0 = mc.expert_tensor(Wd, t, K, rows, name="w")
+    Gd = _dev(gate, cuda) if gate is not None else None
+    gdesc = mc.expert_tensor(Gd, t, K, rows, name="g") if (Gd is not None and claim_gate_table) else None
+    if act == "f32":
+        src1 = _dev(src1_np.astype(np.float32), cuda)
+        s_type, scol, sch = mc.F32, nchannels_y * K, K
+    else:
+        q = O.quantize_act(O.Q8_1, src1_np)                      # [n_tok][nch][K/32*36]
+        src1 = _dev(q, cuda)
+        s_type, scol, sch = mc.Q8_1, nchannels_y * (K // 32), K // 32
+    ids_d = _dev(ids, cuda)
+    dst = torch.full((n_tok, n_used, rows), float("nan"), device=cuda)
+    fd = None
+    sh = None
+    keep = []
+    if gate is not None or shared is not None or x_bias is not None:
+        if shared is not None:
+            sh_up = _dev(shared[0], cuda)
+            sh_gate = _dev(shared[1], cuda) if shared[1] is not None else None
+            sh = torch.full((n_tok, rows), float("nan"), device=cuda)
+            keep += [sh_up, sh_gate]
+        xb = _dev(x_bias, cuda) if x_bias is not None else None
+        gb = _dev(gate_bias, cuda) if gate_bias is not None else None
+        keep += [xb, gb]
+        fd = mc.fusion_device(gate=Gd, x_bias=xb, gate_bias=gb, glu_op=glu_op,
+                              shared_up=sh_up if shared is not None else None,
+                              shared_gate=sh_gate if shared is not None else None,
+                              shared_dst=sh, shared_stride_col_dst=rows)
+    mc.mul_mat_vec_q(src0, src1, s_type, ids_d, dst, ncols_dst=n_tok, nchannels_y=nchannels_y, nchannels_dst=n_used,
+                     stride_col_y=scol, stride_col_dst=n_used * rows, stride_channel_y=sch,
+                     stride_channel_dst=rows, ids_stride=n_used, fusion_gate=gdesc, fusion_dev=fd)
+    assert mc.device_error() == 0
+    torch.cuda.synchronize()
+    return dst.cpu().numpy(), (sh.cpu().numpy() if sh is not None else None)
+
+
+def _ref(t, W, K, src1_np, ids, act):
+    if act == "f32":
+        return O.mul_mat_id(t, W, K, src1_np, ids, exact=0)
+    return O.mul_mat_id_q8_1(t, W, K, O.quantize_act(O.Q8_1, src1_np), ids)
+
+
+@pytest.fixture(autouse=True)
+def _cache(pkg, cuda):
+    pkg.moe_cache.configure(enabled=True)
+    yield
+    pkg.moe_cache.reset()
+
+
+@pytest.mark.parametrize("t", O.WEIGHT_TYPES)
+@pytest.mark.parametrize("act", ["f32", "q8_1"])
+def test_unfused_down_style(pkg, cuda, t, act):
+    """nchannels_y = n_used (each pick its own input, like the down projection)."""
+    E, rows, K, n_tok, n_used = 12, 200, 512, 1, 8
+    W = experts(t, E, rows, K, seed=t)
+    ids = distinct_ids(n_tok, n_used, E, seed=1)
+    src1 = activations((n_tok, n_used, K), seed=2)
+    got, _ = _run(pkg, cuda, t, W, K, rows, ids, src1, act, nchannels_y=n_used)
+    ref = _ref(t, W, K, src1, ids, act)
+    assert rel_err(got, ref) < TIGHT
+
+
+@pytest.mark.parametrize("t", O.WEIGHT_TYPES)
+@pytest.mark.parametrize("n_tok", [1, 3, 8])
+def test_fused_gate_up_shared(pkg, cuda, t, n_tok):
+    """nchannels_y = 1, fused gate + SwiGLU + shared expert (config-2 shape in K)."""
+    E, rows, K, n_used = 16, 96, 1024, 4
+    W = experts(t, E, rows, K, seed=10 + t)
+    G = experts(t, E, rows, K, seed=20 + t)
+    SU = experts(t, 1, rows, K, seed=30 + t)[0]
+    SG = experts(t, 1, rows, K, seed=40 + t)[0]
+    ids = distinct_ids(n_tok, n_used, E, seed=3)
+    x = activations((n_tok, 1, K), seed=4)
+    got, gsh = _run(pkg, cuda, t, W, K, rows, ids, x, "f32", nchannels_y=1, gate=G, shared=(SU, SG))
+    up = O.mul_mat_id(t, W, K, x, ids)
+    gt = O.mul_mat_id(t, G, K, x, ids)
+    ref = O.glu(O.GLU_SWIGLU, gt, up)
+    assert rel_err(got, ref) < TIGHT
+    z = np.zeros((n_tok, 1), np.int32)
+    su = O.mul_mat_id(t, SU[None], K, x, z)[:, 0]
+    sg = O.mul_mat_id(t, SG[None], K, x, z)[:, 0]
+    assert rel_err(gsh, O.glu(O.GLU_SWIGLU, sg, su)) < TIGHT
+
+
+@pytest.mark.parametrize("glu_op", [0, 1, 2, 3, 4])
+def test_glu_ops_and_bias(pkg, cuda, glu_op):
+    t, E, rows, K, n_tok, n_used = O.Q4_K, 8, 64, 512, 2, 3
+    W = experts(t, E, rows, K, seed=5)
+    G = experts(t, E, rows, K, seed=6)
+    ids = distinct_ids(n_tok, n_used, E, seed=7)
+    x = activations((n_tok, 1, K), seed=8)
+    rng = np.random.default_rng(9)
+    xb = rng.normal(0, 0.1, (E, rows)).astype(np.float32)
+    gb = rng.normal(0, 0.1, (E, rows)).astype(np.float32)
+    got, _ = _run(pkg, cuda, t, W, K, rows, ids, x, "f32", 1, gate=G, x_bias=xb, gate_bias=gb, glu_op=glu_op)
+    up = O.mul_mat_id(t, W, K, x, ids) + xb[ids]
+    gt = O.mul_mat_id(t, G, K, x, ids) + gb[ids]
+    ref = O.glu(glu_op, gt, up, 0.0)
+    if glu_op == 3:   # SWIGLU_CLAMP with limit 0 -> all zeros
+        assert np.abs(got).max() == 0.0
+    else:
+        assert rel_err(got, ref) < TIGHT
+
+
+def test_bias_without_gate(pkg, cuda):
+    t, E, rows, K, n_tok, n_used = O.Q8_0, 6, 40, 256, 1, 2
+    W = experts(t, E, rows, K, seed=1)
+    ids = distinct_ids(n_tok, n_used, E, seed=2)
+    x = activations((n_tok, 1, K), seed=3)
+    xb = np.random.default_rng(4).normal(0, 0.5, (E, rows)).astype(np.float32)
+    got, _ = _run(pkg, cuda, t, W, K, rows, ids, x, "f32", 1, x_bias=xb)
+    assert rel_err(got, O.mul_mat_id(t, W, K, x, ids) + xb[ids]) < TIGHT
+
+
+def test_gate_without_table_uses_its_expert(pkg, cuda):
+    """A fused gate that is not registered is read at the routed expert's offset."""
+    t, E, rows, K, n_tok, n_used = O.Q5_K, 6, 32, 256, 1, 3
+    W = experts(t, E, rows, K, seed=1)
+    G = experts(t, E, rows, K, seed=2)
+    ids = distinct_ids(n_tok, n_used, E, seed=3)
+    x = activations((n_tok, 1, K), seed=4)
+    got, _ = _run(pkg, cuda, t, W, K, rows, ids, x, "f32", 1, gate=G, claim_gate_table=False)
+    ref = O.glu(0, O.mul_mat_id(t, G, K, x, ids), O.mul_mat_id(t, W, K, x, ids))
+    assert rel_err(got, ref) < TIGHT
+
+
+@pytest.mark.parametrize("t", [O.Q2_K, O.Q6_K, O.Q5_0])
+def test_duplicates_and_collisions(pkg, cuda, t):
+    """A token picking one expert twice, and tokens sharing experts (grouping)."""
+    E, rows, K, n_tok, n_used = 5, 72, 512, 8, 4
+    W = experts(t, E, rows, K, seed=1)
+    rng = np.random.default_rng(2)
+    ids = rng.integers(0, E, size=(n_tok, n_used)).astype(np.int32)
+    ids[0, :] = 3
+    for act in ("f32", "q8_1"):
+        x = activations((n_tok, n_used, K), seed=3)
+        got, _ = _run(pkg, cuda, t, W, K, rows, ids, x, act, nchannels_y=n_used)
+        assert rel_err(got, _ref(t, W, K, x, ids, act)) < TIGHT
+    x1 = activations((1, n_used, K), seed=4)
+    ids1 = np.array([[1, 1, 1, 2]], np.int32)
+    got, _ = _run(pkg, cuda, t, W, K, rows, ids1, x1, "f32", nchannels_y=n_used)
+    assert rel_err(got, _ref(t, W, K, x1, ids1, "f32")) < TIGHT
+
+
+@pytest.mark.parametrize("t", [O.Q2_K, O.Q4_0])
+def test_config_shapes(pkg, cuda, t):
+    """Config-2 shape (H=3072, F=768) for Q2_K; config-1 shape (H=2048, F=512) for Q4_0."""
+    H, F = (3072, 768) if t == O.Q2_K else (2048, 512)
+    E, n_used = 16, 8
+    Wd = experts(t, E, H, F, seed=1)          # down: rows H, K F
+    ids = distinct_ids(1, n_used, E, seed=2)
+    h = activations((1, n_used, F), seed=3)
+    got, _ = _run(pkg, cuda, t, Wd, F, H, ids, h, "f32", nchannels_y=n_used)
+    assert rel_err(got, _ref(t, Wd, F, h, ids, "f32")) < TIGHT
+    Wu = experts(t, E, F, H, seed=4)
+    x = activations((1, 1, H), seed=5)
+    got, _ = _run(pkg, cuda, t, Wu, H, F, ids, x, "f32", nchannels_y=1)
+    assert rel_err(got, _ref(t, Wu, H, x, ids, "f32")) < TIGHT
+
+
+@pytest.mark.parametrize("t", [O.Q2_K, O.Q4_K, O.Q8_0])
+def test_cross_semantics_tolerance(pkg, cuda, t):
+    """Q8_1-input results (reference GPU semantics) stay within CROSS of llama.cpp's CPU path."""
+    E, rows, K, n_tok, n_used = 8, 128, 1024, 2, 4
+    W = experts(t, E, rows, K, seed=1)
+    ids = distinct_ids(n_tok, n_used, E, seed=2)
+    x = activations((n_tok, 1, K), seed=3)
+    got, _ = _run(pkg, cuda, t, W, K, rows, ids, x, "q8_1", nchannels_y=1)
+    cpu = O.mul_mat_id(t, W, K, x, ids, exact=0)
+    err = rel_err(got, cpu)
+    print(f"cross-semantics rel err {O.TYPE_NAMES[t]}: {err:.3e}")
+    assert err < CROSS
+
+
+def test_edge_shapes(pkg, cuda):
+    """rows not a multiple of the tile, a single row, minimum K, one pick."""
+    for t, rows, K in ((O.Q3_K, 1, 256), (O.Q4_0, 3, 32), (O.Q6_K, 77, 256), (O.Q8_0, 1031, 64)):
+        E = 3
+        W = experts(t, E, rows, K, seed=rows)
+        ids = np.array([[2]], np.int32)
+        x = activations((1, 1, K), seed=1)
+        got, _ = _run(pkg, cuda, t, W, K, rows, ids, x, "f32", 1)
+        assert rel_err(got, _ref(t, W, K, x, ids, "f32")) < TIGHT
+
+
+def test_bad_expert_id_reports_device_error(pkg, cuda):
+    """An id outside [0, n_experts) is caught by the kernel's own check before
+    any table or weight access; the host reads the error word."""
+    mc = pkg.moe_cache
+    t, E, rows, K = O.Q4_0, 4, 16, 64
+    W = _dev(experts(t, E, rows, K, seed=1), cuda)
+    src0 = mc.expert_tensor(W, t, K, rows)
+    x = torch.zeros((1, K), device=cuda)
+    ids = torch.tensor([[E]], dtype=torch.int32, device=cuda)
+    dst = torch.full((1, 1, rows), 7.0, device=cuda)
+    mc.mul_mat_vec_q(src0, x, mc.F32, ids, dst, ncols_dst=1, nchannels_y=1, nchannels_dst=1, stride_col_y=K,
+                     stride_col_dst=rows, stride_channel_y=K, stride_channel_dst=rows, ids_stride=1)
+    assert mc.device_error() == 1
+    assert (dst == 7.0).all()
+    assert mc.device_error() == 0
+
+
+def test_unsupported_arguments_are_errors(pkg, cuda):
+    mc = pkg.moe_cache
+    t, E, rows, K = O.Q4_0, 4, 16, 64
+    W = _dev(experts(t, E, rows, K, seed=1), cuda)
+    src0 = mc.expert_tensor(W, t, K, rows)
+    x = torch.zeros((9, K), device=cuda)
+    ids = torch.zeros((9, 1), dtype=torch.int32, device=cuda)
+    dst = torch.zeros((9, 1, rows), device=cuda)
+    with pytest.raises(pkg.MoeError):
+        mc.mul_mat_vec_q(src0, x, mc.F32, ids, dst, ncols_dst=9, nchannels_y=1, nchannels_dst=1, stride_col_y=K,
+                         stride_col_dst=rows, stride_channel_y=K, stride_channel_dst=rows, ids_stride=1)
