@@ -70,10 +70,7 @@ __global__ void quantize_act_kernel(int act_type, const float *__restrict__ x, u
         const float d = amax / 127.f;
         const float id = d != 0.f ? 1.0f / d : 0.0f;
         blk[2 + lane] = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(v, id))));
-        if (lane == 0) {
-            const __half h = __float2half_rn(d);
-            memcpy(blk, &h, 2);
-        }
+        if (lane == 0) *reinterpret_cast<__half *>(blk) = __float2half_rn(d);   // 34-byte blocks: 2-aligned
     } else {   // Q8_1, llama.cpp CUDA quantize_q8_1 semantics
         uint8_t *blk = y + (row * nb_row + b) * 36;
         const float v = xr[lane];
@@ -86,11 +83,8 @@ __global__ void quantize_act_kernel(int act_type, const float *__restrict__ x, u
         const float d = amax / 127.f;
         const int8_t q = amax == 0.0f ? 0 : static_cast<int8_t>(roundf(v / d));
         blk[4 + lane] = static_cast<uint8_t>(q);
-        if (lane == 0) {
-            const __half hd = __float2half_rn(d), hs = __float2half_rn(sum);
-            memcpy(blk, &hd, 2);
-            memcpy(blk + 2, &hs, 2);
-        }
+        if (lane == 0)   // 36-byte blocks: 4-aligned
+            *reinterpret_cast<__half2 *>(blk) = __halves2half2(__float2half_rn(d), __float2half_rn(sum));
     }
 }
 

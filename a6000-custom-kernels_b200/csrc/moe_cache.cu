@@ -42,6 +42,9 @@ struct Entry {
     int type = 0;
     const char *data = nullptr;
     size_t expert_bytes = 0;
+    uint64_t row_bytes = 0;
+    int64_t rows = 0, cols = 0;
+    bool dead = false;            // retired: its address was reused by another tensor
     int n_experts = 0;
     int n_slots = 0;
     bool host = false;            // tiered (pinned host) vs HBM-resident
@@ -227,18 +230,51 @@ void load_seed() {
 
 char *host_tag(const char *p) { return reinterpret_cast<char *>(reinterpret_cast<uintptr_t>(p) | 1u); }
 
+// Frees an entry's device resources and takes it out of the lookup map. It
+// stays in g.all so tensor ids (and miss-log packing) remain stable.
+void retire(Entry *e) {
+    cudaDeviceSynchronize();   // no kernel may still read its table or pool
+    cudaFree(e->pool);
+    cudaFree(e->d_tbl);
+    cudaFree(e->d_stamps);
+    g.used -= static_cast<size_t>(e->n_slots) * e->expert_bytes;
+    e->pool = nullptr;
+    e->d_tbl = nullptr;
+    e->d_stamps = nullptr;
+    e->n_slots = 0;
+    e->expert_of.clear();
+    e->slot_of.assign(e->slot_of.size(), -1);
+    e->tbl_dirty = false;
+    e->host = false;
+    e->dead = true;
+    g.by_data.erase(e->data);
+}
+
 // reference moe_get_or_create (:525-622)
 int get_or_create(const moe_tensor *src0, cudaStream_t stream, Entry **out) {
     int rc = init_device_globals();
     if (rc) return rc;
     auto it = g.by_data.find(static_cast<const char *>(src0->data));
-    if (it != g.by_data.end()) { *out = it->second; return MOE_OK; }
+    if (it != g.by_data.end()) {
+        Entry *old = it->second;
+        if (old->type == src0->type && old->n_experts == src0->ne[2] && old->expert_bytes == src0->nb[2] &&
+            old->row_bytes == src0->nb[1] && old->rows == src0->ne[1] && old->cols == src0->ne[0]) {
+            *out = old;
+            return MOE_OK;
+        }
+        // the registry is keyed by data pointer (reference :530); a different
+        // tensor now lives at this address, so the old entry is retired
+        retire(old);
+    }
 
     Entry *e = new Entry();
     e->id = static_cast<int32_t>(g.all.size());
     e->type = src0->type;
     e->data = static_cast<const char *>(src0->data);
     e->expert_bytes = src0->nb[2];
+    e->row_bytes = src0->nb[1];
+    e->rows = src0->ne[1];
+    e->cols = src0->ne[0];
     e->n_experts = static_cast<int>(src0->ne[2]);
     e->host = ptr_kind(src0->data) == 1;
     e->name = src0->name ? src0->name : "";
@@ -387,7 +423,7 @@ int step_locked(cudaStream_t stream) {
         count = 0;
         if (cid < 0 || cid >= static_cast<int>(g.all.size())) continue;
         Entry *e = g.all[cid];
-        if (expert < 0 || expert >= e->n_experts || e->slot_of[expert] >= 0) continue;
+        if (e->dead || expert < 0 || expert >= e->n_experts || e->slot_of[expert] >= 0) continue;
         int slot = -1;
         const int rc = acquire_slot(e, stream, &slot);
         if (rc) return rc;
@@ -403,7 +439,7 @@ int step_locked(cudaStream_t stream) {
         g.promotions++;
     }
     for (Entry *e : g.all) {
-        if (!e->tbl_dirty) continue;
+        if (e->dead || !e->tbl_dirty) continue;
         CK(cudaMemcpyAsync(e->d_tbl, e->h_tbl.data(), sizeof(char *) * e->n_experts, cudaMemcpyHostToDevice, stream));
         e->tbl_dirty = false;
     }

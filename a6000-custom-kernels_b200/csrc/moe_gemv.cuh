@@ -31,7 +31,7 @@ constexpr int GEMV_MAX_SEGMENTS = 32;
 constexpr int GEMV_MAX_STAGES = 32;
 constexpr int GEMV_MAX_KEYS = 272;
 constexpr int GEMV_LOG_BASE = 2;         // stats: [0] misses, [1] hits, [2..] miss log
-constexpr int KEY_SHARED = 0xFFFF;
+constexpr uint32_t KEY_SHARED = 0xFFFFu;
 
 struct GemvArgs {
     // weights
@@ -486,7 +486,7 @@ struct GemvCtrl {
     int32_t uexp[GEMV_MAX_ENTRIES];
     int16_t goff[GEMV_MAX_ENTRIES + 2];
     int16_t shslot[8];
-    int32_t keys[GEMV_MAX_KEYS];
+    uint32_t keys[GEMV_MAX_KEYS];
     int32_t seg_g[GEMV_MAX_SEGMENTS], seg_r0[GEMV_MAX_SEGMENTS], seg_r1[GEMV_MAX_SEGMENTS];
     int32_t seg_t0[GEMV_MAX_SEGMENTS + 1];
     int32_t n_unique, n_seg, n_tiles, n_keys, fail;
@@ -628,7 +628,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
                 for (int j = C.goff[g]; j < C.goff[g + 1]; ++j) {
                     const int e = C.gmem[j];
                     const int t = e / nch, p = e % nch;
-                    const int key = ((p % a.nchannels_y) << 16) | t;
+                    const uint32_t key = (static_cast<uint32_t>(p % a.nchannels_y) << 16) | static_cast<uint32_t>(t);
                     int v = 0;
                     while (v < nk && C.keys[v] != key) ++v;
                     if (v == nk) {
@@ -639,7 +639,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
                 }
             } else {
                 for (int t = 0; t < a.ncols_dst; ++t) {
-                    const int key = a.shared_y ? ((KEY_SHARED << 16) | t) : t;
+                    const uint32_t key = a.shared_y ? ((KEY_SHARED << 16) | static_cast<uint32_t>(t)) : static_cast<uint32_t>(t);
                     int v = 0;
                     while (v < nk && C.keys[v] != key) ++v;
                     if (v == nk) {
@@ -681,16 +681,19 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
             tile_coords(i, g, row0, nr);
             const char *src[2] = {nullptr, nullptr};
             bool dev[2] = {true, true};
+            bool host16[2] = {false, false};
             if (g < U) {
                 const int x = C.uexp[g];
                 const uintptr_t p = reinterpret_cast<uintptr_t>(a.tbl[x]);
                 src[0] = reinterpret_cast<const char *>(p & ~static_cast<uintptr_t>(1));
                 dev[0] = !(p & 1u) && a.tma_main;
+                host16[0] = (p & 1u) && a.tma_main;
                 if (a.use_gate) {
                     if (a.tbl_gate) {
                         const uintptr_t pg = reinterpret_cast<uintptr_t>(a.tbl_gate[x]);
                         src[1] = reinterpret_cast<const char *>(pg & ~static_cast<uintptr_t>(1));
                         dev[1] = !(pg & 1u) && a.tma_gate;
+                        host16[1] = (pg & 1u) && a.tma_gate;
                     } else {
                         src[1] = a.gate_dense + static_cast<uint64_t>(x) * a.gate_expert_bytes;
                         dev[1] = a.tma_gate;
@@ -708,15 +711,30 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
                 const char *sp = src[pidx] + static_cast<uint64_t>(row0) * a.row_bytes;
                 const uint32_t bytes = static_cast<uint32_t>(nr) * a.row_bytes;
                 uint8_t *dp = stage + pidx * a.part_bytes;
-                const uintptr_t off = reinterpret_cast<uintptr_t>(sp) & 15u;
+                const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
+                const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
                 if (dev[pidx]) {
-                    tx += static_cast<uint32_t>(((reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15)) -
-                                                (reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15)));
+                    tx += static_cast<uint32_t>(a1 - a0);
+                } else if (host16[pidx]) {
+                    // the same 16-byte aligned range a bulk copy would move (it
+                    // stays inside the expert: 16-byte aligned base and size)
+                    const uint4 *s4 = reinterpret_cast<const uint4 *>(a0);
+                    uint4 *d4 = reinterpret_cast<uint4 *>(dp);
+                    const uint32_t n4 = static_cast<uint32_t>(a1 - a0) / 16u;
+                    for (uint32_t j = lane; j < n4; j += 32) d4[j] = s4[j];
                 } else {
-                    // 2-byte granularity keeps the copy inside [sp, sp + bytes)
-                    const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sp);
-                    uint16_t *d16 = reinterpret_cast<uint16_t *>(dp + off);
-                    for (uint32_t j = lane; j < bytes / 2; j += 32) d16[j] = s16[j];
+                    // 4-byte words when the source allows, else 2-byte units;
+                    // both keep the copy inside [sp, sp + bytes)
+                    const uintptr_t off = reinterpret_cast<uintptr_t>(sp) & 15u;
+                    if (((reinterpret_cast<uintptr_t>(sp) | bytes) & 3u) == 0) {
+                        const uint32_t *s32 = reinterpret_cast<const uint32_t *>(sp);
+                        uint32_t *d32 = reinterpret_cast<uint32_t *>(dp + off);
+                        for (uint32_t j = lane; j < bytes / 4; j += 32) d32[j] = s32[j];
+                    } else {
+                        const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sp);
+                        uint16_t *d16 = reinterpret_cast<uint16_t *>(dp + off);
+                        for (uint32_t j = lane; j < bytes / 2; j += 32) d16[j] = s16[j];
+                    }
                 }
             }
             __syncwarp();
@@ -758,8 +776,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
         const int nb = q81 ? K / 32 : (kq ? K / 256 : K / 32);
         for (int job = warp; job < nk * nb; job += GEMV_CONSUMER_WARPS) {
             const int v = job / nb, b = job % nb;
-            const int key = C.keys[v];
-            const int kc = key >> 16, t = key & 0xFFFF;
+            const uint32_t key = C.keys[v];
+            const uint32_t kc = key >> 16;
+            const int t = static_cast<int>(key & 0xFFFFu);
             uint8_t *slot = act_area + static_cast<size_t>(v) * sb_bytes;
             int8_t *q = reinterpret_cast<int8_t *>(slot);
             int16_t *bs = reinterpret_cast<int16_t *>(slot + K);
@@ -767,7 +786,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
             int64_t off;
             const void *base;
             if (kc == KEY_SHARED) { base = a.shared_y; off = t * a.shared_y_stride_col; }
-            else { base = a.y; off = kc * a.stride_channel_y + t * a.stride_col_y; }
+            else { base = a.y; off = static_cast<int64_t>(kc) * a.stride_channel_y + t * a.stride_col_y; }
             if (q81) {
                 stage_q81_block(reinterpret_cast<const uint8_t *>(base) + off * 36, q, bs, sc, b, lane);
             } else if (kq) {

@@ -85,10 +85,22 @@ class MoELayer:
                                           _ptr(ws), ws.numel(), _stream(stream)))
         return out
 
+    def intermediates(self, n_tok):
+        """Views of the last decode's workspace (layout of moe_b200_layer_decode):
+        ids [n][k], weights [n][k], h [n][k][F] (GLU output), hs [n][F] (shared
+        GLU output), y [n][k][H] (down outputs), ys [n][H] (shared down)."""
+        ws = self._ws[n_tok]
+        n, k, F, H = n_tok, self.k, self.F, self.H
+        out, off = [], 0
+        for count, dt, shape in ((n * k, torch.int32, (n, k)), (n * k, torch.float32, (n, k)),
+                                 (n * k * F, torch.float32, (n, k, F)), (n * F, torch.float32, (n, F)),
+                                 (n * k * H, torch.float32, (n, k, H)), (n * H, torch.float32, (n, H))):
+            nbytes = 4 * count
+            out.append(ws[off: off + nbytes].view(dt).view(shape))
+            off += (nbytes + 255) // 256 * 256
+        return tuple(out)
+
     def routing_of(self, n_tok):
         """(ids, weights) views of the last decode's routing in the workspace."""
-        ws = self._ws[n_tok]
-        ids = ws[: n_tok * self.k * 4].view(torch.int32).view(n_tok, self.k)
-        off = (n_tok * self.k * 4 + 255) // 256 * 256
-        w = ws[off: off + n_tok * self.k * 4].view(torch.float32).view(n_tok, self.k)
+        ids, w = self.intermediates(n_tok)[:2]
         return ids, w

@@ -917,15 +917,16 @@ int orc_moe_layer(const orc_layer *L, const float *x, const float *logits, int64
             out[t * H + r] = acc;
         }
     if (L->shared_type >= 0) {
-        const int st = L->shared_type;
+        /* the shared expert's gate/up/down have the routed gate/up/down types */
+        const int tg = L->type_gate, tu = L->type_up, td = L->type_down;
         const void *sg[1] = {L->shared_gate}, *su[1] = {L->shared_up}, *sd[1] = {L->shared_down};
         int32_t *zid = (int32_t *)calloc((size_t)n_tok, sizeof(int32_t));
         float *sgo = sh, *suo = sh + n_tok * F, *sdo = sh + 2 * n_tok * F;
-        rc = orc_mul_mat_id(st, ACT(st), EX(st), sg, 1, H, F, orc_row_size(st, H), x, 1, n_tok, zid, 1, sgo, n_threads);
-        if (!rc) rc = orc_mul_mat_id(st, ACT(st), EX(st), su, 1, H, F, orc_row_size(st, H), x, 1, n_tok, zid, 1, suo, n_threads);
+        rc = orc_mul_mat_id(tg, ACT(tg), EX(tg), sg, 1, H, F, orc_row_size(tg, H), x, 1, n_tok, zid, 1, sgo, n_threads);
+        if (!rc) rc = orc_mul_mat_id(tu, ACT(tu), EX(tu), su, 1, H, F, orc_row_size(tu, H), x, 1, n_tok, zid, 1, suo, n_threads);
         if (!rc) {
             for (int64_t i = 0; i < n_tok * F; ++i) sgo[i] = orc_glu(L->glu_op, sgo[i], suo[i], L->glu_limit);
-            rc = orc_mul_mat_id(st, ACT(st), EX(st), sd, 1, F, H, orc_row_size(st, F), sgo, 1, n_tok, zid, 1, sdo, n_threads);
+            rc = orc_mul_mat_id(td, ACT(td), EX(td), sd, 1, F, H, orc_row_size(td, F), sgo, 1, n_tok, zid, 1, sdo, n_threads);
         }
         if (!rc)
             for (int64_t i = 0; i < n_tok * H; ++i) out[i] += sdo[i];

@@ -103,7 +103,7 @@ typedef struct {
     const void *const *gate;   /* [n_experts] -> [F][H] */
     const void *const *up;     /* [n_experts] -> [F][H] */
     const void *const *down;   /* [n_experts] -> [H][F] */
-    int          shared_type;  /* -1 = no shared expert */
+    int          shared_type;  /* -1: none; else present, with the routed tensors' types */
     const void  *shared_gate, *shared_up, *shared_down;
     int64_t      H, F, n_experts, k;
     int          glu_op;

@@ -1,15 +1,16 @@
 """A full MoE layer (route, fused gate/up + SwiGLU + shared expert, down,
-weighted combine) on the GPU against the oracle's llama.cpp-order layer.
-Routing ids are compared bit-exactly; outputs within 1e-4 of max |ref|."""
+weighted combine) on the GPU against the oracle's llama.cpp-order layer, stage
+by stage (tests/layer_check.py): routing ids bit-exact, every stage within
+1e-4 of max |ref|, the end-to-end output within 1e-2."""
 import numpy as np
 import pytest
 import torch
 
 import oracle as O
-from moe_data import activations, experts, rel_err, zipf_logits
+from layer_check import check_layer
+from moe_data import activations, experts, zipf_logits
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-4
 
 
 def _layer_np(types, H, F, E, seed):
@@ -36,14 +37,11 @@ def test_layer_decode_matches_oracle(pkg, cuda, types, n_tok):
     L["k"] = k
     x = activations((n_tok, H), seed=1)
     logits = zipf_logits(n_tok, E, seed=2)
-    ref, rid, rw = O.moe_layer(L, x, logits)
     layer = pkg.MoELayer(H, F, E, k, {"gate": types[0], "up": types[1], "down": types[2]}, shared=True,
                          weights={r: L[r] for r in ("gate", "up", "down", "shared_gate", "shared_up", "shared_down")})
     out = layer.decode(torch.from_numpy(x).to(cuda), torch.from_numpy(logits).to(cuda))
     assert pkg.moe_cache.device_error() == 0
-    ids, w = layer.routing_of(n_tok)
-    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
-    assert rel_err(out.cpu().numpy(), ref) < TOL
+    check_layer(layer, L, x, logits, out.cpu().numpy())
 
 
 def test_config2_layer_full_expert_count(pkg, cuda):
@@ -58,7 +56,4 @@ def test_config2_layer_full_expert_count(pkg, cuda):
     for r in ("gate", "up", "down"):
         L[r] = layer.w[r].cpu().numpy()
         L["shared_" + r] = layer.shared[r].cpu().numpy()
-    ref, rid, _ = O.moe_layer(L, x, logits)
-    ids, _ = layer.routing_of(n_tok)
-    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
-    assert rel_err(out, ref) < TOL
+    check_layer(layer, L, x, logits, out)
