@@ -207,6 +207,29 @@ size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok)
 int moe_b200_layer_decode(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
                           int64_t n_tok, void *workspace, size_t workspace_bytes, moe_stream_t stream);
 
+/* No counterpart in the reference. A layer decode for callers that cannot
+ * allocate device memory where they run it: engines that reserve all device
+ * memory at start-up and own every byte, plugins whose host framework forbids
+ * allocations inside its compute callback, or loops that must not take the
+ * implicit synchronisation an allocation can cause. Same kernels and result as
+ * moe_b200_layer_decode, but every piece of scratch (routing ids and weights,
+ * GLU outputs, per-pick down outputs, expert pointer tables, an error word)
+ * lives in one fixed file-scope device array of about 2.3 MB that every GPU
+ * loading the library holds until exit; nothing is allocated and the
+ * hot-expert cache is not used (expert tensors must be in device memory; no
+ * stamps or hit/miss bookkeeping). Limits: n_tok <= 8, k <= 8, H <= 4096,
+ * F <= 4096, n_experts <= 1024; larger requests return MOE_ERR_UNSUPPORTED.
+ * The first call on a device looks up the array's address (cudaGetSymbolAddress)
+ * and should come before any stream capture. All calls share the array and it
+ * keeps the last call's contents, so calls that overlap on the GPU race. */
+int moe_b200_layer_decode_noalloc(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
+                                  int64_t n_tok, moe_stream_t stream);
+
+/* No counterpart in the reference: synchronise `stream`, then read the
+ * moe_b200_layer_decode_noalloc device error word (0 = none; cleared by each
+ * no-alloc call). */
+int moe_b200_noalloc_device_error(moe_stream_t stream, int32_t *code);
+
 /* No counterpart in the reference: synthetic weights for tests and benches:
  * n_rows rows of n_cols values ~ N(0, sigma) from a counter-based hash of
  * (seed, element index), quantized on the device with this project's min/max
