@@ -81,13 +81,42 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
+// try_wait with a suspend-time hint: the warp sleeps in hardware until the
+// phase completes or about hint_ns pass, instead of spinning on the issue slots
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Time limits are counted in SM clock cycles (clock64), taking 2 cycles per
+// nanosecond: %globaltimer was seen advancing far slower than real time on
+// this hardware, so it cannot bound a wait.
+__device__ __forceinline__ uint64_t timeout_cycles(uint64_t timeout_ns) { return 2ull * timeout_ns; }
+
+// Sleeping wait (for consumers): gives up after ~timeout_ns.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = clock64(), lim = timeout_cycles(timeout_ns);
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if (static_cast<uint64_t>(clock64()) - t0 > lim) return false;
+    }
+}
+
 // Wait for the phase with the given parity; gives up after ~timeout_ns.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
+    const uint64_t t0 = clock64(), lim = timeout_cycles(timeout_ns);
     for (uint32_t i = 0;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 255u && global_timer_ns() - t0 > timeout_ns) return false;
+        if ((i & 255u) == 255u && static_cast<uint64_t>(clock64()) - t0 > lim) return false;
     }
 }
 

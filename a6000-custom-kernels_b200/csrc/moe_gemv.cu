@@ -1,5 +1,7 @@
 // moe_gemv.cu -- launch planning and instantiations of the pointer-table GEMV
 // (the B200 counterpart of moe_cache_gemv_launch, kernels/moe-cache.cu:781-819).
+#include <cstdio>
+
 #include "moe_aux.h"
 #include "moe_gemv.cuh"
 
@@ -10,6 +12,8 @@ namespace {
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kActBudget = 96 * 1024;
 constexpr int kTargetStage = 8 * 1024;
+
+char g_launch_diag[256];   // attributes of the last failed launch
 
 template <int TYPE, int ACT, int NMX>
 cudaError_t launch_t(const GemvArgs &a, int grid, size_t smem, cudaStream_t st) {
@@ -24,7 +28,15 @@ cudaError_t launch_t(const GemvArgs &a, int grid, size_t smem, cudaStream_t st) 
         configured[dev] = true;
     }
     kern<<<grid, GEMV_THREADS, smem, st>>>(a);
-    return cudaGetLastError();
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        cudaFuncAttributes fa{};
+        cudaFuncGetAttributes(&fa, kern);
+        snprintf(g_launch_diag, sizeof(g_launch_diag),
+                 "grid=%d threads=%d smem=%zu regs=%d maxThreads=%d maxDynSmem=%d local=%zu", grid, GEMV_THREADS,
+                 smem, fa.numRegs, fa.maxThreadsPerBlock, fa.maxDynamicSharedSizeBytes, fa.localSizeBytes);
+    }
+    return e;
 }
 
 template <int TYPE>
@@ -90,8 +102,20 @@ int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **wh
     while (L > 1 && T % L) L >>= 1;
     const int RP = 32 / L;
     const int parts = a.use_gate ? 2 : 1;
-    int rpt = (kTargetStage / static_cast<int>(a.row_bytes * parts)) / RP * RP;
+    const bool has_shared_ = a.shared_up != nullptr;
+    const int64_t groups_bound_ = (N < a.n_experts ? N : a.n_experts) + (has_shared_ ? 1 : 0);
+    const int64_t total_rows = groups_bound_ * a.nrows;
+    if (total_rows >= (int64_t{1} << 31)) { *why = "row space of the routed experts exceeds 2^31 rows"; return -2; }
+    const int n_sm_ = sm_count();
+    const int64_t grid_ = (total_rows + RP - 1) / RP < n_sm_ ? (total_rows + RP - 1) / RP : n_sm_;
+    // tiles small enough that every consumer warp of a CTA gets one, large
+    // enough to keep the bulk copies efficient (<= ~8 KB per stage)
+    const int64_t rows_cta = (total_rows + grid_ - 1) / grid_;
+    int rpt_max = (kTargetStage / static_cast<int>(a.row_bytes * parts)) / RP * RP;
+    if (rpt_max < RP) rpt_max = RP;
+    int rpt = static_cast<int>(rows_cta / GEMV_CONSUMER_WARPS) / RP * RP;
     if (rpt < RP) rpt = RP;
+    if (rpt > rpt_max) rpt = rpt_max;
     if (rpt > a.nrows) rpt = a.nrows;
     const uint32_t part_bytes = ((static_cast<uint32_t>(rpt) * a.row_bytes + 15u) & ~15u) + 32u;
     const uint32_t slot_bytes = (static_cast<uint32_t>(a.K + a.K / 8 + a.K / 8) + 15u) & ~15u;
@@ -120,10 +144,7 @@ int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **wh
     a.ctrl_bytes = ctrl;
     if (a.timeout_ns == 0) a.timeout_ns = 2000000000ull;
 
-    const int64_t groups_bound = (N < a.n_experts ? N : a.n_experts) + (has_shared ? 1 : 0);
-    const int64_t tiles_bound = (groups_bound * a.nrows + rpt - 1) / rpt;
-    const int n_sm = sm_count();
-    const int grid = static_cast<int>(tiles_bound < n_sm ? tiles_bound : n_sm);
+    const int grid = static_cast<int>(grid_);
 
     const int nmx = a.ncols_dst == 1 ? 1 : 8;
     cudaError_t e;
@@ -138,7 +159,7 @@ int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **wh
         case T_Q6_K: e = dispatch_act<T_Q6_K>(act, nmx, a, grid, smem, st); break;
         default: *why = "unsupported weight type"; return -2;
     }
-    if (e != cudaSuccess) { *cuda_err = e; *why = "GEMV launch failed"; return -3; }
+    if (e != cudaSuccess) { *cuda_err = e; *why = g_launch_diag; return -3; }
     return 0;
 }
 

@@ -13,10 +13,12 @@
 //  * a producer warp streams contiguous row tiles into a shared-memory ring
 //    with 1-D bulk copies (cp.async.bulk, mbarrier completion, no multicast);
 //    host-tagged experts are copied by the same warp with plain loads;
-//  * eight consumer warps dequantize in registers and run dp4a/dp2a integer
-//    dots against activations staged once per CTA in shared memory, reduce
-//    with warp shuffles and apply the fused bias / GLU / shared-expert
-//    epilogue of the reference (:241-284);
+//  * sixteen consumer warps dequantize in registers and run dp4a/dp2a integer
+//    dots against activations staged once per CTA in shared memory, stored in
+//    16-byte pieces interleaved across K-chunks so lanes working on different
+//    chunks hit different banks; a fused gate/up pair shares its activation
+//    loads; rows reduce with warp shuffles and the epilogue applies the
+//    reference's bias / GLU / shared-expert fusion (:241-284);
 //  * the first CTA does the reference's per-(pick, token) bookkeeping: stamps,
 //    hit count and miss log (:163-198).
 #pragma once
@@ -24,11 +26,11 @@
 
 namespace moe {
 
-constexpr int GEMV_CONSUMER_WARPS = 8;
+constexpr int GEMV_CONSUMER_WARPS = 16;
 constexpr int GEMV_THREADS = 32 * (GEMV_CONSUMER_WARPS + 1);
 constexpr int GEMV_MAX_ENTRIES = 256;    // ncols_dst * nchannels_dst
 constexpr int GEMV_MAX_SEGMENTS = 32;
-constexpr int GEMV_MAX_STAGES = 32;
+constexpr int GEMV_MAX_STAGES = 48;
 constexpr int GEMV_MAX_KEYS = 272;
 constexpr int GEMV_LOG_BASE = 2;         // stats: [0] misses, [1] hits, [2..] miss log
 constexpr uint32_t KEY_SHARED = 0xFFFFu;
@@ -78,31 +80,58 @@ struct GemvArgs {
 };
 
 // ---------------------------------------------------------------------------
-// activations staged in shared memory, one slot per distinct input vector:
-//   int8 q[K] | int16 bsum16[K/16] | f32 scale[K/32]
-// scale is per 32 (Q8_0 / Q8_1) or per 256 (Q8_K, first K/256 entries).
+// Activations staged in shared memory, one slot per distinct input vector:
+//   int8 q[K] in 16-byte pieces: piece p of K-chunk c at unit p * NC + c,
+//        a chunk being the CE elements one task reads (NC = K / CE)
+//   int16 bsum16[K/16] (natural order)
+//   f32 scale[K/32]: per 32 (Q8_0 / Q8_1) or per 256 (Q8_K, first K/256)
 // ---------------------------------------------------------------------------
+template <int TYPE> struct chunk_of {
+    static constexpr int CE = is_kquant(TYPE) ? ((TYPE == T_Q4_K || TYPE == T_Q5_K) ? 64 : 128) : 32;
+};
+
+template <int TYPE>
+__device__ __forceinline__ uint32_t act_offset(int e, int NC) {
+    constexpr int CE = chunk_of<TYPE>::CE;
+    const int c = e / CE, o = e % CE;
+    return static_cast<uint32_t>(((o >> 4) * NC + c) * 16 + (o & 15));
+}
+
 template <int NMX>
 struct Acts {
-    const int8_t *q[NMX];
+    const int4 *q[NMX];       // piece units of the slot
     const int16_t *bs[NMX];
     const float *sc[NMX];
-    int nm;
+    int nm, NC;
 };
 
 __device__ __forceinline__ int bs_lo(int w) { return static_cast<int16_t>(w & 0xFFFF); }
 __device__ __forceinline__ int bs_hi(int w) { return w >> 16; }
 
-// Q8_K block (256) from f32: llama.cpp quantize_row_q8_K_ref, bit-exact.
-__device__ __forceinline__ void stage_q8K_block(const float *x, int8_t *q, int16_t *bs, float *sc, int b, int lane) {
+// Q8_K block (256 f32 at x): llama.cpp quantize_row_q8_K_ref, bit-exact. Lane l
+// holds elements 4l..4l+3 and 128+4l..128+4l+3 (coalesced float4 loads when x
+// is 16-byte aligned).
+template <int TYPE>
+__device__ __forceinline__ void stage_q8K_block(const float *x, bool al16, int8_t *q, int16_t *bs, float *sc, int b,
+                                                int lane, int NC) {
     float v[8];
+    const float *xb = x + b * 256;
+    if (al16) {
+        const float4 u0 = reinterpret_cast<const float4 *>(xb)[lane];
+        const float4 u1 = reinterpret_cast<const float4 *>(xb + 128)[lane];
+        v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+        v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { v[j] = xb[4 * lane + j]; v[4 + j] = xb[128 + 4 * lane + j]; }
+    }
     float amax = 0.f, mval = 0.f;
     int midx = 1 << 30;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        v[j] = x[b * 256 + lane * 8 + j];
+        const int idx = j < 4 ? 4 * lane + j : 128 + 4 * lane + (j - 4);
         const float ax = fabsf(v[j]);
-        if (ax > amax) { amax = ax; mval = v[j]; midx = lane * 8 + j; }
+        if (ax > amax) { amax = ax; mval = v[j]; midx = idx; }   // ascending idx within the lane
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
@@ -111,7 +140,7 @@ __device__ __forceinline__ void stage_q8K_block(const float *x, int8_t *q, int16
         const int oi = __shfl_xor_sync(0xffffffffu, midx, off);
         if (oa > amax || (oa == amax && oi < midx)) { amax = oa; mval = ov; midx = oi; }
     }
-    int8_t qq[8];
+    int qq[8];
     float d = 0.f;
     if (amax == 0.f) {
 #pragma unroll
@@ -121,26 +150,37 @@ __device__ __forceinline__ void stage_q8K_block(const float *x, int8_t *q, int16
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int r = nearest_int_dev(__fmul_rn(iscale, v[j]));
-            qq[j] = static_cast<int8_t>(r < 127 ? r : 127);
+            qq[j] = r < 127 ? r : 127;
         }
         d = 1.f / iscale;
     }
     uint32_t w0 = 0, w1 = 0;
-    int s = 0;
+    int s0 = 0, s1 = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        w0 |= (static_cast<uint32_t>(static_cast<uint8_t>(qq[j])) << (8 * j));
-        w1 |= (static_cast<uint32_t>(static_cast<uint8_t>(qq[j + 4])) << (8 * j));
-        s += qq[j] + qq[j + 4];
+        w0 |= (static_cast<uint32_t>(qq[j]) & 0xFFu) << (8 * j);
+        w1 |= (static_cast<uint32_t>(qq[j + 4]) & 0xFFu) << (8 * j);
+        s0 += qq[j];
+        s1 += qq[j + 4];
     }
-    reinterpret_cast<uint2 *>(q + b * 256)[lane] = make_uint2(w0, w1);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    if ((lane & 1) == 0) bs[b * 16 + (lane >> 1)] = static_cast<int16_t>(s);
+    const int e0 = b * 256 + 4 * lane, e1 = e0 + 128;
+    *reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(q) + act_offset<TYPE>(e0, NC)) = w0;
+    *reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(q) + act_offset<TYPE>(e1, NC)) = w1;
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    if ((lane & 3) == 0) {
+        bs[b * 16 + (lane >> 2)] = static_cast<int16_t>(s0);
+        bs[b * 16 + 8 + (lane >> 2)] = static_cast<int16_t>(s1);
+    }
     if (lane == 0) sc[b] = d;
 }
 
 // Q8_0 block (32) from f32: llama.cpp quantize_row_q8_0_ref, bit-exact.
-__device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16_t *bs, float *sc, int b, int lane) {
+template <int TYPE>
+__device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16_t *bs, float *sc, int b, int lane,
+                                                int NC) {
     const float v = x[b * 32 + lane];
     float amax = fabsf(v);
 #pragma unroll
@@ -148,7 +188,7 @@ __device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16
     const float d = amax / 127.f;
     const float id = d != 0.f ? 1.0f / d : 0.0f;
     const int qi = static_cast<int>(roundf(__fmul_rn(v, id)));
-    q[b * 32 + lane] = static_cast<int8_t>(qi);
+    q[act_offset<TYPE>(b * 32 + lane, NC)] = static_cast<int8_t>(qi);
     int s = qi;
 #pragma unroll
     for (int off = 8; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
@@ -157,12 +197,14 @@ __device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16
 }
 
 // Q8_1 block (36 bytes) as given: copy qs, scale = d, per-16 sums.
-__device__ __forceinline__ void stage_q81_block(const uint8_t *yb, int8_t *q, int16_t *bs, float *sc, int b, int lane) {
+template <int TYPE>
+__device__ __forceinline__ void stage_q81_block(const uint8_t *yb, int8_t *q, int16_t *bs, float *sc, int b, int lane,
+                                                int NC) {
     const uint8_t *blk = yb + static_cast<size_t>(b) * 36;
     int s = 0;
     if (lane < 8) {
         const uint32_t w = ld_u32(blk + 4 + 4 * lane);
-        reinterpret_cast<uint32_t *>(q + b * 32)[lane] = w;
+        *reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(q) + act_offset<TYPE>(b * 32 + 4 * lane, NC)) = w;
         s = dp4a_ss(static_cast<int>(w), 0x01010101, 0);
     }
     s += __shfl_xor_sync(0xffffffffu, s, 1);
@@ -173,305 +215,361 @@ __device__ __forceinline__ void stage_q81_block(const uint8_t *yb, int8_t *q, in
 }
 
 // ---------------------------------------------------------------------------
-// per-type task dots. A task is a fixed slice of one weight row; the lane adds
-// its contribution for every member activation vector into acc[m].
+// Per-type task dots. A task is a fixed K-slice of a weight row (one K-chunk).
+// RL weight rows (the up and the gate row of one output row when fused) share
+// the activation loads; the lane adds its contribution for every member
+// vector m into acc[r][m].
 // ---------------------------------------------------------------------------
 
 // Q4_0 / Q5_0 / Q8_0: task = one 32-element block
-template <int TYPE, int NMX>
-__device__ __forceinline__ void task_legacy(const uint8_t *row, int b, const Acts<NMX> &A, float (&acc)[NMX]) {
-    const uint8_t *blk = row + b * fmt<TYPE>::bytes;
-    const float dw = ld_half(blk);
-    uint32_t lo[4], hi[4];
-    uint32_t w8[8];
-    if constexpr (TYPE == T_Q4_0) {
-        uint32_t w[4];
-        ld_words_a2<4>(blk + 2, w);
+template <int TYPE, int NMX, int RL>
+__device__ __forceinline__ void task_legacy(const uint8_t *const (&rows)[RL], int b, const Acts<NMX> &A,
+                                            float (&acc)[RL][NMX]) {
+    float dw[RL];
+    uint32_t lo[RL][4], hi[RL][4], w8[RL][8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) { lo[i] = w[i] & 0x0F0F0F0Fu; hi[i] = (w[i] >> 4) & 0x0F0F0F0Fu; }
-    } else if constexpr (TYPE == T_Q5_0) {
-        uint32_t w[5];
-        ld_words_a2<5>(blk + 2, w);
-        const uint32_t qh = w[0];
+    for (int r = 0; r < RL; ++r) {
+        const uint8_t *blk = rows[r] + b * fmt<TYPE>::bytes;
+        dw[r] = ld_half(blk);
+        if constexpr (TYPE == T_Q4_0) {
+            uint32_t w[4];
+            ld_words_a2<4>(blk + 2, w);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lo[i] = (w[1 + i] & 0x0F0F0F0Fu) | spread4_bit4(qh >> (4 * i));
-            hi[i] = ((w[1 + i] >> 4) & 0x0F0F0F0Fu) | spread4_bit4(qh >> (16 + 4 * i));
+            for (int i = 0; i < 4; ++i) { lo[r][i] = w[i] & 0x0F0F0F0Fu; hi[r][i] = (w[i] >> 4) & 0x0F0F0F0Fu; }
+        } else if constexpr (TYPE == T_Q5_0) {
+            uint32_t w[5];
+            ld_words_a2<5>(blk + 2, w);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lo[r][i] = (w[1 + i] & 0x0F0F0F0Fu) | spread4_bit4(w[0] >> (4 * i));
+                hi[r][i] = ((w[1 + i] >> 4) & 0x0F0F0F0Fu) | spread4_bit4(w[0] >> (16 + 4 * i));
+            }
+        } else {
+            ld_words_a2<8>(blk + 2, w8[r]);
         }
-    } else {
-        ld_words_a2<8>(blk + 2, w8);
     }
 #pragma unroll
     for (int m = 0; m < NMX; ++m) {
         if (m >= A.nm) break;
-        const int4 *aq = reinterpret_cast<const int4 *>(A.q[m] + b * 32);
-        const int4 a0 = aq[0], a1 = aq[1];
-        int S;
-        if constexpr (TYPE == T_Q8_0) {
-            S = dp4a_ss(static_cast<int>(w8[0]), a0.x, 0);
-            S = dp4a_ss(static_cast<int>(w8[1]), a0.y, S);
-            S = dp4a_ss(static_cast<int>(w8[2]), a0.z, S);
-            S = dp4a_ss(static_cast<int>(w8[3]), a0.w, S);
-            S = dp4a_ss(static_cast<int>(w8[4]), a1.x, S);
-            S = dp4a_ss(static_cast<int>(w8[5]), a1.y, S);
-            S = dp4a_ss(static_cast<int>(w8[6]), a1.z, S);
-            S = dp4a_ss(static_cast<int>(w8[7]), a1.w, S);
-        } else {
-            S = dp4a_us(lo[0], a0.x, 0);
-            S = dp4a_us(lo[1], a0.y, S);
-            S = dp4a_us(lo[2], a0.z, S);
-            S = dp4a_us(lo[3], a0.w, S);
-            S = dp4a_us(hi[0], a1.x, S);
-            S = dp4a_us(hi[1], a1.y, S);
-            S = dp4a_us(hi[2], a1.z, S);
-            S = dp4a_us(hi[3], a1.w, S);
-            const int bsw = *reinterpret_cast<const int *>(A.bs[m] + b * 2);
-            const int asum = bs_lo(bsw) + bs_hi(bsw);
-            S -= (TYPE == T_Q4_0 ? 8 : 16) * asum;
+        const int4 a0 = A.q[m][b], a1 = A.q[m][A.NC + b];
+        const int bsw = *reinterpret_cast<const int *>(A.bs[m] + b * 2);
+        const int asum = bs_lo(bsw) + bs_hi(bsw);
+        const float d8 = A.sc[m][b];
+#pragma unroll
+        for (int r = 0; r < RL; ++r) {
+            int S;
+            if constexpr (TYPE == T_Q8_0) {
+                S = dp4a_ss(static_cast<int>(w8[r][0]), a0.x, 0);
+                S = dp4a_ss(static_cast<int>(w8[r][1]), a0.y, S);
+                S = dp4a_ss(static_cast<int>(w8[r][2]), a0.z, S);
+                S = dp4a_ss(static_cast<int>(w8[r][3]), a0.w, S);
+                S = dp4a_ss(static_cast<int>(w8[r][4]), a1.x, S);
+                S = dp4a_ss(static_cast<int>(w8[r][5]), a1.y, S);
+                S = dp4a_ss(static_cast<int>(w8[r][6]), a1.z, S);
+                S = dp4a_ss(static_cast<int>(w8[r][7]), a1.w, S);
+            } else {
+                S = dp4a_us(lo[r][0], a0.x, 0);
+                S = dp4a_us(lo[r][1], a0.y, S);
+                S = dp4a_us(lo[r][2], a0.z, S);
+                S = dp4a_us(lo[r][3], a0.w, S);
+                S = dp4a_us(hi[r][0], a1.x, S);
+                S = dp4a_us(hi[r][1], a1.y, S);
+                S = dp4a_us(hi[r][2], a1.z, S);
+                S = dp4a_us(hi[r][3], a1.w, S);
+                S -= (TYPE == T_Q4_0 ? 8 : 16) * asum;
+            }
+            acc[r][m] += (dw[r] * d8) * static_cast<float>(S);
         }
-        acc[m] += (dw * A.sc[m][b]) * static_cast<float>(S);
     }
 }
 
 // Q2_K: task = (super-block, 128-element half n)
-template <int ACT, int NMX>
-__device__ __forceinline__ void task_q2_K(const uint8_t *row, int t, const Acts<NMX> &A, float (&acc)[NMX]) {
+template <int ACT, int NMX, int RL>
+__device__ __forceinline__ void task_q2_K(const uint8_t *const (&rows)[RL], int t, const Acts<NMX> &A,
+                                          float (&acc)[RL][NMX]) {
     const int sb = t >> 1, n = t & 1;
-    const uint8_t *blk = row + sb * 84;
-    uint32_t q[8];
-    ld_words_a4<8>(blk + 16 + 32 * n, q);
-    const uint32_t sw0 = ld_u32(blk + 8 * n), sw1 = ld_u32(blk + 8 * n + 4);
-    const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(blk + 80));
-    const uint32_t mw0 = (sw0 >> 4) & 0x0F0F0F0Fu, mw1 = (sw1 >> 4) & 0x0F0F0F0Fu;
+    uint32_t q[RL][8], sw0[RL], sw1[RL], mw0[RL], mw1[RL];
+    float2 dm[RL];
+#pragma unroll
+    for (int r = 0; r < RL; ++r) {
+        const uint8_t *blk = rows[r] + sb * 84;
+        ld_words_a4<8>(blk + 16 + 32 * n, q[r]);
+        sw0[r] = ld_u32(blk + 8 * n);
+        sw1[r] = ld_u32(blk + 8 * n + 4);
+        dm[r] = __half22float2(*reinterpret_cast<const __half2 *>(blk + 80));
+        mw0[r] = (sw0[r] >> 4) & 0x0F0F0F0Fu;
+        mw1[r] = (sw1[r] >> 4) & 0x0F0F0F0Fu;
+    }
 #pragma unroll
     for (int m = 0; m < NMX; ++m) {
         if (m >= A.nm) break;
-        const int4 *aq = reinterpret_cast<const int4 *>(A.q[m] + sb * 256 + 128 * n);
-        const int4 bsv = *reinterpret_cast<const int4 *>(A.bs[m] + sb * 16 + 8 * n);
-        int Ih = 0;
-        float fI = 0.f, fM = 0.f;
+        const int4 *aq = A.q[m] + t;
+        const int4 bsv = *reinterpret_cast<const int4 *>(A.bs[m] + t * 8);
+        int Ih[RL];
+        float fI[RL], fM[RL];
+#pragma unroll
+        for (int r = 0; r < RL; ++r) { Ih[r] = 0; fI[r] = 0.f; fM[r] = 0.f; }
 #pragma unroll
         for (int k = 3; k >= 0; --k) {
             const uint32_t M = 0x03030303u << (2 * k);
-            const int4 a0 = aq[2 * k], a1 = aq[2 * k + 1];
-            int S0 = dp4a_us(q[0] & M, a0.x, 0);
-            S0 = dp4a_us(q[1] & M, a0.y, S0);
-            S0 = dp4a_us(q[2] & M, a0.z, S0);
-            S0 = dp4a_us(q[3] & M, a0.w, S0);
-            int S1 = dp4a_us(q[4] & M, a1.x, 0);
-            S1 = dp4a_us(q[5] & M, a1.y, S1);
-            S1 = dp4a_us(q[6] & M, a1.z, S1);
-            S1 = dp4a_us(q[7] & M, a1.w, S1);
-            const uint32_t sw = k < 2 ? sw0 : sw1;
-            const int sc0 = (sw >> (16 * (k & 1))) & 0xF;
-            const int sc1 = (sw >> (16 * (k & 1) + 8)) & 0xF;
-            const int Ik = sc0 * S0 + sc1 * S1;   // 4^k times the true value (exact)
-            if constexpr (ACT == ACT_CPU) {
-                Ih = (k == 3) ? Ik : (Ih >> 2) + Ik;
-            } else {
-                const float d8 = A.sc[m][sb * 8 + 4 * n + k];
-                const int bw = k == 0 ? bsv.x : k == 1 ? bsv.y : k == 2 ? bsv.z : bsv.w;
-                const uint32_t mw = k < 2 ? mw0 : mw1;
-                const int Mk = (k & 1) ? dp2a_hi_su(bw, mw, 0) : dp2a_lo_su(bw, mw, 0);
-                fI += d8 * static_cast<float>(Ik >> (2 * k));
-                fM += d8 * static_cast<float>(Mk);
+            const int4 a0 = aq[(2 * k) * A.NC], a1 = aq[(2 * k + 1) * A.NC];
+            const int bw = k == 0 ? bsv.x : k == 1 ? bsv.y : k == 2 ? bsv.z : bsv.w;
+            float d8k = 0.f;
+            if constexpr (ACT == ACT_Q8_1) d8k = A.sc[m][t * 4 + k];
+#pragma unroll
+            for (int r = 0; r < RL; ++r) {
+                int S0 = dp4a_us(q[r][0] & M, a0.x, 0);
+                S0 = dp4a_us(q[r][1] & M, a0.y, S0);
+                S0 = dp4a_us(q[r][2] & M, a0.z, S0);
+                S0 = dp4a_us(q[r][3] & M, a0.w, S0);
+                int S1 = dp4a_us(q[r][4] & M, a1.x, 0);
+                S1 = dp4a_us(q[r][5] & M, a1.y, S1);
+                S1 = dp4a_us(q[r][6] & M, a1.z, S1);
+                S1 = dp4a_us(q[r][7] & M, a1.w, S1);
+                const uint32_t sw = k < 2 ? sw0[r] : sw1[r];
+                const int sc0 = (sw >> (16 * (k & 1))) & 0xF;
+                const int sc1 = (sw >> (16 * (k & 1) + 8)) & 0xF;
+                const int Ik = sc0 * S0 + sc1 * S1;   // 4^k times the true value (exact)
+                if constexpr (ACT == ACT_CPU) {
+                    Ih[r] = (k == 3) ? Ik : (Ih[r] >> 2) + Ik;
+                } else {
+                    const uint32_t mw = k < 2 ? mw0[r] : mw1[r];
+                    const int Mk = (k & 1) ? dp2a_hi_su(bw, mw, 0) : dp2a_lo_su(bw, mw, 0);
+                    fI[r] += d8k * static_cast<float>(Ik >> (2 * k));
+                    fM[r] += d8k * static_cast<float>(Mk);
+                }
             }
         }
-        if constexpr (ACT == ACT_CPU) {
-            int Mi = dp2a_lo_su(bsv.x, mw0, 0);
-            Mi = dp2a_hi_su(bsv.y, mw0, Mi);
-            Mi = dp2a_lo_su(bsv.z, mw1, Mi);
-            Mi = dp2a_hi_su(bsv.w, mw1, Mi);
-            const float d8 = A.sc[m][sb];
-            acc[m] += d8 * (dm.x * static_cast<float>(Ih) - dm.y * static_cast<float>(Mi));
-        } else {
-            acc[m] += dm.x * fI - dm.y * fM;
+#pragma unroll
+        for (int r = 0; r < RL; ++r) {
+            if constexpr (ACT == ACT_CPU) {
+                int Mi = dp2a_lo_su(bsv.x, mw0[r], 0);
+                Mi = dp2a_hi_su(bsv.y, mw0[r], Mi);
+                Mi = dp2a_lo_su(bsv.z, mw1[r], Mi);
+                Mi = dp2a_hi_su(bsv.w, mw1[r], Mi);
+                acc[r][m] += A.sc[m][sb] * (dm[r].x * static_cast<float>(Ih[r]) - dm[r].y * static_cast<float>(Mi));
+            } else {
+                acc[r][m] += dm[r].x * fI[r] - dm[r].y * fM[r];
+            }
         }
     }
 }
 
 // Q3_K: task = (super-block, 128-element half n)
-template <int ACT, int NMX>
-__device__ __forceinline__ void task_q3_K(const uint8_t *row, int t, const Acts<NMX> &A, float (&acc)[NMX]) {
+template <int ACT, int NMX, int RL>
+__device__ __forceinline__ void task_q3_K(const uint8_t *const (&rows)[RL], int t, const Acts<NMX> &A,
+                                          float (&acc)[RL][NMX]) {
     const int sb = t >> 1, n = t & 1;
-    const uint8_t *blk = row + sb * 110;
-    uint32_t qw[8], hw[8], sc3[3];
-    ld_words_a2<8>(blk + 32 + 32 * n, qw);
-    ld_words_a2<8>(blk, hw);
-    ld_words_a2<3>(blk + 96, sc3);
-    const float d = ld_half(blk + 108);
-    uint32_t SW0, SW1;   // scale + 32 for sub-blocks 8n + 0..3 and 8n + 4..7
-    if (n == 0) {
-        SW0 = (sc3[0] & 0x0F0F0F0Fu) | ((sc3[2] & 0x03030303u) << 4);
-        SW1 = (sc3[1] & 0x0F0F0F0Fu) | (((sc3[2] >> 2) & 0x03030303u) << 4);
-    } else {
-        SW0 = ((sc3[0] >> 4) & 0x0F0F0F0Fu) | (((sc3[2] >> 4) & 0x03030303u) << 4);
-        SW1 = ((sc3[1] >> 4) & 0x0F0F0F0Fu) | (((sc3[2] >> 6) & 0x03030303u) << 4);
-    }
-    uint32_t u[4][8];
+    uint32_t qw[RL][8], hw[RL][8], SW0[RL], SW1[RL];
+    float d[RL];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int hs = 4 * n + k;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            u[k][i] = ((qw[i] >> (2 * k)) & 0x03030303u) | (((hw[i] >> hs) & 0x01010101u) << 2);
+    for (int r = 0; r < RL; ++r) {
+        const uint8_t *blk = rows[r] + sb * 110;
+        uint32_t sc3[3];
+        ld_words_a2<8>(blk + 32 + 32 * n, qw[r]);
+        ld_words_a2<8>(blk, hw[r]);
+        ld_words_a2<3>(blk + 96, sc3);
+        d[r] = ld_half(blk + 108);
+        if (n == 0) {
+            SW0[r] = (sc3[0] & 0x0F0F0F0Fu) | ((sc3[2] & 0x03030303u) << 4);
+            SW1[r] = (sc3[1] & 0x0F0F0F0Fu) | (((sc3[2] >> 2) & 0x03030303u) << 4);
+        } else {
+            SW0[r] = ((sc3[0] >> 4) & 0x0F0F0F0Fu) | (((sc3[2] >> 4) & 0x03030303u) << 4);
+            SW1[r] = ((sc3[1] >> 4) & 0x0F0F0F0Fu) | (((sc3[2] >> 6) & 0x03030303u) << 4);
+        }
     }
 #pragma unroll
     for (int m = 0; m < NMX; ++m) {
         if (m >= A.nm) break;
-        const int4 *aq = reinterpret_cast<const int4 *>(A.q[m] + sb * 256 + 128 * n);
-        const int4 bsv = *reinterpret_cast<const int4 *>(A.bs[m] + sb * 16 + 8 * n);
-        const int bsw[4] = {bsv.x, bsv.y, bsv.z, bsv.w};
-        int I = 0;
-        float fI = 0.f;
+        const int4 *aq = A.q[m] + t;
+        const int4 bsv = *reinterpret_cast<const int4 *>(A.bs[m] + t * 8);
+        int I[RL];
+        float fI[RL];
+#pragma unroll
+        for (int r = 0; r < RL; ++r) { I[r] = 0; fI[r] = 0.f; }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int4 a0 = aq[2 * k], a1 = aq[2 * k + 1];
-            int S0 = dp4a_us(u[k][0], a0.x, 0);
-            S0 = dp4a_us(u[k][1], a0.y, S0);
-            S0 = dp4a_us(u[k][2], a0.z, S0);
-            S0 = dp4a_us(u[k][3], a0.w, S0);
-            int S1 = dp4a_us(u[k][4], a1.x, 0);
-            S1 = dp4a_us(u[k][5], a1.y, S1);
-            S1 = dp4a_us(u[k][6], a1.z, S1);
-            S1 = dp4a_us(u[k][7], a1.w, S1);
-            const uint32_t SW = k < 2 ? SW0 : SW1;
-            const int s0 = static_cast<int>((SW >> (16 * (k & 1))) & 0xFF) - 32;
-            const int s1 = static_cast<int>((SW >> (16 * (k & 1) + 8)) & 0xFF) - 32;
-            const int Ik = s0 * (S0 - 4 * bs_lo(bsw[k])) + s1 * (S1 - 4 * bs_hi(bsw[k]));
-            if constexpr (ACT == ACT_CPU) I += Ik;
-            else fI += A.sc[m][sb * 8 + 4 * n + k] * static_cast<float>(Ik);
+            const int4 a0 = aq[(2 * k) * A.NC], a1 = aq[(2 * k + 1) * A.NC];
+            const int bw = k == 0 ? bsv.x : k == 1 ? bsv.y : k == 2 ? bsv.z : bsv.w;
+            const int hs = 4 * n + k;
+#pragma unroll
+            for (int r = 0; r < RL; ++r) {
+                uint32_t u[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    u[i] = ((qw[r][i] >> (2 * k)) & 0x03030303u) | (((hw[r][i] >> hs) & 0x01010101u) << 2);
+                int S0 = dp4a_us(u[0], a0.x, 0);
+                S0 = dp4a_us(u[1], a0.y, S0);
+                S0 = dp4a_us(u[2], a0.z, S0);
+                S0 = dp4a_us(u[3], a0.w, S0);
+                int S1 = dp4a_us(u[4], a1.x, 0);
+                S1 = dp4a_us(u[5], a1.y, S1);
+                S1 = dp4a_us(u[6], a1.z, S1);
+                S1 = dp4a_us(u[7], a1.w, S1);
+                const uint32_t SW = k < 2 ? SW0[r] : SW1[r];
+                const int s0 = static_cast<int>((SW >> (16 * (k & 1))) & 0xFF) - 32;
+                const int s1 = static_cast<int>((SW >> (16 * (k & 1) + 8)) & 0xFF) - 32;
+                const int Ik = s0 * (S0 - 4 * bs_lo(bw)) + s1 * (S1 - 4 * bs_hi(bw));
+                if constexpr (ACT == ACT_CPU) I[r] += Ik;
+                else fI[r] += A.sc[m][t * 4 + k] * static_cast<float>(Ik);
+            }
         }
-        if constexpr (ACT == ACT_CPU) acc[m] += A.sc[m][sb] * (d * static_cast<float>(I));
-        else acc[m] += d * fI;
+#pragma unroll
+        for (int r = 0; r < RL; ++r) {
+            if constexpr (ACT == ACT_CPU) acc[r][m] += A.sc[m][sb] * (d[r] * static_cast<float>(I[r]));
+            else acc[r][m] += d[r] * fI[r];
+        }
     }
 }
 
 // Q4_K / Q5_K: task = (super-block, 64-element chunk c) = sub-blocks 2c, 2c+1
-template <int TYPE, int ACT, int NMX>
-__device__ __forceinline__ void task_q45_K(const uint8_t *row, int t, const Acts<NMX> &A, float (&acc)[NMX]) {
+template <int TYPE, int ACT, int NMX, int RL>
+__device__ __forceinline__ void task_q45_K(const uint8_t *const (&rows)[RL], int t, const Acts<NMX> &A,
+                                           float (&acc)[RL][NMX]) {
     const int sb = t >> 2, c = t & 3;
-    const uint8_t *blk = row + sb * fmt<TYPE>::bytes;
-    uint32_t qw[8];
-    ld_words_a4<8>(blk + (TYPE == T_Q4_K ? 16 : 48) + 32 * c, qw);
-    const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(blk));
-    const uint32_t Sw = ld_u32(blk + 4), Mw = ld_u32(blk + 8), Xw = ld_u32(blk + 12);
-    uint32_t scw, mnw;   // 4 bytes: scales / mins of sub-blocks (c<2 ? 0..3 : 4..7)
-    if (c < 2) {
-        scw = Sw & 0x3f3f3f3fu;
-        mnw = Mw & 0x3f3f3f3fu;
-    } else {
-        scw = (Xw & 0x0f0f0f0fu) | (((Sw >> 6) & 0x03030303u) << 4);
-        mnw = ((Xw >> 4) & 0x0f0f0f0fu) | (((Mw >> 6) & 0x03030303u) << 4);
-    }
-    const int bsh = 16 * (c & 1);
-    const int sc0 = (scw >> bsh) & 0xFF, sc1 = (scw >> (bsh + 8)) & 0xFF;
-    const int mn0 = (mnw >> bsh) & 0xFF, mn1 = (mnw >> (bsh + 8)) & 0xFF;
-    uint32_t lo[8], hi[8];
-    if constexpr (TYPE == T_Q4_K) {
+    uint32_t lo[RL][8], hi[RL][8];
+    int sc0[RL], sc1[RL], mn0[RL], mn1[RL];
+    float2 dm[RL];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) { lo[i] = qw[i] & 0x0F0F0F0Fu; hi[i] = (qw[i] >> 4) & 0x0F0F0F0Fu; }
-    } else {
-        uint32_t hw[8];
-        ld_words_a4<8>(blk + 16, hw);
+    for (int r = 0; r < RL; ++r) {
+        const uint8_t *blk = rows[r] + sb * fmt<TYPE>::bytes;
+        uint32_t qw[8];
+        ld_words_a4<8>(blk + (TYPE == T_Q4_K ? 16 : 48) + 32 * c, qw);
+        dm[r] = __half22float2(*reinterpret_cast<const __half2 *>(blk));
+        const uint32_t Sw = ld_u32(blk + 4), Mw = ld_u32(blk + 8), Xw = ld_u32(blk + 12);
+        uint32_t scw, mnw;
+        if (c < 2) {
+            scw = Sw & 0x3f3f3f3fu;
+            mnw = Mw & 0x3f3f3f3fu;
+        } else {
+            scw = (Xw & 0x0f0f0f0fu) | (((Sw >> 6) & 0x03030303u) << 4);
+            mnw = ((Xw >> 4) & 0x0f0f0f0fu) | (((Mw >> 6) & 0x03030303u) << 4);
+        }
+        const int bsh = 16 * (c & 1);
+        sc0[r] = (scw >> bsh) & 0xFF; sc1[r] = (scw >> (bsh + 8)) & 0xFF;
+        mn0[r] = (mnw >> bsh) & 0xFF; mn1[r] = (mnw >> (bsh + 8)) & 0xFF;
+        if constexpr (TYPE == T_Q4_K) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            lo[i] = (qw[i] & 0x0F0F0F0Fu) | (((hw[i] >> (2 * c)) & 0x01010101u) << 4);
-            hi[i] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+            for (int i = 0; i < 8; ++i) { lo[r][i] = qw[i] & 0x0F0F0F0Fu; hi[r][i] = (qw[i] >> 4) & 0x0F0F0F0Fu; }
+        } else {
+            uint32_t hw[8];
+            ld_words_a4<8>(blk + 16, hw);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                lo[r][i] = (qw[i] & 0x0F0F0F0Fu) | (((hw[i] >> (2 * c)) & 0x01010101u) << 4);
+                hi[r][i] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+            }
         }
     }
 #pragma unroll
     for (int m = 0; m < NMX; ++m) {
         if (m >= A.nm) break;
-        const int4 *aq = reinterpret_cast<const int4 *>(A.q[m] + sb * 256 + 64 * c);
-        const int4 a0 = aq[0], a1 = aq[1], a2 = aq[2], a3 = aq[3];
-        int S0 = dp4a_us(lo[0], a0.x, 0);
-        S0 = dp4a_us(lo[1], a0.y, S0);
-        S0 = dp4a_us(lo[2], a0.z, S0);
-        S0 = dp4a_us(lo[3], a0.w, S0);
-        S0 = dp4a_us(lo[4], a1.x, S0);
-        S0 = dp4a_us(lo[5], a1.y, S0);
-        S0 = dp4a_us(lo[6], a1.z, S0);
-        S0 = dp4a_us(lo[7], a1.w, S0);
-        int S1 = dp4a_us(hi[0], a2.x, 0);
-        S1 = dp4a_us(hi[1], a2.y, S1);
-        S1 = dp4a_us(hi[2], a2.z, S1);
-        S1 = dp4a_us(hi[3], a2.w, S1);
-        S1 = dp4a_us(hi[4], a3.x, S1);
-        S1 = dp4a_us(hi[5], a3.y, S1);
-        S1 = dp4a_us(hi[6], a3.z, S1);
-        S1 = dp4a_us(hi[7], a3.w, S1);
-        const int2 bsv = *reinterpret_cast<const int2 *>(A.bs[m] + sb * 16 + 4 * c);
+        const int4 *aq = A.q[m] + t;
+        const int4 a0 = aq[0], a1 = aq[A.NC], a2 = aq[2 * A.NC], a3 = aq[3 * A.NC];
+        const int2 bsv = *reinterpret_cast<const int2 *>(A.bs[m] + t * 4);
         const int A0 = bs_lo(bsv.x) + bs_hi(bsv.x), A1 = bs_lo(bsv.y) + bs_hi(bsv.y);
-        if constexpr (ACT == ACT_CPU) {
-            const int I = sc0 * S0 + sc1 * S1;
-            const int Mi = mn0 * A0 + mn1 * A1;
-            acc[m] += A.sc[m][sb] * (dm.x * static_cast<float>(I) - dm.y * static_cast<float>(Mi));
-        } else {
-            const float d80 = A.sc[m][sb * 8 + 2 * c], d81 = A.sc[m][sb * 8 + 2 * c + 1];
-            const float fI = d80 * static_cast<float>(sc0 * S0) + d81 * static_cast<float>(sc1 * S1);
-            const float fM = d80 * static_cast<float>(mn0 * A0) + d81 * static_cast<float>(mn1 * A1);
-            acc[m] += dm.x * fI - dm.y * fM;
+#pragma unroll
+        for (int r = 0; r < RL; ++r) {
+            int S0 = dp4a_us(lo[r][0], a0.x, 0);
+            S0 = dp4a_us(lo[r][1], a0.y, S0);
+            S0 = dp4a_us(lo[r][2], a0.z, S0);
+            S0 = dp4a_us(lo[r][3], a0.w, S0);
+            S0 = dp4a_us(lo[r][4], a1.x, S0);
+            S0 = dp4a_us(lo[r][5], a1.y, S0);
+            S0 = dp4a_us(lo[r][6], a1.z, S0);
+            S0 = dp4a_us(lo[r][7], a1.w, S0);
+            int S1 = dp4a_us(hi[r][0], a2.x, 0);
+            S1 = dp4a_us(hi[r][1], a2.y, S1);
+            S1 = dp4a_us(hi[r][2], a2.z, S1);
+            S1 = dp4a_us(hi[r][3], a2.w, S1);
+            S1 = dp4a_us(hi[r][4], a3.x, S1);
+            S1 = dp4a_us(hi[r][5], a3.y, S1);
+            S1 = dp4a_us(hi[r][6], a3.z, S1);
+            S1 = dp4a_us(hi[r][7], a3.w, S1);
+            if constexpr (ACT == ACT_CPU) {
+                const int I = sc0[r] * S0 + sc1[r] * S1;
+                const int Mi = mn0[r] * A0 + mn1[r] * A1;
+                acc[r][m] += A.sc[m][sb] * (dm[r].x * static_cast<float>(I) - dm[r].y * static_cast<float>(Mi));
+            } else {
+                const float d80 = A.sc[m][t * 2], d81 = A.sc[m][t * 2 + 1];
+                const float fI = d80 * static_cast<float>(sc0[r] * S0) + d81 * static_cast<float>(sc1[r] * S1);
+                const float fM = d80 * static_cast<float>(mn0[r] * A0) + d81 * static_cast<float>(mn1[r] * A1);
+                acc[r][m] += dm[r].x * fI - dm[r].y * fM;
+            }
         }
     }
 }
 
 // Q6_K: task = (super-block, 128-element half n)
-template <int ACT, int NMX>
-__device__ __forceinline__ void task_q6_K(const uint8_t *row, int t, const Acts<NMX> &A, float (&acc)[NMX]) {
+template <int ACT, int NMX, int RL>
+__device__ __forceinline__ void task_q6_K(const uint8_t *const (&rows)[RL], int t, const Acts<NMX> &A,
+                                          float (&acc)[RL][NMX]) {
     const int sb = t >> 1, n = t & 1;
-    const uint8_t *blk = row + sb * 210;
-    uint32_t ql[16], qh[8], scw[2];
-    ld_words_a2<16>(blk + 64 * n, ql);
-    ld_words_a2<8>(blk + 128 + 32 * n, qh);
-    ld_words_a2<2>(blk + 192 + 8 * n, scw);
-    const float d = ld_half(blk + 208);
-    uint32_t g[4][8];
+    uint32_t ql[RL][16], qh[RL][8], scw[RL][2];
+    float d[RL];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        g[0][i] = (ql[i] & 0x0F0F0F0Fu) | ((qh[i] & 0x03030303u) << 4);
-        g[1][i] = (ql[8 + i] & 0x0F0F0F0Fu) | ((qh[i] << 2) & 0x30303030u);
-        g[2][i] = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (qh[i] & 0x30303030u);
-        g[3][i] = ((ql[8 + i] >> 4) & 0x0F0F0F0Fu) | ((qh[i] >> 2) & 0x30303030u);
+    for (int r = 0; r < RL; ++r) {
+        const uint8_t *blk = rows[r] + sb * 210;
+        ld_words_a2<16>(blk + 64 * n, ql[r]);
+        ld_words_a2<8>(blk + 128 + 32 * n, qh[r]);
+        ld_words_a2<2>(blk + 192 + 8 * n, scw[r]);
+        d[r] = ld_half(blk + 208);
     }
 #pragma unroll
     for (int m = 0; m < NMX; ++m) {
         if (m >= A.nm) break;
-        const int4 *aq = reinterpret_cast<const int4 *>(A.q[m] + sb * 256 + 128 * n);
-        const int4 bsv = *reinterpret_cast<const int4 *>(A.bs[m] + sb * 16 + 8 * n);
-        const int bsw[4] = {bsv.x, bsv.y, bsv.z, bsv.w};
-        int I = 0;
-        float fI = 0.f;
+        const int4 *aq = A.q[m] + t;
+        const int4 bsv = *reinterpret_cast<const int4 *>(A.bs[m] + t * 8);
+        int I[RL];
+        float fI[RL];
+#pragma unroll
+        for (int r = 0; r < RL; ++r) { I[r] = 0; fI[r] = 0.f; }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int4 a0 = aq[2 * k], a1 = aq[2 * k + 1];
-            int S0 = dp4a_us(g[k][0], a0.x, 0);
-            S0 = dp4a_us(g[k][1], a0.y, S0);
-            S0 = dp4a_us(g[k][2], a0.z, S0);
-            S0 = dp4a_us(g[k][3], a0.w, S0);
-            int S1 = dp4a_us(g[k][4], a1.x, 0);
-            S1 = dp4a_us(g[k][5], a1.y, S1);
-            S1 = dp4a_us(g[k][6], a1.z, S1);
-            S1 = dp4a_us(g[k][7], a1.w, S1);
-            const uint32_t sw = scw[k >> 1];
-            const int s0 = static_cast<int8_t>((sw >> (16 * (k & 1))) & 0xFF);
-            const int s1 = static_cast<int8_t>((sw >> (16 * (k & 1) + 8)) & 0xFF);
-            const int Ik = s0 * (S0 - 32 * bs_lo(bsw[k])) + s1 * (S1 - 32 * bs_hi(bsw[k]));
-            if constexpr (ACT == ACT_CPU) I += Ik;
-            else fI += A.sc[m][sb * 8 + 4 * n + k] * static_cast<float>(Ik);
+            const int4 a0 = aq[(2 * k) * A.NC], a1 = aq[(2 * k + 1) * A.NC];
+            const int bw = k == 0 ? bsv.x : k == 1 ? bsv.y : k == 2 ? bsv.z : bsv.w;
+#pragma unroll
+            for (int r = 0; r < RL; ++r) {
+                uint32_t g[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    if (k == 0) g[i] = (ql[r][i] & 0x0F0F0F0Fu) | ((qh[r][i] & 0x03030303u) << 4);
+                    else if (k == 1) g[i] = (ql[r][8 + i] & 0x0F0F0F0Fu) | ((qh[r][i] << 2) & 0x30303030u);
+                    else if (k == 2) g[i] = ((ql[r][i] >> 4) & 0x0F0F0F0Fu) | (qh[r][i] & 0x30303030u);
+                    else g[i] = ((ql[r][8 + i] >> 4) & 0x0F0F0F0Fu) | ((qh[r][i] >> 2) & 0x30303030u);
+                }
+                int S0 = dp4a_us(g[0], a0.x, 0);
+                S0 = dp4a_us(g[1], a0.y, S0);
+                S0 = dp4a_us(g[2], a0.z, S0);
+                S0 = dp4a_us(g[3], a0.w, S0);
+                int S1 = dp4a_us(g[4], a1.x, 0);
+                S1 = dp4a_us(g[5], a1.y, S1);
+                S1 = dp4a_us(g[6], a1.z, S1);
+                S1 = dp4a_us(g[7], a1.w, S1);
+                const uint32_t sw = scw[r][k >> 1];
+                const int s0 = static_cast<int8_t>((sw >> (16 * (k & 1))) & 0xFF);
+                const int s1 = static_cast<int8_t>((sw >> (16 * (k & 1) + 8)) & 0xFF);
+                const int Ik = s0 * (S0 - 32 * bs_lo(bw)) + s1 * (S1 - 32 * bs_hi(bw));
+                if constexpr (ACT == ACT_CPU) I[r] += Ik;
+                else fI[r] += A.sc[m][t * 4 + k] * static_cast<float>(Ik);
+            }
         }
-        if constexpr (ACT == ACT_CPU) acc[m] += A.sc[m][sb] * (d * static_cast<float>(I));
-        else acc[m] += d * fI;
+#pragma unroll
+        for (int r = 0; r < RL; ++r) {
+            if constexpr (ACT == ACT_CPU) acc[r][m] += A.sc[m][sb] * (d[r] * static_cast<float>(I[r]));
+            else acc[r][m] += d[r] * fI[r];
+        }
     }
 }
 
-template <int TYPE, int ACT, int NMX>
-__device__ __forceinline__ void task_dot(const uint8_t *row, int t, const Acts<NMX> &A, float (&acc)[NMX]) {
-    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q5_0 || TYPE == T_Q8_0) task_legacy<TYPE, NMX>(row, t, A, acc);
-    else if constexpr (TYPE == T_Q2_K) task_q2_K<ACT, NMX>(row, t, A, acc);
-    else if constexpr (TYPE == T_Q3_K) task_q3_K<ACT, NMX>(row, t, A, acc);
-    else if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) task_q45_K<TYPE, ACT, NMX>(row, t, A, acc);
-    else task_q6_K<ACT, NMX>(row, t, A, acc);
+template <int TYPE, int ACT, int NMX, int RL>
+__device__ __forceinline__ void task_dot(const uint8_t *const (&rows)[RL], int t, const Acts<NMX> &A,
+                                         float (&acc)[RL][NMX]) {
+    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q5_0 || TYPE == T_Q8_0) task_legacy<TYPE, NMX, RL>(rows, t, A, acc);
+    else if constexpr (TYPE == T_Q2_K) task_q2_K<ACT, NMX, RL>(rows, t, A, acc);
+    else if constexpr (TYPE == T_Q3_K) task_q3_K<ACT, NMX, RL>(rows, t, A, acc);
+    else if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) task_q45_K<TYPE, ACT, NMX, RL>(rows, t, A, acc);
+    else task_q6_K<ACT, NMX, RL>(rows, t, A, acc);
 }
 
 // ---------------------------------------------------------------------------
@@ -484,6 +582,9 @@ struct GemvCtrl {
     int16_t eslot[GEMV_MAX_ENTRIES];      // activation slot of entry
     int16_t gmem[GEMV_MAX_ENTRIES];       // CSR members (entry ids)
     int32_t uexp[GEMV_MAX_ENTRIES];
+    const char *usrc[GEMV_MAX_ENTRIES][2];   // weight source of each group (up/main, gate)
+    uint8_t ukind[GEMV_MAX_ENTRIES][2];      // 0 bulk copy, 1 host 16-byte copy, 2 plain copy
+    uint8_t uhost[GEMV_MAX_ENTRIES][2];      // host-tagged table entry
     int16_t goff[GEMV_MAX_ENTRIES + 2];
     int16_t shslot[8];
     uint32_t keys[GEMV_MAX_KEYS];
@@ -491,6 +592,82 @@ struct GemvCtrl {
     int32_t seg_t0[GEMV_MAX_SEGMENTS + 1];
     int32_t n_unique, n_seg, n_tiles, n_keys, fail;
 };
+
+// One consumer warp's pass over a tile. Fused (use_gate): RL = 2 rows per lane
+// are the up and the gate row of one output row; unfused: RL = 1.
+template <int TYPE, int ACT, int NMX, int RL>
+__device__ __forceinline__ void consume_tile(const GemvArgs &a, const GemvCtrl &C, const uint8_t *up_rows,
+                                             const uint8_t *gate_rows, int nr, int g, int U, int row0,
+                                             const uint8_t *act_area, int lane) {
+    const int L = a.lanes_per_row;
+    const int RP = 32 / L;
+    const int sub = lane % L, rr = lane / L;
+    const int K = a.K;
+    constexpr int CE = chunk_of<TYPE>::CE;
+    const int Tk = (K / fmt<TYPE>::qk) * fmt<TYPE>::tasks;
+    const uint32_t rb = a.row_bytes;
+    const int nch = a.nchannels_dst;
+    const int nmem = g < U ? (C.goff[g + 1] - C.goff[g]) : a.ncols_dst;
+    for (int mc = 0; mc < nmem; mc += NMX) {
+        Acts<NMX> A;
+        A.nm = nmem - mc < NMX ? nmem - mc : NMX;
+        A.NC = K / CE;
+#pragma unroll
+        for (int m = 0; m < NMX; ++m) {
+            int v = 0;
+            if (m < A.nm) v = g < U ? C.eslot[C.gmem[C.goff[g] + mc + m]] : C.shslot[mc + m];
+            const uint8_t *slot = act_area + static_cast<size_t>(v) * a.slot_bytes;
+            A.q[m] = reinterpret_cast<const int4 *>(slot);
+            A.bs[m] = reinterpret_cast<const int16_t *>(slot + K);
+            A.sc[m] = reinterpret_cast<const float *>(slot + K + K / 8);
+        }
+        for (int rbase = 0; rbase < nr; rbase += RP) {
+            const int ri = rbase + rr;
+            const bool ok = ri < nr;
+            const uint8_t *wrows[RL];
+            wrows[0] = up_rows + static_cast<size_t>(ok ? ri : 0) * rb;
+            if constexpr (RL == 2) wrows[1] = gate_rows + static_cast<size_t>(ok ? ri : 0) * rb;
+            float acc[RL][NMX];
+#pragma unroll
+            for (int r = 0; r < RL; ++r)
+#pragma unroll
+                for (int m = 0; m < NMX; ++m) acc[r][m] = 0.f;
+            if (ok)
+                for (int t = sub; t < Tk; t += L) task_dot<TYPE, ACT, NMX, RL>(wrows, t, A, acc);
+            for (int off = L >> 1; off >= 1; off >>= 1) {
+#pragma unroll
+                for (int r = 0; r < RL; ++r)
+#pragma unroll
+                    for (int m = 0; m < NMX; ++m) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], off);
+            }
+            if (!ok || sub != 0) continue;
+            const int row = row0 + ri;
+#pragma unroll
+            for (int m = 0; m < NMX; ++m) {
+                if (m >= A.nm) break;
+                int x = 0, t, p = 0;
+                if (g < U) {
+                    const int e = C.gmem[C.goff[g] + mc + m];
+                    t = e / nch; p = e % nch; x = C.x[e];
+                } else {
+                    t = mc + m;
+                }
+                float result = acc[0][m];
+                if (a.has_fusion) {
+                    const int64_t bias_idx = static_cast<int64_t>(x) * a.stride_channel_dst + row;
+                    if (a.x_bias) result += a.x_bias[bias_idx];
+                    if constexpr (RL == 2) {
+                        float gv = acc[1][m];
+                        if (a.gate_bias) gv += a.gate_bias[bias_idx];
+                        result = glu_apply(a.glu_op, gv, result, a.glu_limit);
+                    }
+                }
+                if (g < U) a.dst[p * a.stride_channel_dst + t * a.stride_col_dst + row] = result;
+                else a.shared_dst[t * a.shared_stride_col_dst + row] = result;
+            }
+        }
+    }
+}
 
 template <int TYPE, int ACT, int NMX>
 __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_constant__ GemvArgs a) {
@@ -508,72 +685,150 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
     const bool has_shared = a.shared_up != nullptr;
     const int S = a.n_stages;
 
-    if (tid == 0) {
-        for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        fence_mbar_init();
-        C.fail = 0;
+    for (int s = tid; s < S; s += blockDim.x) {
+        mbar_init(&full[s], 1);
+        mbar_init(&empty[s], 1);
     }
+    if (tid < S) fence_mbar_init();
+    if (tid == 0) C.fail = 0;
     __syncthreads();
 
-    // ---- routed entries: validate and de-duplicate -------------------------
-    for (int e = tid; e < N; e += blockDim.x) {
-        const int t = e / nch, p = e % nch;
-        const int x = a.ids[p + static_cast<int64_t>(t) * a.ids_stride];
-        if (x < 0 || x >= a.n_experts) { C.fail = 1; set_error(a.err, DERR_BAD_ID); }
-        C.x[e] = x;
-    }
-    __syncthreads();
-    if (C.fail) return;
-    for (int e = tid; e < N; e += blockDim.x) {
-        int f = e;
-        for (int j = 0; j < e; ++j) if (C.x[j] == C.x[e]) { f = j; break; }
-        C.first[e] = static_cast<int16_t>(f);
-    }
-    __syncthreads();
-    for (int e = tid; e < N; e += blockDim.x) {
-        if (C.first[e] == e) {
-            int u = 0;
-            for (int j = 0; j < e; ++j) u += (C.first[j] == j);
-            C.uidx[e] = static_cast<int16_t>(u);
-            C.uexp[u] = C.x[e];
+    // ---- routed entries: validate, de-duplicate, resolve table entries ------
+    // Entry e = tok * nchannels_dst + pick. Groups (distinct experts) are
+    // numbered in first-occurrence order; gmem lists each group's entries
+    // (CSR, offsets goff). usrc/ukind hold each group's weight sources.
+    auto resolve = [&](int u, int x) {
+        const uintptr_t p = reinterpret_cast<uintptr_t>(a.tbl[x]);
+        C.usrc[u][0] = reinterpret_cast<const char *>(p & ~static_cast<uintptr_t>(1));
+        C.ukind[u][0] = static_cast<uint8_t>((p & 1u) ? (a.tma_main ? 1 : 2) : (a.tma_main ? 0 : 2));
+        C.uhost[u][0] = static_cast<uint8_t>(p & 1u);
+        C.usrc[u][1] = nullptr;
+        C.ukind[u][1] = 0;
+        C.uhost[u][1] = 0;
+        if (a.use_gate) {
+            if (a.tbl_gate) {
+                const uintptr_t pg = reinterpret_cast<uintptr_t>(a.tbl_gate[x]);
+                C.usrc[u][1] = reinterpret_cast<const char *>(pg & ~static_cast<uintptr_t>(1));
+                C.ukind[u][1] = static_cast<uint8_t>((pg & 1u) ? (a.tma_gate ? 1 : 2) : (a.tma_gate ? 0 : 2));
+                C.uhost[u][1] = static_cast<uint8_t>(pg & 1u);
+            } else {
+                C.usrc[u][1] = a.gate_dense + static_cast<uint64_t>(x) * a.gate_expert_bytes;
+                C.ukind[u][1] = static_cast<uint8_t>(a.tma_gate ? 0 : 2);
+            }
+        }
+    };
+    if (N <= 32) {
+        // one warp, no block barriers: match_any groups equal experts
+        if (warp == 0) {
+            int x = -1 - lane;
+            bool bad = false;
+            if (lane < N) {
+                const int t = lane / nch, p = lane % nch;
+                x = a.ids[p + static_cast<int64_t>(t) * a.ids_stride];
+                bad = x < 0 || x >= a.n_experts;
+                C.x[lane] = x;
+            }
+            if (__ballot_sync(0xffffffffu, bad)) {
+                if (lane == 0) { C.fail = 1; set_error(a.err, DERR_BAD_ID); }
+            } else {
+                const unsigned same = __match_any_sync(0xffffffffu, x);
+                const int f = __ffs(same) - 1;
+                const unsigned firsts = __ballot_sync(0xffffffffu, lane < N && f == lane);
+                const int u = __popc(firsts & ((1u << f) - 1u));
+                int pos = 0;
+                for (int j = 0; j < N; ++j) {
+                    const int fj = __shfl_sync(0xffffffffu, f, j);
+                    pos += (fj < f) || (fj == f && j < lane);
+                }
+                if (lane < N) {
+                    C.first[lane] = static_cast<int16_t>(f);
+                    C.uidx[lane] = static_cast<int16_t>(u);
+                    C.gmem[pos] = static_cast<int16_t>(lane);
+                    if (f == lane) {
+                        C.uexp[u] = x;
+                        C.goff[u] = static_cast<int16_t>(pos);
+                        resolve(u, x);
+                    }
+                }
+                if (lane == 0) {
+                    C.n_unique = __popc(firsts);
+                    C.goff[__popc(firsts)] = static_cast<int16_t>(N);
+                }
+            }
+        }
+    } else {
+        for (int e = tid; e < N; e += blockDim.x) {
+            const int t = e / nch, p = e % nch;
+            const int x = a.ids[p + static_cast<int64_t>(t) * a.ids_stride];
+            if (x < 0 || x >= a.n_experts) { C.fail = 1; set_error(a.err, DERR_BAD_ID); }
+            C.x[e] = x;
+        }
+        __syncthreads();
+        if (!C.fail) {
+            for (int e = tid; e < N; e += blockDim.x) {
+                int f = e;
+                for (int j = 0; j < e; ++j) if (C.x[j] == C.x[e]) { f = j; break; }
+                C.first[e] = static_cast<int16_t>(f);
+            }
+        }
+        __syncthreads();
+        if (!C.fail) {
+            for (int e = tid; e < N; e += blockDim.x) {
+                if (C.first[e] == e) {
+                    int u = 0;
+                    for (int j = 0; j < e; ++j) u += (C.first[j] == j);
+                    C.uidx[e] = static_cast<int16_t>(u);
+                    C.uexp[u] = C.x[e];
+                }
+            }
+        }
+        __syncthreads();
+        if (!C.fail) {
+            for (int e = tid; e < N; e += blockDim.x)
+                if (C.first[e] != e) C.uidx[e] = C.uidx[C.first[e]];
+            if (tid == 0) {
+                int U = 0;
+                for (int e = 0; e < N; ++e) U += (C.first[e] == e);
+                C.n_unique = U;
+            }
+        }
+        __syncthreads();
+        if (!C.fail) {
+            const int U = C.n_unique;
+            for (int u = tid; u < U; u += blockDim.x) {
+                int c = 0;
+                for (int e = 0; e < N; ++e) c += (C.uidx[e] == u);
+                C.goff[u + 1] = static_cast<int16_t>(c);
+                resolve(u, C.uexp[u]);
+            }
+        }
+        __syncthreads();
+        if (!C.fail && tid == 0) {
+            C.goff[0] = 0;
+            for (int u = 0; u < C.n_unique; ++u) C.goff[u + 1] = static_cast<int16_t>(C.goff[u] + C.goff[u + 1]);
+        }
+        __syncthreads();
+        if (!C.fail) {
+            for (int u = tid; u < C.n_unique; u += blockDim.x) {
+                int k = C.goff[u];
+                for (int e = 0; e < N; ++e) if (C.uidx[e] == u) C.gmem[k++] = static_cast<int16_t>(e);
+            }
         }
     }
     __syncthreads();
-    for (int e = tid; e < N; e += blockDim.x)
-        if (C.first[e] != e) C.uidx[e] = C.uidx[C.first[e]];
-    if (tid == 0) {
-        int U = 0;
-        for (int e = 0; e < N; ++e) U += (C.first[e] == e);
-        C.n_unique = U;
-    }
-    __syncthreads();
+    if (C.fail) return;
     const int U = C.n_unique;
-    for (int u = tid; u < U; u += blockDim.x) {
-        int c = 0;
-        for (int e = 0; e < N; ++e) c += (C.uidx[e] == u);
-        C.goff[u + 1] = static_cast<int16_t>(c);
-    }
-    __syncthreads();
-    if (tid == 0) {
-        C.goff[0] = 0;
-        for (int u = 0; u < U; ++u) C.goff[u + 1] = static_cast<int16_t>(C.goff[u] + C.goff[u + 1]);
-    }
-    __syncthreads();
-    for (int u = tid; u < U; u += blockDim.x) {
-        int k = C.goff[u];
-        for (int e = 0; e < N; ++e) if (C.uidx[e] == u) C.gmem[k++] = static_cast<int16_t>(e);
-    }
 
     // ---- bookkeeping of the reference kernel, first CTA only (:163-198) ---
     if (blockIdx.x == 0) {
         const uint32_t clk = a.clock ? *a.clock : 0u;
         for (int e = tid; e < N; e += blockDim.x) {
             const int x = C.x[e];
+            const int u = C.uidx[e];
             if (a.tbl) {
-                const bool host = (reinterpret_cast<uintptr_t>(a.tbl[x]) & 1u) != 0;
                 if (a.stamps) a.stamps[x] = clk;
                 if (a.stats) {
-                    if (host) {
+                    if (C.uhost[u][0]) {
                         const uint32_t s = atomicAdd(a.stats, 1u);
                         if (s < a.log_cap) a.stats[GEMV_LOG_BASE + s] = (static_cast<uint32_t>(a.cache_id) << 12) | x;
                     } else {
@@ -582,10 +837,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
                 }
             }
             if (a.use_gate && a.tbl_gate) {
-                const bool host = (reinterpret_cast<uintptr_t>(a.tbl_gate[x]) & 1u) != 0;
                 if (a.stamps_gate) a.stamps_gate[x] = clk;
                 if (a.stats) {
-                    if (host) {
+                    if (C.uhost[u][1]) {
                         const uint32_t s = atomicAdd(a.stats, 1u);
                         if (s < a.log_cap)
                             a.stats[GEMV_LOG_BASE + s] = (static_cast<uint32_t>(a.cache_id_gate) << 12) | x;
@@ -598,24 +852,30 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
     }
 
     // ---- this CTA's slice of the row space: segments and tiles ------------
-    const int groups = U + (has_shared ? 1 : 0);
-    const int64_t Rt = static_cast<int64_t>(groups) * a.nrows;
-    const int64_t r_begin = Rt * blockIdx.x / gridDim.x;
-    const int64_t r_end = Rt * (blockIdx.x + 1) / gridDim.x;
+    // (32-bit arithmetic: the launcher guarantees groups * nrows < 2^31)
     const int rpt = a.rows_per_tile;
     if (tid == 0) {
+        const uint32_t nrows = static_cast<uint32_t>(a.nrows);
+        const uint32_t Rt = static_cast<uint32_t>(U + (has_shared ? 1 : 0)) * nrows;
+        const uint32_t G = gridDim.x, bid = blockIdx.x;
+        const uint32_t q = Rt / G, rem = Rt % G;
+        const uint32_t r_begin = bid * q + (bid < rem ? bid : rem);
+        const uint32_t r_end = r_begin + q + (bid < rem ? 1u : 0u);
         int ns = 0, nt = 0;
-        int64_t r = r_begin;
+        uint32_t r = r_begin;
         while (r < r_end) {
-            const int g = static_cast<int>(r / a.nrows);
-            const int r0 = static_cast<int>(r - static_cast<int64_t>(g) * a.nrows);
-            const int64_t g_end = static_cast<int64_t>(g + 1) * a.nrows;
-            const int r1 = static_cast<int>((g_end < r_end ? g_end : r_end) - static_cast<int64_t>(g) * a.nrows);
+            const uint32_t g = r / nrows;
+            const uint32_t r0 = r - g * nrows;
+            const uint32_t g_end = (g + 1) * nrows;
+            const uint32_t r1 = (g_end < r_end ? g_end : r_end) - g * nrows;
             if (ns >= GEMV_MAX_SEGMENTS) { C.fail = 1; set_error(a.err, DERR_TOO_MANY_SEGMENTS); break; }
-            C.seg_g[ns] = g; C.seg_r0[ns] = r0; C.seg_r1[ns] = r1; C.seg_t0[ns] = nt;
-            nt += (r1 - r0 + rpt - 1) / rpt;
+            C.seg_g[ns] = static_cast<int32_t>(g);
+            C.seg_r0[ns] = static_cast<int32_t>(r0);
+            C.seg_r1[ns] = static_cast<int32_t>(r1);
+            C.seg_t0[ns] = nt;
+            nt += (static_cast<int>(r1 - r0) + rpt - 1) / rpt;
             ns++;
-            r = static_cast<int64_t>(g) * a.nrows + r1;
+            r = g * nrows + r1;
         }
         C.seg_t0[ns] = nt;
         C.n_seg = ns;
@@ -664,100 +924,147 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
         const int lim = C.seg_r1[s];
         nr = (lim - row0) < rpt ? (lim - row0) : rpt;
     };
+    // source of each part of group g's tiles; kind: 0 = bulk copy, 1 = host with
+    // 16-byte plain copies, 2 = plain 4/2-byte copies (unaligned source)
+    auto tile_sources = [&](int g, const char *&s0, const char *&s1, int &k0, int &k1) {
+        if (g < U) {
+            s0 = C.usrc[g][0];
+            s1 = C.usrc[g][1];
+            k0 = C.ukind[g][0];
+            k1 = C.ukind[g][1];
+        } else {
+            s0 = a.shared_up;
+            s1 = a.shared_gate;
+            k0 = k1 = a.tma_shared ? 0 : 2;
+        }
+    };
 
     if (warp == GEMV_CONSUMER_WARPS) {
         // =========================== producer warp ===========================
+        // Tiles are issued in rounds of up to min(32, S): within a round no
+        // tile reuses a stage of the same round, so every lane can wait for
+        // its own stage and issue its own bulk copies in parallel. Tiles that
+        // need plain copies (host-tagged or unaligned sources) follow, one at a
+        // time, copied by the whole warp.
         const uint64_t pol = l2_evict_first_policy();
+        const int R = S < 32 ? S : 32;
+        const uint32_t rb = a.row_bytes;
         int issued = 0;
-        for (int i = 0; i < n_tiles; ++i) {
-            const int s = i % S;
-            if (i >= S) {
-                if (!mbar_wait_bounded(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), a.timeout_ns)) {
+        bool ok = true;
+        for (int base = 0; base < n_tiles && ok; base += R) {
+            const int cnt = (n_tiles - base) < R ? (n_tiles - base) : R;
+            bool plain_tile = false, lane_ok = true;
+            if (lane < cnt) {
+                const int i = base + lane, s = i % S;
+                int g, row0, nr;
+                tile_coords(i, g, row0, nr);
+                const char *src0, *src1;
+                int k0, k1;
+                tile_sources(g, src0, src1, k0, k1);
+                plain_tile = k0 != 0 || (a.n_parts > 1 && k1 != 0);
+                if (!plain_tile) {
+                    if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), a.timeout_ns)) {
+                        lane_ok = false;
+                    } else {
+                        const uint32_t bytes = static_cast<uint32_t>(nr) * rb;
+                        uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
+                        const uintptr_t p0 = reinterpret_cast<uintptr_t>(src0) + static_cast<uint64_t>(row0) * rb;
+                        const uintptr_t a00 = p0 & ~static_cast<uintptr_t>(15), a01 = (p0 + bytes + 15u) & ~static_cast<uintptr_t>(15);
+                        uint32_t tx = static_cast<uint32_t>(a01 - a00);
+                        uintptr_t a10 = 0, a11 = 0;
+                        if (a.n_parts > 1) {
+                            const uintptr_t p1 = reinterpret_cast<uintptr_t>(src1) + static_cast<uint64_t>(row0) * rb;
+                            a10 = p1 & ~static_cast<uintptr_t>(15);
+                            a11 = (p1 + bytes + 15u) & ~static_cast<uintptr_t>(15);
+                            tx += static_cast<uint32_t>(a11 - a10);
+                        }
+                        mbar_arrive_expect_tx(&full[s], tx);
+                        bulk_g2s(stage, reinterpret_cast<const void *>(a00), static_cast<uint32_t>(a01 - a00), &full[s], pol);
+                        if (a.n_parts > 1)
+                            bulk_g2s(stage + a.part_bytes, reinterpret_cast<const void *>(a10), static_cast<uint32_t>(a11 - a10),
+                                     &full[s], pol);
+                    }
+                }
+            }
+            if (__any_sync(0xffffffffu, !lane_ok)) {
+                if (lane == 0) set_error(a.err, DERR_TIMEOUT_EMPTY);
+                issued = base + cnt;
+                ok = false;
+                break;
+            }
+            unsigned pending = __ballot_sync(0xffffffffu, plain_tile);
+            while (pending) {
+                const int l = __ffs(pending) - 1;
+                pending &= pending - 1u;
+                const int i = base + l, s = i % S;
+                if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), a.timeout_ns)) {
                     if (lane == 0) set_error(a.err, DERR_TIMEOUT_EMPTY);
+                    ok = false;
                     break;
                 }
-            }
-            int g, row0, nr;
-            tile_coords(i, g, row0, nr);
-            const char *src[2] = {nullptr, nullptr};
-            bool dev[2] = {true, true};
-            bool host16[2] = {false, false};
-            if (g < U) {
-                const int x = C.uexp[g];
-                const uintptr_t p = reinterpret_cast<uintptr_t>(a.tbl[x]);
-                src[0] = reinterpret_cast<const char *>(p & ~static_cast<uintptr_t>(1));
-                dev[0] = !(p & 1u) && a.tma_main;
-                host16[0] = (p & 1u) && a.tma_main;
-                if (a.use_gate) {
-                    if (a.tbl_gate) {
-                        const uintptr_t pg = reinterpret_cast<uintptr_t>(a.tbl_gate[x]);
-                        src[1] = reinterpret_cast<const char *>(pg & ~static_cast<uintptr_t>(1));
-                        dev[1] = !(pg & 1u) && a.tma_gate;
-                        host16[1] = (pg & 1u) && a.tma_gate;
-                    } else {
-                        src[1] = a.gate_dense + static_cast<uint64_t>(x) * a.gate_expert_bytes;
-                        dev[1] = a.tma_gate;
-                    }
-                }
-            } else {
-                src[0] = a.shared_up;
-                src[1] = a.shared_gate;
-                dev[0] = dev[1] = a.tma_shared;
-            }
-            uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
-            uint32_t tx = 0;
-            // plain-load copies first (host-tagged or unaligned sources)
-            for (int pidx = 0; pidx < a.n_parts; ++pidx) {
-                const char *sp = src[pidx] + static_cast<uint64_t>(row0) * a.row_bytes;
-                const uint32_t bytes = static_cast<uint32_t>(nr) * a.row_bytes;
-                uint8_t *dp = stage + pidx * a.part_bytes;
-                const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
-                const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                if (dev[pidx]) {
-                    tx += static_cast<uint32_t>(a1 - a0);
-                } else if (host16[pidx]) {
-                    // the same 16-byte aligned range a bulk copy would move (it
-                    // stays inside the expert: 16-byte aligned base and size)
-                    const uint4 *s4 = reinterpret_cast<const uint4 *>(a0);
-                    uint4 *d4 = reinterpret_cast<uint4 *>(dp);
-                    const uint32_t n4 = static_cast<uint32_t>(a1 - a0) / 16u;
-                    for (uint32_t j = lane; j < n4; j += 32) d4[j] = s4[j];
-                } else {
-                    // 4-byte words when the source allows, else 2-byte units;
-                    // both keep the copy inside [sp, sp + bytes)
-                    const uintptr_t off = reinterpret_cast<uintptr_t>(sp) & 15u;
-                    if (((reinterpret_cast<uintptr_t>(sp) | bytes) & 3u) == 0) {
-                        const uint32_t *s32 = reinterpret_cast<const uint32_t *>(sp);
-                        uint32_t *d32 = reinterpret_cast<uint32_t *>(dp + off);
-                        for (uint32_t j = lane; j < bytes / 4; j += 32) d32[j] = s32[j];
-                    } else {
-                        const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sp);
-                        uint16_t *d16 = reinterpret_cast<uint16_t *>(dp + off);
-                        for (uint32_t j = lane; j < bytes / 2; j += 32) d16[j] = s16[j];
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) {
-                fence_proxy_async_smem();
-                mbar_arrive_expect_tx(&full[s], tx);
-                for (int pidx = 0; pidx < a.n_parts; ++pidx) {
-                    if (!dev[pidx]) continue;
-                    const char *sp = src[pidx] + static_cast<uint64_t>(row0) * a.row_bytes;
-                    const uint32_t bytes = static_cast<uint32_t>(nr) * a.row_bytes;
+                int g, row0, nr;
+                tile_coords(i, g, row0, nr);
+                const char *srcp[2];
+                int kind[2];
+                tile_sources(g, srcp[0], srcp[1], kind[0], kind[1]);
+                uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
+                const uint32_t bytes = static_cast<uint32_t>(nr) * rb;
+                uint32_t tx = 0;
+#pragma unroll
+                for (int pidx = 0; pidx < 2; ++pidx) {
+                    if (pidx >= a.n_parts) break;
+                    const char *sp = srcp[pidx] + static_cast<uint64_t>(row0) * rb;
+                    uint8_t *dp = stage + pidx * a.part_bytes;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
                     const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                    bulk_g2s(stage + pidx * a.part_bytes, reinterpret_cast<const void *>(a0), static_cast<uint32_t>(a1 - a0),
-                             &full[s], pol);
+                    if (kind[pidx] == 0) {
+                        tx += static_cast<uint32_t>(a1 - a0);
+                    } else if (kind[pidx] == 1) {
+                        // the range a bulk copy would move (inside the expert:
+                        // 16-byte aligned base and size), with 16-byte loads
+                        const uint4 *s4 = reinterpret_cast<const uint4 *>(a0);
+                        uint4 *d4 = reinterpret_cast<uint4 *>(dp);
+                        const uint32_t n4 = static_cast<uint32_t>(a1 - a0) / 16u;
+                        for (uint32_t j = lane; j < n4; j += 32) d4[j] = s4[j];
+                    } else {
+                        // 4-byte words when the source allows, else 2-byte units;
+                        // both keep the copy inside [sp, sp + bytes)
+                        const uintptr_t off = reinterpret_cast<uintptr_t>(sp) & 15u;
+                        if (((reinterpret_cast<uintptr_t>(sp) | bytes) & 3u) == 0) {
+                            const uint32_t *s32 = reinterpret_cast<const uint32_t *>(sp);
+                            uint32_t *d32 = reinterpret_cast<uint32_t *>(dp + off);
+                            for (uint32_t j = lane; j < bytes / 4; j += 32) d32[j] = s32[j];
+                        } else {
+                            const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sp);
+                            uint16_t *d16 = reinterpret_cast<uint16_t *>(dp + off);
+                            for (uint32_t j = lane; j < bytes / 2; j += 32) d16[j] = s16[j];
+                        }
+                    }
                 }
+                // generic-proxy writes to the stage are ordered before later
+                // bulk-copy (async-proxy) writes to it
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+                    for (int pidx = 0; pidx < 2; ++pidx) {
+                        if (pidx >= a.n_parts || kind[pidx] != 0) continue;
+                        const char *sp = srcp[pidx] + static_cast<uint64_t>(row0) * rb;
+                        const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
+                        const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
+                        bulk_g2s(stage + pidx * a.part_bytes, reinterpret_cast<const void *>(a0),
+                                 static_cast<uint32_t>(a1 - a0), &full[s], pol);
+                    }
+                }
+                __syncwarp();
             }
-            __syncwarp();
-            issued = i + 1;
+            issued = base + cnt;
         }
         // drain: never leave a bulk copy in flight when the CTA exits
         const int first = issued > S ? issued - S : 0;
         for (int i = first; i < issued; ++i) {
-            if (!mbar_wait_bounded(&full[i % S], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
+            if (!mbar_wait_sleep(&full[i % S], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
                 if (lane == 0) set_error(a.err, DERR_DRAIN);
                 break;
             }
@@ -767,19 +1074,20 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
 
     // ============================ consumer warps =============================
     const int K = a.K;
-    const uint32_t sb_bytes = a.slot_bytes;
     {
         // stage the activation vectors this CTA needs
         const int nk = C.n_keys;
         const bool q81 = (ACT == ACT_Q8_1);
         constexpr bool kq = is_kquant(TYPE);
+        constexpr int CE = chunk_of<TYPE>::CE;
+        const int NC = K / CE;
         const int nb = q81 ? K / 32 : (kq ? K / 256 : K / 32);
         for (int job = warp; job < nk * nb; job += GEMV_CONSUMER_WARPS) {
             const int v = job / nb, b = job % nb;
             const uint32_t key = C.keys[v];
             const uint32_t kc = key >> 16;
             const int t = static_cast<int>(key & 0xFFFFu);
-            uint8_t *slot = act_area + static_cast<size_t>(v) * sb_bytes;
+            uint8_t *slot = act_area + static_cast<size_t>(v) * a.slot_bytes;
             int8_t *q = reinterpret_cast<int8_t *>(slot);
             int16_t *bs = reinterpret_cast<int16_t *>(slot + K);
             float *sc = reinterpret_cast<float *>(slot + K + K / 8);
@@ -788,113 +1096,37 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
             if (kc == KEY_SHARED) { base = a.shared_y; off = t * a.shared_y_stride_col; }
             else { base = a.y; off = static_cast<int64_t>(kc) * a.stride_channel_y + t * a.stride_col_y; }
             if (q81) {
-                stage_q81_block(reinterpret_cast<const uint8_t *>(base) + off * 36, q, bs, sc, b, lane);
+                stage_q81_block<TYPE>(reinterpret_cast<const uint8_t *>(base) + off * 36, q, bs, sc, b, lane, NC);
             } else if (kq) {
-                stage_q8K_block(reinterpret_cast<const float *>(base) + off, q, bs, sc, b, lane);
+                const float *xv = reinterpret_cast<const float *>(base) + off;
+                stage_q8K_block<TYPE>(xv, (reinterpret_cast<uintptr_t>(xv) & 15u) == 0, q, bs, sc, b, lane, NC);
             } else {
-                stage_q80_block(reinterpret_cast<const float *>(base) + off, q, bs, sc, b, lane);
+                stage_q80_block<TYPE>(reinterpret_cast<const float *>(base) + off, q, bs, sc, b, lane, NC);
             }
         }
         asm volatile("bar.sync 1, %0;" ::"r"(GEMV_CONSUMER_WARPS * 32) : "memory");
     }
 
-    const int L = a.lanes_per_row;
-    const int RP = 32 / L;
-    const int sub = lane % L, rr = lane / L;
-    const int Tk = (K / fmt<TYPE>::qk) * fmt<TYPE>::tasks;
-    const uint32_t rb = a.row_bytes;
-
     for (int i = warp; i < n_tiles; i += GEMV_CONSUMER_WARPS) {
         const int s = i % S;
-        if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
+        if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
             if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
             break;
         }
         int g, row0, nr;
         tile_coords(i, g, row0, nr);
         const uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
-        // the tile's bytes start at (source address & 15) inside each part
-        const char *srcs[2];
-        if (g < U) {
-            const int x = C.uexp[g];
-            srcs[0] = reinterpret_cast<const char *>(reinterpret_cast<uintptr_t>(a.tbl[x]) & ~static_cast<uintptr_t>(1));
-            if (a.use_gate)
-                srcs[1] = a.tbl_gate ? reinterpret_cast<const char *>(reinterpret_cast<uintptr_t>(a.tbl_gate[x]) &
-                                                                      ~static_cast<uintptr_t>(1))
-                                     : a.gate_dense + static_cast<uint64_t>(x) * a.gate_expert_bytes;
-            else
-                srcs[1] = nullptr;
+        const char *s0, *s1;
+        int k0, k1;
+        tile_sources(g, s0, s1, k0, k1);
+        // each part's bytes start at (source address & 15) inside it
+        const uint8_t *up_rows = stage + ((reinterpret_cast<uintptr_t>(s0) + static_cast<uint64_t>(row0) * a.row_bytes) & 15u);
+        if (a.use_gate) {
+            const uint8_t *gate_rows =
+                stage + a.part_bytes + ((reinterpret_cast<uintptr_t>(s1) + static_cast<uint64_t>(row0) * a.row_bytes) & 15u);
+            consume_tile<TYPE, ACT, NMX, 2>(a, C, up_rows, gate_rows, nr, g, U, row0, act_area, lane);
         } else {
-            srcs[0] = a.shared_up;
-            srcs[1] = a.shared_gate;
-        }
-        const uint8_t *up_rows =
-            stage + ((reinterpret_cast<uintptr_t>(srcs[0]) + static_cast<uint64_t>(row0) * rb) & 15u);
-        const uint8_t *gate_rows =
-            a.use_gate ? stage + a.part_bytes + ((reinterpret_cast<uintptr_t>(srcs[1]) + static_cast<uint64_t>(row0) * rb) & 15u)
-                       : nullptr;
-
-        const int nmem = g < U ? (C.goff[g + 1] - C.goff[g]) : a.ncols_dst;
-        for (int mc = 0; mc < nmem; mc += NMX) {
-            Acts<NMX> A;
-            A.nm = nmem - mc < NMX ? nmem - mc : NMX;
-#pragma unroll
-            for (int m = 0; m < NMX; ++m) {
-                int v = 0;
-                if (m < A.nm) v = g < U ? C.eslot[C.gmem[C.goff[g] + mc + m]] : C.shslot[mc + m];
-                const uint8_t *slot = act_area + static_cast<size_t>(v) * sb_bytes;
-                A.q[m] = reinterpret_cast<const int8_t *>(slot);
-                A.bs[m] = reinterpret_cast<const int16_t *>(slot + K);
-                A.sc[m] = reinterpret_cast<const float *>(slot + K + K / 8);
-            }
-            for (int rbase = 0; rbase < nr; rbase += RP) {
-                const int r = rbase + rr;
-                const bool valid = r < nr;
-                float acc[NMX], accg[NMX];
-#pragma unroll
-                for (int m = 0; m < NMX; ++m) { acc[m] = 0.f; accg[m] = 0.f; }
-                if (valid) {
-                    const uint8_t *urow = up_rows + static_cast<size_t>(r) * rb;
-                    for (int t = sub; t < Tk; t += L) task_dot<TYPE, ACT, NMX>(urow, t, A, acc);
-                    if (a.use_gate) {
-                        const uint8_t *grow = gate_rows + static_cast<size_t>(r) * rb;
-                        for (int t = sub; t < Tk; t += L) task_dot<TYPE, ACT, NMX>(grow, t, A, accg);
-                    }
-                }
-                for (int off = L >> 1; off >= 1; off >>= 1) {
-#pragma unroll
-                    for (int m = 0; m < NMX; ++m) {
-                        acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], off);
-                        if (a.use_gate) accg[m] += __shfl_xor_sync(0xffffffffu, accg[m], off);
-                    }
-                }
-                if (valid && sub == 0) {
-                    const int row = row0 + r;
-#pragma unroll
-                    for (int m = 0; m < NMX; ++m) {
-                        if (m >= A.nm) break;
-                        int x = 0, t, p = 0;
-                        if (g < U) {
-                            const int e = C.gmem[C.goff[g] + mc + m];
-                            t = e / nch; p = e % nch; x = C.x[e];
-                        } else {
-                            t = mc + m;
-                        }
-                        float result = acc[m];
-                        if (a.has_fusion) {
-                            const int64_t bias_idx = static_cast<int64_t>(x) * a.stride_channel_dst + row;
-                            if (a.x_bias) result += a.x_bias[bias_idx];
-                            if (a.use_gate) {
-                                float gv = accg[m];
-                                if (a.gate_bias) gv += a.gate_bias[bias_idx];
-                                result = glu_apply(a.glu_op, gv, result, a.glu_limit);
-                            }
-                        }
-                        if (g < U) a.dst[p * a.stride_channel_dst + t * a.stride_col_dst + row] = result;
-                        else a.shared_dst[t * a.shared_stride_col_dst + row] = result;
-                    }
-                }
-            }
+            consume_tile<TYPE, ACT, NMX, 1>(a, C, up_rows, up_rows, nr, g, U, row0, act_area, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
