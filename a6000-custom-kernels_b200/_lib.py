@@ -102,6 +102,8 @@ def _declare(L):
         "moe_b200_fill_quantized": (i32, [i32, vp, i64, i64, ctypes.c_uint64, ctypes.c_float, vp]),
         "moe_b200_layer_decode_noalloc": (i32, [ctypes.POINTER(MoeLayerDesc), vp, vp, vp, i64, vp]),
         "moe_b200_noalloc_device_error": (i32, [vp, ctypes.POINTER(i32)]),
+        "moe_b200_layer_fused": (i32, [ctypes.POINTER(MoeLayerDesc), i64]),
+        "moe_b200_layer_set_fused": (i32, [i32]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)

@@ -5,6 +5,7 @@
 //   * the weighted combine of the per-pick down projections (+ shared expert);
 //   * synthetic quantized weights for tests and benchmarks.
 #include "moe_aux.h"
+#include "moe_route.cuh"
 #include "moe_common.cuh"
 
 namespace moe {
@@ -105,48 +106,9 @@ cudaError_t launch_quantize_act(int act_type, const float *x, void *y, int64_t n
 // ---------------------------------------------------------------------------
 __global__ void topk_softmax_kernel(const float *__restrict__ logits, int n_experts, int k, int norm_w,
                                     int32_t *__restrict__ ids, float *__restrict__ weights) {
-    const int t = blockIdx.x, lane = threadIdx.x;
-    const float *l = logits + static_cast<int64_t>(t) * n_experts;
-    int sel[32];
-    float selv[32];
-    for (int j = 0; j < k; ++j) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int e = lane; e < n_experts; e += 32) {
-            bool taken = false;
-            for (int q = 0; q < j; ++q) taken |= (sel[q] == e);
-            if (taken) continue;
-            const float v = l[e];
-            if (bi == 0x7fffffff || v > bv || (v == bv && e < bi)) { bv = v; bi = e; }
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
-        }
-        sel[j] = bi;
-        selv[j] = bv;
-    }
-    float mx = -INFINITY;
-    for (int e = lane; e < n_experts; e += 32) mx = fmaxf(mx, l[e]);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float sum = 0.f;
-    for (int e = lane; e < n_experts; e += 32) sum += expf(l[e] - mx);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (lane == 0) {
-        float ws = 0.f;
-        for (int j = 0; j < k; ++j) {
-            const float w = expf(selv[j] - mx) / sum;
-            ids[t * k + j] = sel[j];
-            weights[t * k + j] = w;
-            ws += w;
-        }
-        if (norm_w)
-            for (int j = 0; j < k; ++j) weights[t * k + j] = weights[t * k + j] / ws;
-    }
+    const int t = blockIdx.x;
+    route_token_warp(logits + static_cast<int64_t>(t) * n_experts, n_experts, k, norm_w, threadIdx.x,
+                     ids + static_cast<int64_t>(t) * k, weights + static_cast<int64_t>(t) * k);
 }
 
 cudaError_t launch_topk_softmax(const float *logits, int64_t n_tok, int64_t n_experts, int64_t k, int norm_w,

@@ -7,6 +7,7 @@
 namespace moe {
 
 struct GemvArgs;
+struct LayerArgs;
 
 cudaError_t launch_quantize_act(int act_type, const float *x, void *y, int64_t n_rows, int64_t n_cols,
                                 cudaStream_t st);
@@ -21,5 +22,12 @@ cudaError_t launch_fill_quantized(int type, void *dst, int64_t n_rows, int64_t n
 // `type` with activation semantics `act`. Returns 0, or a negative MOE_ERR_*
 // with *why set, or MOE_ERR_CUDA with *cuda_err set.
 int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
+
+// Fused layer kernel (moe_layer.cu) for gate/up type ta and down type tb:
+// plan_layer fills the geometry of `a` and returns 0 when the fused kernel
+// handles the layer, else -2 with *why; launch_layer plans and launches
+// (-3 with *cuda_err on a CUDA error).
+int plan_layer(int ta, int tb, LayerArgs &a, int *grid, size_t *smem, const char **why);
+int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
 
 }  // namespace moe

@@ -28,6 +28,7 @@
 #include "moe_aux.h"
 #include "moe_cache_b200.h"
 #include "moe_gemv.cuh"
+#include "moe_layer.cuh"
 
 namespace {
 
@@ -66,6 +67,7 @@ struct State {
     size_t used = 0;
     bool claim_device = true;
     bool debug = false;
+    bool layer_fused = true;      // one-kernel layer decode where supported
     std::string seed_path;
     std::unordered_map<const char *, Entry *> by_data;
     std::vector<Entry *> all;
@@ -134,6 +136,7 @@ void read_env() {
     g.seed_path = seed ? seed : "";
     g.claim_device = env_int("GGML_CUDA_MOE_CACHE_DEVICE", 1) != 0;
     g.debug = getenv("GGML_CUDA_MOE_CACHE_DEBUG") != nullptr;
+    g.layer_fused = env_int("GGML_CUDA_MOE_LAYER_FUSED", 1) != 0;
     g.env_read = true;
     if (g.enabled && g.debug)
         fprintf(stderr, "moe-cache: enabled, slots=%d budget=%.1f GB\n", g.slots,
@@ -595,6 +598,7 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 struct LayerWs {
     int32_t *ids;
     float *w, *h, *hs, *y, *ys;
+    uint32_t *gbar;   // fused kernel's grid barrier words (zero between launches)
     size_t bytes;
 };
 
@@ -609,8 +613,126 @@ LayerWs layer_ws(const moe_layer_desc *L, int64_t n_tok, char *base) {
     w.hs = reinterpret_cast<float *>(take(sizeof(float) * n_tok * F));
     w.y = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k * H));
     w.ys = reinterpret_cast<float *>(take(sizeof(float) * n_tok * H));
+    w.gbar = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 2));
     w.bytes = off;
     return w;
+}
+
+
+// One expert tensor of a fused layer: cache-registered tensors keep their
+// bookkeeping; host-tiered ones are read through their table, HBM-resident
+// ones at their dense address (what their table holds).
+int layer_tensor(const moe_tensor *t, bool registered, cudaStream_t st, moe::LayerTensor *out) {
+    *out = moe::LayerTensor{};
+    if (registered) {
+        Entry *e = nullptr;
+        const int rc = get_or_create(t, st, &e);
+        if (rc) return rc;
+        out->stamps = e->d_stamps;
+        out->cache_id = e->id;
+        if (e->host) out->tbl = e->d_tbl;
+    }
+    out->dense = static_cast<const char *>(t->data);
+    out->expert_bytes = t->nb[2];
+    out->tma = aligned16(t->data) && (t->nb[2] % 16) == 0 && (out->tbl || ptr_kind(t->data) == 2);
+    return MOE_OK;
+}
+
+// Fills the fused kernel's arguments for layer L (geometry excluded).
+int layer_args(const moe_layer_desc *L, const float *x, const float *logits, float *out, int64_t n_tok,
+               const LayerWs &w, cudaStream_t st, moe::LayerArgs *pa) {
+    moe::LayerArgs &a = *pa;
+    a = moe::LayerArgs{};
+    const int64_t k = L->k, F = L->F, H = L->H;
+    const bool shared = L->shared_type >= 0;
+    if (!aligned16(L->up.data) || !aligned16(L->gate.data) || !aligned16(L->down.data))
+        return fail(MOE_ERR_UNSUPPORTED, "expert tensor data must be 16-byte aligned");
+    if (shared && (!aligned16(L->shared_up) || !aligned16(L->shared_gate) || !aligned16(L->shared_down)))
+        return fail(MOE_ERR_UNSUPPORTED, "gate / shared expert data must be 16-byte aligned");
+    int rc = layer_tensor(&L->up, true, st, &a.up);
+    if (!rc) rc = layer_tensor(&L->gate, wants_locked(&L->gate) != 0, st, &a.gate);
+    if (!rc) rc = layer_tensor(&L->down, true, st, &a.down);
+    if (rc) return rc;
+    moe::GemvArgs &u = a.gu;
+    u.y = x;
+    u.stride_col_y = H;
+    u.nchannels_y = 1;
+    u.ncols_dst = static_cast<int32_t>(n_tok);
+    u.nchannels_dst = static_cast<int32_t>(k);
+    u.n_experts = static_cast<int32_t>(L->n_experts);
+    u.dst = w.h;
+    u.stride_col_dst = k * F;
+    u.stride_channel_dst = F;
+    u.has_fusion = 1;
+    u.use_gate = 1;
+    u.glu_op = L->glu_op;
+    u.glu_limit = L->glu_limit;
+    u.K = static_cast<int32_t>(H);
+    u.nrows = static_cast<int32_t>(F);
+    u.row_bytes = static_cast<uint32_t>(L->up.nb[1]);
+    moe::GemvArgs &d = a.dn;
+    d.y = w.h;
+    d.stride_col_y = k * F;
+    d.stride_channel_y = F;
+    d.nchannels_y = static_cast<int32_t>(k);
+    d.ncols_dst = static_cast<int32_t>(n_tok);
+    d.nchannels_dst = static_cast<int32_t>(k);
+    d.n_experts = static_cast<int32_t>(L->n_experts);
+    d.dst = w.y;
+    d.stride_col_dst = k * H;
+    d.stride_channel_dst = H;
+    d.K = static_cast<int32_t>(F);
+    d.nrows = static_cast<int32_t>(H);
+    d.row_bytes = static_cast<uint32_t>(L->down.nb[1]);
+    if (shared) {
+        u.shared_up = static_cast<const char *>(L->shared_up);
+        u.shared_gate = static_cast<const char *>(L->shared_gate);
+        u.shared_dst = w.hs;
+        u.shared_stride_col_dst = F;
+        u.tma_shared = (L->up.nb[2] % 16) == 0 && ptr_kind(L->shared_up) == 2 && ptr_kind(L->shared_gate) == 2;
+        d.shared_up = static_cast<const char *>(L->shared_down);
+        d.shared_dst = w.ys;
+        d.shared_stride_col_dst = H;
+        d.shared_y = w.hs;
+        d.shared_y_stride_col = F;
+        a.shared_down = static_cast<const char *>(L->shared_down);
+        a.tma_shared_down = (L->down.nb[2] % 16) == 0 && ptr_kind(L->shared_down) == 2;
+    }
+    a.logits = logits;
+    a.n_tok = static_cast<int32_t>(n_tok);
+    a.k = static_cast<int32_t>(k);
+    a.n_experts = static_cast<int32_t>(L->n_experts);
+    a.norm_w = L->norm_w;
+    a.ids_out = w.ids;
+    a.w_out = w.w;
+    a.out = out;
+    a.stats = g.d_stats;
+    a.clock = g.d_clock;
+    a.log_cap = kLogCap;
+    a.gbar = w.gbar;
+    a.err = g.d_err;
+    u.err = d.err = g.d_err;
+    return MOE_OK;
+}
+
+// True when the fused kernel takes this layer (type pair, sizes, switch).
+bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
+    if (!g.layer_fused) return false;
+    moe::LayerArgs a{};
+    a.n_tok = static_cast<int32_t>(n_tok);
+    a.k = static_cast<int32_t>(L->k);
+    a.n_experts = static_cast<int32_t>(L->n_experts);
+    a.gu.K = static_cast<int32_t>(L->H);
+    a.gu.nrows = static_cast<int32_t>(L->F);
+    a.gu.row_bytes = static_cast<uint32_t>(L->up.nb[1]);
+    a.dn.K = static_cast<int32_t>(L->F);
+    a.dn.nrows = static_cast<int32_t>(L->H);
+    a.dn.row_bytes = static_cast<uint32_t>(L->down.nb[1]);
+    a.gu.shared_up = L->shared_type >= 0 ? static_cast<const char *>(L->shared_up) : nullptr;
+    int grid = 0;
+    size_t smem = 0;
+    const char *why = "";
+    return moe::plan_layer(L->up.type, L->down.type, a, &grid, &smem, &why) == 0;
 }
 
 }  // namespace
@@ -811,6 +933,17 @@ int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *
     const int64_t k = L->k, F = L->F, H = L->H;
     if (L->up.ne[0] != H || L->up.ne[1] != F || L->down.ne[0] != F || L->down.ne[1] != H)
         return fail(MOE_ERR_INVALID, "expert tensor shapes do not match H/F");
+    if (layer_fusable(L, n_tok)) {
+        moe::LayerArgs a;
+        int rc = layer_args(L, x, logits, out, n_tok, w, st, &a);
+        if (rc) return rc;
+        const char *why = "";
+        cudaError_t ce = cudaSuccess;
+        rc = moe::launch_layer(L->up.type, L->down.type, a, st, &why, &ce);
+        if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+        if (rc) return fail(rc, "%s", why);
+        return MOE_OK;
+    }
     CK(moe::launch_topk_softmax(logits, n_tok, L->n_experts, k, L->norm_w, w.ids, w.w, st));
 
     moe_fusion_device fd{};
@@ -862,6 +995,20 @@ int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *
     rc = run_mmvq(d, st);
     if (rc) return rc;
     CK(moe::launch_combine(w.y, w.w, shared ? w.ys : nullptr, out, n_tok, H, k, st));
+    return MOE_OK;
+}
+
+int moe_b200_layer_fused(const moe_layer_desc *L, int64_t n_tok) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || n_tok < 1 || n_tok > 8 || L->gate.type != L->up.type) return 0;
+    return layer_fusable(L, n_tok) ? 1 : 0;
+}
+
+int moe_b200_layer_set_fused(int32_t enable) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    g.layer_fused = enable != 0;
     return MOE_OK;
 }
 

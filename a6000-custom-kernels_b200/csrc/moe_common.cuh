@@ -20,7 +20,7 @@ enum : int { ACT_Q8_1 = 0, ACT_CPU = 1 };
 // device error codes (first writer wins)
 enum : int {
     DERR_NONE = 0, DERR_BAD_ID = 1, DERR_TOO_MANY_KEYS = 2, DERR_TIMEOUT_FULL = 3,
-    DERR_TIMEOUT_EMPTY = 4, DERR_TOO_MANY_SEGMENTS = 5, DERR_DRAIN = 6,
+    DERR_TIMEOUT_EMPTY = 4, DERR_TOO_MANY_SEGMENTS = 5, DERR_DRAIN = 6, DERR_GRID_BARRIER = 7,
 };
 
 template <int T> struct fmt;
@@ -205,6 +205,12 @@ __device__ __forceinline__ uint32_t spread4_bit4(uint32_t nib) { return ((nib & 
 __device__ __forceinline__ int nearest_int_dev(float prod) {
     const float val = __fadd_rn(prod, 12582912.f);
     return (__float_as_int(val) & 0x007fffff) - 0x00400000;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ void set_error(int *err, int code) {

@@ -111,19 +111,25 @@ __device__ __forceinline__ int bs_hi(int w) { return w >> 16; }
 // Q8_K block (256 f32 at x): llama.cpp quantize_row_q8_K_ref, bit-exact. Lane l
 // holds elements 4l..4l+3 and 128+4l..128+4l+3 (coalesced float4 loads when x
 // is 16-byte aligned).
-template <int TYPE>
+// f32 loads; CG: through L2 only (data another CTA of the same grid wrote)
+template <bool CG> __device__ __forceinline__ float ld_f32(const float *p) { return CG ? __ldcg(p) : *p; }
+template <bool CG> __device__ __forceinline__ float4 ld_f32x4(const float *p) {
+    return CG ? __ldcg(reinterpret_cast<const float4 *>(p)) : *reinterpret_cast<const float4 *>(p);
+}
+
+template <int TYPE, bool CG = false>
 __device__ __forceinline__ void stage_q8K_block(const float *x, bool al16, int8_t *q, int16_t *bs, float *sc, int b,
                                                 int lane, int NC) {
     float v[8];
     const float *xb = x + b * 256;
     if (al16) {
-        const float4 u0 = reinterpret_cast<const float4 *>(xb)[lane];
-        const float4 u1 = reinterpret_cast<const float4 *>(xb + 128)[lane];
+        const float4 u0 = ld_f32x4<CG>(xb + 4 * lane);
+        const float4 u1 = ld_f32x4<CG>(xb + 128 + 4 * lane);
         v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
         v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
     } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) { v[j] = xb[4 * lane + j]; v[4 + j] = xb[128 + 4 * lane + j]; }
+        for (int j = 0; j < 4; ++j) { v[j] = ld_f32<CG>(xb + 4 * lane + j); v[4 + j] = ld_f32<CG>(xb + 128 + 4 * lane + j); }
     }
     float amax = 0.f, mval = 0.f;
     int midx = 1 << 30;
@@ -178,10 +184,10 @@ __device__ __forceinline__ void stage_q8K_block(const float *x, bool al16, int8_
 }
 
 // Q8_0 block (32) from f32: llama.cpp quantize_row_q8_0_ref, bit-exact.
-template <int TYPE>
+template <int TYPE, bool CG = false>
 __device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16_t *bs, float *sc, int b, int lane,
                                                 int NC) {
-    const float v = x[b * 32 + lane];
+    const float v = ld_f32<CG>(x + b * 32 + lane);
     float amax = fabsf(v);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
@@ -194,6 +200,20 @@ __device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16
     for (int off = 8; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if ((lane & 15) == 0) bs[b * 2 + (lane >> 4)] = static_cast<int16_t>(s);
     if (lane == 0) sc[b] = __half2float(__float2half_rn(d));
+}
+
+// Block b of an f32 activation vector into its slot with llama.cpp CPU
+// semantics: Q8_K blocks for K-quant weights, Q8_0 blocks otherwise.
+template <int TYPE, bool CG = false>
+__device__ __forceinline__ void stage_f32_block(const float *xv, uint8_t *slot, int K, int b, int lane) {
+    constexpr int CE = chunk_of<TYPE>::CE;
+    int8_t *q = reinterpret_cast<int8_t *>(slot);
+    int16_t *bs = reinterpret_cast<int16_t *>(slot + K);
+    float *sc = reinterpret_cast<float *>(slot + K + K / 8);
+    if constexpr (is_kquant(TYPE))
+        stage_q8K_block<TYPE, CG>(xv, (reinterpret_cast<uintptr_t>(xv) & 15u) == 0, q, bs, sc, b, lane, K / CE);
+    else
+        stage_q80_block<TYPE, CG>(xv, q, bs, sc, b, lane, K / CE);
 }
 
 // Q8_1 block (36 bytes) as given: copy qs, scale = d, per-16 sums.
@@ -669,67 +689,211 @@ __device__ __forceinline__ void consume_tile(const GemvArgs &a, const GemvCtrl &
     }
 }
 
-template <int TYPE, int ACT, int NMX>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_constant__ GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + GEMV_MAX_STAGES;
-    GemvCtrl &C = *reinterpret_cast<GemvCtrl *>(smem + 2 * GEMV_MAX_STAGES * 8);
-    uint8_t *act_area = smem + a.ctrl_bytes;
-    uint8_t *stage_area = act_area + static_cast<size_t>(a.act_slots) * a.slot_bytes;
-    const uint32_t stage_bytes = a.part_bytes * static_cast<uint32_t>(a.n_parts);
+// Weight sources of one tile: part p < n_parts holds rows [row0, row0 + nr)
+// of src[p], rb bytes each. kind: 0 = bulk copy, 1 = host memory, copied with
+// 16-byte loads, 2 = plain 4/2-byte copies (source not 16-byte aligned).
+struct TileSrc {
+    const char *src[2];
+    int kind[2];
+    int n_parts, row0, nr;
+    uint32_t rb;
+};
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nch = a.nchannels_dst;
-    const int N = a.ncols_dst * nch;
-    const bool has_shared = a.shared_up != nullptr;
-    const int S = a.n_stages;
-
-    for (int s = tid; s < S; s += blockDim.x) {
-        mbar_init(&full[s], 1);
-        mbar_init(&empty[s], 1);
-    }
-    if (tid < S) fence_mbar_init();
-    if (tid == 0) C.fail = 0;
-    __syncthreads();
-
-    // ---- routed entries: validate, de-duplicate, resolve table entries ------
-    // Entry e = tok * nchannels_dst + pick. Groups (distinct experts) are
-    // numbered in first-occurrence order; gmem lists each group's entries
-    // (CSR, offsets goff). usrc/ukind hold each group's weight sources.
-    auto resolve = [&](int u, int x) {
-        const uintptr_t p = reinterpret_cast<uintptr_t>(a.tbl[x]);
-        C.usrc[u][0] = reinterpret_cast<const char *>(p & ~static_cast<uintptr_t>(1));
-        C.ukind[u][0] = static_cast<uint8_t>((p & 1u) ? (a.tma_main ? 1 : 2) : (a.tma_main ? 0 : 2));
-        C.uhost[u][0] = static_cast<uint8_t>(p & 1u);
-        C.usrc[u][1] = nullptr;
-        C.ukind[u][1] = 0;
-        C.uhost[u][1] = 0;
-        if (a.use_gate) {
-            if (a.tbl_gate) {
-                const uintptr_t pg = reinterpret_cast<uintptr_t>(a.tbl_gate[x]);
-                C.usrc[u][1] = reinterpret_cast<const char *>(pg & ~static_cast<uintptr_t>(1));
-                C.ukind[u][1] = static_cast<uint8_t>((pg & 1u) ? (a.tma_gate ? 1 : 2) : (a.tma_gate ? 0 : 2));
-                C.uhost[u][1] = static_cast<uint8_t>(pg & 1u);
-            } else {
-                C.usrc[u][1] = a.gate_dense + static_cast<uint64_t>(x) * a.gate_expert_bytes;
-                C.ukind[u][1] = static_cast<uint8_t>(a.tma_gate ? 0 : 2);
+// The producer warp: streams tiles 0..n_tiles-1 through the S-stage ring
+// (tile i -> stage i % S, phase i / S). Part p of a tile lands at
+// stage + p * part_bytes + (source address & 15). Tiles are issued in rounds
+// of up to min(32, S): within a round no tile reuses a stage of the same
+// round, so every lane waits for its own stage and issues its own bulk copies.
+// Tiles that need plain copies (host memory or unaligned sources) follow,
+// one at a time, copied by the whole warp. Ends after every issued copy has
+// landed, so no bulk copy is in flight when the CTA exits.
+template <class Describe>
+__device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full, uint64_t *empty,
+                                              uint8_t *stage_area, uint32_t stage_bytes, uint32_t part_bytes,
+                                              Describe describe, uint64_t timeout_ns, int *err, int lane) {
+    const uint64_t pol = l2_evict_first_policy();
+    const int R = S < 32 ? S : 32;
+    int issued = 0;
+    bool ok = true;
+    for (int base = 0; base < n_tiles && ok; base += R) {
+        const int cnt = (n_tiles - base) < R ? (n_tiles - base) : R;
+        bool plain_tile = false, lane_ok = true;
+        if (lane < cnt) {
+            const int i = base + lane, s = i % S;
+            TileSrc ts;
+            describe(i, ts);
+            plain_tile = ts.kind[0] != 0 || (ts.n_parts > 1 && ts.kind[1] != 0);
+            if (!plain_tile) {
+                if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), timeout_ns)) {
+                    lane_ok = false;
+                } else {
+                    const uint32_t bytes = static_cast<uint32_t>(ts.nr) * ts.rb;
+                    uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
+                    uintptr_t lo[2], hi[2];
+                    uint32_t tx = 0;
+#pragma unroll
+                    for (int p = 0; p < 2; ++p) {
+                        if (p >= ts.n_parts) break;
+                        const uintptr_t sp = reinterpret_cast<uintptr_t>(ts.src[p]) + static_cast<uint64_t>(ts.row0) * ts.rb;
+                        lo[p] = sp & ~static_cast<uintptr_t>(15);
+                        hi[p] = (sp + bytes + 15u) & ~static_cast<uintptr_t>(15);
+                        tx += static_cast<uint32_t>(hi[p] - lo[p]);
+                    }
+                    mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+                    for (int p = 0; p < 2; ++p) {
+                        if (p >= ts.n_parts) break;
+                        bulk_g2s(stage + p * part_bytes, reinterpret_cast<const void *>(lo[p]),
+                                 static_cast<uint32_t>(hi[p] - lo[p]), &full[s], pol);
+                    }
+                }
             }
         }
-    };
+        if (__any_sync(0xffffffffu, !lane_ok)) {
+            if (lane == 0) set_error(err, DERR_TIMEOUT_EMPTY);
+            issued = base + cnt;
+            ok = false;
+            break;
+        }
+        unsigned pending = __ballot_sync(0xffffffffu, plain_tile);
+        while (pending) {
+            const int l = __ffs(pending) - 1;
+            pending &= pending - 1u;
+            const int i = base + l, s = i % S;
+            if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), timeout_ns)) {
+                if (lane == 0) set_error(err, DERR_TIMEOUT_EMPTY);
+                ok = false;
+                break;
+            }
+            TileSrc ts;
+            describe(i, ts);
+            uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
+            const uint32_t bytes = static_cast<uint32_t>(ts.nr) * ts.rb;
+            uint32_t tx = 0;
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                if (p >= ts.n_parts) break;
+                const char *sp = ts.src[p] + static_cast<uint64_t>(ts.row0) * ts.rb;
+                uint8_t *dp = stage + p * part_bytes;
+                const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
+                const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
+                if (ts.kind[p] == 0) {
+                    tx += static_cast<uint32_t>(a1 - a0);
+                } else if (ts.kind[p] == 1) {
+                    // the range a bulk copy would move (inside the expert:
+                    // 16-byte aligned base and size), with 16-byte loads
+                    const uint4 *s4 = reinterpret_cast<const uint4 *>(a0);
+                    uint4 *d4 = reinterpret_cast<uint4 *>(dp);
+                    const uint32_t n4 = static_cast<uint32_t>(a1 - a0) / 16u;
+                    for (uint32_t j = lane; j < n4; j += 32) d4[j] = s4[j];
+                } else {
+                    // 4-byte words when the source allows, else 2-byte units;
+                    // both keep the copy inside [sp, sp + bytes)
+                    const uintptr_t off = reinterpret_cast<uintptr_t>(sp) & 15u;
+                    if (((reinterpret_cast<uintptr_t>(sp) | bytes) & 3u) == 0) {
+                        const uint32_t *s32 = reinterpret_cast<const uint32_t *>(sp);
+                        uint32_t *d32 = reinterpret_cast<uint32_t *>(dp + off);
+                        for (uint32_t j = lane; j < bytes / 4; j += 32) d32[j] = s32[j];
+                    } else {
+                        const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sp);
+                        uint16_t *d16 = reinterpret_cast<uint16_t *>(dp + off);
+                        for (uint32_t j = lane; j < bytes / 2; j += 32) d16[j] = s16[j];
+                    }
+                }
+            }
+            // generic-proxy writes to the stage are ordered before later
+            // bulk-copy (async-proxy) writes to it
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    if (p >= ts.n_parts || ts.kind[p] != 0) continue;
+                    const char *sp = ts.src[p] + static_cast<uint64_t>(ts.row0) * ts.rb;
+                    const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
+                    const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
+                    bulk_g2s(stage + p * part_bytes, reinterpret_cast<const void *>(a0), static_cast<uint32_t>(a1 - a0),
+                             &full[s], pol);
+                }
+            }
+            __syncwarp();
+        }
+        issued = base + cnt;
+    }
+    // drain: never leave a bulk copy in flight when the CTA exits
+    const int first = issued > S ? issued - S : 0;
+    for (int i = first; i < issued; ++i) {
+        if (!mbar_wait_sleep(&full[i % S], static_cast<uint32_t>((i / S) & 1), timeout_ns)) {
+            if (lane == 0) set_error(err, DERR_DRAIN);
+            break;
+        }
+    }
+}
+
+// This CTA's contiguous share of the row space of n_groups groups of nrows
+// rows (CTA b of G takes rows [b*q + min(b, rem), ...) with q, rem =
+// divmod(rows, G)), cut at group boundaries into segments of rpt-row tiles.
+// One thread; 32-bit arithmetic (launchers keep n_groups * nrows < 2^31).
+__device__ __forceinline__ int build_segments(GemvCtrl &C, uint32_t n_groups, uint32_t nrows, int rpt, int *err) {
+    const uint32_t Rt = n_groups * nrows;
+    const uint32_t G = gridDim.x, bid = blockIdx.x;
+    const uint32_t q = Rt / G, rem = Rt % G;
+    const uint32_t r_begin = bid * q + (bid < rem ? bid : rem);
+    const uint32_t r_end = r_begin + q + (bid < rem ? 1u : 0u);
+    int ns = 0, nt = 0;
+    uint32_t r = r_begin;
+    while (r < r_end) {
+        const uint32_t g = r / nrows;
+        const uint32_t r0 = r - g * nrows;
+        const uint32_t g_end = (g + 1) * nrows;
+        const uint32_t r1 = (g_end < r_end ? g_end : r_end) - g * nrows;
+        if (ns >= GEMV_MAX_SEGMENTS) { C.fail = 1; set_error(err, DERR_TOO_MANY_SEGMENTS); break; }
+        C.seg_g[ns] = static_cast<int32_t>(g);
+        C.seg_r0[ns] = static_cast<int32_t>(r0);
+        C.seg_r1[ns] = static_cast<int32_t>(r1);
+        C.seg_t0[ns] = nt;
+        nt += (static_cast<int>(r1 - r0) + rpt - 1) / rpt;
+        ns++;
+        r = g * nrows + r1;
+    }
+    C.seg_t0[ns] = nt;
+    C.n_seg = ns;
+    C.n_tiles = nt;
+    return ns;
+}
+
+// Tile i of the segment list: group, first row, row count.
+__device__ __forceinline__ void segment_tile(const GemvCtrl &C, int n_seg, int rpt, int i, int &g, int &row0, int &nr) {
+    int s = 0;
+    while (s + 1 < n_seg && C.seg_t0[s + 1] <= i) ++s;
+    g = C.seg_g[s];
+    row0 = C.seg_r0[s] + (i - C.seg_t0[s]) * rpt;
+    const int lim = C.seg_r1[s];
+    nr = (lim - row0) < rpt ? (lim - row0) : rpt;
+}
+
+// Groups the N routed entries by expert. x_of(e) gives entry e's expert;
+// groups (distinct experts) are numbered in first-occurrence order, gmem lists
+// each group's entries (CSR, offsets goff) and resolve(u, x) records group u's
+// weight sources. Called by every thread of the block; ends with a block
+// barrier. A bad expert id sets C.fail.
+template <class XOf, class Resolve>
+__device__ __forceinline__ void build_groups(GemvCtrl &C, int N, int n_experts, XOf x_of, Resolve resolve,
+                                             int *err) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (N <= 32) {
         // one warp, no block barriers: match_any groups equal experts
         if (warp == 0) {
             int x = -1 - lane;
             bool bad = false;
             if (lane < N) {
-                const int t = lane / nch, p = lane % nch;
-                x = a.ids[p + static_cast<int64_t>(t) * a.ids_stride];
-                bad = x < 0 || x >= a.n_experts;
+                x = x_of(lane);
+                bad = x < 0 || x >= n_experts;
                 C.x[lane] = x;
             }
             if (__ballot_sync(0xffffffffu, bad)) {
-                if (lane == 0) { C.fail = 1; set_error(a.err, DERR_BAD_ID); }
+                if (lane == 0) { C.fail = 1; set_error(err, DERR_BAD_ID); }
             } else {
                 const unsigned same = __match_any_sync(0xffffffffu, x);
                 const int f = __ffs(same) - 1;
@@ -758,9 +922,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
         }
     } else {
         for (int e = tid; e < N; e += blockDim.x) {
-            const int t = e / nch, p = e % nch;
-            const int x = a.ids[p + static_cast<int64_t>(t) * a.ids_stride];
-            if (x < 0 || x >= a.n_experts) { C.fail = 1; set_error(a.err, DERR_BAD_ID); }
+            const int x = x_of(e);
+            if (x < 0 || x >= n_experts) { C.fail = 1; set_error(err, DERR_BAD_ID); }
             C.x[e] = x;
         }
         __syncthreads();
@@ -816,6 +979,59 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
         }
     }
     __syncthreads();
+}
+
+template <int TYPE, int ACT, int NMX>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + GEMV_MAX_STAGES;
+    GemvCtrl &C = *reinterpret_cast<GemvCtrl *>(smem + 2 * GEMV_MAX_STAGES * 8);
+    uint8_t *act_area = smem + a.ctrl_bytes;
+    uint8_t *stage_area = act_area + static_cast<size_t>(a.act_slots) * a.slot_bytes;
+    const uint32_t stage_bytes = a.part_bytes * static_cast<uint32_t>(a.n_parts);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nch = a.nchannels_dst;
+    const int N = a.ncols_dst * nch;
+    const bool has_shared = a.shared_up != nullptr;
+    const int S = a.n_stages;
+
+    for (int s = tid; s < S; s += blockDim.x) {
+        mbar_init(&full[s], 1);
+        mbar_init(&empty[s], 1);
+    }
+    if (tid < S) fence_mbar_init();
+    if (tid == 0) C.fail = 0;
+    __syncthreads();
+
+    // ---- routed entries: validate, de-duplicate, resolve table entries ------
+    // Entry e = tok * nchannels_dst + pick. Groups (distinct experts) are
+    // numbered in first-occurrence order; gmem lists each group's entries
+    // (CSR, offsets goff). usrc/ukind hold each group's weight sources.
+    auto resolve = [&](int u, int x) {
+        const uintptr_t p = reinterpret_cast<uintptr_t>(a.tbl[x]);
+        C.usrc[u][0] = reinterpret_cast<const char *>(p & ~static_cast<uintptr_t>(1));
+        C.ukind[u][0] = static_cast<uint8_t>((p & 1u) ? (a.tma_main ? 1 : 2) : (a.tma_main ? 0 : 2));
+        C.uhost[u][0] = static_cast<uint8_t>(p & 1u);
+        C.usrc[u][1] = nullptr;
+        C.ukind[u][1] = 0;
+        C.uhost[u][1] = 0;
+        if (a.use_gate) {
+            if (a.tbl_gate) {
+                const uintptr_t pg = reinterpret_cast<uintptr_t>(a.tbl_gate[x]);
+                C.usrc[u][1] = reinterpret_cast<const char *>(pg & ~static_cast<uintptr_t>(1));
+                C.ukind[u][1] = static_cast<uint8_t>((pg & 1u) ? (a.tma_gate ? 1 : 2) : (a.tma_gate ? 0 : 2));
+                C.uhost[u][1] = static_cast<uint8_t>(pg & 1u);
+            } else {
+                C.usrc[u][1] = a.gate_dense + static_cast<uint64_t>(x) * a.gate_expert_bytes;
+                C.ukind[u][1] = static_cast<uint8_t>(a.tma_gate ? 0 : 2);
+            }
+        }
+    };
+    build_groups(
+        C, N, a.n_experts,
+        [&](int e) { return a.ids[e % nch + static_cast<int64_t>(e / nch) * a.ids_stride]; }, resolve, a.err);
     if (C.fail) return;
     const int U = C.n_unique;
 
@@ -855,31 +1071,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
     // (32-bit arithmetic: the launcher guarantees groups * nrows < 2^31)
     const int rpt = a.rows_per_tile;
     if (tid == 0) {
-        const uint32_t nrows = static_cast<uint32_t>(a.nrows);
-        const uint32_t Rt = static_cast<uint32_t>(U + (has_shared ? 1 : 0)) * nrows;
-        const uint32_t G = gridDim.x, bid = blockIdx.x;
-        const uint32_t q = Rt / G, rem = Rt % G;
-        const uint32_t r_begin = bid * q + (bid < rem ? bid : rem);
-        const uint32_t r_end = r_begin + q + (bid < rem ? 1u : 0u);
-        int ns = 0, nt = 0;
-        uint32_t r = r_begin;
-        while (r < r_end) {
-            const uint32_t g = r / nrows;
-            const uint32_t r0 = r - g * nrows;
-            const uint32_t g_end = (g + 1) * nrows;
-            const uint32_t r1 = (g_end < r_end ? g_end : r_end) - g * nrows;
-            if (ns >= GEMV_MAX_SEGMENTS) { C.fail = 1; set_error(a.err, DERR_TOO_MANY_SEGMENTS); break; }
-            C.seg_g[ns] = static_cast<int32_t>(g);
-            C.seg_r0[ns] = static_cast<int32_t>(r0);
-            C.seg_r1[ns] = static_cast<int32_t>(r1);
-            C.seg_t0[ns] = nt;
-            nt += (static_cast<int>(r1 - r0) + rpt - 1) / rpt;
-            ns++;
-            r = g * nrows + r1;
-        }
-        C.seg_t0[ns] = nt;
-        C.n_seg = ns;
-        C.n_tiles = nt;
+        const int ns = build_segments(C, static_cast<uint32_t>(U + (has_shared ? 1 : 0)),
+                                      static_cast<uint32_t>(a.nrows), rpt, a.err);
         // activation keys: (channel_y << 16 | token), KEY_SHARED for the shared block
         int nk = 0;
         for (int s = 0; s < ns && !C.fail; ++s) {
@@ -916,14 +1109,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
     if (C.fail) return;
     const int n_tiles = C.n_tiles, n_seg = C.n_seg;
 
-    auto tile_coords = [&](int i, int &g, int &row0, int &nr) {
-        int s = 0;
-        while (s + 1 < n_seg && C.seg_t0[s + 1] <= i) ++s;
-        g = C.seg_g[s];
-        row0 = C.seg_r0[s] + (i - C.seg_t0[s]) * rpt;
-        const int lim = C.seg_r1[s];
-        nr = (lim - row0) < rpt ? (lim - row0) : rpt;
-    };
+    auto tile_coords = [&](int i, int &g, int &row0, int &nr) { segment_tile(C, n_seg, rpt, i, g, row0, nr); };
     // source of each part of group g's tiles; kind: 0 = bulk copy, 1 = host with
     // 16-byte plain copies, 2 = plain 4/2-byte copies (unaligned source)
     auto tile_sources = [&](int g, const char *&s0, const char *&s1, int &k0, int &k1) {
@@ -941,134 +1127,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
 
     if (warp == GEMV_CONSUMER_WARPS) {
         // =========================== producer warp ===========================
-        // Tiles are issued in rounds of up to min(32, S): within a round no
-        // tile reuses a stage of the same round, so every lane can wait for
-        // its own stage and issue its own bulk copies in parallel. Tiles that
-        // need plain copies (host-tagged or unaligned sources) follow, one at a
-        // time, copied by the whole warp.
-        const uint64_t pol = l2_evict_first_policy();
-        const int R = S < 32 ? S : 32;
-        const uint32_t rb = a.row_bytes;
-        int issued = 0;
-        bool ok = true;
-        for (int base = 0; base < n_tiles && ok; base += R) {
-            const int cnt = (n_tiles - base) < R ? (n_tiles - base) : R;
-            bool plain_tile = false, lane_ok = true;
-            if (lane < cnt) {
-                const int i = base + lane, s = i % S;
-                int g, row0, nr;
-                tile_coords(i, g, row0, nr);
-                const char *src0, *src1;
-                int k0, k1;
-                tile_sources(g, src0, src1, k0, k1);
-                plain_tile = k0 != 0 || (a.n_parts > 1 && k1 != 0);
-                if (!plain_tile) {
-                    if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), a.timeout_ns)) {
-                        lane_ok = false;
-                    } else {
-                        const uint32_t bytes = static_cast<uint32_t>(nr) * rb;
-                        uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
-                        const uintptr_t p0 = reinterpret_cast<uintptr_t>(src0) + static_cast<uint64_t>(row0) * rb;
-                        const uintptr_t a00 = p0 & ~static_cast<uintptr_t>(15), a01 = (p0 + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                        uint32_t tx = static_cast<uint32_t>(a01 - a00);
-                        uintptr_t a10 = 0, a11 = 0;
-                        if (a.n_parts > 1) {
-                            const uintptr_t p1 = reinterpret_cast<uintptr_t>(src1) + static_cast<uint64_t>(row0) * rb;
-                            a10 = p1 & ~static_cast<uintptr_t>(15);
-                            a11 = (p1 + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                            tx += static_cast<uint32_t>(a11 - a10);
-                        }
-                        mbar_arrive_expect_tx(&full[s], tx);
-                        bulk_g2s(stage, reinterpret_cast<const void *>(a00), static_cast<uint32_t>(a01 - a00), &full[s], pol);
-                        if (a.n_parts > 1)
-                            bulk_g2s(stage + a.part_bytes, reinterpret_cast<const void *>(a10), static_cast<uint32_t>(a11 - a10),
-                                     &full[s], pol);
-                    }
-                }
-            }
-            if (__any_sync(0xffffffffu, !lane_ok)) {
-                if (lane == 0) set_error(a.err, DERR_TIMEOUT_EMPTY);
-                issued = base + cnt;
-                ok = false;
-                break;
-            }
-            unsigned pending = __ballot_sync(0xffffffffu, plain_tile);
-            while (pending) {
-                const int l = __ffs(pending) - 1;
-                pending &= pending - 1u;
-                const int i = base + l, s = i % S;
-                if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), a.timeout_ns)) {
-                    if (lane == 0) set_error(a.err, DERR_TIMEOUT_EMPTY);
-                    ok = false;
-                    break;
-                }
-                int g, row0, nr;
-                tile_coords(i, g, row0, nr);
-                const char *srcp[2];
-                int kind[2];
-                tile_sources(g, srcp[0], srcp[1], kind[0], kind[1]);
-                uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
-                const uint32_t bytes = static_cast<uint32_t>(nr) * rb;
-                uint32_t tx = 0;
-#pragma unroll
-                for (int pidx = 0; pidx < 2; ++pidx) {
-                    if (pidx >= a.n_parts) break;
-                    const char *sp = srcp[pidx] + static_cast<uint64_t>(row0) * rb;
-                    uint8_t *dp = stage + pidx * a.part_bytes;
-                    const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
-                    const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                    if (kind[pidx] == 0) {
-                        tx += static_cast<uint32_t>(a1 - a0);
-                    } else if (kind[pidx] == 1) {
-                        // the range a bulk copy would move (inside the expert:
-                        // 16-byte aligned base and size), with 16-byte loads
-                        const uint4 *s4 = reinterpret_cast<const uint4 *>(a0);
-                        uint4 *d4 = reinterpret_cast<uint4 *>(dp);
-                        const uint32_t n4 = static_cast<uint32_t>(a1 - a0) / 16u;
-                        for (uint32_t j = lane; j < n4; j += 32) d4[j] = s4[j];
-                    } else {
-                        // 4-byte words when the source allows, else 2-byte units;
-                        // both keep the copy inside [sp, sp + bytes)
-                        const uintptr_t off = reinterpret_cast<uintptr_t>(sp) & 15u;
-                        if (((reinterpret_cast<uintptr_t>(sp) | bytes) & 3u) == 0) {
-                            const uint32_t *s32 = reinterpret_cast<const uint32_t *>(sp);
-                            uint32_t *d32 = reinterpret_cast<uint32_t *>(dp + off);
-                            for (uint32_t j = lane; j < bytes / 4; j += 32) d32[j] = s32[j];
-                        } else {
-                            const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sp);
-                            uint16_t *d16 = reinterpret_cast<uint16_t *>(dp + off);
-                            for (uint32_t j = lane; j < bytes / 2; j += 32) d16[j] = s16[j];
-                        }
-                    }
-                }
-                // generic-proxy writes to the stage are ordered before later
-                // bulk-copy (async-proxy) writes to it
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(&full[s], tx);
-#pragma unroll
-                    for (int pidx = 0; pidx < 2; ++pidx) {
-                        if (pidx >= a.n_parts || kind[pidx] != 0) continue;
-                        const char *sp = srcp[pidx] + static_cast<uint64_t>(row0) * rb;
-                        const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
-                        const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                        bulk_g2s(stage + pidx * a.part_bytes, reinterpret_cast<const void *>(a0),
-                                 static_cast<uint32_t>(a1 - a0), &full[s], pol);
-                    }
-                }
-                __syncwarp();
-            }
-            issued = base + cnt;
-        }
-        // drain: never leave a bulk copy in flight when the CTA exits
-        const int first = issued > S ? issued - S : 0;
-        for (int i = first; i < issued; ++i) {
-            if (!mbar_wait_sleep(&full[i % S], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
-                if (lane == 0) set_error(a.err, DERR_DRAIN);
-                break;
-            }
-        }
+        produce_tiles(
+            n_tiles, S, full, empty, stage_area, stage_bytes, a.part_bytes,
+            [&](int i, TileSrc &ts) {
+                int g;
+                tile_coords(i, g, ts.row0, ts.nr);
+                tile_sources(g, ts.src[0], ts.src[1], ts.kind[0], ts.kind[1]);
+                ts.n_parts = a.n_parts;
+                ts.rb = a.row_bytes;
+            },
+            a.timeout_ns, a.err, lane);
         return;
     }
 

@@ -1,0 +1,45 @@
+// moe_layer_launch.cuh -- cooperative launch of one moe_layer_kernel
+// instantiation (explicitly instantiated per gate/up type in moe_layer_*.cu).
+#pragma once
+#include <cstdio>
+
+#include "moe_layer.cuh"
+
+namespace moe {
+
+extern char g_layer_diag[256];
+
+template <int TA, int TB>
+cudaError_t launch_layer_t(const LayerArgs &a, int nmx, int grid, size_t smem, cudaStream_t st) {
+    auto kern = nmx == 1 ? moe_layer_kernel<TA, TB, 1> : moe_layer_kernel<TA, TB, 8>;
+    static bool configured[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    bool &done = configured[nmx == 1 ? 0 : 1][dev];
+    if (!done) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        done = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // all CTAs co-resident: one grid barrier
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) {
+        cudaFuncAttributes fa{};
+        cudaFuncGetAttributes(&fa, kern);
+        snprintf(g_layer_diag, sizeof(g_layer_diag), "grid=%d threads=%d smem=%zu regs=%d maxThreads=%d local=%zu",
+                 grid, GEMV_THREADS, smem, fa.numRegs, fa.maxThreadsPerBlock, fa.localSizeBytes);
+    }
+    return e;
+}
+
+}  // namespace moe

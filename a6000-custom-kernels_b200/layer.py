@@ -71,9 +71,14 @@ class MoELayer:
         ws = self._ws.get(n_tok)
         if ws is None:
             nbytes = lib().moe_b200_layer_workspace_size(ctypes.byref(self.desc), n_tok)
-            ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            # zero-filled once: the fused kernel's grid barrier words live at its end
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
             self._ws[n_tok] = ws
         return ws
+
+    def fused(self, n_tok):
+        """True when decode() runs the layer as one fused kernel for n_tok tokens."""
+        return bool(lib().moe_b200_layer_fused(ctypes.byref(self.desc), n_tok))
 
     def decode(self, x, logits, out=None, stream=None):
         """x f32 [n_tok, H], logits f32 [n_tok, E] (device) -> out f32 [n_tok, H]."""

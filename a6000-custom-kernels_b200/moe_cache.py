@@ -173,6 +173,11 @@ def topk_softmax(logits, k, norm_w=False, stream=None):
     return ids, w
 
 
+def set_layer_fused(enable):
+    """Enable (default) or disable the one-kernel layer decode (moe_b200_layer_set_fused)."""
+    check(lib().moe_b200_layer_set_fused(1 if enable else 0))
+
+
 def fill_quantized(ggml_type, dst, n_rows, n_cols, seed, sigma=0.02, stream=None):
     check(lib().moe_b200_fill_quantized(ggml_type, _ptr(dst), n_rows, n_cols, seed, sigma, _stream(stream)))
 

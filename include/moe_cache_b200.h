@@ -196,16 +196,33 @@ typedef struct {
 } moe_layer_desc;
 
 /* No counterpart in the reference: bytes of caller-owned device workspace
- * moe_b200_layer_decode needs for n_tok tokens. */
+ * moe_b200_layer_decode needs for n_tok tokens. Zero-fill the workspace once
+ * before its first use (cudaMemset): its last words are the fused kernel's
+ * grid barrier, which every launch leaves at zero again. */
 size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok);
 
 /* No counterpart in the reference (the upstream graph around two
  * MUL_MAT_ID calls): one MoE layer for n_tok <= 8 decode tokens, f32 in/out on
  * device: route, fused gate/up GEMV + GLU, down GEMV, weighted combine plus the
  * shared expert. Activations use llama.cpp CPU semantics (see src1_type F32).
- * Allocates nothing: `workspace` is caller-owned device memory. */
+ * Allocates nothing: `workspace` is caller-owned device memory (zero-filled
+ * before first use). Where moe_b200_layer_fused says so, the whole layer is
+ * ONE cooperative kernel launch (one CTA per SM, one grid barrier between
+ * gate/up and down); otherwise four launches (routing, gate/up, down,
+ * combine). Both give the same bits. Concurrent calls must not share a
+ * workspace. */
 int moe_b200_layer_decode(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
                           int64_t n_tok, void *workspace, size_t workspace_bytes, moe_stream_t stream);
+
+/* No counterpart in the reference: 1 when moe_b200_layer_decode runs this
+ * layer as one fused kernel for n_tok tokens (gate/up and down type pair with a
+ * fused kernel, n_tok <= 8, n_tok * k <= 64, activations and tiles fit in
+ * shared memory, fusion enabled), else 0. */
+int moe_b200_layer_fused(const moe_layer_desc *layer, int64_t n_tok);
+
+/* No counterpart in the reference: enable (1, the default) or disable the
+ * fused layer kernel; GGML_CUDA_MOE_LAYER_FUSED=0 disables it at start-up. */
+int moe_b200_layer_set_fused(int32_t enable);
 
 /* No counterpart in the reference. A layer decode for callers that cannot
  * allocate device memory where they run it: engines that reserve all device

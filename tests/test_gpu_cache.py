@@ -23,8 +23,9 @@ def _layer_np(t, H, F, E, seed):
                 shared_up=experts(t, 1, F, H, seed + 4)[0], shared_down=experts(t, 1, H, F, seed + 5)[0])
 
 
-@pytest.mark.parametrize("n_tok,slots", [(1, 5), (4, 3)])
-def test_tiered_cache_matches_policy_model(pkg, cuda, tmp_path, n_tok, slots):
+@pytest.mark.parametrize("n_tok,slots,fused", [(1, 5, True), (4, 3, True), (4, 3, False)])
+def test_tiered_cache_matches_policy_model(pkg, cuda, tmp_path, n_tok, slots, fused):
+    """fused: the one-kernel layer decode; else the four-launch path."""
     mc = pkg.moe_cache
     t, H, F, E, k = O.Q4_K, 512, 256, 16, 4
     L = _layer_np(t, H, F, E, seed=11)
@@ -33,10 +34,12 @@ def test_tiered_cache_matches_policy_model(pkg, cuda, tmp_path, n_tok, slots):
     seed_file = tmp_path / "seed.txt"
     seed_file.write_text(seed_text)
     mc.configure(enabled=True, slots=slots, budget_gb=1.0, seed_path=str(seed_file))
+    mc.set_layer_fused(fused)
     try:
         layer = pkg.MoELayer(H, F, E, k, {"gate": t, "up": t, "down": t}, shared=True, host=True,
                              weights={r: L[r] for r in ("gate", "up", "down", "shared_gate", "shared_up", "shared_down")})
         assert all(mc.wants(layer.desc_t[r]) for r in ("gate", "up", "down"))
+        assert layer.fused(n_tok) == fused
         model = CacheModel(slots=slots, budget_bytes=1 << 30, seed=parse_seed(seed_text))
         names = {r: f"blk.0.ffn_{r}_exps.weight" for r in ("gate", "up", "down")}
         eb = {r: layer.w[r][0].numel() for r in ("gate", "up", "down")}
@@ -64,6 +67,7 @@ def test_tiered_cache_matches_policy_model(pkg, cuda, tmp_path, n_tok, slots):
         assert s["promotions"] > 0 and s["evictions"] > 0
         assert mc.device_error() == 0
     finally:
+        mc.set_layer_fused(True)
         mc.reset()
 
 
