@@ -596,9 +596,10 @@ int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 struct LayerWs {
+    uint32_t *gbar;   // fused kernel: [0] launch epoch, [1] finished CTAs (first 256 bytes)
     int32_t *ids;
     float *w, *h, *hs, *y, *ys;
-    uint32_t *gbar;   // fused kernel's grid barrier words (zero between launches)
+    uint64_t *h_tag, *hs_tag;   // fused kernel: h / hs as (value, tag) pairs
     size_t bytes;
 };
 
@@ -607,13 +608,17 @@ LayerWs layer_ws(const moe_layer_desc *L, int64_t n_tok, char *base) {
     size_t off = 0;
     auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
     const int64_t k = L->k, F = L->F, H = L->H;
+    // the epoch sits at offset 0 for every n_tok, so workspaces reused across
+    // batch sizes share one tag sequence
+    w.gbar = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 2));
     w.ids = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * n_tok * k));
     w.w = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k));
     w.h = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k * F));
     w.hs = reinterpret_cast<float *>(take(sizeof(float) * n_tok * F));
     w.y = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k * H));
     w.ys = reinterpret_cast<float *>(take(sizeof(float) * n_tok * H));
-    w.gbar = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 2));
+    w.h_tag = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * n_tok * k * F));
+    w.hs_tag = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * n_tok * F));
     w.bytes = off;
     return w;
 }
@@ -710,6 +715,8 @@ int layer_args(const moe_layer_desc *L, const float *x, const float *logits, flo
     a.clock = g.d_clock;
     a.log_cap = kLogCap;
     a.gbar = w.gbar;
+    a.h_tag = w.h_tag;
+    a.hs_tag = shared ? w.hs_tag : nullptr;
     a.err = g.d_err;
     u.err = d.err = g.d_err;
     return MOE_OK;

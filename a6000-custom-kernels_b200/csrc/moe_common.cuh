@@ -21,6 +21,7 @@ enum : int { ACT_Q8_1 = 0, ACT_CPU = 1 };
 enum : int {
     DERR_NONE = 0, DERR_BAD_ID = 1, DERR_TOO_MANY_KEYS = 2, DERR_TIMEOUT_FULL = 3,
     DERR_TIMEOUT_EMPTY = 4, DERR_TOO_MANY_SEGMENTS = 5, DERR_DRAIN = 6, DERR_GRID_BARRIER = 7,
+    DERR_TIMEOUT_TAG = 8,
 };
 
 template <int T> struct fmt;
@@ -210,6 +211,21 @@ __device__ __forceinline__ int nearest_int_dev(float prod) {
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// two 64-bit words at a 16-byte aligned address (each word single-copy atomic)
+__device__ __forceinline__ void ld_relaxed_u64x2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 

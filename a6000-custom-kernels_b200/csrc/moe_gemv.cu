@@ -132,11 +132,15 @@ int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **wh
     int S = avail > 0 ? static_cast<int>(avail / stage_bytes) : 0;
     if (S > GEMV_MAX_STAGES) S = GEMV_MAX_STAGES;
     if (S < 2) { *why = "rows too wide for the shared-memory ring"; return -2; }
+    // every stage belongs to one tile warp: S a multiple of the tile warps
+    const int nw = S >= GEMV_CONSUMER_WARPS ? GEMV_CONSUMER_WARPS : S;
+    S = S / nw * nw;
     const size_t smem = ctrl + static_cast<size_t>(act_slots) * slot_bytes + static_cast<size_t>(S) * stage_bytes;
 
     a.lanes_per_row = L;
     a.rows_per_tile = rpt;
     a.n_stages = S;
+    a.n_tile_warps = nw;
     a.n_parts = parts;
     a.act_slots = act_slots;
     a.part_bytes = part_bytes;

@@ -72,7 +72,10 @@ struct GemvArgs {
     int32_t K, nrows;
     uint32_t row_bytes;
     // geometry (set by the launcher)
-    int32_t lanes_per_row, rows_per_tile, n_stages, n_parts, act_slots;
+    // n_tile_warps: consumer warps that take tiles (tile i -> warp i % n);
+    // n_stages is a multiple of it, so every stage is always consumed by the
+    // same warp and a warp never waits on a stage more than one phase ahead
+    int32_t lanes_per_row, rows_per_tile, n_stages, n_parts, act_slots, n_tile_warps;
     uint32_t part_bytes, slot_bytes, ctrl_bytes;
     int32_t tma_main, tma_gate, tma_shared;
     int *err;
@@ -108,20 +111,16 @@ struct Acts {
 __device__ __forceinline__ int bs_lo(int w) { return static_cast<int16_t>(w & 0xFFFF); }
 __device__ __forceinline__ int bs_hi(int w) { return w >> 16; }
 
-// Q8_K block (256 f32 at x): llama.cpp quantize_row_q8_K_ref, bit-exact. Lane l
-// holds elements 4l..4l+3 and 128+4l..128+4l+3 (coalesced float4 loads when x
-// is 16-byte aligned).
 // f32 loads; CG: through L2 only (data another CTA of the same grid wrote)
 template <bool CG> __device__ __forceinline__ float ld_f32(const float *p) { return CG ? __ldcg(p) : *p; }
 template <bool CG> __device__ __forceinline__ float4 ld_f32x4(const float *p) {
     return CG ? __ldcg(reinterpret_cast<const float4 *>(p)) : *reinterpret_cast<const float4 *>(p);
 }
 
-template <int TYPE, bool CG = false>
-__device__ __forceinline__ void stage_q8K_block(const float *x, bool al16, int8_t *q, int16_t *bs, float *sc, int b,
-                                                int lane, int NC) {
-    float v[8];
-    const float *xb = x + b * 256;
+// Lane l's values of a Q8_K block (256 f32 at xb): elements 4l..4l+3 and
+// 128+4l..128+4l+3 (coalesced float4 loads when xb is 16-byte aligned).
+template <bool CG>
+__device__ __forceinline__ void load_q8K_vals(const float *xb, bool al16, int lane, float (&v)[8]) {
     if (al16) {
         const float4 u0 = ld_f32x4<CG>(xb + 4 * lane);
         const float4 u1 = ld_f32x4<CG>(xb + 128 + 4 * lane);
@@ -131,6 +130,13 @@ __device__ __forceinline__ void stage_q8K_block(const float *x, bool al16, int8_
 #pragma unroll
         for (int j = 0; j < 4; ++j) { v[j] = ld_f32<CG>(xb + 4 * lane + j); v[4 + j] = ld_f32<CG>(xb + 128 + 4 * lane + j); }
     }
+}
+
+// Q8_K block b from the lane values of load_q8K_vals: llama.cpp
+// quantize_row_q8_K_ref, bit-exact.
+template <int TYPE>
+__device__ __forceinline__ void quant_q8K_vals(const float (&v)[8], int8_t *q, int16_t *bs, float *sc, int b, int lane,
+                                               int NC) {
     float amax = 0.f, mval = 0.f;
     int midx = 1 << 30;
 #pragma unroll
@@ -183,11 +189,19 @@ __device__ __forceinline__ void stage_q8K_block(const float *x, bool al16, int8_
     if (lane == 0) sc[b] = d;
 }
 
-// Q8_0 block (32) from f32: llama.cpp quantize_row_q8_0_ref, bit-exact.
+// Q8_K block (256 f32 at x + 256 b): llama.cpp quantize_row_q8_K_ref, bit-exact.
 template <int TYPE, bool CG = false>
-__device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16_t *bs, float *sc, int b, int lane,
-                                                int NC) {
-    const float v = ld_f32<CG>(x + b * 32 + lane);
+__device__ __forceinline__ void stage_q8K_block(const float *x, bool al16, int8_t *q, int16_t *bs, float *sc, int b,
+                                                int lane, int NC) {
+    float v[8];
+    load_q8K_vals<CG>(x + b * 256, al16, lane, v);
+    quant_q8K_vals<TYPE>(v, q, bs, sc, b, lane, NC);
+}
+
+// Q8_0 block b from lane l's value (element 32 b + l): llama.cpp
+// quantize_row_q8_0_ref, bit-exact.
+template <int TYPE>
+__device__ __forceinline__ void quant_q80_val(float v, int8_t *q, int16_t *bs, float *sc, int b, int lane, int NC) {
     float amax = fabsf(v);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
@@ -200,6 +214,12 @@ __device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16
     for (int off = 8; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if ((lane & 15) == 0) bs[b * 2 + (lane >> 4)] = static_cast<int16_t>(s);
     if (lane == 0) sc[b] = __half2float(__float2half_rn(d));
+}
+
+template <int TYPE, bool CG = false>
+__device__ __forceinline__ void stage_q80_block(const float *x, int8_t *q, int16_t *bs, float *sc, int b, int lane,
+                                                int NC) {
+    quant_q80_val<TYPE>(ld_f32<CG>(x + b * 32 + lane), q, bs, sc, b, lane, NC);
 }
 
 // Block b of an f32 activation vector into its slot with llama.cpp CPU
@@ -613,15 +633,21 @@ struct GemvCtrl {
     int32_t n_unique, n_seg, n_tiles, n_keys, fail;
 };
 
-// One consumer warp's pass over a tile. Fused (use_gate): RL = 2 rows per lane
-// are the up and the gate row of one output row; unfused: RL = 1.
-template <int TYPE, int ACT, int NMX, int RL>
+// One consumer warp's pass over a tile (SW = 32), or one half-warp's
+// (SW = 16: lanes 0-15 and 16-31 each run their own tile). Fused (use_gate):
+// RL = 2 rows per lane are the up and the gate row of one output row;
+// unfused: RL = 1.
+template <int TYPE, int ACT, int NMX, int RL, int SW = 32>
 __device__ __forceinline__ void consume_tile(const GemvArgs &a, const GemvCtrl &C, const uint8_t *up_rows,
                                              const uint8_t *gate_rows, int nr, int g, int U, int row0,
-                                             const uint8_t *act_area, int lane) {
+                                             const uint8_t *act_area, int lane, uint64_t *dst_tag = nullptr,
+                                             uint64_t *shared_tag = nullptr, uint32_t tag = 0) {
+    static_assert(SW == 32 || SW == 16, "whole or half warps");
+    const unsigned mask = SW == 32 ? 0xffffffffu : (0xffffu << (lane & 16));
+    const int sl = lane & (SW - 1);
     const int L = a.lanes_per_row;
-    const int RP = 32 / L;
-    const int sub = lane % L, rr = lane / L;
+    const int RP = SW / L;
+    const int sub = sl % L, rr = sl / L;
     const int K = a.K;
     constexpr int CE = chunk_of<TYPE>::CE;
     const int Tk = (K / fmt<TYPE>::qk) * fmt<TYPE>::tasks;
@@ -658,7 +684,7 @@ __device__ __forceinline__ void consume_tile(const GemvArgs &a, const GemvCtrl &
 #pragma unroll
                 for (int r = 0; r < RL; ++r)
 #pragma unroll
-                    for (int m = 0; m < NMX; ++m) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], off);
+                    for (int m = 0; m < NMX; ++m) acc[r][m] += __shfl_xor_sync(mask, acc[r][m], off);
             }
             if (!ok || sub != 0) continue;
             const int row = row0 + ri;
@@ -682,26 +708,33 @@ __device__ __forceinline__ void consume_tile(const GemvArgs &a, const GemvCtrl &
                         result = glu_apply(a.glu_op, gv, result, a.glu_limit);
                     }
                 }
-                if (g < U) a.dst[p * a.stride_channel_dst + t * a.stride_col_dst + row] = result;
-                else a.shared_dst[t * a.shared_stride_col_dst + row] = result;
+                const int64_t o = g < U ? p * a.stride_channel_dst + t * a.stride_col_dst + row
+                                        : t * a.shared_stride_col_dst + row;
+                (g < U ? a.dst : a.shared_dst)[o] = result;
+                // tagged copy (value, tag) in one 64-bit store: a reader that
+                // sees the tag sees the value
+                uint64_t *tp = g < U ? dst_tag : shared_tag;
+                if (tp) st_relaxed_u64(tp + o, (static_cast<uint64_t>(tag) << 32) | __float_as_uint(result));
             }
         }
     }
 }
 
-// Weight sources of one tile: part p < n_parts holds rows [row0, row0 + nr)
-// of src[p], rb bytes each. kind: 0 = bulk copy, 1 = host memory, copied with
-// 16-byte loads, 2 = plain 4/2-byte copies (source not 16-byte aligned).
+// Weight sources of one tile: part p < n_parts holds rows
+// [row0[p], row0[p] + nr[p]) of src[p], rb bytes each, and lands at
+// stage + p * part_bytes + (its source address & 15). kind: 0 = bulk copy,
+// 1 = host memory, copied with 16-byte loads, 2 = plain 4/2-byte copies
+// (source not 16-byte aligned).
 struct TileSrc {
     const char *src[2];
     int kind[2];
-    int n_parts, row0, nr;
-    uint32_t rb;
+    int row0[2], nr[2];
+    int n_parts;
+    uint32_t rb, part_bytes;
 };
 
 // The producer warp: streams tiles 0..n_tiles-1 through the S-stage ring
-// (tile i -> stage i % S, phase i / S). Part p of a tile lands at
-// stage + p * part_bytes + (source address & 15). Tiles are issued in rounds
+// (tile i -> stage i % S, phase i / S). Tiles are issued in rounds
 // of up to min(32, S): within a round no tile reuses a stage of the same
 // round, so every lane waits for its own stage and issues its own bulk copies.
 // Tiles that need plain copies (host memory or unaligned sources) follow,
@@ -709,8 +742,8 @@ struct TileSrc {
 // landed, so no bulk copy is in flight when the CTA exits.
 template <class Describe>
 __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full, uint64_t *empty,
-                                              uint8_t *stage_area, uint32_t stage_bytes, uint32_t part_bytes,
-                                              Describe describe, uint64_t timeout_ns, int *err, int lane) {
+                                              uint8_t *stage_area, uint32_t stage_bytes, Describe describe,
+                                              uint64_t timeout_ns, int *err, int lane) {
     const uint64_t pol = l2_evict_first_policy();
     const int R = S < 32 ? S : 32;
     int issued = 0;
@@ -727,14 +760,14 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
                 if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), timeout_ns)) {
                     lane_ok = false;
                 } else {
-                    const uint32_t bytes = static_cast<uint32_t>(ts.nr) * ts.rb;
                     uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
                     uintptr_t lo[2], hi[2];
                     uint32_t tx = 0;
 #pragma unroll
                     for (int p = 0; p < 2; ++p) {
                         if (p >= ts.n_parts) break;
-                        const uintptr_t sp = reinterpret_cast<uintptr_t>(ts.src[p]) + static_cast<uint64_t>(ts.row0) * ts.rb;
+                        const uint32_t bytes = static_cast<uint32_t>(ts.nr[p]) * ts.rb;
+                        const uintptr_t sp = reinterpret_cast<uintptr_t>(ts.src[p]) + static_cast<uint64_t>(ts.row0[p]) * ts.rb;
                         lo[p] = sp & ~static_cast<uintptr_t>(15);
                         hi[p] = (sp + bytes + 15u) & ~static_cast<uintptr_t>(15);
                         tx += static_cast<uint32_t>(hi[p] - lo[p]);
@@ -743,7 +776,7 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
 #pragma unroll
                     for (int p = 0; p < 2; ++p) {
                         if (p >= ts.n_parts) break;
-                        bulk_g2s(stage + p * part_bytes, reinterpret_cast<const void *>(lo[p]),
+                        bulk_g2s(stage + p * ts.part_bytes, reinterpret_cast<const void *>(lo[p]),
                                  static_cast<uint32_t>(hi[p] - lo[p]), &full[s], pol);
                     }
                 }
@@ -768,13 +801,13 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
             TileSrc ts;
             describe(i, ts);
             uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
-            const uint32_t bytes = static_cast<uint32_t>(ts.nr) * ts.rb;
             uint32_t tx = 0;
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
                 if (p >= ts.n_parts) break;
-                const char *sp = ts.src[p] + static_cast<uint64_t>(ts.row0) * ts.rb;
-                uint8_t *dp = stage + p * part_bytes;
+                const uint32_t bytes = static_cast<uint32_t>(ts.nr[p]) * ts.rb;
+                const char *sp = ts.src[p] + static_cast<uint64_t>(ts.row0[p]) * ts.rb;
+                uint8_t *dp = stage + p * ts.part_bytes;
                 const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
                 const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
                 if (ts.kind[p] == 0) {
@@ -810,10 +843,11 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
                     if (p >= ts.n_parts || ts.kind[p] != 0) continue;
-                    const char *sp = ts.src[p] + static_cast<uint64_t>(ts.row0) * ts.rb;
+                    const uint32_t bytes = static_cast<uint32_t>(ts.nr[p]) * ts.rb;
+                    const char *sp = ts.src[p] + static_cast<uint64_t>(ts.row0[p]) * ts.rb;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(sp) & ~static_cast<uintptr_t>(15);
                     const uintptr_t a1 = (reinterpret_cast<uintptr_t>(sp) + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                    bulk_g2s(stage + p * part_bytes, reinterpret_cast<const void *>(a0), static_cast<uint32_t>(a1 - a0),
+                    bulk_g2s(stage + p * ts.part_bytes, reinterpret_cast<const void *>(a0), static_cast<uint32_t>(a1 - a0),
                              &full[s], pol);
                 }
             }
@@ -842,12 +876,9 @@ __device__ __forceinline__ int build_segments(GemvCtrl &C, uint32_t n_groups, ui
     const uint32_t r_begin = bid * q + (bid < rem ? bid : rem);
     const uint32_t r_end = r_begin + q + (bid < rem ? 1u : 0u);
     int ns = 0, nt = 0;
-    uint32_t r = r_begin;
-    while (r < r_end) {
-        const uint32_t g = r / nrows;
-        const uint32_t r0 = r - g * nrows;
-        const uint32_t g_end = (g + 1) * nrows;
-        const uint32_t r1 = (g_end < r_end ? g_end : r_end) - g * nrows;
+    uint32_t g = r_begin / nrows, r0 = r_begin - g * nrows;
+    for (uint32_t left = r_end - r_begin; left > 0; ++g, r0 = 0) {
+        const uint32_t r1 = (nrows - r0 < left) ? nrows : r0 + left;
         if (ns >= GEMV_MAX_SEGMENTS) { C.fail = 1; set_error(err, DERR_TOO_MANY_SEGMENTS); break; }
         C.seg_g[ns] = static_cast<int32_t>(g);
         C.seg_r0[ns] = static_cast<int32_t>(r0);
@@ -855,7 +886,7 @@ __device__ __forceinline__ int build_segments(GemvCtrl &C, uint32_t n_groups, ui
         C.seg_t0[ns] = nt;
         nt += (static_cast<int>(r1 - r0) + rpt - 1) / rpt;
         ns++;
-        r = g * nrows + r1;
+        left -= r1 - r0;
     }
     C.seg_t0[ns] = nt;
     C.n_seg = ns;
@@ -873,6 +904,47 @@ __device__ __forceinline__ void segment_tile(const GemvCtrl &C, int n_seg, int r
     nr = (lim - row0) < rpt ? (lim - row0) : rpt;
 }
 
+// build_groups for N <= 32 entries by one warp (lane = its lane), without
+// block barriers: __match_any_sync groups equal experts.
+template <class XOf, class Resolve>
+__device__ __forceinline__ void build_groups_warp(GemvCtrl &C, int N, int n_experts, XOf x_of, Resolve resolve,
+                                                  int *err, int lane) {
+    int x = -1 - lane;
+    bool bad = false;
+    if (lane < N) {
+        x = x_of(lane);
+        bad = x < 0 || x >= n_experts;
+        C.x[lane] = x;
+    }
+    if (__ballot_sync(0xffffffffu, bad)) {
+        if (lane == 0) { C.fail = 1; set_error(err, DERR_BAD_ID); }
+    } else {
+        const unsigned same = __match_any_sync(0xffffffffu, x);
+        const int f = __ffs(same) - 1;
+        const unsigned firsts = __ballot_sync(0xffffffffu, lane < N && f == lane);
+        const int u = __popc(firsts & ((1u << f) - 1u));
+        int pos = 0;
+        for (int j = 0; j < N; ++j) {
+            const int fj = __shfl_sync(0xffffffffu, f, j);
+            pos += (fj < f) || (fj == f && j < lane);
+        }
+        if (lane < N) {
+            C.first[lane] = static_cast<int16_t>(f);
+            C.uidx[lane] = static_cast<int16_t>(u);
+            C.gmem[pos] = static_cast<int16_t>(lane);
+            if (f == lane) {
+                C.uexp[u] = x;
+                C.goff[u] = static_cast<int16_t>(pos);
+                resolve(u, x);
+            }
+        }
+        if (lane == 0) {
+            C.n_unique = __popc(firsts);
+            C.goff[__popc(firsts)] = static_cast<int16_t>(N);
+        }
+    }
+}
+
 // Groups the N routed entries by expert. x_of(e) gives entry e's expert;
 // groups (distinct experts) are numbered in first-occurrence order, gmem lists
 // each group's entries (CSR, offsets goff) and resolve(u, x) records group u's
@@ -883,43 +955,7 @@ __device__ __forceinline__ void build_groups(GemvCtrl &C, int N, int n_experts, 
                                              int *err) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (N <= 32) {
-        // one warp, no block barriers: match_any groups equal experts
-        if (warp == 0) {
-            int x = -1 - lane;
-            bool bad = false;
-            if (lane < N) {
-                x = x_of(lane);
-                bad = x < 0 || x >= n_experts;
-                C.x[lane] = x;
-            }
-            if (__ballot_sync(0xffffffffu, bad)) {
-                if (lane == 0) { C.fail = 1; set_error(err, DERR_BAD_ID); }
-            } else {
-                const unsigned same = __match_any_sync(0xffffffffu, x);
-                const int f = __ffs(same) - 1;
-                const unsigned firsts = __ballot_sync(0xffffffffu, lane < N && f == lane);
-                const int u = __popc(firsts & ((1u << f) - 1u));
-                int pos = 0;
-                for (int j = 0; j < N; ++j) {
-                    const int fj = __shfl_sync(0xffffffffu, f, j);
-                    pos += (fj < f) || (fj == f && j < lane);
-                }
-                if (lane < N) {
-                    C.first[lane] = static_cast<int16_t>(f);
-                    C.uidx[lane] = static_cast<int16_t>(u);
-                    C.gmem[pos] = static_cast<int16_t>(lane);
-                    if (f == lane) {
-                        C.uexp[u] = x;
-                        C.goff[u] = static_cast<int16_t>(pos);
-                        resolve(u, x);
-                    }
-                }
-                if (lane == 0) {
-                    C.n_unique = __popc(firsts);
-                    C.goff[__popc(firsts)] = static_cast<int16_t>(N);
-                }
-            }
-        }
+        if (warp == 0) build_groups_warp(C, N, n_experts, x_of, resolve, err, lane);
     } else {
         for (int e = tid; e < N; e += blockDim.x) {
             const int x = x_of(e);
@@ -1128,13 +1164,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
     if (warp == GEMV_CONSUMER_WARPS) {
         // =========================== producer warp ===========================
         produce_tiles(
-            n_tiles, S, full, empty, stage_area, stage_bytes, a.part_bytes,
+            n_tiles, S, full, empty, stage_area, stage_bytes,
             [&](int i, TileSrc &ts) {
                 int g;
-                tile_coords(i, g, ts.row0, ts.nr);
+                tile_coords(i, g, ts.row0[0], ts.nr[0]);
+                ts.row0[1] = ts.row0[0];
+                ts.nr[1] = ts.nr[0];
                 tile_sources(g, ts.src[0], ts.src[1], ts.kind[0], ts.kind[1]);
                 ts.n_parts = a.n_parts;
                 ts.rb = a.row_bytes;
+                ts.part_bytes = a.part_bytes;
             },
             a.timeout_ns, a.err, lane);
         return;
@@ -1175,7 +1214,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
         asm volatile("bar.sync 1, %0;" ::"r"(GEMV_CONSUMER_WARPS * 32) : "memory");
     }
 
-    for (int i = warp; i < n_tiles; i += GEMV_CONSUMER_WARPS) {
+    const int nw = a.n_tile_warps;
+    for (int i = warp; i < n_tiles && warp < nw; i += nw) {
         const int s = i % S;
         if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
             if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);

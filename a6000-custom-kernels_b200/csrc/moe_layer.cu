@@ -77,7 +77,10 @@ int plan_layer(int ta, int tb, LayerArgs &a, int *grid_out, size_t *smem_out, co
     if (!pair_supported(ta, tb)) { *why = "no fused kernel for this gate/up, down type pair"; return -2; }
     const int H = a.gu.K, F = a.gu.nrows, n_tok = a.n_tok, k = a.k;
     const int N = n_tok * k;
-    if (n_tok < 1 || n_tok > 8 || N > LAYER_MAX_ENTRIES) { *why = "fused layer handles n_tok * k <= 64, n_tok <= 8"; return -2; }
+    if (n_tok < 1 || n_tok > 8 || k < 1 || k > 32 || N > LAYER_MAX_ENTRIES) {
+        *why = "fused layer handles n_tok <= 8, k <= 32, n_tok * k <= 64";
+        return -2;
+    }
     if (a.dn.K != F || a.dn.nrows != H) { *why = "down shape does not match"; return -2; }
     if (H % qk_of(ta) || F % qk_of(tb)) { *why = "H / F not a multiple of the block size"; return -2; }
     const uint32_t rbA = static_cast<uint32_t>((H / qk_of(ta)) * bytes_of(ta));
@@ -85,7 +88,9 @@ int plan_layer(int ta, int tb, LayerArgs &a, int *grid_out, size_t *smem_out, co
     if (a.gu.row_bytes != rbA || a.dn.row_bytes != rbB) { *why = "rows are not contiguous"; return -2; }
     const bool shared = a.gu.shared_up != nullptr;
     const int LA = lanes_for(H, ta), RPA = 32 / LA;
-    const int LB = lanes_for(F, tb), RPB = 32 / LB;
+    int LB = lanes_for(F, tb);
+    if (LB > 16) LB = 16;                      // phase B runs on half-warps
+    const int RPB = 16 / LB;
     const int G = sm_count();
 
     // phase A tiles: as the GEMV, for the routed groups' upper bound
@@ -99,16 +104,25 @@ int plan_layer(int ta, int tb, LayerArgs &a, int *grid_out, size_t *smem_out, co
     if (rpt > F) rpt = F;
     const uint32_t part_a = round16(static_cast<uint64_t>(rpt) * rbA) + 32u;
     uint32_t stage = 2 * part_a;
-    // phase B tiles: rows of one group within [h0, h1), a multiple of the
-    // rows one warp pass covers, no larger than a stage
+    // phase B tiles: rows of one group within [h0, h1), run by half-warps
+    // (RPB rows per pass), two tiles per stage. Aim for ~32 tiles per CTA so
+    // every half-warp has one.
     const int hb = (H + G - 1) / G;
-    const uint32_t min_b = round16(static_cast<uint64_t>(RPB) * rbB) + 32u;
-    if (stage < min_b) stage = min_b;
-    int rows_b = static_cast<int>((stage - 32u) / rbB) / RPB * RPB;
-    const int hb_up = (hb + RPB - 1) / RPB * RPB;
-    if (rows_b > hb_up) rows_b = hb_up;
-    if (rows_b < 1) { *why = "down rows too wide"; return -2; }
-
+    const int ga = static_cast<int>(groups);
+    const int tpg_target = (32 + ga - 1) / ga;
+    int rows_b = (hb + tpg_target - 1) / tpg_target;
+    rows_b = (rows_b + RPB - 1) / RPB * RPB;
+    uint32_t part_b = round16(static_cast<uint64_t>(rows_b) * rbB) + 32u;
+    if (stage < 2 * part_b) {
+        // a smaller phase-B tile fits the stage, or the stage grows
+        const int fit = static_cast<int>((stage / 2 - 32u) / rbB) / RPB * RPB;
+        if (fit >= RPB) {
+            rows_b = fit;
+            part_b = round16(static_cast<uint64_t>(rows_b) * rbB) + 32u;
+        } else {
+            stage = 2 * part_b;
+        }
+    }
     const uint32_t slot_a = round16(static_cast<uint64_t>(H) + H / 8 + H / 8);
     const uint32_t slot_b = round16(static_cast<uint64_t>(F) + F / 8 + F / 8);
     const uint64_t act_a = static_cast<uint64_t>(n_tok) * slot_a;
@@ -119,18 +133,23 @@ int plan_layer(int ta, int tb, LayerArgs &a, int *grid_out, size_t *smem_out, co
     int S = avail > 0 ? static_cast<int>(avail / stage) : 0;
     if (S > GEMV_MAX_STAGES) S = GEMV_MAX_STAGES;
     if (S < 2) { *why = "activations and tiles do not fit in shared memory"; return -2; }
+    const int nw = S >= GEMV_CONSUMER_WARPS ? GEMV_CONSUMER_WARPS : S;   // stage s -> warp s % nw
+    S = S / nw * nw;
 
     a.gu.lanes_per_row = LA;
     a.gu.rows_per_tile = rpt;
     a.gu.n_parts = 2;
+    a.gu.n_tile_warps = nw;
     a.gu.part_bytes = part_a;
     a.gu.slot_bytes = slot_a;
     a.dn.lanes_per_row = LB;
     a.dn.rows_per_tile = rows_b;
     a.dn.n_parts = 1;
+    a.dn.n_tile_warps = nw;
     a.dn.part_bytes = stage;
     a.dn.slot_bytes = slot_b;
     a.rows_b = rows_b;
+    a.part_bytes_b = part_b;
     a.n_stages = S;
     a.stage_bytes = stage;
     a.ctrl_bytes = ctrl;

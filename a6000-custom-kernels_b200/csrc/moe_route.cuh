@@ -8,106 +8,121 @@
 
 namespace moe {
 
-// Running best of a scan: the first candidate is always taken (even -inf or
-// NaN), later ones when larger, ties to the lower expert id.
-__device__ __forceinline__ bool route_better(float v, int e, float bv, int bi) {
-    return bi == 0x7fffffff || v > bv || (v == bv && e < bi);
+// Order-preserving 32-bit key of a logit: larger logit -> larger key (NaN
+// above +inf or below -inf by sign); -0 is folded into +0 first so that equal
+// logits get equal keys. Key 0 is below every logit ("no candidate").
+__device__ __forceinline__ uint32_t logit_key(float x) {
+    const uint32_t u = __float_as_uint(__fadd_rn(x, 0.0f));
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_logit(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-// Top-k of one token's logits l[0..n_experts) (descending, ties to the lower
-// expert id) and gating weights expf(l - max) / sum_e expf(l_e - max), where
-// the sum runs lane-strided (lane j adds experts j, j + 32, ...) and then over
-// the lanes by xor butterfly; with norm_w the k weights are divided by their
-// sum in pick order. Lane 0 writes ids[0..k) and w[0..k). All 32 lanes call.
-__device__ __forceinline__ void route_token_warp(const float *__restrict__ l, int n_experts, int k, int norm_w,
-                                                 int lane, int32_t *ids, float *w) {
-    constexpr int REG = 32;   // logits per lane held in registers (n_experts <= 1024)
-    if (n_experts <= 32 * REG) {
-        float v[REG];
+// Selection, register path for n_experts <= 32 * NV: lane l holds experts
+// l + 32 j. The order is (logit descending, expert id ascending). Each pick
+// reduces the lane's untaken candidates with a pairwise tree (left halves
+// hold the lower ids, so the right side wins only when strictly larger),
+// then the warp with redux max (key) and redux min (id among equal keys).
+// Lane q < k writes ids[q].
+template <int NV>
+__device__ __forceinline__ void route_select_regs(const float *__restrict__ l, int n_experts, int k, int lane,
+                                                  int32_t *ids) {
+    uint32_t key[NV];
+    uint32_t live = 0;   // bit j: expert lane + 32 j exists and is not picked yet
 #pragma unroll
-        for (int j = 0; j < REG; ++j) {
-            const int e = lane + 32 * j;
-            v[j] = e < n_experts ? l[e] : 0.f;
-        }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < REG; ++j)
-            if (lane + 32 * j < n_experts) mx = fmaxf(mx, v[j]);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        float sum = 0.f;
-#pragma unroll
-        for (int j = 0; j < REG; ++j)
-            if (lane + 32 * j < n_experts) sum += expf(v[j] - mx);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        uint32_t taken = 0;
-        float ws = 0.f;
-        for (int q = 0; q < k; ++q) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-#pragma unroll
-            for (int j = 0; j < REG; ++j) {
-                const int e = lane + 32 * j;
-                if (e < n_experts && !((taken >> j) & 1u) && route_better(v[j], e, bv, bi)) { bv = v[j]; bi = e; }
-            }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                if (oi != 0x7fffffff && route_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-            }
-            if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-            if (lane == 0) {
-                const float wq = expf(bv - mx) / sum;
-                ids[q] = bi;
-                w[q] = wq;
-                ws += wq;
-            }
-        }
-        if (lane == 0 && norm_w)
-            for (int q = 0; q < k; ++q) w[q] = w[q] / ws;
-        return;
+    for (int j = 0; j < NV; ++j) {
+        const int e = lane + 32 * j;
+        const bool ok = e < n_experts;
+        key[j] = ok ? logit_key(l[e]) : 0u;
+        live |= (ok ? 1u : 0u) << j;
     }
-    // wide routers: scan the logits in memory; lane q < k remembers pick q
-    // (k <= 32)
-    float mx = -INFINITY;
-    for (int e = lane; e < n_experts; e += 32) mx = fmaxf(mx, l[e]);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float sum = 0.f;
-    for (int e = lane; e < n_experts; e += 32) sum += expf(l[e] - mx);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    int mine = -1;
-    float ws = 0.f;
+    uint32_t pick = 0;   // lane q keeps pick q
     for (int q = 0; q < k; ++q) {
-        float bv = -INFINITY;
+        uint32_t tk[NV];
+        int tj[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) { tk[j] = ((live >> j) & 1u) ? key[j] : 0u; tj[j] = j; }
+#pragma unroll
+        for (int width = 1; width < NV; width *= 2) {
+#pragma unroll
+            for (int j = 0; j + width < NV; j += 2 * width) {
+                const bool right = tk[j + width] > tk[j];
+                tk[j] = right ? tk[j + width] : tk[j];
+                tj[j] = right ? tj[j + width] : tj[j];
+            }
+        }
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, tk[0]);
+        const uint32_t mine = (tk[0] == wk && wk != 0u) ? static_cast<uint32_t>(lane + 32 * tj[0]) : 0xFFFFFFFFu;
+        const uint32_t wi = __reduce_min_sync(0xffffffffu, mine);
+        if (static_cast<int>(wi & 31u) == lane) live &= ~(1u << (wi >> 5));
+        if (lane == q) pick = wi;
+    }
+    if (lane < k) ids[lane] = static_cast<int32_t>(pick);
+}
+
+// Selection for any n_experts: scan the logits in memory; lane q < k
+// remembers pick q (k <= 32) and writes ids[q].
+__device__ __forceinline__ void route_select_wide(const float *__restrict__ l, int n_experts, int k, int lane,
+                                                  int32_t *ids) {
+    int mine = -1;
+    for (int q = 0; q < k; ++q) {
+        uint32_t bk = 0;
         int bi = 0x7fffffff;
         for (int base = 0; base < n_experts; base += 32) {   // same trip count on every lane
             const int e = base + lane;
             bool used = e >= n_experts;
             for (int r = 0; r < q; ++r) used |= (__shfl_sync(0xffffffffu, mine, r) == e);
-            if (used) continue;
-            const float val = l[e];
-            if (route_better(val, e, bv, bi)) { bv = val; bi = e; }
+            const uint32_t kv = used ? 0u : logit_key(l[e]);
+            if (kv > bk) { bk = kv; bi = e; }     // ascending e: ties keep the lower id
         }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (oi != 0x7fffffff && route_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-        }
-        if (lane == q) mine = bi;
-        if (lane == 0) {
-            const float wq = expf(bv - mx) / sum;
-            ids[q] = bi;
-            w[q] = wq;
-            ws += wq;
-        }
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+        const int wi = static_cast<int>(__reduce_min_sync(0xffffffffu, bk == wk ? static_cast<uint32_t>(bi) : 0xFFFFFFFFu));
+        if (lane == q) mine = wi;
     }
-    if (lane == 0 && norm_w)
-        for (int q = 0; q < k; ++q) w[q] = w[q] / ws;
+    if (lane < k) ids[lane] = mine;
+}
+
+// Top-k of one token's logits l[0..n_experts) (descending, ties to the lower
+// expert id; NaN logits rank by their key). Lane q < k writes ids[q]; all 32
+// lanes call; k <= 32.
+__device__ __forceinline__ void route_select(const float *__restrict__ l, int n_experts, int k, int lane,
+                                             int32_t *ids) {
+    if (n_experts <= 32 * 8) route_select_regs<8>(l, n_experts, k, lane, ids);
+    else if (n_experts <= 32 * 16) route_select_regs<16>(l, n_experts, k, lane, ids);
+    else route_select_wide(l, n_experts, k, lane, ids);
+}
+
+// Gating weights of the picks ids[0..k) (written by this warp or visible to
+// it): softmax over all experts, expf(l - max) / sum_e expf(l_e - max) with
+// the sum taken lane-strided (lane j adds experts j, j + 32, ... in order) and
+// then over the lanes by xor butterfly; with norm_w each weight is divided by
+// the k weights' sum in pick order. Lane q < k writes w[q].
+__device__ __forceinline__ void route_weights(const float *__restrict__ l, int n_experts, int k, int norm_w,
+                                              int lane, const int32_t *ids, float *w) {
+    uint32_t lmax = 0;
+    for (int e = lane; e < n_experts; e += 32) lmax = max(lmax, logit_key(l[e]));
+    const float mx = key_logit(__reduce_max_sync(0xffffffffu, lmax));
+    float sum = 0.f;
+    for (int e = lane; e < n_experts; e += 32) sum += expf(l[e] - mx);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float wq = lane < k ? expf(l[ids[lane]] - mx) / sum : 0.f;
+    if (norm_w) {
+        float ws = 0.f;
+        for (int q = 0; q < k; ++q) ws += __shfl_sync(0xffffffffu, wq, q);
+        if (lane < k) w[lane] = wq / ws;
+    } else if (lane < k) {
+        w[lane] = wq;
+    }
+}
+
+// Both: the picks, then their weights.
+__device__ __forceinline__ void route_token_warp(const float *__restrict__ l, int n_experts, int k, int norm_w,
+                                                 int lane, int32_t *ids, float *w) {
+    route_select(l, n_experts, k, lane, ids);
+    __syncwarp();
+    route_weights(l, n_experts, k, norm_w, lane, ids, w);
 }
 
 }  // namespace moe

@@ -71,7 +71,7 @@ class MoELayer:
         ws = self._ws.get(n_tok)
         if ws is None:
             nbytes = lib().moe_b200_layer_workspace_size(ctypes.byref(self.desc), n_tok)
-            # zero-filled once: the fused kernel's grid barrier words live at its end
+            # zero-filled once: the fused kernel's launch epoch lives at its start
             ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
             self._ws[n_tok] = ws
         return ws
@@ -96,7 +96,7 @@ class MoELayer:
         GLU output), y [n][k][H] (down outputs), ys [n][H] (shared down)."""
         ws = self._ws[n_tok]
         n, k, F, H = n_tok, self.k, self.F, self.H
-        out, off = [], 0
+        out, off = [], 256          # the first 256 bytes hold the fused kernel's launch epoch
         for count, dt, shape in ((n * k, torch.int32, (n, k)), (n * k, torch.float32, (n, k)),
                                  (n * k * F, torch.float32, (n, k, F)), (n * F, torch.float32, (n, F)),
                                  (n * k * H, torch.float32, (n, k, H)), (n * H, torch.float32, (n, H))):

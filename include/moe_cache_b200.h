@@ -197,8 +197,11 @@ typedef struct {
 
 /* No counterpart in the reference: bytes of caller-owned device workspace
  * moe_b200_layer_decode needs for n_tok tokens. Zero-fill the workspace once
- * before its first use (cudaMemset): its last words are the fused kernel's
- * grid barrier, which every launch leaves at zero again. */
+ * before its first use (cudaMemset): its first 256 bytes hold the fused
+ * kernel's launch epoch, which tags the data its CTAs exchange. Layout after
+ * them (each part 256-byte aligned): ids int32[n][k], weights f32[n][k],
+ * h f32[n][k][F], hs f32[n][F], y f32[n][k][H], ys f32[n][H], then the
+ * fused kernel's tagged copies of h and hs. */
 size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok);
 
 /* No counterpart in the reference (the upstream graph around two

@@ -38,6 +38,7 @@ NAMES = ("ids", "w", "h", "hs", "y", "ys", "out")
 @pytest.mark.parametrize("types,n_tok,shape", [
     ((O.Q2_K, O.Q2_K), 1, (3072, 768, 512, 8)),        # config 2
     ((O.Q2_K, O.Q2_K), 8, (3072, 768, 512, 8)),
+    ((O.Q2_K, O.Q2_K), -8, (3072, 768, 512, 8)),       # 8 tokens, unskewed routing: 64 distinct experts
     ((O.Q3_K, O.Q6_K), 3, (1024, 512, 64, 8)),
     ((O.Q6_K, O.Q4_K), 2, (2048, 256, 40, 6)),
     ((O.Q4_K, O.Q2_K), 5, (512, 1024, 16, 4)),
@@ -47,11 +48,15 @@ NAMES = ("ids", "w", "h", "hs", "y", "ys", "out")
     ((O.Q5_K, O.Q5_K), 7, (512, 512, 128, 8)),
 ])
 def test_fused_matches_four_launches(pkg, cuda, types, n_tok, shape):
+    """n_tok < 0: |n_tok| tokens with N(0, 1) logits (no Zipf skew)."""
     H, F, E, k = shape
     ta, tb = types
+    uniform = n_tok < 0
+    n_tok = abs(n_tok)
     layer = pkg.MoELayer(H, F, E, k, {"gate": ta, "up": ta, "down": tb}, shared=True, seed=sum(types) + n_tok)
     x = torch.from_numpy(activations((n_tok, H), seed=11)).to(cuda)
-    lg = torch.from_numpy(zipf_logits(n_tok, E, seed=12)).to(cuda)
+    lg_np = activations((n_tok, E), seed=12) if uniform else zipf_logits(n_tok, E, seed=12)
+    lg = torch.from_numpy(lg_np).to(cuda)
     a = _run(pkg, layer, x, lg, True)
     b = _run(pkg, layer, x, lg, False)
     for name, u, v in zip(NAMES, a, b):
@@ -109,3 +114,31 @@ def test_fused_query(pkg, cuda):
     assert same.fused(1) and same.fused(8)
     pkg.moe_cache.set_layer_fused(False)
     assert not same.fused(1)
+
+
+def test_one_workspace_for_many_layers_and_batch_sizes(pkg, cuda):
+    """One caller-owned workspace (zero-filled once) serves two layers and
+    several batch sizes in turn: the launch epoch at its start keeps every
+    launch's exchanged data apart."""
+    import ctypes
+    from importlib import import_module
+    lib = import_module("a6000-custom-kernels_b200._lib").lib()
+    H, F, E, k = 1024, 512, 64, 8
+    layers = [pkg.MoELayer(H, F, E, k, {"gate": O.Q2_K, "up": O.Q2_K, "down": O.Q2_K}, shared=True, seed=s)
+              for s in (31, 32)]
+    nbytes = max(lib.moe_b200_layer_workspace_size(ctypes.byref(L.desc), n) for L in layers for n in (1, 2, 3))
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+    for i, n in enumerate((1, 2, 1, 3, 3, 2, 1, 1)):
+        L = layers[i % 2]
+        x = torch.from_numpy(activations((n, H), seed=40 + i)).to(cuda)
+        lg = torch.from_numpy(zipf_logits(n, E, seed=50 + i)).to(cuda)
+        out = torch.empty((n, H), device=cuda)
+        rc = lib.moe_b200_layer_decode(ctypes.byref(L.desc), x.data_ptr(), lg.data_ptr(), out.data_ptr(), n,
+                                       ws.data_ptr(), nbytes, None)
+        assert rc == 0
+        pkg.moe_cache.set_layer_fused(False)
+        ref = L.decode(x, lg)
+        pkg.moe_cache.set_layer_fused(True)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), i
+    assert pkg.moe_cache.device_error() == 0
