@@ -400,17 +400,28 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer_kernel(const __grid
                 ok[r] = true;
                 if (job < njobs) ok[r] = load(block_of(job), vals[r]);
             }
+            // re-read every block that is not complete yet, all at once, so
+            // each poll costs one round trip
+            for (;;) {
+                unsigned waiting = 0;
+#pragma unroll
+                for (int r = 0; r < BATCH; ++r) {
+                    const int job = base + r * GEMV_CONSUMER_WARPS;
+                    if (job < njobs && !__all_sync(0xffffffffu, ok[r])) waiting |= 1u << r;
+                }
+                if (!waiting) break;
+                if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                    if (lane == 0) set_error(a.err, DERR_TIMEOUT_TAG);
+                    break;
+                }
+#pragma unroll
+                for (int r = 0; r < BATCH; ++r)
+                    if ((waiting >> r) & 1u) ok[r] = load(block_of(base + r * GEMV_CONSUMER_WARPS), vals[r]);
+            }
 #pragma unroll
             for (int r = 0; r < BATCH; ++r) {
                 const int job = base + r * GEMV_CONSUMER_WARPS;
                 if (job >= njobs) break;
-                while (!__all_sync(0xffffffffu, ok[r])) {
-                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
-                        if (lane == 0) set_error(a.err, DERR_TIMEOUT_TAG);
-                        break;
-                    }
-                    ok[r] = load(block_of(job), vals[r]);
-                }
                 uint8_t *slot = act_area + static_cast<size_t>(job / nb) * a.dn.slot_bytes;
                 int8_t *q = reinterpret_cast<int8_t *>(slot);
                 int16_t *bs = reinterpret_cast<int16_t *>(slot + KB);
