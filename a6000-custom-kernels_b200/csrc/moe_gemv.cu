@@ -106,6 +106,8 @@ int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **wh
     const int64_t groups_bound_ = (N < a.n_experts ? N : a.n_experts) + (has_shared_ ? 1 : 0);
     const int64_t total_rows = groups_bound_ * a.nrows;
     if (total_rows >= (int64_t{1} << 31)) { *why = "row space of the routed experts exceeds 2^31 rows"; return -2; }
+    const int nmx_ = a.ncols_dst == 1 ? 1 : 8;
+    if (total_rows * ((N + nmx_ - 1) / nmx_ + 1) >= (int64_t{1} << 32)) { *why = "weighted row space exceeds 2^32"; return -2; }
     const int n_sm_ = sm_count();
     const int64_t grid_ = (total_rows + RP - 1) / RP < n_sm_ ? (total_rows + RP - 1) / RP : n_sm_;
     // tiles small enough that every consumer warp of a CTA gets one, large

@@ -630,6 +630,9 @@ struct GemvCtrl {
     uint32_t keys[GEMV_MAX_KEYS];
     int32_t seg_g[GEMV_MAX_SEGMENTS], seg_r0[GEMV_MAX_SEGMENTS], seg_r1[GEMV_MAX_SEGMENTS];
     int32_t seg_t0[GEMV_MAX_SEGMENTS + 1];
+    uint32_t fmask[GEMV_MAX_ENTRIES / 32];    // first occurrences (block grouping)
+    int16_t cnt[GEMV_MAX_ENTRIES];            // members per group / placement cursors
+    uint32_t wpre[GEMV_MAX_ENTRIES + 2];      // prefix of rows x weight per group (weighted split)
     int32_t n_unique, n_seg, n_tiles, n_keys, fail;
 };
 
@@ -894,6 +897,79 @@ __device__ __forceinline__ int build_segments(GemvCtrl &C, uint32_t n_groups, ui
     return ns;
 }
 
+// Weighted variant: group g's rows cost w_g each (w_g = ceil(members / nmx),
+// the shared group has `shared_members`), so a group many tokens picked is
+// spread over more CTAs. Warp 0 writes the prefix C.wpre[g] = sum of
+// nrows * w over groups before g (groups 0..U-1 routed, U the shared one).
+__device__ __forceinline__ void group_weight_prefix(GemvCtrl &C, int U, bool has_shared, int shared_members,
+                                                    uint32_t nrows, int nmx, int lane) {
+    const int GA = U + (has_shared ? 1 : 0);
+    constexpr int PER = (GEMV_MAX_ENTRIES + 2 + 31) / 32;
+    uint32_t part[PER], sum = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int g = PER * lane + i;
+        uint32_t w = 0;
+        if (g < GA) {
+            const int m = g < U ? C.goff[g + 1] - C.goff[g] : shared_members;
+            w = static_cast<uint32_t>((m + nmx - 1) / nmx);
+            if (w < 1) w = 1;
+        }
+        part[i] = w * nrows;
+        sum += part[i];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+    }
+    uint32_t run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int g = PER * lane + i;
+        if (g <= GA) C.wpre[g] = run;
+        run += part[i];
+    }
+}
+
+// This CTA's share of the weighted row space (one thread): row r of group g
+// goes to CTA floor((wpre[g] + r w_g) G / W), so every CTA gets ~W/G of
+// weight; cut into segments of rpt-row tiles. 64-bit products.
+__device__ __forceinline__ int build_segments_weighted(GemvCtrl &C, int n_groups, uint32_t nrows, int rpt, int *err) {
+    const uint64_t W = C.wpre[n_groups], G = gridDim.x, b = blockIdx.x;
+    const uint64_t lo = b * W, hi = (b + 1) * W;
+    // first group whose weight range reaches past lo
+    int g0 = 0, g1 = n_groups;
+    while (g0 < g1) {
+        const int mid = (g0 + g1) >> 1;
+        if (static_cast<uint64_t>(C.wpre[mid + 1]) * G <= lo) g0 = mid + 1;
+        else g1 = mid;
+    }
+    int ns = 0, nt = 0;
+    for (int g = g0; g < n_groups; ++g) {
+        const uint64_t og = static_cast<uint64_t>(C.wpre[g]) * G;
+        if (og >= hi) break;
+        const uint64_t den = static_cast<uint64_t>((C.wpre[g + 1] - C.wpre[g]) / nrows) * G;
+        uint64_t r0 = lo > og ? (lo - og + den - 1) / den : 0;
+        uint64_t r1 = (hi - og + den - 1) / den;
+        if (r0 > nrows) r0 = nrows;
+        if (r1 > nrows) r1 = nrows;
+        if (r1 <= r0) continue;
+        if (ns >= GEMV_MAX_SEGMENTS) { C.fail = 1; set_error(err, DERR_TOO_MANY_SEGMENTS); break; }
+        C.seg_g[ns] = g;
+        C.seg_r0[ns] = static_cast<int32_t>(r0);
+        C.seg_r1[ns] = static_cast<int32_t>(r1);
+        C.seg_t0[ns] = nt;
+        nt += (static_cast<int>(r1 - r0) + rpt - 1) / rpt;
+        ns++;
+    }
+    C.seg_t0[ns] = nt;
+    C.n_seg = ns;
+    C.n_tiles = nt;
+    return ns;
+}
+
 // Tile i of the segment list: group, first row, row count.
 __device__ __forceinline__ void segment_tile(const GemvCtrl &C, int n_seg, int rpt, int i, int &g, int &row0, int &nr) {
     int s = 0;
@@ -957,60 +1033,84 @@ __device__ __forceinline__ void build_groups(GemvCtrl &C, int N, int n_experts, 
     if (N <= 32) {
         if (warp == 0) build_groups_warp(C, N, n_experts, x_of, resolve, err, lane);
     } else {
-        for (int e = tid; e < N; e += blockDim.x) {
-            const int x = x_of(e);
+        // N <= GEMV_MAX_ENTRIES < blockDim.x: thread e holds entry e, so whole
+        // warps hold consecutive entries. Five block barriers, no serial loops
+        // over the entries.
+        const bool act = tid < N;
+        const bool wact = warp < (N + 31) / 32;
+        int x = -1 - tid;
+        if (act) {
+            x = x_of(tid);
             if (x < 0 || x >= n_experts) { C.fail = 1; set_error(err, DERR_BAD_ID); }
-            C.x[e] = x;
+            C.x[tid] = x;
+        }
+        if (tid < GEMV_MAX_ENTRIES) C.cnt[tid] = 0;
+        __syncthreads();
+        const bool ok = !C.fail;
+        int f = tid;
+        if (ok && wact) {
+            // first occurrence: inside the warp by match_any, else in earlier warps
+            const unsigned same = __match_any_sync(0xffffffffu, x);
+            f = 32 * warp + (__ffs(same) - 1);
+            for (int j = 0; j < 32 * warp; ++j)
+                if (C.x[j] == x) { f = j; break; }
+            const unsigned fm = __ballot_sync(0xffffffffu, act && f == tid);
+            if (lane == 0) C.fmask[warp] = fm;
+            if (act) C.first[tid] = static_cast<int16_t>(f);
         }
         __syncthreads();
-        if (!C.fail) {
-            for (int e = tid; e < N; e += blockDim.x) {
-                int f = e;
-                for (int j = 0; j < e; ++j) if (C.x[j] == C.x[e]) { f = j; break; }
-                C.first[e] = static_cast<int16_t>(f);
+        if (ok && act) {
+            // group = number of first occurrences before this entry's first
+            const int wf = f >> 5;
+            int u = __popc(C.fmask[wf] & ((1u << (f & 31)) - 1u));
+            for (int w = 0; w < wf; ++w) u += __popc(C.fmask[w]);
+            C.uidx[tid] = static_cast<int16_t>(u);
+            if (f == tid) C.uexp[u] = x;
+            atomicAdd(reinterpret_cast<int *>(&C.cnt[u & ~1]), (u & 1) ? 0x10000 : 1);
+        }
+        __syncthreads();
+        if (ok && warp == 0) {
+            // exclusive scan of the group sizes (8 groups per lane)
+            int U = 0;
+            for (int w = 0; w < (N + 31) / 32; ++w) U += __popc(C.fmask[w]);
+            int part[8], sum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int u = 8 * lane + i;
+                part[i] = u < U ? C.cnt[u] : 0;
+                sum += part[i];
             }
-        }
-        __syncthreads();
-        if (!C.fail) {
-            for (int e = tid; e < N; e += blockDim.x) {
-                if (C.first[e] == e) {
-                    int u = 0;
-                    for (int j = 0; j < e; ++j) u += (C.first[j] == j);
-                    C.uidx[e] = static_cast<int16_t>(u);
-                    C.uexp[u] = C.x[e];
+            int incl = sum;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int o = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += o;
+            }
+            int run = incl - sum;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int u = 8 * lane + i;
+                if (u < U) {
+                    C.goff[u] = static_cast<int16_t>(run);
+                    C.cnt[u] = 0;
                 }
+                run += part[i];
             }
-        }
-        __syncthreads();
-        if (!C.fail) {
-            for (int e = tid; e < N; e += blockDim.x)
-                if (C.first[e] != e) C.uidx[e] = C.uidx[C.first[e]];
-            if (tid == 0) {
-                int U = 0;
-                for (int e = 0; e < N; ++e) U += (C.first[e] == e);
+            if (lane == 0) {
                 C.n_unique = U;
+                C.goff[U] = static_cast<int16_t>(N);
             }
         }
         __syncthreads();
-        if (!C.fail) {
-            const int U = C.n_unique;
-            for (int u = tid; u < U; u += blockDim.x) {
-                int c = 0;
-                for (int e = 0; e < N; ++e) c += (C.uidx[e] == u);
-                C.goff[u + 1] = static_cast<int16_t>(c);
-                resolve(u, C.uexp[u]);
-            }
-        }
-        __syncthreads();
-        if (!C.fail && tid == 0) {
-            C.goff[0] = 0;
-            for (int u = 0; u < C.n_unique; ++u) C.goff[u + 1] = static_cast<int16_t>(C.goff[u] + C.goff[u + 1]);
-        }
-        __syncthreads();
-        if (!C.fail) {
-            for (int u = tid; u < C.n_unique; u += blockDim.x) {
-                int k = C.goff[u];
-                for (int e = 0; e < N; ++e) if (C.uidx[e] == u) C.gmem[k++] = static_cast<int16_t>(e);
+        if (ok) {
+            if (tid < C.n_unique) resolve(tid, C.uexp[tid]);
+            if (act) {
+                // member slot inside the group; the order of a group's members
+                // does not change any result
+                const int u = C.uidx[tid];
+                const int r = atomicAdd(reinterpret_cast<int *>(&C.cnt[u & ~1]), (u & 1) ? 0x10000 : 1);
+                const int pos = (u & 1) ? (r >> 16) : (r & 0xFFFF);
+                C.gmem[C.goff[u] + pos] = static_cast<int16_t>(tid);
             }
         }
     }
@@ -1103,12 +1203,15 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
         }
     }
 
-    // ---- this CTA's slice of the row space: segments and tiles ------------
-    // (32-bit arithmetic: the launcher guarantees groups * nrows < 2^31)
+    // ---- this CTA's slice of the row space (weighted by members per pass):
+    //      segments and tiles --------------------------------------------------
     const int rpt = a.rows_per_tile;
+    if (warp == 0) {
+        group_weight_prefix(C, U, has_shared, a.ncols_dst, static_cast<uint32_t>(a.nrows), NMX, lane);
+        __syncwarp();
+    }
     if (tid == 0) {
-        const int ns = build_segments(C, static_cast<uint32_t>(U + (has_shared ? 1 : 0)),
-                                      static_cast<uint32_t>(a.nrows), rpt, a.err);
+        const int ns = build_segments_weighted(C, U + (has_shared ? 1 : 0), static_cast<uint32_t>(a.nrows), rpt, a.err);
         // activation keys: (channel_y << 16 | token), KEY_SHARED for the shared block
         int nk = 0;
         for (int s = 0; s < ns && !C.fail; ++s) {

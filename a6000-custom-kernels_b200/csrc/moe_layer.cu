@@ -16,7 +16,7 @@ char g_layer_diag[256];
     X(T_Q4_0, T_Q4_0) X(T_Q5_0, T_Q5_0) X(T_Q8_0, T_Q8_0) X(T_Q5_K, T_Q5_K)
 
 #define MOE_LAYER_DECLARE(A, B) \
-    extern template cudaError_t launch_layer_t<A, B>(const LayerArgs &, int, int, size_t, cudaStream_t);
+    extern template cudaError_t launch_layer_t<A, B>(const LayerArgs &, int, size_t, cudaStream_t);
 MOE_LAYER_PAIRS(MOE_LAYER_DECLARE)
 
 namespace {
@@ -166,9 +166,8 @@ int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why
     size_t smem = 0;
     const int rc = plan_layer(ta, tb, a, &grid, &smem, why);
     if (rc) return rc;
-    const int nmx = a.n_tok == 1 ? 1 : 8;
     cudaError_t e = cudaErrorInvalidValue;
-#define MOE_LAYER_LAUNCH(A, B) else if (ta == A && tb == B) e = launch_layer_t<A, B>(a, nmx, grid, smem, st);
+#define MOE_LAYER_LAUNCH(A, B) else if (ta == A && tb == B) e = launch_layer_t<A, B>(a, grid, smem, st);
     if (false) {}
     MOE_LAYER_PAIRS(MOE_LAYER_LAUNCH)
 #undef MOE_LAYER_LAUNCH

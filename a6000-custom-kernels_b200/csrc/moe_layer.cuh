@@ -115,8 +115,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer_kernel(const __grid
     const int rpt = a.gu.rows_per_tile, rows_b = a.rows_b;
     // this CTA's tiles (one thread): phase A = its share of the (groups x F)
     // row space, phase B = rows [h0, h1) of every group
-    auto plan_tiles = [&](int GA) {
-        build_segments(C, static_cast<uint32_t>(GA), static_cast<uint32_t>(F), rpt, a.err);
+    // weighted: the split weighs each group by its members (C.wpre, made by
+    // group_weight_prefix); unweighted: equal rows (one token: k distinct
+    // picks of one member each, so the two agree in cost)
+    auto plan_tiles = [&](int GA, bool weighted) {
+        if (weighted) build_segments_weighted(C, GA, static_cast<uint32_t>(F), rpt, a.err);
+        else build_segments(C, static_cast<uint32_t>(GA), static_cast<uint32_t>(F), rpt, a.err);
         const uint32_t G = gridDim.x, bid = blockIdx.x;
         const uint32_t q = static_cast<uint32_t>(H) / G, rem = static_cast<uint32_t>(H) % G;
         const int h0 = static_cast<int>(bid * q + (bid < rem ? bid : rem));
@@ -186,7 +190,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer_kernel(const __grid
                 asm volatile("bar.sync 2, %0;" ::"r"(n_tok * 32) : "memory");
                 build_groups_warp(C, N, a.n_experts, x_of, resolve, a.err, lane);
                 __syncwarp();
-                if (lane == 0 && !C.fail) plan_tiles(C.n_unique + (has_shared ? 1 : 0));
+                if (!C.fail) {
+                    group_weight_prefix(C, C.n_unique, has_shared, n_tok, static_cast<uint32_t>(F), NMX, lane);
+                    __syncwarp();
+                    if (lane == 0) plan_tiles(C.n_unique + (has_shared ? 1 : 0), true);
+                }
             }
             __syncwarp();
             asm volatile("bar.arrive 3, %0;" ::"r"(GEMV_THREADS) : "memory");
@@ -195,7 +203,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer_kernel(const __grid
         if (small && one && warp == 0) {
             if (lane == 0) {
                 C.fail = 0;
-                plan_tiles(GA1);
+                plan_tiles(GA1, false);
             }
             __syncwarp();
             asm volatile("bar.arrive 4, 64;" ::: "memory");
@@ -225,7 +233,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer_kernel(const __grid
     } else {
         __syncthreads();
         build_groups(C, N, a.n_experts, x_of, resolve, a.err);   // ends with a block barrier
-        if (tid == 0 && !C.fail) plan_tiles(C.n_unique + (has_shared ? 1 : 0));
+        if (warp == 0 && !C.fail) {
+            group_weight_prefix(C, C.n_unique, has_shared, n_tok, static_cast<uint32_t>(F), NMX, lane);
+            __syncwarp();
+            if (lane == 0) plan_tiles(C.n_unique + (has_shared ? 1 : 0), true);
+        }
         __syncthreads();
     }
     const int U = C.n_unique;

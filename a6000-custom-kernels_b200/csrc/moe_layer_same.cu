@@ -2,8 +2,8 @@
 // down tensor of the gate/up type.
 #include "moe_layer_launch.cuh"
 namespace moe {
-template cudaError_t launch_layer_t<T_Q4_0, T_Q4_0>(const LayerArgs &, int, int, size_t, cudaStream_t);
-template cudaError_t launch_layer_t<T_Q5_0, T_Q5_0>(const LayerArgs &, int, int, size_t, cudaStream_t);
-template cudaError_t launch_layer_t<T_Q8_0, T_Q8_0>(const LayerArgs &, int, int, size_t, cudaStream_t);
-template cudaError_t launch_layer_t<T_Q5_K, T_Q5_K>(const LayerArgs &, int, int, size_t, cudaStream_t);
+template cudaError_t launch_layer_t<T_Q4_0, T_Q4_0>(const LayerArgs &, int, size_t, cudaStream_t);
+template cudaError_t launch_layer_t<T_Q5_0, T_Q5_0>(const LayerArgs &, int, size_t, cudaStream_t);
+template cudaError_t launch_layer_t<T_Q8_0, T_Q8_0>(const LayerArgs &, int, size_t, cudaStream_t);
+template cudaError_t launch_layer_t<T_Q5_K, T_Q5_K>(const LayerArgs &, int, size_t, cudaStream_t);
 }  // namespace moe
