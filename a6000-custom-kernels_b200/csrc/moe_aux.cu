@@ -120,6 +120,21 @@ cudaError_t launch_topk_softmax(const float *logits, int64_t n_tok, int64_t n_ex
 }
 
 // ---------------------------------------------------------------------------
+// GLU pass for gate/up computed by separate GEMVs: the same glu_apply as the
+// fused epilogue (reference kernels/moe-cache.cu:264-280)
+// ---------------------------------------------------------------------------
+__global__ void glu_kernel(const float *__restrict__ g, float *__restrict__ u, int64_t n, int op, float limit) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) u[i] = glu_apply(op, g[i], u[i], limit);
+}
+
+cudaError_t launch_glu(const float *g, float *u, int64_t n, int op, float limit, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    glu_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(g, u, n, op, limit);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // combine: out[t][r] = sum_p w[t][p] * y[t][p][r] (pick order) + ys[t][r]
 // ---------------------------------------------------------------------------
 __global__ void combine_kernel(const float *__restrict__ y, const float *__restrict__ w, const float *__restrict__ ys,

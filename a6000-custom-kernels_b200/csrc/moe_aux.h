@@ -13,6 +13,8 @@ cudaError_t launch_quantize_act(int act_type, const float *x, void *y, int64_t n
                                 cudaStream_t st);
 cudaError_t launch_topk_softmax(const float *logits, int64_t n_tok, int64_t n_experts, int64_t k, int norm_w,
                                 int32_t *ids, float *weights, cudaStream_t st);
+// u[i] = GLU(op, g[i], u[i]) for i < n (the fused epilogue's glu_apply)
+cudaError_t launch_glu(const float *g, float *u, int64_t n, int op, float limit, cudaStream_t st);
 cudaError_t launch_combine(const float *y, const float *w, const float *ys, float *out, int64_t n_tok, int64_t H,
                            int64_t k, cudaStream_t st);
 cudaError_t launch_fill_quantized(int type, void *dst, int64_t n_rows, int64_t n_cols, uint64_t seed, float sigma,

@@ -599,6 +599,7 @@ struct LayerWs {
     uint32_t *gbar;   // fused kernel: [0] launch epoch, [1] finished CTAs (first 256 bytes)
     int32_t *ids;
     float *w, *h, *hs, *y, *ys;
+    float *hg, *hsg;  // gate outputs when gate and up differ in type
     uint64_t *h_tag, *hs_tag;   // fused kernel: h / hs as (value, tag) pairs
     size_t bytes;
 };
@@ -619,6 +620,8 @@ LayerWs layer_ws(const moe_layer_desc *L, int64_t n_tok, char *base) {
     w.ys = reinterpret_cast<float *>(take(sizeof(float) * n_tok * H));
     w.h_tag = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * n_tok * k * F));
     w.hs_tag = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * n_tok * F));
+    w.hg = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k * F));
+    w.hsg = reinterpret_cast<float *>(take(sizeof(float) * n_tok * F));
     w.bytes = off;
     return w;
 }
@@ -724,7 +727,7 @@ int layer_args(const moe_layer_desc *L, const float *x, const float *logits, flo
 
 // True when the fused kernel takes this layer (type pair, sizes, switch).
 bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
-    if (!g.layer_fused) return false;
+    if (!g.layer_fused || L->gate.type != L->up.type) return false;
     moe::LayerArgs a{};
     a.n_tok = static_cast<int32_t>(n_tok);
     a.k = static_cast<int32_t>(L->k);
@@ -934,8 +937,8 @@ int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *
     if (n_tok < 1 || n_tok > 8) return fail(MOE_ERR_UNSUPPORTED, "layer decode handles 1..8 tokens");
     const LayerWs w = layer_ws(L, n_tok, static_cast<char *>(workspace));
     if (!workspace || workspace_bytes < w.bytes) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, w.bytes);
-    if (L->gate.type != L->up.type) return fail(MOE_ERR_UNSUPPORTED, "gate and up must share a type for the fused GEMV");
-    const bool shared = L->shared_type >= 0;   // shared gate/up take up's type, shared down takes down's
+    const bool shared = L->shared_type >= 0;   // the shared gate/up/down take gate's/up's/down's types
+    const bool split_gate = L->gate.type != L->up.type;   // no fused gate/up GEMV: two GEMVs and a GLU pass
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int64_t k = L->k, F = L->F, H = L->H;
     if (L->up.ne[0] != H || L->up.ne[1] != F || L->down.ne[0] != F || L->down.ne[1] != H)
@@ -953,19 +956,11 @@ int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *
     }
     CK(moe::launch_topk_softmax(logits, n_tok, L->n_experts, k, L->norm_w, w.ids, w.w, st));
 
-    moe_fusion_device fd{};
-    fd.gate = L->gate.data;
-    fd.glu_op = L->glu_op;
-    fd.glu_limit = L->glu_limit;
-    if (shared) {
-        fd.shared_up = L->shared_up;
-        fd.shared_gate = L->shared_gate;
-        fd.shared_dst = w.hs;
-        fd.shared_stride_col_dst = F;
-    }
+    // gate/up: one fused GEMV with the GLU in its epilogue, or (types differ,
+    // as llama.cpp then runs them) an up GEMV, a gate GEMV and a GLU pass
     MmvqCall c;
+    moe_fusion_device fd{};
     c.src0 = &L->up;
-    c.gate = &L->gate;
     c.fd = &fd;
     c.src1 = x;
     c.src1_type = MOE_TYPE_F32;
@@ -976,8 +971,39 @@ int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *
     c.stride_col_y = H; c.stride_channel_y = 0;
     c.stride_col_dst = k * F; c.stride_channel_dst = F;
     c.ids_stride = k;
-    int rc = run_mmvq(c, st);
-    if (rc) return rc;
+    if (shared) {
+        fd.shared_up = L->shared_up;
+        fd.shared_dst = w.hs;
+        fd.shared_stride_col_dst = F;
+    }
+    int rc;
+    if (!split_gate) {
+        c.gate = &L->gate;
+        fd.gate = L->gate.data;
+        fd.glu_op = L->glu_op;
+        fd.glu_limit = L->glu_limit;
+        if (shared) fd.shared_gate = L->shared_gate;
+        rc = run_mmvq(c, st);
+        if (rc) return rc;
+    } else {
+        rc = run_mmvq(c, st);   // up (and the shared up) -> h, hs
+        if (rc) return rc;
+        MmvqCall cg = c;
+        moe_fusion_device fg{};
+        cg.src0 = &L->gate;
+        cg.fd = &fg;
+        cg.dst = w.hg;
+        cg.s01 = static_cast<int64_t>(L->gate.nb[1]) / type_size(L->gate.type);
+        if (shared) {
+            fg.shared_up = L->shared_gate;
+            fg.shared_dst = w.hsg;
+            fg.shared_stride_col_dst = F;
+        }
+        rc = run_mmvq(cg, st);   // gate (and the shared gate) -> hg, hsg
+        if (rc) return rc;
+        CK(moe::launch_glu(w.hg, w.h, n_tok * k * F, L->glu_op, L->glu_limit, st));
+        if (shared) CK(moe::launch_glu(w.hsg, w.hs, n_tok * F, L->glu_op, L->glu_limit, st));
+    }
 
     moe_fusion_device fd2{};
     if (shared) {

@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=32, help="independent layer copies cycled by the timed loop")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=2,
+                    help="BASELINE config; 2 (default) is the headline line, 1/3/5 print their own lines")
+    ap.add_argument("--batch", type=int, default=1, help="decode tokens per step (configs 3 and 5)")
     return ap.parse_args()
 
 
@@ -475,12 +478,201 @@ def run_e2e(pkg, layers, xs_np, lg_np, dev, stream, steps):
     return {"seconds": ev0.elapsed_time(ev1) / 1e3, "steps": steps, "h2d": (H + E) * 4, "d2h": H * 4}
 
 
+# ---------------------------------------------------------------------------
+# Other BASELINE configs (their own JSON lines; the headline is config 2)
+# ---------------------------------------------------------------------------
+STACK_TYPES = (Q2_K, 11, 12, 14)              # Q2_K, Q3_K, Q4_K, Q6_K
+STACK_P = (0.40, 0.30, 0.15, 0.15)            # ~0.47 B/weight: ~77 GiB for 48 layers
+BYTES_PER_W = {2: 18 / 32, 10: 84 / 256, 11: 110 / 256, 12: 144 / 256, 14: 210 / 256}
+
+
+def stack_types(n_layers, seed=3):
+    """Per-layer types drawn by seed: one draw for the gate/up pair (llama.cpp's
+    quantization mixes give ffn_gate and ffn_up the same type) and one for down."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n_layers):
+        gu, dn = (int(t) for t in rng.choice(STACK_TYPES, size=2, p=STACK_P))
+        out.append({"gate": gu, "up": gu, "down": dn})
+    return out
+
+
+def run_other_config(args):
+    """Config 1: one small Q4_0 layer (32 copies cycled). Config 3: the
+    48-layer stack, one decode step = every layer in turn with a residual add,
+    batch 1..64 (chunks of 8 tokens per layer launch above 8). Config 5:
+    config 3's shape with experts in pinned host memory behind a pool capped at
+    25 % of the experts, seeded from a Zipf frequency table; eager steps with
+    the cache step between them (it cannot run inside graph capture)."""
+    import torch
+    import importlib
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    mc = pkg.moe_cache
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+    B = args.batch
+    seed_path = None
+    if args.config == 1:
+        H1, F1, E1, R = 2048, 512, 64, 32
+        mc.configure(enabled=True)
+        layers = [pkg.MoELayer(H1, F1, E1, 8, {"gate": 2, "up": 2, "down": 2}, shared=False, device=dev, seed=l,
+                               name=f"c1.{l}") for l in range(R)]
+        rng = np.random.default_rng(11)
+        P = 64
+        xs = torch.from_numpy(rng.normal(0, 1, (P, B, H1)).astype(np.float32)).to(dev)
+        lgs = torch.from_numpy(rng.normal(0, 1, (P, B, E1)).astype(np.float32)).to(dev)
+        outs = torch.empty((P, B, H1), device=dev)
+        step_bytes = []
+        lg_np = lgs.cpu().numpy()
+        for i in range(P):
+            picks = set(np.argsort(-lg_np[i], axis=1, kind="stable")[:, :8].reshape(-1).tolist())
+            step_bytes.append(len(picks) * 3 * F1 * H1 * BYTES_PER_W[2])
+
+        def step(i):
+            layers[i % R].decode(xs[i % P], lgs[i % P], outs[i % P], stream=stream)
+        launches = 1 if layers[0].fused(B) else 4
+        workload = f"config1: H=2048, E=64, F=512, top-8 over N(0,1) logits, Q4_0, no shared expert; batch {B}"
+        n_layers_step = 1
+        mean_bytes = float(np.mean(step_bytes))
+    else:
+        n_layers = 48 if args.config == 3 else 8       # config 5: 8 layers in pinned host memory
+        types = stack_types(n_layers)
+        host = args.config == 5
+        seed_path = None
+        if host:
+            # seed each tensor's pool with its 128 most frequent experts under
+            # the layer's Zipf permutation (the routing-frequency table)
+            import tempfile
+            lines = []
+            for l in range(n_layers):
+                perm = np.random.default_rng(1000 + l).permutation(E)
+                hot = np.argsort(perm)[:128]
+                for r in ("gate", "up", "down"):
+                    lines.append(f"blk.{l}.ffn_{r}_exps.weight " + ",".join(str(int(e)) for e in hot))
+            fd_, seed_path = tempfile.mkstemp(suffix=".seed")
+            os.write(fd_, ("\n".join(lines) + "\n").encode())
+            os.close(fd_)
+            mc.configure(enabled=True, slots=128, budget_gb=1e6, seed_path=seed_path)
+        else:
+            mc.configure(enabled=True)
+        layers = [pkg.MoELayer(H, F, E, K_TOP, types[l], shared=True, device=dev, host=host, seed=7000 + l,
+                               name=f"blk.{l}") for l in range(n_layers)]
+        P = 16
+        rng = np.random.default_rng(33)
+        xs = torch.from_numpy(rng.normal(0, 1, (P, B, H)).astype(np.float32)).to(dev)
+        lg_np = np.zeros((n_layers, P, B, E), np.float32)
+        for l in range(n_layers):
+            perm = np.random.default_rng(1000 + l).permutation(E)
+            base = -1.1 * np.log(perm + 1.0)
+            lg_np[l] = base[None, None, :] + rng.normal(0, 1, (P, B, E))
+        lgs = torch.from_numpy(lg_np).to(dev)
+        xbuf = torch.empty((B, H), device=dev)
+        obuf = torch.empty((B, H), device=dev)
+        chunks = [(c, min(B, c + 8)) for c in range(0, B, 8)]
+        step_bytes = []
+        for i in range(P):
+            tot = 0.0
+            for l in range(n_layers):
+                picks = set(np.argsort(-lg_np[l, i], axis=1, kind="stable")[:, :8].reshape(-1).tolist())
+                for r, t in types[l].items():
+                    rows, cols = (F, H) if r != "down" else (H, F)
+                    tot += (len(picks) + 1) * rows * cols * BYTES_PER_W[t]
+            step_bytes.append(tot)
+
+        def step(i):
+            with torch.cuda.stream(stream):
+                xbuf.copy_(xs[i % P])
+                for l in range(n_layers):
+                    for c0, c1 in chunks:
+                        layers[l].decode(xbuf[c0:c1], lgs[l, i % P, c0:c1], obuf[c0:c1], stream=stream)
+                    xbuf.add_(obuf)
+        fused = all(L.fused(c1 - c0) for L in layers for c0, c1 in chunks)
+        launches = n_layers * len(chunks) * (1 if fused else 4)
+        gib = sum(sum(L.w[r].numel() for r in ("gate", "up", "down")) for L in layers) / 2 ** 30
+        workload = (f"config{args.config}: {n_layers}-layer stack of config-2 layers, per-tensor types from "
+                    f"{{Q2_K,Q3_K,Q4_K,Q6_K}} drawn by seed (gate/up pair, down) ({gib:.1f} GiB of experts), per-layer Zipf(1.1) routing, "
+                    f"shared expert, f32 residual; batch {B}")
+        if host:
+            workload += "; experts in pinned host memory, pool 128 of 512 per tensor, seeded"
+        n_layers_step = n_layers
+        mean_bytes = float(np.mean(step_bytes))
+
+    K = args.steps
+    W = max(args.warmup, 3)
+    if args.config == 5:
+        for i in range(W):
+            step(i)
+            mc.step(stream)
+        torch.cuda.synchronize()
+        s0 = mc.stats()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for i in range(K):
+            step(i)
+            mc.step(stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        s1 = mc.stats()
+        hits, misses = s1["hits"] - s0["hits"], s1["misses"] - s0["misses"]
+        extra = {"hit_rate": round(hits / max(1, hits + misses), 4),
+                 "promotions_per_step": round((s1["promotions"] - s0["promotions"]) / K, 2),
+                 "timing": "eager steps (cache step between them), device events"}
+    else:
+        with torch.cuda.stream(stream):
+            for i in range(W):
+                step(i)
+        torch.cuda.synchronize()
+        G = 64 if n_layers_step > 1 else 512
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for j in range(G):
+                step(j)
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = max(1, K // G)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        K = reps * G
+        extra = {"timing": f"CUDA graphs of {G} steps, device events"}
+        del g
+    assert mc.device_error(stream) == 0
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs") or 6650.0
+    gbs = mean_bytes * K / (ms / 1e3) / 1e9
+    line = {"metric": METRIC, "value": round(B * K / (ms / 1e3), 2), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+            "warmup": W, "ms_per_step": round(ms / K, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": workload, "global_batch": B, "layers_per_step": n_layers_step},
+            "expert_gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
+            "bytes_per_step": round(mean_bytes), "gpu_launches": launches * K, **extra}
+    print(json.dumps(line), flush=True)
+    for L in layers:
+        L._ws.clear()
+    if seed_path:
+        os.unlink(seed_path)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
-    else:
+    elif args.config == 2:
         run_mine(args)
+    else:
+        run_other_config(args)
 
 
 if __name__ == "__main__":

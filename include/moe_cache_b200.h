@@ -186,8 +186,8 @@ int moe_b200_topk_softmax(const float *logits, int64_t n_tok, int64_t n_experts,
 /* One MoE FFN layer (gate/up/down expert tensors + optional shared expert). */
 typedef struct {
     moe_tensor  gate, up, down;        /* expert tensors: [E][F][H], [E][F][H], [E][H][F] */
-    int32_t     shared_type;           /* -1: no shared expert; otherwise the shared gate/up
-                                          have up.type and the shared down has down.type */
+    int32_t     shared_type;           /* -1: no shared expert; otherwise the shared gate, up
+                                          and down have gate.type, up.type and down.type */
     const void *shared_gate, *shared_up, *shared_down;
     int64_t     H, F, n_experts, k;
     int32_t     glu_op;
@@ -201,13 +201,16 @@ typedef struct {
  * kernel's launch epoch, which tags the data its CTAs exchange. Layout after
  * them (each part 256-byte aligned): ids int32[n][k], weights f32[n][k],
  * h f32[n][k][F], hs f32[n][F], y f32[n][k][H], ys f32[n][H], then the
- * fused kernel's tagged copies of h and hs. */
+ * fused kernel's tagged copies of h and hs, then the gate outputs when gate
+ * and up differ in type (f32[n][k][F], f32[n][F]). */
 size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok);
 
 /* No counterpart in the reference (the upstream graph around two
  * MUL_MAT_ID calls): one MoE layer for n_tok <= 8 decode tokens, f32 in/out on
  * device: route, fused gate/up GEMV + GLU, down GEMV, weighted combine plus the
- * shared expert. Activations use llama.cpp CPU semantics (see src1_type F32).
+ * shared expert; gate and up of different types run as two GEMVs and a GLU
+ * pass (as llama.cpp does). Activations use llama.cpp CPU semantics (see
+ * src1_type F32).
  * Allocates nothing: `workspace` is caller-owned device memory (zero-filled
  * before first use). Where moe_b200_layer_fused says so, the whole layer is
  * ONE cooperative kernel launch (one CTA per SM, one grid barrier between

@@ -30,7 +30,9 @@ def _cache(pkg, cuda):
 
 @pytest.mark.parametrize("types,n_tok", [((O.Q2_K, O.Q2_K, O.Q2_K), 1), ((O.Q3_K, O.Q3_K, O.Q6_K), 4),
                                          ((O.Q4_K, O.Q4_K, O.Q5_K), 8), ((O.Q4_0, O.Q4_0, O.Q8_0), 2),
-                                         ((O.Q5_0, O.Q5_0, O.Q4_0), 1)])
+                                         ((O.Q5_0, O.Q5_0, O.Q4_0), 1),
+                                         # gate and up of different types: two GEMVs and a GLU pass
+                                         ((O.Q2_K, O.Q4_K, O.Q3_K), 1), ((O.Q6_K, O.Q3_K, O.Q2_K), 5)])
 def test_layer_decode_matches_oracle(pkg, cuda, types, n_tok):
     H, F, E, k = 1024, 512, 24, 8
     L = _layer_np(types, H, F, E, seed=sum(types))
