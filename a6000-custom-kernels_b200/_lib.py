@@ -104,6 +104,7 @@ def _declare(L):
         "moe_b200_noalloc_device_error": (i32, [vp, ctypes.POINTER(i32)]),
         "moe_b200_layer_fused": (i32, [ctypes.POINTER(MoeLayerDesc), i64]),
         "moe_b200_layer_set_fused": (i32, [i32]),
+        "moe_b200_ep_layer_decode": (i32, [ctypes.POINTER(MoeLayerDesc), i64, i64, i32, vp, vp, vp, i64, vp, sz, vp]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)

@@ -152,6 +152,35 @@ __global__ void combine_kernel(const float *__restrict__ y, const float *__restr
     out[static_cast<int64_t>(t) * H + r] = acc;
 }
 
+__global__ void combine_local_kernel(const float *__restrict__ y, const float *__restrict__ w,
+                                     const float *__restrict__ ys, const int32_t *__restrict__ ids, int id_lo,
+                                     int n_local, float *__restrict__ out, int H, int k) {
+    const int t = blockIdx.y;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= H) return;
+    const float *yt = y + static_cast<int64_t>(t) * k * H;
+    float acc = 0.f;
+    bool any = false;
+    for (int p = 0; p < k; ++p) {
+        const int x = ids[t * k + p] - id_lo;
+        if (x < 0 || x >= n_local) continue;
+        const float v = __fmul_rn(yt[static_cast<int64_t>(p) * H + r], w[t * k + p]);
+        acc = any ? __fadd_rn(acc, v) : v;
+        any = true;
+    }
+    if (ys) acc = __fadd_rn(acc, ys[static_cast<int64_t>(t) * H + r]);
+    out[static_cast<int64_t>(t) * H + r] = acc;
+}
+
+cudaError_t launch_combine_local(const float *y, const float *w, const float *ys, const int32_t *ids, int id_lo,
+                                 int n_local, float *out, int64_t n_tok, int64_t H, int64_t k, cudaStream_t st) {
+    if (n_tok == 0) return cudaSuccess;
+    dim3 grid(static_cast<unsigned>((H + 255) / 256), static_cast<unsigned>(n_tok));
+    combine_local_kernel<<<grid, 256, 0, st>>>(y, w, ys, ids, id_lo, n_local, out, static_cast<int>(H),
+                                                static_cast<int>(k));
+    return cudaGetLastError();
+}
+
 cudaError_t launch_combine(const float *y, const float *w, const float *ys, float *out, int64_t n_tok, int64_t H,
                            int64_t k, cudaStream_t st) {
     if (n_tok == 0) return cudaSuccess;

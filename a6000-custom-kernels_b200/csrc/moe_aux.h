@@ -15,6 +15,10 @@ cudaError_t launch_topk_softmax(const float *logits, int64_t n_tok, int64_t n_ex
                                 int32_t *ids, float *weights, cudaStream_t st);
 // u[i] = GLU(op, g[i], u[i]) for i < n (the fused epilogue's glu_apply)
 cudaError_t launch_glu(const float *g, float *u, int64_t n, int op, float limit, cudaStream_t st);
+// out[t][r] = sum over the picks p with ids[t][p] in [id_lo, id_lo + n_local)
+// of w * y (pick order), plus ys; 0 + ys when no pick is local
+cudaError_t launch_combine_local(const float *y, const float *w, const float *ys, const int32_t *ids, int id_lo,
+                                 int n_local, float *out, int64_t n_tok, int64_t H, int64_t k, cudaStream_t st);
 cudaError_t launch_combine(const float *y, const float *w, const float *ys, float *out, int64_t n_tok, int64_t H,
                            int64_t k, cudaStream_t st);
 cudaError_t launch_fill_quantized(int type, void *dst, int64_t n_rows, int64_t n_cols, uint64_t seed, float sigma,

@@ -494,6 +494,8 @@ struct MmvqCall {
     int64_t stride_channel_y = 0, stride_channel_dst = 0, ids_stride = 0;
     const void *shared_y = nullptr;               // layer path: shared-block activations
     int64_t shared_y_stride_col = 0;
+    int64_t id_offset = 0;                        // expert-parallel: first expert of this GPU
+    int skip_foreign = 0;                         // expert-parallel: other GPUs' ids are skipped
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -573,6 +575,8 @@ int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
     a.nchannels_y = static_cast<int32_t>(c.nchannels_y);
     a.ids = c.ids;
     a.ids_stride = c.ids_stride;
+    a.id_offset = static_cast<int32_t>(c.id_offset);
+    a.skip_foreign = c.skip_foreign;
     a.ncols_dst = static_cast<int32_t>(c.ncols_dst);
     a.nchannels_dst = static_cast<int32_t>(c.nchannels_dst);
     a.n_experts = e->n_experts;
@@ -1028,6 +1032,86 @@ int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *
     rc = run_mmvq(d, st);
     if (rc) return rc;
     CK(moe::launch_combine(w.y, w.w, shared ? w.ys : nullptr, out, n_tok, H, k, st));
+    return MOE_OK;
+}
+
+int moe_b200_ep_layer_decode(const moe_layer_desc *L, int64_t expert_lo, int64_t n_experts_global,
+                              int32_t with_shared, const float *x, const float *logits, float *out, int64_t n_tok,
+                              void *workspace, size_t workspace_bytes, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || !x || !logits || !out) return fail(MOE_ERR_INVALID, "null argument");
+    if (n_tok < 1 || n_tok > 8) return fail(MOE_ERR_UNSUPPORTED, "layer decode handles 1..8 tokens");
+    if (expert_lo < 0 || expert_lo + L->n_experts > n_experts_global || n_experts_global > 65536)
+        return fail(MOE_ERR_INVALID, "local experts [%lld, %lld) outside the %lld routed experts",
+                    static_cast<long long>(expert_lo), static_cast<long long>(expert_lo + L->n_experts),
+                    static_cast<long long>(n_experts_global));
+    const LayerWs w = layer_ws(L, n_tok, static_cast<char *>(workspace));
+    if (!workspace || workspace_bytes < w.bytes) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, w.bytes);
+    if (L->gate.type != L->up.type) return fail(MOE_ERR_UNSUPPORTED, "expert-parallel decode needs one gate/up type");
+    const bool shared = with_shared && L->shared_type >= 0;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t k = L->k, F = L->F, H = L->H;
+    if (k < 1 || k > 32 || k > n_experts_global) return fail(MOE_ERR_INVALID, "need 1 <= k <= min(32, n_experts)");
+    if (L->up.ne[0] != H || L->up.ne[1] != F || L->down.ne[0] != F || L->down.ne[1] != H)
+        return fail(MOE_ERR_INVALID, "expert tensor shapes do not match H/F");
+    // every GPU routes over all experts (same logits, same bits)
+    CK(moe::launch_topk_softmax(logits, n_tok, n_experts_global, k, L->norm_w, w.ids, w.w, st));
+    moe_fusion_device fd{};
+    fd.gate = L->gate.data;
+    fd.glu_op = L->glu_op;
+    fd.glu_limit = L->glu_limit;
+    if (shared) {
+        fd.shared_up = L->shared_up;
+        fd.shared_gate = L->shared_gate;
+        fd.shared_dst = w.hs;
+        fd.shared_stride_col_dst = F;
+    }
+    MmvqCall c;
+    c.src0 = &L->up;
+    c.gate = &L->gate;
+    c.fd = &fd;
+    c.src1 = x;
+    c.src1_type = MOE_TYPE_F32;
+    c.ids = w.ids;
+    c.dst = w.h;
+    c.ne00 = H; c.ne01 = F; c.ncols_dst = n_tok; c.s01 = static_cast<int64_t>(L->up.nb[1]) / type_size(L->up.type);
+    c.nchannels_y = 1; c.nchannels_dst = k;
+    c.stride_col_y = H; c.stride_channel_y = 0;
+    c.stride_col_dst = k * F; c.stride_channel_dst = F;
+    c.ids_stride = k;
+    c.id_offset = expert_lo;
+    c.skip_foreign = 1;
+    int rc = run_mmvq(c, st);
+    if (rc) return rc;
+    moe_fusion_device fd2{};
+    if (shared) {
+        fd2.shared_up = L->shared_down;
+        fd2.shared_dst = w.ys;
+        fd2.shared_stride_col_dst = H;
+    }
+    MmvqCall d;
+    d.src0 = &L->down;
+    d.fd = &fd2;
+    d.src1 = w.h;
+    d.src1_type = MOE_TYPE_F32;
+    d.ids = w.ids;
+    d.dst = w.y;
+    d.ne00 = F; d.ne01 = H; d.ncols_dst = n_tok; d.s01 = static_cast<int64_t>(L->down.nb[1]) / type_size(L->down.type);
+    d.nchannels_y = k; d.nchannels_dst = k;
+    d.stride_col_y = k * F; d.stride_channel_y = F;
+    d.stride_col_dst = k * H; d.stride_channel_dst = H;
+    d.ids_stride = k;
+    d.shared_y = shared ? w.hs : nullptr;
+    d.shared_y_stride_col = F;
+    d.id_offset = expert_lo;
+    d.skip_foreign = 1;
+    rc = run_mmvq(d, st);
+    if (rc) return rc;
+    // this GPU's share of the weighted sum: its own picks (pick order) and,
+    // where it holds it, the shared expert; the caller sums the GPUs' shares
+    CK(moe::launch_combine_local(w.y, w.w, shared ? w.ys : nullptr, w.ids, static_cast<int>(expert_lo),
+                                 static_cast<int>(L->n_experts), out, n_tok, H, k, st));
     return MOE_OK;
 }
 

@@ -56,9 +56,12 @@ struct GemvArgs {
     const void *y;
     int64_t stride_col_y, stride_channel_y;
     int32_t nchannels_y;
-    // routing
+    // routing; expert-parallel: ids are global, this tensor holds experts
+    // [id_offset, id_offset + n_experts), and with skip_foreign the other ids
+    // are left out (no output) instead of being errors
     const int32_t *ids;
     int64_t ids_stride;
+    int32_t id_offset, skip_foreign;
     int32_t ncols_dst, nchannels_dst, n_experts;
     // output
     float *dst;
@@ -984,27 +987,31 @@ __device__ __forceinline__ void segment_tile(const GemvCtrl &C, int n_seg, int r
 // block barriers: __match_any_sync groups equal experts.
 template <class XOf, class Resolve>
 __device__ __forceinline__ void build_groups_warp(GemvCtrl &C, int N, int n_experts, XOf x_of, Resolve resolve,
-                                                  int *err, int lane) {
+                                                  int *err, int lane, bool skip_foreign = false) {
     int x = -1 - lane;
-    bool bad = false;
+    bool bad = false, valid = false;
     if (lane < N) {
-        x = x_of(lane);
-        bad = x < 0 || x >= n_experts;
-        C.x[lane] = x;
+        const int xe = x_of(lane);
+        const bool out = xe < 0 || xe >= n_experts;
+        bad = out && !skip_foreign;
+        valid = !out;
+        C.x[lane] = out ? -1 : xe;      // -1: another GPU's expert
+        if (!out) x = xe;
     }
     if (__ballot_sync(0xffffffffu, bad)) {
         if (lane == 0) { C.fail = 1; set_error(err, DERR_BAD_ID); }
     } else {
         const unsigned same = __match_any_sync(0xffffffffu, x);
         const int f = __ffs(same) - 1;
-        const unsigned firsts = __ballot_sync(0xffffffffu, lane < N && f == lane);
+        const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+        const unsigned firsts = __ballot_sync(0xffffffffu, valid && f == lane);
         const int u = __popc(firsts & ((1u << f) - 1u));
         int pos = 0;
         for (int j = 0; j < N; ++j) {
             const int fj = __shfl_sync(0xffffffffu, f, j);
-            pos += (fj < f) || (fj == f && j < lane);
+            pos += ((vmask >> j) & 1u) && ((fj < f) || (fj == f && j < lane));
         }
-        if (lane < N) {
+        if (valid) {
             C.first[lane] = static_cast<int16_t>(f);
             C.uidx[lane] = static_cast<int16_t>(u);
             C.gmem[pos] = static_cast<int16_t>(lane);
@@ -1016,7 +1023,7 @@ __device__ __forceinline__ void build_groups_warp(GemvCtrl &C, int N, int n_expe
         }
         if (lane == 0) {
             C.n_unique = __popc(firsts);
-            C.goff[__popc(firsts)] = static_cast<int16_t>(N);
+            C.goff[__popc(firsts)] = static_cast<int16_t>(__popc(vmask));
         }
     }
 }
@@ -1028,21 +1035,24 @@ __device__ __forceinline__ void build_groups_warp(GemvCtrl &C, int N, int n_expe
 // barrier. A bad expert id sets C.fail.
 template <class XOf, class Resolve>
 __device__ __forceinline__ void build_groups(GemvCtrl &C, int N, int n_experts, XOf x_of, Resolve resolve,
-                                             int *err) {
+                                             int *err, bool skip_foreign = false) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (N <= 32) {
-        if (warp == 0) build_groups_warp(C, N, n_experts, x_of, resolve, err, lane);
+        if (warp == 0) build_groups_warp(C, N, n_experts, x_of, resolve, err, lane, skip_foreign);
     } else {
         // N <= GEMV_MAX_ENTRIES < blockDim.x: thread e holds entry e, so whole
         // warps hold consecutive entries. Five block barriers, no serial loops
         // over the entries.
-        const bool act = tid < N;
+        bool act = tid < N;     // a valid entry of this GPU's experts
         const bool wact = warp < (N + 31) / 32;
         int x = -1 - tid;
         if (act) {
-            x = x_of(tid);
-            if (x < 0 || x >= n_experts) { C.fail = 1; set_error(err, DERR_BAD_ID); }
-            C.x[tid] = x;
+            const int xe = x_of(tid);
+            const bool out = xe < 0 || xe >= n_experts;
+            if (out && !skip_foreign) { C.fail = 1; set_error(err, DERR_BAD_ID); }
+            C.x[tid] = out ? -1 : xe;   // -1: another GPU's expert
+            if (!out) x = xe;
+            act = !out;
         }
         if (tid < GEMV_MAX_ENTRIES) C.cnt[tid] = 0;
         __syncthreads();
@@ -1086,6 +1096,7 @@ __device__ __forceinline__ void build_groups(GemvCtrl &C, int N, int n_experts, 
                 const int o = __shfl_up_sync(0xffffffffu, incl, off);
                 if (lane >= off) incl += o;
             }
+            const int total = __shfl_sync(0xffffffffu, incl, 31);   // valid entries
             int run = incl - sum;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -1098,7 +1109,7 @@ __device__ __forceinline__ void build_groups(GemvCtrl &C, int N, int n_experts, 
             }
             if (lane == 0) {
                 C.n_unique = U;
-                C.goff[U] = static_cast<int16_t>(N);
+                C.goff[U] = static_cast<int16_t>(total);
             }
         }
         __syncthreads();
@@ -1167,7 +1178,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
     };
     build_groups(
         C, N, a.n_experts,
-        [&](int e) { return a.ids[e % nch + static_cast<int64_t>(e / nch) * a.ids_stride]; }, resolve, a.err);
+        [&](int e) { return a.ids[e % nch + static_cast<int64_t>(e / nch) * a.ids_stride] - a.id_offset; }, resolve,
+        a.err, a.skip_foreign != 0);
     if (C.fail) return;
     const int U = C.n_unique;
 
@@ -1176,6 +1188,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
         const uint32_t clk = a.clock ? *a.clock : 0u;
         for (int e = tid; e < N; e += blockDim.x) {
             const int x = C.x[e];
+            if (x < 0) continue;   // another GPU's expert
             const int u = C.uidx[e];
             if (a.tbl) {
                 if (a.stamps) a.stamps[x] = clk;

@@ -220,6 +220,19 @@ size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok)
 int moe_b200_layer_decode(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
                           int64_t n_tok, void *workspace, size_t workspace_bytes, moe_stream_t stream);
 
+/* No counterpart in the reference: the expert-parallel share of one MoE
+ * layer decode. `layer` describes THIS GPU's experts: its gate/up/down tensors
+ * hold n_experts = E_local experts, global experts [expert_lo, expert_lo +
+ * E_local) of the n_experts_global the router picks from. Every GPU routes the
+ * same tokens over all experts (same logits, same picks and weights), runs
+ * the GEMVs on the picks it holds, and writes its share of the weighted sum to
+ * `out` (its picks in pick order, plus the shared expert when with_shared);
+ * the caller sums the shares over GPUs (e.g. an NCCL all-reduce). Workspace
+ * as moe_b200_layer_decode. Gate and up must share a type. */
+int moe_b200_ep_layer_decode(const moe_layer_desc *layer, int64_t expert_lo, int64_t n_experts_global,
+                             int32_t with_shared, const float *x, const float *logits, float *out, int64_t n_tok,
+                             void *workspace, size_t workspace_bytes, moe_stream_t stream);
+
 /* No counterpart in the reference: 1 when moe_b200_layer_decode runs this
  * layer as one fused kernel for n_tok tokens (gate/up and down type pair with a
  * fused kernel, n_tok <= 8, n_tok * k <= 64, activations and tiles fit in

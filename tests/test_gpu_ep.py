@@ -1,0 +1,93 @@
+"""Expert-parallel decode (a6000-custom-kernels_b200/ep.py,
+moe_b200_ep_layer_decode): each rank's share, summed over ranks, equals the
+single-GPU layer. The ranks are emulated one after another on one GPU (the sum
+is what the all-reduce computes); with two or more GPUs a real NCCL run is
+checked too."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from moe_data import activations, zipf_logits
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _cache(pkg, cuda):
+    pkg.moe_cache.configure(enabled=True)
+    yield
+    pkg.moe_cache.reset()
+
+
+def _ep(pkg):
+    from importlib import import_module
+    return import_module("a6000-custom-kernels_b200.ep")
+
+
+@pytest.mark.parametrize("world,n_tok,types", [(2, 1, (O.Q2_K, O.Q2_K, O.Q2_K)), (4, 3, (O.Q4_K, O.Q4_K, O.Q6_K)),
+                                               (8, 8, (O.Q3_K, O.Q3_K, O.Q2_K)), (3, 2, (O.Q4_0, O.Q4_0, O.Q8_0))])
+def test_rank_shares_sum_to_the_layer(pkg, cuda, world, n_tok, types):
+    ep = _ep(pkg)
+    H, F, E, k = 1024, 512, 64, 8
+    full = pkg.MoELayer(H, F, E, k, {"gate": types[0], "up": types[1], "down": types[2]}, shared=True, seed=9)
+    x = torch.from_numpy(activations((n_tok, H), seed=3)).to(cuda)
+    lg = torch.from_numpy(zipf_logits(n_tok, E, seed=4)).to(cuda)
+    pkg.moe_cache.set_layer_fused(False)      # the four-launch path: same pick-order combine per rank
+    ref = full.decode(x, lg).cpu().numpy()
+    ids_ref = full.routing_of(n_tok)[0].cpu().numpy()
+    pkg.moe_cache.set_layer_fused(True)
+    total = np.zeros_like(ref)
+    for r in range(world):
+        part = ep.EPMoELayer(full, r, world).partial(x, lg).cpu().numpy()
+        total += part
+    assert pkg.moe_cache.device_error() == 0
+    err = np.abs(total - ref).max() / np.abs(ref).max()
+    assert err < 1e-5, err
+    # every rank routed the same picks
+    lo, hi = ep.expert_range(E, 1 % world, world)
+    assert ids_ref.min() >= 0 and ids_ref.max() < E and hi > lo
+
+
+def _nccl_worker(rank, world, port, q):
+    import importlib
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    ep = importlib.import_module("a6000-custom-kernels_b200.ep")
+    pkg.moe_cache.configure(enabled=True)
+    H, F, E, k = 1024, 512, 64, 8
+    full = pkg.MoELayer(H, F, E, k, {"gate": 10, "up": 10, "down": 10}, shared=True, seed=9, device=f"cuda:{rank}")
+    x = torch.from_numpy(activations((2, H), seed=3)).cuda()
+    lg = torch.from_numpy(zipf_logits(2, E, seed=4)).cuda()
+    pkg.moe_cache.set_layer_fused(False)
+    ref = full.decode(x, lg)
+    out = ep.EPMoELayer(full, rank, world).decode(x, lg)
+    torch.cuda.synchronize()
+    err = float((out - ref).abs().max() / ref.abs().max())
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((rank, err))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_all_reduce_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert all(p.exitcode == 0 for p in procs)
+    assert all(e < 1e-5 for e in res.values()), res
