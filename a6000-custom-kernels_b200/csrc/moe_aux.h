@@ -8,6 +8,7 @@ namespace moe {
 
 struct GemvArgs;
 struct LayerArgs;
+struct MmqArgs;
 
 cudaError_t launch_quantize_act(int act_type, const float *x, void *y, int64_t n_rows, int64_t n_cols,
                                 cudaStream_t st);
@@ -35,5 +36,14 @@ int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **wh
 // (-3 with *cuda_err on a CUDA error).
 int plan_layer(int ta, int tb, LayerArgs &a, int *grid, size_t *smem, const char **why);
 int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
+
+// Prefill grouped GEMM on the tensor cores (moe_mmq.cu): launch_mmq_group
+// groups the (token, pick) entries by expert into offsets / entries and the
+// tile prefix; launch_mmq runs the int8 MMQ over that tile list (-2 with *why
+// when the type or shape has no tensor-core path, -3 with *cuda_err).
+cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int row_blocks,
+                             int32_t *cnt, int32_t *offsets, int32_t *cursor, int32_t *entries, int32_t *tile_off,
+                             int *err, cudaStream_t st);
+int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
 
 }  // namespace moe

@@ -29,6 +29,7 @@
 #include "moe_cache_b200.h"
 #include "moe_gemv.cuh"
 #include "moe_layer.cuh"
+#include "moe_mmq.cuh"
 
 namespace {
 
@@ -749,6 +750,29 @@ bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
     return moe::plan_layer(L->up.type, L->down.type, a, &grid, &smem, &why) == 0;
 }
 
+
+// Prefill workspace: the tokens' Q8_K blocks, then the grouping arrays
+struct PrefillWs {
+    uint8_t *x8;
+    int32_t *cnt, *offsets, *cursor, *entries, *tile_off;
+    size_t bytes;
+};
+
+PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, char *base) {
+    PrefillWs w{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
+    const int64_t E = src0->ne[2], K = src0->ne[0];
+    w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(n_tok) * (K / 256) * 292));
+    w.cnt = reinterpret_cast<int32_t *>(take(4 * E));
+    w.offsets = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
+    w.cursor = reinterpret_cast<int32_t *>(take(4 * E));
+    w.entries = reinterpret_cast<int32_t *>(take(4 * n_tok * k));
+    w.tile_off = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
+    w.bytes = off;
+    return w;
+}
+
 }  // namespace
 
 // ============================================================================
@@ -1112,6 +1136,80 @@ int moe_b200_ep_layer_decode(const moe_layer_desc *L, int64_t expert_lo, int64_t
     // where it holds it, the shared expert; the caller sums the GPUs' shares
     CK(moe::launch_combine_local(w.y, w.w, shared ? w.ys : nullptr, w.ids, static_cast<int>(expert_lo),
                                  static_cast<int>(L->n_experts), out, n_tok, H, k, st));
+    return MOE_OK;
+}
+
+size_t moe_b200_prefill_workspace_size(const moe_tensor *src0, int64_t n_tok, int64_t k) {
+    if (!src0 || n_tok < 0 || k < 0) return 0;
+    return prefill_ws(src0, n_tok, k, nullptr).bytes;
+}
+
+int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t n_tok, const int32_t *ids, int64_t k,
+                                int64_t ids_stride, float *dst, void *workspace, size_t workspace_bytes,
+                                int32_t *used_tensor_cores, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (used_tensor_cores) *used_tensor_cores = 0;
+    if (!src0 || !src0->data || !x || !ids || !dst) return fail(MOE_ERR_INVALID, "null argument");
+    if (n_tok < 1 || k < 1 || ids_stride < k) return fail(MOE_ERR_INVALID, "need n_tok >= 1, k >= 1, ids_stride >= k");
+    if (!type_supported(src0->type)) return fail(MOE_ERR_UNSUPPORTED, "unsupported expert type %d", src0->type);
+    if (!contiguous(src0) || !aligned16(src0->data))
+        return fail(MOE_ERR_UNSUPPORTED, "expert tensor must be contiguous and 16-byte aligned");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t K = src0->ne[0], rows = src0->ne[1], E = src0->ne[2];
+    const bool tc = src0->type == MOE_TYPE_Q2_K && K % 256 == 0 && rows % moe::MMQ_M == 0 &&
+                    static_cast<uint64_t>(moe::MMQ_M) * src0->nb[1] <= moe::MMQ_MAX_PACKED && ptr_kind(src0->data) == 2 &&
+                    (src0->nb[2] % 16) == 0 && n_tok * k < (int64_t{1} << 30);
+    if (!tc) {
+        // no tensor-core path: the decode GEMV over chunks of 8 tokens
+        for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
+            const int64_t nt = n_tok - t0 < 8 ? n_tok - t0 : 8;
+            MmvqCall c;
+            c.src0 = src0;
+            c.src1 = x + t0 * K;
+            c.src1_type = MOE_TYPE_F32;
+            c.ids = ids + t0 * ids_stride;
+            c.dst = dst + t0 * k * rows;
+            c.ne00 = K; c.ne01 = rows; c.ncols_dst = nt; c.s01 = static_cast<int64_t>(src0->nb[1]) / type_size(src0->type);
+            c.nchannels_y = 1; c.nchannels_dst = k;
+            c.stride_col_y = K; c.stride_channel_y = 0;
+            c.stride_col_dst = k * rows; c.stride_channel_dst = rows;
+            c.ids_stride = ids_stride;
+            const int rc = run_mmvq(c, st);
+            if (rc) return rc;
+        }
+        return MOE_OK;
+    }
+    const PrefillWs w = prefill_ws(src0, n_tok, k, static_cast<char *>(workspace));
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
+    int rc = init_device_globals();
+    if (rc) return rc;
+    CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, n_tok, K, st));
+    CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
+                             static_cast<int>(rows / moe::MMQ_M), w.cnt, w.offsets, w.cursor, w.entries, w.tile_off,
+                             g.d_err, st));
+    moe::MmqArgs a{};
+    a.dense = static_cast<const char *>(src0->data);
+    a.expert_bytes = src0->nb[2];
+    a.n_experts = static_cast<int32_t>(E);
+    a.K = static_cast<int32_t>(K);
+    a.nrows = static_cast<int32_t>(rows);
+    a.row_bytes = static_cast<uint32_t>(src0->nb[1]);
+    a.x8 = w.x8;
+    a.n_tok = static_cast<int32_t>(n_tok);
+    a.k = static_cast<int32_t>(k);
+    a.offsets = w.offsets;
+    a.entries = w.entries;
+    a.tile_off = w.tile_off;
+    a.dst = dst;
+    a.err = g.d_err;
+    const char *why = "";
+    cudaError_t ce = cudaSuccess;
+    rc = moe::launch_mmq(src0->type, a, st, &why, &ce);
+    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+    if (rc) return fail(rc, "%s", why);
+    if (used_tensor_cores) *used_tensor_cores = 1;
     return MOE_OK;
 }
 

@@ -173,6 +173,26 @@ def topk_softmax(logits, k, norm_w=False, stream=None):
     return ids, w
 
 
+def prefill_mul_mat_id(src0, x, ids, dst=None, workspace=None, stream=None):
+    """Prefill MUL_MAT_ID (moe_b200_prefill_mul_mat_id): x f32 [n_tok, K] and
+    ids i32 [n_tok, k] on the device -> dst f32 [n_tok, k, rows], llama.cpp CPU
+    semantics. Returns (dst, used_tensor_cores)."""
+    assert x.dtype == torch.float32 and x.is_cuda and x.is_contiguous() and ids.dtype == torch.int32
+    n_tok, K = x.shape
+    k = ids.shape[1]
+    rows = src0.ne[1]
+    if dst is None:
+        dst = torch.empty((n_tok, k, rows), dtype=torch.float32, device=x.device)
+    need = lib().moe_b200_prefill_workspace_size(ctypes.byref(src0), n_tok, k)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    used = ctypes.c_int32(0)
+    check(lib().moe_b200_prefill_mul_mat_id(ctypes.byref(src0), _ptr(x), n_tok, _ptr(ids), k, ids.stride(0),
+                                            _ptr(dst), _ptr(workspace), workspace.numel(), ctypes.byref(used),
+                                            _stream(stream)))
+    return dst, bool(used.value)
+
+
 def set_layer_fused(enable):
     """Enable (default) or disable the one-kernel layer decode (moe_b200_layer_set_fused)."""
     check(lib().moe_b200_layer_set_fused(1 if enable else 0))
@@ -184,4 +204,4 @@ def fill_quantized(ggml_type, dst, n_rows, n_cols, seed, sigma=0.02, stream=None
 
 __all__ = ["MoeError", "MoeTensor", "enabled", "wants", "active", "pin_host", "step", "mul_mat_vec_q",
            "fusion_device", "expert_tensor", "configure", "reset", "stats", "table", "device_error",
-           "quantize_act", "topk_softmax", "fill_quantized"]
+           "quantize_act", "topk_softmax", "fill_quantized", "prefill_mul_mat_id"]

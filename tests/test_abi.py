@@ -52,3 +52,6 @@ def test_errors_are_status_codes_not_aborts(pkg):
     assert b"act_type" in L.moe_b200_last_error()
     rc = L.moe_b200_topk_softmax(None, 1, 4, 8, 0, None, None, None)
     assert rc == pkg._lib.MOE_ERR_INVALID
+    rc = L.moe_b200_prefill_mul_mat_id(None, None, 1, None, 8, 8, None, None, 0, None, None)
+    assert rc == pkg._lib.MOE_ERR_INVALID
+    assert L.moe_b200_prefill_workspace_size(None, 1, 8) == 0

@@ -1,0 +1,99 @@
+"""Prefill MUL_MAT_ID (moe_b200_prefill_mul_mat_id) against the oracle's
+llama.cpp CPU MUL_MAT_ID (Q8_K activations).
+
+Q2_K on the tensor-core path computes each super-block's integer dot exactly
+and finishes it with llama.cpp's own float steps in the same order, so the
+result is compared bit for bit. Types without a tensor-core path run the
+decode GEMV (in-kernel Q8_K): max |gpu - ref| / max |ref| <= 1e-4 per output
+vector (float summation order only)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from moe_data import activations, experts, rel_err, zipf_logits
+
+pytestmark = pytest.mark.gpu
+
+TIGHT = 1e-4
+
+
+def _zipf_ids(n_tok, E, k, seed):
+    """top-k of Zipf-skewed logits: distinct experts per token, a few hot experts"""
+    lg = zipf_logits(n_tok, E, seed)
+    return np.argsort(-lg, axis=1, kind="stable")[:, :k].astype(np.int32)
+
+
+def _run(pkg, cuda, t, W, K, rows, x, ids):
+    mc = pkg.moe_cache
+    Wd = torch.from_numpy(W).to(cuda)
+    src0 = mc.expert_tensor(Wd, t, K, rows, name="w")
+    dst, tc = mc.prefill_mul_mat_id(src0, torch.from_numpy(x).to(cuda), torch.from_numpy(ids).to(cuda))
+    torch.cuda.synchronize()
+    assert mc.device_error() == 0
+    return dst.cpu().numpy(), tc
+
+
+@pytest.mark.parametrize("K,rows,E,k,n_tok,seed", [
+    (256, 128, 4, 1, 1, 1),          # one super-block, one token: a tile of 1 of 32 token slots
+    (768, 256, 8, 2, 100, 2),        # odd super-block count, ragged token chunks
+    (1024, 384, 16, 4, 33, 3),       # 33 tokens: chunks of 32 + 1 on the hot experts
+    (3072, 768, 32, 8, 64, 4),       # config-2 gate/up shape (1008-byte rows: the widest packed tile)
+    (768, 3072, 32, 8, 48, 5),       # config-2 down shape (24 row blocks)
+])
+def test_prefill_q2k_tensor_cores_bit_exact(pkg, cuda, K, rows, E, k, n_tok, seed):
+    W = experts(O.Q2_K, E, rows, K, seed)
+    x = activations((n_tok, K), seed + 10)
+    ids = _zipf_ids(n_tok, E, k, seed + 20)
+    got, tc = _run(pkg, cuda, O.Q2_K, W, K, rows, x, ids)
+    assert tc
+    ref = O.mul_mat_id(O.Q2_K, W, K, x[:, None, :], ids)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_prefill_q2k_all_tokens_one_expert(pkg, cuda):
+    """every pick on one expert (many chunks of one expert), others idle"""
+    K, rows, E, k, n_tok = 512, 256, 8, 1, 200
+    W = experts(O.Q2_K, E, rows, K, 7)
+    x = activations((n_tok, K), 8)
+    ids = np.full((n_tok, k), 5, dtype=np.int32)
+    got, tc = _run(pkg, cuda, O.Q2_K, W, K, rows, x, ids)
+    assert tc
+    np.testing.assert_array_equal(got, O.mul_mat_id(O.Q2_K, W, K, x[:, None, :], ids))
+
+
+def test_prefill_q2k_repeat_same_result(pkg, cuda):
+    """entry order inside an expert comes from atomics; results must not depend on it"""
+    K, rows, E, k, n_tok = 512, 128, 4, 4, 96
+    W = experts(O.Q2_K, E, rows, K, 9)
+    x = activations((n_tok, K), 10)
+    ids = _zipf_ids(n_tok, E, k, 11)
+    a, _ = _run(pkg, cuda, O.Q2_K, W, K, rows, x, ids)
+    b, _ = _run(pkg, cuda, O.Q2_K, W, K, rows, x, ids)
+    np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("t,K,rows", [(O.Q4_K, 512, 256), (O.Q6_K, 256, 128), (O.Q4_0, 256, 96),
+                                      (O.Q2_K, 256, 192)])   # rows not a multiple of 128
+def test_prefill_fallback_gemv(pkg, cuda, t, K, rows):
+    E, k, n_tok = 8, 2, 19
+    W = experts(t, E, rows, K, 12)
+    x = activations((n_tok, K), 13)
+    ids = _zipf_ids(n_tok, E, k, 14)
+    got, tc = _run(pkg, cuda, t, W, K, rows, x, ids)
+    assert not tc
+    assert rel_err(got, O.mul_mat_id(t, W, K, x[:, None, :], ids)) <= TIGHT
+
+
+def test_prefill_bad_id_reported(pkg, cuda):
+    """an out-of-range expert id is skipped and reported as a device error"""
+    K, rows, E, k, n_tok = 256, 128, 4, 2, 8
+    W = experts(O.Q2_K, E, rows, K, 15)
+    x = activations((n_tok, K), 16)
+    ids = _zipf_ids(n_tok, E, k, 17)
+    ids[3, 1] = E + 7
+    mc = pkg.moe_cache
+    src0 = mc.expert_tensor(torch.from_numpy(W).to(cuda), O.Q2_K, K, rows)
+    mc.prefill_mul_mat_id(src0, torch.from_numpy(x).to(cuda), torch.from_numpy(ids).to(cuda))
+    torch.cuda.synchronize()
+    assert mc.device_error() != 0
