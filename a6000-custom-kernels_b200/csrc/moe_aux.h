@@ -44,6 +44,12 @@ int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why
 cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int row_blocks,
                              int32_t *cnt, int32_t *offsets, int32_t *cursor, int32_t *entries, int32_t *tile_off,
                              int *err, cudaStream_t st);
+// launch_mmq_gather writes the chunks' B tiles (MMQ layout) from Q8_K rows;
+// max_chunks bounds the chunk count (mmq_max_chunks).
+cudaError_t launch_mmq_gather(const uint8_t *x8, int nsb, int E, int row_blocks, int k, const int32_t *offsets,
+                              const int32_t *entries, const int32_t *tile_off, int64_t max_chunks, uint8_t *btiles,
+                              cudaStream_t st);
+bool mmq_supported(int type, int64_t K, int64_t nrows);
 int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
 
 }  // namespace moe

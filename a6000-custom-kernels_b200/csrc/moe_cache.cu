@@ -753,8 +753,9 @@ bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
 
 // Prefill workspace: the tokens' Q8_K blocks, then the grouping arrays
 struct PrefillWs {
-    uint8_t *x8;
+    uint8_t *x8, *btiles;
     int32_t *cnt, *offsets, *cursor, *entries, *tile_off;
+    int64_t max_chunks;
     size_t bytes;
 };
 
@@ -769,6 +770,8 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, char *bas
     w.cursor = reinterpret_cast<int32_t *>(take(4 * E));
     w.entries = reinterpret_cast<int32_t *>(take(4 * n_tok * k));
     w.tile_off = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
+    w.max_chunks = moe::mmq_max_chunks(n_tok * k, E);
+    w.btiles = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(w.max_chunks) * (K / 256) * moe::MMQ_BT_BYTES));
     w.bytes = off;
     return w;
 }
@@ -1157,8 +1160,7 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
         return fail(MOE_ERR_UNSUPPORTED, "expert tensor must be contiguous and 16-byte aligned");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int64_t K = src0->ne[0], rows = src0->ne[1], E = src0->ne[2];
-    const bool tc = src0->type == MOE_TYPE_Q2_K && K % 256 == 0 && rows % moe::MMQ_M == 0 &&
-                    static_cast<uint64_t>(moe::MMQ_M) * src0->nb[1] <= moe::MMQ_MAX_PACKED && ptr_kind(src0->data) == 2 &&
+    const bool tc = moe::mmq_supported(src0->type, K, rows) && ptr_kind(src0->data) == 2 &&
                     (src0->nb[2] % 16) == 0 && n_tok * k < (int64_t{1} << 30);
     if (!tc) {
         // no tensor-core path: the decode GEMV over chunks of 8 tokens
@@ -1189,6 +1191,8 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
     CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
                              static_cast<int>(rows / moe::MMQ_M), w.cnt, w.offsets, w.cursor, w.entries, w.tile_off,
                              g.d_err, st));
+    CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K / 256), static_cast<int>(E), static_cast<int>(rows / moe::MMQ_M),
+                              static_cast<int>(k), w.offsets, w.entries, w.tile_off, w.max_chunks, w.btiles, st));
     moe::MmqArgs a{};
     a.dense = static_cast<const char *>(src0->data);
     a.expert_bytes = src0->nb[2];
@@ -1196,7 +1200,7 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
     a.K = static_cast<int32_t>(K);
     a.nrows = static_cast<int32_t>(rows);
     a.row_bytes = static_cast<uint32_t>(src0->nb[1]);
-    a.x8 = w.x8;
+    a.btiles = w.btiles;
     a.n_tok = static_cast<int32_t>(n_tok);
     a.k = static_cast<int32_t>(k);
     a.offsets = w.offsets;
