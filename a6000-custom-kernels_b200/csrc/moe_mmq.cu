@@ -154,41 +154,63 @@ __global__ void __launch_bounds__(256) mmq_gather_q8K_kernel(const uint8_t *__re
 template <int TYPE>
 struct MmqType;
 template <> struct MmqType<T_Q2_K> {
-    static constexpr int BPB = 84;       // bytes per super-block
-    static constexpr int NPLANE = 1;     // int8 planes of the folded weights
-    static constexpr bool MINS = true;   // has the dmin * summs term
+    static constexpr int BPB = 84;          // bytes per super-block
+    static constexpr int NPLANE = 1;        // int8 planes of the folded weights
+    static constexpr bool MINS = true;      // has the dmin * summs term
+    static constexpr bool A_SIGNED = false; // folded weights sc * q in [0, 45]
 };
 
-// Shared-memory layout of one CTA for weight type TYPE
+// Shared-memory and TMEM layout of one CTA for weight type TYPE. TMEM
+// columns: accumulator set s at s * 128 (isum planes from 0, summs at
+// SUMMS_COL), A buffer b at 256 + b * 128 (quant planes: 64 columns each,
+// then the mins: 8 columns).
 template <int TYPE>
 struct MmqLayout {
     using Ty = MmqType<TYPE>;
     static constexpr uint32_t SLOT = (Ty::BPB + 15) / 16 * 16 + 16;     // one row's window of one super-block
-    static constexpr uint32_t CTRL = 2048;
-    static constexpr uint32_t PLANE = MMQ_M * 256;                       // one int8 plane of A (32 KB)
-    static constexpr uint32_t MINS_OFF = Ty::NPLANE * PLANE;             // chunks (mins, zero, mins)
-    static constexpr uint32_t A_BYTES = MINS_OFF + (Ty::MINS ? 3 * (MMQ_M / 8) * 128 : 0);
-    static constexpr int NA = (2 * A_BYTES <= 96u * 1024u) ? 2 : 1;     // A buffers
+    static constexpr uint32_t CTRL = 8192;
     static constexpr int NB = 4;                                         // B-tile stages
-    static constexpr uint32_t OFF_A = CTRL;
-    static constexpr uint32_t OFF_B = OFF_A + NA * A_BYTES;
+    static constexpr uint32_t OFF_B = CTRL;
     static constexpr uint32_t OFF_P = (OFF_B + NB * MMQ_BT_BYTES + 127) / 128 * 128;
     static constexpr uint32_t STAGE = MMQ_M * SLOT;
     static constexpr int NP_FIT = static_cast<int>((227u * 1024u - OFF_P) / STAGE);
     static constexpr int NP = NP_FIT > 8 ? 8 : NP_FIT;                   // weight stages
     static constexpr uint32_t TOTAL = OFF_P + NP * STAGE;
-    static constexpr uint32_t ACC_COLS = 256;                            // TMEM columns per accumulator set
+    static constexpr uint32_t ACC_COLS = 128;                            // TMEM columns per accumulator set
+    static constexpr uint32_t SUMMS_COL = Ty::NPLANE * MMQ_NT;           // summs plane within a set
+    static constexpr uint32_t A_COL0 = 2 * ACC_COLS;                     // first A buffer
+    static constexpr uint32_t A_COLS = 128;                              // TMEM columns per A buffer
+    static constexpr uint32_t MINS_COL = Ty::NPLANE * 64;                // mins within an A buffer
     static_assert(NP >= 2, "at least two weight stages");
     static_assert(TOTAL <= 227u * 1024u, "shared memory budget");
-    static_assert(Ty::NPLANE * MMQ_NT + (Ty::MINS ? 2 * MMQ_NT : 0) <= ACC_COLS, "TMEM columns");
+    static_assert(SUMMS_COL + (Ty::MINS ? MMQ_NT : 0) <= ACC_COLS, "TMEM accumulator columns");
+    static_assert(MINS_COL + (Ty::MINS ? 8 : 0) <= A_COLS && A_COL0 + 2 * A_COLS <= 512, "TMEM A columns");
     static_assert(SLOT % 16 == 0 && SLOT <= 256, "TMA box width");
 };
 
+// Warp roles: warps 0-7 finish the accumulators (warp w reads TMEM lanes
+// 32 (w % 4) .. + 31, i.e. those weight rows, for token slices w / 4, w / 4 + 2),
+// warps 8-15 unpack the weights (warp 8 + i: rows 32 (i % 4) + lane, elements
+// 128 (i / 4) .. + 127 of each super-block), warp 16 loads, warps 17 and 18
+// issue the MMAs of the even and the odd steps (an MMA instruction holds its
+// issuing thread for ~100 cycles whatever N; two issuers overlap).
+constexpr int MMQ_EPI_WARPS = 8;
+constexpr int MMQ_UNP_WARPS = 8;
+constexpr int MMQ_PROD_WARP = MMQ_EPI_WARPS + MMQ_UNP_WARPS;
+constexpr int MMQ_MMA_WARP = MMQ_PROD_WARP + 1;   // and MMQ_MMA_WARP + 1
+constexpr int MMQ_WS_THREADS = 32 * (MMQ_MMA_WARP + 2);
+constexpr int MMQ_RING = 4;   // steps of row scales and token scales kept for the epilogue
+
 struct MmqCtrl {   // fits MmqLayout::CTRL (static_assert in the kernel)
-    uint64_t p_full[8], p_empty[8], b_full[4], b_empty[4], mma[2];
+    uint64_t p_full[8], p_empty[8], b_full[4], b_empty[4];
+    uint64_t mma_done[2];      // step g's MMAs complete (accumulator set g & 1 full, A buffer g & 1 free)
+    uint64_t acc_empty[2];     // the epilogue has read accumulator set g & 1
+    uint64_t a_ready[2];       // step g's A buffer g & 1 unpacked
+    uint64_t s_full[MMQ_RING]; // step g's row and token scales written
     uint32_t tmem;
-    int32_t tok[3][MMQ_NT];    // entries of the CTA's last three tiles
-    float da[3][MMQ_NT];       // the tokens' block scales of the last three steps
+    int32_t abort;             // a wait timed out somewhere: every role stops
+    alignas(16) float da[MMQ_RING][MMQ_NT];
+    float2 rs[MMQ_RING][MMQ_M];
 };
 
 struct MmqTile {
@@ -223,62 +245,68 @@ __device__ __forceinline__ uint64_t l2_evict_last_policy() {
     return p;
 }
 
-// AND of v over the consumer warps (named barrier 1)
-__device__ __forceinline__ bool mmq_consumer_and(bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.and.pred q, 1, %2, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"(v ? 1u : 0u), "n"(MMQ_CWARPS * 32)
-        : "memory");
-    return r != 0;
+// Bounded wait that also gives up once another role has aborted; a timeout
+// aborts the block.
+__device__ __forceinline__ bool mmq_wait(MmqCtrl &C, uint64_t *bar, uint32_t parity, const MmqArgs &a) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 2000u)) return true;
+        if (*reinterpret_cast<volatile int32_t *>(&C.abort)) return false;
+        if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+            *reinterpret_cast<volatile int32_t *>(&C.abort) = 1;
+            set_error(a.err, DERR_TIMEOUT_FULL);
+            return false;
+        }
+    }
 }
 
-// Q2_K super-block (84 bytes at blk) of row r -> 256 folded int8 (sc * q,
-// element 16 kb + i in chunk kb) and the 16 mins (m_g = sc_g >> 4) twice,
-// in the K-major layout of A; the row's d and dmin.
-__device__ __forceinline__ void unpack_q2K(const uint8_t *blk, uint8_t *A, int r, float &d, float &dm) {
-    uint32_t sc4[4], qs[16];
+// Half h of a Q2_K super-block (84 bytes at blk) of this thread's row:
+// elements 128 h .. 128 h + 127 as folded int8 (sc * q) into A columns
+// 32 h .. 32 h + 31 of the thread's TMEM lane at a_cols (element k in byte
+// k % 4 of column k / 4); half 0 also writes the 16 mins as (16 m_g, m_g)
+// into the 8 mins columns and returns the row's d and dmin.
+__device__ __forceinline__ void unpack_q2K(const uint8_t *blk, uint32_t a_cols, int h, float &d, float &dm) {
+    uint32_t sc4[4], qs[8], v[32];
 #pragma unroll
     for (int i = 0; i < 4; ++i) sc4[i] = ld_u32(blk + 4 * i);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) qs[i] = ld_u32(blk + 16 + 4 * i);
-    uint8_t *rowp = A + (r >> 3) * 128 + (r & 7) * 16;
+    for (int i = 0; i < 8; ++i) qs[i] = ld_u32(blk + 16 + 32 * h + 4 * i);
 #pragma unroll
-    for (int kb = 0; kb < 16; ++kb) {
-        // elements 16 kb .. 16 kb + 15: half n = kb / 8, plane = (kb % 8) / 2,
-        // bytes 16 (kb % 2) .. + 15 of the half's 32 quant bytes; one scale
-        const int n = kb >> 3, plane = (kb & 7) >> 1, hb = kb & 1;
+    for (int c = 0; c < 8; ++c) {
+        // elements 16 kb .. 16 kb + 15 (kb = 8 h + c): plane c / 2 of quant
+        // bytes 16 (c % 2) .. + 15 of the half's 32 bytes; one scale
+        const int kb = 8 * h + c, plane = c >> 1, hb = c & 1;
         const uint32_t sc = (sc4[kb >> 2] >> (8 * (kb & 3))) & 0xFu;
-        uint4 v;
-        v.x = ((qs[8 * n + 4 * hb + 0] >> (2 * plane)) & 0x03030303u) * sc;
-        v.y = ((qs[8 * n + 4 * hb + 1] >> (2 * plane)) & 0x03030303u) * sc;
-        v.z = ((qs[8 * n + 4 * hb + 2] >> (2 * plane)) & 0x03030303u) * sc;
-        v.w = ((qs[8 * n + 4 * hb + 3] >> (2 * plane)) & 0x03030303u) * sc;
-        *reinterpret_cast<uint4 *>(rowp + kb * (MMQ_M / 8) * 128) = v;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[4 * c + i] = ((qs[4 * hb + i] >> (2 * plane)) & 0x03030303u) * sc;
     }
-    const uint4 m = make_uint4((sc4[0] >> 4) & 0x0F0F0F0Fu, (sc4[1] >> 4) & 0x0F0F0F0Fu, (sc4[2] >> 4) & 0x0F0F0F0Fu,
-                               (sc4[3] >> 4) & 0x0F0F0F0Fu);
-    constexpr uint32_t MO = MmqLayout<T_Q2_K>::MINS_OFF;
-    *reinterpret_cast<uint4 *>(rowp + MO) = m;
-    *reinterpret_cast<uint4 *>(rowp + MO + 2 * (MMQ_M / 8) * 128) = m;
-    d = ld_half(blk + 80);
-    dm = ld_half(blk + 82);
+    tmem_st32(a_cols + 32 * h, v);
+    if (h == 0) {
+        const uint32_t m[8] = {sc4[0] & 0xF0F0F0F0u, sc4[1] & 0xF0F0F0F0u, sc4[2] & 0xF0F0F0F0u, sc4[3] & 0xF0F0F0F0u,
+                               (sc4[0] >> 4) & 0x0F0F0F0Fu, (sc4[1] >> 4) & 0x0F0F0F0Fu, (sc4[2] >> 4) & 0x0F0F0F0Fu,
+                               (sc4[3] >> 4) & 0x0F0F0F0Fu};
+        tmem_st8(a_cols + MmqLayout<T_Q2_K>::MINS_COL, m);
+        d = ld_half(blk + 80);
+        dm = ld_half(blk + 82);
+    }
+}
+
+// Instruction descriptor of kind::i8 with s32 accumulation: A unsigned or
+// signed int8, B signed int8, both K-major
+__host__ __device__ constexpr uint32_t mmq_idesc(bool a_signed, int N) {
+    return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(MMQ_M >> 4) << 24);
 }
 
 template <int TYPE>
-__global__ void __launch_bounds__(MMQ_THREADS, 1) moe_mmq_kernel(const __grid_constant__ MmqArgs a) {
+__global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid_constant__ MmqArgs a) {
     using Lay = MmqLayout<TYPE>;
     using Ty = MmqType<TYPE>;
     static_assert(sizeof(MmqCtrl) <= Lay::CTRL, "control block too large");
     constexpr int BPB = Ty::BPB;
-    constexpr uint32_t ACS = (MMQ_M / 8) * 128;    // A: byte stride of one 16-byte K chunk over the rows
     extern __shared__ __align__(1024) uint8_t smem[];
     MmqCtrl &C = *reinterpret_cast<MmqCtrl *>(smem);
-    uint8_t *A = smem + Lay::OFF_A;
     uint8_t *B = smem + Lay::OFF_B;
     uint8_t *P = smem + Lay::OFF_P;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -290,35 +318,34 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) moe_mmq_kernel(const __grid_co
     if (tid == 0) {
         for (int s = 0; s < Lay::NP; ++s) {
             mbar_init(&C.p_full[s], 1);
-            mbar_init(&C.p_empty[s], MMQ_CWARPS);
+            mbar_init(&C.p_empty[s], MMQ_UNP_WARPS);
         }
         for (int s = 0; s < Lay::NB; ++s) {
             mbar_init(&C.b_full[s], 1);
             mbar_init(&C.b_empty[s], 1);
         }
-        mbar_init(&C.mma[0], 1);
-        mbar_init(&C.mma[1], 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&C.mma_done[s], 1);
+            mbar_init(&C.acc_empty[s], MMQ_EPI_WARPS);
+            mbar_init(&C.a_ready[s], MMQ_UNP_WARPS);
+        }
+        for (int s = 0; s < MMQ_RING; ++s) mbar_init(&C.s_full[s], MMQ_UNP_WARPS);
+        C.abort = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
-        // 512 TMEM columns: two accumulator sets of ACC_COLS
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&C.tmem)),
-                     "r"(2 * Lay::ACC_COLS)
+                     "r"(512u)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    if (Ty::MINS && tid < MMQ_M) {   // the zero chunk between the two copies of the mins
-        for (int s = 0; s < Lay::NA; ++s)
-            *reinterpret_cast<uint4 *>(A + s * Lay::A_BYTES + Lay::MINS_OFF + ACS + (tid >> 3) * 128 + (tid & 7) * 16) =
-                make_uint4(0, 0, 0, 0);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = C.tmem;
 
-    if (warp == MMQ_CWARPS) {
-        // ---------------- producer warp: B tiles and weight rows -----------------
+    if (warp == MMQ_PROD_WARP) {
+        // ---------------- producer: B tiles and weight rows ----------------------
         const uint64_t pol_w = l2_evict_first_policy(), pol_b = l2_evict_last_policy();
         uint32_t ps = 0, pph = 0, bs = 0, bph = 0, fills_p = 0, fills_b = 0;
         bool pok = true;
@@ -327,7 +354,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) moe_mmq_kernel(const __grid_co
             const uint32_t bbytes = mmq_bt_bytes(mmq_chunk_n(T.nt));
             const int y0 = (T.e * a.nrows + T.rb * MMQ_M) / G;   // first tensor-map row of the tile
             for (int sb = 0; sb < nsb; ++sb) {
-                bool w = lane == 0 ? mbar_wait_bounded(&C.b_empty[bs], bph ^ 1u, a.timeout_ns) : true;
+                bool w = lane == 0 ? mmq_wait(C, &C.b_empty[bs], bph ^ 1u, a) : true;
                 if (!__shfl_sync(0xffffffffu, w, 0)) { pok = false; break; }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&C.b_full[bs], bbytes);
@@ -337,7 +364,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) moe_mmq_kernel(const __grid_co
                 ++fills_b;
                 if (++bs == Lay::NB) { bs = 0; bph ^= 1u; }
 
-                w = lane == 0 ? mbar_wait_bounded(&C.p_empty[ps], pph ^ 1u, a.timeout_ns) : true;
+                w = lane == 0 ? mmq_wait(C, &C.p_empty[ps], pph ^ 1u, a) : true;
                 if (!__shfl_sync(0xffffffffu, w, 0)) { pok = false; break; }
                 // box j: the sb windows of rows G i + j, i < GR (16-byte aligned x)
                 if (lane == 0) mbar_arrive_expect_tx(&C.p_full[ps], Lay::STAGE);
@@ -351,136 +378,149 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) moe_mmq_kernel(const __grid_co
             }
         }
         if (lane == 0) {
-            if (!pok) set_error(a.err, DERR_TIMEOUT_EMPTY);
-            // copies still in flight (only after an error): wait for every
+            // copies still in flight (only after an abort): wait for every
             // stage's last fill before the block may exit
             for (uint32_t s = 0; s < static_cast<uint32_t>(Lay::NP) && s < fills_p; ++s)
                 mbar_wait_bounded(&C.p_full[s], ((fills_p - 1 - s) / Lay::NP) & 1u, a.timeout_ns);
             for (uint32_t s = 0; s < static_cast<uint32_t>(Lay::NB) && s < fills_b; ++s)
                 mbar_wait_bounded(&C.b_full[s], ((fills_b - 1 - s) / Lay::NB) & 1u, a.timeout_ns);
         }
-    } else {
-        // ---------------- consumer warps: thread r owns weight row r ---------------
-        const int r = tid;
+    } else if (warp >= MMQ_MMA_WARP) {
+        // ---------------- MMA issuers (lane 0): steps g with g % 2 == warp parity ----
+        const uint32_t par = static_cast<uint32_t>(warp - MMQ_MMA_WARP);
+        if (lane == 0) {
+            uint32_t g = 0, last = 0;
+            bool ok = true, any = false;
+            for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x) {
+                const MmqTile T = mmq_tile(a, ti, row_blocks);
+                const int N = mmq_chunk_n(T.nt);
+                const uint32_t bcs = 16u * N;   // B: bytes of one 16-byte K chunk over the N tokens
+                const uint32_t idesc = mmq_idesc(Ty::A_SIGNED, N), idesc_m = mmq_idesc(false, N);
+                for (int sb = 0; sb < nsb; ++sb, ++g) {
+                    if ((g & 1u) != par) continue;
+                    const uint32_t bs = g % Lay::NB, bph = (g / Lay::NB) & 1u;
+                    // A buffer g & 1 unpacked, B tile landed, accumulator set
+                    // g & 1 read by step g - 2's epilogue
+                    ok = mmq_wait(C, &C.a_ready[par], (g >> 1) & 1u, a) && mmq_wait(C, &C.b_full[bs], bph, a) &&
+                         (g < 2 || mmq_wait(C, &C.acc_empty[par], ((g - 2) >> 1) & 1u, a));
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = tmem + Lay::A_COL0 + par * Lay::A_COLS;
+                    const uint32_t b0 = smem_u32(B + bs * MMQ_BT_BYTES) + MMQ_BT_HEAD;
+                    const uint32_t d0 = tmem + par * Lay::ACC_COLS;
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        umma_i8_ts(d0, a0 + 8 * kk, umma_desc(b0 + kk * 2 * bcs, bcs, 128), idesc, kk > 0 ? 1u : 0u);
+                    if (Ty::MINS)   // summs = sum_g (16 m_g) hi_g + m_g lo_g
+                        umma_i8_ts(d0 + Lay::SUMMS_COL, a0 + Lay::MINS_COL, umma_desc(b0 + 16 * bcs, bcs, 128), idesc_m, 0u);
+                    umma_commit(&C.mma_done[par]);
+                    umma_commit(&C.b_empty[bs]);
+                    last = g;
+                    any = true;
+                }
+            }
+            if (any)   // this issuer's last MMAs before TMEM is freed
+                mbar_wait_bounded(&C.mma_done[par], (last >> 1) & 1u, a.timeout_ns);
+        }
+    } else if (warp >= MMQ_EPI_WARPS) {
+        // ---------------- unpack warps -------------------------------------------
+        const int uw = warp - MMQ_EPI_WARPS;
+        const int r = 32 * (uw & 3) + lane, h = uw >> 2;   // row, half of the super-block
         // row r's window in a weight stage: box r % G, line r / G
         const uint32_t slot_off = static_cast<uint32_t>((r % G) * GR + r / G) * Lay::SLOT;
         const uint32_t row_in_group = static_cast<uint32_t>(r % G) * a.row_bytes;
-        float acc[MMQ_NT];
-#pragma unroll
-        for (int n = 0; n < MMQ_NT; ++n) acc[n] = 0.f;
         uint32_t ps = 0, pph = 0, bs = 0, bph = 0, g = 0;
-        float pd = 0.f, pdm = 0.f;                      // row scales of step g - 1
-        int p_nt = 0, p_tb = 0, p_row = 0;              // its tile
-        bool p_last = false, ok = true, mok = true;   // mok: last epilogue's MMA wait succeeded
-
-        // finish step q (accumulator set q & 1): llama.cpp's
-        // sumf += (d_a d) * isum - (d_a dmin) * summs, per token
-        auto epilogue = [&](uint32_t q) {
-            const uint32_t cols = tmem + (static_cast<uint32_t>(32 * warp) << 16) + (q & 1u) * Lay::ACC_COLS;
-            const float *dav = C.da[q % 3];
-#pragma unroll
-            for (int sl = 0; sl < MMQ_NT / 16; ++sl) {
-                if (sl * 16 < p_nt) {
-                    uint32_t S[16], H[16], L[16];
-                    tmem_ld16(cols + sl * 16, S);
-                    tmem_ld16(cols + MMQ_NT + sl * 16, H);
-                    tmem_ld16(cols + 2 * MMQ_NT + sl * 16, L);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float da = dav[sl * 16 + j];
-                        const float dall = __fmul_rn(da, pd), dmin = __fmul_rn(da, pdm);
-                        const float fi = small_int_to_float(static_cast<int>(S[j]));
-                        const float fm = small_int_to_float(16 * static_cast<int>(H[j]) + static_cast<int>(L[j]));
-                        acc[sl * 16 + j] = __fadd_rn(acc[sl * 16 + j], __fsub_rn(__fmul_rn(dall, fi), __fmul_rn(dmin, fm)));
-                    }
-                }
-            }
-        };
-        auto store = [&]() {
-            const int32_t *tk = C.tok[p_tb];
-#pragma unroll
-            for (int n = 0; n < MMQ_NT; ++n) {
-                if (n < p_nt) a.dst[static_cast<int64_t>(tk[n]) * a.nrows + p_row] = acc[n];
-                acc[n] = 0.f;
-            }
-        };
-
-        int tcount = 0;
-        for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x, ++tcount) {
-            const MmqTile T = mmq_tile(a, ti, row_blocks);
-            const int tb = tcount % 3;
-            const int N = mmq_chunk_n(T.nt);
-            if (tid < MMQ_NT) C.tok[tb][tid] = tid < T.nt ? a.entries[T.ebeg + T.chunk * MMQ_NT + tid] : -1;
-            for (int sb = 0; sb < nsb; ++sb) {
-                uint8_t *Ab = A + (g % Lay::NA) * Lay::A_BYTES;
-                bool w = mok && mbar_wait_sleep(&C.p_full[ps], pph, a.timeout_ns);
-                // A buffer g % NA was last read by step g - NA (waited for in
-                // step g - NA + 1's epilogue when NA == 2)
-                if (Lay::NA == 1 && g > 0) w &= mbar_wait_sleep(&C.mma[(g - 1) & 1u], ((g - 1) >> 1) & 1u, a.timeout_ns);
-                // ---- A: this thread's row of super-block sb
+        bool ok = true;
+        // this thread's TMEM lane (row r) in the A buffers
+        const uint32_t a_lane = tmem + (static_cast<uint32_t>(32 * (uw & 3)) << 16) + Lay::A_COL0;
+        for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x) {
+            for (int sb = 0; sb < nsb; ++sb, ++g) {
+                // weight stage landed; A buffer g & 1 last read by step g - 2's MMAs
+                ok = mmq_wait(C, &C.p_full[ps], pph, a) &&
+                     (g < 2 || mmq_wait(C, &C.mma_done[g & 1u], ((g - 2) >> 1) & 1u, a));
+                if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+                tc_fence_after();
                 const uint8_t *slot = P + ps * Lay::STAGE + slot_off + ((row_in_group + static_cast<uint32_t>(sb) * BPB) & 15u);
                 float d, dm;
-                unpack_q2K(slot, Ab, r, d, dm);
+                unpack_q2K(slot, a_lane + (g & 1u) * Lay::A_COLS, h, d, dm);
+                if (h == 0) C.rs[g % MMQ_RING][r] = make_float2(d, dm);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&C.p_empty[ps]);
                 if (++ps == Lay::NP) { ps = 0; pph ^= 1u; }
-                // ---- B: the chunk's tile of super-block sb
-                w &= mbar_wait_sleep(&C.b_full[bs], bph, a.timeout_ns);
-                const uint8_t *Bst = B + bs * MMQ_BT_BYTES;
-                if (tid < MMQ_NT) C.da[g % 3][tid] = reinterpret_cast<const float *>(Bst)[tid];
-                if (!w) set_error(a.err, DERR_TIMEOUT_FULL);
-                fence_proxy_async_smem();
-                tc_fence_before();
-                ok = mmq_consumer_and(w);
-                if (!ok) break;
-                // ---- one thread issues the step's MMAs into accumulator set g & 1
-                if (tid == 0) {
-                    tc_fence_after();
-                    const uint32_t bcs = 16u * N;   // B: byte stride of one 16-byte K chunk over the N tokens
-                    const uint32_t idesc = umma_idesc_i8(MMQ_M, N);
-                    const uint32_t a0 = smem_u32(Ab), b0 = smem_u32(Bst) + MMQ_BT_HEAD;
-                    const uint32_t d0 = tmem + (g & 1u) * Lay::ACC_COLS;
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        umma_i8(d0, umma_desc(a0 + kk * 2 * ACS, ACS, 128), umma_desc(b0 + kk * 2 * bcs, bcs, 128), idesc,
-                                kk > 0 ? 1u : 0u);
-                    if (Ty::MINS) {
-                        // H = sum_g m_g hi_g (A chunks mins, zero) and L = sum_g m_g lo_g (zero, mins)
-                        const uint64_t bd = umma_desc(b0 + 16 * bcs, bcs, 128);
-                        umma_i8(d0 + MMQ_NT, umma_desc(a0 + Lay::MINS_OFF, ACS, 128), bd, idesc, 0u);
-                        umma_i8(d0 + 2 * MMQ_NT, umma_desc(a0 + Lay::MINS_OFF + ACS, ACS, 128), bd, idesc, 0u);
-                    }
-                    umma_commit(&C.mma[g & 1u]);
-                    umma_commit(&C.b_empty[bs]);
+                if (uw < 2) {   // rows 0-63 of half 0 copy the token scales
+                    ok = mmq_wait(C, &C.b_full[bs], bph, a);
+                    if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+                    C.da[g % MMQ_RING][r] = reinterpret_cast<const float *>(B + bs * MMQ_BT_BYTES)[r];
                 }
                 if (++bs == Lay::NB) { bs = 0; bph ^= 1u; }
-                // ---- finish step g - 1 while this one multiplies
-                if (g > 0) {
-                    if (Lay::NA == 2) mok = mbar_wait_sleep(&C.mma[(g - 1) & 1u], ((g - 1) >> 1) & 1u, a.timeout_ns);
-                    if (!mok) set_error(a.err, DERR_TIMEOUT_FULL);   // agreed on at the next step's barrier
-                    tc_fence_after();
-                    epilogue(g - 1);
-                    if (p_last) store();
-                    tc_fence_before();
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&C.a_ready[g & 1u]);
+                    mbar_arrive(&C.s_full[g % MMQ_RING]);
                 }
-                pd = d;
-                pdm = dm;
-                p_nt = T.nt;
-                p_tb = tb;
-                p_row = T.rb * MMQ_M + r;
-                p_last = sb == nsb - 1;
-                ++g;
             }
         }
-        if (g > 0) {
-            // the last step (also waited for after an error, before TMEM is freed)
-            const bool w = mbar_wait_sleep(&C.mma[(g - 1) & 1u], ((g - 1) >> 1) & 1u, a.timeout_ns);
-            if (!w) set_error(a.err, DERR_TIMEOUT_FULL);
-            if (ok && mok && w) {
+    } else {
+        // ---------------- epilogue warps -----------------------------------------
+        const int r = 32 * (warp & 3) + lane, half = warp >> 2;   // row; token slices half, half + 2
+        float acc[MMQ_NT / 2];
+#pragma unroll
+        for (int n = 0; n < MMQ_NT / 2; ++n) acc[n] = 0.f;
+        uint32_t g = 0;
+        bool ok = true;
+        for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x) {
+            const MmqTile T = mmq_tile(a, ti, row_blocks);
+            for (int sb = 0; sb < nsb; ++sb, ++g) {
+                ok = mmq_wait(C, &C.s_full[g % MMQ_RING], (g / MMQ_RING) & 1u, a) &&
+                     mmq_wait(C, &C.mma_done[g & 1u], (g >> 1) & 1u, a);
+                if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
                 tc_fence_after();
-                epilogue(g - 1);
-                store();
+                const uint32_t cols = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + (g & 1u) * Lay::ACC_COLS;
+                const float2 rs = C.rs[g % MMQ_RING][r];
+                const float *dav = C.da[g % MMQ_RING];
+                // llama.cpp's sumf += (d_a d) * isum - (d_a dmin) * summs, per token
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int sl = half + 2 * q;
+                    if (sl * 16 < T.nt) {
+                        uint32_t S[16], M[16];
+                        tmem_ld16(cols + sl * 16, S);
+                        tmem_ld16(cols + Lay::SUMMS_COL + sl * 16, M);
+                        tmem_wait_ld();
+                        float dv[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) {
+                            const float4 t4 = *reinterpret_cast<const float4 *>(dav + sl * 16 + j);
+                            dv[j] = t4.x; dv[j + 1] = t4.y; dv[j + 2] = t4.z; dv[j + 3] = t4.w;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float da = dv[j];
+                            const float dall = __fmul_rn(da, rs.x), dmin = __fmul_rn(da, rs.y);
+                            const float fi = small_int_to_float(static_cast<int>(S[j]));
+                            const float fm = small_int_to_float(static_cast<int>(M[j]));
+                            acc[q * 16 + j] = __fadd_rn(acc[q * 16 + j], __fsub_rn(__fmul_rn(dall, fi), __fmul_rn(dmin, fm)));
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&C.acc_empty[g & 1u]);
+                if (sb == nsb - 1) {
+                    const int row = T.rb * MMQ_M + r;
+                    const int32_t *ent = a.entries + T.ebeg + T.chunk * MMQ_NT;
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = (half + 2 * q) * 16 + j;
+                            if (n < T.nt) a.dst[static_cast<int64_t>(ent[n]) * a.nrows + row] = acc[q * 16 + j];
+                            acc[q * 16 + j] = 0.f;
+                        }
+                    }
+                }
             }
         }
     }
@@ -488,7 +528,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) moe_mmq_kernel(const __grid_co
     __syncthreads();
     tc_fence_after();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * Lay::ACC_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u)
                      : "memory");
 }
 
@@ -577,7 +617,7 @@ int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaErro
     }
     int n_sm = 148;
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    kern<<<n_sm, MMQ_THREADS, Lay::TOTAL, st>>>(a);
+    kern<<<n_sm, MMQ_WS_THREADS, Lay::TOTAL, st>>>(a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { *cuda_err = e; *why = "moe_mmq_kernel launch"; return -3; }
     return 0;
