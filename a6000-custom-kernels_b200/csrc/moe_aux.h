@@ -41,14 +41,15 @@ int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why
 // groups the (token, pick) entries by expert into offsets / entries and the
 // tile prefix; launch_mmq runs the int8 MMQ over that tile list (-2 with *why
 // when the type or shape has no tensor-core path, -3 with *cuda_err).
-cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int row_blocks,
-                             int32_t *cnt, int32_t *offsets, int32_t *cursor, int32_t *entries, int32_t *tile_off,
-                             int *err, cudaStream_t st);
-// launch_mmq_gather writes the chunks' B tiles (MMQ layout) from Q8_K rows;
-// max_chunks bounds the chunk count (mmq_max_chunks).
-cudaError_t launch_mmq_gather(const uint8_t *x8, int nsb, int E, int row_blocks, int k, const int32_t *offsets,
-                              const int32_t *entries, const int32_t *tile_off, int64_t max_chunks, uint8_t *btiles,
-                              cudaStream_t st);
+cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int ntc,
+                             int32_t *entries, int4 *chunks, int32_t *n_chunks, int *err, cudaStream_t st);
+// launch_mmq_gather writes the chunks' B tiles (MMQ layout) from the tokens'
+// Q8_K rows x8 [n_tok][K / 256]; max_chunks bounds the chunk count
+// (mmq_max_chunks).
+cudaError_t launch_mmq_gather(const uint8_t *x8, int K, int k, int ntc, const int32_t *entries, const int4 *chunks,
+                              const int32_t *n_chunks, int64_t max_chunks, uint8_t *btiles, cudaStream_t st);
+// tokens per chunk of the tensor-core path for a weight type (0: none)
+int mmq_chunk_tokens(int type);
 bool mmq_supported(int type, int64_t K, int64_t nrows);
 int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
 

@@ -754,7 +754,8 @@ bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
 // Prefill workspace: the tokens' Q8_K blocks, then the grouping arrays
 struct PrefillWs {
     uint8_t *x8, *btiles;
-    int32_t *cnt, *offsets, *cursor, *entries, *tile_off;
+    int32_t *entries, *n_chunks;
+    int4 *chunks;
     int64_t max_chunks;
     size_t bytes;
 };
@@ -765,12 +766,11 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, char *bas
     auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
     const int64_t E = src0->ne[2], K = src0->ne[0];
     w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(n_tok) * (K / 256) * 292));
-    w.cnt = reinterpret_cast<int32_t *>(take(4 * E));
-    w.offsets = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
-    w.cursor = reinterpret_cast<int32_t *>(take(4 * E));
     w.entries = reinterpret_cast<int32_t *>(take(4 * n_tok * k));
-    w.tile_off = reinterpret_cast<int32_t *>(take(4 * (E + 1)));
-    w.max_chunks = moe::mmq_max_chunks(n_tok * k, E);
+    const int ntc = moe::mmq_chunk_tokens(src0->type) > 0 ? moe::mmq_chunk_tokens(src0->type) : moe::MMQ_NT;
+    w.max_chunks = moe::mmq_max_chunks(n_tok * k, E, ntc);
+    w.chunks = reinterpret_cast<int4 *>(take(16 * static_cast<size_t>(w.max_chunks)));
+    w.n_chunks = reinterpret_cast<int32_t *>(take(4));
     w.btiles = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(w.max_chunks) * (K / 256) * moe::MMQ_BT_BYTES));
     w.bytes = off;
     return w;
@@ -1161,7 +1161,7 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int64_t K = src0->ne[0], rows = src0->ne[1], E = src0->ne[2];
     const bool tc = moe::mmq_supported(src0->type, K, rows) && ptr_kind(src0->data) == 2 &&
-                    (src0->nb[2] % 16) == 0 && n_tok * k < (int64_t{1} << 30);
+                    (src0->nb[2] % 16) == 0 && n_tok * k < (int64_t{1} << 30) && E <= 16384;
     if (!tc) {
         // no tensor-core path: the decode GEMV over chunks of 8 tokens
         for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
@@ -1187,12 +1187,12 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
         return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
     int rc = init_device_globals();
     if (rc) return rc;
+    const int ntc = moe::mmq_chunk_tokens(src0->type);
+    CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E), ntc,
+                             w.entries, w.chunks, w.n_chunks, g.d_err, st));
     CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, n_tok, K, st));
-    CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
-                             static_cast<int>(rows / moe::MMQ_M), w.cnt, w.offsets, w.cursor, w.entries, w.tile_off,
-                             g.d_err, st));
-    CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K / 256), static_cast<int>(E), static_cast<int>(rows / moe::MMQ_M),
-                              static_cast<int>(k), w.offsets, w.entries, w.tile_off, w.max_chunks, w.btiles, st));
+    CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), static_cast<int>(k), ntc, w.entries, w.chunks, w.n_chunks,
+                              w.max_chunks, w.btiles, st));
     moe::MmqArgs a{};
     a.dense = static_cast<const char *>(src0->data);
     a.expert_bytes = src0->nb[2];
@@ -1203,9 +1203,9 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
     a.btiles = w.btiles;
     a.n_tok = static_cast<int32_t>(n_tok);
     a.k = static_cast<int32_t>(k);
-    a.offsets = w.offsets;
     a.entries = w.entries;
-    a.tile_off = w.tile_off;
+    a.chunks = w.chunks;
+    a.n_chunks = w.n_chunks;
     a.dst = dst;
     a.err = g.d_err;
     const char *why = "";

@@ -208,6 +208,52 @@ __device__ __forceinline__ int nearest_int_dev(float prod) {
     return (__float_as_int(val) & 0x007fffff) - 0x00400000;
 }
 
+// One Q8_K block (256 values at xr) by one warp, llama.cpp's
+// quantize_row_q8_K_ref: lane l quantizes values 8 l .. 8 l + 7 into q
+// (scale -127 / (the value of largest magnitude, first index on ties), values
+// clamped to 127); returns d = 1 / iscale (0 for an all-zero block) and in s
+// the lane's 8-value sum plus its neighbour's (lane 2 g then holds bsum g).
+// (quant_q8K_vals: the same from the lane's 8 values already loaded)
+__device__ __forceinline__ float quant_q8K_vals(const float (&v)[8], int lane, int8_t (&q)[8], int &s) {
+    float amax = 0.f, mval = 0.f;
+    int midx = 1 << 30;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float ax = fabsf(v[j]);
+        if (ax > amax) { amax = ax; mval = v[j]; midx = lane * 8 + j; }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+        const float ov = __shfl_xor_sync(0xffffffffu, mval, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, midx, off);
+        if (oa > amax || (oa == amax && oi < midx)) { amax = oa; mval = ov; midx = oi; }
+    }
+    s = 0;
+    float d = 0.f;
+    if (amax != 0.f) {
+        const float iscale = -127.f / mval;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int r = nearest_int_dev(__fmul_rn(iscale, v[j]));
+            q[j] = static_cast<int8_t>(r < 127 ? r : 127);
+            s += q[j];
+        }
+        d = 1.f / iscale;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = 0;
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    return d;
+}
+__device__ __forceinline__ float quant_q8K_warp(const float *__restrict__ xr, int lane, int8_t (&q)[8], int &s) {
+    const float4 a = *reinterpret_cast<const float4 *>(xr + lane * 8);
+    const float4 b = *reinterpret_cast<const float4 *>(xr + lane * 8 + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    return quant_q8K_vals(v, lane, q, s);
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -10,39 +10,60 @@
 namespace moe {
 
 // ---------------------------------------------------------------------------
-// Grouping (one block): counts per expert, offsets, entries grouped by expert,
-// and the tile prefix tile_off[e] = sum of ceil(count / NT) * row_blocks.
-// Entry order inside an expert does not change any result.
+// Grouping (one block, counters in shared memory): the entries (tok * k +
+// pick) grouped by expert, and the chunk table: an expert's entries form
+// chunks of up to ntc, chunk c = {expert, first entry, token count}, chunks of
+// an expert consecutive, *n_chunks their count. Entry order inside an expert
+// does not change any result.
 // ---------------------------------------------------------------------------
-__global__ void mmq_group_kernel(const int32_t *__restrict__ ids, int64_t ids_stride, int n_tok, int k, int E,
-                                 int row_blocks, int32_t *cnt, int32_t *offsets, int32_t *cursor, int32_t *entries,
-                                 int32_t *tile_off, int *err) {
+constexpr int MMQ_GROUP_REG = 8;   // ids kept in registers per thread (n_tok * k <= 8192)
+
+__global__ void __launch_bounds__(1024) mmq_group_kernel(const int32_t *__restrict__ ids, int64_t ids_stride, int n_tok,
+                                                         int k, int E, int ntc, int32_t *entries, int4 *chunks,
+                                                         int32_t *n_chunks, int *err) {
+    extern __shared__ int32_t cnt[];   // [E] counts, then scatter cursors
     __shared__ int32_t warp_sum[32];
     __shared__ int32_t carry[2];
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5;
     for (int e = tid; e < E; e += nth) cnt[e] = 0;
-    __syncthreads();
-    const int N = n_tok * k;
-    for (int i = tid; i < N; i += nth) {
-        const int t = i / k, p = i % k;
-        const int x = ids[static_cast<int64_t>(t) * ids_stride + p];
-        if (x < 0 || x >= E) {
-            set_error(err, DERR_BAD_ID);
-            continue;
-        }
-        atomicAdd(&cnt[x], 1);
-    }
-    __syncthreads();
-    // two exclusive scans over the experts, nth at a time: offsets (entries)
-    // and tile_off (tiles)
     if (tid == 0) { carry[0] = 0; carry[1] = 0; }
     __syncthreads();
+    const int N = n_tok * k;
+    const bool in_regs = N <= MMQ_GROUP_REG * nth;
+    int xr[MMQ_GROUP_REG];
+    auto id_of = [&](int i) {
+        const int t = i / k, p = i - t * k;
+        return ids[static_cast<int64_t>(t) * ids_stride + p];
+    };
+#pragma unroll
+    for (int u = 0; u < MMQ_GROUP_REG; ++u) {
+        const int i = tid + u * nth;
+        xr[u] = (in_regs && i < N) ? id_of(i) : -1;
+    }
+    // warp-aggregated increments: one atomic per distinct expert in the warp
+    auto count = [&](int x, bool valid) {
+        const bool bad = valid && (x < 0 || x >= E);
+        if (bad) set_error(err, DERR_BAD_ID);
+        const bool use = valid && !bad;
+        const unsigned peers = __match_any_sync(0xffffffffu, use ? x : -1);
+        if (use && lane == __ffs(peers) - 1) atomicAdd(&cnt[x], __popc(peers));
+    };
+    if (in_regs) {
+#pragma unroll
+        for (int u = 0; u < MMQ_GROUP_REG; ++u) count(xr[u], tid + u * nth < N);
+    } else {
+        for (int i0 = 0; i0 < N; i0 += nth) count(i0 + tid < N ? id_of(i0 + tid) : -1, i0 + tid < N);
+    }
+    __syncthreads();
+    // two exclusive scans over the experts, nth at a time: first entries and
+    // first chunks; the counts become the scatter cursors
     for (int base = 0; base < E; base += nth) {
         const int e = base + tid;
         const int c = e < E ? cnt[e] : 0;
-        const int tl = e < E ? ((c + MMQ_NT - 1) / MMQ_NT) * row_blocks : 0;
+        const int nc = (c + ntc - 1) / ntc;
+        int excl_v[2];
         for (int which = 0; which < 2; ++which) {
-            const int v = which == 0 ? c : tl;
+            const int v = which == 0 ? c : nc;
             int incl = v;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
@@ -62,113 +83,147 @@ __global__ void mmq_group_kernel(const int32_t *__restrict__ ids, int64_t ids_st
                 warp_sum[lane] = wincl - ws;   // exclusive prefix of warp sums
             }
             __syncthreads();
-            const int excl = carry[which] + warp_sum[warp] + incl - v;
-            if (e < E) {
-                if (which == 0) { offsets[e] = excl; cursor[e] = excl; }
-                else tile_off[e] = excl;
-            }
+            excl_v[which] = carry[which] + warp_sum[warp] + incl - v;
             __syncthreads();
-            if (tid == nth - 1) carry[which] = excl + v;
+            if (tid == nth - 1) carry[which] = excl_v[which] + v;
             __syncthreads();
         }
+        if (e < E) {
+            cnt[e] = excl_v[0];
+            for (int q = 0; q < nc; ++q)
+                chunks[excl_v[1] + q] = make_int4(e, excl_v[0] + q * ntc, min(ntc, c - q * ntc), q);
+        }
     }
-    if (tid == 0) { offsets[E] = carry[0]; tile_off[E] = carry[1]; }
+    if (tid == 0) *n_chunks = carry[1];
     __syncthreads();
-    for (int i = tid; i < N; i += nth) {
-        const int t = i / k, p = i % k;
-        const int x = ids[static_cast<int64_t>(t) * ids_stride + p];
-        if (x < 0 || x >= E) continue;
-        entries[atomicAdd(&cursor[x], 1)] = i;
+    // warp-aggregated placement: the lowest lane of each expert's peers takes
+    // a run of slots, the peers fill it in lane order
+    auto place = [&](int i, int x, bool valid) {
+        const bool use = valid && x >= 0 && x < E;
+        const unsigned peers = __match_any_sync(0xffffffffu, use ? x : -1);
+        const int leader = __ffs(peers) - 1;
+        int base = 0;
+        if (use && lane == leader) base = atomicAdd(&cnt[x], __popc(peers));
+        base = __shfl_sync(0xffffffffu, base, leader);
+        if (use) entries[base + __popc(peers & ((1u << lane) - 1u))] = i;
+    };
+    if (in_regs) {
+#pragma unroll
+        for (int u = 0; u < MMQ_GROUP_REG; ++u) place(tid + u * nth, xr[u], tid + u * nth < N);
+    } else {
+        for (int i0 = 0; i0 < N; i0 += nth) place(i0 + tid, i0 + tid < N ? id_of(i0 + tid) : -1, i0 + tid < N);
     }
 }
 
 // ---------------------------------------------------------------------------
-// B tiles: per chunk (up to MMQ_NT entries of one expert) and super-block,
-// with N = the chunk's token count rounded up to 16: the N float block scales
-// (MMQ_BT_HEAD bytes), then the tokens' Q8_K quants in the MMA's K-major
-// layout (16-byte chunk c of token j at c * 16 N + (j / 8) * 128 + (j % 8) * 16),
-// chunk 16 = the 16 bsums' high parts (bsum >> 4, in [-127, 127]) and chunk
-// 17 = their low nibbles (bsum & 15). Token slots past the chunk's count are
-// zero.
+// B tiles: per chunk and super-block, with N = the chunk's token count
+// rounded up to 16: the head (block scales, bsum pairs; MMQ_BT_HEAD bytes), then the
+// tokens' Q8_K quants in the MMA's K-major layout (16-byte chunk c of token j
+// at c * 16 N + (j / 8) * 128 + (j % 8) * 16), chunk 16 = the 16 bsums' high
+// parts (bsum >> 4, in [-127, 127]) and chunk 17 = their low nibbles
+// (bsum & 15); the head also holds the 8 sums of bsum pairs (one per 32
+// values). Token slots past the chunk's count are zero. Copied from the
+// tokens' Q8_K rows x8 (292-byte blocks), one warp per token slot for all its
+// super-blocks.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) mmq_gather_q8K_kernel(const uint8_t *__restrict__ x8, int nsb, int E,
-                                                             int row_blocks, int k, const int32_t *__restrict__ offsets,
-                                                             const int32_t *__restrict__ entries,
-                                                             const int32_t *__restrict__ tile_off,
-                                                             uint8_t *__restrict__ btiles) {
-    const int total = tile_off[E] / row_blocks * nsb;
-    const int j = threadIdx.x >> 2, part = threadIdx.x & 3;
-    for (int w = blockIdx.x; w < total; w += gridDim.x) {
-        const int gc = w / nsb, sb = w - gc * nsb;
-        // expert of chunk gc: the last e whose tile prefix is <= gc * row_blocks
-        const int target = gc * row_blocks;
-        int lo = 0, hi = E;
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (tile_off[mid] <= target) lo = mid;
-            else hi = mid;
+constexpr int MMQ_GATHER_MAX_SB = 16;   // K <= 4096
+
+__device__ __forceinline__ void mmq_gather_slot(const uint8_t *__restrict__ x8, int nsb, int k, int ntc,
+                                                const int32_t *__restrict__ entries, const int4 *__restrict__ chunks,
+                                                uint8_t *__restrict__ btiles, int wg, int lane) {
+    const int gc = wg / ntc, j = wg - gc * ntc;   // chunk, token slot
+    const int4 ch = chunks[gc];
+    const int nt = ch.z, N = mmq_chunk_n(nt), CS = 16 * N;
+    if (j >= N) return;
+    const int t = j < nt ? entries[ch.y + j] / k : -1;
+    const uint8_t *row = x8 + static_cast<size_t>(t < 0 ? 0 : t) * nsb * 292;
+    // all super-blocks' loads first (nsb <= MMQ_GATHER_MAX_SB), then the stores
+    uint32_t w0[MMQ_GATHER_MAX_SB], w1[MMQ_GATHER_MAX_SB], hl[MMQ_GATHER_MAX_SB];
+    int bsv[MMQ_GATHER_MAX_SB];
+    float d[MMQ_GATHER_MAX_SB];
+#pragma unroll
+    for (int sb = 0; sb < MMQ_GATHER_MAX_SB; ++sb) {
+        w0[sb] = w1[sb] = hl[sb] = 0u;
+        bsv[sb] = 0;
+        d[sb] = 0.f;
+        if (sb < nsb && t >= 0) {
+            const uint8_t *blk = row + sb * 292;   // 4-byte aligned
+            // quants 8 lane .. 8 lane + 7; lane 2 g: bsum g; lane 0: the scale
+            w0[sb] = *reinterpret_cast<const uint32_t *>(blk + 4 + 8 * lane);
+            w1[sb] = *reinterpret_cast<const uint32_t *>(blk + 8 + 8 * lane);
+            const int bs = reinterpret_cast<const int16_t *>(blk + 260)[lane >> 1];
+            hl[sb] = (static_cast<uint32_t>(bs >> 4) & 0xFFu) | ((static_cast<uint32_t>(bs) & 0xFu) << 8);
+            bsv[sb] = bs;
+            if (lane == 0) d[sb] = *reinterpret_cast<const float *>(blk);
         }
-        const int chunk = gc - tile_off[lo] / row_blocks;
-        const int ebeg = offsets[lo];
-        const int nt = min(MMQ_NT, offsets[lo + 1] - ebeg - chunk * MMQ_NT);
-        const int N = mmq_chunk_n(nt), CS = 16 * N;
-        if (j >= N) continue;
-        uint8_t *bt = btiles + static_cast<size_t>(w) * MMQ_BT_BYTES;
-        uint8_t *tok = bt + MMQ_BT_HEAD + (j >> 3) * 128 + (j & 7) * 16;
-        if (j < nt) {
-            const int t = entries[ebeg + chunk * MMQ_NT + j] / k;
-            const uint8_t *q8 = x8 + (static_cast<size_t>(t) * nsb + sb) * 292;
+    }
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int kb = part * 4 + c;
-                const uint32_t *q = reinterpret_cast<const uint32_t *>(q8 + 4 + 16 * kb);
-                *reinterpret_cast<uint4 *>(tok + kb * CS) = make_uint4(q[0], q[1], q[2], q[3]);
+    for (int sb = 0; sb < MMQ_GATHER_MAX_SB; ++sb) {
+        if (sb < nsb) {
+            uint8_t *bt = btiles + (static_cast<size_t>(gc) * nsb + sb) * MMQ_BT_BYTES;
+            uint8_t *tok = bt + MMQ_BT_HEAD + (j >> 3) * 128 + (j & 7) * 16;
+            *reinterpret_cast<uint2 *>(tok + (lane >> 1) * CS + 8 * (lane & 1)) = make_uint2(w0[sb], w1[sb]);
+            if ((lane & 1) == 0) {
+                tok[16 * CS + (lane >> 1)] = static_cast<uint8_t>(hl[sb] & 0xFFu);
+                tok[17 * CS + (lane >> 1)] = static_cast<uint8_t>(hl[sb] >> 8);
             }
-            if (part < 2) {
-                uint32_t h[2] = {0u, 0u}, l[2] = {0u, 0u};
-#pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                    const int bs = reinterpret_cast<const int16_t *>(q8 + 260)[8 * part + g];
-                    h[g >> 2] |= (static_cast<uint32_t>(bs >> 4) & 0xFFu) << (8 * (g & 3));
-                    l[g >> 2] |= (static_cast<uint32_t>(bs) & 0xFu) << (8 * (g & 3));
-                }
-                *reinterpret_cast<uint2 *>(tok + 16 * CS + 8 * part) = make_uint2(h[0], h[1]);
-                *reinterpret_cast<uint2 *>(tok + 17 * CS + 8 * part) = make_uint2(l[0], l[1]);
-            }
-            if (part == 3) reinterpret_cast<float *>(bt)[j] = *reinterpret_cast<const float *>(q8);
-        } else {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4 *>(tok + (part * 4 + c) * CS) = make_uint4(0, 0, 0, 0);
-            if (part < 2) {
-                *reinterpret_cast<uint2 *>(tok + 16 * CS + 8 * part) = make_uint2(0, 0);
-                *reinterpret_cast<uint2 *>(tok + 17 * CS + 8 * part) = make_uint2(0, 0);
-            }
-            if (part == 3) reinterpret_cast<float *>(bt)[j] = 0.f;
+            if (lane == 0) reinterpret_cast<float *>(bt)[j] = d[sb];
+            // 32-value bsum pairs: lane 4 i holds bsum 2 i, lane 4 i + 2 bsum 2 i + 1
+            const int pair = bsv[sb] + __shfl_down_sync(0xffffffffu, bsv[sb], 2);
+            if ((lane & 3) == 0)
+                reinterpret_cast<int16_t *>(bt + MMQ_BT_BS2 + 16 * j)[lane >> 2] = static_cast<int16_t>(pair);
         }
     }
 }
+
+__global__ void __launch_bounds__(256) mmq_gather_q8K_kernel(const uint8_t *__restrict__ x8, int nsb, int k, int ntc,
+                                                             const int32_t *__restrict__ entries,
+                                                             const int4 *__restrict__ chunks,
+                                                             const int32_t *__restrict__ n_chunks,
+                                                             uint8_t *__restrict__ btiles) {
+    const int lane = threadIdx.x & 31;
+    const int n_items = *n_chunks * ntc;
+    for (int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wg < n_items; wg += (gridDim.x * blockDim.x) >> 5)
+        mmq_gather_slot(x8, nsb, k, ntc, entries, chunks, btiles, wg, lane);
+}
+
 
 // ---------------------------------------------------------------------------
 // The grouped GEMM
 // ---------------------------------------------------------------------------
+// Per weight type: bytes per super-block, int8 planes of the folded weights
+// (plane 0 = low byte, plane 1 = high byte of a 16-bit fold), whether plane p
+// is signed, the mins term (Q2_K on the tensor core, Q4_K with dp2a in the
+// epilogue) and the tokens per chunk (TMEM: two accumulator sets of
+// (planes + summs) x NT columns plus two A buffers of 64 columns per plane).
 template <int TYPE>
 struct MmqType;
 template <> struct MmqType<T_Q2_K> {
-    static constexpr int BPB = 84;          // bytes per super-block
-    static constexpr int NPLANE = 1;        // int8 planes of the folded weights
-    static constexpr bool MINS = true;      // has the dmin * summs term
-    static constexpr bool A_SIGNED = false; // folded weights sc * q in [0, 45]
+    static constexpr int BPB = 84, NPLANE = 1, NT = 64;
+    static constexpr bool MINS_TC = true, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = false;
+};
+template <> struct MmqType<T_Q3_K> {
+    static constexpr int BPB = 110, NPLANE = 1, NT = 64;
+    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = true, P1_SIGNED = false;
+};
+template <> struct MmqType<T_Q4_K> {
+    static constexpr int BPB = 144, NPLANE = 2, NT = 32;
+    static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false;
+};
+template <> struct MmqType<T_Q6_K> {
+    static constexpr int BPB = 210, NPLANE = 2, NT = 32;
+    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = true;
 };
 
 // Shared-memory and TMEM layout of one CTA for weight type TYPE. TMEM
-// columns: accumulator set s at s * 128 (isum planes from 0, summs at
-// SUMMS_COL), A buffer b at 256 + b * 128 (quant planes: 64 columns each,
-// then the mins: 8 columns).
+// columns: accumulator set s at s * ACC_COLS (plane p at p * NT, summs after
+// the planes), A buffer b at A_COL0 + b * A_COLS (plane p: 64 columns at
+// p * 64, then the Q2_K mins: 8 columns).
 template <int TYPE>
 struct MmqLayout {
     using Ty = MmqType<TYPE>;
     static constexpr uint32_t SLOT = (Ty::BPB + 15) / 16 * 16 + 16;     // one row's window of one super-block
-    static constexpr uint32_t CTRL = 8192;
+    static constexpr uint32_t CTRL = 16384;
     static constexpr int NB = 4;                                         // B-tile stages
     static constexpr uint32_t OFF_B = CTRL;
     static constexpr uint32_t OFF_P = (OFF_B + NB * MMQ_BT_BYTES + 127) / 128 * 128;
@@ -176,30 +231,31 @@ struct MmqLayout {
     static constexpr int NP_FIT = static_cast<int>((227u * 1024u - OFF_P) / STAGE);
     static constexpr int NP = NP_FIT > 8 ? 8 : NP_FIT;                   // weight stages
     static constexpr uint32_t TOTAL = OFF_P + NP * STAGE;
-    static constexpr uint32_t ACC_COLS = 128;                            // TMEM columns per accumulator set
-    static constexpr uint32_t SUMMS_COL = Ty::NPLANE * MMQ_NT;           // summs plane within a set
-    static constexpr uint32_t A_COL0 = 2 * ACC_COLS;                     // first A buffer
-    static constexpr uint32_t A_COLS = 128;                              // TMEM columns per A buffer
-    static constexpr uint32_t MINS_COL = Ty::NPLANE * 64;                // mins within an A buffer
+    static constexpr uint32_t SUMMS_COL = Ty::NPLANE * Ty::NT;           // summs plane within a set
+    static constexpr uint32_t ACC_COLS = SUMMS_COL + (Ty::MINS_TC ? Ty::NT : 0);
+    static constexpr uint32_t A_COL0 = 2 * ACC_COLS;
+    static constexpr uint32_t MINS_COL = Ty::NPLANE * 64;                // Q2_K mins within an A buffer
+    static constexpr uint32_t A_COLS = MINS_COL + (Ty::MINS_TC ? 8 : 0);
     static_assert(NP >= 2, "at least two weight stages");
     static_assert(TOTAL <= 227u * 1024u, "shared memory budget");
-    static_assert(SUMMS_COL + (Ty::MINS ? MMQ_NT : 0) <= ACC_COLS, "TMEM accumulator columns");
-    static_assert(MINS_COL + (Ty::MINS ? 8 : 0) <= A_COLS && A_COL0 + 2 * A_COLS <= 512, "TMEM A columns");
+    static_assert(A_COL0 + 2 * A_COLS <= 512, "TMEM columns");
     static_assert(SLOT % 16 == 0 && SLOT <= 256, "TMA box width");
+    static_assert(Ty::NT == 32 || Ty::NT == 64, "chunk width");
 };
 
 // Warp roles: warps 0-7 finish the accumulators (warp w reads TMEM lanes
-// 32 (w % 4) .. + 31, i.e. those weight rows, for token slices w / 4, w / 4 + 2),
-// warps 8-15 unpack the weights (warp 8 + i: rows 32 (i % 4) + lane, elements
-// 128 (i / 4) .. + 127 of each super-block), warp 16 loads, warps 17 and 18
-// issue the MMAs of the even and the odd steps (an MMA instruction holds its
-// issuing thread for ~100 cycles whatever N; two issuers overlap).
+// 32 (w % 4) .. + 31, i.e. those weight rows, for the 16-token slices
+// w / 4, w / 4 + 2), warps 8-15 unpack the weights (warp 8 + i: rows
+// 32 (i % 4) + lane, elements 128 (i / 4) .. + 127 of each super-block),
+// warp 16 loads, warps 17 and 18 issue the MMAs of the even and the odd steps
+// (an MMA instruction holds its issuing thread for ~100 cycles whatever N; two
+// issuers overlap).
 constexpr int MMQ_EPI_WARPS = 8;
 constexpr int MMQ_UNP_WARPS = 8;
 constexpr int MMQ_PROD_WARP = MMQ_EPI_WARPS + MMQ_UNP_WARPS;
 constexpr int MMQ_MMA_WARP = MMQ_PROD_WARP + 1;   // and MMQ_MMA_WARP + 1
 constexpr int MMQ_WS_THREADS = 32 * (MMQ_MMA_WARP + 2);
-constexpr int MMQ_RING = 4;   // steps of row scales and token scales kept for the epilogue
+constexpr int MMQ_RING = 4;   // steps of row and token scales kept for the epilogue
 
 struct MmqCtrl {   // fits MmqLayout::CTRL (static_assert in the kernel)
     uint64_t p_full[8], p_empty[8], b_full[4], b_empty[4];
@@ -210,32 +266,24 @@ struct MmqCtrl {   // fits MmqLayout::CTRL (static_assert in the kernel)
     uint32_t tmem;
     int32_t abort;             // a wait timed out somewhere: every role stops
     alignas(16) float da[MMQ_RING][MMQ_NT];
-    float2 rs[MMQ_RING][MMQ_M];
+    alignas(16) int16_t bs2[MMQ_RING][MMQ_NT][8];   // Q4_K: the tokens' 32-value bsum pairs
+    float2 rs[MMQ_RING][MMQ_M];                      // the rows' d, dmin
+    uint2 rm[MMQ_RING][MMQ_M];                       // Q4_K: the rows' 8 mins (bytes)
 };
 
 struct MmqTile {
-    int e, rb, chunk, gchunk, ebeg, nt;
+    int e, rb, gchunk, first, nt;
 };
 
-// Tile ti: expert (binary search of the tile prefix), row block, chunk of
-// that expert, chunk index over all experts, first entry, token count.
-// Consecutive tiles share the chunk and walk the row blocks.
-__device__ __forceinline__ MmqTile mmq_tile(const MmqArgs &a, int ti, int row_blocks) {
-    int lo = 0, hi = a.n_experts;
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (a.tile_off[mid] <= ti) lo = mid;
-        else hi = mid;
-    }
+// Tile ti = chunk ti / row_blocks, row block ti % row_blocks: consecutive
+// tiles share the chunk and walk the row blocks.
+__device__ __forceinline__ MmqTile mmq_tile(const int4 ch, int ti, int row_blocks) {
     MmqTile T;
-    T.e = lo;
-    const int t0 = a.tile_off[lo];
-    const int local = ti - t0;
-    T.rb = local % row_blocks;
-    T.chunk = local / row_blocks;
-    T.gchunk = t0 / row_blocks + T.chunk;
-    T.ebeg = a.offsets[lo];
-    T.nt = min(MMQ_NT, a.offsets[lo + 1] - T.ebeg - T.chunk * MMQ_NT);
+    T.gchunk = ti / row_blocks;
+    T.rb = ti - T.gchunk * row_blocks;
+    T.e = ch.x;
+    T.first = ch.y;
+    T.nt = ch.z;
     return T;
 }
 
@@ -261,35 +309,185 @@ __device__ __forceinline__ bool mmq_wait(MmqCtrl &C, uint64_t *bar, uint32_t par
     }
 }
 
-// Half h of a Q2_K super-block (84 bytes at blk) of this thread's row:
-// elements 128 h .. 128 h + 127 as folded int8 (sc * q) into A columns
-// 32 h .. 32 h + 31 of the thread's TMEM lane at a_cols (element k in byte
-// k % 4 of column k / 4); half 0 also writes the 16 mins as (16 m_g, m_g)
-// into the 8 mins columns and returns the row's d and dmin.
-__device__ __forceinline__ void unpack_q2K(const uint8_t *blk, uint32_t a_cols, int h, float &d, float &dm) {
-    uint32_t sc4[4], qs[8], v[32];
+// ---- unpacking: half h (elements 128 h .. + 127) of one row's super-block
+// into the A planes in TMEM (element k of plane p in byte k % 4 of column
+// p * 64 + k / 4 of the thread's lane); half 0 also returns the row's scales.
+// A word holds 4 consecutive elements; the 16-bit-lane helpers below fold a
+// per-chunk scale into 4 elements at once: ev/od hold elements (0, 2) and
+// (1, 3) in 16-bit lanes, sc * lanes + bias stays inside each lane.
+struct RowScales {
+    float d, dm;
+    uint2 m;   // Q4_K mins
+};
+
+__device__ __forceinline__ uint32_t lo_bytes(uint32_t ev, uint32_t od) { return __byte_perm(ev, od, 0x6240); }
+__device__ __forceinline__ uint32_t hi_bytes(uint32_t ev, uint32_t od) { return __byte_perm(ev, od, 0x7351); }
+// 4 unsigned bytes x -> 16-bit lanes sc * x + bias (even and odd elements)
+__device__ __forceinline__ void lane_fold(uint32_t x, int sc, int bias, uint32_t &ev, uint32_t &od) {
+    const int b2 = bias * 0x10001;
+    ev = static_cast<uint32_t>(sc * static_cast<int>(x & 0x00FF00FFu) + b2);
+    od = static_cast<uint32_t>(sc * static_cast<int>((x >> 8) & 0x00FF00FFu) + b2);
+}
+
+template <int TYPE>
+__device__ __forceinline__ void mmq_unpack(const uint8_t *blk, uint32_t a_cols, int h, RowScales &rs);
+
+// Q2_K (84 bytes: scales[16] (low nibble scale, high nibble min), qs[64],
+// d, dmin): sc * q in [0, 45]; mins (16 m_g, m_g) for the summs MMA.
+template <>
+__device__ __forceinline__ void mmq_unpack<T_Q2_K>(const uint8_t *blk, uint32_t a_cols, int h, RowScales &rs) {
+    uint32_t sc4[4], qs[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) sc4[i] = ld_u32(blk + 4 * i);
 #pragma unroll
     for (int i = 0; i < 8; ++i) qs[i] = ld_u32(blk + 16 + 32 * h + 4 * i);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        // elements 16 kb .. 16 kb + 15 (kb = 8 h + c): plane c / 2 of quant
-        // bytes 16 (c % 2) .. + 15 of the half's 32 bytes; one scale
-        const int kb = 8 * h + c, plane = c >> 1, hb = c & 1;
-        const uint32_t sc = (sc4[kb >> 2] >> (8 * (kb & 3))) & 0xFu;
+    for (int part = 0; part < 2; ++part) {
+        uint32_t v[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[4 * c + i] = ((qs[4 * hb + i] >> (2 * plane)) & 0x03030303u) * sc;
+        for (int cc = 0; cc < 4; ++cc) {
+            // elements 16 kb .. + 15 (kb = 8 h + c): plane c / 2 of quant bytes
+            // 16 (c % 2) .. + 15 of the half's 32 bytes; one scale
+            const int c = 4 * part + cc, kb = 8 * h + c, plane = c >> 1, hb = c & 1;
+            const uint32_t sc = (sc4[kb >> 2] >> (8 * (kb & 3))) & 0xFu;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[4 * cc + i] = ((qs[4 * hb + i] >> (2 * plane)) & 0x03030303u) * sc;
+        }
+        tmem_st16(a_cols + 32 * h + 16 * part, v);
     }
-    tmem_st32(a_cols + 32 * h, v);
     if (h == 0) {
         const uint32_t m[8] = {sc4[0] & 0xF0F0F0F0u, sc4[1] & 0xF0F0F0F0u, sc4[2] & 0xF0F0F0F0u, sc4[3] & 0xF0F0F0F0u,
                                (sc4[0] >> 4) & 0x0F0F0F0Fu, (sc4[1] >> 4) & 0x0F0F0F0Fu, (sc4[2] >> 4) & 0x0F0F0F0Fu,
                                (sc4[3] >> 4) & 0x0F0F0F0Fu};
         tmem_st8(a_cols + MmqLayout<T_Q2_K>::MINS_COL, m);
-        d = ld_half(blk + 80);
-        dm = ld_half(blk + 82);
+        rs.d = ld_half(blk + 80);
+        rs.dm = ld_half(blk + 82);
     }
+}
+
+// Q3_K (110 bytes: hmask[32], qs[64], scales[12] (16 six-bit values, +32), d):
+// value u - 4 with u = 2 low bits | high bit << 2; the plane holds
+// -(sc - 32) * (u - 4) in [-128, 124], so isum = -(plane dot).
+template <>
+__device__ __forceinline__ void mmq_unpack<T_Q3_K>(const uint8_t *blk, uint32_t a_cols, int h, RowScales &rs) {
+    uint32_t hm[8], qs[8], sw[3];
+    ld_words_a2(blk, hm);
+    ld_words_a2(blk + 32 + 32 * h, qs);
+    ld_words_a2(blk + 96, sw);
+    // the half's 8 scales (ggml's 6-bit scale unpacking, kmask1/kmask2)
+    const uint32_t s_lo = h == 0 ? ((sw[0] & 0x0F0F0F0Fu) | (((sw[2] >> 0) & 0x03030303u) << 4))
+                                 : (((sw[0] >> 4) & 0x0F0F0F0Fu) | (((sw[2] >> 4) & 0x03030303u) << 4));
+    const uint32_t s_hi = h == 0 ? ((sw[1] & 0x0F0F0F0Fu) | (((sw[2] >> 2) & 0x03030303u) << 4))
+                                 : (((sw[1] >> 4) & 0x0F0F0F0Fu) | (((sw[2] >> 6) & 0x03030303u) << 4));
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        uint32_t v[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            // chunk c: shift j = c / 2, 16-element half c % 2 of the 32
+            const int c = 4 * part + cc, j = c >> 1, hh = c & 1;
+            const int s = static_cast<int>(((c < 4 ? s_lo : s_hi) >> (8 * (c & 3))) & 0xFFu) - 32;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t u = ((qs[4 * hh + i] >> (2 * j)) & 0x03030303u) |
+                                   (((hm[4 * hh + i] >> (4 * h + j)) & 0x01010101u) << 2);
+                uint32_t ev, od;
+                lane_fold(u, -s, 4 * s + 256, ev, od);   // -s u + 4 s + 256 in [132, 384]
+                v[4 * cc + i] = lo_bytes(ev, od);
+            }
+        }
+        tmem_st16(a_cols + 32 * h + 16 * part, v);
+    }
+    if (h == 0) rs.d = ld_half(blk + 108);
+}
+
+// Q4_K (144 bytes: d, dmin, scales[12] (8 six-bit scales and mins), qs[128]):
+// sc * q in [0, 945] as two planes (low byte, high byte).
+__device__ __forceinline__ void q4K_scale_min(const uint32_t (&sw)[3], int j, int &sc, int &m) {
+    const auto byte = [&](int i) { return static_cast<int>((sw[i >> 2] >> (8 * (i & 3))) & 0xFFu); };
+    if (j < 4) {
+        sc = byte(j) & 63;
+        m = byte(j + 4) & 63;
+    } else {
+        sc = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
+        m = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+    }
+}
+
+template <>
+__device__ __forceinline__ void mmq_unpack<T_Q4_K>(const uint8_t *blk, uint32_t a_cols, int h, RowScales &rs) {
+    uint32_t sw[3], qs[16];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) sw[i] = ld_u32(blk + 4 + 4 * i);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qs[i] = ld_u32(blk + 16 + 64 * h + 4 * i);
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            // chunk c: 32-byte group c / 4 of the half's 64 quant bytes, nibble
+            // (c / 2) % 2, bytes 16 (c % 2) .. + 15; sub-block 4 h + 2 (c / 4) + (c / 2) % 2
+            const int c = 4 * part + cc, nib = (c >> 1) & 1;
+            int sc, m;
+            q4K_scale_min(sw, 4 * h + 2 * (c >> 2) + nib, sc, m);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t q = (qs[8 * (c >> 2) + 4 * (c & 1) + i] >> (4 * nib)) & 0x0F0F0F0Fu;
+                uint32_t ev, od;
+                lane_fold(q, sc, 0, ev, od);
+                lo[4 * cc + i] = lo_bytes(ev, od);
+                hi[4 * cc + i] = hi_bytes(ev, od);
+            }
+        }
+        tmem_st16(a_cols + 32 * h + 16 * part, lo);
+        tmem_st16(a_cols + 64 + 32 * h + 16 * part, hi);
+    }
+    if (h == 0) {
+        uint32_t mb[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int sc, m;
+            q4K_scale_min(sw, j, sc, m);
+            mb[j >> 2] |= static_cast<uint32_t>(m) << (8 * (j & 3));
+        }
+        rs.m = make_uint2(mb[0], mb[1]);
+        rs.d = ld_half(blk);
+        rs.dm = ld_half(blk + 2);
+    }
+}
+
+// Q6_K (210 bytes: ql[128], qh[64], scales[16] (int8), d): sc * (q - 32) in
+// [-4064, 4096] as two planes (low byte unsigned, high byte signed).
+template <>
+__device__ __forceinline__ void mmq_unpack<T_Q6_K>(const uint8_t *blk, uint32_t a_cols, int h, RowScales &rs) {
+    uint32_t ql[16], qh[8], sw[2];
+    ld_words_a2(blk + 64 * h, ql);
+    ld_words_a2(blk + 128 + 32 * h, qh);
+    ld_words_a2(blk + 192 + 8 * h, sw);
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            // chunk c: group g = c / 2 (ql bytes 32 (g % 2) .., nibble g / 2,
+            // qh bits 2 g), 16-element half c % 2 of the 32; scale 8 h + c
+            const int c = 4 * part + cc, g = c >> 1, lh = c & 1;
+            const int sc = static_cast<int>(static_cast<int8_t>((sw[c >> 2] >> (8 * (c & 3))) & 0xFFu));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t q = ((ql[8 * (g & 1) + 4 * lh + i] >> (4 * (g >> 1))) & 0x0F0F0F0Fu) |
+                                   (((qh[4 * lh + i] >> (2 * g)) & 0x03030303u) << 4);
+                uint32_t ev, od;
+                lane_fold(q, sc, 32768 - 32 * sc, ev, od);   // sc (q - 32) + 32768
+                lo[4 * cc + i] = lo_bytes(ev, od);
+                hi[4 * cc + i] = hi_bytes(ev, od) ^ 0x80808080u;
+            }
+        }
+        tmem_st16(a_cols + 32 * h + 16 * part, lo);
+        tmem_st16(a_cols + 64 + 32 * h + 16 * part, hi);
+    }
+    if (h == 0) rs.d = ld_half(blk + 208);
 }
 
 // Instruction descriptor of kind::i8 with s32 accumulation: A unsigned or
@@ -299,12 +497,21 @@ __host__ __device__ constexpr uint32_t mmq_idesc(bool a_signed, int N) {
            (static_cast<uint32_t>(MMQ_M >> 4) << 24);
 }
 
+// summs of Q4_K: sum over the 8 sub-blocks of m_j * (bsum 2 j + bsum 2 j + 1)
+__device__ __forceinline__ int q4K_summs(const int16_t *bs2, uint2 m) {
+    const int4 b = *reinterpret_cast<const int4 *>(bs2);
+    int acc = __dp2a_lo(b.x, static_cast<int>(m.x), 0);
+    acc = __dp2a_hi(b.y, static_cast<int>(m.x), acc);
+    acc = __dp2a_lo(b.z, static_cast<int>(m.y), acc);
+    return __dp2a_hi(b.w, static_cast<int>(m.y), acc);
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid_constant__ MmqArgs a) {
     using Lay = MmqLayout<TYPE>;
     using Ty = MmqType<TYPE>;
     static_assert(sizeof(MmqCtrl) <= Lay::CTRL, "control block too large");
-    constexpr int BPB = Ty::BPB;
+    constexpr int BPB = Ty::BPB, NT = Ty::NT;
     extern __shared__ __align__(1024) uint8_t smem[];
     MmqCtrl &C = *reinterpret_cast<MmqCtrl *>(smem);
     uint8_t *B = smem + Lay::OFF_B;
@@ -312,7 +519,7 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nsb = a.K / 256;
     const int row_blocks = a.nrows / MMQ_M;
-    const int total = a.tile_off[a.n_experts];
+    const int total = *a.n_chunks * row_blocks;
     const int G = a.G, GR = MMQ_M / a.G;     // rows per tensor-map row; tensor-map rows per box
 
     if (tid == 0) {
@@ -349,8 +556,10 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
         const uint64_t pol_w = l2_evict_first_policy(), pol_b = l2_evict_last_policy();
         uint32_t ps = 0, pph = 0, bs = 0, bph = 0, fills_p = 0, fills_b = 0;
         bool pok = true;
+        int4 ch = static_cast<int>(blockIdx.x) < total ? a.chunks[blockIdx.x / row_blocks] : make_int4(0, 0, 0, 0);
         for (int ti = blockIdx.x; ti < total && pok; ti += gridDim.x) {
-            const MmqTile T = mmq_tile(a, ti, row_blocks);
+            const MmqTile T = mmq_tile(ch, ti, row_blocks);
+            if (ti + static_cast<int>(gridDim.x) < total) ch = a.chunks[(ti + gridDim.x) / row_blocks];   // next tile's chunk
             const uint32_t bbytes = mmq_bt_bytes(mmq_chunk_n(T.nt));
             const int y0 = (T.e * a.nrows + T.rb * MMQ_M) / G;   // first tensor-map row of the tile
             for (int sb = 0; sb < nsb; ++sb) {
@@ -391,11 +600,13 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
         if (lane == 0) {
             uint32_t g = 0, last = 0;
             bool ok = true, any = false;
+            int4 ch = static_cast<int>(blockIdx.x) < total ? a.chunks[blockIdx.x / row_blocks] : make_int4(0, 0, 0, 0);
             for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x) {
-                const MmqTile T = mmq_tile(a, ti, row_blocks);
+                const MmqTile T = mmq_tile(ch, ti, row_blocks);
+                if (ti + static_cast<int>(gridDim.x) < total) ch = a.chunks[(ti + gridDim.x) / row_blocks];
                 const int N = mmq_chunk_n(T.nt);
                 const uint32_t bcs = 16u * N;   // B: bytes of one 16-byte K chunk over the N tokens
-                const uint32_t idesc = mmq_idesc(Ty::A_SIGNED, N), idesc_m = mmq_idesc(false, N);
+                const uint32_t id0 = mmq_idesc(Ty::P0_SIGNED, N), id1 = mmq_idesc(Ty::P1_SIGNED, N);
                 for (int sb = 0; sb < nsb; ++sb, ++g) {
                     if ((g & 1u) != par) continue;
                     const uint32_t bs = g % Lay::NB, bph = (g / Lay::NB) & 1u;
@@ -409,10 +620,14 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                     const uint32_t b0 = smem_u32(B + bs * MMQ_BT_BYTES) + MMQ_BT_HEAD;
                     const uint32_t d0 = tmem + par * Lay::ACC_COLS;
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        umma_i8_ts(d0, a0 + 8 * kk, umma_desc(b0 + kk * 2 * bcs, bcs, 128), idesc, kk > 0 ? 1u : 0u);
-                    if (Ty::MINS)   // summs = sum_g (16 m_g) hi_g + m_g lo_g
-                        umma_i8_ts(d0 + Lay::SUMMS_COL, a0 + Lay::MINS_COL, umma_desc(b0 + 16 * bcs, bcs, 128), idesc_m, 0u);
+                    for (int p = 0; p < Ty::NPLANE; ++p)
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk)
+                            umma_i8_ts(d0 + p * NT, a0 + p * 64 + 8 * kk, umma_desc(b0 + kk * 2 * bcs, bcs, 128),
+                                       p == 0 ? id0 : id1, kk > 0 ? 1u : 0u);
+                    if (Ty::MINS_TC)   // summs = sum_g (16 m_g) hi_g + m_g lo_g
+                        umma_i8_ts(d0 + Lay::SUMMS_COL, a0 + Lay::MINS_COL, umma_desc(b0 + 16 * bcs, bcs, 128),
+                                   mmq_idesc(false, N), 0u);
                     umma_commit(&C.mma_done[par]);
                     umma_commit(&C.b_empty[bs]);
                     last = g;
@@ -429,10 +644,10 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
         // row r's window in a weight stage: box r % G, line r / G
         const uint32_t slot_off = static_cast<uint32_t>((r % G) * GR + r / G) * Lay::SLOT;
         const uint32_t row_in_group = static_cast<uint32_t>(r % G) * a.row_bytes;
-        uint32_t ps = 0, pph = 0, bs = 0, bph = 0, g = 0;
-        bool ok = true;
         // this thread's TMEM lane (row r) in the A buffers
         const uint32_t a_lane = tmem + (static_cast<uint32_t>(32 * (uw & 3)) << 16) + Lay::A_COL0;
+        uint32_t ps = 0, pph = 0, bs = 0, bph = 0, g = 0;
+        bool ok = true;
         for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x) {
             for (int sb = 0; sb < nsb; ++sb, ++g) {
                 // weight stage landed; A buffer g & 1 last read by step g - 2's MMAs
@@ -441,16 +656,23 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                 if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
                 tc_fence_after();
                 const uint8_t *slot = P + ps * Lay::STAGE + slot_off + ((row_in_group + static_cast<uint32_t>(sb) * BPB) & 15u);
-                float d, dm;
-                unpack_q2K(slot, a_lane + (g & 1u) * Lay::A_COLS, h, d, dm);
-                if (h == 0) C.rs[g % MMQ_RING][r] = make_float2(d, dm);
+                RowScales rsc{};
+                mmq_unpack<TYPE>(slot, a_lane + (g & 1u) * Lay::A_COLS, h, rsc);
+                if (h == 0) {
+                    C.rs[g % MMQ_RING][r] = make_float2(rsc.d, rsc.dm);
+                    if (Ty::MINS_DP) C.rm[g % MMQ_RING][r] = rsc.m;
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&C.p_empty[ps]);
                 if (++ps == Lay::NP) { ps = 0; pph ^= 1u; }
                 if (uw < 2) {   // rows 0-63 of half 0 copy the token scales
                     ok = mmq_wait(C, &C.b_full[bs], bph, a);
                     if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-                    C.da[g % MMQ_RING][r] = reinterpret_cast<const float *>(B + bs * MMQ_BT_BYTES)[r];
+                    const uint8_t *Bst = B + bs * MMQ_BT_BYTES;
+                    C.da[g % MMQ_RING][r] = reinterpret_cast<const float *>(Bst)[r];
+                    if (Ty::MINS_DP)
+                        *reinterpret_cast<int4 *>(C.bs2[g % MMQ_RING][r]) =
+                            *reinterpret_cast<const int4 *>(Bst + MMQ_BT_BS2 + 16 * r);
                 }
                 if (++bs == Lay::NB) { bs = 0; bph ^= 1u; }
                 tmem_wait_st();
@@ -464,14 +686,19 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
         }
     } else {
         // ---------------- epilogue warps -----------------------------------------
-        const int r = 32 * (warp & 3) + lane, half = warp >> 2;   // row; token slices half, half + 2
-        float acc[MMQ_NT / 2];
+        constexpr int NQ = NT / 32;                               // 16-token slices per warp
+        const int r = 32 * (warp & 3) + lane, half = warp >> 2;   // row; slices half + 2 q
+        float acc[16 * NQ], accm[Ty::MINS_DP ? 16 * NQ : 1];
 #pragma unroll
-        for (int n = 0; n < MMQ_NT / 2; ++n) acc[n] = 0.f;
+        for (int n = 0; n < 16 * NQ; ++n) acc[n] = 0.f;
+#pragma unroll
+        for (int n = 0; n < (Ty::MINS_DP ? 16 * NQ : 1); ++n) accm[n] = 0.f;
         uint32_t g = 0;
         bool ok = true;
+        int4 ch = static_cast<int>(blockIdx.x) < total ? a.chunks[blockIdx.x / row_blocks] : make_int4(0, 0, 0, 0);
         for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x) {
-            const MmqTile T = mmq_tile(a, ti, row_blocks);
+            const MmqTile T = mmq_tile(ch, ti, row_blocks);
+            if (ti + static_cast<int>(gridDim.x) < total) ch = a.chunks[(ti + gridDim.x) / row_blocks];
             for (int sb = 0; sb < nsb; ++sb, ++g) {
                 ok = mmq_wait(C, &C.s_full[g % MMQ_RING], (g / MMQ_RING) & 1u, a) &&
                      mmq_wait(C, &C.mma_done[g & 1u], (g >> 1) & 1u, a);
@@ -480,14 +707,14 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                 const uint32_t cols = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + (g & 1u) * Lay::ACC_COLS;
                 const float2 rs = C.rs[g % MMQ_RING][r];
                 const float *dav = C.da[g % MMQ_RING];
-                // llama.cpp's sumf += (d_a d) * isum - (d_a dmin) * summs, per token
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
+                for (int q = 0; q < NQ; ++q) {
                     const int sl = half + 2 * q;
                     if (sl * 16 < T.nt) {
-                        uint32_t S[16], M[16];
-                        tmem_ld16(cols + sl * 16, S);
-                        tmem_ld16(cols + Lay::SUMMS_COL + sl * 16, M);
+                        uint32_t S0[16], S1[16];
+                        tmem_ld16(cols + sl * 16, S0);
+                        if (Ty::NPLANE == 2) tmem_ld16(cols + NT + sl * 16, S1);
+                        if (Ty::MINS_TC) tmem_ld16(cols + Lay::SUMMS_COL + sl * 16, S1);
                         tmem_wait_ld();
                         float dv[16];
 #pragma unroll
@@ -497,11 +724,26 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                         }
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            const float da = dv[j];
-                            const float dall = __fmul_rn(da, rs.x), dmin = __fmul_rn(da, rs.y);
-                            const float fi = small_int_to_float(static_cast<int>(S[j]));
-                            const float fm = small_int_to_float(static_cast<int>(M[j]));
-                            acc[q * 16 + j] = __fadd_rn(acc[q * 16 + j], __fsub_rn(__fmul_rn(dall, fi), __fmul_rn(dmin, fm)));
+                            float &A = acc[q * 16 + j];
+                            const float dall = __fmul_rn(dv[j], rs.x);
+                            if (TYPE == T_Q2_K) {
+                                // llama.cpp's sumf += (d_a d) * isum - (d_a dmin) * summs
+                                const float dmin = __fmul_rn(dv[j], rs.y);
+                                const float fi = small_int_to_float(static_cast<int>(S0[j]));
+                                const float fm = small_int_to_float(static_cast<int>(S1[j]));
+                                A = __fadd_rn(A, __fsub_rn(__fmul_rn(dall, fi), __fmul_rn(dmin, fm)));
+                            } else if (TYPE == T_Q3_K) {
+                                A = __fadd_rn(A, __fmul_rn(dall, small_int_to_float(-static_cast<int>(S0[j]))));
+                            } else {
+                                const int isum = static_cast<int>(S0[j]) + 256 * static_cast<int>(S1[j]);
+                                A = __fadd_rn(A, __fmul_rn(dall, __int2float_rn(isum)));
+                                if (Ty::MINS_DP) {
+                                    // sumf -= (d_a dmin) * summs
+                                    const int sm = q4K_summs(C.bs2[g % MMQ_RING][sl * 16 + j], C.rm[g % MMQ_RING][r]);
+                                    accm[q * 16 + j] = __fsub_rn(accm[q * 16 + j],
+                                                                 __fmul_rn(__fmul_rn(dv[j], rs.y), small_int_to_float(sm)));
+                                }
+                            }
                         }
                     }
                 }
@@ -510,13 +752,18 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                 if (lane == 0) mbar_arrive(&C.acc_empty[g & 1u]);
                 if (sb == nsb - 1) {
                     const int row = T.rb * MMQ_M + r;
-                    const int32_t *ent = a.entries + T.ebeg + T.chunk * MMQ_NT;
+                    const int32_t *ent = a.entries + T.first;
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {
+                    for (int q = 0; q < NQ; ++q) {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int n = (half + 2 * q) * 16 + j;
-                            if (n < T.nt) a.dst[static_cast<int64_t>(ent[n]) * a.nrows + row] = acc[q * 16 + j];
+                            float v = acc[q * 16 + j];
+                            if (Ty::MINS_DP) {
+                                v = __fadd_rn(accm[q * 16 + j], v);
+                                accm[q * 16 + j] = 0.f;
+                            }
+                            if (n < T.nt) a.dst[static_cast<int64_t>(ent[n]) * a.nrows + row] = v;
                             acc[q * 16 + j] = 0.f;
                         }
                     }
@@ -528,32 +775,44 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
     __syncthreads();
     tc_fence_after();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u)
-                     : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
 }
 
-cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int row_blocks,
-                             int32_t *cnt, int32_t *offsets, int32_t *cursor, int32_t *entries, int32_t *tile_off,
-                             int *err, cudaStream_t st) {
-    mmq_group_kernel<<<1, 1024, 0, st>>>(ids, ids_stride, n_tok, k, E, row_blocks, cnt, offsets, cursor, entries,
-                                         tile_off, err);
+cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int ntc,
+                             int32_t *entries, int4 *chunks, int32_t *n_chunks, int *err, cudaStream_t st) {
+    const size_t smem = static_cast<size_t>(E) * sizeof(int32_t);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(mmq_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    mmq_group_kernel<<<1, 1024, smem, st>>>(ids, ids_stride, n_tok, k, E, ntc, entries, chunks, n_chunks, err);
     return cudaGetLastError();
 }
 
-cudaError_t launch_mmq_gather(const uint8_t *x8, int nsb, int E, int row_blocks, int k, const int32_t *offsets,
-                              const int32_t *entries, const int32_t *tile_off, int64_t max_chunks, uint8_t *btiles,
-                              cudaStream_t st) {
+cudaError_t launch_mmq_gather(const uint8_t *x8, int K, int k, int ntc, const int32_t *entries, const int4 *chunks,
+                              const int32_t *n_chunks, int64_t max_chunks, uint8_t *btiles, cudaStream_t st) {
     int dev = 0, n_sm = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t work = max_chunks * nsb;
-    const int grid = static_cast<int>(work < 8 * n_sm ? (work > 0 ? work : 1) : 8 * n_sm);
-    mmq_gather_q8K_kernel<<<grid, 256, 0, st>>>(x8, nsb, E, row_blocks, k, offsets, entries, tile_off, btiles);
+    const int64_t blocks = (max_chunks * ntc + 7) / 8;   // one warp per token slot, 8 warps a block
+    const int grid = static_cast<int>(blocks < 8 * n_sm ? (blocks > 0 ? blocks : 1) : 8 * n_sm);
+    mmq_gather_q8K_kernel<<<grid, 256, 0, st>>>(x8, K / 256, k, ntc, entries, chunks, n_chunks, btiles);
     return cudaGetLastError();
 }
 
+int mmq_chunk_tokens(int type) {
+    switch (type) {
+        case T_Q2_K: return MmqType<T_Q2_K>::NT;
+        case T_Q3_K: return MmqType<T_Q3_K>::NT;
+        case T_Q4_K: return MmqType<T_Q4_K>::NT;
+        case T_Q6_K: return MmqType<T_Q6_K>::NT;
+        default: return 0;
+    }
+}
+
 bool mmq_supported(int type, int64_t K, int64_t nrows) {
-    return type == T_Q2_K && K % 256 == 0 && nrows % MMQ_M == 0;
+    return mmq_chunk_tokens(type) > 0 && K % 256 == 0 && K / 256 <= MMQ_GATHER_MAX_SB && nrows % MMQ_M == 0;
 }
 
 namespace {
@@ -591,16 +850,9 @@ bool encode_rows_map(MmqArgs &a, uint32_t slot) {
     return r == CUDA_SUCCESS;
 }
 
-}  // namespace
-
-int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err) {
-    *cuda_err = cudaSuccess;
-    if (!mmq_supported(type, a.K, a.nrows)) {
-        *why = "tensor-core prefill needs Q2_K, K % 256 == 0 and rows % 128 == 0";
-        return -2;
-    }
-    if (a.timeout_ns == 0) a.timeout_ns = 2000000000ull;
-    using Lay = MmqLayout<T_Q2_K>;
+template <int TYPE>
+int launch_mmq_t(MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err) {
+    using Lay = MmqLayout<TYPE>;
     if ((reinterpret_cast<uintptr_t>(a.dense) & 15u) != 0 || !encode_rows_map(a, Lay::SLOT)) {
         *why = "cannot describe the expert rows as a TMA tensor map";
         return -2;
@@ -609,7 +861,7 @@ int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaErro
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return -3;
-    auto kern = moe_mmq_kernel<T_Q2_K>;
+    auto kern = moe_mmq_kernel<TYPE>;
     if (!configured[dev]) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL);
         if (e != cudaSuccess) { *cuda_err = e; *why = "cudaFuncSetAttribute"; return -3; }
@@ -621,6 +873,23 @@ int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaErro
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { *cuda_err = e; *why = "moe_mmq_kernel launch"; return -3; }
     return 0;
+}
+
+}  // namespace
+
+int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err) {
+    *cuda_err = cudaSuccess;
+    if (!mmq_supported(type, a.K, a.nrows)) {
+        *why = "tensor-core prefill needs Q2_K/Q3_K/Q4_K/Q6_K, K % 256 == 0, K <= 4096, rows % 128 == 0";
+        return -2;
+    }
+    if (a.timeout_ns == 0) a.timeout_ns = 2000000000ull;
+    switch (type) {
+        case T_Q2_K: return launch_mmq_t<T_Q2_K>(a, st, why, cuda_err);
+        case T_Q3_K: return launch_mmq_t<T_Q3_K>(a, st, why, cuda_err);
+        case T_Q4_K: return launch_mmq_t<T_Q4_K>(a, st, why, cuda_err);
+        default: return launch_mmq_t<T_Q6_K>(a, st, why, cuda_err);
+    }
 }
 
 }  // namespace moe

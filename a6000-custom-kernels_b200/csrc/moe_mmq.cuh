@@ -34,7 +34,10 @@ constexpr int MMQ_NT = 64;                 // tokens per chunk (MMA N)
 constexpr int MMQ_CWARPS = 4;              // consumer warps: thread r owns row r
 constexpr int MMQ_THREADS = 32 * (MMQ_CWARPS + 1);
 constexpr int MMQ_BCHUNKS = 18;            // 16 chunks of quants + bsum hi + bsum lo (16 bytes per token each)
-constexpr uint32_t MMQ_BT_HEAD = MMQ_NT * 4;                        // the tokens' block scales
+// B-tile head: the tokens' block scales (float [MMQ_NT]), then their 32-value
+// bsum pairs (int16 [MMQ_NT][8])
+constexpr uint32_t MMQ_BT_BS2 = MMQ_NT * 4;
+constexpr uint32_t MMQ_BT_HEAD = MMQ_BT_BS2 + MMQ_NT * 16;
 constexpr uint32_t MMQ_BT_BYTES = MMQ_BT_HEAD + MMQ_BCHUNKS * MMQ_NT * 16;
 // B tile of a chunk of nt tokens: N = nt rounded up to 16 token columns
 __host__ __device__ constexpr int mmq_chunk_n(int nt) { return (nt + 15) / 16 * 16; }
@@ -49,17 +52,18 @@ struct MmqArgs {
     uint32_t row_bytes;
     const uint8_t *btiles;          // [chunk][K / 256][MMQ_BT_BYTES], the first mmq_bt_bytes(N) used
     int32_t n_tok, k;
-    const int32_t *offsets;         // [n_experts + 1] into entries
     const int32_t *entries;         // entry = tok * k + pick, grouped by expert
-    const int32_t *tile_off;        // [n_experts + 1] tile prefix: expert e has ceil(cnt / NT) * (nrows / M) tiles
+    const int4 *chunks;             // [chunk] {expert, first entry, token count, -}; tile t is chunk t / (nrows / M)
+    const int32_t *n_chunks;        // device count of chunks (chunks of up to MmqType::NT tokens)
     float *dst;                     // [tok][pick][nrows]
     int *err;
     uint64_t timeout_ns;
 };
 
-// Bound on the number of chunks of n entries over E experts (workspace sizing)
-__host__ __device__ constexpr int64_t mmq_max_chunks(int64_t n, int64_t E) {
-    return n / MMQ_NT + (E < n ? E : n);
+// Bound on the number of chunks of up to nt of n entries over E experts
+// (workspace sizing)
+__host__ __device__ constexpr int64_t mmq_max_chunks(int64_t n, int64_t E, int64_t nt) {
+    return n / nt + (E < n ? E : n);
 }
 
 // ---- tcgen05 / UMMA helpers -------------------------------------------------
@@ -106,7 +110,15 @@ __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
-// 32 / 8 consecutive 32-bit TMEM columns of this thread's lane (no wait)
+// 32 / 16 / 8 consecutive 32-bit TMEM columns of this thread's lane (no wait)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "

@@ -3,9 +3,11 @@ llama.cpp CPU MUL_MAT_ID (Q8_K activations).
 
 Q2_K on the tensor-core path computes each super-block's integer dot exactly
 and finishes it with llama.cpp's own float steps in the same order, so the
-result is compared bit for bit. Types without a tensor-core path run the
-decode GEMV (in-kernel Q8_K): max |gpu - ref| / max |ref| <= 1e-4 per output
-vector (float summation order only)."""
+result is compared bit for bit. Q3_K, Q4_K and Q6_K also have exact integer
+super-block dots but sum them in float once per super-block where llama.cpp
+keeps 8 lane sums; those and the types without a tensor-core path (decode
+GEMV, in-kernel Q8_K) are held to max |gpu - ref| / max |ref| <= 1e-4 per
+output vector."""
 import numpy as np
 import pytest
 import torch
@@ -35,9 +37,9 @@ def _run(pkg, cuda, t, W, K, rows, x, ids):
 
 
 @pytest.mark.parametrize("K,rows,E,k,n_tok,seed", [
-    (256, 128, 4, 1, 1, 1),          # one super-block, one token: a tile of 1 of 32 token slots
+    (256, 128, 4, 1, 1, 1),          # one super-block, one token: 1 of a chunk's 64 token slots
     (768, 256, 8, 2, 100, 2),        # odd super-block count, ragged token chunks
-    (1024, 384, 16, 4, 33, 3),       # 33 tokens: chunks of 32 + 1 on the hot experts
+    (1024, 384, 16, 4, 130, 3),      # 130 tokens: chunks of 64 + 64 + 2 on the hot experts
     (3072, 768, 32, 8, 64, 4),       # config-2 gate/up shape (1008-byte rows: the widest packed tile)
     (768, 3072, 32, 8, 48, 5),       # config-2 down shape (24 row blocks)
 ])
@@ -73,7 +75,29 @@ def test_prefill_q2k_repeat_same_result(pkg, cuda):
     np.testing.assert_array_equal(a, b)
 
 
-@pytest.mark.parametrize("t,K,rows", [(O.Q4_K, 512, 256), (O.Q6_K, 256, 128), (O.Q4_0, 256, 96),
+@pytest.mark.parametrize("t,K,rows,E,k,n_tok,seed", [
+    (O.Q3_K, 256, 128, 4, 1, 1, 21),
+    (O.Q3_K, 768, 256, 8, 2, 100, 22),     # 330-byte rows: 8-row tensor-map groups, 2-byte aligned blocks
+    (O.Q3_K, 3072, 768, 32, 8, 64, 23),
+    (O.Q4_K, 512, 128, 8, 2, 70, 24),      # 32-token chunks: 70 tokens -> 32 + 32 + 6
+    (O.Q4_K, 3072, 768, 32, 8, 64, 25),
+    (O.Q4_K, 768, 3072, 32, 8, 48, 26),
+    (O.Q6_K, 256, 128, 4, 1, 33, 27),
+    (O.Q6_K, 768, 256, 8, 2, 100, 28),     # 630-byte rows
+    (O.Q6_K, 3072, 768, 32, 8, 64, 29),
+])
+def test_prefill_kquants_tensor_cores(pkg, cuda, t, K, rows, E, k, n_tok, seed):
+    """Q3_K / Q4_K / Q6_K on the tensor cores: exact integer dots, llama.cpp's
+    float steps up to the order of the sub-block sums"""
+    W = experts(t, E, rows, K, seed)
+    x = activations((n_tok, K), seed + 10)
+    ids = _zipf_ids(n_tok, E, k, seed + 20)
+    got, tc = _run(pkg, cuda, t, W, K, rows, x, ids)
+    assert tc
+    assert rel_err(got, O.mul_mat_id(t, W, K, x[:, None, :], ids)) <= TIGHT
+
+
+@pytest.mark.parametrize("t,K,rows", [(O.Q5_K, 512, 256), (O.Q4_0, 256, 96), (O.Q8_0, 256, 128),
                                       (O.Q2_K, 256, 192)])   # rows not a multiple of 128
 def test_prefill_fallback_gemv(pkg, cuda, t, K, rows):
     E, k, n_tok = 8, 2, 19
