@@ -106,6 +106,8 @@ def _declare(L):
         "moe_b200_layer_set_fused": (i32, [i32]),
         "moe_b200_ep_layer_decode": (i32, [ctypes.POINTER(MoeLayerDesc), i64, i64, i32, vp, vp, vp, i64, vp, sz, vp]),
         "moe_b200_prefill_workspace_size": (sz, [ctypes.POINTER(MoeTensor), i64, i64]),
+        "moe_b200_layer_prefill_workspace_size": (sz, [ctypes.POINTER(MoeLayerDesc), i64]),
+        "moe_b200_layer_prefill": (i32, [ctypes.POINTER(MoeLayerDesc), vp, vp, vp, i64, vp, sz, vp]),
         "moe_b200_prefill_mul_mat_id": (i32, [ctypes.POINTER(MoeTensor), vp, i64, vp, i64, i64, vp, vp, sz,
                                              ctypes.POINTER(i32), vp]),
     }

@@ -760,18 +760,152 @@ struct PrefillWs {
     size_t bytes;
 };
 
-PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, char *base) {
+// x_rows: activation rows (n_tok, or n_tok * k when each pick has its own row)
+PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x_rows, char *base) {
     PrefillWs w{};
     size_t off = 0;
     auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
     const int64_t E = src0->ne[2], K = src0->ne[0];
-    w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(n_tok) * (K / 256) * 292));
+    w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(x_rows) * (K / 256) * 292));
     w.entries = reinterpret_cast<int32_t *>(take(4 * n_tok * k));
     const int ntc = moe::mmq_chunk_tokens(src0->type) > 0 ? moe::mmq_chunk_tokens(src0->type) : moe::MMQ_NT;
     w.max_chunks = moe::mmq_max_chunks(n_tok * k, E, ntc);
     w.chunks = reinterpret_cast<int4 *>(take(16 * static_cast<size_t>(w.max_chunks)));
     w.n_chunks = reinterpret_cast<int32_t *>(take(4));
     w.btiles = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(w.max_chunks) * (K / 256) * moe::MMQ_BT_BYTES));
+    w.bytes = off;
+    return w;
+}
+
+
+// One prefill MUL_MAT_ID: dst[(t * k + p) * rows + r] = row r of expert
+// ids[t][p] . x row (t, or t * k + p when x_per_pick). Tensor cores where
+// the type and shape allow (grouping, Q8_K quantization, B-tile gather, MMQ),
+// else the decode GEMV over chunks of 8 tokens.
+int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t n_tok, const int32_t *ids, int64_t k,
+                int64_t ids_stride, float *dst, char *workspace, size_t workspace_bytes, bool *used_tc,
+                cudaStream_t st) {
+    *used_tc = false;
+    if (!src0 || !src0->data || !x || !ids || !dst) return fail(MOE_ERR_INVALID, "null argument");
+    if (n_tok < 1 || k < 1 || ids_stride < k) return fail(MOE_ERR_INVALID, "need n_tok >= 1, k >= 1, ids_stride >= k");
+    if (!type_supported(src0->type)) return fail(MOE_ERR_UNSUPPORTED, "unsupported expert type %d", src0->type);
+    if (!contiguous(src0) || !aligned16(src0->data))
+        return fail(MOE_ERR_UNSUPPORTED, "expert tensor must be contiguous and 16-byte aligned");
+    const int64_t K = src0->ne[0], rows = src0->ne[1], E = src0->ne[2];
+    const int64_t x_rows = x_per_pick ? n_tok * k : n_tok;
+    const bool tc = moe::mmq_supported(src0->type, K, rows) && ptr_kind(src0->data) == 2 &&
+                    (src0->nb[2] % 16) == 0 && n_tok * k < (int64_t{1} << 30) && E <= 16384;
+    if (!tc) {
+        // no tensor-core path: the decode GEMV over chunks of 8 tokens
+        for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
+            const int64_t nt = n_tok - t0 < 8 ? n_tok - t0 : 8;
+            MmvqCall c;
+            c.src0 = src0;
+            c.src1 = x + t0 * (x_per_pick ? k : 1) * K;
+            c.src1_type = MOE_TYPE_F32;
+            c.ids = ids + t0 * ids_stride;
+            c.dst = dst + t0 * k * rows;
+            c.ne00 = K; c.ne01 = rows; c.ncols_dst = nt; c.s01 = static_cast<int64_t>(src0->nb[1]) / type_size(src0->type);
+            c.nchannels_y = x_per_pick ? k : 1; c.nchannels_dst = k;
+            c.stride_col_y = (x_per_pick ? k : 1) * K; c.stride_channel_y = x_per_pick ? K : 0;
+            c.stride_col_dst = k * rows; c.stride_channel_dst = rows;
+            c.ids_stride = ids_stride;
+            const int rc = run_mmvq(c, st);
+            if (rc) return rc;
+        }
+        return MOE_OK;
+    }
+    const PrefillWs w = prefill_ws(src0, n_tok, k, x_rows, workspace);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
+    int rc = init_device_globals();
+    if (rc) return rc;
+    const int ntc = moe::mmq_chunk_tokens(src0->type);
+    CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E), ntc,
+                             w.entries, w.chunks, w.n_chunks, g.d_err, st));
+    CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, x_rows, K, st));
+    // the gather reads activation row entry / k_div (entry = t * k + p)
+    CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries,
+                              w.chunks, w.n_chunks, w.max_chunks, w.btiles, st));
+    moe::MmqArgs a{};
+    a.dense = static_cast<const char *>(src0->data);
+    a.expert_bytes = src0->nb[2];
+    a.n_experts = static_cast<int32_t>(E);
+    a.K = static_cast<int32_t>(K);
+    a.nrows = static_cast<int32_t>(rows);
+    a.row_bytes = static_cast<uint32_t>(src0->nb[1]);
+    a.btiles = w.btiles;
+    a.n_tok = static_cast<int32_t>(n_tok);
+    a.k = static_cast<int32_t>(k);
+    a.entries = w.entries;
+    a.chunks = w.chunks;
+    a.n_chunks = w.n_chunks;
+    a.dst = dst;
+    a.err = g.d_err;
+    const char *why = "";
+    cudaError_t ce = cudaSuccess;
+    rc = moe::launch_mmq(src0->type, a, st, &why, &ce);
+    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+    if (rc) return fail(rc, "%s", why);
+    *used_tc = true;
+    return MOE_OK;
+}
+
+// A shared-expert matrix as a one-expert tensor of the given type
+moe_tensor shared_tensor(const void *data, int32_t type, int64_t K, int64_t rows) {
+    moe_tensor t{};
+    t.data = const_cast<void *>(data);
+    t.type = type;
+    const uint64_t rb = static_cast<uint64_t>(K / blck_size(type)) * type_size(type);
+    t.ne[0] = K; t.ne[1] = rows; t.ne[2] = 1; t.ne[3] = 1;
+    t.nb[0] = type_size(type); t.nb[1] = rb; t.nb[2] = rb * rows; t.nb[3] = rb * rows;
+    return t;
+}
+
+// Layer prefill workspace: ids, weights, gate / up (then h) / down outputs,
+// the shared expert's outputs, zero ids, then the MUL_MAT_ID scratch
+struct LayerPrefillWs {
+    int32_t *ids, *zero_ids;
+    float *w, *g, *u, *y, *sg, *su, *ys;
+    char *scratch;
+    size_t scratch_bytes, bytes;
+};
+
+LayerPrefillWs layer_prefill_ws(const moe_layer_desc *L, int64_t n, char *base) {
+    LayerPrefillWs w{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
+    const int64_t H = L->H, F = L->F, k = L->k;
+    w.ids = reinterpret_cast<int32_t *>(take(4 * n * k));
+    w.w = reinterpret_cast<float *>(take(4 * n * k));
+    w.g = reinterpret_cast<float *>(take(4 * n * k * F));
+    w.u = reinterpret_cast<float *>(take(4 * n * k * F));
+    w.y = reinterpret_cast<float *>(take(4 * n * k * H));
+    const bool shared = L->shared_type >= 0;
+    if (shared) {
+        w.sg = reinterpret_cast<float *>(take(4 * n * F));
+        w.su = reinterpret_cast<float *>(take(4 * n * F));
+        w.ys = reinterpret_cast<float *>(take(4 * n * H));
+        w.zero_ids = reinterpret_cast<int32_t *>(take(4 * n));
+    }
+    size_t sc = 0;
+    auto need = [&](const moe_tensor &t, int64_t kk, int64_t rows) {
+        const size_t b = prefill_ws(&t, n, kk, rows, nullptr).bytes;
+        sc = b > sc ? b : sc;
+    };
+    need(L->gate, k, n);
+    need(L->up, k, n);
+    need(L->down, k, n * k);
+    if (shared) {
+        const moe_tensor sg = shared_tensor(L->shared_gate, L->gate.type, H, F);
+        const moe_tensor su = shared_tensor(L->shared_up, L->up.type, H, F);
+        const moe_tensor sd = shared_tensor(L->shared_down, L->down.type, F, H);
+        need(sg, 1, n);
+        need(su, 1, n);
+        need(sd, 1, n);
+    }
+    w.scratch = take(sc);
+    w.scratch_bytes = sc;
     w.bytes = off;
     return w;
 }
@@ -1144,7 +1278,7 @@ int moe_b200_ep_layer_decode(const moe_layer_desc *L, int64_t expert_lo, int64_t
 
 size_t moe_b200_prefill_workspace_size(const moe_tensor *src0, int64_t n_tok, int64_t k) {
     if (!src0 || n_tok < 0 || k < 0) return 0;
-    return prefill_ws(src0, n_tok, k, nullptr).bytes;
+    return prefill_ws(src0, n_tok, k, n_tok, nullptr).bytes;
 }
 
 int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t n_tok, const int32_t *ids, int64_t k,
@@ -1152,68 +1286,54 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
                                 int32_t *used_tensor_cores, moe_stream_t stream) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     read_env();
-    if (used_tensor_cores) *used_tensor_cores = 0;
-    if (!src0 || !src0->data || !x || !ids || !dst) return fail(MOE_ERR_INVALID, "null argument");
-    if (n_tok < 1 || k < 1 || ids_stride < k) return fail(MOE_ERR_INVALID, "need n_tok >= 1, k >= 1, ids_stride >= k");
-    if (!type_supported(src0->type)) return fail(MOE_ERR_UNSUPPORTED, "unsupported expert type %d", src0->type);
-    if (!contiguous(src0) || !aligned16(src0->data))
-        return fail(MOE_ERR_UNSUPPORTED, "expert tensor must be contiguous and 16-byte aligned");
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int64_t K = src0->ne[0], rows = src0->ne[1], E = src0->ne[2];
-    const bool tc = moe::mmq_supported(src0->type, K, rows) && ptr_kind(src0->data) == 2 &&
-                    (src0->nb[2] % 16) == 0 && n_tok * k < (int64_t{1} << 30) && E <= 16384;
-    if (!tc) {
-        // no tensor-core path: the decode GEMV over chunks of 8 tokens
-        for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
-            const int64_t nt = n_tok - t0 < 8 ? n_tok - t0 : 8;
-            MmvqCall c;
-            c.src0 = src0;
-            c.src1 = x + t0 * K;
-            c.src1_type = MOE_TYPE_F32;
-            c.ids = ids + t0 * ids_stride;
-            c.dst = dst + t0 * k * rows;
-            c.ne00 = K; c.ne01 = rows; c.ncols_dst = nt; c.s01 = static_cast<int64_t>(src0->nb[1]) / type_size(src0->type);
-            c.nchannels_y = 1; c.nchannels_dst = k;
-            c.stride_col_y = K; c.stride_channel_y = 0;
-            c.stride_col_dst = k * rows; c.stride_channel_dst = rows;
-            c.ids_stride = ids_stride;
-            const int rc = run_mmvq(c, st);
-            if (rc) return rc;
-        }
-        return MOE_OK;
-    }
-    const PrefillWs w = prefill_ws(src0, n_tok, k, static_cast<char *>(workspace));
+    bool tc = false;
+    const int rc = run_prefill(src0, x, false, n_tok, ids, k, ids_stride, dst, static_cast<char *>(workspace),
+                               workspace_bytes, &tc, reinterpret_cast<cudaStream_t>(stream));
+    if (used_tensor_cores) *used_tensor_cores = tc ? 1 : 0;
+    return rc;
+}
+
+size_t moe_b200_layer_prefill_workspace_size(const moe_layer_desc *L, int64_t n_tok) {
+    if (!L || n_tok < 1) return 0;
+    return layer_prefill_ws(L, n_tok, nullptr).bytes;
+}
+
+int moe_b200_layer_prefill(const moe_layer_desc *L, const float *x, const float *logits, float *out, int64_t n_tok,
+                           void *workspace, size_t workspace_bytes, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || !x || !logits || !out || n_tok < 1) return fail(MOE_ERR_INVALID, "null argument or n_tok < 1");
+    if (L->k < 1 || L->k > L->n_experts || L->k > 32) return fail(MOE_ERR_INVALID, "need 1 <= k <= min(32, n_experts)");
+    const LayerPrefillWs w = layer_prefill_ws(L, n_tok, static_cast<char *>(workspace));
     if (!workspace || workspace_bytes < w.bytes)
         return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
-    int rc = init_device_globals();
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t H = L->H, F = L->F, k = L->k;
+    bool tc = false;
+    // route, then the experts: gate and up per pick, GLU, down per pick
+    CK(moe::launch_topk_softmax(logits, n_tok, L->n_experts, k, L->norm_w, w.ids, w.w, st));
+    int rc = run_prefill(&L->gate, x, false, n_tok, w.ids, k, k, w.g, w.scratch, w.scratch_bytes, &tc, st);
     if (rc) return rc;
-    const int ntc = moe::mmq_chunk_tokens(src0->type);
-    CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E), ntc,
-                             w.entries, w.chunks, w.n_chunks, g.d_err, st));
-    CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, n_tok, K, st));
-    CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), static_cast<int>(k), ntc, w.entries, w.chunks, w.n_chunks,
-                              w.max_chunks, w.btiles, st));
-    moe::MmqArgs a{};
-    a.dense = static_cast<const char *>(src0->data);
-    a.expert_bytes = src0->nb[2];
-    a.n_experts = static_cast<int32_t>(E);
-    a.K = static_cast<int32_t>(K);
-    a.nrows = static_cast<int32_t>(rows);
-    a.row_bytes = static_cast<uint32_t>(src0->nb[1]);
-    a.btiles = w.btiles;
-    a.n_tok = static_cast<int32_t>(n_tok);
-    a.k = static_cast<int32_t>(k);
-    a.entries = w.entries;
-    a.chunks = w.chunks;
-    a.n_chunks = w.n_chunks;
-    a.dst = dst;
-    a.err = g.d_err;
-    const char *why = "";
-    cudaError_t ce = cudaSuccess;
-    rc = moe::launch_mmq(src0->type, a, st, &why, &ce);
-    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
-    if (rc) return fail(rc, "%s", why);
-    if (used_tensor_cores) *used_tensor_cores = 1;
+    rc = run_prefill(&L->up, x, false, n_tok, w.ids, k, k, w.u, w.scratch, w.scratch_bytes, &tc, st);
+    if (rc) return rc;
+    CK(moe::launch_glu(w.g, w.u, n_tok * k * F, L->glu_op, L->glu_limit, st));
+    rc = run_prefill(&L->down, w.u, true, n_tok, w.ids, k, k, w.y, w.scratch, w.scratch_bytes, &tc, st);
+    if (rc) return rc;
+    if (L->shared_type >= 0) {
+        // the shared expert: a one-expert MUL_MAT_ID of every token
+        const moe_tensor sg = shared_tensor(L->shared_gate, L->gate.type, H, F);
+        const moe_tensor su = shared_tensor(L->shared_up, L->up.type, H, F);
+        const moe_tensor sd = shared_tensor(L->shared_down, L->down.type, F, H);
+        CK(cudaMemsetAsync(w.zero_ids, 0, 4 * n_tok, st));
+        rc = run_prefill(&sg, x, false, n_tok, w.zero_ids, 1, 1, w.sg, w.scratch, w.scratch_bytes, &tc, st);
+        if (rc) return rc;
+        rc = run_prefill(&su, x, false, n_tok, w.zero_ids, 1, 1, w.su, w.scratch, w.scratch_bytes, &tc, st);
+        if (rc) return rc;
+        CK(moe::launch_glu(w.sg, w.su, n_tok * F, L->glu_op, L->glu_limit, st));
+        rc = run_prefill(&sd, w.su, false, n_tok, w.zero_ids, 1, 1, w.ys, w.scratch, w.scratch_bytes, &tc, st);
+        if (rc) return rc;
+    }
+    CK(moe::launch_combine(w.y, w.w, L->shared_type >= 0 ? w.ys : nullptr, out, n_tok, H, k, st));
     return MOE_OK;
 }
 

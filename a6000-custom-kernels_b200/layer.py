@@ -90,6 +90,40 @@ class MoELayer:
                                           _ptr(ws), ws.numel(), _stream(stream)))
         return out
 
+    def prefill(self, x, logits, out=None, stream=None):
+        """x f32 [n_tok, H], logits f32 [n_tok, E] (device) -> out f32 [n_tok, H] for any
+        n_tok: the tensor-core prefill path (moe_b200_layer_prefill)."""
+        n_tok = x.shape[0]
+        if out is None:
+            out = torch.empty((n_tok, self.H), dtype=torch.float32, device=self.device)
+        key = ("prefill", n_tok)
+        ws = self._ws.get(key)
+        if ws is None:
+            nbytes = lib().moe_b200_layer_prefill_workspace_size(ctypes.byref(self.desc), n_tok)
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self._ws[key] = ws
+        check(lib().moe_b200_layer_prefill(ctypes.byref(self.desc), _ptr(x), _ptr(logits), _ptr(out), n_tok,
+                                           _ptr(ws), ws.numel(), _stream(stream)))
+        return out
+
+    def prefill_intermediates(self, n_tok):
+        """Views of the last prefill's workspace (layout of moe_b200_layer_prefill):
+        ids [n][k], weights [n][k], gate [n][k][F], h [n][k][F] (GLU output),
+        y [n][k][H] (down outputs), then with a shared expert its gate [n][F],
+        hs [n][F] and ys [n][H]."""
+        ws = self._ws[("prefill", n_tok)]
+        n, k, F, H = n_tok, self.k, self.F, self.H
+        parts = [(n * k, torch.int32, (n, k)), (n * k, torch.float32, (n, k)), (n * k * F, torch.float32, (n, k, F)),
+                 (n * k * F, torch.float32, (n, k, F)), (n * k * H, torch.float32, (n, k, H))]
+        if self.shared:
+            parts += [(n * F, torch.float32, (n, F)), (n * F, torch.float32, (n, F)), (n * H, torch.float32, (n, H))]
+        out, off = [], 0
+        for count, dt, shape in parts:
+            nbytes = 4 * count
+            out.append(ws[off: off + nbytes].view(dt).view(shape))
+            off += (nbytes + 255) // 256 * 256
+        return tuple(out)
+
     def intermediates(self, n_tok):
         """Views of the last decode's workspace (layout of moe_b200_layer_decode):
         ids [n][k], weights [n][k], h [n][k][F] (GLU output), hs [n][F] (shared

@@ -236,17 +236,29 @@ int moe_b200_ep_layer_decode(const moe_layer_desc *layer, int64_t expert_lo, int
 /* Prefill MUL_MAT_ID. No counterpart in the reference, which leaves batches
  * above its GEMV limit to llama.cpp's MMQ (patches/apply_patches.py:81-87):
  * dst[(t * k + p) * rows + r] = row r of expert ids[t * ids_stride + p] . x[t]
- * for n_tok tokens (x f32 [n_tok][ne00], contiguous), with llama.cpp CPU
- * semantics (Q8_K activations). Q2_K experts in device memory with rows a
- * multiple of 128 run as a grouped int8 GEMM on the tensor cores (results equal
- * to the CPU path bit for bit); other types or host-tiered tensors run the
- * decode GEMV over chunks of 8 tokens. *used_tensor_cores (optional) reports
- * which ran. Workspace: moe_b200_prefill_workspace_size bytes of device memory,
- * no initialisation needed. */
+ * for n_tok tokens (x f32 [n_tok][ne00], contiguous, 16-byte aligned), with
+ * llama.cpp CPU semantics (Q8_K activations). Q2_K, Q3_K, Q4_K and Q6_K
+ * experts in device memory with rows a multiple of 128 and ne00 <= 4096 run
+ * as a grouped int8 GEMM on the tensor cores (exact integer super-block dots;
+ * Q2_K results equal the CPU path bit for bit, the others differ only in the
+ * order of float sums); other types or host-tiered tensors run the decode
+ * GEMV over chunks of 8 tokens. *used_tensor_cores (optional) reports which
+ * ran. Workspace: moe_b200_prefill_workspace_size bytes of device memory, no
+ * initialisation needed. */
 size_t moe_b200_prefill_workspace_size(const moe_tensor *src0, int64_t n_tok, int64_t k);
 int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t n_tok, const int32_t *ids,
                                 int64_t k, int64_t ids_stride, float *dst, void *workspace, size_t workspace_bytes,
                                 int32_t *used_tensor_cores, moe_stream_t stream);
+
+/* No counterpart in the reference (the upstream graph around two
+ * MUL_MAT_ID calls, for a prompt): one MoE layer for any n_tok, f32 in/out on
+ * device: route, gate and up per pick (tensor-core prefill MUL_MAT_ID), GLU,
+ * down per pick, the shared expert as a one-expert MUL_MAT_ID of every
+ * token, weighted combine. Workspace: moe_b200_layer_prefill_workspace_size
+ * bytes of device memory (no initialisation needed); allocates nothing. */
+size_t moe_b200_layer_prefill_workspace_size(const moe_layer_desc *layer, int64_t n_tok);
+int moe_b200_layer_prefill(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
+                           int64_t n_tok, void *workspace, size_t workspace_bytes, moe_stream_t stream);
 
 /* No counterpart in the reference: 1 when moe_b200_layer_decode runs this
  * layer as one fused kernel for n_tok tokens (gate/up and down type pair with a
