@@ -108,6 +108,10 @@ def _declare(L):
         "moe_b200_prefill_workspace_size": (sz, [ctypes.POINTER(MoeTensor), i64, i64]),
         "moe_b200_layer_prefill_workspace_size": (sz, [ctypes.POINTER(MoeLayerDesc), i64]),
         "moe_b200_layer_prefill": (i32, [ctypes.POINTER(MoeLayerDesc), vp, vp, vp, i64, vp, sz, vp]),
+        "moe_b200_experts_prefill_workspace_size": (sz, [ctypes.POINTER(MoeLayerDesc), i64, i64]),
+        "moe_b200_experts_prefill": (i32, [ctypes.POINTER(MoeLayerDesc), vp, i32, vp, i64, i64, vp, vp, sz, vp]),
+        "moe_b200_shared_prefill": (i32, [ctypes.POINTER(MoeLayerDesc), vp, i64, vp, vp, sz, vp]),
+        "moe_b200_combine": (i32, [vp, vp, vp, vp, i64, i64, i64, vp]),
         "moe_b200_prefill_mul_mat_id": (i32, [ctypes.POINTER(MoeTensor), vp, i64, vp, i64, i64, vp, vp, sz,
                                              ctypes.POINTER(i32), vp]),
     }

@@ -871,11 +871,12 @@ struct LayerPrefillWs {
     size_t scratch_bytes, bytes;
 };
 
-LayerPrefillWs layer_prefill_ws(const moe_layer_desc *L, int64_t n, char *base) {
+// k picks per token (the layer's k, or 1 for expert-parallel received rows)
+LayerPrefillWs layer_prefill_ws(const moe_layer_desc *L, int64_t n, int64_t k, char *base) {
     LayerPrefillWs w{};
     size_t off = 0;
     auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
-    const int64_t H = L->H, F = L->F, k = L->k;
+    const int64_t H = L->H, F = L->F;
     w.ids = reinterpret_cast<int32_t *>(take(4 * n * k));
     w.w = reinterpret_cast<float *>(take(4 * n * k));
     w.g = reinterpret_cast<float *>(take(4 * n * k * F));
@@ -893,8 +894,8 @@ LayerPrefillWs layer_prefill_ws(const moe_layer_desc *L, int64_t n, char *base) 
         const size_t b = prefill_ws(&t, n, kk, rows, nullptr).bytes;
         sc = b > sc ? b : sc;
     };
-    need(L->gate, k, n);
-    need(L->up, k, n);
+    need(L->gate, k, n * k);   // rows: per pick when the caller gives one row per pick
+    need(L->up, k, n * k);
     need(L->down, k, n * k);
     if (shared) {
         const moe_tensor sg = shared_tensor(L->shared_gate, L->gate.type, H, F);
@@ -1295,8 +1296,41 @@ int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t 
 
 size_t moe_b200_layer_prefill_workspace_size(const moe_layer_desc *L, int64_t n_tok) {
     if (!L || n_tok < 1) return 0;
-    return layer_prefill_ws(L, n_tok, nullptr).bytes;
+    return layer_prefill_ws(L, n_tok, L->k, nullptr).bytes;
 }
+
+namespace {
+
+// gate and up per pick, GLU, down per pick into y [n][k][H]
+int experts_prefill(const moe_layer_desc *L, const float *x, bool x_per_pick, const int32_t *ids, int64_t n_tok,
+                    int64_t k, const LayerPrefillWs &w, float *y, cudaStream_t st) {
+    bool tc = false;
+    int rc = run_prefill(&L->gate, x, x_per_pick, n_tok, ids, k, k, w.g, w.scratch, w.scratch_bytes, &tc, st);
+    if (rc) return rc;
+    rc = run_prefill(&L->up, x, x_per_pick, n_tok, ids, k, k, w.u, w.scratch, w.scratch_bytes, &tc, st);
+    if (rc) return rc;
+    CK(moe::launch_glu(w.g, w.u, n_tok * k * L->F, L->glu_op, L->glu_limit, st));
+    return run_prefill(&L->down, w.u, true, n_tok, ids, k, k, y, w.scratch, w.scratch_bytes, &tc, st);
+}
+
+// the shared expert of every token into ys [n][H]
+int shared_prefill(const moe_layer_desc *L, const float *x, int64_t n_tok, const LayerPrefillWs &w, float *ys,
+                   cudaStream_t st) {
+    const int64_t H = L->H, F = L->F;
+    bool tc = false;
+    const moe_tensor sg = shared_tensor(L->shared_gate, L->gate.type, H, F);
+    const moe_tensor su = shared_tensor(L->shared_up, L->up.type, H, F);
+    const moe_tensor sd = shared_tensor(L->shared_down, L->down.type, F, H);
+    CK(cudaMemsetAsync(w.zero_ids, 0, 4 * n_tok, st));
+    int rc = run_prefill(&sg, x, false, n_tok, w.zero_ids, 1, 1, w.sg, w.scratch, w.scratch_bytes, &tc, st);
+    if (rc) return rc;
+    rc = run_prefill(&su, x, false, n_tok, w.zero_ids, 1, 1, w.su, w.scratch, w.scratch_bytes, &tc, st);
+    if (rc) return rc;
+    CK(moe::launch_glu(w.sg, w.su, n_tok * F, L->glu_op, L->glu_limit, st));
+    return run_prefill(&sd, w.su, false, n_tok, w.zero_ids, 1, 1, ys, w.scratch, w.scratch_bytes, &tc, st);
+}
+
+}  // namespace
 
 int moe_b200_layer_prefill(const moe_layer_desc *L, const float *x, const float *logits, float *out, int64_t n_tok,
                            void *workspace, size_t workspace_bytes, moe_stream_t stream) {
@@ -1304,36 +1338,55 @@ int moe_b200_layer_prefill(const moe_layer_desc *L, const float *x, const float 
     read_env();
     if (!L || !x || !logits || !out || n_tok < 1) return fail(MOE_ERR_INVALID, "null argument or n_tok < 1");
     if (L->k < 1 || L->k > L->n_experts || L->k > 32) return fail(MOE_ERR_INVALID, "need 1 <= k <= min(32, n_experts)");
-    const LayerPrefillWs w = layer_prefill_ws(L, n_tok, static_cast<char *>(workspace));
+    const LayerPrefillWs w = layer_prefill_ws(L, n_tok, L->k, static_cast<char *>(workspace));
     if (!workspace || workspace_bytes < w.bytes)
         return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int64_t H = L->H, F = L->F, k = L->k;
-    bool tc = false;
-    // route, then the experts: gate and up per pick, GLU, down per pick
-    CK(moe::launch_topk_softmax(logits, n_tok, L->n_experts, k, L->norm_w, w.ids, w.w, st));
-    int rc = run_prefill(&L->gate, x, false, n_tok, w.ids, k, k, w.g, w.scratch, w.scratch_bytes, &tc, st);
-    if (rc) return rc;
-    rc = run_prefill(&L->up, x, false, n_tok, w.ids, k, k, w.u, w.scratch, w.scratch_bytes, &tc, st);
-    if (rc) return rc;
-    CK(moe::launch_glu(w.g, w.u, n_tok * k * F, L->glu_op, L->glu_limit, st));
-    rc = run_prefill(&L->down, w.u, true, n_tok, w.ids, k, k, w.y, w.scratch, w.scratch_bytes, &tc, st);
+    CK(moe::launch_topk_softmax(logits, n_tok, L->n_experts, L->k, L->norm_w, w.ids, w.w, st));
+    int rc = experts_prefill(L, x, false, w.ids, n_tok, L->k, w, w.y, st);
     if (rc) return rc;
     if (L->shared_type >= 0) {
-        // the shared expert: a one-expert MUL_MAT_ID of every token
-        const moe_tensor sg = shared_tensor(L->shared_gate, L->gate.type, H, F);
-        const moe_tensor su = shared_tensor(L->shared_up, L->up.type, H, F);
-        const moe_tensor sd = shared_tensor(L->shared_down, L->down.type, F, H);
-        CK(cudaMemsetAsync(w.zero_ids, 0, 4 * n_tok, st));
-        rc = run_prefill(&sg, x, false, n_tok, w.zero_ids, 1, 1, w.sg, w.scratch, w.scratch_bytes, &tc, st);
-        if (rc) return rc;
-        rc = run_prefill(&su, x, false, n_tok, w.zero_ids, 1, 1, w.su, w.scratch, w.scratch_bytes, &tc, st);
-        if (rc) return rc;
-        CK(moe::launch_glu(w.sg, w.su, n_tok * F, L->glu_op, L->glu_limit, st));
-        rc = run_prefill(&sd, w.su, false, n_tok, w.zero_ids, 1, 1, w.ys, w.scratch, w.scratch_bytes, &tc, st);
+        rc = shared_prefill(L, x, n_tok, w, w.ys, st);
         if (rc) return rc;
     }
-    CK(moe::launch_combine(w.y, w.w, L->shared_type >= 0 ? w.ys : nullptr, out, n_tok, H, k, st));
+    CK(moe::launch_combine(w.y, w.w, L->shared_type >= 0 ? w.ys : nullptr, out, n_tok, L->H, L->k, st));
+    return MOE_OK;
+}
+
+size_t moe_b200_experts_prefill_workspace_size(const moe_layer_desc *L, int64_t n_tok, int64_t k) {
+    if (!L || n_tok < 1 || k < 1) return 0;
+    return layer_prefill_ws(L, n_tok, k, nullptr).bytes;
+}
+
+int moe_b200_experts_prefill(const moe_layer_desc *L, const float *x, int32_t x_per_pick, const int32_t *ids,
+                             int64_t n_tok, int64_t k, float *y, void *workspace, size_t workspace_bytes,
+                             moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || !x || !ids || !y || n_tok < 1 || k < 1) return fail(MOE_ERR_INVALID, "null argument, n_tok < 1 or k < 1");
+    const LayerPrefillWs w = layer_prefill_ws(L, n_tok, k, static_cast<char *>(workspace));
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
+    return experts_prefill(L, x, x_per_pick != 0, ids, n_tok, k, w, y, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int moe_b200_shared_prefill(const moe_layer_desc *L, const float *x, int64_t n_tok, float *ys, void *workspace,
+                            size_t workspace_bytes, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || !x || !ys || n_tok < 1) return fail(MOE_ERR_INVALID, "null argument or n_tok < 1");
+    if (L->shared_type < 0) return fail(MOE_ERR_INVALID, "layer has no shared expert");
+    const LayerPrefillWs w = layer_prefill_ws(L, n_tok, L->k, static_cast<char *>(workspace));
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
+    return shared_prefill(L, x, n_tok, w, ys, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int moe_b200_combine(const float *y, const float *weights, const float *ys, float *out, int64_t n_tok, int64_t H,
+                     int64_t k, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!y || !weights || !out || n_tok < 1 || H < 1 || k < 1) return fail(MOE_ERR_INVALID, "bad combine arguments");
+    CK(moe::launch_combine(y, weights, ys, out, n_tok, H, k, reinterpret_cast<cudaStream_t>(stream)));
     return MOE_OK;
 }
 

@@ -260,6 +260,27 @@ size_t moe_b200_layer_prefill_workspace_size(const moe_layer_desc *layer, int64_
 int moe_b200_layer_prefill(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
                            int64_t n_tok, void *workspace, size_t workspace_bytes, moe_stream_t stream);
 
+/* No counterpart in the reference: the expert part of a layer prefill,
+ * y[t][p] = down_e(GLU(gate_e . x, up_e . x)) with e = ids[t * k + p] for
+ * n_tok tokens of k picks (x f32 [n_tok][H], or [n_tok][k][H] with
+ * x_per_pick; y f32 [n_tok][k][H]); no routing, shared expert or combine. An
+ * expert-parallel GPU runs it on the rows other GPUs sent it (k = 1, ids
+ * local to its experts). Workspace: moe_b200_experts_prefill_workspace_size. */
+size_t moe_b200_experts_prefill_workspace_size(const moe_layer_desc *layer, int64_t n_tok, int64_t k);
+int moe_b200_experts_prefill(const moe_layer_desc *layer, const float *x, int32_t x_per_pick, const int32_t *ids,
+                             int64_t n_tok, int64_t k, float *y, void *workspace, size_t workspace_bytes,
+                             moe_stream_t stream);
+
+/* No counterpart in the reference: the shared expert of every token,
+ * ys f32 [n_tok][H]; workspace as moe_b200_layer_prefill. */
+int moe_b200_shared_prefill(const moe_layer_desc *layer, const float *x, int64_t n_tok, float *ys, void *workspace,
+                            size_t workspace_bytes, moe_stream_t stream);
+
+/* No counterpart in the reference (upstream graph ops): out[t] = sum over p
+ * in order of weights[t][p] * y[t][p] (+ ys[t] when ys is not null). */
+int moe_b200_combine(const float *y, const float *weights, const float *ys, float *out, int64_t n_tok, int64_t H,
+                     int64_t k, moe_stream_t stream);
+
 /* No counterpart in the reference: 1 when moe_b200_layer_decode runs this
  * layer as one fused kernel for n_tok tokens (gate/up and down type pair with a
  * fused kernel, n_tok <= 8, n_tok * k <= 64, activations and tiles fit in

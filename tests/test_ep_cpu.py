@@ -101,3 +101,53 @@ def test_gloo_two_ranks_sum_to_the_layer():
     assert all(p.exitcode == 0 for p in procs)
     for rank, err, rng in res:
         assert err < 1e-5, (rank, err)        # oracle layer vs shares: float summation order only
+
+
+def _prefill_worker(rank, world, port, q):
+    """dispatch / combine of the expert-parallel prefill on gloo: every entry's
+    row reaches the rank owning its expert, and its output comes back to its
+    (token, pick) slot. The stand-in expert is y = (global expert + 1) * x."""
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import importlib
+    import torch
+    import torch.distributed as dist
+    ep = importlib.import_module("a6000-custom-kernels_b200.ep")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    E, k, H, n = 13, 3, 8, 7 + rank          # uneven expert slices, different token counts per rank
+    g = torch.Generator().manual_seed(100 + rank)
+    x = torch.randn((n, H), generator=g)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(n)]).to(torch.int32)
+    lo, hi = ep.expert_range(E, rank, world)
+    seen = []
+
+    def compute(rows, lids):
+        seen.append(int(lids.numel()))
+        if lids.numel():
+            assert int(lids.min()) >= 0 and int(lids.max()) < hi - lo
+        return rows * (lids.to(torch.float32) + lo + 1)[:, None]
+
+    y = ep.exchange(x, ids, E, world, compute)
+    ref = x[:, None, :] * (ids.to(torch.float32) + 1)[:, :, None]
+    err = float((y - ref).abs().max())
+    dist.destroy_process_group()
+    q.put((rank, err, seen[0]))
+
+
+def test_gloo_prefill_dispatch_combine():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29800 + os.getpid() % 1000
+    world = 3
+    procs = [ctx.Process(target=_prefill_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    res = [q.get(timeout=5) for _ in range(world)]
+    assert all(p.exitcode == 0 for p in procs)
+    for rank, err, n_recv in res:
+        assert err == 0.0, (rank, err)
+    assert sum(r[2] for r in res) == sum(3 * (7 + r) for r in range(world))   # every entry computed once

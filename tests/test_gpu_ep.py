@@ -91,3 +91,66 @@ def test_nccl_all_reduce_two_gpus():
     res = dict(q.get(timeout=5) for _ in range(2))
     assert all(p.exitcode == 0 for p in procs)
     assert all(e < 1e-5 for e in res.values()), res
+
+
+@pytest.mark.parametrize("world,types", [(2, (O.Q2_K, O.Q2_K, O.Q2_K)), (3, (O.Q4_K, O.Q4_K, O.Q6_K)),
+                                         (5, (O.Q3_K, O.Q3_K, O.Q2_K))])
+def test_prefill_emulated_ranks_equal_layer_prefill(pkg, cuda, world, types):
+    """Expert-parallel prefill (each rank its own prompt, experts spread over
+    the ranks, dispatch / combine by all-to-all) emulated on one GPU: every
+    rank's output equals the single-GPU layer prefill of its prompt bit for
+    bit (each (row, token) result is independent of which tokens share its
+    tile)."""
+    ep = _ep(pkg)
+    H, F, E, k = 1024, 512, 40, 8
+    full = pkg.MoELayer(H, F, E, k, {"gate": types[0], "up": types[1], "down": types[2]}, shared=True, seed=21)
+    ranks = [ep.EPMoELayer(full, r, world) for r in range(world)]
+    xs = [torch.from_numpy(activations((24 + 5 * r, H), seed=30 + r)).to(cuda) for r in range(world)]
+    lgs = [torch.from_numpy(zipf_logits(24 + 5 * r, E, seed=40 + r)).to(cuda) for r in range(world)]
+    outs = ep.prefill_emulated(ranks, xs, lgs)
+    assert pkg.moe_cache.device_error() == 0
+    for r in range(world):
+        ref = full.prefill(xs[r], lgs[r]).cpu().numpy()
+        np.testing.assert_array_equal(outs[r].cpu().numpy(), ref)
+
+
+def _nccl_prefill_worker(rank, world, port, q):
+    import importlib
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    ep = importlib.import_module("a6000-custom-kernels_b200.ep")
+    pkg.moe_cache.configure(enabled=True)
+    H, F, E, k = 1024, 512, 64, 8
+    full = pkg.MoELayer(H, F, E, k, {"gate": 10, "up": 10, "down": 10}, shared=True, seed=9, device=f"cuda:{rank}")
+    x = torch.from_numpy(activations((40 + 3 * rank, H), seed=50 + rank)).cuda()
+    lg = torch.from_numpy(zipf_logits(40 + 3 * rank, E, seed=60 + rank)).cuda()
+    ref = full.prefill(x, lg)
+    out = ep.EPMoELayer(full, rank, world).prefill(x, lg)
+    torch.cuda.synchronize()
+    err = float((out - ref).abs().max())
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((rank, err))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_prefill_all_to_all_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 1000
+    procs = [ctx.Process(target=_nccl_prefill_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert all(p.exitcode == 0 for p in procs)
+    assert all(e == 0.0 for e in res.values()), res
