@@ -52,8 +52,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=32, help="independent layer copies cycled by the timed loop")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=2000)
-    ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=2,
-                    help="BASELINE config; 2 (default) is the headline line, 1/3/5 print their own lines")
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=2,
+                    help="BASELINE config; 2 (default) is the headline line, 1/3/4/5 print their own lines")
+    ap.add_argument("--prompt", type=int, default=512, help="prefill tokens per rank (config 4)")
     ap.add_argument("--batch", type=int, default=1, help="decode tokens per step (configs 3 and 5)")
     return ap.parse_args()
 
@@ -665,12 +666,132 @@ def run_other_config(args):
         os.unlink(seed_path)
 
 
+def run_config4(args):
+    """Config 4: expert-parallel prefill through the config-3 stack (48
+    layers, per-tensor types from {Q2_K,Q3_K,Q4_K,Q6_K} drawn by seed). Every
+    rank holds 512 / N experts of each layer and prefills its own prompt of
+    --prompt tokens: route, dispatch all-to-all (NCCL), tensor-core expert
+    prefill on the rows it received, return all-to-all, shared expert,
+    weighted combine, residual add. N = 1 runs the single-GPU layer prefill
+    (no exchange). value = all ranks' prompt tokens / max-over-ranks time."""
+    import datetime
+    import importlib
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    ep = importlib.import_module("a6000-custom-kernels_b200.ep")
+    mc = pkg.moe_cache
+    mc.configure(enabled=True)
+    n_layers, B = 48, args.prompt
+    types = stack_types(n_layers)
+    lo, hi = ep.expert_range(E, rank, world)
+    layers = []
+    for l in range(n_layers):
+        L = pkg.MoELayer(H, F, hi - lo, K_TOP, types[l], shared=True, device=dev, seed=7000 + 97 * l + rank,
+                         name=f"blk.{l}")
+        layers.append(ep.EPMoELayer(L, rank, world, local=True, n_experts=E) if world > 1 else L)
+    rng = np.random.default_rng(33 + rank)
+    P = 2
+    xs_host = torch.from_numpy(rng.normal(0, 1, (P, B, H)).astype(np.float32)).pin_memory()
+    lg_np = np.zeros((n_layers, B, E), np.float32)
+    touched = 0
+    for l in range(n_layers):
+        perm = np.random.default_rng(1000 + l).permutation(E)
+        lg_np[l] = (-1.1 * np.log(perm + 1.0))[None, :] + rng.normal(0, 1, (B, E))
+        picks = np.argsort(-lg_np[l], axis=1, kind="stable")[:, :K_TOP]
+        touched += len(set(picks.reshape(-1).tolist())) * sum(
+            (F * H) * BYTES_PER_W[t] for t in types[l].values())
+    lgs = torch.from_numpy(lg_np).to(dev)
+    x = torch.empty((B, H), device=dev)
+    out = torch.empty((B, H), device=dev)
+    res_host = torch.empty((B, H), dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    xs_dev = xs_host.to(dev)
+
+    def step(i, e2e=False):
+        # a fresh prompt every step (the residual adds overwrite x): from HBM,
+        # or for the end-to-end number from pinned host memory
+        x.copy_(xs_host[i % P] if e2e else xs_dev[i % P], non_blocking=True)
+        for l in range(n_layers):
+            layers[l].prefill(x, lgs[l], out, stream=stream)
+            x.add_(out)
+        if e2e:
+            res_host.copy_(x, non_blocking=True)
+
+    W = max(args.warmup, 3)
+    K = max(1, min(args.steps, 20))
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(K):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    # end to end: each step copies its prompt in from pinned host memory and the result back
+    if world > 1:
+        dist.barrier()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record(stream)
+    for i in range(K):
+        step(i, e2e=True)
+    ev3.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = ev2.elapsed_time(ev3)
+    assert mc.device_error() == 0
+    if world > 1:
+        t = torch.tensor([ms, ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = float(t[0]), float(t[1])
+    tok = world * B * K
+    # launches per layer: routing 1, gate/up/down 4 each (grouping, quantize,
+    # gather, MMQ) + GLU 1, shared expert 3 x 4 + GLU 1, combine 1
+    launches = n_layers * (1 + 13 + 13 + 1) * K
+    if rank == 0:
+        gib = sum(sum(L.w[r].numel() for r in ("gate", "up", "down")) for L in layers) / 2 ** 30
+        line = {"metric": "MoE prefill tokens/s (expert-parallel)", "value": round(tok / (ms / 1e3), 2),
+                "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic",
+                "config": {"workload": f"config4: {n_layers}-layer config-3 stack ({gib:.1f} GiB of experts on rank 0), "
+                                       f"{B}-token prompt per rank, 512 experts over {world} GPU(s) "
+                                       f"({hi - lo} on rank 0), per-layer Zipf(1.1) top-8, shared expert, "
+                                       f"f32 residual; dispatch/combine by NCCL all-to-all" if world > 1 else
+                                       f"config4 on one GPU: {n_layers}-layer config-3 stack, {B}-token prompt, "
+                                       f"all 512 experts local (layer prefill, no exchange)",
+                           "global_batch": tok // K, "layers_per_step": n_layers,
+                           "parallelism": f"ep{world}"},
+                "expert_gbs_rank0": round(touched * K / (ms / 1e3) / 1e9, 1),
+                "e2e": {"value": round(tok / (ms_e2e / 1e3), 2), "unit": "tokens/s",
+                        "h2d_bytes_per_step": B * H * 4, "d2h_bytes_per_step": B * H * 4},
+                "gpu_launches": launches, "timing": "eager steps, device events, max over ranks"}
+        print(json.dumps(line), flush=True)
+    for L in layers:
+        L._ws.clear()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.config == 2:
         run_mine(args)
+    elif args.config == 4:
+        run_config4(args)
     else:
         run_other_config(args)
 
