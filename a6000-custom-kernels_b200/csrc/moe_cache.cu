@@ -781,10 +781,12 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x
 // One prefill MUL_MAT_ID: dst[(t * k + p) * rows + r] = row r of expert
 // ids[t][p] . x row (t, or t * k + p when x_per_pick). Tensor cores where
 // the type and shape allow (grouping, Q8_K quantization, B-tile gather, MMQ),
-// else the decode GEMV over chunks of 8 tokens.
+// else the decode GEMV over chunks of 8 tokens. With dst2 / src2 set (a
+// second tensor of the same type and shape, e.g. up beside gate), the second
+// product reuses the grouping and the B tiles.
 int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t n_tok, const int32_t *ids, int64_t k,
                 int64_t ids_stride, float *dst, char *workspace, size_t workspace_bytes, bool *used_tc,
-                cudaStream_t st) {
+                cudaStream_t st, const moe_tensor *src2 = nullptr, float *dst2 = nullptr) {
     *used_tc = false;
     if (!src0 || !src0->data || !x || !ids || !dst) return fail(MOE_ERR_INVALID, "null argument");
     if (n_tok < 1 || k < 1 || ids_stride < k) return fail(MOE_ERR_INVALID, "need n_tok >= 1, k >= 1, ids_stride >= k");
@@ -793,8 +795,13 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
         return fail(MOE_ERR_UNSUPPORTED, "expert tensor must be contiguous and 16-byte aligned");
     const int64_t K = src0->ne[0], rows = src0->ne[1], E = src0->ne[2];
     const int64_t x_rows = x_per_pick ? n_tok * k : n_tok;
-    const bool tc = moe::mmq_supported(src0->type, K, rows) && ptr_kind(src0->data) == 2 &&
-                    (src0->nb[2] % 16) == 0 && n_tok * k < (int64_t{1} << 30) && E <= 16384;
+    auto tc_ok = [&](const moe_tensor *t) {
+        return moe::mmq_supported(t->type, t->ne[0], t->ne[1]) && ptr_kind(t->data) == 2 && (t->nb[2] % 16) == 0 &&
+               contiguous(t) && aligned16(t->data) && n_tok * k < (int64_t{1} << 30) && t->ne[2] <= 16384;
+    };
+    const bool tc = tc_ok(src0);
+    const bool pair = src2 && dst2 && tc && tc_ok(src2) && src2->type == src0->type && src2->ne[0] == K &&
+                      src2->ne[1] == rows && src2->ne[2] == E;
     if (!tc) {
         // no tensor-core path: the decode GEMV over chunks of 8 tokens
         for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
@@ -813,41 +820,48 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
             const int rc = run_mmvq(c, st);
             if (rc) return rc;
         }
-        return MOE_OK;
+    } else {
+        const PrefillWs w = prefill_ws(src0, n_tok, k, x_rows, workspace);
+        if (!workspace || workspace_bytes < w.bytes)
+            return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
+        int rc = init_device_globals();
+        if (rc) return rc;
+        const int ntc = moe::mmq_chunk_tokens(src0->type);
+        CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
+                                 ntc, w.entries, w.chunks, w.n_chunks, g.d_err, st));
+        CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, x_rows, K, st));
+        // the gather reads activation row entry / k_div (entry = t * k + p)
+        CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries,
+                                  w.chunks, w.n_chunks, w.max_chunks, w.btiles, st));
+        for (int pass = 0; pass < (pair ? 2 : 1); ++pass) {
+            const moe_tensor *t = pass == 0 ? src0 : src2;
+            moe::MmqArgs a{};
+            a.dense = static_cast<const char *>(t->data);
+            a.expert_bytes = t->nb[2];
+            a.n_experts = static_cast<int32_t>(E);
+            a.K = static_cast<int32_t>(K);
+            a.nrows = static_cast<int32_t>(rows);
+            a.row_bytes = static_cast<uint32_t>(t->nb[1]);
+            a.btiles = w.btiles;
+            a.n_tok = static_cast<int32_t>(n_tok);
+            a.k = static_cast<int32_t>(k);
+            a.entries = w.entries;
+            a.chunks = w.chunks;
+            a.n_chunks = w.n_chunks;
+            a.dst = pass == 0 ? dst : dst2;
+            a.err = g.d_err;
+            const char *why = "";
+            cudaError_t ce = cudaSuccess;
+            rc = moe::launch_mmq(t->type, a, st, &why, &ce);
+            if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+            if (rc) return fail(rc, "%s", why);
+        }
+        *used_tc = true;
     }
-    const PrefillWs w = prefill_ws(src0, n_tok, k, x_rows, workspace);
-    if (!workspace || workspace_bytes < w.bytes)
-        return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
-    int rc = init_device_globals();
-    if (rc) return rc;
-    const int ntc = moe::mmq_chunk_tokens(src0->type);
-    CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E), ntc,
-                             w.entries, w.chunks, w.n_chunks, g.d_err, st));
-    CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, x_rows, K, st));
-    // the gather reads activation row entry / k_div (entry = t * k + p)
-    CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries,
-                              w.chunks, w.n_chunks, w.max_chunks, w.btiles, st));
-    moe::MmqArgs a{};
-    a.dense = static_cast<const char *>(src0->data);
-    a.expert_bytes = src0->nb[2];
-    a.n_experts = static_cast<int32_t>(E);
-    a.K = static_cast<int32_t>(K);
-    a.nrows = static_cast<int32_t>(rows);
-    a.row_bytes = static_cast<uint32_t>(src0->nb[1]);
-    a.btiles = w.btiles;
-    a.n_tok = static_cast<int32_t>(n_tok);
-    a.k = static_cast<int32_t>(k);
-    a.entries = w.entries;
-    a.chunks = w.chunks;
-    a.n_chunks = w.n_chunks;
-    a.dst = dst;
-    a.err = g.d_err;
-    const char *why = "";
-    cudaError_t ce = cudaSuccess;
-    rc = moe::launch_mmq(src0->type, a, st, &why, &ce);
-    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
-    if (rc) return fail(rc, "%s", why);
-    *used_tc = true;
+    if (src2 && dst2 && !pair) {   // the second tensor on its own
+        bool tc2 = false;
+        return run_prefill(src2, x, x_per_pick, n_tok, ids, k, ids_stride, dst2, workspace, workspace_bytes, &tc2, st);
+    }
     return MOE_OK;
 }
 
@@ -1305,9 +1319,9 @@ namespace {
 int experts_prefill(const moe_layer_desc *L, const float *x, bool x_per_pick, const int32_t *ids, int64_t n_tok,
                     int64_t k, const LayerPrefillWs &w, float *y, cudaStream_t st) {
     bool tc = false;
-    int rc = run_prefill(&L->gate, x, x_per_pick, n_tok, ids, k, k, w.g, w.scratch, w.scratch_bytes, &tc, st);
-    if (rc) return rc;
-    rc = run_prefill(&L->up, x, x_per_pick, n_tok, ids, k, k, w.u, w.scratch, w.scratch_bytes, &tc, st);
+    // gate and up: one grouping and B-tile gather when they share a type
+    int rc = run_prefill(&L->gate, x, x_per_pick, n_tok, ids, k, k, w.g, w.scratch, w.scratch_bytes, &tc, st, &L->up,
+                         w.u);
     if (rc) return rc;
     CK(moe::launch_glu(w.g, w.u, n_tok * k * L->F, L->glu_op, L->glu_limit, st));
     return run_prefill(&L->down, w.u, true, n_tok, ids, k, k, y, w.scratch, w.scratch_bytes, &tc, st);
@@ -1322,9 +1336,7 @@ int shared_prefill(const moe_layer_desc *L, const float *x, int64_t n_tok, const
     const moe_tensor su = shared_tensor(L->shared_up, L->up.type, H, F);
     const moe_tensor sd = shared_tensor(L->shared_down, L->down.type, F, H);
     CK(cudaMemsetAsync(w.zero_ids, 0, 4 * n_tok, st));
-    int rc = run_prefill(&sg, x, false, n_tok, w.zero_ids, 1, 1, w.sg, w.scratch, w.scratch_bytes, &tc, st);
-    if (rc) return rc;
-    rc = run_prefill(&su, x, false, n_tok, w.zero_ids, 1, 1, w.su, w.scratch, w.scratch_bytes, &tc, st);
+    int rc = run_prefill(&sg, x, false, n_tok, w.zero_ids, 1, 1, w.sg, w.scratch, w.scratch_bytes, &tc, st, &su, w.su);
     if (rc) return rc;
     CK(moe::launch_glu(w.sg, w.su, n_tok * F, L->glu_op, L->glu_limit, st));
     return run_prefill(&sd, w.su, false, n_tok, w.zero_ids, 1, 1, ys, w.scratch, w.scratch_bytes, &tc, st);

@@ -55,6 +55,7 @@ def parse():
     ap.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=2,
                     help="BASELINE config; 2 (default) is the headline line, 1/3/4/5 print their own lines")
     ap.add_argument("--prompt", type=int, default=512, help="prefill tokens per rank (config 4)")
+    ap.add_argument("--stack-layers", type=int, default=48, help="layers of the config-3/4 stack (48 in BASELINE)")
     ap.add_argument("--batch", type=int, default=1, help="decode tokens per step (configs 3 and 5)")
     return ap.parse_args()
 
@@ -689,7 +690,7 @@ def run_config4(args):
     ep = importlib.import_module("a6000-custom-kernels_b200.ep")
     mc = pkg.moe_cache
     mc.configure(enabled=True)
-    n_layers, B = 48, args.prompt
+    n_layers, B = args.stack_layers, args.prompt
     types = stack_types(n_layers)
     lo, hi = ep.expert_range(E, rank, world)
     layers = []
@@ -756,9 +757,9 @@ def run_config4(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
     tok = world * B * K
-    # launches per layer: routing 1, gate/up/down 4 each (grouping, quantize,
-    # gather, MMQ) + GLU 1, shared expert 3 x 4 + GLU 1, combine 1
-    launches = n_layers * (1 + 13 + 13 + 1) * K
+    # launches per layer: routing 1; gate + up 5 (one grouping, quantize and
+    # gather, two MMQ), GLU 1, down 4; the shared expert the same 10; combine 1
+    launches = n_layers * (1 + 10 + 10 + 1) * K
     if rank == 0:
         gib = sum(sum(L.w[r].numel() for r in ("gate", "up", "down")) for L in layers) / 2 ** 30
         line = {"metric": "MoE prefill tokens/s (expert-parallel)", "value": round(tok / (ms / 1e3), 2),
