@@ -112,6 +112,16 @@ def _declare(L):
         "moe_b200_experts_prefill": (i32, [ctypes.POINTER(MoeLayerDesc), vp, i32, vp, i64, i64, vp, vp, sz, vp]),
         "moe_b200_shared_prefill": (i32, [ctypes.POINTER(MoeLayerDesc), vp, i64, vp, vp, sz, vp]),
         "moe_b200_combine": (i32, [vp, vp, vp, vp, i64, i64, i64, vp]),
+        "moe_b200_ipc_alloc": (i32, [sz, ctypes.POINTER(vp)]),
+        "moe_b200_ipc_free": (i32, [vp]),
+        "moe_b200_ipc_handle": (i32, [vp, vp]),
+        "moe_b200_ipc_open": (i32, [vp, ctypes.POINTER(vp)]),
+        "moe_b200_ipc_close": (i32, [vp]),
+        "moe_b200_ep_dispatch": (i32, [vp, i32, i32, i64, vp, i64, i64, i64, vp, i64, vp, vp]),
+        "moe_b200_ep_wait": (i32, [vp, ctypes.c_uint32, vp]),
+        "moe_b200_ep_experts_rows_workspace_size": (sz, [ctypes.POINTER(MoeLayerDesc), i64]),
+        "moe_b200_ep_experts_rows": (i32, [ctypes.POINTER(MoeLayerDesc), vp, vp, i64, vp, vp, vp, vp, sz, vp]),
+        "moe_b200_ep_return": (i32, [vp, i32, i64, vp, vp, vp, i64, vp, vp]),
         "moe_b200_prefill_mul_mat_id": (i32, [ctypes.POINTER(MoeTensor), vp, i64, vp, i64, i64, vp, vp, sz,
                                              ctypes.POINTER(i32), vp]),
     }

@@ -42,12 +42,29 @@ int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why
 // tile prefix; launch_mmq runs the int8 MMQ over that tile list (-2 with *why
 // when the type or shape has no tensor-core path, -3 with *cuda_err).
 cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int ntc,
-                             int32_t *entries, int4 *chunks, int32_t *n_chunks, int *err, cudaStream_t st);
+                             int32_t *entries, int4 *chunks, int32_t *n_chunks, int *err, cudaStream_t st,
+                             bool skip_empty = false);
+// B tiles quantized from f32 rows x [rows][K] (one row per entry), or from
+// GLU(op, x, u) when u is set
+cudaError_t launch_mmq_gather_rows(const float *x, const float *u, int glu_op, float glu_limit, int K,
+                                   const int32_t *entries, const int4 *chunks, const int32_t *n_chunks, int ntc,
+                                   int64_t max_chunks, uint8_t *btiles, cudaStream_t st);
 // launch_mmq_gather writes the chunks' B tiles (MMQ layout) from the tokens'
 // Q8_K rows x8 [n_tok][K / 256]; max_chunks bounds the chunk count
 // (mmq_max_chunks).
 cudaError_t launch_mmq_gather(const uint8_t *x8, int K, int k, int ntc, const int32_t *entries, const int4 *chunks,
                               const int32_t *n_chunks, int64_t max_chunks, uint8_t *btiles, cudaStream_t st);
+// Expert-parallel exchange over peer memory (moe_ep.cu). peer_ptrs: [5][W]
+// device pointers as seen from this GPU (received rows, their ids, their
+// source entries, returned outputs, arrival counters) of every GPU; scratch:
+// 16 zeroed uint32 per GPU (cursors and block counters, reset after use).
+cudaError_t launch_ep_dispatch(const void *const *peer_ptrs, int W, int me, int cap, const int32_t *ids,
+                               int n_entries, int k, int E, const float *x, int H, uint32_t *scratch, int *err,
+                               cudaStream_t st);
+cudaError_t launch_ep_return(const void *const *peer_ptrs, int W, int cap, const int32_t *ids, const int32_t *src,
+                             const float *y, int H, uint32_t *scratch, cudaStream_t st);
+cudaError_t launch_ep_wait(const uint32_t *flag, uint32_t target, uint64_t timeout_ns, int *err, cudaStream_t st);
+
 // tokens per chunk of the tensor-core path for a weight type (0: none)
 int mmq_chunk_tokens(int type);
 bool mmq_supported(int type, int64_t K, int64_t nrows);

@@ -74,6 +74,7 @@ struct State {
     std::vector<Entry *> all;
     uint32_t *d_stats = nullptr, *h_stats = nullptr, *d_clock = nullptr;
     int *d_err = nullptr;
+    uint64_t timeout_ns_ep = 2000000000ull;   // expert-parallel arrival waits
     uint32_t h_clock = 0;
     int device = -1;
     std::unordered_map<uint32_t, int> admission;
@@ -1400,6 +1401,183 @@ int moe_b200_combine(const float *y, const float *weights, const float *ys, floa
     if (!y || !weights || !out || n_tok < 1 || H < 1 || k < 1) return fail(MOE_ERR_INVALID, "bad combine arguments");
     CK(moe::launch_combine(y, weights, ys, out, n_tok, H, k, reinterpret_cast<cudaStream_t>(stream)));
     return MOE_OK;
+}
+
+// ---- expert-parallel exchange over peer memory ------------------------------
+
+int moe_b200_ipc_alloc(size_t bytes, void **ptr) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!ptr || bytes == 0) return fail(MOE_ERR_INVALID, "null pointer or zero size");
+    *ptr = nullptr;
+    if (cudaMalloc(ptr, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MOE_ERR_OOM, "cudaMalloc of %zu bytes failed", bytes);
+    }
+    CK(cudaMemset(*ptr, 0, bytes));
+    return MOE_OK;
+}
+
+int moe_b200_ipc_free(void *ptr) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (ptr) CK(cudaFree(ptr));
+    return MOE_OK;
+}
+
+int moe_b200_ipc_handle(const void *ptr, void *handle) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!ptr || !handle) return fail(MOE_ERR_INVALID, "null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == MOE_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, const_cast<void *>(ptr)));
+    memcpy(handle, &h, sizeof(h));
+    return MOE_OK;
+}
+
+int moe_b200_ipc_open(const void *handle, void **ptr) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!handle || !ptr) return fail(MOE_ERR_INVALID, "null argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    CK(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return MOE_OK;
+}
+
+int moe_b200_ipc_close(void *ptr) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (ptr) CK(cudaIpcCloseMemHandle(ptr));
+    return MOE_OK;
+}
+
+int moe_b200_ep_dispatch(const void *const *peer_ptrs, int32_t world, int32_t rank, int64_t cap, const int32_t *ids,
+                         int64_t n_entries, int64_t k, int64_t n_experts, const float *x, int64_t H, void *scratch,
+                         moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!peer_ptrs || !ids || !x || !scratch || world < 1 || world > 8 || rank < 0 || rank >= world || k < 1 ||
+        n_entries < 0 || n_entries > cap || H % 4 || cap >= (int64_t{1} << 31) / world)
+        return fail(MOE_ERR_INVALID, "bad expert-parallel dispatch arguments");
+    int rc = init_device_globals();
+    if (rc) return rc;
+    CK(moe::launch_ep_dispatch(peer_ptrs, world, rank, static_cast<int>(cap), ids, static_cast<int>(n_entries),
+                               static_cast<int>(k), static_cast<int>(n_experts), x, static_cast<int>(H),
+                               static_cast<uint32_t *>(scratch), g.d_err, reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap, const int32_t *ids,
+                       const int32_t *src, const float *y, int64_t H, void *scratch, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!peer_ptrs || !ids || !src || !y || !scratch || world < 1 || world > 8 || H % 4)
+        return fail(MOE_ERR_INVALID, "bad expert-parallel return arguments");
+    CK(moe::launch_ep_return(peer_ptrs, world, static_cast<int>(cap), ids, src, y, static_cast<int>(H),
+                             static_cast<uint32_t *>(scratch), reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+int moe_b200_ep_wait(const uint32_t *flag, uint32_t target, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!flag) return fail(MOE_ERR_INVALID, "null flag");
+    int rc = init_device_globals();
+    if (rc) return rc;
+    CK(moe::launch_ep_wait(flag, target, g.timeout_ns_ep, g.d_err, reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+namespace {
+
+// The received rows' experts: gate and up (one grouping and quantizing
+// gather from the f32 rows), down from GLU(gate, up) quantized in the
+// gather; every type on the tensor cores. Empty slots (id -1) are skipped.
+struct EpRowsWs {
+    int32_t *entries, *n_chunks;
+    int4 *chunks;
+    uint8_t *btiles;
+    int64_t max_chunks;
+    size_t bytes;
+};
+
+EpRowsWs ep_rows_ws(const moe_layer_desc *L, int64_t n_rows, char *base) {
+    EpRowsWs w{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
+    w.entries = reinterpret_cast<int32_t *>(take(4 * n_rows));
+    w.max_chunks = moe::mmq_max_chunks(n_rows, L->n_experts, 32);
+    w.chunks = reinterpret_cast<int4 *>(take(16 * static_cast<size_t>(w.max_chunks)));
+    w.n_chunks = reinterpret_cast<int32_t *>(take(4));
+    const int64_t kmax = L->H > L->F ? L->H : L->F;
+    w.btiles = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(w.max_chunks) * (kmax / 256) * moe::MMQ_BT_BYTES));
+    w.bytes = off;
+    return w;
+}
+
+int mmq_call(const moe_tensor *t, const EpRowsWs &w, int64_t n_rows, float *dst, cudaStream_t st) {
+    moe::MmqArgs a{};
+    a.dense = static_cast<const char *>(t->data);
+    a.expert_bytes = t->nb[2];
+    a.n_experts = static_cast<int32_t>(t->ne[2]);
+    a.K = static_cast<int32_t>(t->ne[0]);
+    a.nrows = static_cast<int32_t>(t->ne[1]);
+    a.row_bytes = static_cast<uint32_t>(t->nb[1]);
+    a.btiles = w.btiles;
+    a.n_tok = static_cast<int32_t>(n_rows);
+    a.k = 1;
+    a.entries = w.entries;
+    a.chunks = w.chunks;
+    a.n_chunks = w.n_chunks;
+    a.dst = dst;
+    a.err = g.d_err;
+    const char *why = "";
+    cudaError_t ce = cudaSuccess;
+    const int rc = moe::launch_mmq(t->type, a, st, &why, &ce);
+    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+    if (rc) return fail(rc, "%s", why);
+    return MOE_OK;
+}
+
+}  // namespace
+
+size_t moe_b200_ep_experts_rows_workspace_size(const moe_layer_desc *L, int64_t n_rows) {
+    if (!L || n_rows < 1) return 0;
+    return ep_rows_ws(L, n_rows, nullptr).bytes;
+}
+
+int moe_b200_ep_experts_rows(const moe_layer_desc *L, const float *x, const int32_t *ids, int64_t n_rows, float *g_out,
+                             float *u_out, float *y, void *workspace, size_t workspace_bytes, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || !x || !ids || !g_out || !u_out || !y || n_rows < 1) return fail(MOE_ERR_INVALID, "null argument");
+    for (const moe_tensor *t : {&L->gate, &L->up, &L->down}) {
+        if (!moe::mmq_supported(t->type, t->ne[0], t->ne[1]) || !t->data || ptr_kind(t->data) != 2 || !contiguous(t) ||
+            !aligned16(t->data) || (t->nb[2] % 16) != 0 || t->ne[2] != L->n_experts)
+            return fail(MOE_ERR_UNSUPPORTED, "expert-parallel rows need tensor-core types in device memory");
+    }
+    const EpRowsWs w = ep_rows_ws(L, n_rows, static_cast<char *>(workspace));
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
+    int rc = init_device_globals();
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int E = static_cast<int>(L->n_experts), n = static_cast<int>(n_rows);
+    int ntc = moe::mmq_chunk_tokens(L->gate.type);
+    CK(moe::launch_mmq_group(ids, 1, n, 1, E, ntc, w.entries, w.chunks, w.n_chunks, g.d_err, st, true));
+    CK(moe::launch_mmq_gather_rows(x, nullptr, 0, 0.f, static_cast<int>(L->H), w.entries, w.chunks, w.n_chunks, ntc,
+                                   w.max_chunks, w.btiles, st));
+    rc = mmq_call(&L->gate, w, n_rows, g_out, st);
+    if (rc) return rc;
+    if (moe::mmq_chunk_tokens(L->up.type) != ntc) {
+        ntc = moe::mmq_chunk_tokens(L->up.type);
+        CK(moe::launch_mmq_group(ids, 1, n, 1, E, ntc, w.entries, w.chunks, w.n_chunks, g.d_err, st, true));
+        CK(moe::launch_mmq_gather_rows(x, nullptr, 0, 0.f, static_cast<int>(L->H), w.entries, w.chunks, w.n_chunks,
+                                       ntc, w.max_chunks, w.btiles, st));
+    }
+    rc = mmq_call(&L->up, w, n_rows, u_out, st);
+    if (rc) return rc;
+    if (moe::mmq_chunk_tokens(L->down.type) != ntc) {
+        ntc = moe::mmq_chunk_tokens(L->down.type);
+        CK(moe::launch_mmq_group(ids, 1, n, 1, E, ntc, w.entries, w.chunks, w.n_chunks, g.d_err, st, true));
+    }
+    CK(moe::launch_mmq_gather_rows(g_out, u_out, L->glu_op, L->glu_limit, static_cast<int>(L->F), w.entries, w.chunks,
+                                   w.n_chunks, ntc, w.max_chunks, w.btiles, st));
+    return mmq_call(&L->down, w, n_rows, y, st);
 }
 
 int moe_b200_layer_fused(const moe_layer_desc *L, int64_t n_tok) {

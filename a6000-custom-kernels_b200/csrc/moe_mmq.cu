@@ -14,13 +14,14 @@ namespace moe {
 // pick) grouped by expert, and the chunk table: an expert's entries form
 // chunks of up to ntc, chunk c = {expert, first entry, token count}, chunks of
 // an expert consecutive, *n_chunks their count. Entry order inside an expert
-// does not change any result.
+// does not change any result. With skip_empty, id -1 marks an empty slot
+// (expert-parallel receive regions) and is left out without an error.
 // ---------------------------------------------------------------------------
 constexpr int MMQ_GROUP_REG = 8;   // ids kept in registers per thread (n_tok * k <= 8192)
 
 __global__ void __launch_bounds__(1024) mmq_group_kernel(const int32_t *__restrict__ ids, int64_t ids_stride, int n_tok,
-                                                         int k, int E, int ntc, int32_t *entries, int4 *chunks,
-                                                         int32_t *n_chunks, int *err) {
+                                                         int k, int E, int ntc, int skip_empty, int32_t *entries,
+                                                         int4 *chunks, int32_t *n_chunks, int *err) {
     extern __shared__ int32_t cnt[];   // [E] counts, then scatter cursors
     __shared__ int32_t warp_sum[32];
     __shared__ int32_t carry[2];
@@ -42,9 +43,9 @@ __global__ void __launch_bounds__(1024) mmq_group_kernel(const int32_t *__restri
     }
     // warp-aggregated increments: one atomic per distinct expert in the warp
     auto count = [&](int x, bool valid) {
-        const bool bad = valid && (x < 0 || x >= E);
+        const bool bad = valid && (x >= E || (x < 0 && !(skip_empty && x == -1)));   // -1: an empty slot
         if (bad) set_error(err, DERR_BAD_ID);
-        const bool use = valid && !bad;
+        const bool use = valid && !bad && x >= 0;
         const unsigned peers = __match_any_sync(0xffffffffu, use ? x : -1);
         if (use && lane == __ffs(peers) - 1) atomicAdd(&cnt[x], __popc(peers));
     };
@@ -187,6 +188,66 @@ __global__ void __launch_bounds__(256) mmq_gather_q8K_kernel(const uint8_t *__re
         mmq_gather_slot(x8, nsb, k, ntc, entries, chunks, btiles, wg, lane);
 }
 
+
+// The same B tiles quantized here from f32 rows, one row per entry (k = 1):
+// row r = x[r], or with u set GLU(op, x[r], u[r]) (the down projection's
+// input made from the gate and up outputs); llama.cpp's quantize_row_q8_K_ref
+// and the same GLU as glu_kernel, so the bits equal quantize_act of the f32 h.
+__global__ void __launch_bounds__(256) mmq_gather_rows_kernel(const float *__restrict__ x, const float *__restrict__ u,
+                                                              int glu_op, float glu_limit, int K,
+                                                              const int32_t *__restrict__ entries,
+                                                              const int4 *__restrict__ chunks,
+                                                              const int32_t *__restrict__ n_chunks, int ntc,
+                                                              uint8_t *__restrict__ btiles) {
+    const int lane = threadIdx.x & 31;
+    const int nsb = K / 256;
+    const int n_items = *n_chunks * ntc;
+    for (int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wg < n_items; wg += (gridDim.x * blockDim.x) >> 5) {
+        const int gc = wg / ntc, j = wg - gc * ntc;
+        const int4 ch = chunks[gc];
+        const int nt = ch.z, N = mmq_chunk_n(nt), CS = 16 * N;
+        if (j >= N) continue;
+        const int row = j < nt ? entries[ch.y + j] : -1;
+        for (int sb = 0; sb < nsb; ++sb) {
+            uint8_t *bt = btiles + (static_cast<size_t>(gc) * nsb + sb) * MMQ_BT_BYTES;
+            uint8_t *tok = bt + MMQ_BT_HEAD + (j >> 3) * 128 + (j & 7) * 16;
+            int8_t q[8];
+            int s = 0;
+            float d = 0.f;
+            if (row >= 0) {
+                const float *xr = x + static_cast<size_t>(row) * K + sb * 256 + lane * 8;
+                const float4 a0 = *reinterpret_cast<const float4 *>(xr), a1 = *reinterpret_cast<const float4 *>(xr + 4);
+                float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                if (u) {
+                    const float *ur = u + static_cast<size_t>(row) * K + sb * 256 + lane * 8;
+                    const float4 b0 = *reinterpret_cast<const float4 *>(ur), b1 = *reinterpret_cast<const float4 *>(ur + 4);
+                    const float w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[i] = glu_apply(glu_op, v[i], w[i], glu_limit);
+                }
+                d = quant_q8K_vals(v, lane, q, s);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) q[i] = 0;
+            }
+            uint32_t lo4 = 0, hi4 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lo4 |= static_cast<uint32_t>(static_cast<uint8_t>(q[i])) << (8 * i);
+                hi4 |= static_cast<uint32_t>(static_cast<uint8_t>(q[4 + i])) << (8 * i);
+            }
+            *reinterpret_cast<uint2 *>(tok + (lane >> 1) * CS + 8 * (lane & 1)) = make_uint2(lo4, hi4);
+            if ((lane & 1) == 0) {
+                tok[16 * CS + (lane >> 1)] = static_cast<uint8_t>((s >> 4) & 0xFF);
+                tok[17 * CS + (lane >> 1)] = static_cast<uint8_t>(s & 15);
+            }
+            if (lane == 0) reinterpret_cast<float *>(bt)[j] = d;
+            const int pair = s + __shfl_down_sync(0xffffffffu, s, 2);
+            if ((lane & 3) == 0)
+                reinterpret_cast<int16_t *>(bt + MMQ_BT_BS2 + 16 * j)[lane >> 2] = static_cast<int16_t>(pair);
+        }
+    }
+}
 
 // ---------------------------------------------------------------------------
 // The grouped GEMM
@@ -779,14 +840,16 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
 }
 
 cudaError_t launch_mmq_group(const int32_t *ids, int64_t ids_stride, int n_tok, int k, int E, int ntc,
-                             int32_t *entries, int4 *chunks, int32_t *n_chunks, int *err, cudaStream_t st) {
+                             int32_t *entries, int4 *chunks, int32_t *n_chunks, int *err, cudaStream_t st,
+                             bool skip_empty) {
     const size_t smem = static_cast<size_t>(E) * sizeof(int32_t);
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(mmq_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
-    mmq_group_kernel<<<1, 1024, smem, st>>>(ids, ids_stride, n_tok, k, E, ntc, entries, chunks, n_chunks, err);
+    mmq_group_kernel<<<1, 1024, smem, st>>>(ids, ids_stride, n_tok, k, E, ntc, skip_empty ? 1 : 0, entries, chunks,
+                                            n_chunks, err);
     return cudaGetLastError();
 }
 
@@ -798,6 +861,18 @@ cudaError_t launch_mmq_gather(const uint8_t *x8, int K, int k, int ntc, const in
     const int64_t blocks = (max_chunks * ntc + 7) / 8;   // one warp per token slot, 8 warps a block
     const int grid = static_cast<int>(blocks < 8 * n_sm ? (blocks > 0 ? blocks : 1) : 8 * n_sm);
     mmq_gather_q8K_kernel<<<grid, 256, 0, st>>>(x8, K / 256, k, ntc, entries, chunks, n_chunks, btiles);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mmq_gather_rows(const float *x, const float *u, int glu_op, float glu_limit, int K,
+                                   const int32_t *entries, const int4 *chunks, const int32_t *n_chunks, int ntc,
+                                   int64_t max_chunks, uint8_t *btiles, cudaStream_t st) {
+    int dev = 0, n_sm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t blocks = (max_chunks * ntc + 7) / 8;   // one warp per token slot, 8 warps a block
+    const int grid = static_cast<int>(blocks < 8 * n_sm ? (blocks > 0 ? blocks : 1) : 8 * n_sm);
+    mmq_gather_rows_kernel<<<grid, 256, 0, st>>>(x, u, glu_op, glu_limit, K, entries, chunks, n_chunks, ntc, btiles);
     return cudaGetLastError();
 }
 

@@ -186,6 +186,128 @@ def exchange(x, ids, n_experts, world, compute, group=None):
     return y.view(n, k, H)
 
 
+class PeerExchange:
+    """One GPU's buffers for the expert-parallel prefill exchange over NVLink
+    peer memory, and the other GPUs' (opened by CUDA IPC): received rows x
+    [W * cap][H], their local expert ids and source entries [W * cap], the
+    outputs of this GPU's own entries y_ret [cap][H], arrival counters [2].
+    cap = the entries one GPU sends per layer (prompt tokens x k). With
+    `local_peers` (ranks emulated in one process on one GPU) the other ranks'
+    buffers are used directly instead of IPC."""
+
+    NAMES = ("x", "ids", "src", "y_ret", "flags")
+
+    def __init__(self, H, cap, rank, world, group=None, local_peers=None):
+        self.H, self.cap, self.rank, self.world = H, cap, rank, world
+        sizes = {"x": 4 * world * cap * H, "ids": 4 * world * cap, "src": 4 * world * cap, "y_ret": 4 * cap * H,
+                 "flags": 256}
+        self.own = {}
+        for name in self.NAMES:
+            p = ctypes.c_void_p()
+            check(lib().moe_b200_ipc_alloc(sizes[name], ctypes.byref(p)))
+            self.own[name] = p.value
+        p = ctypes.c_void_p()
+        check(lib().moe_b200_ipc_alloc(64, ctypes.byref(p)))
+        self.scratch = p.value
+        self.opened = []
+        self.local_peers = local_peers
+        self.calls = 0
+        self.group = group
+
+    def connect(self, peers=None):
+        """Build the [5][W] pointer table: IPC handles over the process group,
+        or the emulated ranks' own buffers."""
+        W = self.world
+        table = [[0] * W for _ in self.NAMES]
+        if peers is not None:
+            for r, ex in enumerate(peers):
+                for i, name in enumerate(self.NAMES):
+                    table[i][r] = ex.own[name]
+        else:
+            import torch.distributed as dist
+            mine = {}
+            for name in self.NAMES:
+                h = (ctypes.c_char * 64)()
+                check(lib().moe_b200_ipc_handle(self.own[name], h))
+                mine[name] = bytes(h)
+            every = [None] * W
+            dist.all_gather_object(every, mine, group=self.group)
+            for r in range(W):
+                for i, name in enumerate(self.NAMES):
+                    if r == self.rank:
+                        table[i][r] = self.own[name]
+                    else:
+                        p = ctypes.c_void_p()
+                        h = (ctypes.c_char * 64).from_buffer_copy(every[r][name])
+                        check(lib().moe_b200_ipc_open(h, ctypes.byref(p)))
+                        self.opened.append(p.value)
+                        table[i][r] = p.value
+        self.table = (ctypes.c_void_p * (5 * W))(*[v for row in table for v in row])
+        return self
+
+    def close(self):
+        for p in self.opened:
+            lib().moe_b200_ipc_close(p)
+        self.opened = []
+        for p in list(self.own.values()) + [self.scratch]:
+            lib().moe_b200_ipc_free(p)
+        self.own = {}
+
+
+def prefill_p2p_stages(L, ex, x, logits, stream=None):
+    """Stage 1 of a layer on one rank: route and dispatch (peer stores)."""
+    n, k = x.shape[0], L.k
+    assert n * k <= ex.cap
+    ids, w = L.route(logits, stream)
+    check(lib().moe_b200_ep_dispatch(ex.table, L.world, L.rank, ex.cap, _ptr(ids), n * k, k, L.E, _ptr(x), L.H,
+                                     ex.scratch, _stream(stream)))
+    ex.calls += 1
+    return w
+
+
+def _ep_rows(L, ex, stream=None):
+    """Stage 2 on an owner: its experts on every received row, outputs back."""
+    W, rows = L.world, L.world * ex.cap
+    key = ("rows", rows)
+    bufs = L._ws.get(key)
+    if bufs is None:
+        nbytes = lib().moe_b200_ep_experts_rows_workspace_size(ctypes.byref(L.desc), rows)
+        bufs = (torch.empty(nbytes, dtype=torch.uint8, device=L.device),
+                torch.empty((rows, L.F), dtype=torch.float32, device=L.device),
+                torch.empty((rows, L.F), dtype=torch.float32, device=L.device),
+                torch.empty((rows, L.H), dtype=torch.float32, device=L.device))
+        L._ws[key] = bufs
+    ws, g, u, y = bufs
+    check(lib().moe_b200_ep_experts_rows(ctypes.byref(L.desc), ex.own["x"], ex.own["ids"], rows, _ptr(g), _ptr(u),
+                                         _ptr(y), _ptr(ws), ws.numel(), _stream(stream)))
+    check(lib().moe_b200_ep_return(ex.table, W, ex.cap, ex.own["ids"], ex.own["src"], _ptr(y), L.H, ex.scratch,
+                                   _stream(stream)))
+
+
+def prefill_p2p(L, ex, x, logits, out=None, stream=None):
+    """One layer of the expert-parallel prefill with the exchange over peer
+    memory: route, dispatch, wait for every GPU's rows, the owned experts on
+    them, return, wait for every owner's outputs, shared expert and combine.
+    Nothing waits on the host: the stream carries every dependency."""
+    w = prefill_p2p_stages(L, ex, x, logits, stream)
+    target = L.world * ex.calls
+    check(lib().moe_b200_ep_wait(ex.own["flags"], target, _stream(stream)))
+    _ep_rows(L, ex, stream)
+    check(lib().moe_b200_ep_wait(ex.own["flags"] + 4, target, _stream(stream)))
+    n = x.shape[0]
+    return L.finish(x, w, ex.own["y_ret"], out, stream)
+
+
+def prefill_p2p_emulated(ranks, exs, xs, logits):
+    """prefill_p2p of len(ranks) ranks in ONE process on one GPU, stage by
+    stage over all ranks (every dispatch before any owner reads, every return
+    before any source combines), so no wait is left pending."""
+    ws_ = [prefill_p2p_stages(L, ex, xs[r], logits[r]) for r, (L, ex) in enumerate(zip(ranks, exs))]
+    for L, ex in zip(ranks, exs):
+        _ep_rows(L, ex)
+    return [L.finish(xs[r], ws_[r], ex.own["y_ret"]) for r, (L, ex) in enumerate(zip(ranks, exs))]
+
+
 def prefill_emulated(ranks, xs, logits):
     """The expert-parallel prefill of len(ranks) ranks in ONE process (one GPU):
     the all-to-alls become slicing; every other step is the ranks' own. For

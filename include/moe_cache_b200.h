@@ -281,6 +281,42 @@ int moe_b200_shared_prefill(const moe_layer_desc *layer, const float *x, int64_t
 int moe_b200_combine(const float *y, const float *weights, const float *ys, float *out, int64_t n_tok, int64_t H,
                      int64_t k, moe_stream_t stream);
 
+/* No counterpart in the reference: expert-parallel prefill exchange over
+ * NVLink peer memory (no host round trip per layer). Every GPU allocates its
+ * exchange buffers with moe_b200_ipc_alloc (zero-filled; cudaMalloc'd so a
+ * CUDA IPC handle covers exactly the buffer), shares handles
+ * (moe_b200_ipc_handle, MOE_IPC_HANDLE_BYTES each) and opens the others'
+ * (moe_b200_ipc_open). Per GPU: x f32 [W * cap][H] received rows (region s:
+ * rows from GPU s; cap = entries per GPU, n_tok * k), ids int32 [W * cap]
+ * (local expert, -1 = empty), src int32 [W * cap] (entry t * k + p at the
+ * source), y_ret f32 [cap][H] (this GPU's entries' outputs), flags uint32[2]
+ * (dispatch and return arrivals, counting up). peer_ptrs is a host array
+ * [5][W] of those five pointers for every GPU as seen from the caller.
+ * moe_b200_ep_dispatch writes this GPU's entries into their owners' regions
+ * and counts one arrival at every GPU; moe_b200_ep_wait (a bounded device
+ * wait; timeout -> device error word) holds the stream until a counter
+ * reaches target (W per layer call); moe_b200_ep_experts_rows runs an
+ * owner's experts on its received rows (gate, up, GLU, down on the tensor
+ * cores; empty slots skipped); moe_b200_ep_return writes the outputs back
+ * into the sources' y_ret and counts one return arrival at every GPU.
+ * scratch: 16 zeroed uint32 of device memory per GPU. */
+#define MOE_IPC_HANDLE_BYTES 64
+int moe_b200_ipc_alloc(size_t bytes, void **ptr);
+int moe_b200_ipc_free(void *ptr);
+int moe_b200_ipc_handle(const void *ptr, void *handle);
+int moe_b200_ipc_open(const void *handle, void **ptr);
+int moe_b200_ipc_close(void *ptr);
+int moe_b200_ep_dispatch(const void *const *peer_ptrs, int32_t world, int32_t rank, int64_t cap, const int32_t *ids,
+                         int64_t n_entries, int64_t k, int64_t n_experts, const float *x, int64_t H, void *scratch,
+                         moe_stream_t stream);
+int moe_b200_ep_wait(const uint32_t *flag, uint32_t target, moe_stream_t stream);
+size_t moe_b200_ep_experts_rows_workspace_size(const moe_layer_desc *layer, int64_t n_rows);
+int moe_b200_ep_experts_rows(const moe_layer_desc *layer, const float *x, const int32_t *ids, int64_t n_rows,
+                             float *gate_out, float *up_out, float *y, void *workspace, size_t workspace_bytes,
+                             moe_stream_t stream);
+int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap, const int32_t *ids,
+                       const int32_t *src, const float *y, int64_t H, void *scratch, moe_stream_t stream);
+
 /* No counterpart in the reference: 1 when moe_b200_layer_decode runs this
  * layer as one fused kernel for n_tok tokens (gate/up and down type pair with a
  * fused kernel, n_tok <= 8, n_tok * k <= 64, activations and tiles fit in

@@ -154,3 +154,85 @@ def test_nccl_prefill_all_to_all_two_gpus():
     res = dict(q.get(timeout=5) for _ in range(2))
     assert all(p.exitcode == 0 for p in procs)
     assert all(e == 0.0 for e in res.values()), res
+
+
+@pytest.mark.parametrize("world,types", [(2, (O.Q2_K, O.Q2_K, O.Q2_K)), (3, (O.Q4_K, O.Q4_K, O.Q6_K)),
+                                         (4, (O.Q3_K, O.Q3_K, O.Q2_K))])
+def test_prefill_peer_exchange_emulated(pkg, cuda, world, types):
+    """The peer-memory exchange (dispatch straight into the owners' regions,
+    empty slots marked -1, the owners' experts on the received rows with the
+    quantization and the GLU inside the gathers, outputs written back) with
+    the ranks emulated on one GPU: every rank's output equals the single-GPU
+    layer prefill of its prompt bit for bit, over two layer calls (the
+    arrival counters and regions are reused)."""
+    ep = _ep(pkg)
+    H, F, E, k = 1024, 512, 40, 8
+    full = pkg.MoELayer(H, F, E, k, {"gate": types[0], "up": types[1], "down": types[2]}, shared=True, seed=23)
+    ranks = [ep.EPMoELayer(full, r, world) for r in range(world)]
+    n = [24 + 5 * r for r in range(world)]
+    cap = max(n) * k
+    exs = [ep.PeerExchange(H, cap, r, world) for r in range(world)]
+    for ex in exs:
+        ex.connect(peers=exs)
+    try:
+        for call in range(2):
+            xs = [torch.from_numpy(activations((n[r], H), seed=70 + 10 * call + r)).to(cuda) for r in range(world)]
+            lgs = [torch.from_numpy(zipf_logits(n[r], E, seed=90 + 10 * call + r)).to(cuda) for r in range(world)]
+            outs = ep.prefill_p2p_emulated(ranks, exs, xs, lgs)
+            assert pkg.moe_cache.device_error() == 0
+            for r in range(world):
+                np.testing.assert_array_equal(outs[r].cpu().numpy(), full.prefill(xs[r], lgs[r]).cpu().numpy())
+    finally:
+        torch.cuda.synchronize()
+        for ex in exs:
+            ex.close()
+
+
+def _p2p_worker(rank, world, port, q):
+    import importlib
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    ep = importlib.import_module("a6000-custom-kernels_b200.ep")
+    pkg.moe_cache.configure(enabled=True)
+    H, F, E, k = 1024, 512, 64, 8
+    full = pkg.MoELayer(H, F, E, k, {"gate": 10, "up": 10, "down": 12}, shared=True, seed=9, device=f"cuda:{rank}")
+    L = ep.EPMoELayer(full, rank, world)
+    n = 40 + 3 * rank
+    ex = ep.PeerExchange(H, 43 * k, rank, world).connect()
+    errs = []
+    for call in range(3):
+        x = torch.from_numpy(activations((n, H), seed=50 + 7 * call + rank)).cuda()
+        lg = torch.from_numpy(zipf_logits(n, E, seed=60 + 7 * call + rank)).cuda()
+        ref = full.prefill(x, lg)
+        out = ep.prefill_p2p(L, ex, x, lg)
+        torch.cuda.synchronize()
+        errs.append(float((out - ref).abs().max()))
+    code = pkg.moe_cache.device_error()
+    dist.barrier()
+    ex.close()
+    dist.destroy_process_group()
+    q.put((rank, max(errs), code))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_prefill_peer_exchange_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29650 + os.getpid() % 1000
+    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    res = [q.get(timeout=5) for _ in range(2)]
+    assert all(p.exitcode == 0 for p in procs)
+    for rank, err, code in res:
+        assert code == 0 and err == 0.0, (rank, err, code)
