@@ -56,6 +56,8 @@ def parse():
                     help="BASELINE config; 2 (default) is the headline line, 1/3/4/5 print their own lines")
     ap.add_argument("--prompt", type=int, default=512, help="prefill tokens per rank (config 4)")
     ap.add_argument("--stack-layers", type=int, default=48, help="layers of the config-3/4 stack (48 in BASELINE)")
+    ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="config 4 dispatch/combine: peer-memory kernels (default) or NCCL all-to-all")
     ap.add_argument("--batch", type=int, default=1, help="decode tokens per step (configs 3 and 5)")
     return ap.parse_args()
 
@@ -710,6 +712,9 @@ def run_config4(args):
         touched += len(set(picks.reshape(-1).tolist())) * sum(
             (F * H) * BYTES_PER_W[t] for t in types[l].values())
     lgs = torch.from_numpy(lg_np).to(dev)
+    ex = None
+    if world > 1 and args.ep_exchange == "p2p":
+        ex = ep.PeerExchange(H, B * K_TOP, rank, world).connect()
     x = torch.empty((B, H), device=dev)
     out = torch.empty((B, H), device=dev)
     res_host = torch.empty((B, H), dtype=torch.float32).pin_memory()
@@ -722,7 +727,10 @@ def run_config4(args):
         # or for the end-to-end number from pinned host memory
         x.copy_(xs_host[i % P] if e2e else xs_dev[i % P], non_blocking=True)
         for l in range(n_layers):
-            layers[l].prefill(x, lgs[l], out, stream=stream)
+            if ex is not None:
+                ep.prefill_p2p(layers[l], ex, x, lgs[l], out, stream=stream)
+            else:
+                layers[l].prefill(x, lgs[l], out, stream=stream)
             x.add_(out)
         if e2e:
             res_host.copy_(x, non_blocking=True)
@@ -769,7 +777,9 @@ def run_config4(args):
                 "config": {"workload": f"config4: {n_layers}-layer config-3 stack ({gib:.1f} GiB of experts on rank 0), "
                                        f"{B}-token prompt per rank, 512 experts over {world} GPU(s) "
                                        f"({hi - lo} on rank 0), per-layer Zipf(1.1) top-8, shared expert, "
-                                       f"f32 residual; dispatch/combine by NCCL all-to-all" if world > 1 else
+                                       f"f32 residual; dispatch/combine "
+                                       + ("by peer-memory stores over NVLink (no host round trip)"
+                                          if ex is not None else "by NCCL all-to-all") if world > 1 else
                                        f"config4 on one GPU: {n_layers}-layer config-3 stack, {B}-token prompt, "
                                        f"all 512 experts local (layer prefill, no exchange)",
                            "global_batch": tok // K, "layers_per_step": n_layers,
@@ -779,6 +789,11 @@ def run_config4(args):
                         "h2d_bytes_per_step": B * H * 4, "d2h_bytes_per_step": B * H * 4},
                 "gpu_launches": launches, "timing": "eager steps, device events, max over ranks"}
         print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if ex is not None:
+        ex.close()
     for L in layers:
         L._ws.clear()
     if world > 1:
