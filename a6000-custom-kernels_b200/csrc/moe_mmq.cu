@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(256) mmq_gather_rows_kernel(const float *__res
 // (plane 0 = low byte, plane 1 = high byte of a 16-bit fold), whether plane p
 // is signed, the mins term (Q2_K on the tensor core, Q4_K with dp2a in the
 // epilogue) and the tokens per chunk (TMEM: two accumulator sets of
-// (planes + summs) x NT columns plus two A buffers of 64 columns per plane).
+// (planes + summs) x NT columns plus two A buffers of 64 columns per plane:
+// 512 columns at most).
 template <int TYPE>
 struct MmqType;
 template <> struct MmqType<T_Q2_K> {
@@ -268,11 +269,11 @@ template <> struct MmqType<T_Q3_K> {
     static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = true, P1_SIGNED = false;
 };
 template <> struct MmqType<T_Q4_K> {
-    static constexpr int BPB = 144, NPLANE = 2, NT = 32;
+    static constexpr int BPB = 144, NPLANE = 2, NT = 64;
     static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false;
 };
 template <> struct MmqType<T_Q6_K> {
-    static constexpr int BPB = 210, NPLANE = 2, NT = 32;
+    static constexpr int BPB = 210, NPLANE = 2, NT = 64;
     static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = true;
 };
 
@@ -749,11 +750,9 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
         // ---------------- epilogue warps -----------------------------------------
         constexpr int NQ = NT / 32;                               // 16-token slices per warp
         const int r = 32 * (warp & 3) + lane, half = warp >> 2;   // row; slices half + 2 q
-        float acc[16 * NQ], accm[Ty::MINS_DP ? 16 * NQ : 1];
+        float acc[16 * NQ];
 #pragma unroll
         for (int n = 0; n < 16 * NQ; ++n) acc[n] = 0.f;
-#pragma unroll
-        for (int n = 0; n < (Ty::MINS_DP ? 16 * NQ : 1); ++n) accm[n] = 0.f;
         uint32_t g = 0;
         bool ok = true;
         int4 ch = static_cast<int>(blockIdx.x) < total ? a.chunks[blockIdx.x / row_blocks] : make_int4(0, 0, 0, 0);
@@ -797,13 +796,13 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                                 A = __fadd_rn(A, __fmul_rn(dall, small_int_to_float(-static_cast<int>(S0[j]))));
                             } else {
                                 const int isum = static_cast<int>(S0[j]) + 256 * static_cast<int>(S1[j]);
-                                A = __fadd_rn(A, __fmul_rn(dall, __int2float_rn(isum)));
+                                float t = __fmul_rn(dall, __int2float_rn(isum));
                                 if (Ty::MINS_DP) {
-                                    // sumf -= (d_a dmin) * summs
+                                    // - (d_a dmin) * summs
                                     const int sm = q4K_summs(C.bs2[g % MMQ_RING][sl * 16 + j], C.rm[g % MMQ_RING][r]);
-                                    accm[q * 16 + j] = __fsub_rn(accm[q * 16 + j],
-                                                                 __fmul_rn(__fmul_rn(dv[j], rs.y), small_int_to_float(sm)));
+                                    t = __fsub_rn(t, __fmul_rn(__fmul_rn(dv[j], rs.y), small_int_to_float(sm)));
                                 }
+                                A = __fadd_rn(A, t);
                             }
                         }
                     }
@@ -819,12 +818,7 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int n = (half + 2 * q) * 16 + j;
-                            float v = acc[q * 16 + j];
-                            if (Ty::MINS_DP) {
-                                v = __fadd_rn(accm[q * 16 + j], v);
-                                accm[q * 16 + j] = 0.f;
-                            }
-                            if (n < T.nt) a.dst[static_cast<int64_t>(ent[n]) * a.nrows + row] = v;
+                            if (n < T.nt) a.dst[static_cast<int64_t>(ent[n]) * a.nrows + row] = acc[q * 16 + j];
                             acc[q * 16 + j] = 0.f;
                         }
                     }

@@ -79,7 +79,7 @@ def test_prefill_q2k_repeat_same_result(pkg, cuda):
     (O.Q3_K, 256, 128, 4, 1, 1, 21),
     (O.Q3_K, 768, 256, 8, 2, 100, 22),     # 330-byte rows: 8-row tensor-map groups, 2-byte aligned blocks
     (O.Q3_K, 3072, 768, 32, 8, 64, 23),
-    (O.Q4_K, 512, 128, 8, 2, 70, 24),      # 32-token chunks: 70 tokens -> 32 + 32 + 6
+    (O.Q4_K, 512, 128, 8, 2, 70, 24),      # 70 tokens on the hot expert: chunks of 64 + 6
     (O.Q4_K, 3072, 768, 32, 8, 64, 25),
     (O.Q4_K, 768, 3072, 32, 8, 48, 26),
     (O.Q6_K, 256, 128, 4, 1, 33, 27),
