@@ -384,12 +384,14 @@ struct RowScales {
 
 __device__ __forceinline__ uint32_t lo_bytes(uint32_t ev, uint32_t od) { return __byte_perm(ev, od, 0x6240); }
 __device__ __forceinline__ uint32_t hi_bytes(uint32_t ev, uint32_t od) { return __byte_perm(ev, od, 0x7351); }
-// 4 unsigned bytes x -> 16-bit lanes sc * x + bias (even and odd elements)
-__device__ __forceinline__ void lane_fold(uint32_t x, int sc, int bias, uint32_t &ev, uint32_t &od) {
-    const int b2 = bias * 0x10001;
-    ev = static_cast<uint32_t>(sc * static_cast<int>(x & 0x00FF00FFu) + b2);
-    od = static_cast<uint32_t>(sc * static_cast<int>((x >> 8) & 0x00FF00FFu) + b2);
+// 4 unsigned bytes x -> 16-bit lanes sc * x + bias (even and odd elements);
+// b2 = bias * 0x10001
+__device__ __forceinline__ void lane_fold(uint32_t x, int sc, int b2, uint32_t &ev, uint32_t &od) {
+    ev = static_cast<uint32_t>(sc * static_cast<int>(__byte_perm(x, 0u, 0x4240)) + b2);   // bytes 0, 2
+    od = static_cast<uint32_t>(sc * static_cast<int>(__byte_perm(x, 0u, 0x4341)) + b2);   // bytes 1, 3
 }
+// x >> s for s >= 0, x << -s otherwise
+__device__ __forceinline__ uint32_t shr_signed(uint32_t x, int s) { return s >= 0 ? x >> s : x << -s; }
 
 template <int TYPE>
 __device__ __forceinline__ void mmq_unpack(const uint8_t *blk, uint32_t a_cols, int h, RowScales &rs);
@@ -449,12 +451,14 @@ __device__ __forceinline__ void mmq_unpack<T_Q3_K>(const uint8_t *blk, uint32_t 
             // chunk c: shift j = c / 2, 16-element half c % 2 of the 32
             const int c = 4 * part + cc, j = c >> 1, hh = c & 1;
             const int s = static_cast<int>(((c < 4 ? s_lo : s_hi) >> (8 * (c & 3))) & 0xFFu) - 32;
+            const int b2 = (4 * s + 256) * 0x10001;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
+                // u = 2 low bits | high bit << 2 (the high bit moved straight to bit 2)
                 const uint32_t u = ((qs[4 * hh + i] >> (2 * j)) & 0x03030303u) |
-                                   (((hm[4 * hh + i] >> (4 * h + j)) & 0x01010101u) << 2);
+                                   (shr_signed(hm[4 * hh + i], 4 * h + j - 2) & 0x04040404u);
                 uint32_t ev, od;
-                lane_fold(u, -s, 4 * s + 256, ev, od);   // -s u + 4 s + 256 in [132, 384]
+                lane_fold(u, -s, b2, ev, od);   // -s u + 4 s + 256 in [132, 384]
                 v[4 * cc + i] = lo_bytes(ev, od);
             }
         }
@@ -495,9 +499,9 @@ __device__ __forceinline__ void mmq_unpack<T_Q4_K>(const uint8_t *blk, uint32_t 
             q4K_scale_min(sw, 4 * h + 2 * (c >> 2) + nib, sc, m);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint32_t q = (qs[8 * (c >> 2) + 4 * (c & 1) + i] >> (4 * nib)) & 0x0F0F0F0Fu;
-                uint32_t ev, od;
-                lane_fold(q, sc, 0, ev, od);
+                const uint32_t w = qs[8 * (c >> 2) + 4 * (c & 1) + i] >> (4 * nib);
+                const uint32_t ev = static_cast<uint32_t>(sc) * (w & 0x000F000Fu);          // elements 0, 2
+                const uint32_t od = static_cast<uint32_t>(sc) * ((w >> 8) & 0x000F000Fu);   // elements 1, 3
                 lo[4 * cc + i] = lo_bytes(ev, od);
                 hi[4 * cc + i] = hi_bytes(ev, od);
             }
@@ -536,12 +540,14 @@ __device__ __forceinline__ void mmq_unpack<T_Q6_K>(const uint8_t *blk, uint32_t 
             // qh bits 2 g), 16-element half c % 2 of the 32; scale 8 h + c
             const int c = 4 * part + cc, g = c >> 1, lh = c & 1;
             const int sc = static_cast<int>(static_cast<int8_t>((sw[c >> 2] >> (8 * (c & 3))) & 0xFFu));
+            const int b2 = (32768 - 32 * sc) * 0x10001;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
+                // q = low nibble | 2 high bits << 4 (moved straight to bits 4-5)
                 const uint32_t q = ((ql[8 * (g & 1) + 4 * lh + i] >> (4 * (g >> 1))) & 0x0F0F0F0Fu) |
-                                   (((qh[4 * lh + i] >> (2 * g)) & 0x03030303u) << 4);
+                                   (shr_signed(qh[4 * lh + i], 2 * g - 4) & 0x30303030u);
                 uint32_t ev, od;
-                lane_fold(q, sc, 32768 - 32 * sc, ev, od);   // sc (q - 32) + 32768
+                lane_fold(q, sc, b2, ev, od);   // sc (q - 32) + 32768
                 lo[4 * cc + i] = lo_bytes(ev, od);
                 hi[4 * cc + i] = hi_bytes(ev, od) ^ 0x80808080u;
             }
