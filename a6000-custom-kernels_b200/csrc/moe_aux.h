@@ -65,6 +65,11 @@ cudaError_t launch_ep_return(const void *const *peer_ptrs, int W, int cap, const
                              const float *y, int H, uint32_t *scratch, cudaStream_t st);
 cudaError_t launch_ep_wait(const uint32_t *flag, uint32_t target, uint64_t timeout_ns, int *err, cudaStream_t st);
 
+// chunk table of a one-expert call with all ids 0: entries in order, chunks
+// of ntc consecutive entries
+cudaError_t launch_mmq_identity_chunks(int n, int ntc, int32_t *entries, int4 *chunks, int32_t *n_chunks,
+                                       cudaStream_t st);
+
 // tokens per chunk of the tensor-core path for a weight type (0: none)
 int mmq_chunk_tokens(int type);
 bool mmq_supported(int type, int64_t K, int64_t nrows);

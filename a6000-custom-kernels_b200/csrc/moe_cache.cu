@@ -761,6 +761,14 @@ struct PrefillWs {
     size_t bytes;
 };
 
+// Tokens per chunk of the tensor-core path (the type's width). Narrower
+// chunks do not speed up a one-expert call with few tiles: a tile's cost is
+// the per-super-block unpack of its weight rows, which more chunks repeat.
+int chunk_tokens_for(const moe_tensor *src0, int64_t) {
+    const int ntc = moe::mmq_chunk_tokens(src0->type);
+    return ntc > 0 ? ntc : moe::MMQ_NT;
+}
+
 // x_rows: activation rows (n_tok, or n_tok * k when each pick has its own row)
 PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x_rows, char *base) {
     PrefillWs w{};
@@ -769,8 +777,7 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x
     const int64_t E = src0->ne[2], K = src0->ne[0];
     w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(x_rows) * (K / 256) * 292));
     w.entries = reinterpret_cast<int32_t *>(take(4 * n_tok * k));
-    const int ntc = moe::mmq_chunk_tokens(src0->type) > 0 ? moe::mmq_chunk_tokens(src0->type) : moe::MMQ_NT;
-    w.max_chunks = moe::mmq_max_chunks(n_tok * k, E, ntc);
+    w.max_chunks = moe::mmq_max_chunks(n_tok * k, E, chunk_tokens_for(src0, n_tok * k));
     w.chunks = reinterpret_cast<int4 *>(take(16 * static_cast<size_t>(w.max_chunks)));
     w.n_chunks = reinterpret_cast<int32_t *>(take(4));
     w.btiles = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(w.max_chunks) * (K / 256) * moe::MMQ_BT_BYTES));
@@ -787,7 +794,7 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x
 // product reuses the grouping and the B tiles.
 int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t n_tok, const int32_t *ids, int64_t k,
                 int64_t ids_stride, float *dst, char *workspace, size_t workspace_bytes, bool *used_tc,
-                cudaStream_t st, const moe_tensor *src2 = nullptr, float *dst2 = nullptr) {
+                cudaStream_t st, const moe_tensor *src2 = nullptr, float *dst2 = nullptr, bool ids_zero = false) {
     *used_tc = false;
     if (!src0 || !src0->data || !x || !ids || !dst) return fail(MOE_ERR_INVALID, "null argument");
     if (n_tok < 1 || k < 1 || ids_stride < k) return fail(MOE_ERR_INVALID, "need n_tok >= 1, k >= 1, ids_stride >= k");
@@ -827,9 +834,12 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
             return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
         int rc = init_device_globals();
         if (rc) return rc;
-        const int ntc = moe::mmq_chunk_tokens(src0->type);
-        CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
-                                 ntc, w.entries, w.chunks, w.n_chunks, g.d_err, st));
+        const int ntc = chunk_tokens_for(src0, n_tok * k);
+        if (ids_zero && E == 1 && k == 1)   // the caller's ids are all 0: entries in order
+            CK(moe::launch_mmq_identity_chunks(static_cast<int>(n_tok), ntc, w.entries, w.chunks, w.n_chunks, st));
+        else
+            CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
+                                     ntc, w.entries, w.chunks, w.n_chunks, g.d_err, st));
         CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, x_rows, K, st));
         // the gather reads activation row entry / k_div (entry = t * k + p)
         CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries,
@@ -1337,10 +1347,12 @@ int shared_prefill(const moe_layer_desc *L, const float *x, int64_t n_tok, const
     const moe_tensor su = shared_tensor(L->shared_up, L->up.type, H, F);
     const moe_tensor sd = shared_tensor(L->shared_down, L->down.type, F, H);
     CK(cudaMemsetAsync(w.zero_ids, 0, 4 * n_tok, st));
-    int rc = run_prefill(&sg, x, false, n_tok, w.zero_ids, 1, 1, w.sg, w.scratch, w.scratch_bytes, &tc, st, &su, w.su);
+    int rc = run_prefill(&sg, x, false, n_tok, w.zero_ids, 1, 1, w.sg, w.scratch, w.scratch_bytes, &tc, st, &su, w.su,
+                         true);
     if (rc) return rc;
     CK(moe::launch_glu(w.sg, w.su, n_tok * F, L->glu_op, L->glu_limit, st));
-    return run_prefill(&sd, w.su, false, n_tok, w.zero_ids, 1, 1, ys, w.scratch, w.scratch_bytes, &tc, st);
+    return run_prefill(&sd, w.su, false, n_tok, w.zero_ids, 1, 1, ys, w.scratch, w.scratch_bytes, &tc, st, nullptr,
+                       nullptr, true);
 }
 
 }  // namespace

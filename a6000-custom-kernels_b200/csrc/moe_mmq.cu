@@ -876,6 +876,24 @@ cudaError_t launch_mmq_gather_rows(const float *x, const float *u, int glu_op, f
     return cudaGetLastError();
 }
 
+// The chunk table of a one-expert call whose ids are all 0 (the shared
+// expert): entries in order, chunks of ntc consecutive entries.
+__global__ void mmq_identity_chunks_kernel(int n, int ntc, int32_t *entries, int4 *chunks, int32_t *n_chunks) {
+    const int nch = (n + ntc - 1) / ntc;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        entries[i] = i;
+        if (i % ntc == 0) chunks[i / ntc] = make_int4(0, i, min(ntc, n - i), i / ntc);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *n_chunks = nch;
+}
+
+cudaError_t launch_mmq_identity_chunks(int n, int ntc, int32_t *entries, int4 *chunks, int32_t *n_chunks,
+                                       cudaStream_t st) {
+    const int grid = (n + 255) / 256 < 148 ? (n + 255) / 256 : 148;
+    mmq_identity_chunks_kernel<<<grid > 0 ? grid : 1, 256, 0, st>>>(n, ntc, entries, chunks, n_chunks);
+    return cudaGetLastError();
+}
+
 int mmq_chunk_tokens(int type) {
     switch (type) {
         case T_Q2_K: return MmqType<T_Q2_K>::NT;
