@@ -775,11 +775,13 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x
     size_t off = 0;
     auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
     const int64_t E = src0->ne[2], K = src0->ne[0];
-    w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(x_rows) * (K / 256) * 292));
+    // the grouping first: its place depends only on the entries, the experts
+    // and the chunk width, so a later call on the same ids can reuse it
     w.entries = reinterpret_cast<int32_t *>(take(4 * n_tok * k));
     w.max_chunks = moe::mmq_max_chunks(n_tok * k, E, chunk_tokens_for(src0, n_tok * k));
     w.chunks = reinterpret_cast<int4 *>(take(16 * static_cast<size_t>(w.max_chunks)));
     w.n_chunks = reinterpret_cast<int32_t *>(take(4));
+    w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(x_rows) * (K / 256) * 292));
     w.btiles = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(w.max_chunks) * (K / 256) * moe::MMQ_BT_BYTES));
     w.bytes = off;
     return w;
@@ -794,7 +796,8 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x
 // product reuses the grouping and the B tiles.
 int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t n_tok, const int32_t *ids, int64_t k,
                 int64_t ids_stride, float *dst, char *workspace, size_t workspace_bytes, bool *used_tc,
-                cudaStream_t st, const moe_tensor *src2 = nullptr, float *dst2 = nullptr, bool ids_zero = false) {
+                cudaStream_t st, const moe_tensor *src2 = nullptr, float *dst2 = nullptr, bool ids_zero = false,
+                bool reuse_groups = false) {
     *used_tc = false;
     if (!src0 || !src0->data || !x || !ids || !dst) return fail(MOE_ERR_INVALID, "null argument");
     if (n_tok < 1 || k < 1 || ids_stride < k) return fail(MOE_ERR_INVALID, "need n_tok >= 1, k >= 1, ids_stride >= k");
@@ -835,7 +838,10 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
         int rc = init_device_globals();
         if (rc) return rc;
         const int ntc = chunk_tokens_for(src0, n_tok * k);
-        if (ids_zero && E == 1 && k == 1)   // the caller's ids are all 0: entries in order
+        if (reuse_groups) {
+            // the previous call on this workspace grouped the same ids over the
+            // same experts with the same chunk width
+        } else if (ids_zero && E == 1 && k == 1)   // the caller's ids are all 0: entries in order
             CK(moe::launch_mmq_identity_chunks(static_cast<int>(n_tok), ntc, w.entries, w.chunks, w.n_chunks, st));
         else
             CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
@@ -1335,7 +1341,15 @@ int experts_prefill(const moe_layer_desc *L, const float *x, bool x_per_pick, co
                          w.u);
     if (rc) return rc;
     CK(moe::launch_glu(w.g, w.u, n_tok * k * L->F, L->glu_op, L->glu_limit, st));
-    return run_prefill(&L->down, w.u, true, n_tok, ids, k, k, y, w.scratch, w.scratch_bytes, &tc, st);
+    // down: same ids and experts; its grouping is the gate/up one when both
+    // ran on the tensor cores with the same chunk width
+    bool tc_down = false;
+    const bool reuse = tc && moe::mmq_supported(L->down.type, L->down.ne[0], L->down.ne[1]) &&
+                       ptr_kind(L->down.data) == 2 && (L->down.nb[2] % 16) == 0 &&
+                       chunk_tokens_for(&L->down, n_tok * k) == chunk_tokens_for(&L->gate, n_tok * k) &&
+                       L->down.ne[2] == L->gate.ne[2] && L->gate.type == L->up.type;
+    return run_prefill(&L->down, w.u, true, n_tok, ids, k, k, y, w.scratch, w.scratch_bytes, &tc_down, st, nullptr,
+                       nullptr, false, reuse);
 }
 
 // the shared expert of every token into ys [n][H]
@@ -1352,7 +1366,7 @@ int shared_prefill(const moe_layer_desc *L, const float *x, int64_t n_tok, const
     if (rc) return rc;
     CK(moe::launch_glu(w.sg, w.su, n_tok * F, L->glu_op, L->glu_limit, st));
     return run_prefill(&sd, w.su, false, n_tok, w.zero_ids, 1, 1, ys, w.scratch, w.scratch_bytes, &tc, st, nullptr,
-                       nullptr, true);
+                       nullptr, true);   // (the identity table is one cheap launch)
 }
 
 }  // namespace
