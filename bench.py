@@ -56,6 +56,8 @@ def parse():
                     help="BASELINE config; 2 (default) is the headline line, 1/3/4/5 print their own lines")
     ap.add_argument("--prompt", type=int, default=512, help="prefill tokens per rank (config 4)")
     ap.add_argument("--stack-layers", type=int, default=48, help="layers of the config-3/4 stack (48 in BASELINE)")
+    ap.add_argument("--kernel-shares", action="store_true",
+                    help="config 4: also print each kernel's share of the device time (torch profiler, rank 0)")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="config 4 dispatch/combine: peer-memory kernels (default) or NCCL all-to-all")
     ap.add_argument("--batch", type=int, default=1, help="decode tokens per step (configs 3 and 5)")
@@ -759,6 +761,25 @@ def run_config4(args):
     ev3.record(stream)
     torch.cuda.synchronize()
     ms_e2e = ev2.elapsed_time(ev3)
+    if args.kernel_shares and rank == 0:
+        # device time per kernel over two steps (CUPTI timestamps; the kernels
+        # run back to back as in the timed loop, nothing is serialized)
+        import collections
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for i in range(2):
+                step(i)
+            torch.cuda.synchronize()
+        agg = collections.defaultdict(lambda: [0, 0.0])
+        for e in prof.events():
+            if e.device_type.name == "CUDA":
+                a = agg[e.name.split("(")[0].replace("void ", "")[:48]]
+                a[0] += 1
+                a[1] += e.device_time_total
+        tot = sum(v[1] for v in agg.values())
+        print("kernel shares over 2 steps (us per layer):", file=sys.stderr)
+        for name, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:12]:
+            print(f"  {name:48s} {c:6d} launches {t / 2 / n_layers:8.1f} us {100 * t / tot:5.1f} %", file=sys.stderr)
     assert mc.device_error() == 0
     if world > 1:
         t = torch.tensor([ms, ms_e2e], device=dev)
