@@ -80,14 +80,21 @@ class MoELayer:
         """True when decode() runs the layer as one fused kernel for n_tok tokens."""
         return bool(lib().moe_b200_layer_fused(ctypes.byref(self.desc), n_tok))
 
-    def decode(self, x, logits, out=None, stream=None):
-        """x f32 [n_tok, H], logits f32 [n_tok, E] (device) -> out f32 [n_tok, H]."""
+    def decode(self, x, logits, out=None, stream=None, trace=None):
+        """x f32 [n_tok, H], logits f32 [n_tok, E] (device) -> out f32 [n_tok, H].
+        With `trace` (a seed.TraceWriter) the step's routing is appended as one
+        record per expert tensor, as the reference's trace hook writes it for
+        each MUL_MAT_ID (this reads the ids back to the host)."""
         n_tok = x.shape[0]
         if out is None:
             out = torch.empty((n_tok, self.H), dtype=torch.float32, device=self.device)
         ws = self.workspace(n_tok)
         check(lib().moe_b200_layer_decode(ctypes.byref(self.desc), _ptr(x), _ptr(logits), _ptr(out), n_tok,
                                           _ptr(ws), ws.numel(), _stream(stream)))
+        if trace is not None:
+            ids = self.routing_of(n_tok)[0].cpu().numpy()
+            for r in ("gate", "up", "down"):
+                trace.record(self.desc_t[r].name.decode(), ids, self.E)
         return out
 
     def prefill(self, x, logits, out=None, stream=None):

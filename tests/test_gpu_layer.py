@@ -59,3 +59,27 @@ def test_config2_layer_full_expert_count(pkg, cuda):
         L[r] = layer.w[r].cpu().numpy()
         L["shared_" + r] = layer.shared[r].cpu().numpy()
     check_layer(layer, L, x, logits, out)
+
+
+def test_decode_trace_builds_seed(pkg, cuda, tmp_path):
+    """decode steps traced in the trace hook's format give a seed file whose
+    lines start with the most picked experts of each tensor"""
+    from importlib import import_module
+    S = import_module("a6000-custom-kernels_b200.seed")
+    H, F, E, k = 1024, 512, 24, 8
+    layer = pkg.MoELayer(H, F, E, k, {"gate": O.Q2_K, "up": O.Q2_K, "down": O.Q2_K}, shared=False, seed=5,
+                         name="blk.3")
+    path = tmp_path / "trace.bin"
+    picks = {}
+    with S.TraceWriter(str(path)) as w:
+        for step in range(12):
+            x = torch.from_numpy(activations((1, H), seed=100 + step)).to(cuda)
+            lg = torch.from_numpy(zipf_logits(1, E, seed=200 + step)).to(cuda)
+            layer.decode(x, lg, trace=w)
+            for e in layer.routing_of(1)[0].cpu().numpy().reshape(-1).tolist():
+                picks[e] = picks.get(e, 0) + 1
+    order = S.build_seed(str(path), str(tmp_path / "seed.txt"))
+    assert list(order) == [f"blk.3.ffn_{r}_exps.weight" for r in ("gate", "up", "down")]
+    top = max(picks.values())
+    assert picks[order["blk.3.ffn_gate_exps.weight"][0]] == top
+    assert sorted(order["blk.3.ffn_down_exps.weight"]) == sorted(picks)
