@@ -75,6 +75,7 @@ struct State {
     uint32_t *d_stats = nullptr, *h_stats = nullptr, *d_clock = nullptr;
     int *d_err = nullptr;
     uint64_t timeout_ns_ep = 2000000000ull;   // expert-parallel arrival waits
+    uint64_t timeout_ns_kernel = 2000000000ull;   // waits inside the GEMV / layer / prefill kernels
     uint32_t h_clock = 0;
     int device = -1;
     std::unordered_map<uint32_t, int> admission;
@@ -590,6 +591,7 @@ int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
     a.row_bytes = static_cast<uint32_t>(c.s01 * type_size(src0->type));
     if (a.row_bytes != src0->nb[1]) return fail(MOE_ERR_INVALID, "s01 does not match src0->nb[1]");
     a.err = g.d_err;
+    a.timeout_ns = g.timeout_ns_kernel;
     const char *why = "";
     cudaError_t ce = cudaSuccess;
     const int act = c.src1_type == MOE_TYPE_Q8_1 ? moe::ACT_Q8_1 : moe::ACT_CPU;
@@ -727,7 +729,9 @@ int layer_args(const moe_layer_desc *L, const float *x, const float *logits, flo
     a.h_tag = w.h_tag;
     a.hs_tag = shared ? w.hs_tag : nullptr;
     a.err = g.d_err;
+    a.timeout_ns = g.timeout_ns_kernel;
     u.err = d.err = g.d_err;
+    u.timeout_ns = d.timeout_ns = g.timeout_ns_kernel;
     return MOE_OK;
 }
 
@@ -867,6 +871,7 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
             a.n_chunks = w.n_chunks;
             a.dst = pass == 0 ? dst : dst2;
             a.err = g.d_err;
+            a.timeout_ns = g.timeout_ns_kernel;
             const char *why = "";
             cudaError_t ce = cudaSuccess;
             rc = moe::launch_mmq(t->type, a, st, &why, &ce);
@@ -1431,6 +1436,17 @@ int moe_b200_combine(const float *y, const float *weights, const float *ys, floa
 
 // ---- expert-parallel exchange over peer memory ------------------------------
 
+}  // extern "C"
+namespace {
+// rows of the peer table (x: row 0, y_ret: row 3) are copied as float4
+bool peer_rows_aligned(const void *const *peer_ptrs, int32_t world) {
+    for (int32_t r = 0; r < world; ++r)
+        if (!aligned16(peer_ptrs[0 * world + r]) || !aligned16(peer_ptrs[3 * world + r])) return false;
+    return true;
+}
+}  // namespace
+extern "C" {
+
 int moe_b200_ipc_alloc(size_t bytes, void **ptr) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     if (!ptr || bytes == 0) return fail(MOE_ERR_INVALID, "null pointer or zero size");
@@ -1483,6 +1499,8 @@ int moe_b200_ep_dispatch(const void *const *peer_ptrs, int32_t world, int32_t ra
         return fail(MOE_ERR_INVALID, "bad expert-parallel dispatch arguments");
     int rc = init_device_globals();
     if (rc) return rc;
+    if (!aligned16(x) || !peer_rows_aligned(peer_ptrs, world))
+        return fail(MOE_ERR_INVALID, "x and every peer's row buffers (x, y_ret) must be 16-byte aligned");
     CK(moe::launch_ep_dispatch(peer_ptrs, world, rank, static_cast<int>(cap), ids, static_cast<int>(n_entries),
                                static_cast<int>(k), static_cast<int>(n_experts), x, static_cast<int>(H),
                                static_cast<uint32_t *>(scratch), g.d_err, reinterpret_cast<cudaStream_t>(stream)));
@@ -1494,8 +1512,18 @@ int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap,
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     if (!peer_ptrs || !ids || !src || !y || !scratch || world < 1 || world > 8 || H % 4)
         return fail(MOE_ERR_INVALID, "bad expert-parallel return arguments");
+    if (!aligned16(y) || !peer_rows_aligned(peer_ptrs, world))
+        return fail(MOE_ERR_INVALID, "y and every peer's row buffers (x, y_ret) must be 16-byte aligned");
     CK(moe::launch_ep_return(peer_ptrs, world, static_cast<int>(cap), ids, src, y, static_cast<int>(H),
                              static_cast<uint32_t *>(scratch), reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+int moe_b200_set_wait_limits(int64_t kernel_wait_ns, int64_t exchange_wait_ns) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    constexpr uint64_t kDefault = 2000000000ull;
+    g.timeout_ns_kernel = kernel_wait_ns > 0 ? static_cast<uint64_t>(kernel_wait_ns) : kDefault;
+    g.timeout_ns_ep = exchange_wait_ns > 0 ? static_cast<uint64_t>(exchange_wait_ns) : kDefault;
     return MOE_OK;
 }
 
@@ -1551,6 +1579,7 @@ int mmq_call(const moe_tensor *t, const EpRowsWs &w, int64_t n_rows, float *dst,
     a.n_chunks = w.n_chunks;
     a.dst = dst;
     a.err = g.d_err;
+    a.timeout_ns = g.timeout_ns_kernel;
     const char *why = "";
     cudaError_t ce = cudaSuccess;
     const int rc = moe::launch_mmq(t->type, a, st, &why, &ce);

@@ -21,7 +21,7 @@ enum : int { ACT_Q8_1 = 0, ACT_CPU = 1 };
 enum : int {
     DERR_NONE = 0, DERR_BAD_ID = 1, DERR_TOO_MANY_KEYS = 2, DERR_TIMEOUT_FULL = 3,
     DERR_TIMEOUT_EMPTY = 4, DERR_TOO_MANY_SEGMENTS = 5, DERR_DRAIN = 6, DERR_GRID_BARRIER = 7,
-    DERR_TIMEOUT_TAG = 8,
+    DERR_TIMEOUT_TAG = 8, DERR_EP_OVERFLOW = 9,
 };
 
 template <int T> struct fmt;
@@ -101,14 +101,23 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parit
 // this hardware, so it cannot bound a wait.
 __device__ __forceinline__ uint64_t timeout_cycles(uint64_t timeout_ns) { return 2ull * timeout_ns; }
 
-// Sleeping wait (for consumers): gives up after ~timeout_ns.
+// Sleeping wait (for consumers): gives up after ~timeout_ns. The suspend
+// hint never exceeds the limit, so a tiny limit gives up at once.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = clock64(), lim = timeout_cycles(timeout_ns);
+    const uint32_t hint = timeout_ns < 20000u ? static_cast<uint32_t>(timeout_ns) + 1u : 20000u;
     for (;;) {
-        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if (mbar_try_wait_hint(bar, parity, hint)) return true;
         if (static_cast<uint64_t>(clock64()) - t0 > lim) return false;
     }
+}
+
+// Limit of the wait for copies already in flight before a CTA exits: never
+// below 200 ms, whatever limit the other waits run with, so a CTA whose
+// other waits gave up still lets every issued copy land.
+__device__ __forceinline__ uint64_t drain_limit_ns(uint64_t timeout_ns) {
+    return timeout_ns > 200000000ull ? timeout_ns : 200000000ull;
 }
 
 // Wait for the phase with the given parity; gives up after ~timeout_ns.

@@ -78,7 +78,7 @@ __global__ void ep_dispatch_kernel(EpPeers P, int W, int me, int cap, const int3
         if (lane == 0) slot = atomicAdd(&cursor[d], 1u);
         slot = __shfl_sync(0xffffffffu, slot, 0);
         if (slot >= static_cast<uint32_t>(cap)) {   // more entries than the region holds: a caller error
-            if (lane == 0) set_error(err, DERR_BAD_ID);
+            if (lane == 0) set_error(err, DERR_EP_OVERFLOW);
             continue;
         }
         const size_t row = static_cast<size_t>(me) * cap + slot;
@@ -141,6 +141,8 @@ __global__ void ep_wait_kernel(const uint32_t *flag, uint32_t target, uint64_t t
 
 namespace {
 
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 bool load_peers(const void *const *ptrs, int W, EpPeers &P) {
     if (W < 1 || W > EP_MAX_WORLD) return false;
     memset(&P, 0, sizeof(P));
@@ -151,6 +153,8 @@ bool load_peers(const void *const *ptrs, int W, EpPeers &P) {
         P.y_ret[r] = static_cast<float *>(const_cast<void *>(ptrs[3 * W + r]));
         P.flags[r] = static_cast<uint32_t *>(const_cast<void *>(ptrs[4 * W + r]));
         if (!P.x[r] || !P.ids[r] || !P.src[r] || !P.y_ret[r] || !P.flags[r]) return false;
+        // rows move as float4: every peer row buffer must be 16-byte aligned
+        if (!aligned16(P.x[r]) || !aligned16(P.y_ret[r])) return false;
     }
     return true;
 }
@@ -169,7 +173,7 @@ cudaError_t launch_ep_dispatch(const void *const *peer_ptrs, int W, int me, int 
                                int n_entries, int k, int E, const float *x, int H, uint32_t *scratch, int *err,
                                cudaStream_t st) {
     EpPeers P;
-    if (!load_peers(peer_ptrs, W, P) || H % 4) return cudaErrorInvalidValue;
+    if (!load_peers(peer_ptrs, W, P) || H % 4 || !aligned16(x)) return cudaErrorInvalidValue;
     ep_dispatch_kernel<<<grid_for(n_entries), 256, 0, st>>>(P, W, me, cap, ids, n_entries, k, E, x, H, scratch,
                                                             scratch + EP_MAX_WORLD, err);
     return cudaGetLastError();
@@ -178,7 +182,7 @@ cudaError_t launch_ep_dispatch(const void *const *peer_ptrs, int W, int me, int 
 cudaError_t launch_ep_return(const void *const *peer_ptrs, int W, int cap, const int32_t *ids, const int32_t *src,
                              const float *y, int H, uint32_t *scratch, cudaStream_t st) {
     EpPeers P;
-    if (!load_peers(peer_ptrs, W, P) || H % 4) return cudaErrorInvalidValue;
+    if (!load_peers(peer_ptrs, W, P) || H % 4 || !aligned16(y)) return cudaErrorInvalidValue;
     ep_return_kernel<<<grid_for(static_cast<int64_t>(W) * cap), 256, 0, st>>>(P, W, cap, ids, src, y, H,
                                                                               scratch + EP_MAX_WORLD + 1);
     return cudaGetLastError();

@@ -864,7 +864,7 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
     // drain: never leave a bulk copy in flight when the CTA exits
     const int first = issued > S ? issued - S : 0;
     for (int i = first; i < issued; ++i) {
-        if (!mbar_wait_sleep(&full[i % S], static_cast<uint32_t>((i / S) & 1), timeout_ns)) {
+        if (!mbar_wait_sleep(&full[i % S], static_cast<uint32_t>((i / S) & 1), drain_limit_ns(timeout_ns))) {
             if (lane == 0) set_error(err, DERR_DRAIN);
             break;
         }

@@ -232,8 +232,9 @@ extern "C" int moe_b200_layer_decode_noalloc(const moe_layer_desc *L, const floa
     return MOE_OK;
 }
 
-// No counterpart in the reference: read back and clear the no-alloc path's
-// device error word (0 = none). Synchronises `stream`.
+// No counterpart in the reference: read the no-alloc path's device error word
+// (0 = none) after synchronising `stream`. It is not cleared here: the next
+// no-alloc call clears it (noalloc_tables_kernel).
 extern "C" int moe_b200_noalloc_device_error(moe_stream_t stream, int32_t *code) {
     if (code) *code = 0;
     std::lock_guard<std::mutex> lock(g_na_mu);

@@ -156,6 +156,15 @@ def device_error(stream=None):
     return code.value
 
 
+# device error codes (moe_b200_device_error)
+DERR_BAD_ID, DERR_TIMEOUT_FULL, DERR_TIMEOUT_EMPTY, DERR_TIMEOUT_TAG, DERR_EP_OVERFLOW = 1, 3, 4, 8, 9
+
+
+def set_wait_limits(kernel_wait_ns=0, exchange_wait_ns=0):
+    """Limits of the bounded device waits (moe_b200_set_wait_limits); <= 0 restores the 2 s default."""
+    check(lib().moe_b200_set_wait_limits(int(kernel_wait_ns), int(exchange_wait_ns)))
+
+
 def quantize_act(act_type, x, stream=None):
     """f32 [rows, cols] (device) -> uint8 blocks [rows, row_size] (device), llama.cpp bit-exact."""
     assert x.dtype == torch.float32 and x.is_cuda and x.is_contiguous()
@@ -204,4 +213,4 @@ def fill_quantized(ggml_type, dst, n_rows, n_cols, seed, sigma=0.02, stream=None
 
 __all__ = ["MoeError", "MoeTensor", "enabled", "wants", "active", "pin_host", "step", "mul_mat_vec_q",
            "fusion_device", "expert_tensor", "configure", "reset", "stats", "table", "device_error",
-           "quantize_act", "topk_softmax", "fill_quantized", "prefill_mul_mat_id"]
+           "quantize_act", "topk_softmax", "fill_quantized", "prefill_mul_mat_id", "set_wait_limits"]

@@ -823,6 +823,10 @@ def run_config4(args):
 
 def main():
     args = parse()
+    if args.kernel_shares and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # the profiled steps would run on one rank only: its exchange waits
+        # would wait for dispatches the other ranks never send
+        sys.exit("--kernel-shares profiles a one-GPU run; run it without torchrun")
     if args.impl == "reference":
         run_reference(args)
     elif args.config == 2:

@@ -169,6 +169,28 @@ int moe_b200_table(const void *data, int32_t *slot_of, int32_t n_experts, int32_
  * the kernels' device-side error word (0 = none). */
 int moe_b200_device_error(moe_stream_t stream, int32_t *code);
 
+/* No counterpart in the reference: limits of the bounded device-side waits,
+ * in nanoseconds; a value <= 0 restores the default of 2 s. kernel_wait_ns
+ * bounds the waits inside the GEMV, layer and prefill kernels (a weight tile
+ * landing, a ring stage coming free, another CTA's results); exchange_wait_ns
+ * bounds moe_b200_ep_wait and the layer kernels' waits for other GPUs. A
+ * wait that runs out sets the device error word (moe_b200_device_error:
+ * DERR_TIMEOUT_* codes) and its kernel returns once the copies it has in
+ * flight have landed (that last wait is never shorter than 200 ms); the
+ * context stays usable. Applies to launches issued after the call. */
+int moe_b200_set_wait_limits(int64_t kernel_wait_ns, int64_t exchange_wait_ns);
+
+/* Device error codes read by moe_b200_device_error. */
+#define MOE_DERR_BAD_ID          1   /* an expert id outside [0, n_experts) */
+#define MOE_DERR_TOO_MANY_KEYS   2
+#define MOE_DERR_TIMEOUT_FULL    3   /* a wait for data (a weight tile, another GPU's arrivals) ran out */
+#define MOE_DERR_TIMEOUT_EMPTY   4   /* a wait for a free ring stage ran out */
+#define MOE_DERR_TOO_MANY_SEGMENTS 5
+#define MOE_DERR_DRAIN           6   /* copies in flight did not land before exit */
+#define MOE_DERR_GRID_BARRIER    7
+#define MOE_DERR_TIMEOUT_TAG     8   /* a wait for another CTA's results ran out */
+#define MOE_DERR_EP_OVERFLOW     9   /* an expert-parallel receive region was full */
+
 /* No counterpart in the reference: message of the last failed call. */
 const char *moe_b200_last_error(void);
 
@@ -339,6 +361,8 @@ int moe_b200_layer_set_fused(int32_t enable);
  * hot-expert cache is not used (expert tensors must be in device memory; no
  * stamps or hit/miss bookkeeping). Limits: n_tok <= 8, k <= 8, H <= 4096,
  * F <= 4096, n_experts <= 1024; larger requests return MOE_ERR_UNSUPPORTED.
+ * Gate and up must share one type and shape (else MOE_ERR_INVALID); the
+ * shared expert, when present, is read with the routed tensors' types.
  * The first call on a device looks up the array's address (cudaGetSymbolAddress)
  * and should come before any stream capture. All calls share the array and it
  * keeps the last call's contents, so calls that overlap on the GPU race. */
