@@ -1,25 +1,34 @@
 // moe_cache.cu -- host side of the hot-expert cache and the C ABI.
 //
-// Restates the reference's host code (kernels/moe-cache.cu of
-// Zapdev-labs/a6000-custom-kernels) for B200:
-//   registry / slot sizing / seeding  -> moe_get_or_create      (:525-622)
-//   promotion + LRU eviction          -> ggml_cuda_moe_cache_step, moe_acquire_slot (:628-775)
-//   eligibility / env / pinning       -> :345-469
-// Differences, each deliberate:
-//   * every entry point returns a status instead of aborting;
-//   * one step's misses are processed in sorted (tensor << 12 | expert) order,
-//     so the cache state does not depend on the GPU's block scheduling (the
-//     reference uses atomicAdd arrival order, :168-172);
-//   * HBM-resident expert tensors are claimed too: their table points straight
-//     at the weights (no pool), so the step has nothing to do for them and
-//     returns without a device sync when no tensor is host-tiered;
-//   * a gate tensor without a table is read at its expert's offset (the
-//     reference reads expert 0 there, :200).
+// Serves the reference's boundary (kernels/moe-cache.cuh:15-40 of
+// Zapdev-labs/a6000-custom-kernels) with a B200 design of its own:
+//   * Each registered expert tensor owns one device block holding its
+//     pointer table, stamps, slot maps and admission bits, plus an HBM pool
+//     when its experts live in pinned host memory. Tensors already in HBM
+//     (the normal case on a 180 GB B200) get a table of direct pointers and
+//     no pool; the promotion pass skips them.
+//   * The promotion step runs on the GPU (moe_promote.cu): the host enqueues
+//     two kernels and never waits, where the reference copies the miss log
+//     back and synchronises the stream every step (moe-cache.cu:677-678)
+//     and again for the stamps on an eviction (:641-642). The policy is the
+//     reference's: second-sighting admission, at most 48 promotions per
+//     step, LRU eviction with ties to the lowest slot, misses taken in
+//     (tensor << 12 | expert) order (the reference takes them in atomicAdd
+//     arrival order, which depends on block scheduling; sorted order is one
+//     of the orders it can produce and makes the state reproducible).
+//   * Pool sizing follows the reference's rule (:542-561): the configured
+//     slot count, capped by the budget left, by free HBM minus 2 GiB and by
+//     the expert count; seeding fills slots 0.. in seed-file order (:584-609).
+//   * Every entry point returns a status instead of aborting; a gate tensor
+//     without a table is read at its expert's offset (the reference reads
+//     expert 0 there, :200).
 #include <algorithm>
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -30,62 +39,67 @@
 #include "moe_gemv.cuh"
 #include "moe_layer.cuh"
 #include "moe_mmq.cuh"
+#include "moe_promote.cuh"
 
 namespace {
 
-constexpr int kMaxPromotions = 48;             // reference :37
-constexpr uint32_t kLogCap = 16382;            // miss-log entries (reference: 8190)
-constexpr int kStatsWords = 2 + static_cast<int>(kLogCap);
-constexpr size_t kAdmissionGc = 8192;          // reference :766
-constexpr size_t kVramMargin = 2ull << 30;     // reference :553
+constexpr uint32_t kLogCap = 16382;            // miss-log entries per step (the reference keeps 8190)
+constexpr int kLogWords = 2 + static_cast<int>(kLogCap);
+constexpr size_t kHbmReserve = 2ull << 30;     // free HBM a pool never takes
+constexpr int kMaxExperts = 4096;              // 12 bits of the miss-log packing
 
-struct Entry {
-    int32_t id = -1;
+// One expert tensor known to the cache (keyed by its data pointer).
+struct Tensor {
+    int32_t id = -1;               // registry index, packed into miss-log entries
     int type = 0;
     const char *data = nullptr;
-    size_t expert_bytes = 0;
-    uint64_t row_bytes = 0;
+    uint64_t expert_bytes = 0, row_bytes = 0;
     int64_t rows = 0, cols = 0;
-    bool dead = false;            // retired: its address was reused by another tensor
-    int n_experts = 0;
-    int n_slots = 0;
-    bool host = false;            // tiered (pinned host) vs HBM-resident
+    int n_experts = 0, n_slots = 0;
+    bool tiered = false;           // experts in pinned host memory, served through a pool
+    bool retired = false;          // its address now holds another tensor
     std::string name;
+    // device block: table, stamps, slot map, slot owners, admission bits
+    char *block = nullptr;
+    char **table = nullptr;
+    uint32_t *stamps = nullptr;
+    int32_t *slot_map = nullptr, *slot_owner = nullptr;
+    uint8_t *seen = nullptr;
     char *pool = nullptr;
-    char **d_tbl = nullptr;
-    std::vector<char *> h_tbl;
-    uint32_t *d_stamps = nullptr;
-    std::vector<int32_t> slot_of, expert_of;
-    std::vector<uint32_t> h_stamps;
-    uint32_t stamps_clock = 0xFFFFFFFFu;
-    bool tbl_dirty = false;
 };
 
-struct State {
+struct Cache {
+    // configuration (environment or moe_b200_configure)
     bool enabled = false, env_read = false, configured = false;
     int slots = 320;
     size_t budget = 30ull << 30;
-    size_t used = 0;
     bool claim_device = true;
     bool debug = false;
     bool layer_fused = true;      // one-kernel layer decode where supported
     std::string seed_path;
-    std::unordered_map<const char *, Entry *> by_data;
-    std::vector<Entry *> all;
-    uint32_t *d_stats = nullptr, *h_stats = nullptr, *d_clock = nullptr;
-    int *d_err = nullptr;
-    uint64_t timeout_ns_ep = 2000000000ull;   // expert-parallel arrival waits
-    uint64_t timeout_ns_kernel = 2000000000ull;   // waits inside the GEMV / layer / prefill kernels
-    uint32_t h_clock = 0;
+    // registry
+    std::unordered_map<const char *, Tensor *> by_ptr;
+    std::vector<Tensor *> tensors;
+    size_t pool_bytes = 0;
+    bool any_tiered = false;
+    // seed lists by tensor name, read on first registration
+    std::unordered_map<std::string, std::vector<int>> seeds;
+    bool seeds_read = false;
+    // device side
     int device = -1;
-    std::unordered_map<uint32_t, int> admission;
-    std::unordered_map<std::string, std::vector<int>> seed;
-    bool seed_loaded = false;
+    moe::CacheDev *dev = nullptr;           // registry pointer, clock, totals, copy jobs
+    moe::CacheTensorDev *d_reg = nullptr;   // registry array
+    int reg_cap = 0;
+    uint32_t *d_log = nullptr;              // [0] misses, [1] hits, [2..] miss log
+    int *d_err = nullptr;
+    uint64_t timeout_ns_ep = 2000000000ull;       // expert-parallel arrival waits
+    uint64_t timeout_ns_kernel = 2000000000ull;   // waits inside the GEMV / layer / prefill kernels
+    uint64_t idle_steps = 0;                // step calls with nothing tiered (no kernel launched)
+    uint64_t step_calls = 0;
     std::unordered_map<const void *, int> ptr_kind;   // 1 host, 2 device, 0 other
-    uint64_t steps = 0, hits = 0, misses = 0, promotions = 0, evictions = 0, overflow = 0;
 };
 
-State g;
+Cache g;
 std::recursive_mutex g_mu;
 thread_local std::string g_err;
 
@@ -120,21 +134,21 @@ int type_size(int t) {
 }
 int blck_size(int t) { return (t >= MOE_TYPE_Q2_K && t <= MOE_TYPE_Q6_K) ? 256 : 32; }
 
-// reference moe_type_supported (:407-421)
+// the eight formats of the reference's op (moe-cache.cu:407-421)
 bool type_supported(int t) { return type_size(t) != 0; }
 
 int env_int(const char *n, int fb) { const char *s = getenv(n); return s ? atoi(s) : fb; }
 double env_double(const char *n, double fb) { const char *s = getenv(n); return s ? atof(s) : fb; }
 
-// reference ggml_cuda_moe_cache_enabled (:345-363)
+// The drop-in's configuration variables (names as in moe-cache.cu:345-363),
+// read once unless moe_b200_configure set the configuration.
 void read_env() {
     if (g.env_read) return;
-    const char *env = getenv("GGML_CUDA_MOE_CACHE");
-    g.enabled = env && env[0] && env[0] != '0';
-    g.slots = env_int("GGML_CUDA_MOE_CACHE_SLOTS", g.slots);
-    if (g.slots < 0) g.slots = 0;
-    const double gb = env_double("GGML_CUDA_MOE_CACHE_BUDGET_GB", 0.0);
-    if (gb > 0) g.budget = static_cast<size_t>(gb * 1024.0 * 1024.0 * 1024.0);
+    const char *on = getenv("GGML_CUDA_MOE_CACHE");
+    g.enabled = on && on[0] && on[0] != '0';
+    g.slots = std::max(0, env_int("GGML_CUDA_MOE_CACHE_SLOTS", g.slots));
+    const double gib = env_double("GGML_CUDA_MOE_CACHE_BUDGET_GB", 0.0);
+    if (gib > 0) g.budget = static_cast<size_t>(gib * 1073741824.0);
     const char *seed = getenv("GGML_CUDA_MOE_CACHE_SEED");
     g.seed_path = seed ? seed : "";
     g.claim_device = env_int("GGML_CUDA_MOE_CACHE_DEVICE", 1) != 0;
@@ -142,8 +156,8 @@ void read_env() {
     g.layer_fused = env_int("GGML_CUDA_MOE_LAYER_FUSED", 1) != 0;
     g.env_read = true;
     if (g.enabled && g.debug)
-        fprintf(stderr, "moe-cache: enabled, slots=%d budget=%.1f GB\n", g.slots,
-                static_cast<double>(g.budget) / (1024.0 * 1024.0 * 1024.0));
+        fprintf(stderr, "[moe_b200] cache on: %d slots per tensor, %.1f GiB pool budget\n", g.slots,
+                static_cast<double>(g.budget) / 1073741824.0);
 }
 
 // 1 = pinned host, 2 = device memory of the current device, 0 = neither
@@ -172,315 +186,308 @@ bool contiguous(const moe_tensor *t) {
            t->nb[2] == t->nb[1] * static_cast<uint64_t>(t->ne[1]) && t->nb[3] == t->nb[2] * static_cast<uint64_t>(t->ne[2]);
 }
 
-// reference ggml_cuda_moe_cache_wants (:442-469), widened to HBM-resident tensors
+// The reference's eligibility test (moe-cache.cu:442-469), widened to
+// tensors in device memory (HBM-resident experts).
 int wants_locked(const moe_tensor *src0) {
     read_env();
     if (!g.enabled || !src0 || !src0->data) return 0;
-    if (src0->flags & MOE_TENSOR_NO_BUFFER) return 0;
+    if (src0->flags & (MOE_TENSOR_NO_BUFFER | MOE_TENSOR_VIEW)) return 0;
     const int kind = ptr_kind(src0->data);
     if (kind == 0 || (kind == 2 && !g.claim_device)) return 0;
-    if (!type_supported(src0->type)) return 0;
-    if (src0->ne[2] < 2 || src0->ne[3] != 1 || (src0->flags & MOE_TENSOR_VIEW)) return 0;
-    if (!contiguous(src0)) return 0;
-    return 1;
+    if (!type_supported(src0->type) || src0->ne[2] < 2 || src0->ne[3] != 1) return 0;
+    return contiguous(src0) ? 1 : 0;
 }
 
-int init_device_globals() {
+uint32_t *clock_ptr() {
+    return reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(g.dev) + offsetof(moe::CacheDev, clock));
+}
+
+// The cache's device state on the current device, made on first use.
+int ensure_device() {
     int dev = 0;
     CK(cudaGetDevice(&dev));
-    if (g.d_stats) {
+    if (g.dev) {
         if (dev != g.device) return fail(MOE_ERR_STATE, "moe-cache state belongs to device %d, called on %d", g.device, dev);
         return MOE_OK;
     }
-    CK(cudaMalloc(&g.d_stats, sizeof(uint32_t) * kStatsWords));
-    CK(cudaMallocHost(&g.h_stats, sizeof(uint32_t) * kStatsWords));
-    CK(cudaMemset(g.d_stats, 0, sizeof(uint32_t) * kStatsWords));
-    CK(cudaMalloc(&g.d_clock, sizeof(uint32_t)));
-    CK(cudaMemset(g.d_clock, 0, sizeof(uint32_t)));
+    CK(cudaMalloc(&g.dev, sizeof(moe::CacheDev)));
+    CK(cudaMemset(g.dev, 0, sizeof(moe::CacheDev)));
+    CK(cudaMalloc(&g.d_log, sizeof(uint32_t) * kLogWords));
+    CK(cudaMemset(g.d_log, 0, sizeof(uint32_t) * kLogWords));
     CK(cudaMalloc(&g.d_err, sizeof(int)));
     CK(cudaMemset(g.d_err, 0, sizeof(int)));
-    g.h_clock = 0;
     g.device = dev;
     return MOE_OK;
 }
 
-// reference moe_load_seed (:487-523): lines of "tensorname id1,id2,..."
-void load_seed() {
-    if (g.seed_loaded) return;
-    g.seed_loaded = true;
+// ---- seed lists -------------------------------------------------------------
+// One line per tensor: "<tensor name> <id>,<id>,..." (the format written by
+// the reference's tools/make_seed.py). Ids are read up to the first token
+// that is not an integer.
+bool parse_id(const std::string &tok, int *out) {
+    size_t a = 0, b = tok.size();
+    while (a < b && isspace(static_cast<unsigned char>(tok[a]))) ++a;
+    while (b > a && isspace(static_cast<unsigned char>(tok[b - 1]))) --b;
+    if (a == b) return false;
+    size_t i = a;
+    if (tok[i] == '+' || tok[i] == '-') ++i;
+    if (i == b) return false;
+    long v = 0;
+    for (; i < b; ++i) {
+        if (tok[i] < '0' || tok[i] > '9') return false;
+        v = v * 10 + (tok[i] - '0');
+        if (v > (1L << 30)) return false;
+    }
+    *out = static_cast<int>(tok[a] == '-' ? -v : v);
+    return true;
+}
+
+void read_seeds() {
+    if (g.seeds_read) return;
+    g.seeds_read = true;
     if (g.seed_path.empty()) return;
-    FILE *f = fopen(g.seed_path.c_str(), "r");
-    if (!f) {
-        fprintf(stderr, "moe-cache: seed file %s not found, starting cold\n", g.seed_path.c_str());
+    std::ifstream in(g.seed_path);
+    if (!in) {
+        fprintf(stderr, "[moe_b200] no seed file at %s; pools start empty\n", g.seed_path.c_str());
         return;
     }
-    std::vector<char> line(1 << 16);
-    while (fgets(line.data(), static_cast<int>(line.size()), f)) {
-        char *sp = strchr(line.data(), ' ');
-        if (!sp) continue;
-        *sp = 0;
+    std::string line;
+    while (std::getline(in, line)) {
+        if (!line.empty() && line.back() == '\r') line.pop_back();
+        const size_t sp = line.find(' ');
+        if (sp == std::string::npos) continue;
         std::vector<int> ids;
-        char *p = sp + 1;
-        while (*p) {
-            char *end = nullptr;
-            const long v = strtol(p, &end, 10);
-            if (end == p) break;
-            ids.push_back(static_cast<int>(v));
-            p = (*end == ',') ? end + 1 : end;
+        for (size_t pos = sp + 1;;) {
+            const size_t comma = line.find(',', pos);
+            int id = 0;
+            if (!parse_id(line.substr(pos, comma == std::string::npos ? std::string::npos : comma - pos), &id)) break;
+            ids.push_back(id);
+            if (comma == std::string::npos) break;
+            pos = comma + 1;
         }
-        g.seed[line.data()] = std::move(ids);
+        g.seeds[line.substr(0, sp)] = std::move(ids);
     }
-    fclose(f);
-    if (g.debug) fprintf(stderr, "moe-cache: loaded seed for %zu tensors from %s\n", g.seed.size(), g.seed_path.c_str());
+    if (g.debug) fprintf(stderr, "[moe_b200] seed lists for %zu tensors from %s\n", g.seeds.size(), g.seed_path.c_str());
 }
 
-char *host_tag(const char *p) { return reinterpret_cast<char *>(reinterpret_cast<uintptr_t>(p) | 1u); }
+// ---- registry ---------------------------------------------------------------
+char *tagged_host(const char *p) { return reinterpret_cast<char *>(reinterpret_cast<uintptr_t>(p) | 1u); }
+size_t round_up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// Frees an entry's device resources and takes it out of the lookup map. It
-// stays in g.all so tensor ids (and miss-log packing) remain stable.
-void retire(Entry *e) {
-    cudaDeviceSynchronize();   // no kernel may still read its table or pool
-    cudaFree(e->pool);
-    cudaFree(e->d_tbl);
-    cudaFree(e->d_stamps);
-    g.used -= static_cast<size_t>(e->n_slots) * e->expert_bytes;
-    e->pool = nullptr;
-    e->d_tbl = nullptr;
-    e->d_stamps = nullptr;
-    e->n_slots = 0;
-    e->expert_of.clear();
-    e->slot_of.assign(e->slot_of.size(), -1);
-    e->tbl_dirty = false;
-    e->host = false;
-    e->dead = true;
-    g.by_data.erase(e->data);
+// Pool slots for a tiered tensor: the configured count, capped by the budget
+// left, by free HBM beyond the reserve, and by the expert count.
+int pool_slots(const Tensor &t) {
+    if (!t.tiered) return 0;
+    int64_t s = g.slots;
+    const size_t budget_left = g.budget > g.pool_bytes ? g.budget - g.pool_bytes : 0;
+    s = std::min<int64_t>(s, static_cast<int64_t>(budget_left / t.expert_bytes));
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) { cudaGetLastError(); return -1; }
+    const size_t usable = free_b > kHbmReserve ? free_b - kHbmReserve : 0;
+    s = std::min<int64_t>(s, static_cast<int64_t>(usable / t.expert_bytes));
+    return static_cast<int>(std::min<int64_t>(s, t.n_experts));
 }
 
-// reference moe_get_or_create (:525-622)
-int get_or_create(const moe_tensor *src0, cudaStream_t stream, Entry **out) {
-    int rc = init_device_globals();
+// The registry array has room for tensor id `id` (grows by doubling; the
+// promotion pass reads it, so the device is idle while it moves).
+int reserve_registry(int id) {
+    if (id < g.reg_cap) return MOE_OK;
+    const int cap = std::max(256, 2 * g.reg_cap);
+    moe::CacheTensorDev *fresh = nullptr;
+    CK(cudaDeviceSynchronize());
+    CK(cudaMalloc(&fresh, sizeof(moe::CacheTensorDev) * cap));
+    CK(cudaMemset(fresh, 0, sizeof(moe::CacheTensorDev) * cap));
+    if (g.d_reg) CK(cudaMemcpy(fresh, g.d_reg, sizeof(moe::CacheTensorDev) * g.reg_cap, cudaMemcpyDeviceToDevice));
+    CK(cudaMemcpy(reinterpret_cast<char *>(g.dev) + offsetof(moe::CacheDev, reg), &fresh, sizeof(fresh),
+                  cudaMemcpyHostToDevice));
+    if (g.d_reg) CK(cudaFree(g.d_reg));
+    g.d_reg = fresh;
+    g.reg_cap = cap;
+    return MOE_OK;
+}
+
+int publish(const Tensor &t, cudaStream_t st) {
+    moe::CacheTensorDev d{};
+    d.tbl = t.table;
+    d.stamps = t.stamps;
+    d.slot_of = t.slot_map;
+    d.expert_of = t.slot_owner;
+    d.seen = t.seen;
+    d.host = t.data;
+    d.pool = t.pool;
+    d.expert_bytes = t.expert_bytes;
+    d.n_experts = t.n_experts;
+    d.n_slots = t.n_slots;
+    d.live = (t.tiered && !t.retired) ? 1 : 0;
+    CK(cudaMemcpyAsync(g.d_reg + t.id, &d, sizeof(d), cudaMemcpyHostToDevice, st));
+    const int32_t n = static_cast<int32_t>(g.tensors.size());
+    CK(cudaMemcpyAsync(reinterpret_cast<char *>(g.dev) + offsetof(moe::CacheDev, n_tensors), &n, sizeof(n),
+                       cudaMemcpyHostToDevice, st));
+    return MOE_OK;
+}
+
+void release(Tensor *t) {
+    cudaFree(t->block);
+    cudaFree(t->pool);
+    t->block = t->pool = nullptr;
+    t->table = nullptr;
+    t->stamps = nullptr;
+    t->slot_map = t->slot_owner = nullptr;
+    t->seen = nullptr;
+}
+
+// A different tensor now lives at this tensor's address: free its device
+// state (after the device is idle) and mark it dead. It keeps its id so
+// the ids of later tensors, packed into miss-log entries, stay valid.
+int retire(Tensor *t) {
+    CK(cudaDeviceSynchronize());
+    release(t);
+    g.pool_bytes -= static_cast<size_t>(t->n_slots) * t->expert_bytes;
+    t->n_slots = 0;
+    t->retired = true;
+    g.by_ptr.erase(t->data);
+    moe::CacheTensorDev dead{};
+    CK(cudaMemcpy(g.d_reg + t->id, &dead, sizeof(dead), cudaMemcpyHostToDevice));
+    return MOE_OK;
+}
+
+// The cache's record of src0, registering it on first sight: device block,
+// pool, initial table (tagged host addresses or direct device addresses),
+// seeded slots, and its registry entry for the promotion pass.
+int enroll(const moe_tensor *src0, cudaStream_t st, Tensor **out) {
+    int rc = ensure_device();
     if (rc) return rc;
-    auto it = g.by_data.find(static_cast<const char *>(src0->data));
-    if (it != g.by_data.end()) {
-        Entry *old = it->second;
-        if (old->type == src0->type && old->n_experts == src0->ne[2] && old->expert_bytes == src0->nb[2] &&
-            old->row_bytes == src0->nb[1] && old->rows == src0->ne[1] && old->cols == src0->ne[0]) {
-            *out = old;
+    const char *key = static_cast<const char *>(src0->data);
+    auto hit = g.by_ptr.find(key);
+    if (hit != g.by_ptr.end()) {
+        Tensor *t = hit->second;
+        if (t->type == src0->type && t->n_experts == src0->ne[2] && t->expert_bytes == src0->nb[2] &&
+            t->row_bytes == src0->nb[1] && t->rows == src0->ne[1] && t->cols == src0->ne[0]) {
+            *out = t;
             return MOE_OK;
         }
-        // the registry is keyed by data pointer (reference :530); a different
-        // tensor now lives at this address, so the old entry is retired
-        retire(old);
-    }
-
-    Entry *e = new Entry();
-    e->id = static_cast<int32_t>(g.all.size());
-    e->type = src0->type;
-    e->data = static_cast<const char *>(src0->data);
-    e->expert_bytes = src0->nb[2];
-    e->row_bytes = src0->nb[1];
-    e->rows = src0->ne[1];
-    e->cols = src0->ne[0];
-    e->n_experts = static_cast<int>(src0->ne[2]);
-    e->host = ptr_kind(src0->data) == 1;
-    e->name = src0->name ? src0->name : "";
-    if (e->n_experts > 4096) { delete e; return fail(MOE_ERR_UNSUPPORTED, "more than 4096 experts"); }
-
-    int slots = 0;
-    size_t free_vram = 0, total_vram = 0;
-    if (e->host) {
-        slots = g.slots;
-        const size_t free_budget = g.budget > g.used ? g.budget - g.used : 0;
-        if (static_cast<size_t>(slots) * e->expert_bytes > free_budget) slots = static_cast<int>(free_budget / e->expert_bytes);
-        if (cudaMemGetInfo(&free_vram, &total_vram) != cudaSuccess) { delete e; return fail(MOE_ERR_CUDA, "cudaMemGetInfo failed"); }
-        const size_t usable = free_vram > kVramMargin ? free_vram - kVramMargin : 0;
-        if (static_cast<size_t>(slots) * e->expert_bytes > usable) slots = static_cast<int>(usable / e->expert_bytes);
-        if (slots > e->n_experts) slots = e->n_experts;
-    }
-    e->n_slots = slots;
-    e->h_tbl.resize(e->n_experts);
-    for (int i = 0; i < e->n_experts; ++i) {
-        const char *p = e->data + static_cast<size_t>(i) * e->expert_bytes;
-        e->h_tbl[i] = e->host ? host_tag(p) : const_cast<char *>(p);
-    }
-    if (cudaMalloc(&e->d_tbl, sizeof(char *) * e->n_experts) != cudaSuccess ||
-        cudaMalloc(&e->d_stamps, sizeof(uint32_t) * e->n_experts) != cudaSuccess) {
-        cudaGetLastError();
-        cudaFree(e->d_tbl);
-        delete e;
-        return fail(MOE_ERR_OOM, "table allocation failed");
-    }
-    CK(cudaMemsetAsync(e->d_stamps, 0, sizeof(uint32_t) * e->n_experts, stream));
-    e->h_stamps.assign(e->n_experts, 0);
-    e->slot_of.assign(e->n_experts, -1);
-    e->expert_of.assign(slots, -1);
-    if (slots > 0) {
-        if (cudaMalloc(&e->pool, static_cast<size_t>(slots) * e->expert_bytes) != cudaSuccess) {
-            cudaGetLastError();
-            cudaFree(e->d_tbl);
-            cudaFree(e->d_stamps);
-            delete e;
-            return fail(MOE_ERR_OOM, "pool allocation failed");
-        }
-        g.used += static_cast<size_t>(slots) * e->expert_bytes;
-    }
-    g.by_data[e->data] = e;
-    g.all.push_back(e);
-
-    // seeding: all slots free, seeded experts take slots 0..seeded-1 (:584-609)
-    load_seed();
-    auto sit = g.seed.find(e->name);
-    if (sit != g.seed.end() && e->n_slots > 0) {
-        int seeded = 0;
-        for (const int expert : sit->second) {
-            if (seeded >= e->n_slots) break;
-            if (expert < 0 || expert >= e->n_experts || e->slot_of[expert] >= 0) continue;
-            const int slot = seeded;
-            CK(cudaMemcpyAsync(e->pool + static_cast<size_t>(slot) * e->expert_bytes,
-                               e->data + static_cast<size_t>(expert) * e->expert_bytes, e->expert_bytes,
-                               cudaMemcpyHostToDevice, stream));
-            e->h_tbl[expert] = e->pool + static_cast<size_t>(slot) * e->expert_bytes;
-            e->slot_of[expert] = slot;
-            e->expert_of[slot] = expert;
-            seeded++;
-        }
-        if (seeded > 0 && g.debug) fprintf(stderr, "moe-cache: seeded %d/%d experts for %s\n", seeded, e->n_slots, e->name.c_str());
-    }
-    // one table upload, ordered after the seed copies on the same stream (:611-613)
-    CK(cudaMemcpyAsync(e->d_tbl, e->h_tbl.data(), sizeof(char *) * e->n_experts, cudaMemcpyHostToDevice, stream));
-    if (g.debug)
-        fprintf(stderr, "moe-cache: registered %s type=%d experts=%d slot_bytes=%zu slots=%d %s\n", e->name.c_str(),
-                e->type, e->n_experts, e->expert_bytes, e->n_slots, e->host ? "(host-tiered)" : "(HBM-resident)");
-    *out = e;
-    return MOE_OK;
-}
-
-// reference moe_acquire_slot (:628-667)
-int acquire_slot(Entry *e, cudaStream_t stream, int *slot_out) {
-    *slot_out = -1;
-    if (e->n_slots == 0) return MOE_OK;
-    for (int s = 0; s < e->n_slots; ++s)
-        if (e->expert_of[s] < 0) { *slot_out = s; return MOE_OK; }
-    if (e->stamps_clock != g.h_clock) {
-        CK(cudaMemcpyAsync(e->h_stamps.data(), e->d_stamps, sizeof(uint32_t) * e->n_experts, cudaMemcpyDeviceToHost, stream));
-        CK(cudaStreamSynchronize(stream));
-        e->stamps_clock = g.h_clock;
-    }
-    int victim_slot = -1;
-    uint32_t best = UINT32_MAX;
-    for (int s = 0; s < e->n_slots; ++s) {
-        const int expert = e->expert_of[s];
-        const uint32_t stamp = expert >= 0 ? e->h_stamps[expert] : 0;
-        if (stamp < best) { best = stamp; victim_slot = s; }
-    }
-    if (victim_slot < 0) return MOE_OK;
-    const int victim = e->expert_of[victim_slot];
-    if (victim >= 0) {
-        e->slot_of[victim] = -1;
-        e->h_tbl[victim] = host_tag(e->data + static_cast<size_t>(victim) * e->expert_bytes);
-        e->tbl_dirty = true;
-        g.evictions++;
-    }
-    e->expert_of[victim_slot] = -1;
-    *slot_out = victim_slot;
-    return MOE_OK;
-}
-
-// reference ggml_cuda_moe_cache_step (:669-775)
-int step_locked(cudaStream_t stream) {
-    if (!g.enabled || g.all.empty()) return MOE_OK;
-    bool any_host = false;
-    for (const Entry *e : g.all) any_host |= e->host;
-    if (!any_host) { g.steps++; return MOE_OK; }
-
-    CK(cudaMemcpyAsync(g.h_stats, g.d_stats, sizeof(uint32_t) * kStatsWords, cudaMemcpyDeviceToHost, stream));
-    CK(cudaStreamSynchronize(stream));
-    uint32_t n = g.h_stats[0];
-    if (n > kLogCap) { g.overflow += n - kLogCap; n = kLogCap; }
-    const uint32_t step_hits = g.h_stats[1];
-
-    g.h_clock += 1;
-    CK(cudaMemcpyAsync(g.d_clock, &g.h_clock, sizeof(uint32_t), cudaMemcpyHostToDevice, stream));
-    CK(cudaMemsetAsync(g.d_stats, 0, 2 * sizeof(uint32_t), stream));
-    g.steps++;
-    g.hits += step_hits;
-    g.misses += g.h_stats[0];
-    if (g.debug && g.steps % 64 == 0) {
-        size_t resident = 0;
-        for (const Entry *e : g.all)
-            for (int s = 0; s < e->n_slots; ++s) resident += e->expert_of[s] >= 0;
-        fprintf(stderr, "moe-cache: step %llu: hits=%u misses=%u (totals: hits %llu, misses %llu, promos %llu), resident %zu\n",
-                static_cast<unsigned long long>(g.steps), step_hits, n, static_cast<unsigned long long>(g.hits),
-                static_cast<unsigned long long>(g.misses), static_cast<unsigned long long>(g.promotions), resident);
-    }
-    if (n == 0) return MOE_OK;
-
-    // order-independent processing: sort this step's log
-    uint32_t *log = g.h_stats + moe::GEMV_LOG_BASE;
-    std::sort(log, log + n);
-    int promoted = 0;
-    for (uint32_t i = 0; i < n && promoted < kMaxPromotions; ++i) {
-        const uint32_t packed = log[i];
-        const int32_t cid = static_cast<int32_t>(packed >> 12);
-        const int32_t expert = static_cast<int32_t>(packed & 0xFFF);
-        int &count = g.admission[packed];
-        count += 1;
-        if (count < 2) continue;
-        count = 0;
-        if (cid < 0 || cid >= static_cast<int>(g.all.size())) continue;
-        Entry *e = g.all[cid];
-        if (e->dead || expert < 0 || expert >= e->n_experts || e->slot_of[expert] >= 0) continue;
-        int slot = -1;
-        const int rc = acquire_slot(e, stream, &slot);
+        rc = retire(t);
         if (rc) return rc;
-        if (slot < 0) continue;
-        CK(cudaMemcpyAsync(e->pool + static_cast<size_t>(slot) * e->expert_bytes,
-                           e->data + static_cast<size_t>(expert) * e->expert_bytes, e->expert_bytes,
-                           cudaMemcpyHostToDevice, stream));
-        e->h_tbl[expert] = e->pool + static_cast<size_t>(slot) * e->expert_bytes;
-        e->tbl_dirty = true;
-        e->slot_of[expert] = slot;
-        e->expert_of[slot] = expert;
-        promoted++;
-        g.promotions++;
     }
-    for (Entry *e : g.all) {
-        if (e->dead || !e->tbl_dirty) continue;
-        CK(cudaMemcpyAsync(e->d_tbl, e->h_tbl.data(), sizeof(char *) * e->n_experts, cudaMemcpyHostToDevice, stream));
-        e->tbl_dirty = false;
+    if (src0->ne[2] > kMaxExperts) return fail(MOE_ERR_UNSUPPORTED, "more than %d experts", kMaxExperts);
+
+    Tensor *t = new Tensor();
+    t->id = static_cast<int32_t>(g.tensors.size());
+    t->type = src0->type;
+    t->data = key;
+    t->expert_bytes = src0->nb[2];
+    t->row_bytes = src0->nb[1];
+    t->rows = src0->ne[1];
+    t->cols = src0->ne[0];
+    t->n_experts = static_cast<int>(src0->ne[2]);
+    t->tiered = ptr_kind(src0->data) == 1;
+    t->name = src0->name ? src0->name : "";
+    t->n_slots = pool_slots(*t);
+    if (t->n_slots < 0) { delete t; return fail(MOE_ERR_CUDA, "cudaMemGetInfo failed"); }
+    rc = reserve_registry(t->id);
+    if (rc) { delete t; return rc; }
+
+    const size_t E = static_cast<size_t>(t->n_experts);
+    const size_t o_stamps = round_up256(sizeof(char *) * E), o_map = o_stamps + round_up256(4 * E),
+                 o_owner = o_map + round_up256(4 * E), o_seen = o_owner + round_up256(4 * (t->n_slots + 1)),
+                 bytes = o_seen + round_up256(E);
+    if (cudaMalloc(&t->block, bytes) != cudaSuccess ||
+        (t->n_slots > 0 && cudaMalloc(&t->pool, static_cast<size_t>(t->n_slots) * t->expert_bytes) != cudaSuccess)) {
+        cudaGetLastError();
+        release(t);
+        delete t;
+        return fail(MOE_ERR_OOM, "cache allocation for %s failed", src0->name ? src0->name : "<tensor>");
     }
-    if (g.admission.size() > kAdmissionGc) {
-        for (auto it = g.admission.begin(); it != g.admission.end();) {
-            if (it->second == 0) it = g.admission.erase(it);
-            else ++it;
+    t->table = reinterpret_cast<char **>(t->block);
+    t->stamps = reinterpret_cast<uint32_t *>(t->block + o_stamps);
+    t->slot_map = reinterpret_cast<int32_t *>(t->block + o_map);
+    t->slot_owner = reinterpret_cast<int32_t *>(t->block + o_owner);
+    t->seen = reinterpret_cast<uint8_t *>(t->block + o_seen);
+    g.pool_bytes += static_cast<size_t>(t->n_slots) * t->expert_bytes;
+    g.any_tiered |= t->tiered;
+
+    // initial state on the host, then one upload per array
+    std::vector<char *> table(E);
+    std::vector<int32_t> slot_map(E, -1), slot_owner(static_cast<size_t>(t->n_slots), -1);
+    for (size_t x = 0; x < E; ++x) {
+        const char *p = t->data + x * t->expert_bytes;
+        table[x] = t->tiered ? tagged_host(p) : const_cast<char *>(p);
+    }
+    read_seeds();
+    const auto seed = g.seeds.find(t->name);
+    int filled = 0;
+    if (seed != g.seeds.end()) {
+        for (const int x : seed->second) {
+            if (filled == t->n_slots) break;
+            if (x < 0 || x >= t->n_experts || slot_map[x] >= 0) continue;
+            char *slot = t->pool + static_cast<size_t>(filled) * t->expert_bytes;
+            CK(cudaMemcpyAsync(slot, t->data + static_cast<size_t>(x) * t->expert_bytes, t->expert_bytes,
+                               cudaMemcpyHostToDevice, st));
+            table[x] = slot;
+            slot_map[x] = filled;
+            slot_owner[filled] = x;
+            ++filled;
         }
+    }
+    CK(cudaMemsetAsync(t->stamps, 0, 4 * E, st));
+    CK(cudaMemsetAsync(t->seen, 0, E, st));
+    CK(cudaMemcpyAsync(t->slot_map, slot_map.data(), 4 * E, cudaMemcpyHostToDevice, st));
+    if (t->n_slots > 0)
+        CK(cudaMemcpyAsync(t->slot_owner, slot_owner.data(), 4 * static_cast<size_t>(t->n_slots), cudaMemcpyHostToDevice, st));
+    // the table goes last: no kernel reads a slot before its expert is copied
+    CK(cudaMemcpyAsync(t->table, table.data(), sizeof(char *) * E, cudaMemcpyHostToDevice, st));
+    g.by_ptr[key] = t;
+    g.tensors.push_back(t);
+    rc = publish(*t, st);
+    if (rc) return rc;
+    // the host vectors above are pageable: the copies have taken them by now
+    if (g.debug)
+        fprintf(stderr, "[moe_b200] tensor %d %s: type %d, %d experts of %llu B, %s, %d slots (%d seeded)\n", t->id,
+                t->name.c_str(), t->type, t->n_experts, static_cast<unsigned long long>(t->expert_bytes),
+                t->tiered ? "pinned host memory" : "HBM", t->n_slots, filled);
+    *out = t;
+    return MOE_OK;
+}
+
+// ---- the step between graphs ---------------------------------------------------
+int step_locked(cudaStream_t st) {
+    if (!g.enabled || g.tensors.empty()) return MOE_OK;
+    if (!g.any_tiered) { g.idle_steps++; return MOE_OK; }
+    CK(moe::launch_promote(g.dev, g.d_log, kLogCap, st));
+    if (g.debug && ++g.step_calls % 64 == 0) {
+        moe::CacheDev s;
+        CK(cudaStreamSynchronize(st));
+        CK(cudaMemcpy(&s, g.dev, sizeof(s), cudaMemcpyDeviceToHost));
+        fprintf(stderr, "[moe_b200] after %llu steps: %llu hits, %llu misses, %llu promoted, %llu evicted\n",
+                s.steps, s.hits, s.misses, s.promotions, s.evictions);
     }
     return MOE_OK;
 }
 
 void free_all() {
-    for (Entry *e : g.all) {
-        cudaFree(e->pool);
-        cudaFree(e->d_tbl);
-        cudaFree(e->d_stamps);
-        delete e;
+    if (g.dev) cudaDeviceSynchronize();
+    for (Tensor *t : g.tensors) {
+        release(t);
+        delete t;
     }
-    g.all.clear();
-    g.by_data.clear();
-    if (g.d_stats) cudaFree(g.d_stats);
-    if (g.h_stats) cudaFreeHost(g.h_stats);
-    if (g.d_clock) cudaFree(g.d_clock);
-    if (g.d_err) cudaFree(g.d_err);
-    g.d_stats = g.h_stats = g.d_clock = nullptr;
+    g.tensors.clear();
+    g.by_ptr.clear();
+    cudaFree(g.dev);
+    cudaFree(g.d_reg);
+    cudaFree(g.d_log);
+    cudaFree(g.d_err);
+    g.dev = nullptr;
+    g.d_reg = nullptr;
+    g.reg_cap = 0;
+    g.d_log = nullptr;
     g.d_err = nullptr;
-    g.h_clock = 0;
-    g.used = 0;
     g.device = -1;
-    g.admission.clear();
-    g.seed.clear();
-    g.seed_loaded = false;
+    g.pool_bytes = 0;
+    g.any_tiered = false;
+    g.seeds.clear();
+    g.seeds_read = false;
     g.ptr_kind.clear();
-    g.steps = g.hits = g.misses = g.promotions = g.evictions = g.overflow = 0;
+    g.idle_steps = g.step_calls = 0;
 }
 
 // common GEMV argument setup for the boundary call and the layer path
@@ -517,21 +524,21 @@ int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
     if (c.fd && ((c.fd->gate && !aligned16(c.fd->gate)) || (c.fd->shared_up && !aligned16(c.fd->shared_up)) ||
                  (c.fd->shared_gate && !aligned16(c.fd->shared_gate))))
         return fail(MOE_ERR_UNSUPPORTED, "gate / shared expert data must be 16-byte aligned");
-    Entry *e = nullptr;
-    int rc = get_or_create(src0, stream, &e);
+    Tensor *e = nullptr;
+    int rc = enroll(src0, stream, &e);
     if (rc) return rc;
     const moe_fusion_device *fd = c.fd;
     const bool use_gate = fd && fd->gate;
-    Entry *ge = nullptr;
+    Tensor *ge = nullptr;
     if (use_gate && c.gate && wants_locked(c.gate)) {
         if (c.gate->type != src0->type || c.gate->ne[0] != src0->ne[0] || c.gate->ne[1] != src0->ne[1])
             return fail(MOE_ERR_UNSUPPORTED, "fused gate must match the up tensor's type and shape");
-        rc = get_or_create(c.gate, stream, &ge);
+        rc = enroll(c.gate, stream, &ge);
         if (rc) return rc;
     }
     moe::GemvArgs a{};
-    a.tbl = e->d_tbl;
-    a.stamps = e->d_stamps;
+    a.tbl = e->table;
+    a.stamps = e->stamps;
     a.cache_id = e->id;
     a.use_gate = use_gate ? 1 : 0;
     a.has_fusion = fd && (fd->gate || fd->x_bias || fd->gate_bias || fd->x_scale || fd->gate_scale) ? 1 : 0;
@@ -539,8 +546,8 @@ int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
     a.tma_main = tma_main;
     if (use_gate) {
         if (ge) {
-            a.tbl_gate = ge->d_tbl;
-            a.stamps_gate = ge->d_stamps;
+            a.tbl_gate = ge->table;
+            a.stamps_gate = ge->stamps;
             a.cache_id_gate = ge->id;
             a.tma_gate = aligned16(ge->data) && (ge->expert_bytes % 16) == 0;
         } else {
@@ -569,8 +576,8 @@ int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
     }
     a.shared_y = c.shared_y;
     a.shared_y_stride_col = c.shared_y_stride_col;
-    a.stats = g.d_stats;
-    a.clock = g.d_clock;
+    a.stats = g.d_log;
+    a.clock = clock_ptr();
     a.log_cap = kLogCap;
     a.y = c.src1;
     a.stride_col_y = c.stride_col_y;
@@ -641,12 +648,12 @@ LayerWs layer_ws(const moe_layer_desc *L, int64_t n_tok, char *base) {
 int layer_tensor(const moe_tensor *t, bool registered, cudaStream_t st, moe::LayerTensor *out) {
     *out = moe::LayerTensor{};
     if (registered) {
-        Entry *e = nullptr;
-        const int rc = get_or_create(t, st, &e);
+        Tensor *e = nullptr;
+        const int rc = enroll(t, st, &e);
         if (rc) return rc;
-        out->stamps = e->d_stamps;
+        out->stamps = e->stamps;
         out->cache_id = e->id;
-        if (e->host) out->tbl = e->d_tbl;
+        if (e->tiered) out->tbl = e->table;
     }
     out->dense = static_cast<const char *>(t->data);
     out->expert_bytes = t->nb[2];
@@ -722,8 +729,8 @@ int layer_args(const moe_layer_desc *L, const float *x, const float *logits, flo
     a.ids_out = w.ids;
     a.w_out = w.w;
     a.out = out;
-    a.stats = g.d_stats;
-    a.clock = g.d_clock;
+    a.stats = g.d_log;
+    a.clock = clock_ptr();
     a.log_cap = kLogCap;
     a.gbar = w.gbar;
     a.h_tag = w.h_tag;
@@ -839,7 +846,7 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
         const PrefillWs w = prefill_ws(src0, n_tok, k, x_rows, workspace);
         if (!workspace || workspace_bytes < w.bytes)
             return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
-        int rc = init_device_globals();
+        int rc = ensure_device();
         if (rc) return rc;
         const int ntc = chunk_tokens_for(src0, n_tok * k);
         if (reuse_groups) {
@@ -998,7 +1005,7 @@ int ggml_cuda_moe_cache_step(moe_stream_t stream) {
 
 int ggml_cuda_moe_cache_active(void) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
-    return g.all.empty() ? 0 : 1;
+    return g.tensors.empty() ? 0 : 1;
 }
 
 // reference ggml_cuda_moe_cache_pin_host (:372-405)
@@ -1059,40 +1066,49 @@ int moe_b200_reset(void) {
 int moe_b200_stats(moe_cache_stats *out) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     if (!out) return fail(MOE_ERR_INVALID, "null stats");
-    uint64_t resident = 0;
-    for (const Entry *e : g.all)
-        for (int s = 0; s < e->n_slots; ++s) resident += e->expert_of[s] >= 0;
-    out->steps = g.steps;
-    out->hits = g.hits;
-    out->misses = g.misses;
-    out->promotions = g.promotions;
-    out->evictions = g.evictions;
-    out->resident = resident;
-    out->registered = g.all.size();
-    out->log_overflow = g.overflow;
-    out->pool_bytes = g.used;
+    memset(out, 0, sizeof(*out));
+    out->registered = g.tensors.size();
+    out->pool_bytes = g.pool_bytes;
+    out->steps = g.idle_steps;
+    if (!g.dev) return MOE_OK;
+    // totals live on the device (the promotion pass keeps them)
+    moe::CacheDev s;
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(&s, g.dev, sizeof(s), cudaMemcpyDeviceToHost));
+    out->steps += s.steps;
+    out->hits = s.hits;
+    out->misses = s.misses;
+    out->promotions = s.promotions;
+    out->evictions = s.evictions;
+    out->log_overflow = s.overflow;
+    for (const Tensor *t : g.tensors) {
+        if (t->retired || t->n_slots == 0) continue;
+        std::vector<int32_t> owner(static_cast<size_t>(t->n_slots));
+        CK(cudaMemcpy(owner.data(), t->slot_owner, 4 * owner.size(), cudaMemcpyDeviceToHost));
+        for (const int32_t x : owner) out->resident += x >= 0;
+    }
     return MOE_OK;
 }
 
 int moe_b200_table(const void *data, int32_t *slot_of, int32_t n_experts, int32_t *n_slots, int32_t *tensor_id) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
-    auto it = g.by_data.find(static_cast<const char *>(data));
-    if (it == g.by_data.end()) return fail(MOE_ERR_INVALID, "tensor is not registered");
-    Entry *e = it->second;
-    if (n_experts < e->n_experts) return fail(MOE_ERR_INVALID, "slot_of too small");
-    std::vector<char *> tbl(e->n_experts);
+    auto it = g.by_ptr.find(static_cast<const char *>(data));
+    if (it == g.by_ptr.end()) return fail(MOE_ERR_INVALID, "tensor is not registered");
+    const Tensor *t = it->second;
+    if (n_experts < t->n_experts) return fail(MOE_ERR_INVALID, "slot_of too small");
+    std::vector<char *> tbl(t->n_experts);
     CK(cudaDeviceSynchronize());
-    CK(cudaMemcpy(tbl.data(), e->d_tbl, sizeof(char *) * e->n_experts, cudaMemcpyDeviceToHost));
-    for (int i = 0; i < e->n_experts; ++i) {
+    CK(cudaMemcpy(tbl.data(), t->table, sizeof(char *) * t->n_experts, cudaMemcpyDeviceToHost));
+    const uintptr_t pool = reinterpret_cast<uintptr_t>(t->pool);
+    const uintptr_t pool_end = pool + static_cast<uintptr_t>(t->n_slots) * t->expert_bytes;
+    for (int i = 0; i < t->n_experts; ++i) {
         const uintptr_t p = reinterpret_cast<uintptr_t>(tbl[i]);
         if (p & 1u) slot_of[i] = -1;
-        else if (e->pool && p >= reinterpret_cast<uintptr_t>(e->pool) &&
-                 p < reinterpret_cast<uintptr_t>(e->pool) + static_cast<uintptr_t>(e->n_slots) * e->expert_bytes)
-            slot_of[i] = static_cast<int32_t>((p - reinterpret_cast<uintptr_t>(e->pool)) / e->expert_bytes);
+        else if (t->pool && p >= pool && p < pool_end) slot_of[i] = static_cast<int32_t>((p - pool) / t->expert_bytes);
         else slot_of[i] = -2;
     }
-    if (n_slots) *n_slots = e->n_slots;
-    if (tensor_id) *tensor_id = e->id;
+    if (n_slots) *n_slots = t->n_slots;
+    if (tensor_id) *tensor_id = t->id;
     return MOE_OK;
 }
 
@@ -1497,7 +1513,7 @@ int moe_b200_ep_dispatch(const void *const *peer_ptrs, int32_t world, int32_t ra
     if (!peer_ptrs || !ids || !x || !scratch || world < 1 || world > 8 || rank < 0 || rank >= world || k < 1 ||
         n_entries < 0 || n_entries > cap || H % 4 || cap >= (int64_t{1} << 31) / world)
         return fail(MOE_ERR_INVALID, "bad expert-parallel dispatch arguments");
-    int rc = init_device_globals();
+    int rc = ensure_device();
     if (rc) return rc;
     if (!aligned16(x) || !peer_rows_aligned(peer_ptrs, world))
         return fail(MOE_ERR_INVALID, "x and every peer's row buffers (x, y_ret) must be 16-byte aligned");
@@ -1530,7 +1546,7 @@ int moe_b200_set_wait_limits(int64_t kernel_wait_ns, int64_t exchange_wait_ns) {
 int moe_b200_ep_wait(const uint32_t *flag, uint32_t target, moe_stream_t stream) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     if (!flag) return fail(MOE_ERR_INVALID, "null flag");
-    int rc = init_device_globals();
+    int rc = ensure_device();
     if (rc) return rc;
     CK(moe::launch_ep_wait(flag, target, g.timeout_ns_ep, g.d_err, reinterpret_cast<cudaStream_t>(stream)));
     return MOE_OK;
@@ -1608,7 +1624,7 @@ int moe_b200_ep_experts_rows(const moe_layer_desc *L, const float *x, const int3
     const EpRowsWs w = ep_rows_ws(L, n_rows, static_cast<char *>(workspace));
     if (!workspace || workspace_bytes < w.bytes)
         return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
-    int rc = init_device_globals();
+    int rc = ensure_device();
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int E = static_cast<int>(L->n_experts), n = static_cast<int>(n_rows);

@@ -108,3 +108,105 @@ def test_device_resident_tables_are_direct(pkg, cuda):
         assert mc.stats()["misses"] == 0
     finally:
         mc.reset()
+
+
+def test_promotion_cap_and_many_tensors(pkg, cuda):
+    """Six tiered layers at batch 8: every step logs several hundred misses
+    with repeats over 18 tensors, more than 48 experts become candidates, so
+    the per-step cap decides which keys are read; the device tables, slot
+    maps and totals must still equal the policy model's after every step."""
+    mc = pkg.moe_cache
+    t, H, F, E, k, n_tok, slots, n_layers = O.Q2_K, 256, 256, 64, 8, 8, 6, 6
+    mc.configure(enabled=True, slots=slots, budget_gb=4.0)
+    try:
+        layers, Ls = [], []
+        for l in range(n_layers):
+            L = _layer_np(t, H, F, E, seed=40 + 7 * l)
+            L["k"] = k
+            Ls.append(L)
+            layers.append(pkg.MoELayer(H, F, E, k, {"gate": t, "up": t, "down": t}, shared=True, host=True,
+                                       name=f"blk.{l}",
+                                       weights={r: L[r] for r in ("gate", "up", "down", "shared_gate", "shared_up",
+                                                                  "shared_down")}))
+        model = CacheModel(slots=slots, budget_bytes=4 << 30)
+        mt = {}
+        capped = 0
+        for step in range(10):
+            for l, layer in enumerate(layers):
+                x = activations((n_tok, H), seed=500 + 31 * step + l)
+                logits = zipf_logits(n_tok, E, seed=60 + l) + 2.0 * activations((n_tok, E), seed=900 + 31 * step + l)
+                out = layer.decode(torch.from_numpy(x).to(cuda), torch.from_numpy(logits).to(cuda))
+                if step % 3 == 0:
+                    check_layer(layer, Ls[l], x, logits, out.cpu().numpy())
+                ids = layer.routing_of(n_tok)[0].cpu().numpy()
+                if step == 0:
+                    for r in ("up", "gate", "down"):
+                        mt[(l, r)] = model.register((l, r), f"blk.{l}.ffn_{r}_exps.weight", E,
+                                                    layer.w[r][0].numel())
+                for r in ("up", "gate", "down"):
+                    model.launch(mt[(l, r)], ids.reshape(-1).tolist())
+            mc.step()
+            capped += model.step() == 48
+            for l, layer in enumerate(layers):
+                for r in ("up", "gate", "down"):
+                    tbl, n_slots, tid = mc.table(layer.desc_t[r])
+                    assert tid == mt[(l, r)].id and n_slots == slots
+                    assert tbl == mt[(l, r)].slot_of, (step, l, r)
+        s = mc.stats()
+        assert capped > 0, "no step reached the 48-promotion cap"
+        assert s["promotions"] == model.promotions and s["hits"] == model.hits
+        assert s["resident"] == sum(sum(1 for e in m.expert_of if e >= 0) for m in mt.values())
+        assert mc.device_error() == 0
+    finally:
+        mc.reset()
+
+
+def test_step_inside_a_cuda_graph(pkg, cuda):
+    """The promotion step enqueues device work only, so decode + step can be
+    captured in one CUDA graph; replaying it moves the cache exactly as the
+    eager sequence does."""
+    mc = pkg.moe_cache
+    t, H, F, E, k = O.Q4_K, 256, 256, 32, 4
+    L = _layer_np(t, H, F, E, seed=77)
+    L["k"] = k
+    w = {r: L[r] for r in ("gate", "up", "down", "shared_gate", "shared_up", "shared_down")}
+    x = torch.from_numpy(activations((2, H), seed=1)).to(cuda)
+    lgs = [torch.from_numpy(zipf_logits(2, E, seed=3) + 1.5 * activations((2, E), seed=10 + i)).to(cuda)
+           for i in range(4)]
+    tables = []
+    for graph in (False, True):
+        mc.configure(enabled=True, slots=4, budget_gb=1.0)
+        try:
+            layer = pkg.MoELayer(H, F, E, k, {"gate": t, "up": t, "down": t}, shared=True, host=True, weights=w)
+            stream = torch.cuda.Stream(cuda)
+            out = torch.empty((2, H), device=cuda)
+            with torch.cuda.stream(stream):
+                layer.decode(x, lgs[0], out, stream=stream)   # registers the tensors (not capturable)
+                mc.step(stream)
+            stream.synchronize()
+
+            def seq():
+                for lg in lgs:
+                    layer.decode(x, lg, out, stream=stream)
+                    mc.step(stream)
+            if graph:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    seq()
+                for _ in range(3):
+                    g.replay()
+                torch.cuda.synchronize()
+                del g
+            else:
+                with torch.cuda.stream(stream):
+                    for _ in range(3):
+                        seq()
+                stream.synchronize()
+            tables.append([mc.table(layer.desc_t[r])[0] for r in ("gate", "up", "down")])
+            s = mc.stats()
+            tables[-1].append((s["promotions"], s["evictions"], s["hits"], s["misses"]))
+            assert mc.device_error() == 0
+        finally:
+            mc.reset()
+    assert tables[0] == tables[1]
+    assert tables[0][-1][0] > 0
