@@ -8,6 +8,7 @@ namespace moe {
 
 struct GemvArgs;
 struct LayerArgs;
+struct Layer2Args;
 struct MmqArgs;
 
 cudaError_t launch_quantize_act(int act_type, const float *x, void *y, int64_t n_rows, int64_t n_cols,
@@ -36,6 +37,9 @@ int launch_gemv(int type, int act, GemvArgs &a, cudaStream_t st, const char **wh
 // (-3 with *cuda_err on a CUDA error).
 int plan_layer(int ta, int tb, LayerArgs &a, int *grid, size_t *smem, const char **why);
 int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
+// The per-expert-group layer kernel (moe_layer2.cuh), same contract.
+int plan_layer2(int ta, int tb, Layer2Args &a, int *grid, size_t *smem, const char **why);
+int launch_layer2(int ta, int tb, Layer2Args &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
 
 // Prefill grouped GEMM on the tensor cores (moe_mmq.cu): launch_mmq_group
 // groups the (token, pick) entries by expert into offsets / entries and the

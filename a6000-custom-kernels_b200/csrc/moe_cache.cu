@@ -37,7 +37,7 @@
 #include "moe_aux.h"
 #include "moe_cache_b200.h"
 #include "moe_gemv.cuh"
-#include "moe_layer.cuh"
+#include "moe_layer2.cuh"
 #include "moe_mmq.cuh"
 #include "moe_promote.cuh"
 
@@ -75,7 +75,7 @@ struct Cache {
     size_t budget = 30ull << 30;
     bool claim_device = true;
     bool debug = false;
-    bool layer_fused = true;      // one-kernel layer decode where supported
+    int layer_fused = 1;          // 0: four launches; 1: per-expert-group kernel; 2: grid-exchange kernel
     std::string seed_path;
     // registry
     std::unordered_map<const char *, Tensor *> by_ptr;
@@ -153,7 +153,7 @@ void read_env() {
     g.seed_path = seed ? seed : "";
     g.claim_device = env_int("GGML_CUDA_MOE_CACHE_DEVICE", 1) != 0;
     g.debug = getenv("GGML_CUDA_MOE_CACHE_DEBUG") != nullptr;
-    g.layer_fused = env_int("GGML_CUDA_MOE_LAYER_FUSED", 1) != 0;
+    g.layer_fused = std::min(2, std::max(0, env_int("GGML_CUDA_MOE_LAYER_FUSED", 1)));
     g.env_read = true;
     if (g.enabled && g.debug)
         fprintf(stderr, "[moe_b200] cache on: %d slots per tensor, %.1f GiB pool budget\n", g.slots,
@@ -616,6 +616,7 @@ struct LayerWs {
     float *w, *h, *hs, *y, *ys;
     float *hg, *hsg;  // gate outputs when gate and up differ in type
     uint64_t *h_tag, *hs_tag;   // fused kernel: h / hs as (value, tag) pairs
+    uint32_t *rowcnt;           // per-expert-group kernel: output rows arrived per (token, row block)
     size_t bytes;
 };
 
@@ -627,6 +628,9 @@ LayerWs layer_ws(const moe_layer_desc *L, int64_t n_tok, char *base) {
     // the epoch sits at offset 0 for every n_tok, so workspaces reused across
     // batch sizes share one tag sequence
     w.gbar = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 2));
+    // the row counters follow at a fixed place too, sized for 8 tokens: they
+    // are zero between launches whatever batch size used the workspace last
+    w.rowcnt = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 8 * ((H + moe::LAYER2_RB - 1) / moe::LAYER2_RB)));
     w.ids = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * n_tok * k));
     w.w = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k));
     w.h = reinterpret_cast<float *>(take(sizeof(float) * n_tok * k * F));
@@ -742,6 +746,36 @@ int layer_args(const moe_layer_desc *L, const float *x, const float *logits, flo
     return MOE_OK;
 }
 
+// The per-expert-group kernel's arguments from the fused-layer fields.
+moe::Layer2Args to_layer2(const moe::LayerArgs &a, uint32_t *rowcnt) {
+    moe::Layer2Args b{};
+    b.gu = a.gu;
+    b.dn = a.dn;
+    b.up = a.up;
+    b.gate = a.gate;
+    b.down = a.down;
+    b.shared_down = a.shared_down;
+    b.tma_shared_down = a.tma_shared_down;
+    b.logits = a.logits;
+    b.n_tok = a.n_tok;
+    b.k = a.k;
+    b.n_experts = a.n_experts;
+    b.norm_w = a.norm_w;
+    b.ids_out = a.ids_out;
+    b.w_out = a.w_out;
+    b.out = a.out;
+    b.stats = a.stats;
+    b.clock = a.clock;
+    b.log_cap = a.log_cap;
+    b.h_tag = a.h_tag;
+    b.hs_tag = a.hs_tag;
+    b.gbar = a.gbar;
+    b.rowcnt = rowcnt;
+    b.err = a.err;
+    b.timeout_ns = a.timeout_ns;
+    return b;
+}
+
 // True when the fused kernel takes this layer (type pair, sizes, switch).
 bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
     if (!g.layer_fused || L->gate.type != L->up.type) return false;
@@ -759,7 +793,9 @@ bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
     int grid = 0;
     size_t smem = 0;
     const char *why = "";
-    return moe::plan_layer(L->up.type, L->down.type, a, &grid, &smem, &why) == 0;
+    if (g.layer_fused == 2) return moe::plan_layer(L->up.type, L->down.type, a, &grid, &smem, &why) == 0;
+    moe::Layer2Args b = to_layer2(a, nullptr);
+    return moe::plan_layer2(L->up.type, L->down.type, b, &grid, &smem, &why) == 0;
 }
 
 
@@ -1167,7 +1203,12 @@ int moe_b200_layer_decode(const moe_layer_desc *L, const float *x, const float *
         if (rc) return rc;
         const char *why = "";
         cudaError_t ce = cudaSuccess;
-        rc = moe::launch_layer(L->up.type, L->down.type, a, st, &why, &ce);
+        if (g.layer_fused == 2) {
+            rc = moe::launch_layer(L->up.type, L->down.type, a, st, &why, &ce);
+        } else {
+            moe::Layer2Args b = to_layer2(a, w.rowcnt);
+            rc = moe::launch_layer2(L->up.type, L->down.type, b, st, &why, &ce);
+        }
         if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
         if (rc) return fail(rc, "%s", why);
         return MOE_OK;
@@ -1661,7 +1702,8 @@ int moe_b200_layer_fused(const moe_layer_desc *L, int64_t n_tok) {
 int moe_b200_layer_set_fused(int32_t enable) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     read_env();
-    g.layer_fused = enable != 0;
+    if (enable < 0 || enable > 2) return fail(MOE_ERR_INVALID, "fused layer mode must be 0, 1 or 2");
+    g.layer_fused = enable;
     return MOE_OK;
 }
 

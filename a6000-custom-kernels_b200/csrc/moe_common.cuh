@@ -101,12 +101,33 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parit
 // this hardware, so it cannot bound a wait.
 __device__ __forceinline__ uint64_t timeout_cycles(uint64_t timeout_ns) { return 2ull * timeout_ns; }
 
-// Sleeping wait (for consumers): gives up after ~timeout_ns. The suspend
-// hint never exceeds the limit, so a tiny limit gives up at once.
+// Non-blocking probe of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Sleeping wait (for consumers): gives up after ~timeout_ns. Limits below
+// 20 us poll with the non-blocking probe (try_wait itself may suspend for a
+// hardware-defined time), so a tiny limit gives up at once.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
+    if (timeout_ns < 20000u) {
+        const uint64_t t0 = clock64(), lim = timeout_cycles(timeout_ns);
+        for (;;) {
+            if (mbar_test_wait(bar, parity)) return true;
+            if (static_cast<uint64_t>(clock64()) - t0 > lim) return false;
+        }
+    }
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = clock64(), lim = timeout_cycles(timeout_ns);
-    const uint32_t hint = timeout_ns < 20000u ? static_cast<uint32_t>(timeout_ns) + 1u : 20000u;
+    const uint32_t hint = 20000u;
     for (;;) {
         if (mbar_try_wait_hint(bar, parity, hint)) return true;
         if (static_cast<uint64_t>(clock64()) - t0 > lim) return false;

@@ -1,0 +1,539 @@
+// moe_layer2.cuh -- one MoE layer of decode tokens in ONE launch, split into
+// per-expert CTA groups.
+//
+// The layer is routed experts + the shared expert, each a "unit" (a distinct
+// expert with the tokens that picked it). The grid (one CTA per SM,
+// cooperative launch) is cut into contiguous CTA groups, one per unit, sized
+// by the unit's member count. CTA j of a group of C owns
+//   gate/up rows [F j / C, F (j + 1) / C) and down rows [H j / C, H (j + 1) / C)
+// of its unit's expert, for every member token. Its producer warp streams all
+// of those weights into a shared-memory ring at once -- a batch-1 CTA's
+// ~145 KB fit, so every weight byte of the layer is requested within a few
+// microseconds of launch -- and the shared expert's CTAs start before routing
+// is known, since their weights do not depend on it.
+//
+// Data exchange stays inside a group: gate/up results h go out as (value,
+// launch tag) pairs, and each CTA of the group takes its unit's h (768
+// values a member at config 2) as soon as every tag is this launch's. Down
+// results y are combined without any wait: output rows are cut into blocks of
+// RB rows with one arrival counter per (token, block); a CTA adds the rows it
+// wrote, and the CTA whose addition completes a block (k + 1 contributions of
+// every row) sums that block in pick order plus the shared expert and resets
+// the counter. The per-row arithmetic is the GEMV's (consume_tile), and the
+// combine adds in the same order as the combine kernel, so results equal the
+// four-launch path bit for bit.
+#pragma once
+#include "moe_layer.cuh"
+
+namespace moe {
+
+constexpr int LAYER2_RB = 64;            // output rows per combine block
+constexpr int LAYER2_ROUTE_WARPS = 4;    // warps routing the single token of a batch-1 launch
+
+struct Layer2Args {
+    GemvArgs gu, dn;                     // per-phase shapes, tile geometry, outputs
+    LayerTensor up, gate, down;
+    const char *shared_down;
+    int32_t tma_shared_down;
+    const float *logits;
+    int32_t n_tok, k, n_experts, norm_w;
+    int32_t *ids_out;
+    float *w_out, *out;
+    uint32_t *stats;
+    const uint32_t *clock;
+    uint32_t log_cap;
+    uint64_t *h_tag, *hs_tag;            // h / hs as (value, tag) pairs
+    uint32_t *gbar;                      // [0] launch epoch, [1] finished CTAs
+    uint32_t *rowcnt;                    // [n_tok][n_rb] rows arrived per combine block (zero between launches)
+    int32_t n_rb;
+    int32_t n_stages, n_tile_warps;
+    uint32_t stage_bytes, ctrl_bytes, act_bytes;
+    int *err;
+    uint64_t timeout_ns;
+};
+
+struct Layer2Ctrl {
+    GemvCtrl g;
+    const char *dsrc[LAYER_MAX_ENTRIES];
+    uint8_t dkind[LAYER_MAX_ENTRIES], dhost[LAYER_MAX_ENTRIES];
+    float wt[LAYER_MAX_ENTRIES];
+    uint32_t cand_key[512];
+    int32_t cand_id[512];
+    uint32_t uw[LAYER_MAX_ENTRIES + 2];  // prefix of unit weights (members)
+    uint32_t tag;
+};
+
+// This CTA's place in the unit partition. Unit u (of nu) gets CTAs
+// [c_u, c_{u+1}) with c_u = u + floor((G - nu) * W_u / W), W_u the prefix of
+// the unit weights (pre == nullptr: every unit weighs 1), so every unit has
+// at least one CTA and the rest are shared by weight.
+struct UnitPlan {
+    int u, j, c;                         // unit, index in its group, group size
+    int a0, a1, b0, b1;                  // gate/up rows, down rows
+    int nA, nB;                          // tiles of each phase
+};
+
+__device__ __forceinline__ int unit_first_cta(int u, int nu, int G, const uint32_t *pre) {
+    const uint64_t Wu = pre ? pre[u] : static_cast<uint64_t>(u);
+    const uint64_t W = pre ? pre[nu] : static_cast<uint64_t>(nu);
+    return u + static_cast<int>((static_cast<uint64_t>(G - nu) * Wu) / W);
+}
+
+__device__ __forceinline__ UnitPlan unit_plan(int nu, const uint32_t *pre, int G, int bid, int F, int H, int rpt,
+                                              int rows_b) {
+    UnitPlan P;
+    int lo = 0, hi = nu - 1;             // last u with c_u <= bid
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (unit_first_cta(mid, nu, G, pre) <= bid) lo = mid;
+        else hi = mid - 1;
+    }
+    P.u = lo;
+    const int c0 = unit_first_cta(lo, nu, G, pre);
+    const int c1 = lo + 1 < nu ? unit_first_cta(lo + 1, nu, G, pre) : G;
+    P.j = bid - c0;
+    P.c = c1 - c0;
+    P.a0 = static_cast<int>(static_cast<int64_t>(F) * P.j / P.c);
+    P.a1 = static_cast<int>(static_cast<int64_t>(F) * (P.j + 1) / P.c);
+    P.b0 = static_cast<int>(static_cast<int64_t>(H) * P.j / P.c);
+    P.b1 = static_cast<int>(static_cast<int64_t>(H) * (P.j + 1) / P.c);
+    P.nA = (P.a1 - P.a0 + rpt - 1) / rpt;
+    P.nB = (P.b1 - P.b0 + rows_b - 1) / rows_b;
+    return P;
+}
+
+// Selection of NV-wide slices (NV = experts per lane in a warp's slice).
+template <int NV>
+__device__ __forceinline__ void route_slices_nv(const float *l, int n_experts, int k, int w, int lane,
+                                                uint32_t *ck, int *ci) {
+    route_block_slices<NV>(l, n_experts, k, w, lane, ck, ci);
+}
+__device__ __forceinline__ bool route_slices(const float *l, int n_experts, int k, int w, int nw, int lane,
+                                             uint32_t *ck, int *ci) {
+    const int per = (n_experts + 32 * nw - 1) / (32 * nw);
+    if (per <= 1) route_slices_nv<1>(l, n_experts, k, w, lane, ck, ci);
+    else if (per <= 2) route_slices_nv<2>(l, n_experts, k, w, lane, ck, ci);
+    else if (per <= 4) route_slices_nv<4>(l, n_experts, k, w, lane, ck, ci);
+    else if (per <= 8) route_slices_nv<8>(l, n_experts, k, w, lane, ck, ci);
+    else if (per <= 16) route_slices_nv<16>(l, n_experts, k, w, lane, ck, ci);
+    else return false;
+    return true;
+}
+
+
+template <int TA, int TB>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __grid_constant__ Layer2Args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + GEMV_MAX_STAGES;
+    Layer2Ctrl &LC = *reinterpret_cast<Layer2Ctrl *>(smem + 2 * GEMV_MAX_STAGES * 8);
+    GemvCtrl &C = LC.g;
+    uint8_t *act_area = smem + a.ctrl_bytes;
+    uint8_t *stage_area = act_area + a.act_bytes;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = a.n_stages, k = a.k, n_tok = a.n_tok, N = n_tok * k, E = a.n_experts;
+    const int H = a.dn.nrows, F = a.gu.nrows, KA = a.gu.K, KB = a.dn.K;
+    const bool has_shared = a.gu.shared_up != nullptr;
+    const int hs = has_shared ? 1 : 0;
+    const int G = gridDim.x, bid = blockIdx.x;
+    const int rpt = a.gu.rows_per_tile, rows_b = a.dn.rows_per_tile;
+    constexpr int PW = GEMV_CONSUMER_WARPS;          // the producer warp
+    const bool one = n_tok == 1;
+
+    auto src_of = [&](const LayerTensor &T, int x, const char *&src, uint8_t &kind, uint8_t &host) {
+        if (T.tbl) {
+            const uintptr_t p = reinterpret_cast<uintptr_t>(T.tbl[x]);
+            src = reinterpret_cast<const char *>(p & ~static_cast<uintptr_t>(1));
+            host = static_cast<uint8_t>(p & 1u);
+        } else {
+            src = T.dense + static_cast<uint64_t>(x) * T.expert_bytes;
+            host = 0;
+        }
+        kind = static_cast<uint8_t>(host ? (T.tma ? 1 : 2) : (T.tma ? 0 : 2));
+    };
+    auto resolve = [&](int u, int x) {
+        src_of(a.up, x, C.usrc[u][0], C.ukind[u][0], C.uhost[u][0]);
+        src_of(a.gate, x, C.usrc[u][1], C.ukind[u][1], C.uhost[u][1]);
+        src_of(a.down, x, LC.dsrc[u], LC.dkind[u], LC.dhost[u]);
+    };
+    // the producer's description of tile i of unit plan P (phase A, then B)
+    auto describe = [&](const UnitPlan &P, int i, TileSrc &ts) {
+        const int U = C.n_unique;
+        const bool routed = P.u < U;
+        if (i < P.nA) {
+            ts.row0[0] = ts.row0[1] = P.a0 + i * rpt;
+            ts.nr[0] = ts.nr[1] = min(rpt, P.a1 - ts.row0[0]);
+            ts.src[0] = routed ? C.usrc[P.u][0] : a.gu.shared_up;
+            ts.src[1] = routed ? C.usrc[P.u][1] : a.gu.shared_gate;
+            ts.kind[0] = routed ? C.ukind[P.u][0] : (a.gu.tma_shared ? 0 : 2);
+            ts.kind[1] = routed ? C.ukind[P.u][1] : (a.gu.tma_shared ? 0 : 2);
+            ts.n_parts = 2;
+            ts.rb = a.gu.row_bytes;
+            ts.part_bytes = a.gu.part_bytes;
+        } else {
+            const int j = i - P.nA;
+            ts.row0[0] = ts.row0[1] = P.b0 + j * rows_b;
+            ts.nr[0] = ts.nr[1] = min(rows_b, P.b1 - ts.row0[0]);
+            ts.src[0] = ts.src[1] = routed ? LC.dsrc[P.u] : a.shared_down;
+            ts.kind[0] = ts.kind[1] = routed ? LC.dkind[P.u] : (a.tma_shared_down ? 0 : 2);
+            ts.n_parts = 1;
+            ts.rb = a.dn.row_bytes;
+            ts.part_bytes = a.stage_bytes;
+        }
+    };
+    auto produce = [&](const UnitPlan &P) {
+        produce_tiles(P.nA + P.nB, S, full, empty, stage_area, a.stage_bytes,
+                      [&](int i, TileSrc &ts) { describe(P, i, ts); }, a.timeout_ns, a.err, lane);
+    };
+    // x of token t into activation slot t (llama.cpp CPU quantization)
+    auto stage_x = [&](int t, int b) {
+        stage_f32_block<TA>(reinterpret_cast<const float *>(a.gu.y) + static_cast<int64_t>(t) * a.gu.stride_col_y,
+                            act_area + static_cast<size_t>(t) * a.gu.slot_bytes, KA, b, lane);
+    };
+    constexpr int QA = is_kquant(TA) ? 256 : 32;
+    const int nbx = KA / QA;
+
+    // ---- 1. routing, units, plan --------------------------------------------
+    UnitPlan P{};
+    uint32_t tokmask = 0;                 // tokens whose x (and weights) this CTA needs
+    if (one) {
+        // One token: its k picks are distinct, so unit u = pick u and the
+        // shared expert is unit k whatever the routing: the plan is fixed
+        // before the logits are read, and the shared expert's CTAs stream at once.
+        P = unit_plan(k + hs, nullptr, G, bid, F, H, rpt, rows_b);
+        tokmask = 1u;
+        const bool early = has_shared && P.u == k;
+        if (warp == PW) {
+            for (int s = lane; s < S; s += 32) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            fence_mbar_init();
+            __syncwarp();
+            if (early) {
+                C.n_unique = k;           // read by describe(); warp rw0 writes the same value
+                produce(P);
+                asm volatile("bar.sync 4, 64;" ::: "memory");
+            } else {
+                asm volatile("bar.sync 4, 64;" ::: "memory");   // the routing warp's picks and sources
+                if (!C.fail) produce(P);
+            }
+            return;
+        }
+        constexpr int RW = LAYER2_ROUTE_WARPS, rw0 = PW - RW;
+        if (warp >= rw0) {
+            const int w = warp - rw0;
+            const bool sliced = k <= 16 && route_slices(a.logits, E, k, w, RW, lane, LC.cand_key, LC.cand_id);
+            asm volatile("bar.sync 2, %0;" ::"r"(RW * 32) : "memory");
+            if (w == 0) {
+                if (sliced) merge_topk(LC.cand_key, LC.cand_id, RW * k, k, lane, C.x);
+                else route_select(a.logits, E, k, lane, C.x);
+                __syncwarp();
+                bool bad = false;
+                if (lane < k) {
+                    const int x = C.x[lane];
+                    bad = x < 0 || x >= E;
+                    C.first[lane] = static_cast<int16_t>(lane);
+                    C.uidx[lane] = static_cast<int16_t>(lane);
+                    C.gmem[lane] = static_cast<int16_t>(lane);
+                    C.goff[lane] = static_cast<int16_t>(lane);
+                    C.uexp[lane] = x;
+                    C.eslot[lane] = 0;
+                    if (!bad) resolve(lane, x);
+                }
+                bad = __any_sync(0xffffffffu, bad);
+                if (lane == 0) {
+                    C.n_unique = k;
+                    C.goff[k] = static_cast<int16_t>(k);
+                    C.shslot[0] = 0;
+                    C.fail = bad ? 1 : 0;
+                    if (bad) set_error(a.err, DERR_BAD_ID);
+                }
+                __syncwarp();
+                asm volatile("bar.arrive 4, 64;" ::: "memory");
+            }
+        } else {
+            for (int b = warp; b < nbx; b += rw0) stage_x(0, b);
+            if (tid == 0) LC.tag = ld_relaxed_u32(&a.gbar[0]) + 1u;
+        }
+        consumer_sync();
+    } else {
+        // Several tokens: GW warps route each token over slices, one merges;
+        // the picks are grouped by expert (block barriers, the producer
+        // included), and the groups weighted by their member counts.
+        if (warp == PW) {
+            for (int s = lane; s < S; s += 32) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            fence_mbar_init();
+        }
+        if (tid == 0) {
+            C.fail = 0;
+            LC.tag = ld_relaxed_u32(&a.gbar[0]) + 1u;
+        }
+        const int GW = PW / n_tok;
+        const int per = (E + 32 * GW - 1) / (32 * GW);
+        const bool sliced = k <= 16 && per <= 16 && GW * k <= 512;
+        if (sliced && warp < GW * n_tok) {
+            const int t = warp / GW, w = warp % GW;
+            route_slices(a.logits + static_cast<int64_t>(t) * E, E, k, w, GW, lane, LC.cand_key + t * GW * k,
+                         LC.cand_id + t * GW * k);
+        }
+        __syncthreads();
+        if (warp < n_tok) {
+            const int t = warp;
+            if (sliced) merge_topk(LC.cand_key + t * GW * k, LC.cand_id + t * GW * k, GW * k, k, lane, &C.x[t * k]);
+            else route_select(a.logits + static_cast<int64_t>(t) * E, E, k, lane, &C.x[t * k]);
+        }
+        __syncthreads();
+        build_groups(C, N, E, [&](int e) { return C.x[e]; }, resolve, a.err);   // ends with a block barrier
+        if (warp == 0 && !C.fail) {
+            const int U = C.n_unique;
+            uint32_t run = 0;
+            for (int u0 = 0; u0 <= U + hs; u0 += 32) {
+                const int u = u0 + lane;
+                uint32_t w = 0;
+                if (u < U) w = static_cast<uint32_t>(C.goff[u + 1] - C.goff[u]);
+                else if (u == U && hs) w = static_cast<uint32_t>(n_tok);
+                uint32_t incl = w;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+                    if (lane >= off) incl += o;
+                }
+                if (u <= U + hs) LC.uw[u] = run + incl - w;
+                run += __shfl_sync(0xffffffffu, incl, 31);
+            }
+        }
+        __syncthreads();
+        if (!C.fail) {
+            P = unit_plan(C.n_unique + hs, LC.uw, G, bid, F, H, rpt, rows_b);
+            if (P.u < C.n_unique) {
+                for (int m = C.goff[P.u]; m < C.goff[P.u + 1]; ++m) tokmask |= 1u << (C.gmem[m] / k);
+            } else {
+                tokmask = (1u << n_tok) - 1u;
+            }
+        }
+        if (warp == PW) {
+            if (!C.fail) produce(P);
+            return;
+        }
+        for (int job = warp; job < n_tok * nbx; job += PW) {
+            const int t = job / nbx;
+            if ((tokmask >> t) & 1u) stage_x(t, job % nbx);
+        }
+        for (int e = tid; e < N; e += PW * 32) C.eslot[e] = static_cast<int16_t>(e / k);
+        if (tid < n_tok) C.shslot[tid] = static_cast<int16_t>(tid);
+        consumer_sync();
+    }
+
+    // ============================ consumer warps =============================
+    const int U = C.n_unique;
+    const bool run = !C.fail;
+    const int u = P.u;
+    const bool routed = u < U;
+    const int nA = run ? P.nA : 0, nB = run ? P.nB : 0;
+    const uint32_t tag = LC.tag;
+    const int nw = a.n_tile_warps;
+
+    // ---- gating weights of this CTA's tokens (warps from the top) and the
+    //      reference kernel's bookkeeping (:163-198, the first CTA) -----------
+    if (run && warp >= PW - n_tok && ((tokmask >> (PW - 1 - warp)) & 1u)) {
+        const int t = PW - 1 - warp;
+        route_weights(a.logits + static_cast<int64_t>(t) * E, E, k, a.norm_w, lane, &C.x[t * k], &LC.wt[t * k]);
+        __syncwarp();
+        if (bid == 0 && lane < k) a.w_out[t * k + lane] = LC.wt[t * k + lane];
+    }
+    if (bid == 0 && run && warp == PW - 1 - n_tok) {
+        const uint32_t clk = a.clock ? *a.clock : 0u;
+        for (int e = lane; e < N; e += 32) {
+            const int x = C.x[e], g = C.uidx[e];
+            a.ids_out[e] = x;
+            const LayerTensor *T[3] = {&a.up, &a.gate, &a.down};
+            const uint8_t host[3] = {C.uhost[g][0], C.uhost[g][1], LC.dhost[g]};
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                if (!T[j]->stamps) continue;
+                T[j]->stamps[x] = clk;
+                if (!a.stats) continue;
+                if (host[j]) {
+                    const uint32_t s = atomicAdd(a.stats, 1u);
+                    if (s < a.log_cap) a.stats[GEMV_LOG_BASE + s] = (static_cast<uint32_t>(T[j]->cache_id) << 12) | x;
+                } else {
+                    atomicAdd(a.stats + 1, 1u);
+                }
+            }
+        }
+    }
+    if (bid == 0 && !run && tid == 0) {
+        // keep the routing visible even when a bad id stopped the launch
+        for (int e = 0; e < N; ++e) a.ids_out[e] = C.x[e];
+    }
+
+    // ---- 2a. gate/up + GLU of this CTA's rows -> h (and tagged copies) ------
+    for (int i = warp; i < nA && warp < nw; i += nw) {
+        const int s = i % S;
+        if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
+            if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+            break;
+        }
+        const int row0 = P.a0 + i * rpt, nr = min(rpt, P.a1 - row0);
+        const char *s0 = routed ? C.usrc[u][0] : a.gu.shared_up;
+        const char *s1 = routed ? C.usrc[u][1] : a.gu.shared_gate;
+        const uint8_t *stage = stage_area + static_cast<size_t>(s) * a.stage_bytes;
+        const uint64_t off = static_cast<uint64_t>(row0) * a.gu.row_bytes;
+        const uint8_t *up_rows = stage + ((reinterpret_cast<uintptr_t>(s0) + off) & 15u);
+        const uint8_t *gate_rows = stage + a.gu.part_bytes + ((reinterpret_cast<uintptr_t>(s1) + off) & 15u);
+        consume_tile<TA, ACT_CPU, 1, 2>(a.gu, C, up_rows, gate_rows, nr, u, U, row0, act_area, lane, a.h_tag,
+                                        a.hs_tag, tag);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    consumer_sync();
+    // phase-B activation slots: member m of the unit -> slot m
+    const int nm = run ? (routed ? C.goff[u + 1] - C.goff[u] : n_tok) : 0;
+    if (routed) {
+        for (int m = tid; m < nm; m += PW * 32) C.eslot[C.gmem[C.goff[u] + m]] = static_cast<int16_t>(m);
+    } else if (tid < n_tok) {
+        C.shslot[tid] = static_cast<int16_t>(tid);
+    }
+    consumer_sync();
+
+    // ---- 2b. the unit's h from the CTAs of its group, quantized for down. A
+    //      block is taken once all its values carry this launch's tag; each
+    //      warp loads up to 4 blocks before quantizing any ------------------
+    {
+        constexpr bool KQ = is_kquant(TB);
+        constexpr int QB = KQ ? 256 : 32, NV = KQ ? 8 : 1, BATCH = 4;
+        const int nb = KB / QB;
+        const int njobs = nm * nb;
+        auto block_of = [&](int job) -> const uint64_t * {
+            const int m = job / nb, b = job % nb;
+            const uint64_t *base;
+            if (routed) {
+                const int e = C.gmem[C.goff[u] + m], t = e / k, p = e % k;
+                base = a.h_tag + static_cast<int64_t>(p) * a.dn.stride_channel_y + static_cast<int64_t>(t) * a.dn.stride_col_y;
+            } else {
+                base = a.hs_tag + static_cast<int64_t>(m) * a.dn.shared_y_stride_col;
+            }
+            return base + b * QB;
+        };
+        auto load = [&](const uint64_t *xb, float (&v)[NV]) -> bool {
+            uint64_t w[NV];
+            if constexpr (KQ) {
+                ld_relaxed_u64x2(xb + 4 * lane, w[0], w[1]);
+                ld_relaxed_u64x2(xb + 4 * lane + 2, w[2], w[3]);
+                ld_relaxed_u64x2(xb + 128 + 4 * lane, w[4], w[5]);
+                ld_relaxed_u64x2(xb + 128 + 4 * lane + 2, w[6], w[7]);
+            } else {
+                uint64_t other;
+                ld_relaxed_u64x2(xb + (lane & ~1), w[0], other);
+                if (lane & 1) w[0] = other;
+            }
+            bool ok = true;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                ok &= static_cast<uint32_t>(w[j] >> 32) == tag;
+                v[j] = __uint_as_float(static_cast<uint32_t>(w[j]));
+            }
+            return ok;
+        };
+        const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
+        for (int base = warp; base < njobs; base += PW * BATCH) {
+            float vals[BATCH][NV];
+            bool ok[BATCH];
+#pragma unroll
+            for (int r = 0; r < BATCH; ++r) {
+                const int job = base + r * PW;
+                ok[r] = true;
+                if (job < njobs) ok[r] = load(block_of(job), vals[r]);
+            }
+            for (;;) {
+                unsigned waiting = 0;
+#pragma unroll
+                for (int r = 0; r < BATCH; ++r) {
+                    const int job = base + r * PW;
+                    if (job < njobs && !__all_sync(0xffffffffu, ok[r])) waiting |= 1u << r;
+                }
+                if (!waiting) break;
+                if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                    if (lane == 0) set_error(a.err, DERR_TIMEOUT_TAG);
+                    break;
+                }
+#pragma unroll
+                for (int r = 0; r < BATCH; ++r)
+                    if ((waiting >> r) & 1u) ok[r] = load(block_of(base + r * PW), vals[r]);
+            }
+#pragma unroll
+            for (int r = 0; r < BATCH; ++r) {
+                const int job = base + r * PW;
+                if (job >= njobs) break;
+                uint8_t *slot = act_area + static_cast<size_t>(job / nb) * a.dn.slot_bytes;
+                int8_t *q = reinterpret_cast<int8_t *>(slot);
+                int16_t *bs = reinterpret_cast<int16_t *>(slot + KB);
+                float *sc = reinterpret_cast<float *>(slot + KB + KB / 8);
+                if constexpr (KQ) quant_q8K_vals<TB>(vals[r], q, bs, sc, job % nb, lane, KB / chunk_of<TB>::CE);
+                else quant_q80_val<TB>(vals[r][0], q, bs, sc, job % nb, lane, KB / chunk_of<TB>::CE);
+            }
+        }
+    }
+    consumer_sync();
+
+    // ---- 2c. down rows of this CTA for every member -> y / ys ----------------
+    for (int i = nA + ((warp - nA % nw) % nw + nw) % nw; i < nA + nB && warp < nw; i += nw) {
+        const int s = i % S;
+        if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((i / S) & 1), a.timeout_ns)) {
+            if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+            break;
+        }
+        const int row0 = P.b0 + (i - nA) * rows_b, nr = min(rows_b, P.b1 - row0);
+        const char *s0 = routed ? LC.dsrc[u] : a.shared_down;
+        const uint8_t *rows = stage_area + static_cast<size_t>(s) * a.stage_bytes +
+                              ((reinterpret_cast<uintptr_t>(s0) + static_cast<uint64_t>(row0) * a.dn.row_bytes) & 15u);
+        consume_tile<TB, ACT_CPU, 1, 1, 32>(a.dn, C, rows, rows, nr, u, U, row0, act_area, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    __threadfence();          // this thread's y stores before the CTA's arrivals below
+    consumer_sync();
+
+    // ---- 2d. arrivals per (token, row block); the CTA completing a block sums
+    //      it: picks in order, then the shared expert --------------------------
+    if (run && P.b1 > P.b0) {
+        const int RB = LAYER2_RB;
+        const int rb0 = P.b0 / RB, nblk = (P.b1 - 1) / RB - rb0 + 1;
+        for (int pair = warp; pair < nm * nblk; pair += PW) {
+            const int m = pair / nblk, b = rb0 + pair % nblk;
+            const int t = routed ? C.gmem[C.goff[u] + m] / k : m;
+            const int lo = b * RB, hi = min(H, lo + RB);
+            const uint32_t mine = static_cast<uint32_t>(min(P.b1, hi) - max(P.b0, lo));
+            uint32_t old = 0;
+            if (lane == 0) old = atomicAdd(&a.rowcnt[t * a.n_rb + b], mine);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old + mine != static_cast<uint32_t>(hi - lo) * static_cast<uint32_t>(k + hs)) continue;
+            __threadfence();
+            const float *y = a.dn.dst + static_cast<int64_t>(t) * a.dn.stride_col_dst;
+            for (int r = lo + lane; r < hi; r += 32) {
+                float acc = 0.f;
+                for (int p = 0; p < k; ++p) {
+                    const float v = __fmul_rn(__ldcg(y + static_cast<int64_t>(p) * a.dn.stride_channel_dst + r), LC.wt[t * k + p]);
+                    acc = p == 0 ? v : __fadd_rn(acc, v);
+                }
+                if (has_shared) acc = __fadd_rn(acc, __ldcg(a.dn.shared_dst + static_cast<int64_t>(t) * a.dn.shared_stride_col_dst + r));
+                a.out[static_cast<int64_t>(t) * H + r] = acc;
+            }
+            if (lane == 0) atomicExch(&a.rowcnt[t * a.n_rb + b], 0u);
+        }
+    }
+
+    // ---- the last CTA to finish advances the epoch (every tagged read of this
+    //      launch is done) ------------------------------------------------------
+    if (tid == 0 && atomicAdd(&a.gbar[1], 1u) == gridDim.x - 1) {
+        atomicExch(&a.gbar[1], 0u);
+        atomicAdd(&a.gbar[0], 1u);
+    }
+}
+
+}  // namespace moe

@@ -3,7 +3,7 @@
 #pragma once
 #include <cstdio>
 
-#include "moe_layer.cuh"
+#include "moe_layer2.cuh"
 
 namespace moe {
 
@@ -41,6 +41,39 @@ cudaError_t launch_layer_t(const LayerArgs &a, int grid, size_t smem, cudaStream
         cudaFuncGetAttributes(&fa, kern);
         snprintf(g_layer_diag, sizeof(g_layer_diag), "grid=%d threads=%d smem=%zu regs=%d maxThreads=%d local=%zu",
                  grid, GEMV_THREADS, smem, fa.numRegs, fa.maxThreadsPerBlock, fa.localSizeBytes);
+    }
+    return e;
+}
+
+// The per-expert-group kernel (moe_layer2.cuh), same launch shape.
+template <int TA, int TB>
+cudaError_t launch_layer2_t(const Layer2Args &a, int grid, size_t smem, cudaStream_t st) {
+    auto kern = moe_layer2_kernel<TA, TB>;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // all CTAs co-resident: the h waits inside a group end
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) {
+        cudaFuncAttributes fa{};
+        cudaFuncGetAttributes(&fa, kern);
+        snprintf(g_layer_diag, sizeof(g_layer_diag), "grid=%d threads=%d smem=%zu regs=%d local=%zu", grid,
+                 GEMV_THREADS, smem, fa.numRegs, fa.localSizeBytes);
     }
     return e;
 }

@@ -93,6 +93,84 @@ __device__ __forceinline__ void route_select(const float *__restrict__ l, int n_
     else route_select_wide(l, n_experts, k, lane, ids);
 }
 
+// Top-k of one warp's slice [lo, lo + 32 NV) of the logits (n_experts caps
+// it): lane q < k receives pick q of the slice as (key, id), key 0 where the
+// slice has fewer than q + 1 experts. Order as route_select.
+template <int NV>
+__device__ __forceinline__ void route_slice_topk(const float *__restrict__ l, int lo, int n_experts, int k, int lane,
+                                                 uint32_t &out_key, int &out_id) {
+    uint32_t key[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int e = lo + lane + 32 * j;
+        key[j] = e < n_experts ? logit_key(l[e]) : 0u;
+    }
+    out_key = 0;
+    out_id = 0x7fffffff;
+    for (int q = 0; q < k; ++q) {
+        uint32_t tk = 0;
+        int tj = 0;
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+            if (key[j] > tk) { tk = key[j]; tj = j; }      // ascending j: ties keep the lower id
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, tk);
+        const uint32_t mine = (tk == wk && wk != 0u) ? static_cast<uint32_t>(lo + lane + 32 * tj) : 0xFFFFFFFFu;
+        const uint32_t wi = __reduce_min_sync(0xffffffffu, mine);
+        if (wk != 0u && static_cast<int>((wi - lo) & 31u) == lane) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (static_cast<uint32_t>(lo + lane + 32 * j) == wi) key[j] = 0u;
+        }
+        if (lane == q) { out_key = wk; out_id = wk ? static_cast<int>(wi) : 0x7fffffff; }
+    }
+}
+
+// Top-k over n_experts logits by NW warps of a block: warp w takes the slice
+// [w CH, (w + 1) CH) (CH = 32 NV) and keeps its k best in cand_key/cand_id
+// [w * k + q]; after the caller's barrier, merge_topk (one warp) picks the k
+// best of the NW * k candidates. Every global pick is among its slice's k
+// best, so the result equals route_select's bit for bit. k <= 16.
+template <int NV>
+__device__ __forceinline__ void route_block_slices(const float *__restrict__ l, int n_experts, int k, int warp,
+                                                   int lane, uint32_t *cand_key, int *cand_id) {
+    uint32_t kk;
+    int id;
+    route_slice_topk<NV>(l, warp * 32 * NV, n_experts, k, lane, kk, id);
+    if (lane < k) { cand_key[warp * k + lane] = kk; cand_id[warp * k + lane] = id; }
+}
+
+// The k best of nc <= 512 candidates (key, id), order (key desc, id asc);
+// lane q < k writes ids[q].
+__device__ __forceinline__ void merge_topk(const uint32_t *cand_key, const int *cand_id, int nc, int k, int lane,
+                                           int32_t *ids) {
+    constexpr int MAXC = 16;
+    uint32_t ck[MAXC];
+    int ci[MAXC];
+#pragma unroll
+    for (int j = 0; j < MAXC; ++j) {
+        const int c = lane + 32 * j;
+        ck[j] = c < nc ? cand_key[c] : 0u;
+        ci[j] = c < nc ? cand_id[c] : 0x7fffffff;
+    }
+    int pick = -1;
+    for (int q = 0; q < k; ++q) {
+        uint32_t bk = 0;
+        int bi = 0x7fffffff, bj = -1;
+#pragma unroll
+        for (int j = 0; j < MAXC; ++j)
+            if (ck[j] > bk || (ck[j] == bk && ck[j] != 0u && ci[j] < bi)) { bk = ck[j]; bi = ci[j]; bj = j; }
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+        const int wi = static_cast<int>(__reduce_min_sync(0xffffffffu, bk == wk ? static_cast<uint32_t>(bi) : 0xFFFFFFFFu));
+        if (bj >= 0 && bk == wk && bi == wi) {
+#pragma unroll
+            for (int j = 0; j < MAXC; ++j)
+                if (j == bj) ck[j] = 0u;
+        }
+        if (lane == q) pick = wi;
+    }
+    if (lane < k) ids[lane] = pick;
+}
+
 // Gating weights of the picks ids[0..k) (written by this warp or visible to
 // it): softmax over all experts, expf(l - max) / sum_e expf(l_e - max) with
 // the sum taken lane-strided (lane j adds experts j, j + 32, ... in order) and

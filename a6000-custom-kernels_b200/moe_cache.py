@@ -202,9 +202,11 @@ def prefill_mul_mat_id(src0, x, ids, dst=None, workspace=None, stream=None):
     return dst, bool(used.value)
 
 
-def set_layer_fused(enable):
-    """Enable (default) or disable the one-kernel layer decode (moe_b200_layer_set_fused)."""
-    check(lib().moe_b200_layer_set_fused(1 if enable else 0))
+def set_layer_fused(mode):
+    """Kernel of the layer decode (moe_b200_layer_set_fused): True / 1 the
+    per-expert-group kernel (default), 2 the grid-exchange kernel, False / 0
+    four launches."""
+    check(lib().moe_b200_layer_set_fused(int(mode)))
 
 
 def fill_quantized(ggml_type, dst, n_rows, n_cols, seed, sigma=0.02, stream=None):

@@ -220,11 +220,15 @@ typedef struct {
 /* No counterpart in the reference: bytes of caller-owned device workspace
  * moe_b200_layer_decode needs for n_tok tokens. Zero-fill the workspace once
  * before its first use (cudaMemset): its first 256 bytes hold the fused
- * kernel's launch epoch, which tags the data its CTAs exchange. Layout after
- * them (each part 256-byte aligned): ids int32[n][k], weights f32[n][k],
+ * kernels' launch epoch, which tags the data their CTAs exchange, then come
+ * uint32[8][H / 64 rounded up]: rows of output arrived per (token, block of
+ * 64 rows), which the per-expert-group kernel leaves at zero after every
+ * launch (a workspace shared by several layers must serve layers of one H).
+ * Then (each part 256-byte aligned): ids int32[n][k], weights f32[n][k],
  * h f32[n][k][F], hs f32[n][F], y f32[n][k][H], ys f32[n][H], then the
  * fused kernel's tagged copies of h and hs, then the gate outputs when gate
- * and up differ in type (f32[n][k][F], f32[n][F]). */
+ * and up differ in type (f32[n][k][F], f32[n][F]). After a launch that
+ * reported a device error, zero the workspace again. */
 size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok);
 
 /* No counterpart in the reference (the upstream graph around two
@@ -235,9 +239,9 @@ size_t moe_b200_layer_workspace_size(const moe_layer_desc *layer, int64_t n_tok)
  * src1_type F32).
  * Allocates nothing: `workspace` is caller-owned device memory (zero-filled
  * before first use). Where moe_b200_layer_fused says so, the whole layer is
- * ONE cooperative kernel launch (one CTA per SM, one grid barrier between
- * gate/up and down); otherwise four launches (routing, gate/up, down,
- * combine). Both give the same bits. Concurrent calls must not share a
+ * ONE cooperative kernel launch (one CTA per SM; see moe_b200_layer_set_fused
+ * for its two forms); otherwise four launches (routing, gate/up, down,
+ * combine). All give the same bits. Concurrent calls must not share a
  * workspace. */
 int moe_b200_layer_decode(const moe_layer_desc *layer, const float *x, const float *logits, float *out,
                           int64_t n_tok, void *workspace, size_t workspace_bytes, moe_stream_t stream);
@@ -345,8 +349,13 @@ int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap,
  * shared memory, fusion enabled), else 0. */
 int moe_b200_layer_fused(const moe_layer_desc *layer, int64_t n_tok);
 
-/* No counterpart in the reference: enable (1, the default) or disable the
- * fused layer kernel; GGML_CUDA_MOE_LAYER_FUSED=0 disables it at start-up. */
+/* No counterpart in the reference: which kernel moe_b200_layer_decode runs
+ * for fusable layers. 1 (the default): one launch with the grid cut into
+ * per-expert CTA groups (h exchanged inside a group, output rows summed by
+ * the CTA that completes them). 2: one launch where every CTA computes all
+ * picks' down rows of its own output slice after a grid-wide exchange of h.
+ * 0: four launches (routing, gate/up GEMV, down GEMV, combine). All three
+ * give the same bits. GGML_CUDA_MOE_LAYER_FUSED=0/1/2 sets it at start-up. */
 int moe_b200_layer_set_fused(int32_t enable);
 
 /* No counterpart in the reference. A layer decode for callers that cannot

@@ -1,6 +1,6 @@
-"""The one-kernel layer decode (moe_layer_kernel: routing, gate/up + GLU, one
-grid barrier, down, combine in a single cooperative launch) against the
-four-launch path: every intermediate and the output bit for bit, in eager
+"""The one-kernel layer decodes -- moe_layer2_kernel (per-expert CTA groups,
+mode 1, the default) and moe_layer_kernel (grid-wide exchange of h, mode 2)
+-- against the four-launch path: every intermediate and the output bit for bit, in eager
 mode, under CUDA-graph replay, and for host-tiered experts. Oracle parity of
 the fused path itself is covered by test_gpu_layer.py and test_gpu_cache.py,
 which run it by default."""
@@ -25,7 +25,7 @@ def _cache(pkg, cuda):
 
 def _run(pkg, layer, x, lg, fused):
     pkg.moe_cache.set_layer_fused(fused)
-    assert layer.fused(x.shape[0]) == fused
+    assert layer.fused(x.shape[0]) == bool(fused)
     out = layer.decode(x, lg)
     torch.cuda.synchronize()
     assert pkg.moe_cache.device_error() == 0
@@ -47,7 +47,8 @@ NAMES = ("ids", "w", "h", "hs", "y", "ys", "out")
     ((O.Q5_0, O.Q5_0), 2, (512, 256, 16, 2)),
     ((O.Q5_K, O.Q5_K), 7, (512, 512, 128, 8)),
 ])
-def test_fused_matches_four_launches(pkg, cuda, types, n_tok, shape):
+@pytest.mark.parametrize("mode", [1, 2])
+def test_fused_matches_four_launches(pkg, cuda, types, n_tok, shape, mode):
     """n_tok < 0: |n_tok| tokens with N(0, 1) logits (no Zipf skew)."""
     H, F, E, k = shape
     ta, tb = types
@@ -57,10 +58,13 @@ def test_fused_matches_four_launches(pkg, cuda, types, n_tok, shape):
     x = torch.from_numpy(activations((n_tok, H), seed=11)).to(cuda)
     lg_np = activations((n_tok, E), seed=12) if uniform else zipf_logits(n_tok, E, seed=12)
     lg = torch.from_numpy(lg_np).to(cuda)
-    a = _run(pkg, layer, x, lg, True)
+    a = _run(pkg, layer, x, lg, mode)
     b = _run(pkg, layer, x, lg, False)
     for name, u, v in zip(NAMES, a, b):
         np.testing.assert_array_equal(u, v, err_msg=name)
+    # a second launch on the same workspace (epoch and row counters carried over)
+    c = _run(pkg, layer, x, lg, mode)
+    np.testing.assert_array_equal(c[-1], b[-1], err_msg="out, second launch")
 
 
 def test_fused_without_shared_expert(pkg, cuda):
