@@ -137,7 +137,9 @@ class MoELayer:
         GLU output), y [n][k][H] (down outputs), ys [n][H] (shared down)."""
         ws = self._ws[n_tok]
         n, k, F, H = n_tok, self.k, self.F, self.H
-        out, off = [], 256          # the first 256 bytes hold the fused kernel's launch epoch
+        # the first 256 bytes hold the fused kernels' launch epoch, then the
+        # per-expert-group kernel's row counters (8 tokens x H / 64 blocks)
+        out, off = [], 256 + (4 * 8 * ((H + 63) // 64) + 255) // 256 * 256
         for count, dt, shape in ((n * k, torch.int32, (n, k)), (n * k, torch.float32, (n, k)),
                                  (n * k * F, torch.float32, (n, k, F)), (n * F, torch.float32, (n, F)),
                                  (n * k * H, torch.float32, (n, k, H)), (n * H, torch.float32, (n, H))):
