@@ -340,7 +340,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
 
     // ---- gating weights of this CTA's tokens (warps from the top) and the
     //      reference kernel's bookkeeping (:163-198, the first CTA) -----------
-    if (run && warp >= PW - n_tok && ((tokmask >> (PW - 1 - warp)) & 1u)) {
+    // (the first CTA does every token: it publishes the weights)
+    const uint32_t wmask = bid == 0 ? (1u << n_tok) - 1u : tokmask;
+    if (run && warp >= PW - n_tok && ((wmask >> (PW - 1 - warp)) & 1u)) {
         const int t = PW - 1 - warp;
         route_weights(a.logits + static_cast<int64_t>(t) * E, E, k, a.norm_w, lane, &C.x[t * k], &LC.wt[t * k]);
         __syncwarp();
