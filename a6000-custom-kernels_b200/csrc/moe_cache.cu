@@ -1082,6 +1082,8 @@ int moe_b200_configure(const moe_cache_config *cfg) {
     g.debug = cfg->debug != 0;
     g.env_read = true;
     g.configured = true;
+    // the kernel choice is not cache configuration: the environment still picks it
+    g.layer_fused = std::min(2, std::max(0, env_int("GGML_CUDA_MOE_LAYER_FUSED", g.layer_fused)));
     return MOE_OK;
 }
 

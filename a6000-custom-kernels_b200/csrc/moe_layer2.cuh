@@ -28,6 +28,21 @@
 namespace moe {
 
 constexpr int LAYER2_RB = 64;            // output rows per combine block
+
+// Optional timeline (built with -DMOE_LAYER2_TRACE): per CTA and mark, the
+// global timer (ns) and the SM clock; off by default.
+#ifdef MOE_LAYER2_TRACE
+__device__ unsigned long long g_layer2_trace[148 * 32];
+#define L2_MARK(i)                                                                               \
+    do {                                                                                         \
+        if (lane == 0) {                                                                         \
+            g_layer2_trace[blockIdx.x * 32 + (i)] = global_timer_ns();                           \
+            g_layer2_trace[blockIdx.x * 32 + 16 + (i)] = clock64();                              \
+        }                                                                                        \
+    } while (0)
+#else
+#define L2_MARK(i) do {} while (0)
+#endif
 constexpr int LAYER2_ROUTE_WARPS = 4;    // warps routing the single token of a batch-1 launch
 
 struct Layer2Args {
@@ -140,6 +155,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     const int rpt = a.gu.rows_per_tile, rows_b = a.dn.rows_per_tile;
     constexpr int PW = GEMV_CONSUMER_WARPS;          // the producer warp
     const bool one = n_tok == 1;
+    if (warp == 0) L2_MARK(0);
+    if (warp == PW) L2_MARK(13);
 
     auto src_of = [&](const LayerTensor &T, int x, const char *&src, uint8_t &kind, uint8_t &host) {
         if (T.tbl) {
@@ -196,6 +213,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
 
     // ---- 1. routing, units, plan --------------------------------------------
     UnitPlan P{};
+    bool early = false;                   // a batch-1 CTA of the shared expert
     uint32_t tokmask = 0;                 // tokens whose x (and weights) this CTA needs
     if (one) {
         // One token: its k picks are distinct, so unit u = pick u and the
@@ -203,7 +221,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         // before the logits are read, and the shared expert's CTAs stream at once.
         P = unit_plan(k + hs, nullptr, G, bid, F, H, rpt, rows_b);
         tokmask = 1u;
-        const bool early = has_shared && P.u == k;
+        early = has_shared && P.u == k;
         if (warp == PW) {
             for (int s = lane; s < S; s += 32) {
                 mbar_init(&full[s], 1);
@@ -217,19 +235,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                 asm volatile("bar.sync 4, 64;" ::: "memory");
             } else {
                 asm volatile("bar.sync 4, 64;" ::: "memory");   // the routing warp's picks and sources
+                L2_MARK(5);
                 if (!C.fail) produce(P);
             }
             return;
         }
-        constexpr int RW = LAYER2_ROUTE_WARPS, rw0 = PW - RW;
-        if (warp >= rw0) {
-            const int w = warp - rw0;
-            const bool sliced = k <= 16 && route_slices(a.logits, E, k, w, RW, lane, LC.cand_key, LC.cand_id);
-            asm volatile("bar.sync 2, %0;" ::"r"(RW * 32) : "memory");
-            if (w == 0) {
-                if (sliced) merge_topk(LC.cand_key, LC.cand_id, RW * k, k, lane, C.x);
+        // Routed CTAs: every consumer warp takes a slice of the logits, warp
+        // PW - 1 merges, records the groups and hands the sources to the
+        // producer (named barrier 4) while the others quantize x. The
+        // shared expert's CTAs quantize x and start on their tiles at once;
+        // they route later (their routing only feeds the gating weights).
+        if (!early) {
+            const bool sliced = k <= 16 && route_slices(a.logits, E, k, warp, PW, lane, LC.cand_key, LC.cand_id);
+            if (warp == PW - 1) L2_MARK(1);
+            consumer_sync();
+            if (warp == PW - 1) {
+                L2_MARK(2);
+                if (sliced) merge_topk(LC.cand_key, LC.cand_id, PW * k, k, lane, C.x);
                 else route_select(a.logits, E, k, lane, C.x);
                 __syncwarp();
+                L2_MARK(3);
                 bool bad = false;
                 if (lane < k) {
                     const int x = C.x[lane];
@@ -251,13 +276,21 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                     if (bad) set_error(a.err, DERR_BAD_ID);
                 }
                 __syncwarp();
+                L2_MARK(4);
                 asm volatile("bar.arrive 4, 64;" ::: "memory");
             }
-        } else {
-            for (int b = warp; b < nbx; b += rw0) stage_x(0, b);
-            if (tid == 0) LC.tag = ld_relaxed_u32(&a.gbar[0]) + 1u;
+        } else if (tid == 0) {
+            C.fail = 0;
+            C.n_unique = k;               // the producer wrote the same value for itself
+            C.goff[k] = static_cast<int16_t>(k);
+            C.shslot[0] = 0;
         }
+        if (warp < PW - 1)
+            for (int b = warp; b < nbx; b += PW - 1) stage_x(0, b);
+        if (warp == 0) L2_MARK(6);
+        if (tid == 0) LC.tag = ld_relaxed_u32(&a.gbar[0]) + 1u;
         consumer_sync();
+        if (warp == 0) L2_MARK(7);
     } else {
         // Several tokens: GW warps route each token over slices, one merges;
         // the picks are grouped by expert (block barriers, the producer
@@ -342,6 +375,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     //      reference kernel's bookkeeping (:163-198, the first CTA) -----------
     // (the first CTA does every token: it publishes the weights)
     const uint32_t wmask = bid == 0 ? (1u << n_tok) - 1u : tokmask;
+    if (one && early && warp == PW - 1) {
+        // the shared expert's CTAs route now, off their critical path
+        route_select(a.logits, E, k, lane, C.x);
+        __syncwarp();
+    }
     if (run && warp >= PW - n_tok && ((wmask >> (PW - 1 - warp)) & 1u)) {
         const int t = PW - 1 - warp;
         route_weights(a.logits + static_cast<int64_t>(t) * E, E, k, a.norm_w, lane, &C.x[t * k], &LC.wt[t * k]);
@@ -381,6 +419,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
             break;
         }
+        if (i == 0) L2_MARK(8);
         const int row0 = P.a0 + i * rpt, nr = min(rpt, P.a1 - row0);
         const char *s0 = routed ? C.usrc[u][0] : a.gu.shared_up;
         const char *s1 = routed ? C.usrc[u][1] : a.gu.shared_gate;
@@ -394,6 +433,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         if (lane == 0) mbar_arrive(&empty[s]);
     }
     consumer_sync();
+    if (warp == 0) L2_MARK(9);
     // phase-B activation slots: member m of the unit -> slot m
     const int nm = run ? (routed ? C.goff[u + 1] - C.goff[u] : n_tok) : 0;
     if (routed) {
@@ -482,6 +522,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         }
     }
     consumer_sync();
+    if (warp == 0) L2_MARK(10);
 
     // ---- 2c. down rows of this CTA for every member -> y / ys ----------------
     for (int i = nA + ((warp - nA % nw) % nw + nw) % nw; i < nA + nB && warp < nw; i += nw) {
@@ -498,8 +539,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __threadfence();          // this thread's y stores before the CTA's arrivals below
-    consumer_sync();
+    consumer_sync();          // the CTA's y stores, ordered before each warp's release below
+    if (warp == 0) L2_MARK(11);
 
     // ---- 2d. arrivals per (token, row block); the CTA completing a block sums
     //      it: picks in order, then the shared expert --------------------------
@@ -512,10 +553,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             const int lo = b * RB, hi = min(H, lo + RB);
             const uint32_t mine = static_cast<uint32_t>(min(P.b1, hi) - max(P.b0, lo));
             uint32_t old = 0;
-            if (lane == 0) old = atomicAdd(&a.rowcnt[t * a.n_rb + b], mine);
+            if (lane == 0) old = atom_add_acq_rel_gpu(&a.rowcnt[t * a.n_rb + b], mine);
             old = __shfl_sync(0xffffffffu, old, 0);
             if (old + mine != static_cast<uint32_t>(hi - lo) * static_cast<uint32_t>(k + hs)) continue;
-            __threadfence();
+            __syncwarp();
             const float *y = a.dn.dst + static_cast<int64_t>(t) * a.dn.stride_col_dst;
             for (int r = lo + lane; r < hi; r += 32) {
                 float acc = 0.f;
@@ -530,6 +571,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         }
     }
 
+#ifdef MOE_LAYER2_TRACE
+    consumer_sync();
+    if (warp == 0) L2_MARK(12);
+    if (tid == 0) g_layer2_trace[blockIdx.x * 32 + 14] = u;
+#endif
     // ---- the last CTA to finish advances the epoch (every tagged read of this
     //      launch is done) ------------------------------------------------------
     if (tid == 0 && atomicAdd(&a.gbar[1], 1u) == gridDim.x - 1) {

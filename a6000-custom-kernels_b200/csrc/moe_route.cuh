@@ -139,11 +139,11 @@ __device__ __forceinline__ void route_block_slices(const float *__restrict__ l, 
     if (lane < k) { cand_key[warp * k + lane] = kk; cand_id[warp * k + lane] = id; }
 }
 
-// The k best of nc <= 512 candidates (key, id), order (key desc, id asc);
-// lane q < k writes ids[q].
-__device__ __forceinline__ void merge_topk(const uint32_t *cand_key, const int *cand_id, int nc, int k, int lane,
-                                           int32_t *ids) {
-    constexpr int MAXC = 16;
+// The k best of nc <= 32 MAXC candidates (key, id), order (key desc, id
+// asc); lane q < k writes ids[q]. Lane l holds candidates l + 32 j.
+template <int MAXC>
+__device__ __forceinline__ void merge_topk_n(const uint32_t *cand_key, const int *cand_id, int nc, int k, int lane,
+                                             int32_t *ids) {
     uint32_t ck[MAXC];
     int ci[MAXC];
 #pragma unroll
@@ -154,14 +154,14 @@ __device__ __forceinline__ void merge_topk(const uint32_t *cand_key, const int *
     }
     int pick = -1;
     for (int q = 0; q < k; ++q) {
-        uint32_t bk = 0;
-        int bi = 0x7fffffff, bj = -1;
+        uint32_t bk = ck[0];
+        int bi = ci[0], bj = 0;
 #pragma unroll
-        for (int j = 0; j < MAXC; ++j)
-            if (ck[j] > bk || (ck[j] == bk && ck[j] != 0u && ci[j] < bi)) { bk = ck[j]; bi = ci[j]; bj = j; }
+        for (int j = 1; j < MAXC; ++j)
+            if (ck[j] > bk || (ck[j] == bk && ci[j] < bi)) { bk = ck[j]; bi = ci[j]; bj = j; }
         const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
         const int wi = static_cast<int>(__reduce_min_sync(0xffffffffu, bk == wk ? static_cast<uint32_t>(bi) : 0xFFFFFFFFu));
-        if (bj >= 0 && bk == wk && bi == wi) {
+        if (bk == wk && bi == wi) {
 #pragma unroll
             for (int j = 0; j < MAXC; ++j)
                 if (j == bj) ck[j] = 0u;
@@ -169,6 +169,14 @@ __device__ __forceinline__ void merge_topk(const uint32_t *cand_key, const int *
         if (lane == q) pick = wi;
     }
     if (lane < k) ids[lane] = pick;
+}
+__device__ __forceinline__ void merge_topk(const uint32_t *cand_key, const int *cand_id, int nc, int k, int lane,
+                                           int32_t *ids) {
+    if (nc <= 32) merge_topk_n<1>(cand_key, cand_id, nc, k, lane, ids);
+    else if (nc <= 64) merge_topk_n<2>(cand_key, cand_id, nc, k, lane, ids);
+    else if (nc <= 128) merge_topk_n<4>(cand_key, cand_id, nc, k, lane, ids);
+    else if (nc <= 256) merge_topk_n<8>(cand_key, cand_id, nc, k, lane, ids);
+    else merge_topk_n<16>(cand_key, cand_id, nc, k, lane, ids);
 }
 
 // Gating weights of the picks ids[0..k) (written by this warp or visible to
