@@ -229,10 +229,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             }
             fence_mbar_init();
             __syncwarp();
+            // the consumers wait on named barrier 3 for the initialised ring
+            asm volatile("bar.arrive 3, %0;" ::"r"(GEMV_THREADS) : "memory");
             if (early) {
-                C.n_unique = k;           // read by describe(); warp rw0 writes the same value
+                C.n_unique = k;           // read by describe(); thread 0 writes the same value
                 produce(P);
-                asm volatile("bar.sync 4, 64;" ::: "memory");
             } else {
                 asm volatile("bar.sync 4, 64;" ::: "memory");   // the routing warp's picks and sources
                 L2_MARK(5);
@@ -289,7 +290,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             for (int b = warp; b < nbx; b += PW - 1) stage_x(0, b);
         if (warp == 0) L2_MARK(6);
         if (tid == 0) LC.tag = ld_relaxed_u32(&a.gbar[0]) + 1u;
-        consumer_sync();
+        asm volatile("bar.sync 3, %0;" ::"r"(GEMV_THREADS) : "memory");   // consumers + the producer's arrival
         if (warp == 0) L2_MARK(7);
     } else {
         // Several tokens: GW warps route each token over slices, one merges;
