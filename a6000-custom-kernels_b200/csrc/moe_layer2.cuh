@@ -247,14 +247,24 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         // shared expert's CTAs quantize x and start on their tiles at once;
         // they route later (their routing only feeds the gating weights).
         if (!early) {
-            const bool sliced = k <= 16 && route_slices(a.logits, E, k, warp, PW, lane, LC.cand_key, LC.cand_id);
+            // E <= 512, k <= 8: rank selection (no serial rounds); else slices + merge
+            const bool ranked = E <= 32 * PW && k <= 8;
+            bool sliced = false;
+            if (ranked) rank_slice(a.logits, E, k, warp, lane, LC.cand_key, LC.cand_id);
+            else sliced = k <= 16 && route_slices(a.logits, E, k, warp, PW, lane, LC.cand_key, LC.cand_id);
             if (warp == PW - 1) L2_MARK(1);
             consumer_sync();
+            if (ranked) {
+                rank_candidates(LC.cand_key, LC.cand_id, PW * k, k, tid, C.x);
+                consumer_sync();
+            }
             if (warp == PW - 1) {
                 L2_MARK(2);
-                if (sliced) merge_topk(LC.cand_key, LC.cand_id, PW * k, k, lane, C.x);
-                else route_select(a.logits, E, k, lane, C.x);
-                __syncwarp();
+                if (!ranked) {
+                    if (sliced) merge_topk(LC.cand_key, LC.cand_id, PW * k, k, lane, C.x);
+                    else route_select(a.logits, E, k, lane, C.x);
+                    __syncwarp();
+                }
                 L2_MARK(3);
                 bool bad = false;
                 if (lane < k) {

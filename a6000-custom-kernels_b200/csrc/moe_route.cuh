@@ -139,6 +139,46 @@ __device__ __forceinline__ void route_block_slices(const float *__restrict__ l, 
     if (lane < k) { cand_key[warp * k + lane] = kk; cand_id[warp * k + lane] = id; }
 }
 
+// Rank selection without serial rounds, for n_experts <= 32 * NWARPS:
+// stage 1 -- warp w holds experts 32 w + lane and ranks each within its
+// warp by counting the warp's keys ahead of it (key desc, id asc; 32
+// shuffles); its k best go to cand[w * k + rank]. Stage 2 (after the
+// caller's barrier) -- every candidate is ranked among all NWARPS * k
+// candidates by 4 threads counting 1/4 each; rank q < k is pick q.
+__device__ __forceinline__ void rank_slice(const float *__restrict__ l, int n_experts, int k, int warp, int lane,
+                                           uint32_t *cand_key, int *cand_id) {
+    const int e = 32 * warp + lane;
+    const uint32_t key = e < n_experts ? logit_key(l[e]) : 0u;
+    int ahead = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t kj = __shfl_sync(0xffffffffu, key, j);
+        ahead += (kj > key || (kj == key && j < lane)) ? 1 : 0;
+    }
+    if (ahead < k) {
+        cand_key[warp * k + ahead] = key;
+        cand_id[warp * k + ahead] = e;
+    }
+}
+// nthreads >= 4 * nc threads call with their thread index; lanes of one
+// group of 4 are consecutive.
+__device__ __forceinline__ void rank_candidates(const uint32_t *cand_key, const int *cand_id, int nc, int k, int tid,
+                                                int32_t *ids) {
+    const int c = tid >> 2, part = tid & 3;
+    const bool live = c < nc;
+    const uint32_t key = live ? cand_key[c] : 0u;
+    const int id = live ? cand_id[c] : 0x7fffffff;
+    int ahead = 0;
+    for (int d = part; d < nc; d += 4) {
+        const uint32_t kd = cand_key[d];
+        const int idd = cand_id[d];
+        ahead += (kd > key || (kd == key && idd < id)) ? 1 : 0;
+    }
+    ahead += __shfl_xor_sync(0xffffffffu, ahead, 1);
+    ahead += __shfl_xor_sync(0xffffffffu, ahead, 2);
+    if (live && part == 0 && ahead < k) ids[ahead] = id;
+}
+
 // The k best of nc <= 32 MAXC candidates (key, id), order (key desc, id
 // asc); lane q < k writes ids[q]. Lane l holds candidates l + 32 j.
 template <int MAXC>
