@@ -120,6 +120,9 @@ def _declare(L):
         "moe_b200_ep_dispatch": (i32, [vp, i32, i32, i64, vp, i64, i64, i64, vp, i64, vp, vp]),
         "moe_b200_ep_wait": (i32, [vp, ctypes.c_uint32, vp]),
         "moe_b200_set_wait_limits": (i32, [i64, i64]),
+        "moe_b200_ep_decode_buffer_bytes": (sz, [i64, i64, i64, i32]),
+        "moe_b200_ep_layer_decode_p2p": (i32, [ctypes.POINTER(MoeLayerDesc), i64, i64, vp, i32, i32, vp, vp, vp, vp,
+                                               sz, vp]),
         "moe_b200_ep_experts_rows_workspace_size": (sz, [ctypes.POINTER(MoeLayerDesc), i64]),
         "moe_b200_ep_experts_rows": (i32, [ctypes.POINTER(MoeLayerDesc), vp, vp, i64, vp, vp, vp, vp, sz, vp]),
         "moe_b200_ep_return": (i32, [vp, i32, i64, vp, vp, vp, i64, vp, vp]),

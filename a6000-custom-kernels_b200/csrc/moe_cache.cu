@@ -1578,6 +1578,60 @@ int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap,
     return MOE_OK;
 }
 
+size_t moe_b200_ep_decode_buffer_bytes(int64_t H, int64_t n_experts, int64_t k, int32_t world) {
+    if (H < 1 || n_experts < 1 || k < 1 || world < 1 || world > moe::EP_DECODE_MAX_WORLD) return 0;
+    return static_cast<size_t>(moe::ep_decode_layout(static_cast<int>(H), static_cast<int>(n_experts),
+                                                     static_cast<int>(k), world).bytes);
+}
+
+int moe_b200_ep_layer_decode_p2p(const moe_layer_desc *L, int64_t expert_lo, int64_t n_experts_global,
+                                 const void *const *peer_bufs, int32_t world, int32_t rank, const float *x,
+                                 const float *logits, float *out, void *workspace, size_t workspace_bytes,
+                                 moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!L || !x || !logits || !out || !peer_bufs) return fail(MOE_ERR_INVALID, "null argument");
+    if (world < 1 || world > moe::EP_DECODE_MAX_WORLD || rank < 0 || rank >= world)
+        return fail(MOE_ERR_INVALID, "world must be 1..%d and 0 <= rank < world", moe::EP_DECODE_MAX_WORLD);
+    if (expert_lo < 0 || expert_lo + L->n_experts > n_experts_global || n_experts_global > 65536)
+        return fail(MOE_ERR_INVALID, "local experts [%lld, %lld) outside the %lld routed experts",
+                    static_cast<long long>(expert_lo), static_cast<long long>(expert_lo + L->n_experts),
+                    static_cast<long long>(n_experts_global));
+    const int64_t k = L->k, F = L->F, H = L->H;
+    if (k < 1 || k > 32 || k > n_experts_global) return fail(MOE_ERR_INVALID, "need 1 <= k <= min(32, n_experts)");
+    if (L->up.ne[0] != H || L->up.ne[1] != F || L->down.ne[0] != F || L->down.ne[1] != H)
+        return fail(MOE_ERR_INVALID, "expert tensor shapes do not match H/F");
+    if (H % 4 || !aligned16(x)) return fail(MOE_ERR_INVALID, "x must be 16-byte aligned with H a multiple of 4");
+    for (int32_t r = 0; r < world; ++r)
+        if (!peer_bufs[r] || !aligned16(peer_bufs[r])) return fail(MOE_ERR_INVALID, "peer buffer %d null or unaligned", r);
+    if (g.layer_fused == 0 || g.layer_fused == 2 || !layer_fusable(L, world))
+        return fail(MOE_ERR_UNSUPPORTED, "the fused expert-parallel decode needs the per-expert-group kernel for this layer");
+    const LayerWs w = layer_ws(L, world, static_cast<char *>(workspace));
+    if (!workspace || workspace_bytes < w.bytes) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, w.bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    moe::LayerArgs a;
+    int rc = layer_args(L, x, logits, out, world, w, st, &a);
+    if (rc) return rc;
+    // the shared expert serves this GPU's token only
+    a.gu.ncols_dst = a.dn.ncols_dst = 1;
+    moe::Layer2Args b = to_layer2(a, w.rowcnt);
+    b.n_experts = static_cast<int32_t>(n_experts_global);
+    b.ep_on = 1;
+    b.ep_timeout_ns = g.timeout_ns_ep;
+    b.ep.world = world;
+    b.ep.rank = rank;
+    b.ep.expert_lo = static_cast<int32_t>(expert_lo);
+    b.ep.n_local = static_cast<int32_t>(L->n_experts);
+    for (int32_t r = 0; r < world; ++r) b.ep.peer[r] = static_cast<char *>(const_cast<void *>(peer_bufs[r]));
+    b.ep.lay = moe::ep_decode_layout(static_cast<int>(H), static_cast<int>(n_experts_global), static_cast<int>(k), world);
+    const char *why = "";
+    cudaError_t ce = cudaSuccess;
+    rc = moe::launch_layer2(L->up.type, L->down.type, b, st, &why, &ce);
+    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+    if (rc) return fail(rc, "%s", why);
+    return MOE_OK;
+}
+
 int moe_b200_set_wait_limits(int64_t kernel_wait_ns, int64_t exchange_wait_ns) {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     constexpr uint64_t kDefault = 2000000000ull;

@@ -45,6 +45,38 @@ __device__ unsigned long long g_layer2_trace[148 * 32];
 #endif
 constexpr int LAYER2_ROUTE_WARPS = 4;    // warps routing the single token of a batch-1 launch
 
+// Expert-parallel decode: each GPU owns one buffer, mapped into the others
+// (CUDA IPC). Parts (byte offsets, 256-aligned): gx f32 [2][W][H] and glog
+// f32 [2][W][E] -- every GPU's token x and router logits, written by their
+// owners into slot [parity][src] (parity = exchange epoch & 1); yhome f32
+// [k][H] -- the down rows of this GPU's token, pick p written by the GPU
+// that owns its expert; arr u32 [8] -- per source, the exchange epoch + 1 of
+// its last dispatch here; rowcnt u32 [H / 64] -- rows of this GPU's token
+// arrived per block of 64; epoch u32 -- layer calls through the exchange.
+struct EpDecodeLayout {
+    uint64_t gx, glog, yhome, arr, rowcnt, epoch, bytes;
+};
+__host__ __device__ inline EpDecodeLayout ep_decode_layout(int H, int E, int k, int W) {
+    auto up = [](uint64_t x) { return (x + 255u) & ~uint64_t{255}; };
+    EpDecodeLayout L;
+    uint64_t off = 0;
+    L.gx = off;     off += up(4ull * 2 * W * H);
+    L.glog = off;   off += up(4ull * 2 * W * E);
+    L.yhome = off;  off += up(4ull * k * H);
+    L.arr = off;    off += up(4ull * 8);
+    L.rowcnt = off; off += up(4ull * ((H + 63) / 64));
+    L.epoch = off;  off += 256;
+    L.bytes = off;
+    return L;
+}
+constexpr int EP_DECODE_MAX_WORLD = 8;
+struct EpDecodeArgs {
+    int32_t world, rank;                 // one token per GPU: token t lives on GPU t
+    int32_t expert_lo, n_local;          // this GPU's experts [expert_lo, expert_lo + n_local)
+    char *peer[EP_DECODE_MAX_WORLD];     // every GPU's exchange buffer as seen from this GPU
+    EpDecodeLayout lay;
+};
+
 struct Layer2Args {
     GemvArgs gu, dn;                     // per-phase shapes, tile geometry, outputs
     LayerTensor up, gate, down;
@@ -65,6 +97,9 @@ struct Layer2Args {
     uint32_t stage_bytes, ctrl_bytes, act_bytes;
     int *err;
     uint64_t timeout_ns;
+    int32_t ep_on;                       // expert-parallel decode (ep below); n_tok = world
+    uint64_t ep_timeout_ns;              // limit of the waits for other GPUs
+    EpDecodeArgs ep;
 };
 
 struct Layer2Ctrl {
@@ -75,7 +110,8 @@ struct Layer2Ctrl {
     uint32_t cand_key[512];
     int32_t cand_id[512];
     uint32_t uw[LAYER_MAX_ENTRIES + 2];  // prefix of unit weights (members)
-    uint32_t tag;
+    int32_t gid[LAYER_MAX_ENTRIES];      // routed experts (global ids; C.x holds local ones)
+    uint32_t tag, xep;                   // launch tag; expert-parallel exchange epoch
 };
 
 // This CTA's place in the unit partition. Unit u (of nu) gets CTAs
@@ -154,7 +190,15 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     const int G = gridDim.x, bid = blockIdx.x;
     const int rpt = a.gu.rows_per_tile, rows_b = a.dn.rows_per_tile;
     constexpr int PW = GEMV_CONSUMER_WARPS;          // the producer warp
-    const bool one = n_tok == 1;
+    const bool epm = a.ep_on != 0;                   // expert-parallel decode (n_tok = world)
+    const int me = epm ? a.ep.rank : 0;
+    const int lo_e = epm ? a.ep.expert_lo : 0, n_loc = epm ? a.ep.n_local : E;
+    const int n_sh = epm ? 1 : n_tok;                // tokens of the shared expert (this GPU's own in EP)
+    const bool one = n_tok == 1 && !epm;
+    // the routed tokens' x and logits: the caller's, or (EP) every GPU's
+    // token from this GPU's gather slots
+    const float *x_base = reinterpret_cast<const float *>(a.gu.y);
+    const float *lg_base = a.logits;
     if (warp == 0) L2_MARK(0);
     if (warp == PW) L2_MARK(13);
 
@@ -205,7 +249,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     };
     // x of token t into activation slot t (llama.cpp CPU quantization)
     auto stage_x = [&](int t, int b) {
-        stage_f32_block<TA>(reinterpret_cast<const float *>(a.gu.y) + static_cast<int64_t>(t) * a.gu.stride_col_y,
+        stage_f32_block<TA>(x_base + static_cast<int64_t>(t) * a.gu.stride_col_y,
                             act_area + static_cast<size_t>(t) * a.gu.slot_bytes, KA, b, lane);
     };
     constexpr int QA = is_kquant(TA) ? 256 : 32;
@@ -278,6 +322,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                     C.eslot[lane] = 0;
                     if (!bad) resolve(lane, x);
                 }
+                if (lane < k) LC.gid[lane] = C.x[lane];
                 bad = __any_sync(0xffffffffu, bad);
                 if (lane == 0) {
                     C.n_unique = k;
@@ -316,23 +361,61 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         if (tid == 0) {
             C.fail = 0;
             LC.tag = ld_relaxed_u32(&a.gbar[0]) + 1u;
+            if (epm) LC.xep = ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.ep.peer[me] + a.ep.lay.epoch));
         }
+        if (epm) {
+            // dispatch: CTA d < world writes this GPU's x and logits into GPU
+            // d's gather slot [parity][me], then publishes them (release at
+            // system scope); every CTA then waits for all GPUs' slots
+            __syncthreads();
+            const uint32_t xep = LC.xep;
+            const int W = n_tok, par = static_cast<int>(xep & 1u);
+            const EpDecodeLayout &Ly = a.ep.lay;
+            if (bid < W) {
+                char *dst = a.ep.peer[bid];
+                float4 *gx = reinterpret_cast<float4 *>(dst + Ly.gx) + static_cast<int64_t>(par * W + me) * (H / 4);
+                float *gl = reinterpret_cast<float *>(dst + Ly.glog) + static_cast<int64_t>(par * W + me) * E;
+                const float4 *x4 = reinterpret_cast<const float4 *>(a.gu.y);
+                for (int i = tid; i < H / 4; i += GEMV_THREADS) gx[i] = x4[i];
+                for (int i = tid; i < E; i += GEMV_THREADS) gl[i] = a.logits[i];
+                __threadfence_system();
+                __syncthreads();
+                if (tid == 0) st_release_sys_u32(reinterpret_cast<uint32_t *>(dst + Ly.arr) + me, xep + 1u);
+            }
+            if (tid < W) {
+                const uint32_t *arr = reinterpret_cast<const uint32_t *>(a.ep.peer[me] + Ly.arr) + tid;
+                const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
+                while (static_cast<int32_t>(ld_acquire_sys_u32(arr) - (xep + 1u)) < 0) {
+                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                        set_error(a.err, DERR_TIMEOUT_FULL);
+                        C.fail = 1;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            x_base = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.gx) + static_cast<int64_t>(par) * W * H;
+            lg_base = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.glog) + static_cast<int64_t>(par) * W * E;
+        }
+        __syncthreads();
         const int GW = PW / n_tok;
         const int per = (E + 32 * GW - 1) / (32 * GW);
         const bool sliced = k <= 16 && per <= 16 && GW * k <= 512;
         if (sliced && warp < GW * n_tok) {
             const int t = warp / GW, w = warp % GW;
-            route_slices(a.logits + static_cast<int64_t>(t) * E, E, k, w, GW, lane, LC.cand_key + t * GW * k,
+            route_slices(lg_base + static_cast<int64_t>(t) * E, E, k, w, GW, lane, LC.cand_key + t * GW * k,
                          LC.cand_id + t * GW * k);
         }
         __syncthreads();
         if (warp < n_tok) {
             const int t = warp;
             if (sliced) merge_topk(LC.cand_key + t * GW * k, LC.cand_id + t * GW * k, GW * k, k, lane, &C.x[t * k]);
-            else route_select(a.logits + static_cast<int64_t>(t) * E, E, k, lane, &C.x[t * k]);
+            else route_select(lg_base + static_cast<int64_t>(t) * E, E, k, lane, &C.x[t * k]);
         }
         __syncthreads();
-        build_groups(C, N, E, [&](int e) { return C.x[e]; }, resolve, a.err);   // ends with a block barrier
+        if (tid < N) LC.gid[tid] = C.x[tid];
+        // groups of this GPU's experts (EP: other GPUs' picks leave the grouping)
+        build_groups(C, N, n_loc, [&](int e) { return C.x[e] - lo_e; }, resolve, a.err, epm);   // ends with a barrier
         if (warp == 0 && !C.fail) {
             const int U = C.n_unique;
             uint32_t run = 0;
@@ -340,7 +423,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                 const int u = u0 + lane;
                 uint32_t w = 0;
                 if (u < U) w = static_cast<uint32_t>(C.goff[u + 1] - C.goff[u]);
-                else if (u == U && hs) w = static_cast<uint32_t>(n_tok);
+                else if (u == U && hs) w = static_cast<uint32_t>(n_sh);
                 uint32_t incl = w;
 #pragma unroll
                 for (int off = 1; off < 32; off <<= 1) {
@@ -357,7 +440,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             if (P.u < C.n_unique) {
                 for (int m = C.goff[P.u]; m < C.goff[P.u + 1]; ++m) tokmask |= 1u << (C.gmem[m] / k);
             } else {
-                tokmask = (1u << n_tok) - 1u;
+                tokmask = epm ? 1u << me : (1u << n_tok) - 1u;
             }
         }
         if (warp == PW) {
@@ -369,7 +452,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             if ((tokmask >> t) & 1u) stage_x(t, job % nbx);
         }
         for (int e = tid; e < N; e += PW * 32) C.eslot[e] = static_cast<int16_t>(e / k);
-        if (tid < n_tok) C.shslot[tid] = static_cast<int16_t>(tid);
+        if (tid < n_sh) C.shslot[tid] = static_cast<int16_t>(epm ? me : tid);
         consumer_sync();
     }
 
@@ -385,23 +468,24 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     // ---- gating weights of this CTA's tokens (warps from the top) and the
     //      reference kernel's bookkeeping (:163-198, the first CTA) -----------
     // (the first CTA does every token: it publishes the weights)
-    const uint32_t wmask = bid == 0 ? (1u << n_tok) - 1u : tokmask;
+    const uint32_t wmask = epm ? (tokmask | (1u << me)) : (bid == 0 ? (1u << n_tok) - 1u : tokmask);
     if (one && early && warp == PW - 1) {
         // the shared expert's CTAs route now, off their critical path
-        route_select(a.logits, E, k, lane, C.x);
+        route_select(a.logits, E, k, lane, LC.gid);
         __syncwarp();
     }
     if (run && warp >= PW - n_tok && ((wmask >> (PW - 1 - warp)) & 1u)) {
         const int t = PW - 1 - warp;
-        route_weights(a.logits + static_cast<int64_t>(t) * E, E, k, a.norm_w, lane, &C.x[t * k], &LC.wt[t * k]);
+        route_weights(lg_base + static_cast<int64_t>(t) * E, E, k, a.norm_w, lane, &LC.gid[t * k], &LC.wt[t * k]);
         __syncwarp();
-        if (bid == 0 && lane < k) a.w_out[t * k + lane] = LC.wt[t * k + lane];
+        if (bid == 0 && lane < k && (!epm || t == me)) a.w_out[(epm ? 0 : t) * k + lane] = LC.wt[t * k + lane];
     }
     if (bid == 0 && run && warp == PW - 1 - n_tok) {
         const uint32_t clk = a.clock ? *a.clock : 0u;
         for (int e = lane; e < N; e += 32) {
             const int x = C.x[e], g = C.uidx[e];
-            a.ids_out[e] = x;
+            if (!epm || e / k == me) a.ids_out[epm ? e % k : e] = LC.gid[e];
+            if (x < 0) continue;              // another GPU's expert
             const LayerTensor *T[3] = {&a.up, &a.gate, &a.down};
             const uint8_t host[3] = {C.uhost[g][0], C.uhost[g][1], LC.dhost[g]};
 #pragma unroll
@@ -420,7 +504,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     }
     if (bid == 0 && !run && tid == 0) {
         // keep the routing visible even when a bad id stopped the launch
-        for (int e = 0; e < N; ++e) a.ids_out[e] = C.x[e];
+        for (int e = 0; e < N; ++e)
+            if (!epm || e / k == me) a.ids_out[epm ? e % k : e] = LC.gid[e];
     }
 
     // ---- 2a. gate/up + GLU of this CTA's rows -> h (and tagged copies) ------
@@ -446,10 +531,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     consumer_sync();
     if (warp == 0) L2_MARK(9);
     // phase-B activation slots: member m of the unit -> slot m
-    const int nm = run ? (routed ? C.goff[u + 1] - C.goff[u] : n_tok) : 0;
+    const int nm = run ? (routed ? C.goff[u + 1] - C.goff[u] : n_sh) : 0;
     if (routed) {
         for (int m = tid; m < nm; m += PW * 32) C.eslot[C.gmem[C.goff[u] + m]] = static_cast<int16_t>(m);
-    } else if (tid < n_tok) {
+    } else if (tid < n_sh) {
         C.shslot[tid] = static_cast<int16_t>(tid);
     }
     consumer_sync();
@@ -555,7 +640,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
 
     // ---- 2d. arrivals per (token, row block); the CTA completing a block sums
     //      it: picks in order, then the shared expert --------------------------
-    if (run && P.b1 > P.b0) {
+    if (run && P.b1 > P.b0 && !epm) {
         const int RB = LAYER2_RB;
         const int rb0 = P.b0 / RB, nblk = (P.b1 - 1) / RB - rb0 + 1;
         for (int pair = warp; pair < nm * nblk; pair += PW) {
@@ -581,6 +666,70 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             if (lane == 0) atomicExch(&a.rowcnt[t * a.n_rb + b], 0u);
         }
     }
+    if (epm) {
+        // Expert-parallel: every routed row goes home -- token t lives on GPU
+        // t -- as pick p of its yhome (peer stores over NVLink), and the rows
+        // are counted at home per block of 64 (release at system scope). The
+        // shared expert's rows stay here (ys). Then CTA c < n_rb of every GPU
+        // waits for block c of its own token and sums it in pick order.
+        const EpDecodeLayout &Ly = a.ep.lay;
+        const int RB = LAYER2_RB;
+        if (run && routed && P.b1 > P.b0) {
+            const int w4 = (P.b1 - P.b0) % 4 == 0 && P.b0 % 4 == 0;
+            for (int m = 0; m < nm; ++m) {
+                const int e = C.gmem[C.goff[u] + m], t = e / k, p = e % k;
+                const float *src = a.dn.dst + static_cast<int64_t>(t) * a.dn.stride_col_dst +
+                                   static_cast<int64_t>(p) * a.dn.stride_channel_dst;
+                float *dst = reinterpret_cast<float *>(a.ep.peer[t] + Ly.yhome) + static_cast<int64_t>(p) * H;
+                if (w4) {
+                    for (int r = P.b0 / 4 + tid; r < P.b1 / 4; r += PW * 32)
+                        reinterpret_cast<float4 *>(dst)[r] = __ldcg(reinterpret_cast<const float4 *>(src) + r);
+                } else {
+                    for (int r = P.b0 + tid; r < P.b1; r += PW * 32) dst[r] = __ldcg(src + r);
+                }
+            }
+        }
+        __threadfence_system();
+        consumer_sync();
+        if (run && P.b1 > P.b0) {
+            const int rb0 = P.b0 / RB, nblk = (P.b1 - 1) / RB - rb0 + 1;
+            for (int pair = tid; pair < nm * nblk; pair += PW * 32) {
+                const int m = pair / nblk, b = rb0 + pair % nblk;
+                const int t = routed ? C.gmem[C.goff[u] + m] / k : me;
+                const int lo = b * RB, hi = min(H, lo + RB);
+                const uint32_t mine = static_cast<uint32_t>(min(P.b1, hi) - max(P.b0, lo));
+                red_release_sys_add(reinterpret_cast<uint32_t *>(a.ep.peer[t] + Ly.rowcnt) + b, mine);
+            }
+        }
+        if (bid < a.n_rb) {
+            const int b = bid, lo = b * RB, hi = min(H, lo + RB);
+            uint32_t *cnt = reinterpret_cast<uint32_t *>(a.ep.peer[me] + Ly.rowcnt) + b;
+            const uint32_t target = static_cast<uint32_t>(hi - lo) * static_cast<uint32_t>(k + hs);
+            if (tid == 0) {
+                const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
+                while (ld_acquire_sys_u32(cnt) < target) {
+                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                        set_error(a.err, DERR_TIMEOUT_FULL);
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
+            consumer_sync();
+            const float *yh = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.yhome);
+            for (int r = lo + tid; r < hi; r += PW * 32) {
+                float acc = 0.f;
+                for (int p = 0; p < k; ++p) {
+                    const float v = __fmul_rn(__ldcg(yh + static_cast<int64_t>(p) * H + r), LC.wt[me * k + p]);
+                    acc = p == 0 ? v : __fadd_rn(acc, v);
+                }
+                if (has_shared) acc = __fadd_rn(acc, __ldcg(a.dn.shared_dst + r));
+                a.out[r] = acc;
+            }
+            consumer_sync();
+            if (tid == 0) atomicExch(cnt, 0u);
+        }
+    }
 
 #ifdef MOE_LAYER2_TRACE
     consumer_sync();
@@ -592,6 +741,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     if (tid == 0 && atomicAdd(&a.gbar[1], 1u) == gridDim.x - 1) {
         atomicExch(&a.gbar[1], 0u);
         atomicAdd(&a.gbar[0], 1u);
+        if (epm) atomicAdd(reinterpret_cast<uint32_t *>(a.ep.peer[me] + a.ep.lay.epoch), 1u);
     }
 }
 

@@ -95,6 +95,19 @@ class EPMoELayer:
                 dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)
         return out
 
+    def decode_p2p(self, ex, x, logits, out=None, stream=None):
+        """This rank's token through the layer with the experts sharded over
+        the ranks and the exchange inside the layer kernel
+        (moe_b200_ep_layer_decode_p2p): x f32 [1, H], logits f32 [1, E]
+        (device) -> out f32 [1, H]. `ex` is a connected DecodeExchange."""
+        if out is None:
+            out = torch.empty((1, self.H), dtype=torch.float32, device=self.device)
+        ws = self.workspace(self.world)
+        check(lib().moe_b200_ep_layer_decode_p2p(ctypes.byref(self.desc), self.lo, self.E, ex.table, self.world,
+                                                 self.rank, _ptr(x), _ptr(logits), _ptr(out), _ptr(ws), ws.numel(),
+                                                 _stream(stream)))
+        return out
+
     # ---- prefill ------------------------------------------------------------
     def _prefill_ws(self, n_tok, k):
         key = ("prefill", n_tok, k)
@@ -252,6 +265,53 @@ class PeerExchange:
         for p in list(self.own.values()) + [self.scratch]:
             lib().moe_b200_ipc_free(p)
         self.own = {}
+
+
+class DecodeExchange:
+    """One GPU's buffer of the expert-parallel decode exchange (gather slots
+    for every GPU's token, the returned down rows of this GPU's token, arrival
+    and row counters; layout in include/moe_cache_b200.h), and the other
+    GPUs' buffers opened by CUDA IPC. One exchange serves any number of layers
+    of one shape, called in the same order on every GPU."""
+
+    def __init__(self, H, n_experts, k, rank, world, group=None):
+        self.rank, self.world, self.group = rank, world, group
+        nbytes = lib().moe_b200_ep_decode_buffer_bytes(H, n_experts, k, world)
+        if nbytes == 0:
+            raise ValueError("bad expert-parallel decode shape")
+        p = ctypes.c_void_p()
+        check(lib().moe_b200_ipc_alloc(nbytes, ctypes.byref(p)))
+        self.own = p.value
+        self.opened = []
+        self.table = None
+
+    def connect(self):
+        W = self.world
+        ptrs = [0] * W
+        ptrs[self.rank] = self.own
+        if W > 1:
+            import torch.distributed as dist
+            h = (ctypes.c_char * 64)()
+            check(lib().moe_b200_ipc_handle(self.own, h))
+            every = [None] * W
+            dist.all_gather_object(every, bytes(h), group=self.group)
+            for r in range(W):
+                if r == self.rank:
+                    continue
+                p = ctypes.c_void_p()
+                check(lib().moe_b200_ipc_open((ctypes.c_char * 64).from_buffer_copy(every[r]), ctypes.byref(p)))
+                self.opened.append(p.value)
+                ptrs[r] = p.value
+        self.table = (ctypes.c_void_p * W)(*ptrs)
+        return self
+
+    def close(self):
+        for p in self.opened:
+            check(lib().moe_b200_ipc_close(p))
+        self.opened = []
+        if self.own:
+            check(lib().moe_b200_ipc_free(self.own))
+            self.own = None
 
 
 def prefill_p2p_stages(L, ex, x, logits, stream=None):

@@ -15,8 +15,13 @@ reads expert weights that the L2 (126 MB) no longer holds.
   python bench.py [--gpus N --steps K --warmup W]       # this implementation
   python bench.py --impl reference [...]                 # CPU reference arm
 
-N > 1 (under torchrun): replicas -- every rank runs the same workload on its
-own GPU with its own layers; value = all ranks' tokens / max-over-ranks time.
+N > 1 (under torchrun): expert-parallel decode -- every layer copy's 512
+experts are split over the N GPUs (512 / N each, the shared expert on every
+GPU), every GPU brings its own batch-1 token per step, and each step is one
+launch per GPU of the layer kernel with the exchange inside it (tokens
+gathered, down rows returned and summed over NVLink peer memory); value = all
+ranks' tokens / max-over-ranks time. Rank 0 checks its outputs against a
+full copy of the layer decoded on its own GPU and reports the difference.
 """
 import argparse
 import json
@@ -201,6 +206,8 @@ def run_mine(args):
     import torch.distributed as dist
     import importlib
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        return run_mine_ep(args)
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -372,6 +379,193 @@ def run_mine(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_mine_ep(args):
+    """Config 2 with the experts sharded over the ranks (see the module
+    docstring). Timed like the one-GPU line: K steps replayed from CUDA graphs,
+    barrier + synchronize around the timed region, max over ranks."""
+    import datetime
+    import importlib
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    ep = importlib.import_module("a6000-custom-kernels_b200.ep")
+    mc = pkg.moe_cache
+    mc.configure(enabled=True)
+    R = args.layers
+    lo, hi = ep.expert_range(E, rank, world)
+    layers, check_full = [], None
+    for l in range(R):
+        # the same full layer on every rank (same seeds), sliced to this rank's experts
+        full = pkg.MoELayer(H, F, E, K_TOP, {"gate": Q2_K, "up": Q2_K, "down": Q2_K}, shared=True, device=dev,
+                            seed=l, name=f"blk.{l}")
+        layers.append(ep.EPMoELayer(full, rank, world))
+        if l == 0 and rank == 0:
+            check_full = full
+        del full
+    torch.cuda.synchronize()
+    ex = ep.DecodeExchange(H, E, K_TOP, rank, world).connect()
+    P = 64
+    xs_np, lg_np = token_pool(P, 1234 + rank)
+    xs = torch.from_numpy(xs_np).to(dev).view(P, 1, H)
+    lgs = torch.from_numpy(lg_np).to(dev).view(P, 1, E)
+    outs = torch.empty((P, 1, H), device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(i):
+        layers[i % R].decode_p2p(ex, xs[i % P], lgs[i % P], outs[i % P], stream=stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, R)):
+            step(i)
+    torch.cuda.synchronize()
+    assert mc.device_error(stream) == 0
+
+    # in-run check (rank 0): layer copy 0 on this GPU alone, same token
+    check = None
+    with torch.cuda.stream(stream):
+        layers[0].decode_p2p(ex, xs[0], lgs[0], outs[0], stream=stream)
+    torch.cuda.synchronize()
+    if rank == 0:
+        ref = check_full.decode(xs[0], lgs[0])
+        torch.cuda.synchronize()
+        check = float((outs[0] - ref).abs().max() / ref.abs().max())
+        del check_full, ref
+
+    G = 512
+    K = args.steps
+
+    def graph_for(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for j in range(n):
+                step(j)
+        return g
+
+    full_g = graph_for(G) if K >= G else None
+    rem = graph_for(K % G) if K % G else None
+    with torch.cuda.stream(stream):
+        if full_g is not None:
+            full_g.replay()
+        if rem is not None:
+            rem.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    clocks.start()
+    time.sleep(0.3)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(K // G):
+            full_g.replay()
+        if rem is not None:
+            rem.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    dist.barrier()
+    clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    assert mc.device_error(stream) == 0
+    value = world * K / (ms / 1e3)
+
+    # end to end: per step, H2D of the token and logits, the layer, D2H of the output
+    hx = torch.from_numpy(xs_np).pin_memory()
+    hl = torch.from_numpy(lg_np).pin_memory()
+    hout = torch.empty((P, H), dtype=torch.float32).pin_memory()
+    dx, dl, dout = torch.empty((1, H), device=dev), torch.empty((1, E), device=dev), torch.empty((1, H), device=dev)
+    n_e2e = min(args.e2e_steps, 1000)
+
+    def one(i):
+        with torch.cuda.stream(stream):
+            dx.copy_(hx[i % P:i % P + 1], non_blocking=True)
+            dl.copy_(hl[i % P:i % P + 1], non_blocking=True)
+            layers[i % R].decode_p2p(ex, dx, dl, dout, stream=stream)
+            hout[i % P:i % P + 1].copy_(dout, non_blocking=True)
+        stream.synchronize()
+
+    for i in range(20):
+        one(i)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n_e2e):
+        one(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * n_e2e / float(t.item())
+
+    # expert bytes this rank streams per step: its experts picked by any rank's
+    # token (each once) plus the shared expert, 3 matrices each
+    pools = [token_pool(P, 1234 + r)[1] for r in range(world)]
+    per_step = []
+    for i in range(P):
+        picks = set()
+        for r in range(world):
+            picks |= set(np.argsort(-pools[r][i], kind="stable")[:K_TOP].tolist())
+        mine = sum(1 for e in picks if lo <= e < hi)
+        per_step.append((mine + 1) * 3 * EXPERT_BYTES)
+    bytes_rank0 = float(np.mean(per_step))
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs") or 6650.0
+    k_us = 1e3 * ms / K
+    achieved = bytes_rank0 / (k_us * 1e-6) / 1e9
+    if rank == 0:
+        ck = clocks.summary(wall0, wall1)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(ms / K, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD + f"; experts sharded {E // world} per GPU, one token per GPU per step",
+                       "global_batch": world, "seq_len": 1, "parallelism": f"ep{world}",
+                       "layers_cycled": R, "l2": f"inputs larger than L2: {R} layer copies "
+                                                 f"({R * 3 * E * EXPERT_BYTES / world / 1e9:.1f} GB per GPU) cycled",
+                       "graph": "CUDA graphs of 512-step chunks",
+                       "exchange": "inside the layer kernel: peer stores over NVLink (CUDA IPC), no NCCL on the data path"},
+            "layer_gbs_rank0": round(achieved, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": "of measured",
+                         "traffic": None, "bytes_per_launch": round(bytes_rank0),
+                         "kernel": "moe_layer2_kernel<Q2_K,Q2_K> with the expert-parallel exchange (rank 0)",
+                         "us_per_launch": round(k_us, 3),
+                         "timing": f"timed region: {K} back-to-back launches in CUDA graphs, per-step time"},
+            "parity_check": {"rank0_max_rel_err_vs_one_gpu": check,
+                             "what": "rank 0's token through layer copy 0 sharded over all GPUs vs the same layer "
+                                     "whole on rank 0's GPU"},
+            "cpu_baseline": None,
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": (H + E) * 4 * world,
+                    "d2h_bytes_per_step": H * 4 * world, "steps": n_e2e},
+            "gpu_launches": world * K,
+            "clocks": ck,
+        }
+        print(json.dumps(line), flush=True)
+    del full_g, rem
+    torch.cuda.synchronize()
+    dist.barrier()
+    ex.close()
+    for L in layers:
+        L._ws.clear()
+    dist.destroy_process_group()
 
 
 def time_gateup_kernel(pkg, layers, xs, dev, stream, n):

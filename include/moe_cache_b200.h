@@ -343,6 +343,34 @@ int moe_b200_ep_experts_rows(const moe_layer_desc *layer, const float *x, const 
 int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap, const int32_t *ids,
                        const int32_t *src, const float *y, int64_t H, void *scratch, moe_stream_t stream);
 
+/* No counterpart in the reference (the reference runs on one GPU): one MoE
+ * layer decode with the experts sharded over `world` GPUs of one node and the
+ * exchange fused into the per-expert-group layer kernel, one launch per GPU
+ * per layer, no host round trip. GPU r holds global experts [expert_lo,
+ * expert_lo + layer->n_experts) of n_experts_global (its gate/up/down
+ * tensors hold just those) and the shared expert, and brings ONE token: x
+ * f32 [H] and its router logits f32 [n_experts_global]; `out` f32 [H]
+ * receives that token's layer output. Each GPU allocates one exchange buffer
+ * of moe_b200_ep_decode_buffer_bytes with moe_b200_ipc_alloc (zero-filled),
+ * shares its handle and opens the others'; peer_bufs[r] is GPU r's buffer as
+ * seen from the caller. In the kernel each GPU writes its token into every
+ * GPU's gather slot (peer stores over NVLink, one slot per source, double
+ * buffered by call parity) and waits for all of them; routes every token;
+ * runs its own experts for every token that picked them (per-expert CTA
+ * groups) and the shared expert for its own token; writes each routed down
+ * row into the token's GPU and counts it there; and sums its own token's
+ * rows in pick order once they have all arrived. Waits for other GPUs are
+ * bounded by the exchange limit of moe_b200_set_wait_limits (device error
+ * MOE_DERR_TIMEOUT_FULL). Every GPU must make the same sequence of calls.
+ * Workspace: moe_b200_layer_workspace_size(layer, world) bytes, zero-filled
+ * once. Gate and up share a type; the type pair needs a fused kernel
+ * (moe_b200_layer_fused(layer, world)); world <= 8. */
+size_t moe_b200_ep_decode_buffer_bytes(int64_t H, int64_t n_experts_global, int64_t k, int32_t world);
+int moe_b200_ep_layer_decode_p2p(const moe_layer_desc *layer, int64_t expert_lo, int64_t n_experts_global,
+                                 const void *const *peer_bufs, int32_t world, int32_t rank, const float *x,
+                                 const float *logits, float *out, void *workspace, size_t workspace_bytes,
+                                 moe_stream_t stream);
+
 /* No counterpart in the reference: 1 when moe_b200_layer_decode runs this
  * layer as one fused kernel for n_tok tokens (gate/up and down type pair with a
  * fused kernel, n_tok <= 8, n_tok * k <= 64, activations and tiles fit in

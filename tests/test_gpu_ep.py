@@ -236,3 +236,106 @@ def test_prefill_peer_exchange_two_gpus():
     assert all(p.exitcode == 0 for p in procs)
     for rank, err, code in res:
         assert code == 0 and err == 0.0, (rank, err, code)
+
+
+def _fused_ep_reference(pkg, full, x, lg):
+    pkg.moe_cache.set_layer_fused(False)          # the four-launch path: the same arithmetic, pick-order combine
+    ref = full.decode(x, lg).clone()
+    pkg.moe_cache.set_layer_fused(True)
+    return ref
+
+
+@pytest.mark.parametrize("types", [(O.Q2_K, O.Q2_K, O.Q2_K), (O.Q4_K, O.Q4_K, O.Q6_K)])
+def test_fused_ep_decode_one_gpu(pkg, cuda, types):
+    """The fused expert-parallel decode with world = 1 (the GPU exchanges with
+    itself: gather slot, arrival word, returned rows and row counters all take
+    the real path) equals the single-GPU layer bit for bit, over calls that
+    alternate the gather parity, eagerly and replayed from a CUDA graph."""
+    ep = _ep(pkg)
+    H, F, E, k = 3072, 768, 512, 8
+    full = pkg.MoELayer(H, F, E, k, {"gate": types[0], "up": types[1], "down": types[2]}, shared=True, seed=31)
+    L = ep.EPMoELayer(full, 0, 1)
+    ex = ep.DecodeExchange(H, E, k, 0, 1).connect()
+    try:
+        xs = [torch.from_numpy(activations((1, H), seed=80 + i)).to(cuda) for i in range(5)]
+        lgs = [torch.from_numpy(zipf_logits(1, E, seed=90 + i)).to(cuda) for i in range(5)]
+        refs = [_fused_ep_reference(pkg, full, xs[i], lgs[i]) for i in range(5)]
+        for i in range(5):
+            out = L.decode_p2p(ex, xs[i], lgs[i])
+            assert pkg.moe_cache.device_error() == 0
+            assert torch.equal(out, refs[i]), i
+        s = torch.cuda.Stream()
+        outs = torch.zeros((5, 1, H), device=cuda)
+        with torch.cuda.stream(s):
+            L.decode_p2p(ex, xs[0], lgs[0], outs[0], stream=s)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(5):
+                L.decode_p2p(ex, xs[i], lgs[i], outs[i], stream=s)
+        for _ in range(3):
+            outs.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            for i in range(5):
+                assert torch.equal(outs[i], refs[i]), i
+        del g
+        assert pkg.moe_cache.device_error() == 0
+    finally:
+        torch.cuda.synchronize()
+        ex.close()
+
+
+def _fused_ep_worker(rank, world, port, q):
+    import importlib
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    ep = importlib.import_module("a6000-custom-kernels_b200.ep")
+    pkg.moe_cache.configure(enabled=True)
+    pkg.moe_cache.set_wait_limits(0, 5_000_000_000)
+    H, F, E, k = 3072, 768, 512, 8
+    layers = [pkg.MoELayer(H, F, E, k, {"gate": 10, "up": 10, "down": t}, shared=True, seed=40 + t,
+                           device=f"cuda:{rank}") for t in (10, 12)]
+    shards = [ep.EPMoELayer(full, rank, world) for full in layers]
+    ex = ep.DecodeExchange(H, E, k, rank, world).connect()
+    worst, codes = 0.0, []
+    for call in range(6):
+        full, L = layers[call % 2], shards[call % 2]
+        x = torch.from_numpy(activations((1, H), seed=100 + 10 * call + rank)).cuda()
+        lg = torch.from_numpy(zipf_logits(1, E, seed=200 + 10 * call + rank)).cuda()
+        ref = _fused_ep_reference(pkg, full, x, lg)
+        out = L.decode_p2p(ex, x, lg)
+        torch.cuda.synchronize()
+        worst = max(worst, float((out - ref).abs().max()))
+        codes.append(pkg.moe_cache.device_error())
+    dist.barrier()
+    ex.close()
+    dist.destroy_process_group()
+    q.put((rank, worst, max(codes)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_ep_decode_two_gpus():
+    """Two GPUs, one token each, 512 experts split 256/256, the exchange inside
+    the layer kernel over NVLink peer memory: each GPU's output equals the
+    single-GPU layer of its token bit for bit, over six calls of two layers."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29750 + os.getpid() % 1000
+    procs = [ctx.Process(target=_fused_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    res = [q.get(timeout=5) for _ in range(2)]
+    assert all(p.exitcode == 0 for p in procs)
+    for rank, err, code in res:
+        assert code == 0 and err == 0.0, (rank, err, code)
