@@ -32,12 +32,12 @@ constexpr int LAYER2_RB = 64;            // output rows per combine block
 // Optional timeline (built with -DMOE_LAYER2_TRACE): per CTA and mark, the
 // global timer (ns) and the SM clock; off by default.
 #ifdef MOE_LAYER2_TRACE
-__device__ unsigned long long g_layer2_trace[148 * 32];
+__device__ unsigned long long g_layer2_trace[148 * 64];
 #define L2_MARK(i)                                                                               \
     do {                                                                                         \
         if (lane == 0) {                                                                         \
-            g_layer2_trace[blockIdx.x * 32 + (i)] = global_timer_ns();                           \
-            g_layer2_trace[blockIdx.x * 32 + 16 + (i)] = clock64();                              \
+            g_layer2_trace[blockIdx.x * 64 + (i)] = global_timer_ns();                           \
+            g_layer2_trace[blockIdx.x * 64 + 32 + (i)] = clock64();                              \
         }                                                                                        \
     } while (0)
 #else
@@ -382,6 +382,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                 __syncthreads();
                 if (tid == 0) st_release_sys_u32(reinterpret_cast<uint32_t *>(dst + Ly.arr) + me, xep + 1u);
             }
+            if (warp == 0) L2_MARK(15);
             if (tid < W) {
                 const uint32_t *arr = reinterpret_cast<const uint32_t *>(a.ep.peer[me] + Ly.arr) + tid;
                 const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
@@ -394,6 +395,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                     __nanosleep(64);
                 }
             }
+            if (warp == 0) L2_MARK(16);
             x_base = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.gx) + static_cast<int64_t>(par) * W * H;
             lg_base = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.glog) + static_cast<int64_t>(par) * W * E;
         }
@@ -413,6 +415,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             else route_select(lg_base + static_cast<int64_t>(t) * E, E, k, lane, &C.x[t * k]);
         }
         __syncthreads();
+        if (warp == 0) L2_MARK(17);
         if (tid < N) LC.gid[tid] = C.x[tid];
         // groups of this GPU's experts (EP: other GPUs' picks leave the grouping)
         build_groups(C, N, n_loc, [&](int e) { return C.x[e] - lo_e; }, resolve, a.err, epm);   // ends with a barrier
@@ -443,6 +446,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                 tokmask = epm ? 1u << me : (1u << n_tok) - 1u;
             }
         }
+        if (warp == 0) L2_MARK(18);
         if (warp == PW) {
             if (!C.fail) produce(P);
             return;
@@ -691,6 +695,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
         }
         __threadfence_system();
         consumer_sync();
+        if (warp == 0) L2_MARK(19);
         if (run && P.b1 > P.b0) {
             const int rb0 = P.b0 / RB, nblk = (P.b1 - 1) / RB - rb0 + 1;
             for (int pair = tid; pair < nm * nblk; pair += PW * 32) {
@@ -716,6 +721,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
                 }
             }
             consumer_sync();
+            if (warp == 0) L2_MARK(20);
             const float *yh = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.yhome);
             for (int r = lo + tid; r < hi; r += PW * 32) {
                 float acc = 0.f;
@@ -734,7 +740,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
 #ifdef MOE_LAYER2_TRACE
     consumer_sync();
     if (warp == 0) L2_MARK(12);
-    if (tid == 0) g_layer2_trace[blockIdx.x * 32 + 14] = u;
+    if (tid == 0) g_layer2_trace[blockIdx.x * 64 + 31] = u;
 #endif
     // ---- the last CTA to finish advances the epoch (every tagged read of this
     //      launch is done) ------------------------------------------------------

@@ -36,7 +36,9 @@ class MoELayer:
                 buf = torch.empty((n_experts, rows, row_size(t, K)), dtype=torch.uint8, device=self.device)
                 fill_quantized(t, buf, n_experts * rows, K, seed * 1000003 + i)
                 if host:
-                    buf = buf.cpu().pin_memory()
+                    pinned = torch.empty(buf.shape, dtype=torch.uint8, pin_memory=True)
+                    pinned.copy_(buf)
+                    buf = pinned
             self.w[role] = buf
         self.desc_t = {r: expert_tensor(self.w[r], self.types[r], shapes[r][1], shapes[r][0],
                                         name=f"{name}.ffn_{r}_exps.weight") for r in ("gate", "up", "down")}

@@ -700,10 +700,7 @@ def stack_types(n_layers, seed=3):
 def run_other_config(args):
     """Config 1: one small Q4_0 layer (32 copies cycled). Config 3: the
     48-layer stack, one decode step = every layer in turn with a residual add,
-    batch 1..64 (chunks of 8 tokens per layer launch above 8). Config 5:
-    config 3's shape with experts in pinned host memory behind a pool capped at
-    25 % of the experts, seeded from a Zipf frequency table; eager steps with
-    the cache step between them (it cannot run inside graph capture)."""
+    batch 1..64 (chunks of 8 tokens per layer launch above 8)."""
     import torch
     import importlib
     pkg = importlib.import_module("a6000-custom-kernels_b200")
@@ -712,7 +709,6 @@ def run_other_config(args):
     torch.cuda.set_device(dev)
     stream = torch.cuda.Stream(device=dev)
     B = args.batch
-    seed_path = None
     if args.config == 1:
         H1, F1, E1, R = 2048, 512, 64, 32
         mc.configure(enabled=True)
@@ -736,27 +732,10 @@ def run_other_config(args):
         n_layers_step = 1
         mean_bytes = float(np.mean(step_bytes))
     else:
-        n_layers = 48 if args.config == 3 else 8       # config 5: 8 layers in pinned host memory
+        n_layers = args.stack_layers
         types = stack_types(n_layers)
-        host = args.config == 5
-        seed_path = None
-        if host:
-            # seed each tensor's pool with its 128 most frequent experts under
-            # the layer's Zipf permutation (the routing-frequency table)
-            import tempfile
-            lines = []
-            for l in range(n_layers):
-                perm = np.random.default_rng(1000 + l).permutation(E)
-                hot = np.argsort(perm)[:128]
-                for r in ("gate", "up", "down"):
-                    lines.append(f"blk.{l}.ffn_{r}_exps.weight " + ",".join(str(int(e)) for e in hot))
-            fd_, seed_path = tempfile.mkstemp(suffix=".seed")
-            os.write(fd_, ("\n".join(lines) + "\n").encode())
-            os.close(fd_)
-            mc.configure(enabled=True, slots=128, budget_gb=1e6, seed_path=seed_path)
-        else:
-            mc.configure(enabled=True)
-        layers = [pkg.MoELayer(H, F, E, K_TOP, types[l], shared=True, device=dev, host=host, seed=7000 + l,
+        mc.configure(enabled=True)
+        layers = [pkg.MoELayer(H, F, E, K_TOP, types[l], shared=True, device=dev, seed=7000 + l,
                                name=f"blk.{l}") for l in range(n_layers)]
         P = 16
         rng = np.random.default_rng(33)
@@ -793,57 +772,35 @@ def run_other_config(args):
         workload = (f"config{args.config}: {n_layers}-layer stack of config-2 layers, per-tensor types from "
                     f"{{Q2_K,Q3_K,Q4_K,Q6_K}} drawn by seed (gate/up pair, down) ({gib:.1f} GiB of experts), per-layer Zipf(1.1) routing, "
                     f"shared expert, f32 residual; batch {B}")
-        if host:
-            workload += "; experts in pinned host memory, pool 128 of 512 per tensor, seeded"
         n_layers_step = n_layers
         mean_bytes = float(np.mean(step_bytes))
 
     K = args.steps
     W = max(args.warmup, 3)
-    if args.config == 5:
+    with torch.cuda.stream(stream):
         for i in range(W):
             step(i)
-            mc.step(stream)
-        torch.cuda.synchronize()
-        s0 = mc.stats()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    G = 64 if n_layers_step > 1 else 512
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for j in range(G):
+            step(j)
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = max(1, K // G)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
         ev0.record(stream)
-        for i in range(K):
-            step(i)
-            mc.step(stream)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1)
-        s1 = mc.stats()
-        hits, misses = s1["hits"] - s0["hits"], s1["misses"] - s0["misses"]
-        extra = {"hit_rate": round(hits / max(1, hits + misses), 4),
-                 "promotions_per_step": round((s1["promotions"] - s0["promotions"]) / K, 2),
-                 "timing": "eager steps (cache step between them), device events"}
-    else:
-        with torch.cuda.stream(stream):
-            for i in range(W):
-                step(i)
-        torch.cuda.synchronize()
-        G = 64 if n_layers_step > 1 else 512
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for j in range(G):
-                step(j)
-        with torch.cuda.stream(stream):
+        for _ in range(reps):
             g.replay()
-        torch.cuda.synchronize()
-        reps = max(1, K // G)
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            ev0.record(stream)
-            for _ in range(reps):
-                g.replay()
-            ev1.record(stream)
-        torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1)
-        K = reps * G
-        extra = {"timing": f"CUDA graphs of {G} steps, device events"}
-        del g
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    K = reps * G
+    extra = {"timing": f"CUDA graphs of {G} steps, device events"}
+    del g
     assert mc.device_error(stream) == 0
     peaks = {}
     try:
@@ -861,8 +818,157 @@ def run_other_config(args):
     print(json.dumps(line), flush=True)
     for L in layers:
         L._ws.clear()
-    if seed_path:
-        os.unlink(seed_path)
+
+
+def zipf_gumbel_logits(gen, base, n, device):
+    """n router-logit rows for one layer: log Zipf(1.1) weights of the layer's
+    expert permutation plus Gumbel(0, 1) noise, so the top-8 of a row is a
+    sample of 8 experts without replacement from Zipf(1.1)."""
+    import torch
+    u = torch.rand((n, base.shape[0]), generator=gen, device=device).clamp_(1e-12, 1.0 - 1e-7)
+    return base[None, :] - torch.log(-torch.log(u))
+
+
+def run_config5(args):
+    """Config 5 (tiered-cache stress): the config-3 stack (48 layers, per-tensor
+    types drawn by seed) with every expert tensor in pinned host memory behind
+    an HBM pool capped at 128 of 512 experts per tensor, seeded from a routing
+    frequency table sampled from the same distribution (4096 tokens per
+    layer). Each decode step routes a fresh token with fresh logits drawn as
+    Gumbel-top-8 over log Zipf(1.1) with the layer's own expert permutation,
+    runs every layer (residual added), then the cache's promotion step -- on
+    the GPU, so steps are captured in CUDA graphs of 50 with their fresh
+    inputs refilled on the device before each replay (inside the timed
+    region). Experts the pool misses are read zero-copy over the host link."""
+    import importlib
+    import tempfile
+    import torch
+    pkg = importlib.import_module("a6000-custom-kernels_b200")
+    mc = pkg.moe_cache
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+    n_layers = args.stack_layers
+    types = stack_types(n_layers)
+    POOL = 128
+    bases = []
+    lines = []
+    rng = np.random.default_rng(55)
+    for l in range(n_layers):
+        perm = np.random.default_rng(1000 + l).permutation(E)
+        base = -1.1 * np.log(perm + 1.0)
+        bases.append(base)
+        # routing-frequency table: 4096 sampled tokens of this layer
+        g = -np.log(-np.log(np.clip(rng.random((4096, E)), 1e-12, 1 - 1e-7)))
+        picks = np.argpartition(-(base[None, :] + g), K_TOP, axis=1)[:, :K_TOP]
+        cnt = np.bincount(picks.reshape(-1), minlength=E)
+        hot = sorted(range(E), key=lambda e: (-cnt[e], e))[:POOL]
+        for r in ("gate", "up", "down"):
+            lines.append(f"blk.{l}.ffn_{r}_exps.weight " + ",".join(str(e) for e in hot))
+    fd_, seed_path = tempfile.mkstemp(suffix=".seed")
+    os.write(fd_, ("\n".join(lines) + "\n").encode())
+    os.close(fd_)
+    mc.configure(enabled=True, slots=POOL, budget_gb=1e6, seed_path=seed_path)
+    t_build = time.time()
+    layers = [pkg.MoELayer(H, F, E, K_TOP, types[l], shared=True, device=dev, host=True, seed=7000 + l,
+                           name=f"blk.{l}") for l in range(n_layers)]
+    t_build = time.time() - t_build
+    host_gib = sum(sum(L.w[r].numel() for r in ("gate", "up", "down")) for L in layers) / 2 ** 30
+    mean_expert = float(np.mean([L.w[r][0].numel() for L in layers for r in ("gate", "up", "down")]))
+    base_d = torch.tensor(np.stack(bases), dtype=torch.float32, device=dev)
+    C = 50
+    lg = torch.empty((n_layers, C, 1, E), device=dev)
+    xin = torch.empty((C, 1, H), device=dev)
+    xbuf = torch.empty((1, H), device=dev)
+    obuf = torch.empty((1, H), device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+
+    def refill():
+        for l in range(n_layers):
+            lg[l, :, 0].copy_(zipf_gumbel_logits(gen, base_d[l], C, dev))
+        xin.normal_(generator=gen)
+
+    def step(j):
+        xbuf.copy_(xin[j])
+        for l in range(n_layers):
+            layers[l].decode(xbuf, lg[l, j], obuf, stream=stream)
+            xbuf.add_(obuf)
+        mc.step(stream)
+
+    # warm-up: eager steps register every tensor (seeded pools) and settle the cache
+    W = max(args.warmup, 3)
+    with torch.cuda.stream(stream):
+        for i in range(W):
+            if i % C == 0:
+                refill()
+            step(i % C)
+    torch.cuda.synchronize()
+    assert mc.device_error(stream) == 0
+    # the promotion pass alone (device time), eager
+    evs = []
+    with torch.cuda.stream(stream):
+        refill()
+        for j in range(20):
+            xbuf.copy_(xin[j])
+            for l in range(n_layers):
+                layers[l].decode(xbuf, lg[l, j], obuf, stream=stream)
+                xbuf.add_(obuf)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            mc.step(stream)
+            e1.record(stream)
+            evs.append((e0, e1))
+    torch.cuda.synchronize()
+    pass_us = 1e3 * float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for j in range(C):
+            step(j)
+    torch.cuda.synchronize()
+    K = max(C, min(args.steps, 2000)) // C * C
+    s0 = mc.stats()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    clocks.start()
+    time.sleep(0.3)
+    wall0 = time.time()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(K // C):
+            refill()
+            g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    s1 = mc.stats()
+    assert mc.device_error(stream) == 0
+    hits, misses = s1["hits"] - s0["hits"], s1["misses"] - s0["misses"]
+    promos, evicts = s1["promotions"] - s0["promotions"], s1["evictions"] - s0["evictions"]
+    line = {"metric": METRIC, "value": round(K / (ms / 1e3), 2), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+            "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"config5: {n_layers}-layer config-3 stack ({host_gib:.1f} GiB of experts in pinned "
+                                   f"host memory), HBM pool {POOL} of {E} experts per tensor seeded from a sampled "
+                                   f"frequency table, fresh Gumbel-top-8 Zipf(1.1) routing every step, batch 1",
+                       "global_batch": 1, "layers_per_step": n_layers, "pool_slots": POOL},
+            "hit_rate": round(hits / max(1, hits + misses), 4),
+            "hits_per_step": round(hits / K, 1), "misses_per_step": round(misses / K, 1),
+            "promotions_per_step": round(promos / K, 2), "evictions_per_step": round(evicts / K, 2),
+            "resident_experts": s1["resident"],
+            "hbm_expert_bytes_per_step": round(hits / K * mean_expert),
+            "host_link_bytes_per_step": round((misses + promos) / K * mean_expert),
+            "promotion_pass_us": round(pass_us, 2),
+            "gpu_launches": K * (n_layers * 2 + 2),
+            "timing": f"CUDA graphs of {C} steps (decode of every layer + residual + promotion step), inputs "
+                      f"refilled on the device before each replay, device events",
+            "build_seconds": round(t_build, 1), "clocks": clocks.summary(wall0, wall1)}
+    print(json.dumps(line), flush=True)
+    for L in layers:
+        L._ws.clear()
+    os.unlink(seed_path)
 
 
 def run_config4(args):
@@ -1027,6 +1133,8 @@ def main():
         run_mine(args)
     elif args.config == 4:
         run_config4(args)
+    elif args.config == 5:
+        run_config5(args)
     else:
         run_other_config(args)
 
