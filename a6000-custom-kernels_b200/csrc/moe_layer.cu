@@ -1,6 +1,8 @@
 // moe_layer.cu -- planning and dispatch of the fused layer kernel
 // (moe_layer.cuh). The tile geometry of each phase follows the GEMV's
 // launcher (moe_gemv.cu) so both paths cut rows the same way.
+#include <algorithm>
+
 #include "moe_aux.h"
 #include "moe_layer_launch.cuh"
 
@@ -219,8 +221,10 @@ int plan_layer2(int ta, int tb, Layer2Args &a, int *grid_out, size_t *smem_out, 
     if (part_b > stage) stage = part_b;
     const uint32_t slot_a = round16(static_cast<uint64_t>(H) + H / 8 + H / 8);
     const uint32_t slot_b = round16(static_cast<uint64_t>(F) + F / 8 + F / 8);
-    const uint32_t act = static_cast<uint32_t>((static_cast<uint64_t>(n_tok) * (slot_a > slot_b ? slot_a : slot_b) + 127u) &
-                                               ~uint64_t{127});
+    uint64_t act64 = static_cast<uint64_t>(n_tok) * (slot_a > slot_b ? slot_a : slot_b);
+    // expert-parallel: the area first holds every GPU's router logits (f32 [world][E])
+    if (a.ep_on) act64 = std::max<uint64_t>(act64, 4ull * n_tok * static_cast<uint64_t>(a.n_experts));
+    const uint32_t act = static_cast<uint32_t>((act64 + 127u) & ~uint64_t{127});
     const uint32_t ctrl = (2u * GEMV_MAX_STAGES * 8u + static_cast<uint32_t>(sizeof(Layer2Ctrl)) + 127u) & ~127u;
     const int64_t avail = kSmemLimit - static_cast<int64_t>(ctrl) - act;
     int fit = avail > 0 ? static_cast<int>(avail / stage) : 0;

@@ -46,28 +46,71 @@ __device__ unsigned long long g_layer2_trace[148 * 64];
 constexpr int LAYER2_ROUTE_WARPS = 4;    // warps routing the single token of a batch-1 launch
 
 // Expert-parallel decode: each GPU owns one buffer, mapped into the others
-// (CUDA IPC). Parts (byte offsets, 256-aligned): gx f32 [2][W][H] and glog
-// f32 [2][W][E] -- every GPU's token x and router logits, written by their
-// owners into slot [parity][src] (parity = exchange epoch & 1); yhome f32
-// [k][H] -- the down rows of this GPU's token, pick p written by the GPU
-// that owns its expert; arr u32 [8] -- per source, the exchange epoch + 1 of
-// its last dispatch here; rowcnt u32 [H / 64] -- rows of this GPU's token
-// arrived per block of 64; epoch u32 -- layer calls through the exchange.
+// (CUDA IPC). Every value crosses as one 64-bit word (float bits | tag << 32,
+// tag = exchange epoch + 1), so a reader that sees the tag sees the value:
+// no fence, flag or counter. Parts (byte offsets, 256-aligned): gx u64
+// [2][W][H] and glog u64 [2][W][E] -- every GPU's token x and router logits,
+// written by their owners into slot [parity][src] (parity = epoch & 1);
+// yhome u64 [k + 1][H] -- the down rows of this GPU's token, row p < k
+// written by the GPU owning pick p's expert, row k the shared expert's;
+// epoch u32 -- layer calls through the exchange.
 struct EpDecodeLayout {
-    uint64_t gx, glog, yhome, arr, rowcnt, epoch, bytes;
+    uint64_t gx, glog, yhome, epoch, bytes;
 };
 __host__ __device__ inline EpDecodeLayout ep_decode_layout(int H, int E, int k, int W) {
     auto up = [](uint64_t x) { return (x + 255u) & ~uint64_t{255}; };
     EpDecodeLayout L;
     uint64_t off = 0;
-    L.gx = off;     off += up(4ull * 2 * W * H);
-    L.glog = off;   off += up(4ull * 2 * W * E);
-    L.yhome = off;  off += up(4ull * k * H);
-    L.arr = off;    off += up(4ull * 8);
-    L.rowcnt = off; off += up(4ull * ((H + 63) / 64));
+    L.gx = off;     off += up(8ull * 2 * W * H);
+    L.glog = off;   off += up(8ull * 2 * W * E);
+    L.yhome = off;  off += up(8ull * (k + 1) * H);
     L.epoch = off;  off += 256;
     L.bytes = off;
     return L;
+}
+
+__device__ __forceinline__ uint64_t tagged(float v, uint32_t tag) {
+    return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_u64x2(uint64_t *p, uint64_t a, uint64_t b) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void ld_relaxed_sys_u64x2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// One activation block of tagged words (a Q8_K block of 256 or a Q8_0 block
+// of 32) in the lane layout of load_q8K_vals / stage_q80_block; true when
+// every word of the lane carries `tag`.
+template <bool KQ>
+__device__ __forceinline__ bool load_tagged_block(const uint64_t *xb, uint32_t tag, int lane,
+                                                  float (&v)[KQ ? 8 : 1]) {
+    constexpr int NV = KQ ? 8 : 1;
+    uint64_t w[NV];
+    if constexpr (KQ) {
+        ld_relaxed_sys_u64x2(xb + 4 * lane, w[0], w[1]);
+        ld_relaxed_sys_u64x2(xb + 4 * lane + 2, w[2], w[3]);
+        ld_relaxed_sys_u64x2(xb + 128 + 4 * lane, w[4], w[5]);
+        ld_relaxed_sys_u64x2(xb + 128 + 4 * lane + 2, w[6], w[7]);
+    } else {
+        uint64_t other;
+        ld_relaxed_sys_u64x2(xb + (lane & ~1), w[0], other);
+        if (lane & 1) w[0] = other;
+    }
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        ok &= static_cast<uint32_t>(w[j] >> 32) == tag;
+        v[j] = __uint_as_float(static_cast<uint32_t>(w[j]));
+    }
+    return ok;
 }
 constexpr int EP_DECODE_MAX_WORLD = 8;
 struct EpDecodeArgs {
@@ -199,6 +242,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     // token from this GPU's gather slots
     const float *x_base = reinterpret_cast<const float *>(a.gu.y);
     const float *lg_base = a.logits;
+    const uint64_t *x_tag = nullptr;                 // EP: every GPU's token x as tagged words
+    uint32_t ep_tag = 0;
     if (warp == 0) L2_MARK(0);
     if (warp == PW) L2_MARK(13);
 
@@ -249,8 +294,28 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     };
     // x of token t into activation slot t (llama.cpp CPU quantization)
     auto stage_x = [&](int t, int b) {
-        stage_f32_block<TA>(x_base + static_cast<int64_t>(t) * a.gu.stride_col_y,
-                            act_area + static_cast<size_t>(t) * a.gu.slot_bytes, KA, b, lane);
+        uint8_t *slot = act_area + static_cast<size_t>(t) * a.gu.slot_bytes;
+        if (!x_tag) {
+            stage_f32_block<TA>(x_base + static_cast<int64_t>(t) * a.gu.stride_col_y, slot, KA, b, lane);
+            return;
+        }
+        // EP: the gathered token, polled until every word carries this call's tag
+        constexpr bool KQ = is_kquant(TA);
+        constexpr int QB = KQ ? 256 : 32;
+        const uint64_t *xb = x_tag + static_cast<int64_t>(t) * KA + b * QB;
+        float v[KQ ? 8 : 1];
+        const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
+        while (!__all_sync(0xffffffffu, load_tagged_block<KQ>(xb, ep_tag, lane, v))) {
+            if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+                break;
+            }
+        }
+        int8_t *q = reinterpret_cast<int8_t *>(slot);
+        int16_t *bs = reinterpret_cast<int16_t *>(slot + KA);
+        float *sc = reinterpret_cast<float *>(slot + KA + KA / 8);
+        if constexpr (KQ) quant_q8K_vals<TA>(v, q, bs, sc, b, lane, KA / chunk_of<TA>::CE);
+        else quant_q80_val<TA>(v[0], q, bs, sc, b, lane, KA / chunk_of<TA>::CE);
     };
     constexpr int QA = is_kquant(TA) ? 256 : 32;
     const int nbx = KA / QA;
@@ -364,40 +429,48 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
             if (epm) LC.xep = ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.ep.peer[me] + a.ep.lay.epoch));
         }
         if (epm) {
-            // dispatch: CTA d < world writes this GPU's x and logits into GPU
-            // d's gather slot [parity][me], then publishes them (release at
-            // system scope); every CTA then waits for all GPUs' slots
+            // dispatch: CTA d < world writes this GPU's x and logits as
+            // tagged words into GPU d's gather slot [parity][me]; then every
+            // CTA takes all GPUs' logits from its own slots (polling the
+            // tags) into shared memory for routing
             __syncthreads();
-            const uint32_t xep = LC.xep;
+            const uint32_t xep = LC.xep, etag = xep + 1u;
             const int W = n_tok, par = static_cast<int>(xep & 1u);
             const EpDecodeLayout &Ly = a.ep.lay;
             if (bid < W) {
                 char *dst = a.ep.peer[bid];
-                float4 *gx = reinterpret_cast<float4 *>(dst + Ly.gx) + static_cast<int64_t>(par * W + me) * (H / 4);
-                float *gl = reinterpret_cast<float *>(dst + Ly.glog) + static_cast<int64_t>(par * W + me) * E;
-                const float4 *x4 = reinterpret_cast<const float4 *>(a.gu.y);
-                for (int i = tid; i < H / 4; i += GEMV_THREADS) gx[i] = x4[i];
-                for (int i = tid; i < E; i += GEMV_THREADS) gl[i] = a.logits[i];
-                __threadfence_system();
-                __syncthreads();
-                if (tid == 0) st_release_sys_u32(reinterpret_cast<uint32_t *>(dst + Ly.arr) + me, xep + 1u);
+                uint64_t *gx = reinterpret_cast<uint64_t *>(dst + Ly.gx) + static_cast<int64_t>(par * W + me) * H;
+                uint64_t *gl = reinterpret_cast<uint64_t *>(dst + Ly.glog) + static_cast<int64_t>(par * W + me) * E;
+                const float2 *x2 = reinterpret_cast<const float2 *>(a.gu.y);
+                for (int i = tid; i < H / 2; i += GEMV_THREADS) {
+                    const float2 v = x2[i];
+                    st_relaxed_sys_u64x2(gx + 2 * i, tagged(v.x, etag), tagged(v.y, etag));
+                }
+                for (int i = tid; i < E; i += GEMV_THREADS) st_relaxed_sys_u64(gl + i, tagged(a.logits[i], etag));
             }
             if (warp == 0) L2_MARK(15);
-            if (tid < W) {
-                const uint32_t *arr = reinterpret_cast<const uint32_t *>(a.ep.peer[me] + Ly.arr) + tid;
-                const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
-                while (static_cast<int32_t>(ld_acquire_sys_u32(arr) - (xep + 1u)) < 0) {
-                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
-                        set_error(a.err, DERR_TIMEOUT_FULL);
-                        C.fail = 1;
-                        break;
-                    }
-                    __nanosleep(64);
+            const uint64_t *gl_own = reinterpret_cast<const uint64_t *>(a.ep.peer[me] + Ly.glog) +
+                                     static_cast<int64_t>(par) * W * E;
+            float *lg_s = reinterpret_cast<float *>(act_area);     // free until x is staged
+            const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
+            bool late = false;
+            for (int i = tid; i < W * E; i += GEMV_THREADS) {
+                uint64_t w = ld_relaxed_sys_u64(gl_own + i);
+                while (static_cast<uint32_t>(w >> 32) != etag) {
+                    if (static_cast<uint64_t>(clock64()) - t0 > lim) { late = true; break; }
+                    w = ld_relaxed_sys_u64(gl_own + i);
                 }
+                lg_s[i] = __uint_as_float(static_cast<uint32_t>(w));
+                if (late) break;
+            }
+            if (late) {
+                set_error(a.err, DERR_TIMEOUT_FULL);
+                C.fail = 1;
             }
             if (warp == 0) L2_MARK(16);
-            x_base = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.gx) + static_cast<int64_t>(par) * W * H;
-            lg_base = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.glog) + static_cast<int64_t>(par) * W * E;
+            x_tag = reinterpret_cast<const uint64_t *>(a.ep.peer[me] + Ly.gx) + static_cast<int64_t>(par) * W * H;
+            ep_tag = etag;
+            lg_base = lg_s;
         }
         __syncthreads();
         const int GW = PW / n_tok;
@@ -472,7 +545,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     // ---- gating weights of this CTA's tokens (warps from the top) and the
     //      reference kernel's bookkeeping (:163-198, the first CTA) -----------
     // (the first CTA does every token: it publishes the weights)
-    const uint32_t wmask = epm ? (tokmask | (1u << me)) : (bid == 0 ? (1u << n_tok) - 1u : tokmask);
+    // (EP: only this GPU's own token is summed here; its logits are the caller's)
+    const uint32_t wmask = epm ? (1u << me) : (bid == 0 ? (1u << n_tok) - 1u : tokmask);
     if (one && early && warp == PW - 1) {
         // the shared expert's CTAs route now, off their critical path
         route_select(a.logits, E, k, lane, LC.gid);
@@ -480,7 +554,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     }
     if (run && warp >= PW - n_tok && ((wmask >> (PW - 1 - warp)) & 1u)) {
         const int t = PW - 1 - warp;
-        route_weights(lg_base + static_cast<int64_t>(t) * E, E, k, a.norm_w, lane, &LC.gid[t * k], &LC.wt[t * k]);
+        const float *lw = epm ? a.logits : lg_base + static_cast<int64_t>(t) * E;
+        route_weights(lw, E, k, a.norm_w, lane, &LC.gid[t * k], &LC.wt[t * k]);
         __syncwarp();
         if (bid == 0 && lane < k && (!epm || t == me)) a.w_out[(epm ? 0 : t) * k + lane] = LC.wt[t * k + lane];
     }
@@ -672,68 +747,56 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_layer2_kernel(const __gri
     }
     if (epm) {
         // Expert-parallel: every routed row goes home -- token t lives on GPU
-        // t -- as pick p of its yhome (peer stores over NVLink), and the rows
-        // are counted at home per block of 64 (release at system scope). The
-        // shared expert's rows stay here (ys). Then CTA c < n_rb of every GPU
-        // waits for block c of its own token and sums it in pick order.
+        // t -- as row p of its yhome (tagged words stored over NVLink); the
+        // shared expert's rows go to row k of this GPU's own yhome. CTA c <
+        // n_rb of every GPU then sums rows [64 c, 64 c + 64) of its own token:
+        // each row's words polled until they carry this call's tag, picks in
+        // order, then the shared expert. No fence or counter is needed.
         const EpDecodeLayout &Ly = a.ep.lay;
         const int RB = LAYER2_RB;
-        if (run && routed && P.b1 > P.b0) {
-            const int w4 = (P.b1 - P.b0) % 4 == 0 && P.b0 % 4 == 0;
-            for (int m = 0; m < nm; ++m) {
-                const int e = C.gmem[C.goff[u] + m], t = e / k, p = e % k;
-                const float *src = a.dn.dst + static_cast<int64_t>(t) * a.dn.stride_col_dst +
-                                   static_cast<int64_t>(p) * a.dn.stride_channel_dst;
-                float *dst = reinterpret_cast<float *>(a.ep.peer[t] + Ly.yhome) + static_cast<int64_t>(p) * H;
-                if (w4) {
-                    for (int r = P.b0 / 4 + tid; r < P.b1 / 4; r += PW * 32)
-                        reinterpret_cast<float4 *>(dst)[r] = __ldcg(reinterpret_cast<const float4 *>(src) + r);
-                } else {
-                    for (int r = P.b0 + tid; r < P.b1; r += PW * 32) dst[r] = __ldcg(src + r);
-                }
-            }
-        }
-        __threadfence_system();
-        consumer_sync();
-        if (warp == 0) L2_MARK(19);
+        const uint32_t etag = LC.xep + 1u;
         if (run && P.b1 > P.b0) {
-            const int rb0 = P.b0 / RB, nblk = (P.b1 - 1) / RB - rb0 + 1;
-            for (int pair = tid; pair < nm * nblk; pair += PW * 32) {
-                const int m = pair / nblk, b = rb0 + pair % nblk;
-                const int t = routed ? C.gmem[C.goff[u] + m] / k : me;
-                const int lo = b * RB, hi = min(H, lo + RB);
-                const uint32_t mine = static_cast<uint32_t>(min(P.b1, hi) - max(P.b0, lo));
-                red_release_sys_add(reinterpret_cast<uint32_t *>(a.ep.peer[t] + Ly.rowcnt) + b, mine);
+            for (int m = 0; m < nm; ++m) {
+                const float *src;
+                uint64_t *dst;
+                if (routed) {
+                    const int e = C.gmem[C.goff[u] + m], t = e / k, p = e % k;
+                    src = a.dn.dst + static_cast<int64_t>(t) * a.dn.stride_col_dst +
+                          static_cast<int64_t>(p) * a.dn.stride_channel_dst;
+                    dst = reinterpret_cast<uint64_t *>(a.ep.peer[t] + Ly.yhome) + static_cast<int64_t>(p) * H;
+                } else {
+                    src = a.dn.shared_dst + static_cast<int64_t>(m) * a.dn.shared_stride_col_dst;
+                    dst = reinterpret_cast<uint64_t *>(a.ep.peer[me] + Ly.yhome) + static_cast<int64_t>(k) * H;
+                }
+                for (int r = P.b0 + tid; r < P.b1; r += PW * 32) st_relaxed_sys_u64(dst + r, tagged(__ldcg(src + r), etag));
             }
         }
+        if (warp == 0) L2_MARK(19);
         if (bid < a.n_rb) {
-            const int b = bid, lo = b * RB, hi = min(H, lo + RB);
-            uint32_t *cnt = reinterpret_cast<uint32_t *>(a.ep.peer[me] + Ly.rowcnt) + b;
-            const uint32_t target = static_cast<uint32_t>(hi - lo) * static_cast<uint32_t>(k + hs);
-            if (tid == 0) {
-                const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
-                while (ld_acquire_sys_u32(cnt) < target) {
+            const int lo = bid * RB, hi = min(H, lo + RB);
+            const uint64_t *yh = reinterpret_cast<const uint64_t *>(a.ep.peer[me] + Ly.yhome);
+            const uint64_t t0 = clock64(), lim = timeout_cycles(a.ep_timeout_ns);
+            auto take = [&](int p, int r) -> float {
+                uint64_t w = ld_relaxed_sys_u64(yh + static_cast<int64_t>(p) * H + r);
+                while (static_cast<uint32_t>(w >> 32) != etag) {
                     if (static_cast<uint64_t>(clock64()) - t0 > lim) {
                         set_error(a.err, DERR_TIMEOUT_FULL);
                         break;
                     }
-                    __nanosleep(32);
+                    w = ld_relaxed_sys_u64(yh + static_cast<int64_t>(p) * H + r);
                 }
-            }
-            consumer_sync();
-            if (warp == 0) L2_MARK(20);
-            const float *yh = reinterpret_cast<const float *>(a.ep.peer[me] + Ly.yhome);
+                return __uint_as_float(static_cast<uint32_t>(w));
+            };
             for (int r = lo + tid; r < hi; r += PW * 32) {
                 float acc = 0.f;
                 for (int p = 0; p < k; ++p) {
-                    const float v = __fmul_rn(__ldcg(yh + static_cast<int64_t>(p) * H + r), LC.wt[me * k + p]);
+                    const float v = __fmul_rn(take(p, r), LC.wt[me * k + p]);
                     acc = p == 0 ? v : __fadd_rn(acc, v);
                 }
-                if (has_shared) acc = __fadd_rn(acc, __ldcg(a.dn.shared_dst + r));
+                if (has_shared) acc = __fadd_rn(acc, take(k, r));
                 a.out[r] = acc;
             }
-            consumer_sync();
-            if (tid == 0) atomicExch(cnt, 0u);
+            if (warp == 0) L2_MARK(20);
         }
     }
 
