@@ -8,4 +8,4 @@ importlib.import_module("a6000-custom-kernels_b200") from the repository root.
 from ._lib import MoeError, build, lib  # noqa: F401
 from . import moe_cache  # noqa: F401
 from .moe_cache import *  # noqa: F401,F403
-from .layer import MoELayer  # noqa: F401
+from .layer import MoELayer, Stack  # noqa: F401

@@ -121,6 +121,9 @@ def _declare(L):
         "moe_b200_ep_wait": (i32, [vp, ctypes.c_uint32, vp]),
         "moe_b200_set_wait_limits": (i32, [i64, i64]),
         "moe_b200_ep_decode_buffer_bytes": (sz, [i64, i64, i64, i32]),
+        "moe_b200_stack_workspace_size": (sz, [ctypes.POINTER(MoeLayerDesc), i64]),
+        "moe_b200_stack_prepare": (i32, [ctypes.POINTER(MoeLayerDesc), i64, vp, vp, vp, vp, vp, sz, vp]),
+        "moe_b200_stack_run": (i32, [ctypes.POINTER(MoeLayerDesc), i64, vp, sz, vp]),
         "moe_b200_ep_layer_decode_p2p": (i32, [ctypes.POINTER(MoeLayerDesc), i64, i64, vp, i32, i32, vp, vp, vp, vp,
                                                sz, vp]),
         "moe_b200_ep_experts_rows_workspace_size": (sz, [ctypes.POINTER(MoeLayerDesc), i64]),

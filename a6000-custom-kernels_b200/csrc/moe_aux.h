@@ -9,6 +9,7 @@ namespace moe {
 struct GemvArgs;
 struct LayerArgs;
 struct Layer2Args;
+struct StackArgs;
 struct MmqArgs;
 
 cudaError_t launch_quantize_act(int act_type, const float *x, void *y, int64_t n_rows, int64_t n_cols,
@@ -40,6 +41,9 @@ int launch_layer(int ta, int tb, LayerArgs &a, cudaStream_t st, const char **why
 // The per-expert-group layer kernel (moe_layer2.cuh), same contract.
 int plan_layer2(int ta, int tb, Layer2Args &a, int *grid, size_t *smem, const char **why);
 int launch_layer2(int ta, int tb, Layer2Args &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
+// The persistent stack kernel (moe_stack.cuh) for layers of one type.
+bool stack_type_supported(int ta, int tb);
+int launch_stack(int type, StackArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
 
 // Prefill grouped GEMM on the tensor cores (moe_mmq.cu): launch_mmq_group
 // groups the (token, pick) entries by expert into offsets / entries and the

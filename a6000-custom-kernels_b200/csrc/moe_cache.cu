@@ -38,6 +38,7 @@
 #include "moe_cache_b200.h"
 #include "moe_gemv.cuh"
 #include "moe_layer2.cuh"
+#include "moe_stack.cuh"
 #include "moe_mmq.cuh"
 #include "moe_promote.cuh"
 
@@ -1575,6 +1576,106 @@ int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap,
         return fail(MOE_ERR_INVALID, "y and every peer's row buffers (x, y_ret) must be 16-byte aligned");
     CK(moe::launch_ep_return(peer_ptrs, world, static_cast<int>(cap), ids, src, y, static_cast<int>(H),
                              static_cast<uint32_t *>(scratch), reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+size_t moe_b200_stack_workspace_size(const moe_layer_desc *L, int64_t n_layers) {
+    if (!L || n_layers < 1) return 0;
+    return layer_ws(L, 1, nullptr).bytes + align256(sizeof(moe::StackLayer) * static_cast<size_t>(n_layers));
+}
+
+int moe_b200_stack_prepare(const moe_layer_desc *layers, int64_t n_layers, const float *const *x,
+                           const float *const *logits, float *const *out, float *const *x_next, void *workspace,
+                           size_t workspace_bytes, moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!layers || n_layers < 1 || !x || !logits || !out) return fail(MOE_ERR_INVALID, "null argument");
+    const moe_layer_desc &L0 = layers[0];
+    const size_t need = moe_b200_stack_workspace_size(&L0, n_layers);
+    if (!workspace || workspace_bytes < need) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, need);
+    if (L0.gate.type != L0.up.type || !moe::stack_type_supported(L0.up.type, L0.down.type))
+        return fail(MOE_ERR_UNSUPPORTED, "the stack kernel needs one type for gate, up and down");
+    if (L0.up.ne[0] != L0.H || L0.up.ne[1] != L0.F || L0.down.ne[0] != L0.F || L0.down.ne[1] != L0.H)
+        return fail(MOE_ERR_INVALID, "expert tensor shapes do not match H/F");
+    const bool shared = L0.shared_type >= 0;
+    std::vector<moe::StackLayer> d(static_cast<size_t>(n_layers));
+    const LayerWs w = layer_ws(&L0, 1, static_cast<char *>(workspace));
+    for (int64_t l = 0; l < n_layers; ++l) {
+        const moe_layer_desc &Ll = layers[l];
+        const bool same = Ll.up.type == L0.up.type && Ll.gate.type == L0.gate.type && Ll.down.type == L0.down.type &&
+                          Ll.H == L0.H && Ll.F == L0.F && Ll.n_experts == L0.n_experts && Ll.k == L0.k &&
+                          Ll.glu_op == L0.glu_op && Ll.glu_limit == L0.glu_limit && Ll.norm_w == L0.norm_w &&
+                          (Ll.shared_type >= 0) == shared;
+        if (!same) return fail(MOE_ERR_INVALID, "layer %lld differs from layer 0 in type or shape", static_cast<long long>(l));
+        const moe_tensor *T[3] = {&Ll.gate, &Ll.up, &Ll.down};
+        for (const moe_tensor *t : T)
+            if (!t->data || !contiguous(t) || t->ne[2] != Ll.n_experts || !aligned16(t->data) || t->nb[2] % 16 ||
+                ptr_kind(t->data) != 2)
+                return fail(MOE_ERR_UNSUPPORTED, "stack layers need contiguous, 16-byte aligned expert tensors in device memory");
+        if (shared && (!aligned16(Ll.shared_gate) || !aligned16(Ll.shared_up) || !aligned16(Ll.shared_down)))
+            return fail(MOE_ERR_UNSUPPORTED, "shared expert data must be 16-byte aligned");
+        if (!x[l] || !logits[l] || !out[l]) return fail(MOE_ERR_INVALID, "null x, logits or out of layer %lld", static_cast<long long>(l));
+        moe::StackLayer &s = d[static_cast<size_t>(l)];
+        s.up = static_cast<const char *>(Ll.up.data);
+        s.gate = static_cast<const char *>(Ll.gate.data);
+        s.down = static_cast<const char *>(Ll.down.data);
+        s.sh_up = shared ? static_cast<const char *>(Ll.shared_up) : nullptr;
+        s.sh_gate = shared ? static_cast<const char *>(Ll.shared_gate) : nullptr;
+        s.sh_down = shared ? static_cast<const char *>(Ll.shared_down) : nullptr;
+        s.x = x[l];
+        s.logits = logits[l];
+        s.out = out[l];
+        s.x_next = x_next ? x_next[l] : nullptr;
+        s.ids_out = w.ids;
+        s.w_out = w.w;
+    }
+    char *tail = static_cast<char *>(workspace) + layer_ws(&L0, 1, nullptr).bytes;
+    CK(cudaMemcpyAsync(tail, d.data(), sizeof(moe::StackLayer) * d.size(), cudaMemcpyHostToDevice,
+                       reinterpret_cast<cudaStream_t>(stream)));
+    return MOE_OK;
+}
+
+int moe_b200_stack_run(const moe_layer_desc *layer0, int64_t n_layers, void *workspace, size_t workspace_bytes,
+                       moe_stream_t stream) {
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    read_env();
+    if (!layer0 || n_layers < 1) return fail(MOE_ERR_INVALID, "null argument");
+    const size_t need = moe_b200_stack_workspace_size(layer0, n_layers);
+    if (!workspace || workspace_bytes < need) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, need);
+    if (layer0->gate.type != layer0->up.type || !moe::stack_type_supported(layer0->up.type, layer0->down.type))
+        return fail(MOE_ERR_UNSUPPORTED, "the stack kernel needs one type for gate, up and down");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const LayerWs w = layer_ws(layer0, 1, static_cast<char *>(workspace));
+    // the per-phase shapes and outputs (pointers of layer 0 stand in; the
+    // kernel reads every layer's own from its descriptor)
+    const float *dummy = reinterpret_cast<const float *>(workspace);
+    moe::LayerArgs la;
+    int rc = layer_args(layer0, dummy, dummy, const_cast<float *>(dummy), 1, w, st, &la);
+    if (rc) return rc;
+    moe::StackArgs a{};
+    a.gu = la.gu;
+    a.dn = la.dn;
+    a.layers = reinterpret_cast<const moe::StackLayer *>(static_cast<char *>(workspace) + layer_ws(layer0, 1, nullptr).bytes);
+    a.n_layers = static_cast<int32_t>(n_layers);
+    a.k = static_cast<int32_t>(layer0->k);
+    a.n_experts = static_cast<int32_t>(layer0->n_experts);
+    a.norm_w = layer0->norm_w;
+    a.eb_up = layer0->up.nb[2];
+    a.eb_gate = layer0->gate.nb[2];
+    a.eb_down = layer0->down.nb[2];
+    a.tma = 1;
+    a.has_shared = layer0->shared_type >= 0 ? 1 : 0;
+    a.h_tag = w.h_tag;
+    a.hs_tag = w.hs_tag;
+    a.gbar = w.gbar;
+    a.rowcnt = w.rowcnt;
+    a.err = g.d_err;
+    a.timeout_ns = g.timeout_ns_kernel;
+    const char *why = "";
+    cudaError_t ce = cudaSuccess;
+    rc = moe::launch_stack(layer0->up.type, a, st, &why, &ce);
+    if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+    if (rc) return fail(rc, "%s", why);
     return MOE_OK;
 }
 

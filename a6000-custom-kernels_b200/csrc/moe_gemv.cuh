@@ -740,7 +740,8 @@ struct TileSrc {
 };
 
 // The producer warp: streams tiles 0..n_tiles-1 through the S-stage ring
-// (tile i -> stage i % S, phase i / S). Tiles are issued in rounds
+// (tile i -> ring index g = g0 + i -> stage g % S, phase g / S; g0 > 0 when
+// the ring carries on from earlier tiles of a persistent kernel). Tiles are issued in rounds
 // of up to min(32, S): within a round no tile reuses a stage of the same
 // round, so every lane waits for its own stage and issues its own bulk copies.
 // Tiles that need plain copies (host memory or unaligned sources) follow,
@@ -749,7 +750,7 @@ struct TileSrc {
 template <class Describe>
 __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full, uint64_t *empty,
                                               uint8_t *stage_area, uint32_t stage_bytes, Describe describe,
-                                              uint64_t timeout_ns, int *err, int lane) {
+                                              uint64_t timeout_ns, int *err, int lane, int g0 = 0) {
     const uint64_t pol = l2_evict_first_policy();
     const int R = S < 32 ? S : 32;
     int issued = 0;
@@ -758,12 +759,12 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
         const int cnt = (n_tiles - base) < R ? (n_tiles - base) : R;
         bool plain_tile = false, lane_ok = true;
         if (lane < cnt) {
-            const int i = base + lane, s = i % S;
+            const int i = base + lane, gi = g0 + i, s = gi % S;
             TileSrc ts;
             describe(i, ts);
             plain_tile = ts.kind[0] != 0 || (ts.n_parts > 1 && ts.kind[1] != 0);
             if (!plain_tile) {
-                if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), timeout_ns)) {
+                if (gi >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((gi / S - 1) & 1), timeout_ns)) {
                     lane_ok = false;
                 } else {
                     uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
@@ -798,8 +799,8 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
         while (pending) {
             const int l = __ffs(pending) - 1;
             pending &= pending - 1u;
-            const int i = base + l, s = i % S;
-            if (i >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((i / S - 1) & 1), timeout_ns)) {
+            const int i = base + l, gi = g0 + i, s = gi % S;
+            if (gi >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((gi / S - 1) & 1), timeout_ns)) {
                 if (lane == 0) set_error(err, DERR_TIMEOUT_EMPTY);
                 ok = false;
                 break;
@@ -864,7 +865,8 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
     // drain: never leave a bulk copy in flight when the CTA exits
     const int first = issued > S ? issued - S : 0;
     for (int i = first; i < issued; ++i) {
-        if (!mbar_wait_sleep(&full[i % S], static_cast<uint32_t>((i / S) & 1), drain_limit_ns(timeout_ns))) {
+        const int gi = g0 + i;
+        if (!mbar_wait_sleep(&full[gi % S], static_cast<uint32_t>((gi / S) & 1), drain_limit_ns(timeout_ns))) {
             if (lane == 0) set_error(err, DERR_DRAIN);
             break;
         }

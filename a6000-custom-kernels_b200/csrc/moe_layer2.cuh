@@ -155,6 +155,7 @@ struct Layer2Ctrl {
     uint32_t uw[LAYER_MAX_ENTRIES + 2];  // prefix of unit weights (members)
     int32_t gid[LAYER_MAX_ENTRIES];      // routed experts (global ids; C.x holds local ones)
     uint32_t tag, xep;                   // launch tag; expert-parallel exchange epoch
+    uint32_t halt;                       // persistent stack kernel: stop at this layer (a wait ran out)
 };
 
 // This CTA's place in the unit partition. Unit u (of nu) gets CTAs

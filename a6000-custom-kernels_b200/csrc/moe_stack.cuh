@@ -1,0 +1,349 @@
+// moe_stack.cuh -- batch-1 MoE layers back to back in ONE persistent launch.
+//
+// The per-expert-group layer kernel (moe_layer2.cuh) spends most of a launch
+// waiting on instruction fetch: each code region runs once per launch and
+// starts cold (ncu: instruction-cache hit rate 50 %, top stall
+// no_instruction). This kernel runs the same per-layer work for a list of
+// layers in one cooperative launch, so from the second layer on the code is
+// warm, there is no launch gap, and the shared expert's CTAs stream the next
+// layer's weights while the current layer finishes.
+//
+// Per layer l (one token): the same static plan as moe_layer2_kernel at batch
+// 1 (unit u = pick u, the shared expert = unit k, CTA groups fixed), the same
+// rank selection, tiles, h exchange by (value, tag) pairs (tag = launch epoch
+// + 1 + l), down rows and combine by the CTA that completes a 64-row block.
+// The combining CTA writes out_l (and x_next_l = x_l + out_l when asked) and
+// counts the block done; every CTA waits until all of layer l's blocks are
+// done before it reads layer l + 1's input -- the layers may form a chain.
+// The ring carries on across layers: tile i of layer l has ring index
+// l * (tiles per layer) + i, consumed by warp (ring index) % nw. All waits are
+// bounded. Results equal moe_b200_layer_decode per layer bit for bit.
+#pragma once
+#include "moe_layer2.cuh"
+
+namespace moe {
+
+// One layer of the stack (device memory, read by every CTA).
+struct StackLayer {
+    const char *up, *gate, *down;           // expert 0 of each expert tensor (HBM)
+    const char *sh_up, *sh_gate, *sh_down;  // the shared expert (null when none)
+    const float *x, *logits;                // the token's input [H] and router logits [E]
+    float *out, *x_next;                    // output [H]; x_next = x + out when not null
+    int32_t *ids_out;                       // [k] picks (may be null)
+    float *w_out;                           // [k] gating weights (may be null)
+};
+
+struct StackArgs {
+    GemvArgs gu, dn;                        // geometry; h, hs, y, ys in the workspace
+    const StackLayer *layers;
+    int32_t n_layers, k, n_experts, norm_w;
+    uint64_t eb_up, eb_gate, eb_down;       // bytes of one expert of each tensor
+    int32_t tma, has_shared;                // every source 16-byte aligned (bulk copies)
+    uint64_t *h_tag, *hs_tag;
+    uint32_t *gbar;                         // [0] epoch, [1] finished CTAs, [2] output blocks done
+    uint32_t *rowcnt;                       // [n_rb] rows arrived per 64-row block (zero between layers)
+    int32_t n_rb;
+    int32_t n_stages, n_tile_warps;
+    uint32_t stage_bytes, ctrl_bytes, act_bytes;
+    int *err;
+    uint64_t timeout_ns;
+};
+
+// load_tagged_block for data this GPU's CTAs exchange (GPU scope)
+template <bool KQ>
+__device__ __forceinline__ bool load_tagged_block_gpu(const uint64_t *xb, uint32_t tag, int lane,
+                                                      float (&v)[KQ ? 8 : 1]) {
+    constexpr int NV = KQ ? 8 : 1;
+    uint64_t w[NV];
+    if constexpr (KQ) {
+        ld_relaxed_u64x2(xb + 4 * lane, w[0], w[1]);
+        ld_relaxed_u64x2(xb + 4 * lane + 2, w[2], w[3]);
+        ld_relaxed_u64x2(xb + 128 + 4 * lane, w[4], w[5]);
+        ld_relaxed_u64x2(xb + 128 + 4 * lane + 2, w[6], w[7]);
+    } else {
+        uint64_t other;
+        ld_relaxed_u64x2(xb + (lane & ~1), w[0], other);
+        if (lane & 1) w[0] = other;
+    }
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        ok &= static_cast<uint32_t>(w[j] >> 32) == tag;
+        v[j] = __uint_as_float(static_cast<uint32_t>(w[j]));
+    }
+    return ok;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int TA, int TB>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid_constant__ StackArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + GEMV_MAX_STAGES;
+    Layer2Ctrl &LC = *reinterpret_cast<Layer2Ctrl *>(smem + 2 * GEMV_MAX_STAGES * 8);
+    GemvCtrl &C = LC.g;
+    uint8_t *act_area = smem + a.ctrl_bytes;
+    uint8_t *stage_area = act_area + a.act_bytes;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = a.n_stages, k = a.k, E = a.n_experts, L = a.n_layers;
+    const int H = a.dn.nrows, F = a.gu.nrows, KA = a.gu.K, KB = a.dn.K;
+    const int hs = a.has_shared ? 1 : 0;
+    const int G = gridDim.x, bid = blockIdx.x;
+    const int rpt = a.gu.rows_per_tile, rows_b = a.dn.rows_per_tile;
+    const int nw = a.n_tile_warps;
+    constexpr int PW = GEMV_CONSUMER_WARPS;            // the producer warp
+    const UnitPlan P = unit_plan(k + hs, nullptr, G, bid, F, H, rpt, rows_b);
+    const bool shared_cta = hs && P.u == k;            // streams without routing
+    const int per_layer = P.nA + P.nB;
+    const uint8_t kind = a.tma ? 0 : 2;
+
+    // tile i of layer Lr (phase A: up + gate rows, then phase B: down rows)
+    auto describe = [&](const StackLayer &Lr, int i, TileSrc &ts) {
+        if (i < P.nA) {
+            ts.row0[0] = ts.row0[1] = P.a0 + i * rpt;
+            ts.nr[0] = ts.nr[1] = min(rpt, P.a1 - ts.row0[0]);
+            ts.src[0] = shared_cta ? Lr.sh_up : C.usrc[P.u][0];
+            ts.src[1] = shared_cta ? Lr.sh_gate : C.usrc[P.u][1];
+            ts.kind[0] = ts.kind[1] = kind;
+            ts.n_parts = 2;
+            ts.rb = a.gu.row_bytes;
+            ts.part_bytes = a.gu.part_bytes;
+        } else {
+            const int j = i - P.nA;
+            ts.row0[0] = ts.row0[1] = P.b0 + j * rows_b;
+            ts.nr[0] = ts.nr[1] = min(rows_b, P.b1 - ts.row0[0]);
+            ts.src[0] = ts.src[1] = shared_cta ? Lr.sh_down : LC.dsrc[P.u];
+            ts.kind[0] = ts.kind[1] = kind;
+            ts.n_parts = 1;
+            ts.rb = a.dn.row_bytes;
+            ts.part_bytes = a.stage_bytes;
+        }
+    };
+
+    if (warp == PW) {
+        // ============================ producer warp ===========================
+        for (int s = lane; s < S; s += 32) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+        __syncwarp();
+        asm volatile("bar.arrive 3, %0;" ::"r"(GEMV_THREADS) : "memory");
+        for (int l = 0; l < L; ++l) {
+            const StackLayer &Lr = a.layers[l];
+            // routed CTAs: warp PW - 1 hands over layer l's sources (named
+            // barrier 4); the shared expert's CTAs go ahead, ring permitting
+            if (!shared_cta) asm volatile("bar.sync 4, 64;" ::: "memory");
+            if ((!shared_cta && C.fail) || ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err))) break;
+            produce_tiles(per_layer, S, full, empty, stage_area, a.stage_bytes,
+                          [&](int i, TileSrc &ts) { describe(Lr, i, ts); }, a.timeout_ns, a.err, lane, l * per_layer);
+        }
+        return;
+    }
+    // ============================ consumer warps =============================
+    asm volatile("bar.sync 3, %0;" ::"r"(GEMV_THREADS) : "memory");   // the ring is initialised
+    const uint32_t epoch0 = ld_relaxed_u32(&a.gbar[0]);
+    // the groups are fixed: pick u = unit u, one member (entry u, token 0)
+    if (tid < k) {
+        C.first[tid] = static_cast<int16_t>(tid);
+        C.uidx[tid] = static_cast<int16_t>(tid);
+        C.gmem[tid] = static_cast<int16_t>(tid);
+        C.goff[tid] = static_cast<int16_t>(tid);
+        C.eslot[tid] = 0;
+    }
+    if (tid == 0) {
+        C.n_unique = k;
+        C.goff[k] = static_cast<int16_t>(k);
+        C.shslot[0] = 0;
+        C.fail = 0;
+    }
+    const bool ranked = E <= 32 * PW && k <= 8;
+    constexpr int QA = is_kquant(TA) ? 256 : 32;
+    const int nbx = KA / QA;
+    const int nA = P.nA, nB = P.nB;
+    for (int l = 0; l < L; ++l) {
+        const StackLayer &Lr = a.layers[l];
+        const uint32_t tag = epoch0 + 1u + static_cast<uint32_t>(l);
+        const int g0 = l * per_layer;
+        // ---- layer l - 1's output complete (its input may be this layer's x)
+        if (l > 0) {
+            if (tid == 0) {
+                const uint32_t target = static_cast<uint32_t>(l) * static_cast<uint32_t>(a.n_rb);
+                const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
+                while (ld_acquire_gpu(&a.gbar[2]) < target) {
+                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                        set_error(a.err, DERR_TIMEOUT_TAG);
+                        break;
+                    }
+                }
+                // one decision for the whole CTA: stop once any wait anywhere ran out
+                LC.halt = ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err)) != 0u;
+            }
+            consumer_sync();
+            if (LC.halt) {
+                // release the producer if it waits for this layer's sources; it
+                // then sees the error word and stops too
+                if (!shared_cta && warp == PW - 1) asm volatile("bar.arrive 4, 64;" ::: "memory");
+                break;
+            }
+        }
+        // ---- routing (routed CTAs), x --------------------------------------
+        if (!shared_cta) {
+            if (ranked) rank_slice(Lr.logits, E, k, warp, lane, LC.cand_key, LC.cand_id);
+            consumer_sync();
+            if (ranked) {
+                rank_candidates(LC.cand_key, LC.cand_id, PW * k, k, tid, C.x);
+                consumer_sync();
+            }
+            if (warp == PW - 1) {
+                if (!ranked) {
+                    route_select(Lr.logits, E, k, lane, C.x);
+                    __syncwarp();
+                }
+                bool bad = false;
+                if (lane < k) {
+                    const int x = C.x[lane];
+                    LC.gid[lane] = x;
+                    bad = x < 0 || x >= E;
+                    if (!bad) {
+                        C.usrc[lane][0] = Lr.up + static_cast<uint64_t>(x) * a.eb_up;
+                        C.usrc[lane][1] = Lr.gate + static_cast<uint64_t>(x) * a.eb_gate;
+                        LC.dsrc[lane] = Lr.down + static_cast<uint64_t>(x) * a.eb_down;
+                    }
+                    if (Lr.ids_out && bid == 0) Lr.ids_out[lane] = x;
+                }
+                bad = __any_sync(0xffffffffu, bad);
+                if (lane == 0 && bad) {
+                    C.fail = 1;
+                    set_error(a.err, DERR_BAD_ID);
+                }
+                __syncwarp();
+                asm volatile("bar.arrive 4, 64;" ::: "memory");
+            }
+        }
+        if (warp < PW - 1)
+            for (int b = warp; b < nbx; b += PW - 1)
+                stage_f32_block<TA, true>(Lr.x, act_area, KA, b, lane);   // through L2: x may be a fresh x_next
+        consumer_sync();
+        const bool run = !C.fail;
+        if (!run) break;
+        // ---- gating weights (warp PW - 1; the shared CTAs route here, off
+        //      their critical path) -----------------------------------------
+        if (warp == PW - 1) {
+            if (shared_cta) {
+                route_select(Lr.logits, E, k, lane, LC.gid);
+                __syncwarp();
+            }
+            route_weights(Lr.logits, E, k, a.norm_w, lane, LC.gid, LC.wt);
+            __syncwarp();
+            if (bid == 0 && Lr.w_out && lane < k) Lr.w_out[lane] = LC.wt[lane];
+        }
+        // ---- phase A: gate/up + GLU -> h, tagged copies -----------------------
+        for (int i = 0; i < nA; ++i) {
+            const int gi = g0 + i;
+            if (gi % nw != warp) continue;
+            const int s = gi % S;
+            if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((gi / S) & 1), a.timeout_ns)) {
+                if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+                break;
+            }
+            const int row0 = P.a0 + i * rpt, nr = min(rpt, P.a1 - row0);
+            const char *s0 = shared_cta ? Lr.sh_up : C.usrc[P.u][0];
+            const char *s1 = shared_cta ? Lr.sh_gate : C.usrc[P.u][1];
+            const uint8_t *stage = stage_area + static_cast<size_t>(s) * a.stage_bytes;
+            const uint64_t off = static_cast<uint64_t>(row0) * a.gu.row_bytes;
+            const uint8_t *up_rows = stage + ((reinterpret_cast<uintptr_t>(s0) + off) & 15u);
+            const uint8_t *gate_rows = stage + a.gu.part_bytes + ((reinterpret_cast<uintptr_t>(s1) + off) & 15u);
+            consume_tile<TA, ACT_CPU, 1, 2>(a.gu, C, up_rows, gate_rows, nr, P.u, k, row0, act_area, lane, a.h_tag,
+                                            a.hs_tag, tag);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        consumer_sync();
+        // ---- the unit's h from the CTAs of its group, quantized for down ----
+        {
+            constexpr bool KQ = is_kquant(TB);
+            constexpr int QB = KQ ? 256 : 32;
+            const int nb = KB / QB;
+            const uint64_t *base = shared_cta ? a.hs_tag : a.h_tag + static_cast<int64_t>(P.u) * a.dn.stride_channel_y;
+            const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
+            for (int b = warp; b < nb; b += PW) {
+                float v[KQ ? 8 : 1];
+                while (!__all_sync(0xffffffffu, load_tagged_block_gpu<KQ>(base + b * QB, tag, lane, v))) {
+                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                        if (lane == 0) set_error(a.err, DERR_TIMEOUT_TAG);
+                        break;
+                    }
+                }
+                int8_t *q = reinterpret_cast<int8_t *>(act_area);
+                int16_t *bs = reinterpret_cast<int16_t *>(act_area + KB);
+                float *sc = reinterpret_cast<float *>(act_area + KB + KB / 8);
+                if constexpr (KQ) quant_q8K_vals<TB>(v, q, bs, sc, b, lane, KB / chunk_of<TB>::CE);
+                else quant_q80_val<TB>(v[0], q, bs, sc, b, lane, KB / chunk_of<TB>::CE);
+            }
+        }
+        consumer_sync();
+        // ---- phase B: down rows -> y / ys -------------------------------------
+        for (int i = nA; i < nA + nB; ++i) {
+            const int gi = g0 + i;
+            if (gi % nw != warp) continue;
+            const int s = gi % S;
+            if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((gi / S) & 1), a.timeout_ns)) {
+                if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+                break;
+            }
+            const int row0 = P.b0 + (i - nA) * rows_b, nr = min(rows_b, P.b1 - row0);
+            const char *s0 = shared_cta ? Lr.sh_down : LC.dsrc[P.u];
+            const uint8_t *rows = stage_area + static_cast<size_t>(s) * a.stage_bytes +
+                                  ((reinterpret_cast<uintptr_t>(s0) + static_cast<uint64_t>(row0) * a.dn.row_bytes) & 15u);
+            consume_tile<TB, ACT_CPU, 1, 1, 32>(a.dn, C, rows, rows, nr, P.u, k, row0, act_area, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        consumer_sync();          // the CTA's y stores, ordered before each warp's release below
+        // ---- arrivals per 64-row block; the CTA completing one sums it, writes
+        //      out (and x + out), and counts the block done ----------------------
+        if (P.b1 > P.b0) {
+            const int RB = LAYER2_RB;
+            const int rb0 = P.b0 / RB, nblk = (P.b1 - 1) / RB - rb0 + 1;
+            for (int b = rb0 + warp; b < rb0 + nblk; b += PW) {
+                const int lo = b * RB, hi = min(H, lo + RB);
+                const uint32_t mine = static_cast<uint32_t>(min(P.b1, hi) - max(P.b0, lo));
+                uint32_t old = 0;
+                if (lane == 0) old = atom_add_acq_rel_gpu(&a.rowcnt[b], mine);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old + mine != static_cast<uint32_t>(hi - lo) * static_cast<uint32_t>(k + hs)) continue;
+                __syncwarp();
+                for (int r = lo + lane; r < hi; r += 32) {
+                    float acc = 0.f;
+                    for (int p = 0; p < k; ++p) {
+                        const float v = __fmul_rn(__ldcg(a.dn.dst + static_cast<int64_t>(p) * a.dn.stride_channel_dst + r),
+                                                  LC.wt[p]);
+                        acc = p == 0 ? v : __fadd_rn(acc, v);
+                    }
+                    if (hs) acc = __fadd_rn(acc, __ldcg(a.dn.shared_dst + r));
+                    Lr.out[r] = acc;
+                    if (Lr.x_next) Lr.x_next[r] = __fadd_rn(__ldcg(Lr.x + r), acc);
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    atomicExch(&a.rowcnt[b], 0u);
+                    red_release_gpu_add(&a.gbar[2], 1u);
+                }
+            }
+        }
+    }
+    // ---- the last CTA to finish advances the epoch past every layer's tag and
+    //      clears the layer counter ---------------------------------------------
+    if (tid == 0 && atomicAdd(&a.gbar[1], 1u) == gridDim.x - 1) {
+        atomicExch(&a.gbar[1], 0u);
+        atomicExch(&a.gbar[2], 0u);
+        atomicAdd(&a.gbar[0], static_cast<uint32_t>(L));
+    }
+}
+
+}  // namespace moe

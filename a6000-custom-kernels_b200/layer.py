@@ -154,3 +154,30 @@ class MoELayer:
         """(ids, weights) views of the last decode's routing in the workspace."""
         ids, w = self.intermediates(n_tok)[:2]
         return ids, w
+
+
+class Stack:
+    """Batch-1 layers decoded back to back in one persistent launch
+    (moe_b200_stack_prepare / moe_b200_stack_run). Layer l reads xs[l] and
+    logits[l] (device f32 [1, H] / [1, E]), writes outs[l] and, with
+    x_nexts, x_nexts[l] = xs[l] + outs[l] (a residual chain when xs[l + 1]
+    is x_nexts[l]). run() may be repeated; every tensor must stay alive."""
+
+    def __init__(self, layers, xs, logits, outs, x_nexts=None, stream=None):
+        n = len(layers)
+        self.layers, self.n = layers, n
+        self.desc0 = layers[0].desc
+        arr = (MoeLayerDesc * n)(*[L.desc for L in layers])
+        nbytes = lib().moe_b200_stack_workspace_size(ctypes.byref(self.desc0), n)
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=layers[0].device)
+
+        def ptrs(ts):
+            return (ctypes.c_void_p * n)(*[_ptr(t) for t in ts])
+        check(lib().moe_b200_stack_prepare(arr, n, ptrs(xs), ptrs(logits), ptrs(outs),
+                                           ptrs(x_nexts) if x_nexts is not None else None, _ptr(self.ws),
+                                           self.ws.numel(), _stream(stream)))
+
+    def run(self, stream=None):
+        check(lib().moe_b200_stack_run(ctypes.byref(self.desc0), self.n, _ptr(self.ws), self.ws.numel(),
+                                       _stream(stream)))
+

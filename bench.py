@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="config 4 dispatch/combine: peer-memory kernels (default) or NCCL all-to-all")
     ap.add_argument("--batch", type=int, default=1, help="decode tokens per step (configs 3 and 5)")
+    ap.add_argument("--launch", choices=["stack", "layer"], default="stack",
+                    help="config 2 on one GPU: 512 steps per persistent launch (stack) or one launch per step "
+                         "replayed from CUDA graphs (layer)")
     return ap.parse_args()
 
 
@@ -251,9 +254,28 @@ def run_mine(args):
                 step(start + j)
         return g
 
-    full = graph_for(G, 0) if K >= G else None
-    rem = graph_for(K % G, 0) if K % G else None
-    # warm the graphs (W warm-up steps already ran eagerly)
+    use_stack = args.launch == "stack"
+    if use_stack:
+        # G steps per persistent launch: the layer list repeats every G steps
+        # (G is a multiple of the 32 layer copies and of the 64 tokens)
+        def stack_for(n):
+            return pkg.Stack([layers[j % R] for j in range(n)], [xs[j % P] for j in range(n)],
+                             [lgs[j % P] for j in range(n)], [outs[j % P] for j in range(n)], stream=stream)
+        st_full = stack_for(G) if K >= G else None
+        st_rem = stack_for(K % G) if K % G else None
+
+        class _Run:
+            def __init__(self, st):
+                self.st = st
+
+            def replay(self):
+                self.st.run(stream)
+        full = _Run(st_full) if st_full is not None else None
+        rem = _Run(st_rem) if st_rem is not None else None
+    else:
+        full = graph_for(G, 0) if K >= G else None
+        rem = graph_for(K % G, 0) if K % G else None
+    # warm the graphs / stacks (W warm-up steps already ran eagerly)
     with torch.cuda.stream(stream):
         if full is not None:
             full.replay()
@@ -314,7 +336,13 @@ def run_mine(args):
     peak_src = "of measured" if peak else "of fallback"
     peak = peak or 6650.0
     fused = layers[0].fused(1)
-    if fused:
+    if use_stack:
+        k_us = 1e3 * ms / K
+        k_bytes = STEP_BYTES
+        k_name = "moe_stack_kernel<Q2_K,Q2_K>: 512 layer steps per persistent launch (route, gate/up+SwiGLU+shared, down, combine per step)"
+        k_how = f"timed region: {K} steps in {-(-K // G)} persistent launches, per-step time"
+        tfile = "stack_kernel_traffic.json"
+    elif fused:
         # one launch per step: the timed region's per-step time is the layer
         # kernel's launch-to-launch time (an upper bound of its duration)
         k_us = 1e3 * ms / K
@@ -354,7 +382,7 @@ def run_mine(args):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "layers_cycled": R, "l2": f"inputs larger than L2: {R} layer copies "
                                                  f"({R * 3 * E * EXPERT_BYTES / 1e9:.1f} GB) cycled",
-                       "graph": "CUDA graphs of 512-step chunks"},
+                       "graph": ("persistent launches of 512 steps" if use_stack else "CUDA graphs of 512-step chunks")},
             "layer_gbs": round(STEP_BYTES * value / world / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -369,7 +397,7 @@ def run_mine(args):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"]},
-            "gpu_launches": (1 if fused else 4) * K,
+            "gpu_launches": -(-K // G) if use_stack else (1 if fused else 4) * K,
             "clocks": ck,
         }
         print(json.dumps(line), flush=True)

@@ -343,6 +343,33 @@ int moe_b200_ep_experts_rows(const moe_layer_desc *layer, const float *x, const 
 int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap, const int32_t *ids,
                        const int32_t *src, const float *y, int64_t H, void *scratch, moe_stream_t stream);
 
+/* No counterpart in the reference: n_layers batch-1 layers in ONE persistent
+ * launch (moe_stack_kernel). Layer l reads its token from x[l] and its router
+ * logits from logits[l], writes its output to out[l] and, when x_next (may be
+ * NULL) has a non-null entry, x_next[l] = x[l] + out[l] -- so x[l + 1] may be
+ * x_next[l] and the layers form a residual chain: every layer starts only
+ * after the previous layer's output is complete. Each layer computes what
+ * moe_b200_layer_decode computes for one token (same bits). One launch keeps
+ * the code warm in the instruction caches across layers, has no launch gaps,
+ * and lets the shared expert's weights of the next layer stream early.
+ * Requirements: gate, up and down of one type (Q2_K..Q6_K, Q4_0, Q5_0, Q8_0,
+ * Q5_K), every layer with layer 0's shapes, types, GLU and shared-expert
+ * presence, expert tensors contiguous and 16-byte aligned in device memory
+ * (no host-tiered tensors, no cache bookkeeping). x, logits, out, x_next are
+ * host arrays of n_layers device pointers.
+ * moe_b200_stack_prepare writes the layer list into the workspace (an
+ * asynchronous copy on `stream` from host memory: not during stream
+ * capture); moe_b200_stack_run launches (capturable) and may be repeated for
+ * the same list. Workspace:
+ * moe_b200_stack_workspace_size(layer 0, n_layers) bytes, zero-filled once
+ * (its start is a layer-decode workspace for one token). */
+size_t moe_b200_stack_workspace_size(const moe_layer_desc *layer0, int64_t n_layers);
+int moe_b200_stack_prepare(const moe_layer_desc *layers, int64_t n_layers, const float *const *x,
+                           const float *const *logits, float *const *out, float *const *x_next, void *workspace,
+                           size_t workspace_bytes, moe_stream_t stream);
+int moe_b200_stack_run(const moe_layer_desc *layer0, int64_t n_layers, void *workspace, size_t workspace_bytes,
+                       moe_stream_t stream);
+
 /* No counterpart in the reference (the reference runs on one GPU): one MoE
  * layer decode with the experts sharded over `world` GPUs of one node and the
  * exchange fused into the per-expert-group layer kernel, one launch per GPU
