@@ -739,18 +739,34 @@ struct TileSrc {
     uint32_t rb, part_bytes;
 };
 
+// Waits until the copies of ring indexes [max(lo, end - S), end) have landed
+// (the last S the producer issued): no bulk copy is then in flight.
+__device__ __forceinline__ void drain_tiles(int end, int S, uint64_t *full, uint64_t timeout_ns, int *err, int lane,
+                                            int lo = 0) {
+    const int first = end - S > lo ? end - S : lo;
+    for (int gi = first; gi < end; ++gi) {
+        if (!mbar_wait_sleep(&full[gi % S], static_cast<uint32_t>((gi / S) & 1), drain_limit_ns(timeout_ns))) {
+            if (lane == 0) set_error(err, DERR_DRAIN);
+            break;
+        }
+    }
+}
+
 // The producer warp: streams tiles 0..n_tiles-1 through the S-stage ring
 // (tile i -> ring index g = g0 + i -> stage g % S, phase g / S; g0 > 0 when
 // the ring carries on from earlier tiles of a persistent kernel). Tiles are issued in rounds
 // of up to min(32, S): within a round no tile reuses a stage of the same
 // round, so every lane waits for its own stage and issues its own bulk copies.
 // Tiles that need plain copies (host memory or unaligned sources) follow,
-// one at a time, copied by the whole warp. Ends after every issued copy has
-// landed, so no bulk copy is in flight when the CTA exits.
+// one at a time, copied by the whole warp. With drain set, ends after every
+// issued copy has landed, so no bulk copy is in flight when the CTA exits (a
+// caller that streams on passes drain = false and calls drain_tiles once at
+// the end). Returns the number of tiles issued (n_tiles unless a wait ran out).
 template <class Describe>
-__device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full, uint64_t *empty,
-                                              uint8_t *stage_area, uint32_t stage_bytes, Describe describe,
-                                              uint64_t timeout_ns, int *err, int lane, int g0 = 0) {
+__device__ __forceinline__ int produce_tiles(int n_tiles, int S, uint64_t *full, uint64_t *empty,
+                                             uint8_t *stage_area, uint32_t stage_bytes, Describe describe,
+                                             uint64_t timeout_ns, int *err, int lane, int g0 = 0,
+                                             bool drain = true) {
     const uint64_t pol = l2_evict_first_policy();
     const int R = S < 32 ? S : 32;
     int issued = 0;
@@ -862,15 +878,8 @@ __device__ __forceinline__ void produce_tiles(int n_tiles, int S, uint64_t *full
         }
         issued = base + cnt;
     }
-    // drain: never leave a bulk copy in flight when the CTA exits
-    const int first = issued > S ? issued - S : 0;
-    for (int i = first; i < issued; ++i) {
-        const int gi = g0 + i;
-        if (!mbar_wait_sleep(&full[gi % S], static_cast<uint32_t>((gi / S) & 1), drain_limit_ns(timeout_ns))) {
-            if (lane == 0) set_error(err, DERR_DRAIN);
-            break;
-        }
-    }
+    if (drain) drain_tiles(g0 + issued, S, full, timeout_ns, err, lane, g0);
+    return issued;
 }
 
 // This CTA's contiguous share of the row space of n_groups groups of nrows

@@ -11,6 +11,8 @@ namespace moe {
 
 namespace {
 
+constexpr int kStackSmemLimit = 227 * 1024;
+
 template <int T>
 cudaError_t launch_stack_t(const StackArgs &a, int grid, size_t smem, cudaStream_t st) {
     auto kern = moe_stack_kernel<T, T>;
@@ -63,15 +65,29 @@ int launch_stack(int type, StackArgs &a, cudaStream_t st, const char **why, cuda
     size_t smem = 0;
     const int rc = plan_layer2(type, type, p, &grid, &smem, why);
     if (rc) return rc;
+    if (a.k > STACK_MAX_K) { *why = "the stack kernel handles k <= 32"; return -2; }
     a.gu = p.gu;
     a.dn = p.dn;
     a.n_rb = p.n_rb;
-    a.n_stages = p.n_stages;
-    a.n_tile_warps = p.n_tile_warps;
     a.stage_bytes = p.stage_bytes;
-    a.ctrl_bytes = p.ctrl_bytes;
     a.act_bytes = p.act_bytes;
     a.timeout_ns = p.timeout_ns;
+    // the routing buffers follow the layer kernel's control block; the ring
+    // takes what is left. Every consumer warp takes tiles (the per-layer tile
+    // counts are sized for 16 warps), and the ring should hold one layer of
+    // this CTA's share so the next layer streams in behind the current one.
+    a.route_off = p.ctrl_bytes;
+    a.ctrl_bytes = (p.ctrl_bytes + static_cast<uint32_t>(sizeof(StackShared)) + 127u) & ~127u;
+    const int64_t avail = kStackSmemLimit - static_cast<int64_t>(a.ctrl_bytes) - a.act_bytes;
+    int fit = avail > 0 ? static_cast<int>(avail / a.stage_bytes) : 0;
+    if (fit > GEMV_MAX_STAGES) fit = GEMV_MAX_STAGES;
+    if (fit < 2) { *why = "activations and tiles do not fit in shared memory"; return -2; }
+    const int nw = fit < GEMV_CONSUMER_WARPS ? fit : GEMV_CONSUMER_WARPS;
+    a.n_tile_warps = nw;
+    a.n_stages = fit / nw * nw;
+    a.gu.n_tile_warps = nw;
+    a.dn.n_tile_warps = nw;
+    smem = static_cast<size_t>(a.ctrl_bytes) + a.act_bytes + static_cast<size_t>(a.n_stages) * a.stage_bytes;
     cudaError_t e = cudaErrorInvalidValue;
     switch (type) {
         case T_Q2_K: e = launch_stack_t<T_Q2_K>(a, grid, smem, st); break;

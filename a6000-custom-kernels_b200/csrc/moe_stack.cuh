@@ -1,23 +1,31 @@
 // moe_stack.cuh -- batch-1 MoE layers back to back in ONE persistent launch.
 //
-// The per-expert-group layer kernel (moe_layer2.cuh) spends most of a launch
-// waiting on instruction fetch: each code region runs once per launch and
-// starts cold (ncu: instruction-cache hit rate 50 %, top stall
-// no_instruction). This kernel runs the same per-layer work for a list of
-// layers in one cooperative launch, so from the second layer on the code is
-// warm, there is no launch gap, and the shared expert's CTAs stream the next
-// layer's weights while the current layer finishes.
+// Each layer of a decode step has the same shape, and a layer's router logits
+// are an input of the launch, so which experts a layer reads is known before
+// the layer before it has finished. This kernel uses that: the producer warp
+// of every CTA routes layer l + 1 itself and streams its tiles into the ring
+// while the consumers still work on layer l. When a layer's input arrives,
+// its weights are already in shared memory (the ring holds about one layer of
+// a CTA's share), and what is left on the critical path per layer is the
+// arithmetic and two exchanges between CTAs: the h rows of each expert and
+// the 64-row output blocks. One launch for many layers also keeps the code
+// warm in the instruction cache and removes the launch gaps.
 //
 // Per layer l (one token): the same static plan as moe_layer2_kernel at batch
 // 1 (unit u = pick u, the shared expert = unit k, CTA groups fixed), the same
-// rank selection, tiles, h exchange by (value, tag) pairs (tag = launch epoch
+// picks and weights (route_select / route_weights: descending logit, ties to
+// the lower id), tiles, h exchange by (value, tag) pairs (tag = launch epoch
 // + 1 + l), down rows and combine by the CTA that completes a 64-row block.
 // The combining CTA writes out_l (and x_next_l = x_l + out_l when asked) and
 // counts the block done; every CTA waits until all of layer l's blocks are
 // done before it reads layer l + 1's input -- the layers may form a chain.
-// The ring carries on across layers: tile i of layer l has ring index
-// l * (tiles per layer) + i, consumed by warp (ring index) % nw. All waits are
-// bounded. Results equal moe_b200_layer_decode per layer bit for bit.
+//
+// Ring: tile i of layer l has ring index l * (tiles per layer) + i and is
+// consumed by warp (ring index) % nw. Routing: the producer writes layer j's
+// picks, weights and expert sources into buffer j % 3 and arrives on
+// rt_full[j % 3]; the consumers release the buffer (rt_empty) when layer j is
+// done, so the producer runs at most two layers ahead. All waits are bounded.
+// Results equal moe_b200_layer_decode per layer bit for bit.
 #pragma once
 #include "moe_layer2.cuh"
 
@@ -33,6 +41,24 @@ struct StackLayer {
     float *w_out;                           // [k] gating weights (may be null)
 };
 
+constexpr int STACK_MAX_K = 32;
+constexpr int STACK_ROUTE_BUFS = 3;
+
+// One layer's routing, written by the producer warp, read by the consumers.
+struct StackRoute {
+    const char *usrc[STACK_MAX_K][2];       // up, gate rows of pick q
+    const char *dsrc[STACK_MAX_K];          // down rows of pick q
+    int32_t gid[STACK_MAX_K];
+    float wt[STACK_MAX_K];
+    int32_t bad;                            // a pick outside [0, n_experts)
+};
+
+// Shared memory the stack kernel adds after the layer kernel's control block.
+struct StackShared {
+    uint64_t rt_full[STACK_ROUTE_BUFS], rt_empty[STACK_ROUTE_BUFS];
+    StackRoute r[STACK_ROUTE_BUFS];
+};
+
 struct StackArgs {
     GemvArgs gu, dn;                        // geometry; h, hs, y, ys in the workspace
     const StackLayer *layers;
@@ -45,6 +71,7 @@ struct StackArgs {
     int32_t n_rb;
     int32_t n_stages, n_tile_warps;
     uint32_t stage_bytes, ctrl_bytes, act_bytes;
+    uint32_t route_off;                     // byte offset of StackShared in shared memory
     int *err;
     uint64_t timeout_ns;
 };
@@ -85,6 +112,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
     uint64_t *empty = full + GEMV_MAX_STAGES;
     Layer2Ctrl &LC = *reinterpret_cast<Layer2Ctrl *>(smem + 2 * GEMV_MAX_STAGES * 8);
     GemvCtrl &C = LC.g;
+    StackShared &SS = *reinterpret_cast<StackShared *>(smem + a.route_off);
     uint8_t *act_area = smem + a.ctrl_bytes;
     uint8_t *stage_area = act_area + a.act_bytes;
 
@@ -97,32 +125,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
     const int nw = a.n_tile_warps;
     constexpr int PW = GEMV_CONSUMER_WARPS;            // the producer warp
     const UnitPlan P = unit_plan(k + hs, nullptr, G, bid, F, H, rpt, rows_b);
-    const bool shared_cta = hs && P.u == k;            // streams without routing
+    const bool shared_cta = hs && P.u == k;            // the shared expert's rows
     const int per_layer = P.nA + P.nB;
     const uint8_t kind = a.tma ? 0 : 2;
-
-    // tile i of layer Lr (phase A: up + gate rows, then phase B: down rows)
-    auto describe = [&](const StackLayer &Lr, int i, TileSrc &ts) {
-        if (i < P.nA) {
-            ts.row0[0] = ts.row0[1] = P.a0 + i * rpt;
-            ts.nr[0] = ts.nr[1] = min(rpt, P.a1 - ts.row0[0]);
-            ts.src[0] = shared_cta ? Lr.sh_up : C.usrc[P.u][0];
-            ts.src[1] = shared_cta ? Lr.sh_gate : C.usrc[P.u][1];
-            ts.kind[0] = ts.kind[1] = kind;
-            ts.n_parts = 2;
-            ts.rb = a.gu.row_bytes;
-            ts.part_bytes = a.gu.part_bytes;
-        } else {
-            const int j = i - P.nA;
-            ts.row0[0] = ts.row0[1] = P.b0 + j * rows_b;
-            ts.nr[0] = ts.nr[1] = min(rows_b, P.b1 - ts.row0[0]);
-            ts.src[0] = ts.src[1] = shared_cta ? Lr.sh_down : LC.dsrc[P.u];
-            ts.kind[0] = ts.kind[1] = kind;
-            ts.n_parts = 1;
-            ts.rb = a.dn.row_bytes;
-            ts.part_bytes = a.stage_bytes;
-        }
-    };
 
     if (warp == PW) {
         // ============================ producer warp ===========================
@@ -130,18 +135,88 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
+        if (lane < STACK_ROUTE_BUFS) {
+            mbar_init(&SS.rt_full[lane], 1);
+            mbar_init(&SS.rt_empty[lane], 1);
+        }
         fence_mbar_init();
         __syncwarp();
         asm volatile("bar.arrive 3, %0;" ::"r"(GEMV_THREADS) : "memory");
-        for (int l = 0; l < L; ++l) {
+
+        // layer j's picks, weights and sources into buffer j % 3 (false: stop)
+        auto route_layer = [&](int j) -> bool {
+            const int b = j % STACK_ROUTE_BUFS;
+            if (j >= STACK_ROUTE_BUFS &&
+                !mbar_wait_sleep(&SS.rt_empty[b], static_cast<uint32_t>((j / STACK_ROUTE_BUFS - 1) & 1), a.timeout_ns)) {
+                if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+                return false;
+            }
+            StackRoute &R = SS.r[b];
+            const StackLayer &Lr = a.layers[j];
+            route_select(Lr.logits, E, k, lane, R.gid);
+            __syncwarp();
+            const int x = lane < k ? R.gid[lane] : 0;
+            const bool bad = __any_sync(0xffffffffu, x < 0 || x >= E);
+            if (!bad) {
+                route_weights(Lr.logits, E, k, a.norm_w, lane, R.gid, R.wt);
+                if (lane < k) {
+                    R.usrc[lane][0] = Lr.up + static_cast<uint64_t>(x) * a.eb_up;
+                    R.usrc[lane][1] = Lr.gate + static_cast<uint64_t>(x) * a.eb_gate;
+                    R.dsrc[lane] = Lr.down + static_cast<uint64_t>(x) * a.eb_down;
+                    if (bid == 0 && Lr.ids_out) Lr.ids_out[lane] = x;
+                    if (bid == 0 && Lr.w_out) Lr.w_out[lane] = R.wt[lane];
+                }
+            }
+            if (lane == 0) R.bad = bad ? 1 : 0;   // reported by the consumers when they reach layer j
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&SS.rt_full[b]);   // release: buffer b holds layer j
+            return !bad;
+        };
+        // tile i of layer l (phase A: up + gate rows, then phase B: down rows)
+        auto describe = [&](int l, int i, TileSrc &ts) {
             const StackLayer &Lr = a.layers[l];
-            // routed CTAs: warp PW - 1 hands over layer l's sources (named
-            // barrier 4); the shared expert's CTAs go ahead, ring permitting
-            if (!shared_cta) asm volatile("bar.sync 4, 64;" ::: "memory");
-            if ((!shared_cta && C.fail) || ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err))) break;
-            produce_tiles(per_layer, S, full, empty, stage_area, a.stage_bytes,
-                          [&](int i, TileSrc &ts) { describe(Lr, i, ts); }, a.timeout_ns, a.err, lane, l * per_layer);
+            const StackRoute &R = SS.r[l % STACK_ROUTE_BUFS];
+            if (i < P.nA) {
+                ts.row0[0] = ts.row0[1] = P.a0 + i * rpt;
+                ts.nr[0] = ts.nr[1] = min(rpt, P.a1 - ts.row0[0]);
+                ts.src[0] = shared_cta ? Lr.sh_up : R.usrc[P.u][0];
+                ts.src[1] = shared_cta ? Lr.sh_gate : R.usrc[P.u][1];
+                ts.kind[0] = ts.kind[1] = kind;
+                ts.n_parts = 2;
+                ts.rb = a.gu.row_bytes;
+                ts.part_bytes = a.gu.part_bytes;
+            } else {
+                const int jb = i - P.nA;
+                ts.row0[0] = ts.row0[1] = P.b0 + jb * rows_b;
+                ts.nr[0] = ts.nr[1] = min(rows_b, P.b1 - ts.row0[0]);
+                ts.src[0] = ts.src[1] = shared_cta ? Lr.sh_down : R.dsrc[P.u];
+                ts.kind[0] = ts.kind[1] = kind;
+                ts.n_parts = 1;
+                ts.rb = a.dn.row_bytes;
+                ts.part_bytes = a.stage_bytes;
+            }
+        };
+        // stream: A(0) [route 1] B(0) A(1) [route 2] B(1) ... -- layer l + 1
+        // is routed while layer l's down tiles wait for free stages
+        int end = 0;   // ring indexes [0, end) issued
+        if (route_layer(0)) {
+            for (int l = 0; l < L; ++l) {
+                if (ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err))) break;
+                const int g0 = l * per_layer;
+                int n = produce_tiles(P.nA, S, full, empty, stage_area, a.stage_bytes,
+                                      [&](int i, TileSrc &ts) { describe(l, i, ts); }, a.timeout_ns, a.err, lane, g0,
+                                      false);
+                end = g0 + n;
+                if (n < P.nA) break;
+                const bool next = l + 1 < L ? route_layer(l + 1) : true;
+                n = produce_tiles(P.nB, S, full, empty, stage_area, a.stage_bytes,
+                                  [&](int i, TileSrc &ts) { describe(l, P.nA + i, ts); }, a.timeout_ns, a.err, lane,
+                                  g0 + P.nA, false);
+                end = g0 + P.nA + n;
+                if (n < P.nB || !next) break;
+            }
         }
+        drain_tiles(end, S, full, a.timeout_ns, a.err, lane);   // nothing in flight at exit
         return;
     }
     // ============================ consumer warps =============================
@@ -161,87 +236,47 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         C.shslot[0] = 0;
         C.fail = 0;
     }
-    const bool ranked = E <= 32 * PW && k <= 8;
     constexpr int QA = is_kquant(TA) ? 256 : 32;
     const int nbx = KA / QA;
     const int nA = P.nA, nB = P.nB;
     for (int l = 0; l < L; ++l) {
         const StackLayer &Lr = a.layers[l];
+        const int rb = l % STACK_ROUTE_BUFS;
+        const StackRoute &R = SS.r[rb];
+        const uint32_t rpar = static_cast<uint32_t>((l / STACK_ROUTE_BUFS) & 1);
         const uint32_t tag = epoch0 + 1u + static_cast<uint32_t>(l);
         const int g0 = l * per_layer;
-        // ---- layer l - 1's output complete (its input may be this layer's x)
-        if (l > 0) {
-            if (tid == 0) {
+        // ---- layer l - 1's output complete (its input may be this layer's x),
+        //      layer l routed ----------------------------------------------------
+        if (tid == 0) {
+            bool ok = true;
+            if (l > 0) {
                 const uint32_t target = static_cast<uint32_t>(l) * static_cast<uint32_t>(a.n_rb);
                 const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
                 while (ld_acquire_gpu(&a.gbar[2]) < target) {
                     if (static_cast<uint64_t>(clock64()) - t0 > lim) {
                         set_error(a.err, DERR_TIMEOUT_TAG);
+                        ok = false;
                         break;
                     }
                 }
-                // one decision for the whole CTA: stop once any wait anywhere ran out
-                LC.halt = ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err)) != 0u;
             }
-            consumer_sync();
-            if (LC.halt) {
-                // release the producer if it waits for this layer's sources; it
-                // then sees the error word and stops too
-                if (!shared_cta && warp == PW - 1) asm volatile("bar.arrive 4, 64;" ::: "memory");
-                break;
-            }
+            if (ok && !mbar_wait_sleep(&SS.rt_full[rb], rpar, a.timeout_ns)) set_error(a.err, DERR_TIMEOUT_FULL);
+            // one decision for the whole CTA: stop once any wait anywhere ran out
+            LC.halt = ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err)) != 0u;
         }
-        // ---- routing (routed CTAs), x --------------------------------------
-        if (!shared_cta) {
-            if (ranked) rank_slice(Lr.logits, E, k, warp, lane, LC.cand_key, LC.cand_id);
-            consumer_sync();
-            if (ranked) {
-                rank_candidates(LC.cand_key, LC.cand_id, PW * k, k, tid, C.x);
-                consumer_sync();
-            }
-            if (warp == PW - 1) {
-                if (!ranked) {
-                    route_select(Lr.logits, E, k, lane, C.x);
-                    __syncwarp();
-                }
-                bool bad = false;
-                if (lane < k) {
-                    const int x = C.x[lane];
-                    LC.gid[lane] = x;
-                    bad = x < 0 || x >= E;
-                    if (!bad) {
-                        C.usrc[lane][0] = Lr.up + static_cast<uint64_t>(x) * a.eb_up;
-                        C.usrc[lane][1] = Lr.gate + static_cast<uint64_t>(x) * a.eb_gate;
-                        LC.dsrc[lane] = Lr.down + static_cast<uint64_t>(x) * a.eb_down;
-                    }
-                    if (Lr.ids_out && bid == 0) Lr.ids_out[lane] = x;
-                }
-                bad = __any_sync(0xffffffffu, bad);
-                if (lane == 0 && bad) {
-                    C.fail = 1;
-                    set_error(a.err, DERR_BAD_ID);
-                }
-                __syncwarp();
-                asm volatile("bar.arrive 4, 64;" ::: "memory");
-            }
-        }
-        if (warp < PW - 1)
-            for (int b = warp; b < nbx; b += PW - 1)
-                stage_f32_block<TA, true>(Lr.x, act_area, KA, b, lane);   // through L2: x may be a fresh x_next
         consumer_sync();
-        const bool run = !C.fail;
-        if (!run) break;
-        // ---- gating weights (warp PW - 1; the shared CTAs route here, off
-        //      their critical path) -----------------------------------------
-        if (warp == PW - 1) {
-            if (shared_cta) {
-                route_select(Lr.logits, E, k, lane, LC.gid);
-                __syncwarp();
-            }
-            route_weights(Lr.logits, E, k, a.norm_w, lane, LC.gid, LC.wt);
-            __syncwarp();
-            if (bid == 0 && Lr.w_out && lane < k) Lr.w_out[lane] = LC.wt[lane];
+        if (LC.halt) break;
+        // layer l - 1 is done in every consumer warp: its routing buffer is free
+        if (l > 0 && tid == 0) mbar_arrive(&SS.rt_empty[(l - 1) % STACK_ROUTE_BUFS]);
+        mbar_wait_sleep(&SS.rt_full[rb], rpar, a.timeout_ns);   // complete: acquires the producer's writes
+        if (R.bad) {
+            if (tid == 0) set_error(a.err, DERR_BAD_ID);
+            break;
         }
+        for (int b = warp; b < nbx; b += PW)
+            stage_f32_block<TA, true>(Lr.x, act_area, KA, b, lane);   // through L2: x may be a fresh x_next
+        consumer_sync();
         // ---- phase A: gate/up + GLU -> h, tagged copies -----------------------
         for (int i = 0; i < nA; ++i) {
             const int gi = g0 + i;
@@ -252,8 +287,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                 break;
             }
             const int row0 = P.a0 + i * rpt, nr = min(rpt, P.a1 - row0);
-            const char *s0 = shared_cta ? Lr.sh_up : C.usrc[P.u][0];
-            const char *s1 = shared_cta ? Lr.sh_gate : C.usrc[P.u][1];
+            const char *s0 = shared_cta ? Lr.sh_up : R.usrc[P.u][0];
+            const char *s1 = shared_cta ? Lr.sh_gate : R.usrc[P.u][1];
             const uint8_t *stage = stage_area + static_cast<size_t>(s) * a.stage_bytes;
             const uint64_t off = static_cast<uint64_t>(row0) * a.gu.row_bytes;
             const uint8_t *up_rows = stage + ((reinterpret_cast<uintptr_t>(s0) + off) & 15u);
@@ -297,7 +332,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                 break;
             }
             const int row0 = P.b0 + (i - nA) * rows_b, nr = min(rows_b, P.b1 - row0);
-            const char *s0 = shared_cta ? Lr.sh_down : LC.dsrc[P.u];
+            const char *s0 = shared_cta ? Lr.sh_down : R.dsrc[P.u];
             const uint8_t *rows = stage_area + static_cast<size_t>(s) * a.stage_bytes +
                                   ((reinterpret_cast<uintptr_t>(s0) + static_cast<uint64_t>(row0) * a.dn.row_bytes) & 15u);
             consume_tile<TB, ACT_CPU, 1, 1, 32>(a.dn, C, rows, rows, nr, P.u, k, row0, act_area, lane);
@@ -322,7 +357,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                     float acc = 0.f;
                     for (int p = 0; p < k; ++p) {
                         const float v = __fmul_rn(__ldcg(a.dn.dst + static_cast<int64_t>(p) * a.dn.stride_channel_dst + r),
-                                                  LC.wt[p]);
+                                                  R.wt[p]);
                         acc = p == 0 ? v : __fadd_rn(acc, v);
                     }
                     if (hs) acc = __fadd_rn(acc, __ldcg(a.dn.shared_dst + r));
