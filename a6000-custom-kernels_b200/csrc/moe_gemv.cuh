@@ -774,40 +774,57 @@ __device__ __forceinline__ int produce_tiles(int n_tiles, int S, uint64_t *full,
     for (int base = 0; base < n_tiles && ok; base += R) {
         const int cnt = (n_tiles - base) < R ? (n_tiles - base) : R;
         bool plain_tile = false, lane_ok = true;
+        TileSrc ts;
+        const int gi = g0 + base + lane, s = gi % S;
         if (lane < cnt) {
-            const int i = base + lane, gi = g0 + i, s = gi % S;
-            TileSrc ts;
-            describe(i, ts);
+            describe(base + lane, ts);
             plain_tile = ts.kind[0] != 0 || (ts.n_parts > 1 && ts.kind[1] != 0);
-            if (!plain_tile) {
-                if (gi >= S && !mbar_wait_sleep(&empty[s], static_cast<uint32_t>((gi / S - 1) & 1), timeout_ns)) {
-                    lane_ok = false;
-                } else {
-                    uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
-                    uintptr_t lo[2], hi[2];
-                    uint32_t tx = 0;
+        }
+        // each lane issues its bulk tile as soon as its stage is free (every
+        // pending stage is probed per pass; between passes the warp sleeps on
+        // the oldest), not when the whole round is free
+        bool need = lane < cnt && !plain_tile;
+        const uint64_t t0 = clock64(), lim = timeout_cycles(timeout_ns);
+        for (;;) {
+            if (need && (gi < S || mbar_test_wait(&empty[s], static_cast<uint32_t>((gi / S - 1) & 1)))) {
+                uint8_t *stage = stage_area + static_cast<size_t>(s) * stage_bytes;
+                uintptr_t lo[2], hi[2];
+                uint32_t tx = 0;
 #pragma unroll
-                    for (int p = 0; p < 2; ++p) {
-                        if (p >= ts.n_parts) break;
-                        const uint32_t bytes = static_cast<uint32_t>(ts.nr[p]) * ts.rb;
-                        const uintptr_t sp = reinterpret_cast<uintptr_t>(ts.src[p]) + static_cast<uint64_t>(ts.row0[p]) * ts.rb;
-                        lo[p] = sp & ~static_cast<uintptr_t>(15);
-                        hi[p] = (sp + bytes + 15u) & ~static_cast<uintptr_t>(15);
-                        tx += static_cast<uint32_t>(hi[p] - lo[p]);
-                    }
-                    mbar_arrive_expect_tx(&full[s], tx);
-#pragma unroll
-                    for (int p = 0; p < 2; ++p) {
-                        if (p >= ts.n_parts) break;
-                        bulk_g2s(stage + p * ts.part_bytes, reinterpret_cast<const void *>(lo[p]),
-                                 static_cast<uint32_t>(hi[p] - lo[p]), &full[s], pol);
-                    }
+                for (int p = 0; p < 2; ++p) {
+                    if (p >= ts.n_parts) break;
+                    const uint32_t bytes = static_cast<uint32_t>(ts.nr[p]) * ts.rb;
+                    const uintptr_t sp = reinterpret_cast<uintptr_t>(ts.src[p]) + static_cast<uint64_t>(ts.row0[p]) * ts.rb;
+                    lo[p] = sp & ~static_cast<uintptr_t>(15);
+                    hi[p] = (sp + bytes + 15u) & ~static_cast<uintptr_t>(15);
+                    tx += static_cast<uint32_t>(hi[p] - lo[p]);
                 }
+                mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    if (p >= ts.n_parts) break;
+                    bulk_g2s(stage + p * ts.part_bytes, reinterpret_cast<const void *>(lo[p]),
+                             static_cast<uint32_t>(hi[p] - lo[p]), &full[s], pol);
+                }
+                need = false;
             }
+            const unsigned pend = __ballot_sync(0xffffffffu, need);
+            if (!pend) break;
+            if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                lane_ok = !need;
+                break;
+            }
+            // sleep (in hardware) until the oldest pending stage is free
+            if (lane == __ffs(pend) - 1) mbar_try_wait_hint(&empty[s], static_cast<uint32_t>((gi / S - 1) & 1), 20000u);
+            __syncwarp();
         }
         if (__any_sync(0xffffffffu, !lane_ok)) {
             if (lane == 0) set_error(err, DERR_TIMEOUT_EMPTY);
-            issued = base + cnt;
+            // this round's copies land before the producer gives up (the
+            // caller's drain covers the rounds before it)
+            if (lane < cnt && !plain_tile && lane_ok)
+                mbar_wait_sleep(&full[s], static_cast<uint32_t>((gi / S) & 1), drain_limit_ns(timeout_ns));
+            issued = base;
             ok = false;
             break;
         }

@@ -84,7 +84,7 @@ int launch_stack(int type, StackArgs &a, cudaStream_t st, const char **why, cuda
     if (fit < 2) { *why = "activations and tiles do not fit in shared memory"; return -2; }
     const int nw = fit < GEMV_CONSUMER_WARPS ? fit : GEMV_CONSUMER_WARPS;
     a.n_tile_warps = nw;
-    a.n_stages = fit / nw * nw;
+    a.n_stages = fit;   // stage g % S and warp g % nw need not line up
     a.gu.n_tile_warps = nw;
     a.dn.n_tile_warps = nw;
     smem = static_cast<size_t>(a.ctrl_bytes) + a.act_bytes + static_cast<size_t>(a.n_stages) * a.stage_bytes;

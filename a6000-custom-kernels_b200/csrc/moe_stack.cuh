@@ -105,6 +105,20 @@ __device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Optional timeline (built with -DMOE_LAYER2_TRACE): SM clock marks (64 per
+// CTA) taken at one layer of the stack (MOE_STACK_TRACE_LAYER).
+#ifdef MOE_LAYER2_TRACE
+#ifndef MOE_STACK_TRACE_LAYER
+#define MOE_STACK_TRACE_LAYER 20
+#endif
+#define ST_MARK(l, i)                                                                         \
+    do {                                                                                      \
+        if ((l) == MOE_STACK_TRACE_LAYER && lane == 0) g_layer2_trace[blockIdx.x * 64 + (i)] = clock64(); \
+    } while (0)
+#else
+#define ST_MARK(l, i) do {} while (0)
+#endif
+
 template <int TA, int TB>
 __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid_constant__ StackArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -203,16 +217,20 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             for (int l = 0; l < L; ++l) {
                 if (ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err))) break;
                 const int g0 = l * per_layer;
+                ST_MARK(l, 7);
                 int n = produce_tiles(P.nA, S, full, empty, stage_area, a.stage_bytes,
                                       [&](int i, TileSrc &ts) { describe(l, i, ts); }, a.timeout_ns, a.err, lane, g0,
                                       false);
                 end = g0 + n;
                 if (n < P.nA) break;
+                ST_MARK(l, 8);
                 const bool next = l + 1 < L ? route_layer(l + 1) : true;
+                ST_MARK(l, 9);
                 n = produce_tiles(P.nB, S, full, empty, stage_area, a.stage_bytes,
                                   [&](int i, TileSrc &ts) { describe(l, P.nA + i, ts); }, a.timeout_ns, a.err, lane,
                                   g0 + P.nA, false);
                 end = g0 + P.nA + n;
+                ST_MARK(l, 10);
                 if (n < P.nB || !next) break;
             }
         }
@@ -236,6 +254,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         C.shslot[0] = 0;
         C.fail = 0;
     }
+#ifdef MOE_LAYER2_TRACE
+    if (tid == 0)
+        g_layer2_trace[bid * 64 + 63] = static_cast<unsigned long long>(S) | (static_cast<unsigned long long>(nw) << 8) |
+                                        (static_cast<unsigned long long>(P.nA) << 16) |
+                                        (static_cast<unsigned long long>(P.nB) << 24);
+#endif
     constexpr int QA = is_kquant(TA) ? 256 : 32;
     const int nbx = KA / QA;
     const int nA = P.nA, nB = P.nB;
@@ -246,6 +270,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         const uint32_t rpar = static_cast<uint32_t>((l / STACK_ROUTE_BUFS) & 1);
         const uint32_t tag = epoch0 + 1u + static_cast<uint32_t>(l);
         const int g0 = l * per_layer;
+        if (warp == 0) ST_MARK(l, 0);
         // ---- layer l - 1's output complete (its input may be this layer's x),
         //      layer l routed ----------------------------------------------------
         if (tid == 0) {
@@ -261,11 +286,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                     }
                 }
             }
+            ST_MARK(l, 11);
             if (ok && !mbar_wait_sleep(&SS.rt_full[rb], rpar, a.timeout_ns)) set_error(a.err, DERR_TIMEOUT_FULL);
             // one decision for the whole CTA: stop once any wait anywhere ran out
             LC.halt = ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err)) != 0u;
         }
         consumer_sync();
+        if (warp == 0) ST_MARK(l, 1);
         if (LC.halt) break;
         // layer l - 1 is done in every consumer warp: its routing buffer is free
         if (l > 0 && tid == 0) mbar_arrive(&SS.rt_empty[(l - 1) % STACK_ROUTE_BUFS]);
@@ -277,15 +304,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         for (int b = warp; b < nbx; b += PW)
             stage_f32_block<TA, true>(Lr.x, act_area, KA, b, lane);   // through L2: x may be a fresh x_next
         consumer_sync();
+        if (warp == 0) ST_MARK(l, 2);
         // ---- phase A: gate/up + GLU -> h, tagged copies -----------------------
-        for (int i = 0; i < nA; ++i) {
+        // this warp's tiles: ring indexes = warp (mod nw)
+        const int iw = warp < nw ? ((warp - g0 % nw) % nw + nw) % nw : nA;
+        for (int i = iw; i < nA; i += nw) {
             const int gi = g0 + i;
-            if (gi % nw != warp) continue;
             const int s = gi % S;
             if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((gi / S) & 1), a.timeout_ns)) {
                 if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
                 break;
             }
+            if (i == warp) ST_MARK(l, 12 + warp);
             const int row0 = P.a0 + i * rpt, nr = min(rpt, P.a1 - row0);
             const char *s0 = shared_cta ? Lr.sh_up : R.usrc[P.u][0];
             const char *s1 = shared_cta ? Lr.sh_gate : R.usrc[P.u][1];
@@ -295,10 +325,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             const uint8_t *gate_rows = stage + a.gu.part_bytes + ((reinterpret_cast<uintptr_t>(s1) + off) & 15u);
             consume_tile<TA, ACT_CPU, 1, 2>(a.gu, C, up_rows, gate_rows, nr, P.u, k, row0, act_area, lane, a.h_tag,
                                             a.hs_tag, tag);
+            if (i == warp) ST_MARK(l, 28 + warp);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
+        if (warp == 0) ST_MARK(l, 60);
         consumer_sync();
+        if (warp == 0) ST_MARK(l, 3);
         // ---- the unit's h from the CTAs of its group, quantized for down ----
         {
             constexpr bool KQ = is_kquant(TB);
@@ -322,15 +355,17 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             }
         }
         consumer_sync();
+        if (warp == 0) ST_MARK(l, 4);
         // ---- phase B: down rows -> y / ys -------------------------------------
-        for (int i = nA; i < nA + nB; ++i) {
+        const int ib = warp < nw ? nA + ((warp - (g0 + nA) % nw) % nw + nw) % nw : nA + nB;
+        for (int i = ib; i < nA + nB; i += nw) {
             const int gi = g0 + i;
-            if (gi % nw != warp) continue;
             const int s = gi % S;
             if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((gi / S) & 1), a.timeout_ns)) {
                 if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
                 break;
             }
+            if (i - nA < nw) ST_MARK(l, 44 + warp);
             const int row0 = P.b0 + (i - nA) * rows_b, nr = min(rows_b, P.b1 - row0);
             const char *s0 = shared_cta ? Lr.sh_down : R.dsrc[P.u];
             const uint8_t *rows = stage_area + static_cast<size_t>(s) * a.stage_bytes +
@@ -340,6 +375,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         consumer_sync();          // the CTA's y stores, ordered before each warp's release below
+        if (warp == 0) ST_MARK(l, 5);
         // ---- arrivals per 64-row block; the CTA completing one sums it, writes
         //      out (and x + out), and counts the block done ----------------------
         if (P.b1 > P.b0) {
@@ -353,16 +389,44 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                 old = __shfl_sync(0xffffffffu, old, 0);
                 if (old + mine != static_cast<uint32_t>(hi - lo) * static_cast<uint32_t>(k + hs)) continue;
                 __syncwarp();
-                for (int r = lo + lane; r < hi; r += 32) {
-                    float acc = 0.f;
-                    for (int p = 0; p < k; ++p) {
-                        const float v = __fmul_rn(__ldcg(a.dn.dst + static_cast<int64_t>(p) * a.dn.stride_channel_dst + r),
-                                                  R.wt[p]);
-                        acc = p == 0 ? v : __fadd_rn(acc, v);
+                // rows lo + lane and lo + 32 + lane: every value of both in
+                // flight together (picks 8 at a time), summed in pick order
+                static_assert(LAYER2_RB == 64, "two rows per lane");
+                const int r0 = lo + lane, r1 = lo + 32 + lane;
+                const bool ok0 = r0 < hi, ok1 = r1 < hi;
+                float acc0 = 0.f, acc1 = 0.f;
+                const float sh0 = hs && ok0 ? __ldcg(a.dn.shared_dst + r0) : 0.f;
+                const float sh1 = hs && ok1 ? __ldcg(a.dn.shared_dst + r1) : 0.f;
+                const float x0 = Lr.x_next && ok0 ? __ldcg(Lr.x + r0) : 0.f;
+                const float x1 = Lr.x_next && ok1 ? __ldcg(Lr.x + r1) : 0.f;
+                for (int p0 = 0; p0 < k; p0 += 8) {
+                    float v0[8], v1[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float *yp = a.dn.dst + static_cast<int64_t>(p0 + j) * a.dn.stride_channel_dst;
+                        v0[j] = p0 + j < k && ok0 ? __ldcg(yp + r0) : 0.f;
+                        v1[j] = p0 + j < k && ok1 ? __ldcg(yp + r1) : 0.f;
                     }
-                    if (hs) acc = __fadd_rn(acc, __ldcg(a.dn.shared_dst + r));
-                    Lr.out[r] = acc;
-                    if (Lr.x_next) Lr.x_next[r] = __fadd_rn(__ldcg(Lr.x + r), acc);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (p0 + j >= k) break;
+                        const float w = R.wt[p0 + j];
+                        const float w0 = __fmul_rn(v0[j], w), w1 = __fmul_rn(v1[j], w);
+                        acc0 = p0 + j == 0 ? w0 : __fadd_rn(acc0, w0);
+                        acc1 = p0 + j == 0 ? w1 : __fadd_rn(acc1, w1);
+                    }
+                }
+                if (hs) {
+                    acc0 = __fadd_rn(acc0, sh0);
+                    acc1 = __fadd_rn(acc1, sh1);
+                }
+                if (ok0) {
+                    Lr.out[r0] = acc0;
+                    if (Lr.x_next) Lr.x_next[r0] = __fadd_rn(x0, acc0);
+                }
+                if (ok1) {
+                    Lr.out[r1] = acc1;
+                    if (Lr.x_next) Lr.x_next[r1] = __fadd_rn(x1, acc1);
                 }
                 __syncwarp();
                 if (lane == 0) {
@@ -371,6 +435,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                 }
             }
         }
+        if (warp == 0) ST_MARK(l, 6);
     }
     // ---- the last CTA to finish advances the epoch past every layer's tag and
     //      clears the layer counter ---------------------------------------------
