@@ -1579,9 +1579,29 @@ int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap,
     return MOE_OK;
 }
 
+// The stack's workspace: the layer workspace at one token, the layer
+// descriptors, then the tagged down rows ([k][H] routed + [H] shared) and the
+// tagged x buffers ([2][H]) through which consecutive layers hand over.
+struct StackWs {
+    moe::StackLayer *layers;
+    uint64_t *ytag, *xtag;
+    size_t bytes;
+};
+
+StackWs stack_ws(const moe_layer_desc *L, int64_t n_layers, char *base) {
+    StackWs w{};
+    size_t off = layer_ws(L, 1, nullptr).bytes;
+    auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
+    w.layers = reinterpret_cast<moe::StackLayer *>(take(sizeof(moe::StackLayer) * static_cast<size_t>(n_layers)));
+    w.ytag = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * static_cast<size_t>((L->k + 1) * L->H)));
+    w.xtag = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * static_cast<size_t>(2 * L->H)));
+    w.bytes = off;
+    return w;
+}
+
 size_t moe_b200_stack_workspace_size(const moe_layer_desc *L, int64_t n_layers) {
     if (!L || n_layers < 1) return 0;
-    return layer_ws(L, 1, nullptr).bytes + align256(sizeof(moe::StackLayer) * static_cast<size_t>(n_layers));
+    return stack_ws(L, n_layers, nullptr).bytes;
 }
 
 int moe_b200_stack_prepare(const moe_layer_desc *layers, int64_t n_layers, const float *const *x,
@@ -1628,9 +1648,10 @@ int moe_b200_stack_prepare(const moe_layer_desc *layers, int64_t n_layers, const
         s.x_next = x_next ? x_next[l] : nullptr;
         s.ids_out = w.ids;
         s.w_out = w.w;
+        s.chained = l > 0 && x_next && x_next[l - 1] == x[l] ? 1 : 0;
     }
-    char *tail = static_cast<char *>(workspace) + layer_ws(&L0, 1, nullptr).bytes;
-    CK(cudaMemcpyAsync(tail, d.data(), sizeof(moe::StackLayer) * d.size(), cudaMemcpyHostToDevice,
+    const StackWs sw = stack_ws(&L0, n_layers, static_cast<char *>(workspace));
+    CK(cudaMemcpyAsync(sw.layers, d.data(), sizeof(moe::StackLayer) * d.size(), cudaMemcpyHostToDevice,
                        reinterpret_cast<cudaStream_t>(stream)));
     return MOE_OK;
 }
@@ -1655,7 +1676,8 @@ int moe_b200_stack_run(const moe_layer_desc *layer0, int64_t n_layers, void *wor
     moe::StackArgs a{};
     a.gu = la.gu;
     a.dn = la.dn;
-    a.layers = reinterpret_cast<const moe::StackLayer *>(static_cast<char *>(workspace) + layer_ws(layer0, 1, nullptr).bytes);
+    const StackWs sw = stack_ws(layer0, n_layers, static_cast<char *>(workspace));
+    a.layers = sw.layers;
     a.n_layers = static_cast<int32_t>(n_layers);
     a.k = static_cast<int32_t>(layer0->k);
     a.n_experts = static_cast<int32_t>(layer0->n_experts);
@@ -1667,8 +1689,12 @@ int moe_b200_stack_run(const moe_layer_desc *layer0, int64_t n_layers, void *wor
     a.has_shared = layer0->shared_type >= 0 ? 1 : 0;
     a.h_tag = w.h_tag;
     a.hs_tag = w.hs_tag;
+    if (la.dn.stride_channel_dst != layer0->H) return fail(MOE_ERR_INVALID, "unexpected down-row stride");
+    a.ysc = layer0->H;
+    a.ytag = sw.ytag;
+    a.ytag_s = sw.ytag + static_cast<size_t>(layer0->k * layer0->H);
+    a.xtag = sw.xtag;
     a.gbar = w.gbar;
-    a.rowcnt = w.rowcnt;
     a.err = g.d_err;
     a.timeout_ns = g.timeout_ns_kernel;
     const char *why = "";

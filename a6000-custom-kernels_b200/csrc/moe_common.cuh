@@ -118,6 +118,7 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
 // 20 us poll with the non-blocking probe (try_wait itself may suspend for a
 // hardware-defined time), so a tiny limit gives up at once.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
+    if (mbar_test_wait(bar, parity)) return true;   // the common case: the phase is already complete
     if (timeout_ns < 20000u) {
         const uint64_t t0 = clock64(), lim = timeout_cycles(timeout_ns);
         for (;;) {
@@ -314,6 +315,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
 
 __device__ __forceinline__ void st_relaxed_u64(uint64_t *p, uint64_t v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // two 64-bit words at a 16-byte aligned address (each word single-copy atomic)

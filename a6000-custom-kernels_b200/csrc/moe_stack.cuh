@@ -39,9 +39,13 @@ struct StackLayer {
     float *out, *x_next;                    // output [H]; x_next = x + out when not null
     int32_t *ids_out;                       // [k] picks (may be null)
     float *w_out;                           // [k] gating weights (may be null)
+    int32_t chained;                        // x is the previous layer's x_next
 };
 
 constexpr int STACK_MAX_K = 32;
+#ifndef STACK_POLL_NS
+#define STACK_POLL_NS 100
+#endif
 constexpr int STACK_ROUTE_BUFS = 3;
 
 // One layer's routing, written by the producer warp, read by the consumers.
@@ -66,8 +70,10 @@ struct StackArgs {
     uint64_t eb_up, eb_gate, eb_down;       // bytes of one expert of each tensor
     int32_t tma, has_shared;                // every source 16-byte aligned (bulk copies)
     uint64_t *h_tag, *hs_tag;
-    uint32_t *gbar;                         // [0] epoch, [1] finished CTAs, [2] output blocks done
-    uint32_t *rowcnt;                       // [n_rb] rows arrived per 64-row block (zero between layers)
+    uint64_t *ytag, *ytag_s;                // down rows as (value, tag): [k][ysc] routed, [H] shared
+    int64_t ysc;
+    uint64_t *xtag;                         // [2][H]: x_l + out_l as (value, tag), by layer parity
+    uint32_t *gbar;                         // [0] epoch, [1] finished CTAs
     int32_t n_rb;
     int32_t n_stages, n_tile_warps;
     uint32_t stage_bytes, ctrl_bytes, act_bytes;
@@ -263,6 +269,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
     constexpr int QA = is_kquant(TA) ? 256 : 32;
     const int nbx = KA / QA;
     const int nA = P.nA, nB = P.nB;
+    if (tid == 0) LC.halt = 0u;
+    consumer_sync();
+    // tile cursor of this warp (nw <= S, so one wrap per step at most); warps
+    // past nw take no tiles
+    int cg = warp < nw ? warp : 0x7fffffff, cs = warp < nw ? warp : 0;
+    uint32_t cph = 0;
     for (int l = 0; l < L; ++l) {
         const StackLayer &Lr = a.layers[l];
         const int rb = l % STACK_ROUTE_BUFS;
@@ -271,48 +283,79 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         const uint32_t tag = epoch0 + 1u + static_cast<uint32_t>(l);
         const int g0 = l * per_layer;
         if (warp == 0) ST_MARK(l, 0);
-        // ---- layer l - 1's output complete (its input may be this layer's x),
-        //      layer l routed ----------------------------------------------------
-        if (tid == 0) {
-            bool ok = true;
-            if (l > 0) {
-                const uint32_t target = static_cast<uint32_t>(l) * static_cast<uint32_t>(a.n_rb);
-                const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
-                while (ld_acquire_gpu(&a.gbar[2]) < target) {
-                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
-                        set_error(a.err, DERR_TIMEOUT_TAG);
-                        ok = false;
-                        break;
-                    }
+        // ---- layer l routed; its input staged. From layer 1 on, every value
+        //      of x_l = x_{l-1} + out_{l-1} as layer l - 1's combiners tagged it
+        //      (tag - 1): the layer starts only when layer l - 1 is complete,
+        //      and a chained layer quantizes those values as its input -------
+        if (tid == 0 && !mbar_wait_sleep(&SS.rt_full[rb], rpar, a.timeout_ns)) {
+            set_error(a.err, DERR_TIMEOUT_FULL);
+            LC.halt = 1u;
+        }
+        {
+            constexpr bool KQ = is_kquant(TA);
+            const uint64_t *xin = a.xtag + static_cast<int64_t>(l & 1) * H;
+            const bool from_tags = l > 0 && Lr.chained;
+            const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
+            // one warp watches the last row of every 32-row block (the rows a
+            // combining warp writes together) with a pause between rounds; the
+            // others wait at the barrier instead of polling L2 too
+            if (l > 0 && warp == 0) {
+                for (;;) {
+                    bool got = true;
+                    for (int r = 32 * lane + 31; r < H + 31; r += 32 * 32)
+                        got &= static_cast<uint32_t>(ld_relaxed_u64(xin + min(r, H - 1)) >> 32) == tag - 1u;
+                    if (__all_sync(0xffffffffu, got)) break;
+                    if (static_cast<uint64_t>(clock64()) - t0 > lim) break;   // the block loads below time out too
+                    __nanosleep(STACK_POLL_NS);
                 }
             }
-            ST_MARK(l, 11);
-            if (ok && !mbar_wait_sleep(&SS.rt_full[rb], rpar, a.timeout_ns)) set_error(a.err, DERR_TIMEOUT_FULL);
-            // one decision for the whole CTA: stop once any wait anywhere ran out
-            LC.halt = ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err)) != 0u;
+            if (l > 0) consumer_sync();
+            for (int b = warp; b < nbx; b += PW) {
+                float v[KQ ? 8 : 1];
+                if (l > 0) {
+                    while (!__all_sync(0xffffffffu, load_tagged_block_gpu<KQ>(xin + b * QA, tag - 1u, lane, v))) {
+                        if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                            if (lane == 0) {
+                                set_error(a.err, DERR_TIMEOUT_TAG);
+                                LC.halt = 1u;
+                            }
+                            break;
+                        }
+                    }
+                }
+                if (from_tags) {
+                    int8_t *q = reinterpret_cast<int8_t *>(act_area);
+                    int16_t *bs = reinterpret_cast<int16_t *>(act_area + KA);
+                    float *sc = reinterpret_cast<float *>(act_area + KA + KA / 8);
+                    if constexpr (KQ) quant_q8K_vals<TA>(v, q, bs, sc, b, lane, KA / chunk_of<TA>::CE);
+                    else quant_q80_val<TA>(v[0], q, bs, sc, b, lane, KA / chunk_of<TA>::CE);
+                } else {
+                    stage_f32_block<TA, true>(Lr.x, act_area, KA, b, lane);
+                }
+            }
         }
         consumer_sync();
-        if (warp == 0) ST_MARK(l, 1);
+        if (warp == 0) ST_MARK(l, 2);
         if (LC.halt) break;
         // layer l - 1 is done in every consumer warp: its routing buffer is free
         if (l > 0 && tid == 0) mbar_arrive(&SS.rt_empty[(l - 1) % STACK_ROUTE_BUFS]);
-        mbar_wait_sleep(&SS.rt_full[rb], rpar, a.timeout_ns);   // complete: acquires the producer's writes
+        // thread 0 saw rt_full complete (acquiring the producer's writes) before
+        // the barrier above, which orders it before every consumer's reads
         if (R.bad) {
             if (tid == 0) set_error(a.err, DERR_BAD_ID);
             break;
         }
-        for (int b = warp; b < nbx; b += PW)
-            stage_f32_block<TA, true>(Lr.x, act_area, KA, b, lane);   // through L2: x may be a fresh x_next
-        consumer_sync();
-        if (warp == 0) ST_MARK(l, 2);
         // ---- phase A: gate/up + GLU -> h, tagged copies -----------------------
-        // this warp's tiles: ring indexes = warp (mod nw)
-        const int iw = warp < nw ? ((warp - g0 % nw) % nw + nw) % nw : nA;
-        for (int i = iw; i < nA; i += nw) {
-            const int gi = g0 + i;
-            const int s = gi % S;
-            if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((gi / S) & 1), a.timeout_ns)) {
-                if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+        // this warp's tiles: the ring indexes = warp (mod nw), walked by the
+        // cursor (cg, cs, cph) = (ring index, stage, phase parity)
+        for (; cg < g0 + nA; cg += nw, cs += nw, cph ^= cs >= S ? 1u : 0u, cs -= cs >= S ? S : 0) {
+            const int i = cg - g0, s = cs;
+            if (i == warp && warp == 1) ST_MARK(l, 61);
+            if (!mbar_wait_sleep(&full[s], cph, a.timeout_ns)) {
+                if (lane == 0) {
+                    set_error(a.err, DERR_TIMEOUT_FULL);
+                    LC.halt = 1u;
+                }
                 break;
             }
             if (i == warp) ST_MARK(l, 12 + warp);
@@ -346,6 +389,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                         if (lane == 0) set_error(a.err, DERR_TIMEOUT_TAG);
                         break;
                     }
+                    __nanosleep(STACK_POLL_NS);
                 }
                 int8_t *q = reinterpret_cast<int8_t *>(act_area);
                 int16_t *bs = reinterpret_cast<int16_t *>(act_area + KB);
@@ -357,83 +401,92 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         consumer_sync();
         if (warp == 0) ST_MARK(l, 4);
         // ---- phase B: down rows -> y / ys -------------------------------------
-        const int ib = warp < nw ? nA + ((warp - (g0 + nA) % nw) % nw + nw) % nw : nA + nB;
-        for (int i = ib; i < nA + nB; i += nw) {
-            const int gi = g0 + i;
-            const int s = gi % S;
-            if (!mbar_wait_sleep(&full[s], static_cast<uint32_t>((gi / S) & 1), a.timeout_ns)) {
-                if (lane == 0) set_error(a.err, DERR_TIMEOUT_FULL);
+        for (; cg < g0 + nA + nB; cg += nw, cs += nw, cph ^= cs >= S ? 1u : 0u, cs -= cs >= S ? S : 0) {
+            const int i = cg - g0, s = cs;
+            if (i - nA < nw && warp == 1) ST_MARK(l, 11);
+            if (!mbar_wait_sleep(&full[s], cph, a.timeout_ns)) {
+                if (lane == 0) {
+                    set_error(a.err, DERR_TIMEOUT_FULL);
+                    LC.halt = 1u;
+                }
                 break;
             }
             if (i - nA < nw) ST_MARK(l, 44 + warp);
+            if (i - nA < nw && warp == 1) ST_MARK(l, 62);
             const int row0 = P.b0 + (i - nA) * rows_b, nr = min(rows_b, P.b1 - row0);
             const char *s0 = shared_cta ? Lr.sh_down : R.dsrc[P.u];
             const uint8_t *rows = stage_area + static_cast<size_t>(s) * a.stage_bytes +
                                   ((reinterpret_cast<uintptr_t>(s0) + static_cast<uint64_t>(row0) * a.dn.row_bytes) & 15u);
-            consume_tile<TB, ACT_CPU, 1, 1, 32>(a.dn, C, rows, rows, nr, P.u, k, row0, act_area, lane);
+            consume_tile<TB, ACT_CPU, 1, 1, 32>(a.dn, C, rows, rows, nr, P.u, k, row0, act_area, lane, a.ytag,
+                                                a.ytag_s, tag);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        consumer_sync();          // the CTA's y stores, ordered before each warp's release below
+        consumer_sync();          // phase B has read the activation area; it may be restaged
         if (warp == 0) ST_MARK(l, 5);
-        // ---- arrivals per 64-row block; the CTA completing one sums it, writes
-        //      out (and x + out), and counts the block done ----------------------
-        if (P.b1 > P.b0) {
-            const int RB = LAYER2_RB;
-            const int rb0 = P.b0 / RB, nblk = (P.b1 - 1) / RB - rb0 + 1;
-            for (int b = rb0 + warp; b < rb0 + nblk; b += PW) {
-                const int lo = b * RB, hi = min(H, lo + RB);
-                const uint32_t mine = static_cast<uint32_t>(min(P.b1, hi) - max(P.b0, lo));
-                uint32_t old = 0;
-                if (lane == 0) old = atom_add_acq_rel_gpu(&a.rowcnt[b], mine);
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (old + mine != static_cast<uint32_t>(hi - lo) * static_cast<uint32_t>(k + hs)) continue;
-                __syncwarp();
-                // rows lo + lane and lo + 32 + lane: every value of both in
-                // flight together (picks 8 at a time), summed in pick order
-                static_assert(LAYER2_RB == 64, "two rows per lane");
-                const int r0 = lo + lane, r1 = lo + 32 + lane;
-                const bool ok0 = r0 < hi, ok1 = r1 < hi;
-                float acc0 = 0.f, acc1 = 0.f;
-                const float sh0 = hs && ok0 ? __ldcg(a.dn.shared_dst + r0) : 0.f;
-                const float sh1 = hs && ok1 ? __ldcg(a.dn.shared_dst + r1) : 0.f;
-                const float x0 = Lr.x_next && ok0 ? __ldcg(Lr.x + r0) : 0.f;
-                const float x1 = Lr.x_next && ok1 ? __ldcg(Lr.x + r1) : 0.f;
-                for (int p0 = 0; p0 < k; p0 += 8) {
-                    float v0[8], v1[8];
+        // ---- combine: CTA c sums the 32-row blocks b = c (mod G) (one lane per
+        //      row) once every pick's rows and the shared expert's carry this
+        //      layer's tag, in pick order; writes out (and x_next) and, tagged,
+        //      x_l + out_l for layer l + 1 -----------------------------------------
+        for (int j = PW - 1 - warp;; j += PW) {
+            const int b = bid + j * G;
+            if (b * 32 >= H) break;
+            const int r = b * 32 + lane;
+            const bool ok = r < H;
+            const int np = k + hs;                       // the shared expert is term k
+            const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
+            float acc = 0.f;
+            bool fail = false;
+            for (int p0 = 0; p0 < np && !fail; p0 += 8) {
+                uint64_t w[8];
+                for (;;) {
+                    bool got = true;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float *yp = a.dn.dst + static_cast<int64_t>(p0 + j) * a.dn.stride_channel_dst;
-                        v0[j] = p0 + j < k && ok0 ? __ldcg(yp + r0) : 0.f;
-                        v1[j] = p0 + j < k && ok1 ? __ldcg(yp + r1) : 0.f;
+                    for (int q = 0; q < 8; ++q) {
+                        const int p = p0 + q;
+                        const uint64_t *yp = p < k ? a.ytag + static_cast<int64_t>(p) * a.ysc : a.ytag_s;
+                        w[q] = p < np && ok ? ld_relaxed_u64(yp + r) : tagged(0.f, tag);
+                        got &= static_cast<uint32_t>(w[q] >> 32) == tag;
                     }
+                    if (__all_sync(0xffffffffu, got)) break;
+                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                        fail = true;
+                        break;
+                    }
+                    __nanosleep(STACK_POLL_NS);
+                }
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        if (p0 + j >= k) break;
-                        const float w = R.wt[p0 + j];
-                        const float w0 = __fmul_rn(v0[j], w), w1 = __fmul_rn(v1[j], w);
-                        acc0 = p0 + j == 0 ? w0 : __fadd_rn(acc0, w0);
-                        acc1 = p0 + j == 0 ? w1 : __fadd_rn(acc1, w1);
+                for (int q = 0; q < 8; ++q) {
+                    const int p = p0 + q;
+                    if (p >= np || fail) break;
+                    const float v = __uint_as_float(static_cast<uint32_t>(w[q]));
+                    if (p < k) {
+                        const float wv = __fmul_rn(v, R.wt[p]);
+                        acc = p == 0 ? wv : __fadd_rn(acc, wv);
+                    } else {
+                        acc = __fadd_rn(acc, v);
                     }
-                }
-                if (hs) {
-                    acc0 = __fadd_rn(acc0, sh0);
-                    acc1 = __fadd_rn(acc1, sh1);
-                }
-                if (ok0) {
-                    Lr.out[r0] = acc0;
-                    if (Lr.x_next) Lr.x_next[r0] = __fadd_rn(x0, acc0);
-                }
-                if (ok1) {
-                    Lr.out[r1] = acc1;
-                    if (Lr.x_next) Lr.x_next[r1] = __fadd_rn(x1, acc1);
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    atomicExch(&a.rowcnt[b], 0u);
-                    red_release_gpu_add(&a.gbar[2], 1u);
                 }
             }
+            if (fail) {
+                if (lane == 0) {
+                    set_error(a.err, DERR_TIMEOUT_TAG);
+                    LC.halt = 1u;
+                }
+                break;
+            }
+            if (ok) {
+                // x_l: layer l - 1's tagged values for a chained layer, else the input
+                const float x = l > 0 && Lr.chained
+                                    ? __uint_as_float(static_cast<uint32_t>(
+                                          ld_relaxed_u64(a.xtag + static_cast<int64_t>(l & 1) * H + r)))
+                                    : __ldcg(Lr.x + r);
+                const float xn = __fadd_rn(x, acc);
+                Lr.out[r] = acc;
+                if (Lr.x_next) Lr.x_next[r] = xn;
+                st_relaxed_u64(a.xtag + static_cast<int64_t>((l + 1) & 1) * H + r, tagged(xn, tag));
+            }
+            ST_MARK(l, 40 + (warp & 3));
         }
         if (warp == 0) ST_MARK(l, 6);
     }
@@ -441,7 +494,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
     //      clears the layer counter ---------------------------------------------
     if (tid == 0 && atomicAdd(&a.gbar[1], 1u) == gridDim.x - 1) {
         atomicExch(&a.gbar[1], 0u);
-        atomicExch(&a.gbar[2], 0u);
         atomicAdd(&a.gbar[0], static_cast<uint32_t>(L));
     }
 }
