@@ -84,7 +84,16 @@ int launch_stack(int type, StackArgs &a, cudaStream_t st, const char **why, cuda
     if (fit < 2) { *why = "activations and tiles do not fit in shared memory"; return -2; }
     const int nw = fit < GEMV_CONSUMER_WARPS ? fit : GEMV_CONSUMER_WARPS;
     a.n_tile_warps = nw;
-    a.n_stages = fit;   // stage g % S and warp g % nw need not line up
+    // A parity wait cannot tell phase p of a stage from phase p + 2. Tile g
+    // of a stage follows tile g - S there; if g - S lies in an earlier phase
+    // of the layer (gate/up or down), every consumer warp has passed it
+    // behind a CTA barrier, so any warp may take g. Otherwise the warp that
+    // took g - S must take g too: S a multiple of nw.
+    const int nu = a.k + (a.has_shared ? 1 : 0);
+    const int cmin = 1 + (grid - nu) / nu;                      // smallest CTA group
+    const int max_a = ((a.gu.nrows + cmin - 1) / cmin + a.gu.rows_per_tile - 1) / a.gu.rows_per_tile;
+    const int max_b = ((a.dn.nrows + cmin - 1) / cmin + a.dn.rows_per_tile - 1) / a.dn.rows_per_tile;
+    a.n_stages = max_a <= fit && max_b <= fit ? fit : fit / nw * nw;
     a.gu.n_tile_warps = nw;
     a.dn.n_tile_warps = nw;
     smem = static_cast<size_t>(a.ctrl_bytes) + a.act_bytes + static_cast<size_t>(a.n_stages) * a.stage_bytes;

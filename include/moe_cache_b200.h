@@ -349,9 +349,12 @@ int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap,
  * NULL) has a non-null entry, x_next[l] = x[l] + out[l] -- so x[l + 1] may be
  * x_next[l] and the layers form a residual chain: every layer starts only
  * after the previous layer's output is complete. Each layer computes what
- * moe_b200_layer_decode computes for one token (same bits). One launch keeps
- * the code warm in the instruction caches across layers, has no launch gaps,
- * and lets the shared expert's weights of the next layer stream early.
+ * moe_b200_layer_decode computes for one token (same bits). The router logits
+ * of every layer are inputs, so each CTA routes layer l + 1 and streams its
+ * weights while layer l computes; consecutive layers hand over through tagged
+ * words in the workspace (no atomics, no grid barrier). One launch also keeps
+ * the code warm in the instruction caches and has no launch gaps. Up to 32
+ * picks per layer.
  * Requirements: gate, up and down of one type (Q2_K..Q6_K, Q4_0, Q5_0, Q8_0,
  * Q5_K), every layer with layer 0's shapes, types, GLU and shared-expert
  * presence, expert tensors contiguous and 16-byte aligned in device memory
@@ -385,8 +388,10 @@ int moe_b200_stack_run(const moe_layer_desc *layer0, int64_t n_layers, void *wor
  * buffered by call parity) and waits for all of them; routes every token;
  * runs its own experts for every token that picked them (per-expert CTA
  * groups) and the shared expert for its own token; writes each routed down
- * row into the token's GPU and counts it there; and sums its own token's
- * rows in pick order once they have all arrived. Waits for other GPUs are
+ * row into the token's GPU; and sums its own token's rows in pick order once
+ * they have all arrived. Every value crosses as one 64-bit word (f32 bits |
+ * call tag << 32), so a reader that sees the tag sees the value: no fences,
+ * no counters. Waits for other GPUs are
  * bounded by the exchange limit of moe_b200_set_wait_limits (device error
  * MOE_DERR_TIMEOUT_FULL). Every GPU must make the same sequence of calls.
  * Workspace: moe_b200_layer_workspace_size(layer, world) bytes, zero-filled
