@@ -1,19 +1,34 @@
 """Stage-by-stage comparison of a GPU MoE layer decode with the CPU oracle.
 
-The layer re-quantizes its f32 intermediates (the GLU output h feeds the down
-projection as Q8_K / Q8_0 activations). The GPU's and the CPU's f32 h differ in
-the last bit, and at a rounding near-tie that flips one int8 activation by one
-step, so the end-to-end output may differ by ~1e-3 of its max with both sides
-correct. The stages are therefore checked against oracle stages fed the GPU's
-own inputs (tight, STAGE_TOL), and the end-to-end output against the pure
-oracle with LAYER_TOL."""
+Every stage is checked against the oracle's stage fed the GPU's own inputs
+(STAGE_TOL: only f32 summation order differs). End to end, each token's
+output is held to LAYER_TOL = 1e-3 of its max |ref| -- unless the GPU's and
+the CPU's h quantize differently for the down projection. The layer
+re-quantizes its f32 intermediates (the GLU output h feeds the down
+projection as Q8_K / Q8_0 activations); the two f32 h differ in the last
+bit, and at a rounding near-tie that moves one int8 activation (or a block
+scale) by one step, which moves the output by up to a few 1e-3 of its max
+with both sides correct. Such a token must show that difference (bytes of
+the quantized h that differ) and stay within NEAR_TIE_TOL."""
 import numpy as np
 
 import oracle as O
 from moe_data import rel_err
 
 STAGE_TOL = 1e-4
-LAYER_TOL = 1e-2
+LAYER_TOL = 1e-3
+NEAR_TIE_TOL = 1e-2
+
+
+def requant_diff(t_down, h_gpu, h_ref):
+    """Bytes of the down projection's activation blocks (Q8_K or Q8_0 of h)
+    that differ between the GPU's h and the oracle's, summed over every axis
+    but the first (tokens)."""
+    at = O.vec_dot_type(t_down)
+    a = O.quantize_act(at, np.ascontiguousarray(h_gpu, dtype=np.float32))
+    b = O.quantize_act(at, np.ascontiguousarray(h_ref, dtype=np.float32))
+    d = (a != b).reshape(a.shape[0], -1)
+    return d.sum(axis=1)
 
 
 def check_layer(layer, L, x, logits, out):
@@ -27,20 +42,30 @@ def check_layer(layer, L, x, logits, out):
     H, F = L["H"], L["F"]
     g = O.mul_mat_id(tg, L["gate"], H, x[:, None], ids)
     u = O.mul_mat_id(tu, L["up"], H, x[:, None], ids)
-    errs = {"h": rel_err(h, O.glu(O.GLU_SWIGLU, g, u))}
+    h_ref = O.glu(O.GLU_SWIGLU, g, u)
+    errs = {"h": rel_err(h, h_ref)}
     errs["y"] = rel_err(y, O.mul_mat_id(td, L["down"], F, h, ids))         # down on the GPU's own h
+    flips = requant_diff(td, h, h_ref)
     if L.get("shared_gate") is not None:
         z = np.zeros((n_tok, 1), np.int32)
         sg = O.mul_mat_id(tg, L["shared_gate"][None], H, x[:, None], z)[:, 0]
         su = O.mul_mat_id(tu, L["shared_up"][None], H, x[:, None], z)[:, 0]
-        errs["hs"] = rel_err(hs, O.glu(O.GLU_SWIGLU, sg, su))
+        hs_ref = O.glu(O.GLU_SWIGLU, sg, su)
+        errs["hs"] = rel_err(hs, hs_ref)
         errs["ys"] = rel_err(ys, O.mul_mat_id(td, L["shared_down"][None], F, hs[:, None], z)[:, 0])
+        flips = flips + requant_diff(td, hs, hs_ref)
         comb = (y * w[:, :, None]).sum(1) + ys
     else:
         comb = (y * w[:, :, None]).sum(1)
     errs["combine"] = rel_err(out, comb)
-    errs["layer"] = rel_err(out, ref)
+    per_tok = np.array([rel_err(out[t], ref[t]) for t in range(n_tok)])
+    errs["layer"] = float(per_tok.max())
     for k_, v in errs.items():
-        tol = LAYER_TOL if k_ == "layer" else STAGE_TOL
-        assert v < tol, (k_, v, errs)
+        if k_ != "layer":
+            assert v < STAGE_TOL, (k_, v, errs)
+    for t in range(n_tok):
+        ok = per_tok[t] < LAYER_TOL or (flips[t] > 0 and per_tok[t] < NEAR_TIE_TOL)
+        assert ok, ("layer", t, per_tok[t], int(flips[t]), errs)
+    errs["per_token"] = per_tok
+    errs["requant_bytes_differing"] = flips
     return errs

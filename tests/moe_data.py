@@ -37,3 +37,36 @@ def rel_err(got, ref):
     num = np.abs(got - ref).max(axis=-1)
     den = np.maximum(np.abs(ref).max(axis=-1), 1e-30)
     return float((num / den).max())
+
+
+def act_quant_sigma(t, W, K, x, ids):
+    """Standard deviation of (result with Q8_1 activations) - (result with
+    llama.cpp's CPU activations: Q8_K per 256 for K-quants, Q8_0 per 32
+    otherwise) for every output [n_tok][n_used][rows] of a MUL_MAT_ID with
+    one input row per token (x f32 [n_tok][K]). Both sides dot the same
+    weights w (dequantized rows) with x rounded to their own grid; modelled
+    as independent errors:
+      * element rounding, uniform in +-d/2 with d the block's step
+        (amax / 127): variance w_i^2 (d1_i^2 + dc_i^2) / 12;
+      * the f16 block scales of Q8_1 and Q8_0 (relative error uniform in
+        +-2^-11): variance (sum over the block of w_i x_i)^2 * 2^-22 / 3.
+    No test assumes more than this model."""
+    import oracle as O
+    x = np.asarray(x, dtype=np.float64)
+    n_tok = x.shape[0]
+    step = {}
+    for name, blk in (("q8_1", 32), ("cpu", 256 if O.vec_dot_type(t) == O.Q8_K else 32)):
+        xb = x.reshape(n_tok, K // blk, blk)
+        d = np.abs(xb).max(axis=2) / 127.0
+        step[name] = (np.repeat(d, blk, axis=1), blk)
+    var_el = (step["q8_1"][0] ** 2 + step["cpu"][0] ** 2) / 12.0            # [n_tok][K]
+    f16_cpu = O.vec_dot_type(t) == O.Q8_0
+    out = np.zeros(ids.shape + (W.shape[1],))
+    for ti in range(n_tok):
+        for p in range(ids.shape[1]):
+            w = O.dequantize(t, W[ids[ti, p]], K).astype(np.float64)          # [rows][K]
+            v = (w ** 2) @ var_el[ti]
+            wx = (w * x[ti][None, :]).reshape(w.shape[0], K // 32, 32).sum(axis=2)
+            v += (wx ** 2).sum(axis=1) * (2.0 ** -22) / 3.0 * (2 if f16_cpu else 1)
+            out[ti, p] = np.sqrt(v)
+    return out

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle as O
-from layer_check import LAYER_TOL, STAGE_TOL
+from layer_check import LAYER_TOL, NEAR_TIE_TOL, STAGE_TOL, requant_diff
 from moe_data import activations, experts, rel_err, zipf_logits
 
 pytestmark = pytest.mark.gpu
@@ -68,9 +68,18 @@ def test_layer_prefill_matches_oracle(pkg, cuda, types, n_tok, shared):
         errs["ys"] = rel_err(ys, O.mul_mat_id(td, L["shared_down"][None], F, hs[:, None], z)[:, 0])
         comb = comb + ys
     errs["combine"] = rel_err(out, comb)
-    errs["layer"] = rel_err(out, ref)
     for k_, v in errs.items():
-        assert v < (LAYER_TOL if k_ == "layer" else STAGE_TOL), (k_, v, errs)
+        assert v < STAGE_TOL, (k_, v, errs)
+    # end to end per token: 1e-3, or a near-tie in the re-quantized h (the
+    # oracle's h from its own gate) and 1e-2
+    g_ref = O.mul_mat_id(tg, L["gate"], H, x[:, None], ids)
+    flips = requant_diff(td, h, O.glu(O.GLU_SWIGLU, g_ref, u))
+    if shared:
+        sg_ref = O.mul_mat_id(tg, L["shared_gate"][None], H, x[:, None], z)[:, 0]
+        flips = flips + requant_diff(td, hs, O.glu(O.GLU_SWIGLU, sg_ref, su))
+    for t in range(n_tok):
+        e = rel_err(out[t], ref[t])
+        assert e < LAYER_TOL or (flips[t] > 0 and e < NEAR_TIE_TOL), (t, e, int(flips[t]), errs)
 
 
 def test_layer_prefill_agrees_with_decode(pkg, cuda):
@@ -83,5 +92,11 @@ def test_layer_prefill_agrees_with_decode(pkg, cuda):
     x = torch.from_numpy(activations((n_tok, H), seed=41)).to(cuda)
     lg = torch.from_numpy(zipf_logits(n_tok, E, seed=42)).to(cuda)
     a = layer.prefill(x, lg).cpu().numpy()
+    pa = [t.cpu().numpy() for t in layer.prefill_intermediates(n_tok)]
     b = layer.decode(x, lg).cpu().numpy()
-    assert rel_err(a, b) < LAYER_TOL
+    pb = [t.cpu().numpy() for t in layer.intermediates(n_tok)]
+    # h and the shared expert's hs of both paths, re-quantized for down
+    flips = requant_diff(O.Q2_K, pa[3], pb[2]) + requant_diff(O.Q2_K, pa[6], pb[3])
+    for t in range(n_tok):
+        e = rel_err(a[t], b[t])
+        assert e < LAYER_TOL or (flips[t] > 0 and e < NEAR_TIE_TOL), (t, e, int(flips[t]))
