@@ -272,6 +272,10 @@ template <> struct MmqType<T_Q4_K> {
     static constexpr int BPB = 144, NPLANE = 2, NT = 64;
     static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false;
 };
+template <> struct MmqType<T_Q5_K> {
+    static constexpr int BPB = 176, NPLANE = 2, NT = 64;
+    static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false;
+};
 template <> struct MmqType<T_Q6_K> {
     static constexpr int BPB = 210, NPLANE = 2, NT = 64;
     static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = true;
@@ -502,6 +506,56 @@ __device__ __forceinline__ void mmq_unpack<T_Q4_K>(const uint8_t *blk, uint32_t 
                 const uint32_t w = qs[8 * (c >> 2) + 4 * (c & 1) + i] >> (4 * nib);
                 const uint32_t ev = static_cast<uint32_t>(sc) * (w & 0x000F000Fu);          // elements 0, 2
                 const uint32_t od = static_cast<uint32_t>(sc) * ((w >> 8) & 0x000F000Fu);   // elements 1, 3
+                lo[4 * cc + i] = lo_bytes(ev, od);
+                hi[4 * cc + i] = hi_bytes(ev, od);
+            }
+        }
+        tmem_st16(a_cols + 32 * h + 16 * part, lo);
+        tmem_st16(a_cols + 64 + 32 * h + 16 * part, hi);
+    }
+    if (h == 0) {
+        uint32_t mb[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int sc, m;
+            q4K_scale_min(sw, j, sc, m);
+            mb[j >> 2] |= static_cast<uint32_t>(m) << (8 * (j & 3));
+        }
+        rs.m = make_uint2(mb[0], mb[1]);
+        rs.d = ld_half(blk);
+        rs.dm = ld_half(blk + 2);
+    }
+}
+
+// Q5_K (176 bytes: d, dmin, scales[12] (Q4_K's 6-bit scales and mins),
+// qh[32], qs[128]): element l of 64-element group j is the nibble (j's 32
+// bytes, low nibble for the group's first 32 elements, high for the rest)
+// plus 16 * bit (2 j + half) of qh[l % 32]; sc * q in [0, 1953] as two
+// unsigned planes; mins as Q4_K.
+template <>
+__device__ __forceinline__ void mmq_unpack<T_Q5_K>(const uint8_t *blk, uint32_t a_cols, int h, RowScales &rs) {
+    uint32_t sw[3], qs[16], qh[8];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) sw[i] = ld_u32(blk + 4 + 4 * i);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qh[i] = ld_u32(blk + 16 + 4 * i);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qs[i] = ld_u32(blk + 48 + 64 * h + 4 * i);
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            // chunk c as in Q4_K: group 2 h + c / 4, nibble (c / 2) % 2, bytes 16 (c % 2) .. + 15
+            const int c = 4 * part + cc, nib = (c >> 1) & 1, grp = 2 * h + (c >> 2);
+            int sc, m;
+            q4K_scale_min(sw, 4 * h + 2 * (c >> 2) + nib, sc, m);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w = (qs[8 * (c >> 2) + 4 * (c & 1) + i] >> (4 * nib)) & 0x0F0F0F0Fu;
+                const uint32_t q = w | (((qh[4 * (c & 1) + i] >> (2 * grp + nib)) & 0x01010101u) << 4);
+                const uint32_t ev = static_cast<uint32_t>(sc) * (q & 0x00FF00FFu);          // elements 0, 2
+                const uint32_t od = static_cast<uint32_t>(sc) * ((q >> 8) & 0x00FF00FFu);   // elements 1, 3
                 lo[4 * cc + i] = lo_bytes(ev, od);
                 hi[4 * cc + i] = hi_bytes(ev, od);
             }
@@ -899,6 +953,7 @@ int mmq_chunk_tokens(int type) {
         case T_Q2_K: return MmqType<T_Q2_K>::NT;
         case T_Q3_K: return MmqType<T_Q3_K>::NT;
         case T_Q4_K: return MmqType<T_Q4_K>::NT;
+        case T_Q5_K: return MmqType<T_Q5_K>::NT;
         case T_Q6_K: return MmqType<T_Q6_K>::NT;
         default: return 0;
     }
@@ -973,7 +1028,7 @@ int launch_mmq_t(MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cud
 int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err) {
     *cuda_err = cudaSuccess;
     if (!mmq_supported(type, a.K, a.nrows)) {
-        *why = "tensor-core prefill needs Q2_K/Q3_K/Q4_K/Q6_K, K % 256 == 0, K <= 4096, rows % 128 == 0";
+        *why = "tensor-core prefill needs Q2_K/Q3_K/Q4_K/Q5_K/Q6_K, K % 256 == 0, K <= 4096, rows % 128 == 0";
         return -2;
     }
     if (a.timeout_ns == 0) a.timeout_ns = 2000000000ull;
@@ -981,6 +1036,7 @@ int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaErro
         case T_Q2_K: return launch_mmq_t<T_Q2_K>(a, st, why, cuda_err);
         case T_Q3_K: return launch_mmq_t<T_Q3_K>(a, st, why, cuda_err);
         case T_Q4_K: return launch_mmq_t<T_Q4_K>(a, st, why, cuda_err);
+        case T_Q5_K: return launch_mmq_t<T_Q5_K>(a, st, why, cuda_err);
         default: return launch_mmq_t<T_Q6_K>(a, st, why, cuda_err);
     }
 }

@@ -263,7 +263,7 @@ int moe_b200_ep_layer_decode(const moe_layer_desc *layer, int64_t expert_lo, int
  * above its GEMV limit to llama.cpp's MMQ (patches/apply_patches.py:81-87):
  * dst[(t * k + p) * rows + r] = row r of expert ids[t * ids_stride + p] . x[t]
  * for n_tok tokens (x f32 [n_tok][ne00], contiguous, 16-byte aligned), with
- * llama.cpp CPU semantics (Q8_K activations). Q2_K, Q3_K, Q4_K and Q6_K
+ * llama.cpp CPU semantics (Q8_K activations). Q2_K, Q3_K, Q4_K, Q5_K and Q6_K
  * experts in device memory with rows a multiple of 128 and ne00 <= 4096 run
  * as a grouped int8 GEMM on the tensor cores (exact integer super-block dots;
  * Q2_K results equal the CPU path bit for bit, the others differ only in the

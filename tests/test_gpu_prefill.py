@@ -3,7 +3,7 @@ llama.cpp CPU MUL_MAT_ID (Q8_K activations).
 
 Q2_K on the tensor-core path computes each super-block's integer dot exactly
 and finishes it with llama.cpp's own float steps in the same order, so the
-result is compared bit for bit. Q3_K, Q4_K and Q6_K also have exact integer
+result is compared bit for bit. Q3_K, Q4_K, Q5_K and Q6_K also have exact integer
 super-block dots but sum them in float once per super-block where llama.cpp
 keeps 8 lane sums; those and the types without a tensor-core path (decode
 GEMV, in-kernel Q8_K) are held to max |gpu - ref| / max |ref| <= 1e-4 per
@@ -85,10 +85,14 @@ def test_prefill_q2k_repeat_same_result(pkg, cuda):
     (O.Q6_K, 256, 128, 4, 1, 33, 27),
     (O.Q6_K, 768, 256, 8, 2, 100, 28),     # 630-byte rows
     (O.Q6_K, 3072, 768, 32, 8, 64, 29),
+    (O.Q5_K, 256, 128, 4, 1, 1, 30),
+    (O.Q5_K, 512, 128, 8, 2, 70, 31),      # chunks of 64 + 6 on the hot expert
+    (O.Q5_K, 3072, 768, 32, 8, 64, 32),
+    (O.Q5_K, 768, 3072, 32, 8, 48, 33),
 ])
 def test_prefill_kquants_tensor_cores(pkg, cuda, t, K, rows, E, k, n_tok, seed):
-    """Q3_K / Q4_K / Q6_K on the tensor cores: exact integer dots, llama.cpp's
-    float steps up to the order of the sub-block sums"""
+    """Q3_K / Q4_K / Q5_K / Q6_K on the tensor cores: exact integer dots,
+    llama.cpp's float steps up to the order of the sub-block sums"""
     W = experts(t, E, rows, K, seed)
     x = activations((n_tok, K), seed + 10)
     ids = _zipf_ids(n_tok, E, k, seed + 20)
@@ -97,8 +101,8 @@ def test_prefill_kquants_tensor_cores(pkg, cuda, t, K, rows, E, k, n_tok, seed):
     assert rel_err(got, O.mul_mat_id(t, W, K, x[:, None, :], ids)) <= TIGHT
 
 
-@pytest.mark.parametrize("t,K,rows", [(O.Q5_K, 512, 256), (O.Q4_0, 256, 96), (O.Q8_0, 256, 128),
-                                      (O.Q2_K, 256, 192)])   # rows not a multiple of 128
+@pytest.mark.parametrize("t,K,rows", [(O.Q4_0, 256, 96), (O.Q8_0, 256, 128),
+                                      (O.Q2_K, 256, 192), (O.Q5_K, 512, 200)])   # rows not a multiple of 128
 def test_prefill_fallback_gemv(pkg, cuda, t, K, rows):
     E, k, n_tok = 8, 2, 19
     W = experts(t, E, rows, K, 12)
