@@ -81,6 +81,12 @@ cudaError_t launch_mmq_identity_chunks(int n, int ntc, int32_t *entries, int4 *c
 // tokens per chunk of the tensor-core path for a weight type (0: none)
 int mmq_chunk_tokens(int type);
 bool mmq_supported(int type, int64_t K, int64_t nrows);
+bool mmq_b32(int type);              // Q4_0 / Q5_0 / Q8_0: 32-weight blocks, Q8_0 activations
+int mmq_step(int type);              // weights per row and MMQ step (256, or 128 for Q8_0)
+uint32_t mmq_bt_stride(int type);    // bytes between B tiles
+cudaError_t launch_mmq_gather32(const uint8_t *x8, int K, int sk, int k, int ntc, const int32_t *entries,
+                                const int4 *chunks, const int32_t *n_chunks, int64_t max_chunks, uint8_t *btiles,
+                                uint32_t bt_stride, cudaStream_t st);
 int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
 
 }  // namespace moe

@@ -829,8 +829,13 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x
     w.max_chunks = moe::mmq_max_chunks(n_tok * k, E, chunk_tokens_for(src0, n_tok * k));
     w.chunks = reinterpret_cast<int4 *>(take(16 * static_cast<size_t>(w.max_chunks)));
     w.n_chunks = reinterpret_cast<int32_t *>(take(4));
-    w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(x_rows) * (K / 256) * 292));
-    w.btiles = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(w.max_chunks) * (K / 256) * moe::MMQ_BT_BYTES));
+    // activation rows: Q8_K (292 bytes / 256) or, for the 32-weight-block
+    // types, Q8_0 (34 bytes / 32); B tiles per (chunk, step)
+    const bool b32 = moe::mmq_b32(src0->type);
+    w.x8 = reinterpret_cast<uint8_t *>(take(static_cast<size_t>(x_rows) * (b32 ? (K / 32) * 34 : (K / 256) * 292)));
+    const int64_t steps = K / (b32 ? moe::mmq_step(src0->type) : 256);
+    w.btiles = reinterpret_cast<uint8_t *>(
+        take(static_cast<size_t>(w.max_chunks) * steps * (b32 ? moe::mmq_bt_stride(src0->type) : moe::MMQ_BT_BYTES)));
     w.bytes = off;
     return w;
 }
@@ -894,10 +899,17 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
         else
             CK(moe::launch_mmq_group(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), static_cast<int>(E),
                                      ntc, w.entries, w.chunks, w.n_chunks, g.d_err, st));
-        CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, x_rows, K, st));
         // the gather reads activation row entry / k_div (entry = t * k + p)
-        CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries,
-                                  w.chunks, w.n_chunks, w.max_chunks, w.btiles, st));
+        if (moe::mmq_b32(src0->type)) {
+            CK(moe::launch_quantize_act(MOE_TYPE_Q8_0, x, w.x8, x_rows, K, st));
+            CK(moe::launch_mmq_gather32(w.x8, static_cast<int>(K), moe::mmq_step(src0->type),
+                                        x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries, w.chunks, w.n_chunks,
+                                        w.max_chunks, w.btiles, moe::mmq_bt_stride(src0->type), st));
+        } else {
+            CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, x_rows, K, st));
+            CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries,
+                                      w.chunks, w.n_chunks, w.max_chunks, w.btiles, st));
+        }
         for (int pass = 0; pass < (pair ? 2 : 1); ++pass) {
             const moe_tensor *t = pass == 0 ? src0 : src2;
             moe::MmqArgs a{};
@@ -908,6 +920,7 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
             a.nrows = static_cast<int32_t>(rows);
             a.row_bytes = static_cast<uint32_t>(t->nb[1]);
             a.btiles = w.btiles;
+            a.bt_stride = moe::mmq_bt_stride(t->type);
             a.n_tok = static_cast<int32_t>(n_tok);
             a.k = static_cast<int32_t>(k);
             a.entries = w.entries;
@@ -1841,7 +1854,8 @@ int moe_b200_ep_experts_rows(const moe_layer_desc *L, const float *x, const int3
     read_env();
     if (!L || !x || !ids || !g_out || !u_out || !y || n_rows < 1) return fail(MOE_ERR_INVALID, "null argument");
     for (const moe_tensor *t : {&L->gate, &L->up, &L->down}) {
-        if (!moe::mmq_supported(t->type, t->ne[0], t->ne[1]) || !t->data || ptr_kind(t->data) != 2 || !contiguous(t) ||
+        if (!moe::mmq_supported(t->type, t->ne[0], t->ne[1]) || moe::mmq_b32(t->type) || !t->data ||
+            ptr_kind(t->data) != 2 || !contiguous(t) ||
             !aligned16(t->data) || (t->nb[2] % 16) != 0 || t->ne[2] != L->n_experts)
             return fail(MOE_ERR_UNSUPPORTED, "expert-parallel rows need tensor-core types in device memory");
     }

@@ -189,6 +189,49 @@ __global__ void __launch_bounds__(256) mmq_gather_q8K_kernel(const uint8_t *__re
 }
 
 
+// B tiles of the 32-weight-block types, per chunk and step of sk values:
+// the tokens' Q8_0 block scales (f16 -> float, [MMQ_NT32][8], blocks of the
+// step), then the quants in the MMA's K-major layout (16-byte chunk c of
+// token j at MMQ_BT32_HEAD + c * 16 N + (j / 8) * 128 + (j % 8) * 16). Copied
+// from the tokens' Q8_0 rows x8 (34-byte blocks), one warp per token slot.
+__global__ void __launch_bounds__(256) mmq_gather_q80_kernel(const uint8_t *__restrict__ x8, int K, int sk, int k,
+                                                             int ntc, const int32_t *__restrict__ entries,
+                                                             const int4 *__restrict__ chunks,
+                                                             const int32_t *__restrict__ n_chunks,
+                                                             uint8_t *__restrict__ btiles, uint32_t bt_stride) {
+    const int lane = threadIdx.x & 31;
+    const int nsb = K / sk, nb = sk / 32, per = sk / 32;   // bytes per lane and step: sk / 32
+    const int n_items = *n_chunks * ntc;
+    for (int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wg < n_items; wg += (gridDim.x * blockDim.x) >> 5) {
+        const int gc = wg / ntc, j = wg - gc * ntc;
+        const int4 ch = chunks[gc];
+        const int nt = ch.z, N = mmq_chunk_n(nt), CS = 16 * N;
+        if (j >= N) continue;
+        const int t = j < nt ? entries[ch.y + j] / k : -1;
+        const uint8_t *row = x8 + static_cast<size_t>(t < 0 ? 0 : t) * (K / 32) * 34;
+        for (int sb = 0; sb < nsb; ++sb) {
+            uint8_t *bt = btiles + (static_cast<size_t>(gc) * nsb + sb) * bt_stride;
+            const int e = lane * per, b = e / 32, o = e % 32;
+            uint32_t w[2] = {0u, 0u};
+            if (t >= 0) {
+                const uint8_t *q = row + static_cast<size_t>(sb * nb + b) * 34 + 2 + o;
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+                    if (4 * i < per)
+                        w[i] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(q + 4 * i)) |
+                               (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(q + 4 * i + 2)) << 16);
+            }
+            uint8_t *dst = bt + MMQ_BT32_HEAD + (e / 16) * CS + (j >> 3) * 128 + (j & 7) * 16 + (e % 16);
+            if (per == 8) *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+            else *reinterpret_cast<uint32_t *>(dst) = w[0];
+            if (lane < nb)
+                reinterpret_cast<float *>(bt)[8 * j + lane] =
+                    t >= 0 ? __half2float(*reinterpret_cast<const __half *>(row + static_cast<size_t>(sb * nb + lane) * 34))
+                           : 0.f;
+        }
+    }
+}
+
 // The same B tiles quantized here from f32 rows, one row per entry (k = 1):
 // row r = x[r], or with u set GLU(op, x[r], u[r]) (the down projection's
 // input made from the gate and up outputs); llama.cpp's quantize_row_q8_K_ref
@@ -258,27 +301,44 @@ __global__ void __launch_bounds__(256) mmq_gather_rows_kernel(const float *__res
 // epilogue) and the tokens per chunk (TMEM: two accumulator sets of
 // (planes + summs) x NT columns plus two A buffers of 64 columns per plane:
 // 512 columns at most).
+//
+// Q4_0, Q5_0 and Q8_0 (B32) carry one float scale per 32 weights and meet Q8_0
+// activations (one scale per 32 values): a step is SK weights per row (256,
+// or 128 for Q8_0's 34-byte blocks), each of its K = 32 MMAs goes to its own
+// accumulator, and the epilogue applies llama.cpp's per-block float steps.
 template <int TYPE>
 struct MmqType;
 template <> struct MmqType<T_Q2_K> {
-    static constexpr int BPB = 84, NPLANE = 1, NT = 64;
-    static constexpr bool MINS_TC = true, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = false;
+    static constexpr int BPB = 84, NPLANE = 1, NT = 64, SK = 256, BLK = 0;
+    static constexpr bool MINS_TC = true, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = false, B32 = false;
 };
 template <> struct MmqType<T_Q3_K> {
-    static constexpr int BPB = 110, NPLANE = 1, NT = 64;
-    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = true, P1_SIGNED = false;
+    static constexpr int BPB = 110, NPLANE = 1, NT = 64, SK = 256, BLK = 0;
+    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = true, P1_SIGNED = false, B32 = false;
 };
 template <> struct MmqType<T_Q4_K> {
-    static constexpr int BPB = 144, NPLANE = 2, NT = 64;
-    static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false;
+    static constexpr int BPB = 144, NPLANE = 2, NT = 64, SK = 256, BLK = 0;
+    static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false, B32 = false;
 };
 template <> struct MmqType<T_Q5_K> {
-    static constexpr int BPB = 176, NPLANE = 2, NT = 64;
-    static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false;
+    static constexpr int BPB = 176, NPLANE = 2, NT = 64, SK = 256, BLK = 0;
+    static constexpr bool MINS_TC = false, MINS_DP = true, P0_SIGNED = false, P1_SIGNED = false, B32 = false;
 };
 template <> struct MmqType<T_Q6_K> {
-    static constexpr int BPB = 210, NPLANE = 2, NT = 64;
-    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = true;
+    static constexpr int BPB = 210, NPLANE = 2, NT = 64, SK = 256, BLK = 0;
+    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = false, P1_SIGNED = true, B32 = false;
+};
+template <> struct MmqType<T_Q4_0> {
+    static constexpr int BLK = 18, SK = 256, BPB = BLK * SK / 32, NPLANE = 1, NT = MMQ_NT32;
+    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = true, P1_SIGNED = false, B32 = true;
+};
+template <> struct MmqType<T_Q5_0> {
+    static constexpr int BLK = 22, SK = 256, BPB = BLK * SK / 32, NPLANE = 1, NT = MMQ_NT32;
+    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = true, P1_SIGNED = false, B32 = true;
+};
+template <> struct MmqType<T_Q8_0> {
+    static constexpr int BLK = 34, SK = 128, BPB = BLK * SK / 32, NPLANE = 1, NT = MMQ_NT32;
+    static constexpr bool MINS_TC = false, MINS_DP = false, P0_SIGNED = true, P1_SIGNED = false, B32 = true;
 };
 
 // Shared-memory and TMEM layout of one CTA for weight type TYPE. TMEM
@@ -298,15 +358,16 @@ struct MmqLayout {
     static constexpr int NP = NP_FIT > 8 ? 8 : NP_FIT;                   // weight stages
     static constexpr uint32_t TOTAL = OFF_P + NP * STAGE;
     static constexpr uint32_t SUMMS_COL = Ty::NPLANE * Ty::NT;           // summs plane within a set
-    static constexpr uint32_t ACC_COLS = SUMMS_COL + (Ty::MINS_TC ? Ty::NT : 0);
+    // B32: one accumulator of NT columns per 32-weight block of the step
+    static constexpr uint32_t ACC_COLS = Ty::B32 ? (Ty::SK / 32) * Ty::NT : SUMMS_COL + (Ty::MINS_TC ? Ty::NT : 0);
     static constexpr uint32_t A_COL0 = 2 * ACC_COLS;
     static constexpr uint32_t MINS_COL = Ty::NPLANE * 64;                // Q2_K mins within an A buffer
-    static constexpr uint32_t A_COLS = MINS_COL + (Ty::MINS_TC ? 8 : 0);
+    static constexpr uint32_t A_COLS = Ty::B32 ? Ty::SK / 4 : MINS_COL + (Ty::MINS_TC ? 8 : 0);
     static_assert(NP >= 2, "at least two weight stages");
     static_assert(TOTAL <= 227u * 1024u, "shared memory budget");
     static_assert(A_COL0 + 2 * A_COLS <= 512, "TMEM columns");
     static_assert(SLOT % 16 == 0 && SLOT <= 256, "TMA box width");
-    static_assert(Ty::NT == 32 || Ty::NT == 64, "chunk width");
+    static_assert(Ty::NT == 32 || Ty::NT == 64 || (Ty::B32 && Ty::NT == MMQ_NT32), "chunk width");
 };
 
 // Warp roles: warps 0-7 finish the accumulators (warp w reads TMEM lanes
@@ -332,9 +393,17 @@ struct MmqCtrl {   // fits MmqLayout::CTRL (static_assert in the kernel)
     uint32_t tmem;
     int32_t abort;             // a wait timed out somewhere: every role stops
     alignas(16) float da[MMQ_RING][MMQ_NT];
-    alignas(16) int16_t bs2[MMQ_RING][MMQ_NT][8];   // Q4_K: the tokens' 32-value bsum pairs
-    float2 rs[MMQ_RING][MMQ_M];                      // the rows' d, dmin
-    uint2 rm[MMQ_RING][MMQ_M];                       // Q4_K: the rows' 8 mins (bytes)
+    union {
+        alignas(16) int16_t bs2[MMQ_RING][MMQ_NT][8];        // Q4_K / Q5_K: the tokens' 32-value bsum pairs
+        alignas(16) float da32[MMQ_RING][MMQ_NT32][8];       // B32: the tokens' block scales
+    };
+    union {
+        struct {
+            float2 rs[MMQ_RING][MMQ_M];                      // the rows' d, dmin
+            uint2 rm[MMQ_RING][MMQ_M];                       // Q4_K / Q5_K: the rows' 8 mins (bytes)
+        };
+        __half rd[MMQ_RING][MMQ_M][8];                       // B32: the rows' block scales
+    };
 };
 
 struct MmqTile {
@@ -577,6 +646,51 @@ __device__ __forceinline__ void mmq_unpack<T_Q5_K>(const uint8_t *blk, uint32_t 
     }
 }
 
+// ---- the 32-weight-block types: half h of a step holds blocks
+// [h NB / 2, (h + 1) NB / 2) of the row (NB = SK / 32), each 32 signed int8
+// weights into 8 TMEM columns; the blocks' f16 scales go to rd[b]. Block
+// starts are 2-byte aligned (18-, 22- and 34-byte blocks).
+__device__ __forceinline__ uint32_t ld_u16x2(const uint8_t *p) {
+    return static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(p)) |
+           (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(p + 2)) << 16);
+}
+
+template <int TYPE>
+__device__ __forceinline__ void mmq_unpack32(const uint8_t *step, uint32_t a_cols, int h, __half *rd) {
+    using Ty = MmqType<TYPE>;
+    constexpr int NB = Ty::SK / 32, BLK = Ty::BLK;
+#pragma unroll
+    for (int bb = 0; bb < NB / 2; ++bb) {
+        const int b = h * (NB / 2) + bb;
+        const uint8_t *blk = step + b * BLK;
+        uint32_t v[8];
+        if constexpr (TYPE == T_Q4_0) {
+            // qs[16] at 2: element j = low nibble of qs[j] - 8, element 16 + j = high nibble - 8
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w = ld_u16x2(blk + 2 + 4 * i);
+                v[i] = __vsub4(w & 0x0F0F0F0Fu, 0x08080808u);
+                v[4 + i] = __vsub4((w >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+            }
+        } else if constexpr (TYPE == T_Q5_0) {
+            // qh (32 bits) at 2, qs[16] at 6: the fifth bit of element j is qh bit j
+            const uint32_t qh = ld_u16x2(blk + 2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w = ld_u16x2(blk + 6 + 4 * i);
+                v[i] = __vsub4((w & 0x0F0F0F0Fu) | spread4_bit4(qh >> (4 * i)), 0x10101010u);
+                v[4 + i] = __vsub4(((w >> 4) & 0x0F0F0F0Fu) | spread4_bit4(qh >> (16 + 4 * i)), 0x10101010u);
+            }
+        } else {
+            // Q8_0: qs[32] (int8) at 2
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = ld_u16x2(blk + 2 + 4 * i);
+        }
+        tmem_st8(a_cols + 8 * b, v);
+        rd[b] = *reinterpret_cast<const __half *>(blk);
+    }
+}
+
 // Q6_K (210 bytes: ql[128], qh[64], scales[16] (int8), d): sc * (q - 32) in
 // [-4064, 4096] as two planes (low byte unsigned, high byte signed).
 template <>
@@ -639,7 +753,7 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
     uint8_t *B = smem + Lay::OFF_B;
     uint8_t *P = smem + Lay::OFF_P;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nsb = a.K / 256;
+    const int nsb = a.K / Ty::SK;
     const int row_blocks = a.nrows / MMQ_M;
     const int total = *a.n_chunks * row_blocks;
     const int G = a.G, GR = MMQ_M / a.G;     // rows per tensor-map row; tensor-map rows per box
@@ -682,14 +796,14 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
         for (int ti = blockIdx.x; ti < total && pok; ti += gridDim.x) {
             const MmqTile T = mmq_tile(ch, ti, row_blocks);
             if (ti + static_cast<int>(gridDim.x) < total) ch = a.chunks[(ti + gridDim.x) / row_blocks];   // next tile's chunk
-            const uint32_t bbytes = mmq_bt_bytes(mmq_chunk_n(T.nt));
+            const uint32_t bbytes = Ty::B32 ? mmq_bt32_bytes(mmq_chunk_n(T.nt), Ty::SK) : mmq_bt_bytes(mmq_chunk_n(T.nt));
             const int y0 = (T.e * a.nrows + T.rb * MMQ_M) / G;   // first tensor-map row of the tile
             for (int sb = 0; sb < nsb; ++sb) {
                 bool w = lane == 0 ? mmq_wait(C, &C.b_empty[bs], bph ^ 1u, a) : true;
                 if (!__shfl_sync(0xffffffffu, w, 0)) { pok = false; break; }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&C.b_full[bs], bbytes);
-                    bulk_g2s(B + bs * MMQ_BT_BYTES, a.btiles + (static_cast<size_t>(T.gchunk) * nsb + sb) * MMQ_BT_BYTES,
+                    bulk_g2s(B + bs * MMQ_BT_BYTES, a.btiles + (static_cast<size_t>(T.gchunk) * nsb + sb) * a.bt_stride,
                              bbytes, &C.b_full[bs], pol_b);
                 }
                 ++fills_b;
@@ -739,14 +853,21 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t a0 = tmem + Lay::A_COL0 + par * Lay::A_COLS;
-                    const uint32_t b0 = smem_u32(B + bs * MMQ_BT_BYTES) + MMQ_BT_HEAD;
+                    const uint32_t b0 = smem_u32(B + bs * MMQ_BT_BYTES) + (Ty::B32 ? MMQ_BT32_HEAD : MMQ_BT_HEAD);
                     const uint32_t d0 = tmem + par * Lay::ACC_COLS;
+                    if constexpr (Ty::B32) {
+                        // one accumulator per 32-weight block (its own float scales)
 #pragma unroll
-                    for (int p = 0; p < Ty::NPLANE; ++p)
+                        for (int kk = 0; kk < Ty::SK / 32; ++kk)
+                            umma_i8_ts(d0 + kk * NT, a0 + 8 * kk, umma_desc(b0 + kk * 2 * bcs, bcs, 128), id0, 0u);
+                    } else {
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk)
-                            umma_i8_ts(d0 + p * NT, a0 + p * 64 + 8 * kk, umma_desc(b0 + kk * 2 * bcs, bcs, 128),
-                                       p == 0 ? id0 : id1, kk > 0 ? 1u : 0u);
+                        for (int p = 0; p < Ty::NPLANE; ++p)
+#pragma unroll
+                            for (int kk = 0; kk < 8; ++kk)
+                                umma_i8_ts(d0 + p * NT, a0 + p * 64 + 8 * kk, umma_desc(b0 + kk * 2 * bcs, bcs, 128),
+                                           p == 0 ? id0 : id1, kk > 0 ? 1u : 0u);
+                    }
                     if (Ty::MINS_TC)   // summs = sum_g (16 m_g) hi_g + m_g lo_g
                         umma_i8_ts(d0 + Lay::SUMMS_COL, a0 + Lay::MINS_COL, umma_desc(b0 + 16 * bcs, bcs, 128),
                                    mmq_idesc(false, N), 0u);
@@ -778,23 +899,32 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                 if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
                 tc_fence_after();
                 const uint8_t *slot = P + ps * Lay::STAGE + slot_off + ((row_in_group + static_cast<uint32_t>(sb) * BPB) & 15u);
-                RowScales rsc{};
-                mmq_unpack<TYPE>(slot, a_lane + (g & 1u) * Lay::A_COLS, h, rsc);
-                if (h == 0) {
-                    C.rs[g % MMQ_RING][r] = make_float2(rsc.d, rsc.dm);
-                    if (Ty::MINS_DP) C.rm[g % MMQ_RING][r] = rsc.m;
+                if constexpr (Ty::B32) {
+                    mmq_unpack32<TYPE>(slot, a_lane + (g & 1u) * Lay::A_COLS, h, C.rd[g % MMQ_RING][r]);
+                } else {
+                    RowScales rsc{};
+                    mmq_unpack<TYPE>(slot, a_lane + (g & 1u) * Lay::A_COLS, h, rsc);
+                    if (h == 0) {
+                        C.rs[g % MMQ_RING][r] = make_float2(rsc.d, rsc.dm);
+                        if (Ty::MINS_DP) C.rm[g % MMQ_RING][r] = rsc.m;
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&C.p_empty[ps]);
                 if (++ps == Lay::NP) { ps = 0; pph ^= 1u; }
-                if (uw < 2) {   // rows 0-63 of half 0 copy the token scales
+                if (uw < (Ty::B32 ? 4 : 2)) {   // half 0 copies the token scales
                     ok = mmq_wait(C, &C.b_full[bs], bph, a);
                     if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
                     const uint8_t *Bst = B + bs * MMQ_BT_BYTES;
-                    C.da[g % MMQ_RING][r] = reinterpret_cast<const float *>(Bst)[r];
-                    if (Ty::MINS_DP)
-                        *reinterpret_cast<int4 *>(C.bs2[g % MMQ_RING][r]) =
-                            *reinterpret_cast<const int4 *>(Bst + MMQ_BT_BS2 + 16 * r);
+                    if constexpr (Ty::B32) {
+                        // token n = r / 8, block r % 8 (blocks past the step are not read)
+                        (&C.da32[g % MMQ_RING][0][0])[r] = reinterpret_cast<const float *>(Bst)[r];
+                    } else {
+                        C.da[g % MMQ_RING][r] = reinterpret_cast<const float *>(Bst)[r];
+                        if (Ty::MINS_DP)
+                            *reinterpret_cast<int4 *>(C.bs2[g % MMQ_RING][r]) =
+                                *reinterpret_cast<const int4 *>(Bst + MMQ_BT_BS2 + 16 * r);
+                    }
                 }
                 if (++bs == Lay::NB) { bs = 0; bph ^= 1u; }
                 tmem_wait_st();
@@ -803,6 +933,63 @@ __global__ void __launch_bounds__(MMQ_WS_THREADS, 1) moe_mmq_kernel(const __grid
                 if (lane == 0) {
                     mbar_arrive(&C.a_ready[g & 1u]);
                     mbar_arrive(&C.s_full[g % MMQ_RING]);
+                }
+            }
+        }
+    } else if constexpr (Ty::B32) {
+        // ---------------- epilogue warps, 32-weight blocks -------------------------
+        // thread: row r, tokens 8 half .. + 7; per block llama.cpp's float steps
+        // (Q4_0: sumi * dx * dy, Q5_0: (dx * dy) * sumi, Q8_0: sumi * (dx * dy)),
+        // blocks in order
+        constexpr int NB = Ty::SK / 32;
+        const int r = 32 * (warp & 3) + lane, half = warp >> 2;
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        uint32_t g = 0;
+        bool ok = true;
+        int4 ch = static_cast<int>(blockIdx.x) < total ? a.chunks[blockIdx.x / row_blocks] : make_int4(0, 0, 0, 0);
+        for (int ti = blockIdx.x; ti < total && ok; ti += gridDim.x) {
+            const MmqTile T = mmq_tile(ch, ti, row_blocks);
+            if (ti + static_cast<int>(gridDim.x) < total) ch = a.chunks[(ti + gridDim.x) / row_blocks];
+            for (int sb = 0; sb < nsb; ++sb, ++g) {
+                ok = mmq_wait(C, &C.s_full[g % MMQ_RING], (g / MMQ_RING) & 1u, a) &&
+                     mmq_wait(C, &C.mma_done[g & 1u], (g >> 1) & 1u, a);
+                if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t cols = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + (g & 1u) * Lay::ACC_COLS +
+                                      8u * static_cast<uint32_t>(half);
+                const __half *rdr = C.rd[g % MMQ_RING][r];
+                const float *das = &C.da32[g % MMQ_RING][8 * half][0];
+#pragma unroll
+                for (int kk = 0; kk < NB; ++kk) {
+                    uint32_t S[8];
+                    tmem_ld8(cols + kk * NT, S);
+                    tmem_wait_ld();
+                    const float dx = __half2float(rdr[kk]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float dy = das[8 * j + kk];
+                        const float si = __int2float_rn(static_cast<int>(S[j]));
+                        float t;
+                        if constexpr (TYPE == T_Q4_0) t = __fmul_rn(__fmul_rn(si, dx), dy);
+                        else if constexpr (TYPE == T_Q5_0) t = __fmul_rn(__fmul_rn(dx, dy), si);
+                        else t = __fmul_rn(si, __fmul_rn(dx, dy));
+                        acc[j] = __fadd_rn(acc[j], t);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&C.acc_empty[g & 1u]);
+                if (sb == nsb - 1) {
+                    const int row = T.rb * MMQ_M + r;
+                    const int32_t *ent = a.entries + T.first;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int n = 8 * half + j;
+                        if (n < T.nt) a.dst[static_cast<int64_t>(ent[n]) * a.nrows + row] = acc[j];
+                        acc[j] = 0.f;
+                    }
                 }
             }
         }
@@ -918,6 +1105,18 @@ cudaError_t launch_mmq_gather(const uint8_t *x8, int K, int k, int ntc, const in
     return cudaGetLastError();
 }
 
+cudaError_t launch_mmq_gather32(const uint8_t *x8, int K, int sk, int k, int ntc, const int32_t *entries,
+                                const int4 *chunks, const int32_t *n_chunks, int64_t max_chunks, uint8_t *btiles,
+                                uint32_t bt_stride, cudaStream_t st) {
+    int dev = 0, n_sm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t blocks = (max_chunks * ntc + 7) / 8;   // one warp per token slot, 8 warps a block
+    const int grid = static_cast<int>(blocks < 8 * n_sm ? (blocks > 0 ? blocks : 1) : 8 * n_sm);
+    mmq_gather_q80_kernel<<<grid, 256, 0, st>>>(x8, K, sk, k, ntc, entries, chunks, n_chunks, btiles, bt_stride);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_mmq_gather_rows(const float *x, const float *u, int glu_op, float glu_limit, int K,
                                    const int32_t *entries, const int4 *chunks, const int32_t *n_chunks, int ntc,
                                    int64_t max_chunks, uint8_t *btiles, cudaStream_t st) {
@@ -955,12 +1154,25 @@ int mmq_chunk_tokens(int type) {
         case T_Q4_K: return MmqType<T_Q4_K>::NT;
         case T_Q5_K: return MmqType<T_Q5_K>::NT;
         case T_Q6_K: return MmqType<T_Q6_K>::NT;
+        case T_Q4_0: return MmqType<T_Q4_0>::NT;
+        case T_Q5_0: return MmqType<T_Q5_0>::NT;
+        case T_Q8_0: return MmqType<T_Q8_0>::NT;
         default: return 0;
     }
 }
 
+bool mmq_b32(int type) { return type == T_Q4_0 || type == T_Q5_0 || type == T_Q8_0; }
+
+int mmq_step(int type) { return type == T_Q8_0 ? MmqType<T_Q8_0>::SK : 256; }
+
+uint32_t mmq_bt_stride(int type) {
+    return mmq_b32(type) ? (mmq_bt32_bytes(MMQ_NT32, mmq_step(type)) + 15u) / 16u * 16u : MMQ_BT_BYTES;
+}
+
 bool mmq_supported(int type, int64_t K, int64_t nrows) {
-    return mmq_chunk_tokens(type) > 0 && K % 256 == 0 && K / 256 <= MMQ_GATHER_MAX_SB && nrows % MMQ_M == 0;
+    if (mmq_chunk_tokens(type) <= 0 || nrows % MMQ_M != 0) return false;
+    if (mmq_b32(type)) return K % mmq_step(type) == 0 && K <= 8192;
+    return K % 256 == 0 && K / 256 <= MMQ_GATHER_MAX_SB;
 }
 
 namespace {
@@ -1028,11 +1240,16 @@ int launch_mmq_t(MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cud
 int launch_mmq(int type, MmqArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err) {
     *cuda_err = cudaSuccess;
     if (!mmq_supported(type, a.K, a.nrows)) {
-        *why = "tensor-core prefill needs Q2_K/Q3_K/Q4_K/Q5_K/Q6_K, K % 256 == 0, K <= 4096, rows % 128 == 0";
+        *why = "tensor-core prefill needs Q2_K..Q6_K (K % 256 == 0, K <= 4096) or Q4_0/Q5_0/Q8_0 (K <= 8192), "
+               "rows % 128 == 0";
         return -2;
     }
     if (a.timeout_ns == 0) a.timeout_ns = 2000000000ull;
+    if (a.bt_stride == 0) a.bt_stride = mmq_bt_stride(type);
     switch (type) {
+        case T_Q4_0: return launch_mmq_t<T_Q4_0>(a, st, why, cuda_err);
+        case T_Q5_0: return launch_mmq_t<T_Q5_0>(a, st, why, cuda_err);
+        case T_Q8_0: return launch_mmq_t<T_Q8_0>(a, st, why, cuda_err);
         case T_Q2_K: return launch_mmq_t<T_Q2_K>(a, st, why, cuda_err);
         case T_Q3_K: return launch_mmq_t<T_Q3_K>(a, st, why, cuda_err);
         case T_Q4_K: return launch_mmq_t<T_Q4_K>(a, st, why, cuda_err);

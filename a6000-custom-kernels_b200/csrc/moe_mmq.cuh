@@ -31,6 +31,7 @@ namespace moe {
 
 constexpr int MMQ_M = 128;                 // weight rows per tile (TMEM lanes)
 constexpr int MMQ_NT = 64;                 // tokens per chunk (MMA N)
+constexpr int MMQ_NT32 = 16;               // tokens per chunk for the 32-weight-block types
 constexpr int MMQ_CWARPS = 4;              // consumer warps: thread r owns row r
 constexpr int MMQ_THREADS = 32 * (MMQ_CWARPS + 1);
 constexpr int MMQ_BCHUNKS = 18;            // 16 chunks of quants + bsum hi + bsum lo (16 bytes per token each)
@@ -42,6 +43,10 @@ constexpr uint32_t MMQ_BT_BYTES = MMQ_BT_HEAD + MMQ_BCHUNKS * MMQ_NT * 16;
 // B tile of a chunk of nt tokens: N = nt rounded up to 16 token columns
 __host__ __device__ constexpr int mmq_chunk_n(int nt) { return (nt + 15) / 16 * 16; }
 __host__ __device__ constexpr uint32_t mmq_bt_bytes(int n) { return MMQ_BT_HEAD + MMQ_BCHUNKS * 16u * n; }
+// B tile of the 32-weight-block types (Q8_0 activations), step of sk values:
+// the tokens' block scales (float [MMQ_NT32][8]), then sk / 16 quant chunks
+constexpr uint32_t MMQ_BT32_HEAD = MMQ_NT32 * 8 * 4;
+__host__ __device__ constexpr uint32_t mmq_bt32_bytes(int n, int sk) { return MMQ_BT32_HEAD + (sk / 16) * 16u * n; }
 
 struct MmqArgs {
     CUtensorMap rows;               // uint8 [E * nrows / G][G * row_bytes], box {SLOT, 128 / G}
@@ -50,7 +55,8 @@ struct MmqArgs {
     uint64_t expert_bytes;
     int32_t n_experts, K, nrows;    // per expert: nrows rows of K values
     uint32_t row_bytes;
-    const uint8_t *btiles;          // [chunk][K / 256][MMQ_BT_BYTES], the first mmq_bt_bytes(N) used
+    const uint8_t *btiles;          // [chunk][K / step][bt_stride], the first mmq_bt_bytes(N) (or _bt32_) used
+    uint32_t bt_stride;             // bytes between consecutive B tiles
     int32_t n_tok, k;
     const int32_t *entries;         // entry = tok * k + pick, grouped by expert
     const int4 *chunks;             // [chunk] {expert, first entry, token count, -}; tile t is chunk t / (nrows / M)
@@ -165,6 +171,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr)
         : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 

@@ -36,7 +36,9 @@ def _cache(pkg, cuda):
                                                 ((O.Q3_K, O.Q3_K, O.Q6_K), 40, True),
                                                 ((O.Q4_K, O.Q4_K, O.Q2_K), 33, False),
                                                 ((O.Q6_K, O.Q4_K, O.Q3_K), 20, True),    # gate/up of different types
-                                                ((O.Q4_0, O.Q4_0, O.Q8_0), 12, True)])   # no tensor-core path: GEMV
+                                                ((O.Q4_0, O.Q4_0, O.Q8_0), 12, True),
+                                                ((O.Q5_0, O.Q5_0, O.Q4_0), 40, True),
+                                                ((O.Q5_K, O.Q5_K, O.Q5_0), 24, False)])
 def test_layer_prefill_matches_oracle(pkg, cuda, types, n_tok, shared):
     H, F, E, k = 1024, 512, 24, 8
     L = _layer_np(types, H, F, E, seed=sum(types) + n_tok, shared=shared)

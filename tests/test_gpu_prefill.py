@@ -3,7 +3,8 @@ llama.cpp CPU MUL_MAT_ID (Q8_K activations).
 
 Q2_K on the tensor-core path computes each super-block's integer dot exactly
 and finishes it with llama.cpp's own float steps in the same order, so the
-result is compared bit for bit. Q3_K, Q4_K, Q5_K and Q6_K also have exact integer
+result is compared bit for bit, as are Q4_0, Q5_0 and Q8_0 (per-block float
+steps against Q8_0 activations). Q3_K, Q4_K, Q5_K and Q6_K also have exact integer
 super-block dots but sum them in float once per super-block where llama.cpp
 keeps 8 lane sums; those and the types without a tensor-core path (decode
 GEMV, in-kernel Q8_K) are held to max |gpu - ref| / max |ref| <= 1e-4 per
@@ -101,7 +102,29 @@ def test_prefill_kquants_tensor_cores(pkg, cuda, t, K, rows, E, k, n_tok, seed):
     assert rel_err(got, O.mul_mat_id(t, W, K, x[:, None, :], ids)) <= TIGHT
 
 
-@pytest.mark.parametrize("t,K,rows", [(O.Q4_0, 256, 96), (O.Q8_0, 256, 128),
+@pytest.mark.parametrize("t,K,rows,E,k,n_tok,seed", [
+    (O.Q4_0, 32 * 8, 128, 4, 1, 1, 41),      # one step, one token
+    (O.Q4_0, 2048, 512, 16, 4, 70, 42),      # config-1 gate/up shape, chunks of 16 + ragged
+    (O.Q4_0, 512, 2048, 16, 4, 40, 43),      # config-1 down shape
+    (O.Q5_0, 768, 256, 8, 2, 100, 44),
+    (O.Q5_0, 3072, 768, 32, 8, 64, 45),
+    (O.Q8_0, 128, 128, 4, 1, 5, 46),         # one 128-value step
+    (O.Q8_0, 1024, 384, 8, 2, 33, 47),
+    (O.Q8_0, 3072, 768, 32, 8, 64, 48),
+])
+def test_prefill_block32_tensor_cores_bit_exact(pkg, cuda, t, K, rows, E, k, n_tok, seed):
+    """Q4_0 / Q5_0 / Q8_0 on the tensor cores against Q8_0 activations: exact
+    integer block dots, llama.cpp's per-block float steps in block order --
+    equal to the CPU path bit for bit"""
+    W = experts(t, E, rows, K, seed)
+    x = activations((n_tok, K), seed + 10)
+    ids = _zipf_ids(n_tok, E, k, seed + 20)
+    got, tc = _run(pkg, cuda, t, W, K, rows, x, ids)
+    assert tc
+    np.testing.assert_array_equal(got, O.mul_mat_id(t, W, K, x[:, None, :], ids))
+
+
+@pytest.mark.parametrize("t,K,rows", [(O.Q4_0, 256, 96), (O.Q8_0, 256, 100),
                                       (O.Q2_K, 256, 192), (O.Q5_K, 512, 200)])   # rows not a multiple of 128
 def test_prefill_fallback_gemv(pkg, cuda, t, K, rows):
     E, k, n_tok = 8, 2, 19
