@@ -81,6 +81,9 @@ cudaError_t launch_mmq_identity_chunks(int n, int ntc, int32_t *entries, int4 *c
 // tokens per chunk of the tensor-core path for a weight type (0: none)
 int mmq_chunk_tokens(int type);
 bool mmq_supported(int type, int64_t K, int64_t nrows);
+cudaError_t launch_mmq_pool_ids(const int32_t *ids, int64_t ids_stride, int n_tok, int k, char *const *tbl,
+                                int n_experts, const char *pool, uint64_t expert_bytes, int n_slots, int32_t *out,
+                                cudaStream_t st);
 bool mmq_b32(int type);              // Q4_0 / Q5_0 / Q8_0: 32-weight blocks, Q8_0 activations
 int mmq_step(int type);              // weights per row and MMQ step (256, or 128 for Q8_0)
 uint32_t mmq_bt_stride(int type);    // bytes between B tiles

@@ -507,6 +507,7 @@ struct MmvqCall {
     int64_t shared_y_stride_col = 0;
     int64_t id_offset = 0;                        // expert-parallel: first expert of this GPU
     int skip_foreign = 0;                         // expert-parallel: other GPUs' ids are skipped
+    int host_only = 0;                            // only picks of host-resident experts (prefill split)
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -588,6 +589,7 @@ int run_mmvq(const MmvqCall &c, cudaStream_t stream) {
     a.ids_stride = c.ids_stride;
     a.id_offset = static_cast<int32_t>(c.id_offset);
     a.skip_foreign = c.skip_foreign;
+    a.host_only = c.host_only;
     a.ncols_dst = static_cast<int32_t>(c.ncols_dst);
     a.nchannels_dst = static_cast<int32_t>(c.nchannels_dst);
     a.n_experts = e->n_experts;
@@ -804,6 +806,7 @@ bool layer_fusable(const moe_layer_desc *L, int64_t n_tok) {
 struct PrefillWs {
     uint8_t *x8, *btiles;
     int32_t *entries, *n_chunks;
+    int32_t *pool_ids;             // host-tiered tensors: each pick's pool slot (-1: host memory)
     int4 *chunks;
     int64_t max_chunks;
     size_t bytes;
@@ -829,6 +832,7 @@ PrefillWs prefill_ws(const moe_tensor *src0, int64_t n_tok, int64_t k, int64_t x
     w.max_chunks = moe::mmq_max_chunks(n_tok * k, E, chunk_tokens_for(src0, n_tok * k));
     w.chunks = reinterpret_cast<int4 *>(take(16 * static_cast<size_t>(w.max_chunks)));
     w.n_chunks = reinterpret_cast<int32_t *>(take(4));
+    w.pool_ids = reinterpret_cast<int32_t *>(take(4 * n_tok * k));
     // activation rows: Q8_K (292 bytes / 256) or, for the 32-weight-block
     // types, Q8_0 (34 bytes / 32); B tiles per (chunk, step)
     const bool b32 = moe::mmq_b32(src0->type);
@@ -866,7 +870,76 @@ int run_prefill(const moe_tensor *src0, const float *x, bool x_per_pick, int64_t
     const bool tc = tc_ok(src0);
     const bool pair = src2 && dst2 && tc && tc_ok(src2) && src2->type == src0->type && src2->ne[0] == K &&
                       src2->ne[1] == rows && src2->ne[2] == E;
-    if (!tc) {
+    // a host-tiered tensor: the picks of pool-resident experts on the tensor
+    // cores (the pool as the expert array, slots as expert ids), the others
+    // through the GEMV reading pinned host memory in place
+    Tensor *te = nullptr;
+    const bool tiered_tc = !tc && !reuse_groups && ptr_kind(src0->data) != 2 &&
+                           moe::mmq_supported(src0->type, K, rows) && n_tok * k < (int64_t{1} << 30) &&
+                           wants_locked(src0) && enroll(src0, st, &te) == MOE_OK && te && te->tiered && te->pool &&
+                           te->n_slots > 0 && te->expert_bytes % 16 == 0 && aligned16(te->pool);
+    if (tiered_tc) {
+        for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
+            const int64_t nt = n_tok - t0 < 8 ? n_tok - t0 : 8;
+            MmvqCall c;
+            c.src0 = src0;
+            c.src1 = x + t0 * (x_per_pick ? k : 1) * K;
+            c.src1_type = MOE_TYPE_F32;
+            c.ids = ids + t0 * ids_stride;
+            c.dst = dst + t0 * k * rows;
+            c.ne00 = K; c.ne01 = rows; c.ncols_dst = nt; c.s01 = static_cast<int64_t>(src0->nb[1]) / type_size(src0->type);
+            c.nchannels_y = x_per_pick ? k : 1; c.nchannels_dst = k;
+            c.stride_col_y = (x_per_pick ? k : 1) * K; c.stride_channel_y = x_per_pick ? K : 0;
+            c.stride_col_dst = k * rows; c.stride_channel_dst = rows;
+            c.ids_stride = ids_stride;
+            c.host_only = 1;
+            const int rc = run_mmvq(c, st);
+            if (rc) return rc;
+        }
+        const PrefillWs w = prefill_ws(src0, n_tok, k, x_rows, workspace);
+        if (!workspace || workspace_bytes < w.bytes)
+            return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, w.bytes);
+        int rc = ensure_device();
+        if (rc) return rc;
+        const int ntc = chunk_tokens_for(src0, n_tok * k);
+        CK(moe::launch_mmq_pool_ids(ids, ids_stride, static_cast<int>(n_tok), static_cast<int>(k), te->table,
+                                    te->n_experts, te->pool, te->expert_bytes, te->n_slots, w.pool_ids, st));
+        CK(moe::launch_mmq_group(w.pool_ids, k, static_cast<int>(n_tok), static_cast<int>(k), te->n_slots, ntc,
+                                 w.entries, w.chunks, w.n_chunks, g.d_err, st, true));
+        if (moe::mmq_b32(src0->type)) {
+            CK(moe::launch_quantize_act(MOE_TYPE_Q8_0, x, w.x8, x_rows, K, st));
+            CK(moe::launch_mmq_gather32(w.x8, static_cast<int>(K), moe::mmq_step(src0->type),
+                                        x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries, w.chunks, w.n_chunks,
+                                        w.max_chunks, w.btiles, moe::mmq_bt_stride(src0->type), st));
+        } else {
+            CK(moe::launch_quantize_act(MOE_TYPE_Q8_K, x, w.x8, x_rows, K, st));
+            CK(moe::launch_mmq_gather(w.x8, static_cast<int>(K), x_per_pick ? 1 : static_cast<int>(k), ntc, w.entries,
+                                      w.chunks, w.n_chunks, w.max_chunks, w.btiles, st));
+        }
+        moe::MmqArgs a{};
+        a.dense = te->pool;
+        a.expert_bytes = te->expert_bytes;
+        a.n_experts = te->n_slots;
+        a.K = static_cast<int32_t>(K);
+        a.nrows = static_cast<int32_t>(rows);
+        a.row_bytes = static_cast<uint32_t>(src0->nb[1]);
+        a.btiles = w.btiles;
+        a.bt_stride = moe::mmq_bt_stride(src0->type);
+        a.n_tok = static_cast<int32_t>(n_tok);
+        a.k = static_cast<int32_t>(k);
+        a.entries = w.entries;
+        a.chunks = w.chunks;
+        a.n_chunks = w.n_chunks;
+        a.dst = dst;
+        a.err = g.d_err;
+        a.timeout_ns = g.timeout_ns_kernel;
+        const char *why = "";
+        cudaError_t ce = cudaSuccess;
+        rc = moe::launch_mmq(src0->type, a, st, &why, &ce);
+        if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
+        if (rc) return fail(rc, "%s", why);
+        *used_tc = true;
+    } else if (!tc) {
         // no tensor-core path: the decode GEMV over chunks of 8 tokens
         for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
             const int64_t nt = n_tok - t0 < 8 ? n_tok - t0 : 8;

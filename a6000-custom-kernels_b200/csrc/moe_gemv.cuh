@@ -62,6 +62,7 @@ struct GemvArgs {
     const int32_t *ids;
     int64_t ids_stride;
     int32_t id_offset, skip_foreign;
+    int32_t host_only;              // only picks whose table entry is host memory (others left out, no output)
     int32_t ncols_dst, nchannels_dst, n_experts;
     // output
     float *dst;
@@ -1206,8 +1207,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_gemv_kernel(const __grid_
     };
     build_groups(
         C, N, a.n_experts,
-        [&](int e) { return a.ids[e % nch + static_cast<int64_t>(e / nch) * a.ids_stride] - a.id_offset; }, resolve,
-        a.err, a.skip_foreign != 0);
+        [&](int e) {
+            const int x = a.ids[e % nch + static_cast<int64_t>(e / nch) * a.ids_stride] - a.id_offset;
+            // host_only: a pick served from device memory (pool slot) is another path's
+            return a.host_only && x >= 0 && x < a.n_experts && !(reinterpret_cast<uintptr_t>(a.tbl[x]) & 1u) ? -1 : x;
+        },
+        resolve, a.err, a.skip_foreign != 0 || a.host_only != 0);
     if (C.fail) return;
     const int U = C.n_unique;
 

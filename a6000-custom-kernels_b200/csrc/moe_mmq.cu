@@ -1129,6 +1129,40 @@ cudaError_t launch_mmq_gather_rows(const float *x, const float *u, int glu_op, f
     return cudaGetLastError();
 }
 
+// Picks of a host-tiered tensor as pool slots: out[t * k + p] = the slot of
+// expert ids[t][p] when its table entry points into the pool, else -1 (host
+// memory: left to the GEMV). Out-of-range ids are left as they are (the
+// grouping reports them).
+__global__ void mmq_pool_ids_kernel(const int32_t *__restrict__ ids, int64_t ids_stride, int n_tok, int k,
+                                    char *const *__restrict__ tbl, int n_experts, const char *pool,
+                                    uint64_t expert_bytes, int n_slots, int32_t *out) {
+    const int n = n_tok * k;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(pool);
+    const uintptr_t hi = lo + static_cast<uintptr_t>(n_slots) * expert_bytes;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int t = i / k, p = i - t * k;
+        const int x = ids[static_cast<int64_t>(t) * ids_stride + p];
+        int v = x;
+        if (x >= 0 && x < n_experts) {
+            const uintptr_t q = reinterpret_cast<uintptr_t>(tbl[x]);
+            v = (!(q & 1u) && q >= lo && q < hi) ? static_cast<int>((q - lo) / expert_bytes) : -1;
+        } else if (x == -1) {
+            v = n_slots;   // not a host pick either: out of range for the slot grouping (reported there)
+        }
+        out[i] = v;
+    }
+}
+
+cudaError_t launch_mmq_pool_ids(const int32_t *ids, int64_t ids_stride, int n_tok, int k, char *const *tbl,
+                                int n_experts, const char *pool, uint64_t expert_bytes, int n_slots, int32_t *out,
+                                cudaStream_t st) {
+    const int n = n_tok * k;
+    const int grid = (n + 255) / 256 < 1024 ? ((n + 255) / 256 > 0 ? (n + 255) / 256 : 1) : 1024;
+    mmq_pool_ids_kernel<<<grid, 256, 0, st>>>(ids, ids_stride, n_tok, k, tbl, n_experts, pool, expert_bytes, n_slots,
+                                              out);
+    return cudaGetLastError();
+}
+
 // The chunk table of a one-expert call whose ids are all 0 (the shared
 // expert): entries in order, chunks of ntc consecutive entries.
 __global__ void mmq_identity_chunks_kernel(int n, int ntc, int32_t *entries, int4 *chunks, int32_t *n_chunks) {

@@ -263,14 +263,17 @@ int moe_b200_ep_layer_decode(const moe_layer_desc *layer, int64_t expert_lo, int
  * above its GEMV limit to llama.cpp's MMQ (patches/apply_patches.py:81-87):
  * dst[(t * k + p) * rows + r] = row r of expert ids[t * ids_stride + p] . x[t]
  * for n_tok tokens (x f32 [n_tok][ne00], contiguous, 16-byte aligned), with
- * llama.cpp CPU semantics (Q8_K activations). Q2_K, Q3_K, Q4_K, Q5_K and Q6_K
- * experts in device memory with rows a multiple of 128 and ne00 <= 4096 run
- * as a grouped int8 GEMM on the tensor cores (exact integer super-block dots;
- * Q2_K results equal the CPU path bit for bit, the others differ only in the
- * order of float sums); other types or host-tiered tensors run the decode
- * GEMV over chunks of 8 tokens. *used_tensor_cores (optional) reports which
- * ran. Workspace: moe_b200_prefill_workspace_size bytes of device memory, no
- * initialisation needed. */
+ * llama.cpp CPU semantics (Q8_K activations for K-quants, Q8_0 for Q4_0,
+ * Q5_0 and Q8_0). Experts of all 8 types with rows a multiple of 128 (ne00 <=
+ * 4096 for K-quants, <= 8192 otherwise) run as a grouped int8 GEMM on the
+ * tensor cores with exact integer block dots: Q2_K, Q4_0, Q5_0 and Q8_0 results
+ * equal the CPU path bit for bit, Q3_K..Q6_K differ only in the order of float
+ * sums. For a host-tiered tensor the picks of experts in its device pool run
+ * there (the pool as the expert array), the other picks through the decode
+ * GEMV reading pinned host memory in place; other shapes run the GEMV over
+ * chunks of 8 tokens. *used_tensor_cores (optional) reports whether the
+ * tensor cores ran. Workspace: moe_b200_prefill_workspace_size bytes of device
+ * memory, no initialisation needed. */
 size_t moe_b200_prefill_workspace_size(const moe_tensor *src0, int64_t n_tok, int64_t k);
 int moe_b200_prefill_mul_mat_id(const moe_tensor *src0, const float *x, int64_t n_tok, const int32_t *ids,
                                 int64_t k, int64_t ids_stride, float *dst, void *workspace, size_t workspace_bytes,

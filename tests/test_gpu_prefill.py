@@ -148,3 +148,38 @@ def test_prefill_bad_id_reported(pkg, cuda):
     mc.prefill_mul_mat_id(src0, torch.from_numpy(x).to(cuda), torch.from_numpy(ids).to(cuda))
     torch.cuda.synchronize()
     assert mc.device_error() != 0
+
+
+@pytest.mark.parametrize("t", [O.Q2_K, O.Q4_0, O.Q6_K])
+def test_prefill_tiered_pool_on_tensor_cores(pkg, cuda, tmp_path, t):
+    """A host-tiered tensor (pinned host memory, a pool of 4 slots seeded with
+    4 experts): picks of pool-resident experts run on the tensor cores with
+    the pool as the expert array, the other picks through the GEMV reading
+    host memory in place; together equal to the oracle."""
+    mc = pkg.moe_cache
+    K, rows, E, k, n_tok = 512, 256, 16, 2, 64
+    W = experts(t, E, rows, K, 51)
+    name = "blk.0.ffn_up_exps.weight"
+    seed = tmp_path / "seed.txt"
+    seed.write_text(f"{name} 3,1,4,5,9,2\n")
+    mc.reset()
+    mc.configure(enabled=True, slots=4, budget_gb=1.0, seed_path=str(seed))
+    try:
+        buf = torch.from_numpy(W).pin_memory()
+        src0 = mc.expert_tensor(buf, t, K, rows, name=name)
+        assert mc.wants(src0)
+        x = activations((n_tok, K), 52)
+        ids = _zipf_ids(n_tok, E, k, 53)
+        dst, tc = mc.prefill_mul_mat_id(src0, torch.from_numpy(x).to(cuda), torch.from_numpy(ids).to(cuda))
+        torch.cuda.synchronize()
+        assert mc.device_error() == 0
+        assert tc
+        tbl, n_slots, _ = mc.table(src0)
+        assert n_slots == 4 and sum(1 for v in tbl if v >= 0) == 4
+        picks = ids.reshape(-1)
+        assert any(tbl[e] >= 0 for e in picks) and any(tbl[e] == -1 for e in picks)
+        ref = O.mul_mat_id(t, W, K, x[:, None, :], ids)
+        assert rel_err(dst.cpu().numpy(), ref) <= TIGHT
+    finally:
+        mc.reset()
+        mc.configure(enabled=True)
