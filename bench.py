@@ -675,35 +675,79 @@ def time_gateup_kernel(pkg, layers, xs, dev, stream, n):
 
 def run_e2e(pkg, layers, xs_np, lg_np, dev, stream, steps):
     """Public API end to end: per step, H2D of the token's activations and router
-    logits from pinned host memory, MoELayer.decode, D2H of the layer output."""
+    logits from pinned host memory, MoELayer.decode (one moe_b200_layer_decode
+    call), D2H of the layer output into pinned host memory. The steps go back
+    to back with no host wait between them (the inputs of consecutive steps
+    are independent tokens): copies in, calls and copies out on three streams
+    ordered by events, so a step's copies overlap its neighbours' calls; G
+    steps are captured once into a CUDA graph and replayed, so the host's
+    per-call overhead does not set the pace. Every step's output is on the
+    host when the timed region ends."""
     import torch
     R = len(layers)
     P = xs_np.shape[0]
+    G = 64
     hx = torch.from_numpy(xs_np).pin_memory()
     hl = torch.from_numpy(lg_np).pin_memory()
     hout = torch.empty((P, H), dtype=torch.float32).pin_memory()
-    dx = torch.empty((1, H), device=dev)
-    dl = torch.empty((1, E), device=dev)
-    dout = torch.empty((1, H), device=dev)
+    D = 4                                   # device buffers in rotation
+    dx = torch.empty((D, 1, H), device=dev)
+    dl = torch.empty((D, 1, E), device=dev)
+    dout = torch.empty((D, 1, H), device=dev)
+
+    # copies in on s_in, calls on `stream`, copies out on s_out, ordered by
+    # events over the D buffers: step i + 1's input crosses while step i runs
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(D)]     # step's input landed
+    ev_done = [torch.cuda.Event() for _ in range(D)]   # step's call done (its buffers read and written)
+    ev_out = [torch.cuda.Event() for _ in range(D)]    # step's output copied out
 
     def one(i):
-        with torch.cuda.stream(stream):
-            dx.copy_(hx[i % P:i % P + 1], non_blocking=True)
-            dl.copy_(hl[i % P:i % P + 1], non_blocking=True)
-            layers[i % R].decode(dx, dl, dout, stream=stream)
-            hout[i % P:i % P + 1].copy_(dout, non_blocking=True)
-        stream.synchronize()
+        j = i % D
+        with torch.cuda.stream(s_in):
+            if i >= D:
+                s_in.wait_event(ev_done[j])
+            dx[j].copy_(hx[i % P:i % P + 1], non_blocking=True)
+            dl[j].copy_(hl[i % P:i % P + 1], non_blocking=True)
+            ev_in[j].record(s_in)
+        stream.wait_event(ev_in[j])
+        if i >= D:
+            stream.wait_event(ev_out[j])
+        layers[i % R].decode(dx[j], dl[j], dout[j], stream=stream)
+        ev_done[j].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_done[j])
+            hout[i % P:i % P + 1].copy_(dout[j], non_blocking=True)
+            ev_out[j].record(s_out)
 
-    for i in range(20):
-        one(i)
+    def block():
+        fork = torch.cuda.Event()
+        fork.record(stream)
+        s_in.wait_event(fork)
+        s_out.wait_event(fork)
+        for i in range(G):
+            one(i)
+        stream.wait_stream(s_in)
+        stream.wait_stream(s_out)
+
+    with torch.cuda.stream(stream):
+        block()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        block()
+    reps = max(1, steps // G)
+    with torch.cuda.stream(stream):
+        graph.replay()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for i in range(steps):
-        one(i)
-    ev1.record(stream)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        ev1.record(stream)
     torch.cuda.synchronize()
-    return {"seconds": ev0.elapsed_time(ev1) / 1e3, "steps": steps, "h2d": (H + E) * 4, "d2h": H * 4}
+    return {"seconds": ev0.elapsed_time(ev1) / 1e3, "steps": reps * G, "h2d": (H + E) * 4, "d2h": H * 4}
 
 
 # ---------------------------------------------------------------------------
