@@ -44,6 +44,12 @@ int launch_layer2(int ta, int tb, Layer2Args &a, cudaStream_t st, const char **w
 // The persistent stack kernel (moe_stack.cuh) for layers of one type.
 bool stack_type_supported(int ta, int tb);
 int launch_stack(int type, StackArgs &a, cudaStream_t st, const char **why, cudaError_t *cuda_err);
+// The mixed-type stack kernel: each layer's gate/up and down types among
+// Q2_K, Q3_K, Q4_K, Q6_K (StackLayer::ta / tb = their slots); used_a / used_b
+// = bit masks of the slots in use (the stages are sized for the largest).
+bool stack_mix_supported(int type);
+int launch_stack_mixed(unsigned used_a, unsigned used_b, StackArgs &a, cudaStream_t st, const char **why,
+                       cudaError_t *cuda_err);
 
 // Prefill grouped GEMM on the tensor cores (moe_mmq.cu): launch_mmq_group
 // groups the (token, pick) entries by expert into offsets / entries and the

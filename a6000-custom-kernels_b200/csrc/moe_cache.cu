@@ -1685,6 +1685,11 @@ StackWs stack_ws(const moe_layer_desc *L, int64_t n_layers, char *base) {
     return w;
 }
 
+// Mixed stacks: the type slots in use (gate/up, down) of each workspace that
+// moe_b200_stack_prepare set up with layers of different types; the launch
+// sizes its stages for them. A workspace prepared for one type has no entry.
+std::unordered_map<const void *, std::pair<unsigned, unsigned>> g_stack_mixed;
+
 size_t moe_b200_stack_workspace_size(const moe_layer_desc *L, int64_t n_layers) {
     if (!L || n_layers < 1) return 0;
     return stack_ws(L, n_layers, nullptr).bytes;
@@ -1699,8 +1704,25 @@ int moe_b200_stack_prepare(const moe_layer_desc *layers, int64_t n_layers, const
     const moe_layer_desc &L0 = layers[0];
     const size_t need = moe_b200_stack_workspace_size(&L0, n_layers);
     if (!workspace || workspace_bytes < need) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, need);
-    if (L0.gate.type != L0.up.type || !moe::stack_type_supported(L0.up.type, L0.down.type))
-        return fail(MOE_ERR_UNSUPPORTED, "the stack kernel needs one type for gate, up and down");
+    // one type for every tensor of every layer: the single-type kernel; else
+    // every layer's gate and up share a type and all types are mixed-stack
+    // types: the mixed kernel
+    bool one_type = true, mixable = true;
+    unsigned used_a = 0, used_b = 0;
+    for (int64_t l = 0; l < n_layers; ++l) {
+        const moe_layer_desc &Ll = layers[l];
+        one_type &= Ll.gate.type == L0.up.type && Ll.up.type == L0.up.type && Ll.down.type == L0.up.type;
+        mixable &= Ll.gate.type == Ll.up.type && moe::stack_mix_supported(Ll.up.type) &&
+                   moe::stack_mix_supported(Ll.down.type);
+        if (mixable) {
+            used_a |= 1u << moe::stack_mix_slot(Ll.up.type);
+            used_b |= 1u << moe::stack_mix_slot(Ll.down.type);
+        }
+    }
+    const bool mixed = !(one_type && moe::stack_type_supported(L0.up.type, L0.up.type));
+    if (mixed && !mixable)
+        return fail(MOE_ERR_UNSUPPORTED, "the stack kernel needs one type for gate, up and down, or gate = up and "
+                                         "types among Q2_K, Q3_K, Q4_K, Q6_K per layer");
     if (L0.up.ne[0] != L0.H || L0.up.ne[1] != L0.F || L0.down.ne[0] != L0.F || L0.down.ne[1] != L0.H)
         return fail(MOE_ERR_INVALID, "expert tensor shapes do not match H/F");
     const bool shared = L0.shared_type >= 0;
@@ -1708,11 +1730,11 @@ int moe_b200_stack_prepare(const moe_layer_desc *layers, int64_t n_layers, const
     const LayerWs w = layer_ws(&L0, 1, static_cast<char *>(workspace));
     for (int64_t l = 0; l < n_layers; ++l) {
         const moe_layer_desc &Ll = layers[l];
-        const bool same = Ll.up.type == L0.up.type && Ll.gate.type == L0.gate.type && Ll.down.type == L0.down.type &&
-                          Ll.H == L0.H && Ll.F == L0.F && Ll.n_experts == L0.n_experts && Ll.k == L0.k &&
+        const bool same = Ll.H == L0.H && Ll.F == L0.F && Ll.n_experts == L0.n_experts && Ll.k == L0.k &&
                           Ll.glu_op == L0.glu_op && Ll.glu_limit == L0.glu_limit && Ll.norm_w == L0.norm_w &&
-                          (Ll.shared_type >= 0) == shared;
-        if (!same) return fail(MOE_ERR_INVALID, "layer %lld differs from layer 0 in type or shape", static_cast<long long>(l));
+                          (Ll.shared_type >= 0) == shared && Ll.up.ne[0] == L0.H && Ll.up.ne[1] == L0.F &&
+                          Ll.down.ne[0] == L0.F && Ll.down.ne[1] == L0.H;
+        if (!same) return fail(MOE_ERR_INVALID, "layer %lld differs from layer 0 in shape", static_cast<long long>(l));
         const moe_tensor *T[3] = {&Ll.gate, &Ll.up, &Ll.down};
         for (const moe_tensor *t : T)
             if (!t->data || !contiguous(t) || t->ne[2] != Ll.n_experts || !aligned16(t->data) || t->nb[2] % 16 ||
@@ -1735,7 +1757,11 @@ int moe_b200_stack_prepare(const moe_layer_desc *layers, int64_t n_layers, const
         s.ids_out = w.ids;
         s.w_out = w.w;
         s.chained = l > 0 && x_next && x_next[l - 1] == x[l] ? 1 : 0;
+        s.ta = mixed ? moe::stack_mix_slot(Ll.up.type) : 0;
+        s.tb = mixed ? moe::stack_mix_slot(Ll.down.type) : 0;
     }
+    if (mixed) g_stack_mixed[workspace] = {used_a, used_b};
+    else g_stack_mixed.erase(workspace);
     const StackWs sw = stack_ws(&L0, n_layers, static_cast<char *>(workspace));
     CK(cudaMemcpyAsync(sw.layers, d.data(), sizeof(moe::StackLayer) * d.size(), cudaMemcpyHostToDevice,
                        reinterpret_cast<cudaStream_t>(stream)));
@@ -1749,7 +1775,10 @@ int moe_b200_stack_run(const moe_layer_desc *layer0, int64_t n_layers, void *wor
     if (!layer0 || n_layers < 1) return fail(MOE_ERR_INVALID, "null argument");
     const size_t need = moe_b200_stack_workspace_size(layer0, n_layers);
     if (!workspace || workspace_bytes < need) return fail(MOE_ERR_INVALID, "workspace too small (%zu < %zu)", workspace_bytes, need);
-    if (layer0->gate.type != layer0->up.type || !moe::stack_type_supported(layer0->up.type, layer0->down.type))
+    const auto mix = g_stack_mixed.find(workspace);
+    const bool mixed = mix != g_stack_mixed.end();
+    if (!mixed && (layer0->gate.type != layer0->up.type ||
+                   !moe::stack_type_supported(layer0->up.type, layer0->down.type)))
         return fail(MOE_ERR_UNSUPPORTED, "the stack kernel needs one type for gate, up and down");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const LayerWs w = layer_ws(layer0, 1, static_cast<char *>(workspace));
@@ -1785,7 +1814,8 @@ int moe_b200_stack_run(const moe_layer_desc *layer0, int64_t n_layers, void *wor
     a.timeout_ns = g.timeout_ns_kernel;
     const char *why = "";
     cudaError_t ce = cudaSuccess;
-    rc = moe::launch_stack(layer0->up.type, a, st, &why, &ce);
+    rc = mixed ? moe::launch_stack_mixed(mix->second.first, mix->second.second, a, st, &why, &ce)
+               : moe::launch_stack(layer0->up.type, a, st, &why, &ce);
     if (rc == MOE_ERR_CUDA) return fail(rc, "%s: %s", why, cudaGetErrorString(ce));
     if (rc) return fail(rc, "%s", why);
     return MOE_OK;

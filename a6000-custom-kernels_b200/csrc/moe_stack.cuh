@@ -26,6 +26,15 @@
 // rt_full[j % 3]; the consumers release the buffer (rt_empty) when layer j is
 // done, so the producer runs at most two layers ahead. All waits are bounded.
 // Results equal moe_b200_layer_decode per layer bit for bit.
+//
+// Mixed stacks (moe_stack_kernel<T_STACK_MIXED, T_STACK_MIXED>): every layer
+// names its own gate/up type and down type among Q2_K, Q3_K, Q4_K and Q6_K
+// (llama.cpp's quantization mixes give each layer's tensors their own
+// types). The kernel dispatches on them per layer: the tile geometry of each
+// type comes from StackArgs::gum / dnm, tiles per layer vary (the ring index
+// of a layer's first tile is the running sum), the stages are sized for the
+// largest type present. A row's dot product does not depend on the tile it
+// lands in, so a mixed stack equals moe_b200_layer_decode layer by layer too.
 #pragma once
 #include "moe_layer2.cuh"
 
@@ -40,7 +49,29 @@ struct StackLayer {
     int32_t *ids_out;                       // [k] picks (may be null)
     float *w_out;                           // [k] gating weights (may be null)
     int32_t chained;                        // x is the previous layer's x_next
+    int32_t ta, tb;                         // mixed stacks: type slots of gate/up and down
 };
+
+// Template tag of the mixed-type kernel and its type slots.
+constexpr int T_STACK_MIXED = 1 << 20;
+constexpr int STACK_MIX_TYPES = 4;
+__host__ __device__ constexpr int stack_mix_type(int slot) {
+    return slot == 0 ? T_Q2_K : slot == 1 ? T_Q3_K : slot == 2 ? T_Q4_K : T_Q6_K;
+}
+__host__ __device__ constexpr int stack_mix_slot(int type) {
+    return type == T_Q2_K ? 0 : type == T_Q3_K ? 1 : type == T_Q4_K ? 2 : type == T_Q6_K ? 3 : -1;
+}
+template <int T> struct StackType { static constexpr int value = T; };
+// fn(StackType<type of slot>{}): one instantiation of fn per slot
+template <class Fn>
+__device__ __forceinline__ void with_stack_type(int slot, Fn &&fn) {
+    switch (slot) {
+        case 0: fn(StackType<T_Q2_K>{}); break;
+        case 1: fn(StackType<T_Q3_K>{}); break;
+        case 2: fn(StackType<T_Q4_K>{}); break;
+        default: fn(StackType<T_Q6_K>{}); break;
+    }
+}
 
 constexpr int STACK_MAX_K = 32;
 #ifndef STACK_POLL_NS
@@ -80,6 +111,14 @@ struct StackArgs {
     uint32_t route_off;                     // byte offset of StackShared in shared memory
     int *err;
     uint64_t timeout_ns;
+    GemvArgs gum[STACK_MIX_TYPES], dnm[STACK_MIX_TYPES];   // mixed stacks: gu / dn per type slot
+};
+
+// Tile geometry of one layer of the stack.
+struct StackGeo {
+    int ta, tb;                             // type slots (mixed stacks)
+    int rpt, rows_b, nA, nB;                // rows per tile, tiles of each phase (this CTA)
+    uint32_t rba, rbb, part_a;              // row bytes of gate/up and down, gate/up part size
 };
 
 // load_tagged_block for data this GPU's CTAs exchange (GPU scope)
@@ -146,8 +185,34 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
     constexpr int PW = GEMV_CONSUMER_WARPS;            // the producer warp
     const UnitPlan P = unit_plan(k + hs, nullptr, G, bid, F, H, rpt, rows_b);
     const bool shared_cta = hs && P.u == k;            // the shared expert's rows
-    const int per_layer = P.nA + P.nB;
     const uint8_t kind = a.tma ? 0 : 2;
+    constexpr bool MIX = TA == T_STACK_MIXED;
+    // this CTA's tiles of a layer (rows a0..a1 and b0..b1 do not depend on the type)
+    auto geo_of = [&](const StackLayer &Lr) {
+        StackGeo g;
+        if constexpr (MIX) {
+            g.ta = Lr.ta;
+            g.tb = Lr.tb;
+            const GemvArgs &ga = a.gum[g.ta], &gb = a.dnm[g.tb];
+            g.rpt = ga.rows_per_tile;
+            g.rows_b = gb.rows_per_tile;
+            g.rba = ga.row_bytes;
+            g.rbb = gb.row_bytes;
+            g.part_a = ga.part_bytes;
+            g.nA = (P.a1 - P.a0 + g.rpt - 1) / g.rpt;
+            g.nB = (P.b1 - P.b0 + g.rows_b - 1) / g.rows_b;
+        } else {
+            g.ta = g.tb = 0;
+            g.rpt = rpt;
+            g.rows_b = rows_b;
+            g.rba = a.gu.row_bytes;
+            g.rbb = a.dn.row_bytes;
+            g.part_a = a.gu.part_bytes;
+            g.nA = P.nA;
+            g.nB = P.nB;
+        }
+        return g;
+    };
 
     if (warp == PW) {
         // ============================ producer warp ===========================
@@ -179,10 +244,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             const bool bad = __any_sync(0xffffffffu, x < 0 || x >= E);
             if (!bad) {
                 route_weights(Lr.logits, E, k, a.norm_w, lane, R.gid, R.wt);
+                // contiguous experts: a mixed layer's strides follow from its types
+                uint64_t eb_up = a.eb_up, eb_gate = a.eb_gate, eb_down = a.eb_down;
+                if constexpr (MIX) {
+                    eb_up = eb_gate = static_cast<uint64_t>(F) * a.gum[Lr.ta].row_bytes;
+                    eb_down = static_cast<uint64_t>(H) * a.dnm[Lr.tb].row_bytes;
+                }
                 if (lane < k) {
-                    R.usrc[lane][0] = Lr.up + static_cast<uint64_t>(x) * a.eb_up;
-                    R.usrc[lane][1] = Lr.gate + static_cast<uint64_t>(x) * a.eb_gate;
-                    R.dsrc[lane] = Lr.down + static_cast<uint64_t>(x) * a.eb_down;
+                    R.usrc[lane][0] = Lr.up + static_cast<uint64_t>(x) * eb_up;
+                    R.usrc[lane][1] = Lr.gate + static_cast<uint64_t>(x) * eb_gate;
+                    R.dsrc[lane] = Lr.down + static_cast<uint64_t>(x) * eb_down;
                     if (bid == 0 && Lr.ids_out) Lr.ids_out[lane] = x;
                     if (bid == 0 && Lr.w_out) Lr.w_out[lane] = R.wt[lane];
                 }
@@ -193,26 +264,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             return !bad;
         };
         // tile i of layer l (phase A: up + gate rows, then phase B: down rows)
-        auto describe = [&](int l, int i, TileSrc &ts) {
+        auto describe = [&](int l, const StackGeo &Gl, int i, TileSrc &ts) {
             const StackLayer &Lr = a.layers[l];
             const StackRoute &R = SS.r[l % STACK_ROUTE_BUFS];
-            if (i < P.nA) {
-                ts.row0[0] = ts.row0[1] = P.a0 + i * rpt;
-                ts.nr[0] = ts.nr[1] = min(rpt, P.a1 - ts.row0[0]);
+            if (i < Gl.nA) {
+                ts.row0[0] = ts.row0[1] = P.a0 + i * Gl.rpt;
+                ts.nr[0] = ts.nr[1] = min(Gl.rpt, P.a1 - ts.row0[0]);
                 ts.src[0] = shared_cta ? Lr.sh_up : R.usrc[P.u][0];
                 ts.src[1] = shared_cta ? Lr.sh_gate : R.usrc[P.u][1];
                 ts.kind[0] = ts.kind[1] = kind;
                 ts.n_parts = 2;
-                ts.rb = a.gu.row_bytes;
-                ts.part_bytes = a.gu.part_bytes;
+                ts.rb = Gl.rba;
+                ts.part_bytes = Gl.part_a;
             } else {
-                const int jb = i - P.nA;
-                ts.row0[0] = ts.row0[1] = P.b0 + jb * rows_b;
-                ts.nr[0] = ts.nr[1] = min(rows_b, P.b1 - ts.row0[0]);
+                const int jb = i - Gl.nA;
+                ts.row0[0] = ts.row0[1] = P.b0 + jb * Gl.rows_b;
+                ts.nr[0] = ts.nr[1] = min(Gl.rows_b, P.b1 - ts.row0[0]);
                 ts.src[0] = ts.src[1] = shared_cta ? Lr.sh_down : R.dsrc[P.u];
                 ts.kind[0] = ts.kind[1] = kind;
                 ts.n_parts = 1;
-                ts.rb = a.dn.row_bytes;
+                ts.rb = Gl.rbb;
                 ts.part_bytes = a.stage_bytes;
             }
         };
@@ -220,24 +291,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         // is routed while layer l's down tiles wait for free stages
         int end = 0;   // ring indexes [0, end) issued
         if (route_layer(0)) {
+            int g0 = 0;    // ring index of layer l's first tile
             for (int l = 0; l < L; ++l) {
                 if (ld_relaxed_u32(reinterpret_cast<const uint32_t *>(a.err))) break;
-                const int g0 = l * per_layer;
+                const StackGeo Gl = geo_of(a.layers[l]);
                 ST_MARK(l, 7);
-                int n = produce_tiles(P.nA, S, full, empty, stage_area, a.stage_bytes,
-                                      [&](int i, TileSrc &ts) { describe(l, i, ts); }, a.timeout_ns, a.err, lane, g0,
-                                      false);
+                int n = produce_tiles(Gl.nA, S, full, empty, stage_area, a.stage_bytes,
+                                      [&](int i, TileSrc &ts) { describe(l, Gl, i, ts); }, a.timeout_ns, a.err, lane,
+                                      g0, false);
                 end = g0 + n;
-                if (n < P.nA) break;
+                if (n < Gl.nA) break;
                 ST_MARK(l, 8);
                 const bool next = l + 1 < L ? route_layer(l + 1) : true;
                 ST_MARK(l, 9);
-                n = produce_tiles(P.nB, S, full, empty, stage_area, a.stage_bytes,
-                                  [&](int i, TileSrc &ts) { describe(l, P.nA + i, ts); }, a.timeout_ns, a.err, lane,
-                                  g0 + P.nA, false);
-                end = g0 + P.nA + n;
+                n = produce_tiles(Gl.nB, S, full, empty, stage_area, a.stage_bytes,
+                                  [&](int i, TileSrc &ts) { describe(l, Gl, Gl.nA + i, ts); }, a.timeout_ns, a.err,
+                                  lane, g0 + Gl.nA, false);
+                end = g0 + Gl.nA + n;
                 ST_MARK(l, 10);
-                if (n < P.nB || !next) break;
+                if (n < Gl.nB || !next) break;
+                g0 += Gl.nA + Gl.nB;
             }
         }
         drain_tiles(end, S, full, a.timeout_ns, a.err, lane);   // nothing in flight at exit
@@ -266,22 +339,25 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                                         (static_cast<unsigned long long>(P.nA) << 16) |
                                         (static_cast<unsigned long long>(P.nB) << 24);
 #endif
-    constexpr int QA = is_kquant(TA) ? 256 : 32;
+    // K-quant types (every mixed type) stage 256-value blocks, the others 32
+    constexpr bool KQA = MIX || is_kquant(TA), KQB = MIX || is_kquant(TB);
+    constexpr int QA = KQA ? 256 : 32;
     const int nbx = KA / QA;
-    const int nA = P.nA, nB = P.nB;
     if (tid == 0) LC.halt = 0u;
     consumer_sync();
     // tile cursor of this warp (nw <= S, so one wrap per step at most); warps
     // past nw take no tiles
     int cg = warp < nw ? warp : 0x7fffffff, cs = warp < nw ? warp : 0;
     uint32_t cph = 0;
+    int g0 = 0;    // ring index of layer l's first tile
     for (int l = 0; l < L; ++l) {
         const StackLayer &Lr = a.layers[l];
         const int rb = l % STACK_ROUTE_BUFS;
         const StackRoute &R = SS.r[rb];
         const uint32_t rpar = static_cast<uint32_t>((l / STACK_ROUTE_BUFS) & 1);
         const uint32_t tag = epoch0 + 1u + static_cast<uint32_t>(l);
-        const int g0 = l * per_layer;
+        const StackGeo Gl = geo_of(Lr);
+        const int nA = Gl.nA, nB = Gl.nB;
         if (warp == 0) ST_MARK(l, 0);
         // ---- layer l routed; its input staged. From layer 1 on, every value
         //      of x_l = x_{l-1} + out_{l-1} as layer l - 1's combiners tagged it
@@ -292,7 +368,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             LC.halt = 1u;
         }
         {
-            constexpr bool KQ = is_kquant(TA);
+            constexpr bool KQ = KQA;
             const uint64_t *xin = a.xtag + static_cast<int64_t>(l & 1) * H;
             const bool from_tags = l > 0 && Lr.chained;
             const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
@@ -310,29 +386,35 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                 }
             }
             if (l > 0) consumer_sync();
-            for (int b = warp; b < nbx; b += PW) {
-                float v[KQ ? 8 : 1];
-                if (l > 0) {
-                    while (!__all_sync(0xffffffffu, load_tagged_block_gpu<KQ>(xin + b * QA, tag - 1u, lane, v))) {
-                        if (static_cast<uint64_t>(clock64()) - t0 > lim) {
-                            if (lane == 0) {
-                                set_error(a.err, DERR_TIMEOUT_TAG);
-                                LC.halt = 1u;
+            // the activation layout is the gate/up type's
+            auto stage_x = [&](auto tt) {
+                constexpr int T = decltype(tt)::value;
+                for (int b = warp; b < nbx; b += PW) {
+                    float v[KQ ? 8 : 1];
+                    if (l > 0) {
+                        while (!__all_sync(0xffffffffu, load_tagged_block_gpu<KQ>(xin + b * QA, tag - 1u, lane, v))) {
+                            if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                                if (lane == 0) {
+                                    set_error(a.err, DERR_TIMEOUT_TAG);
+                                    LC.halt = 1u;
+                                }
+                                break;
                             }
-                            break;
                         }
                     }
+                    if (from_tags) {
+                        int8_t *q = reinterpret_cast<int8_t *>(act_area);
+                        int16_t *bs = reinterpret_cast<int16_t *>(act_area + KA);
+                        float *sc = reinterpret_cast<float *>(act_area + KA + KA / 8);
+                        if constexpr (KQ) quant_q8K_vals<T>(v, q, bs, sc, b, lane, KA / chunk_of<T>::CE);
+                        else quant_q80_val<T>(v[0], q, bs, sc, b, lane, KA / chunk_of<T>::CE);
+                    } else {
+                        stage_f32_block<T, true>(Lr.x, act_area, KA, b, lane);
+                    }
                 }
-                if (from_tags) {
-                    int8_t *q = reinterpret_cast<int8_t *>(act_area);
-                    int16_t *bs = reinterpret_cast<int16_t *>(act_area + KA);
-                    float *sc = reinterpret_cast<float *>(act_area + KA + KA / 8);
-                    if constexpr (KQ) quant_q8K_vals<TA>(v, q, bs, sc, b, lane, KA / chunk_of<TA>::CE);
-                    else quant_q80_val<TA>(v[0], q, bs, sc, b, lane, KA / chunk_of<TA>::CE);
-                } else {
-                    stage_f32_block<TA, true>(Lr.x, act_area, KA, b, lane);
-                }
-            }
+            };
+            if constexpr (MIX) with_stack_type(Gl.ta, stage_x);
+            else stage_x(StackType<TA>{});
         }
         consumer_sync();
         if (warp == 0) ST_MARK(l, 2);
@@ -359,15 +441,21 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                 break;
             }
             if (i == warp) ST_MARK(l, 12 + warp);
-            const int row0 = P.a0 + i * rpt, nr = min(rpt, P.a1 - row0);
+            const int row0 = P.a0 + i * Gl.rpt, nr = min(Gl.rpt, P.a1 - row0);
             const char *s0 = shared_cta ? Lr.sh_up : R.usrc[P.u][0];
             const char *s1 = shared_cta ? Lr.sh_gate : R.usrc[P.u][1];
             const uint8_t *stage = stage_area + static_cast<size_t>(s) * a.stage_bytes;
-            const uint64_t off = static_cast<uint64_t>(row0) * a.gu.row_bytes;
+            const uint64_t off = static_cast<uint64_t>(row0) * Gl.rba;
             const uint8_t *up_rows = stage + ((reinterpret_cast<uintptr_t>(s0) + off) & 15u);
-            const uint8_t *gate_rows = stage + a.gu.part_bytes + ((reinterpret_cast<uintptr_t>(s1) + off) & 15u);
-            consume_tile<TA, ACT_CPU, 1, 2>(a.gu, C, up_rows, gate_rows, nr, P.u, k, row0, act_area, lane, a.h_tag,
-                                            a.hs_tag, tag);
+            const uint8_t *gate_rows = stage + Gl.part_a + ((reinterpret_cast<uintptr_t>(s1) + off) & 15u);
+            auto tile_a = [&](auto tt) {
+                constexpr int T = decltype(tt)::value;
+                const GemvArgs &ga = MIX ? a.gum[stack_mix_slot(T) < 0 ? 0 : stack_mix_slot(T)] : a.gu;
+                consume_tile<T, ACT_CPU, 1, 2>(ga, C, up_rows, gate_rows, nr, P.u, k, row0, act_area, lane, a.h_tag,
+                                               a.hs_tag, tag);
+            };
+            if constexpr (MIX) with_stack_type(Gl.ta, tile_a);
+            else tile_a(StackType<TA>{});
             if (i == warp) ST_MARK(l, 28 + warp);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -377,26 +465,32 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
         if (warp == 0) ST_MARK(l, 3);
         // ---- the unit's h from the CTAs of its group, quantized for down ----
         {
-            constexpr bool KQ = is_kquant(TB);
+            constexpr bool KQ = KQB;
             constexpr int QB = KQ ? 256 : 32;
             const int nb = KB / QB;
             const uint64_t *base = shared_cta ? a.hs_tag : a.h_tag + static_cast<int64_t>(P.u) * a.dn.stride_channel_y;
             const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
-            for (int b = warp; b < nb; b += PW) {
-                float v[KQ ? 8 : 1];
-                while (!__all_sync(0xffffffffu, load_tagged_block_gpu<KQ>(base + b * QB, tag, lane, v))) {
-                    if (static_cast<uint64_t>(clock64()) - t0 > lim) {
-                        if (lane == 0) set_error(a.err, DERR_TIMEOUT_TAG);
-                        break;
+            // quantized in the down type's layout
+            auto stage_h = [&](auto tt) {
+                constexpr int T = decltype(tt)::value;
+                for (int b = warp; b < nb; b += PW) {
+                    float v[KQ ? 8 : 1];
+                    while (!__all_sync(0xffffffffu, load_tagged_block_gpu<KQ>(base + b * QB, tag, lane, v))) {
+                        if (static_cast<uint64_t>(clock64()) - t0 > lim) {
+                            if (lane == 0) set_error(a.err, DERR_TIMEOUT_TAG);
+                            break;
+                        }
+                        __nanosleep(STACK_POLL_NS);
                     }
-                    __nanosleep(STACK_POLL_NS);
+                    int8_t *q = reinterpret_cast<int8_t *>(act_area);
+                    int16_t *bs = reinterpret_cast<int16_t *>(act_area + KB);
+                    float *sc = reinterpret_cast<float *>(act_area + KB + KB / 8);
+                    if constexpr (KQ) quant_q8K_vals<T>(v, q, bs, sc, b, lane, KB / chunk_of<T>::CE);
+                    else quant_q80_val<T>(v[0], q, bs, sc, b, lane, KB / chunk_of<T>::CE);
                 }
-                int8_t *q = reinterpret_cast<int8_t *>(act_area);
-                int16_t *bs = reinterpret_cast<int16_t *>(act_area + KB);
-                float *sc = reinterpret_cast<float *>(act_area + KB + KB / 8);
-                if constexpr (KQ) quant_q8K_vals<TB>(v, q, bs, sc, b, lane, KB / chunk_of<TB>::CE);
-                else quant_q80_val<TB>(v[0], q, bs, sc, b, lane, KB / chunk_of<TB>::CE);
-            }
+            };
+            if constexpr (MIX) with_stack_type(Gl.tb, stage_h);
+            else stage_h(StackType<TB>{});
         }
         consumer_sync();
         if (warp == 0) ST_MARK(l, 4);
@@ -413,12 +507,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             }
             if (i - nA < nw) ST_MARK(l, 44 + warp);
             if (i - nA < nw && warp == 1) ST_MARK(l, 62);
-            const int row0 = P.b0 + (i - nA) * rows_b, nr = min(rows_b, P.b1 - row0);
+            const int row0 = P.b0 + (i - nA) * Gl.rows_b, nr = min(Gl.rows_b, P.b1 - row0);
             const char *s0 = shared_cta ? Lr.sh_down : R.dsrc[P.u];
             const uint8_t *rows = stage_area + static_cast<size_t>(s) * a.stage_bytes +
-                                  ((reinterpret_cast<uintptr_t>(s0) + static_cast<uint64_t>(row0) * a.dn.row_bytes) & 15u);
-            consume_tile<TB, ACT_CPU, 1, 1, 32>(a.dn, C, rows, rows, nr, P.u, k, row0, act_area, lane, a.ytag,
-                                                a.ytag_s, tag);
+                                  ((reinterpret_cast<uintptr_t>(s0) + static_cast<uint64_t>(row0) * Gl.rbb) & 15u);
+            auto tile_b = [&](auto tt) {
+                constexpr int T = decltype(tt)::value;
+                const GemvArgs &gb = MIX ? a.dnm[stack_mix_slot(T) < 0 ? 0 : stack_mix_slot(T)] : a.dn;
+                consume_tile<T, ACT_CPU, 1, 1, 32>(gb, C, rows, rows, nr, P.u, k, row0, act_area, lane, a.ytag,
+                                                   a.ytag_s, tag);
+            };
+            if constexpr (MIX) with_stack_type(Gl.tb, tile_b);
+            else tile_b(StackType<TB>{});
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
@@ -489,6 +589,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             ST_MARK(l, 40 + (warp & 3));
         }
         if (warp == 0) ST_MARK(l, 6);
+        g0 += nA + nB;
     }
     // ---- the last CTA to finish advances the epoch past every layer's tag and
     //      clears the layer counter ---------------------------------------------

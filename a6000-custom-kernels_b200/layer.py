@@ -19,7 +19,7 @@ class MoELayer:
     in which case they live in pinned host memory behind the tiered cache."""
 
     def __init__(self, H, F, n_experts, k, types, shared=True, glu_op=GLU_SWIGLU, glu_limit=0.0, norm_w=False,
-                 device="cuda", host=False, name="blk.0", seed=0, weights=None):
+                 device="cuda", host=False, name="blk.0", seed=0, weights=None, sigma=0.02):
         self.H, self.F, self.E, self.k = H, F, n_experts, k
         self.types = dict(types)          # {"gate": t, "up": t, "down": t}
         self.glu_op, self.glu_limit, self.norm_w = glu_op, glu_limit, norm_w
@@ -34,7 +34,7 @@ class MoELayer:
                 buf = src.pin_memory() if host else src.to(self.device)
             else:
                 buf = torch.empty((n_experts, rows, row_size(t, K)), dtype=torch.uint8, device=self.device)
-                fill_quantized(t, buf, n_experts * rows, K, seed * 1000003 + i)
+                fill_quantized(t, buf, n_experts * rows, K, seed * 1000003 + i, sigma=sigma)
                 if host:
                     pinned = torch.empty(buf.shape, dtype=torch.uint8, pin_memory=True)
                     pinned.copy_(buf)
@@ -51,7 +51,7 @@ class MoELayer:
                     buf = torch.as_tensor(weights[f"shared_{role}"]).to(self.device)
                 else:
                     buf = torch.empty((rows, row_size(t, K)), dtype=torch.uint8, device=self.device)
-                    fill_quantized(t, buf, rows, K, seed * 1000003 + 7 + i)
+                    fill_quantized(t, buf, rows, K, seed * 1000003 + 7 + i, sigma=sigma)
                 self.shared[role] = buf
         d = MoeLayerDesc()
         d.gate, d.up, d.down = self.desc_t["gate"], self.desc_t["up"], self.desc_t["down"]

@@ -358,15 +358,19 @@ int moe_b200_ep_return(const void *const *peer_ptrs, int32_t world, int64_t cap,
  * words in the workspace (no atomics, no grid barrier). One launch also keeps
  * the code warm in the instruction caches and has no launch gaps. Up to 32
  * picks per layer.
- * Requirements: gate, up and down of one type (Q2_K..Q6_K, Q4_0, Q5_0, Q8_0,
- * Q5_K), every layer with layer 0's shapes, types, GLU and shared-expert
- * presence, expert tensors contiguous and 16-byte aligned in device memory
- * (no host-tiered tensors, no cache bookkeeping). x, logits, out, x_next are
- * host arrays of n_layers device pointers.
+ * Requirements: either gate, up and down of every layer of one type (Q2_K..
+ * Q6_K, Q4_0, Q5_0, Q8_0, Q5_K), or per layer gate = up and the gate/up and
+ * down types each among Q2_K, Q3_K, Q4_K, Q6_K (a mixed stack: one kernel
+ * that picks each layer's types at run time); every layer with layer 0's
+ * shapes, GLU and shared-expert presence (the shared expert takes its
+ * layer's types), expert tensors contiguous and 16-byte aligned in device
+ * memory (no host-tiered tensors, no cache bookkeeping). x, logits, out,
+ * x_next are host arrays of n_layers device pointers.
  * moe_b200_stack_prepare writes the layer list into the workspace (an
  * asynchronous copy on `stream` from host memory: not during stream
- * capture); moe_b200_stack_run launches (capturable) and may be repeated for
- * the same list. Workspace:
+ * capture) and records, for a mixed stack, the types in use under the
+ * workspace's address; moe_b200_stack_run launches (capturable) and may be
+ * repeated for the same list. Workspace:
  * moe_b200_stack_workspace_size(layer 0, n_layers) bytes, zero-filled once
  * (its start is a layer-decode workspace for one token). */
 size_t moe_b200_stack_workspace_size(const moe_layer_desc *layer0, int64_t n_layers);
