@@ -740,6 +740,30 @@ struct TileSrc {
     uint32_t rb, part_bytes;
 };
 
+// n4 16-byte units from host memory (read over the host link) into shared
+// memory by one warp. A load from host memory takes microseconds, so each
+// lane keeps HOST_COPY_DEPTH loads in flight (all of a batch's loads issue
+// before its stores) instead of one load-store pair at a time.
+#ifndef HOST_COPY_DEPTH
+#define HOST_COPY_DEPTH 8
+#endif
+__device__ __forceinline__ void copy_host16(uint4 *d4, const uint4 *s4, uint32_t n4, int lane) {
+    constexpr int U = HOST_COPY_DEPTH;
+    for (uint32_t j0 = 0; j0 < n4; j0 += 32u * U) {
+        uint4 v[U];
+#pragma unroll
+        for (int q = 0; q < U; ++q) {
+            const uint32_t j = j0 + static_cast<uint32_t>(lane) + 32u * q;
+            if (j < n4) v[q] = s4[j];
+        }
+#pragma unroll
+        for (int q = 0; q < U; ++q) {
+            const uint32_t j = j0 + static_cast<uint32_t>(lane) + 32u * q;
+            if (j < n4) d4[j] = v[q];
+        }
+    }
+}
+
 // Waits until the copies of ring indexes [max(lo, end - S), end) have landed
 // (the last S the producer issued): no bulk copy is then in flight.
 __device__ __forceinline__ void drain_tiles(int end, int S, uint64_t *full, uint64_t timeout_ns, int *err, int lane,
@@ -856,10 +880,8 @@ __device__ __forceinline__ int produce_tiles(int n_tiles, int S, uint64_t *full,
                 } else if (ts.kind[p] == 1) {
                     // the range a bulk copy would move (inside the expert:
                     // 16-byte aligned base and size), with 16-byte loads
-                    const uint4 *s4 = reinterpret_cast<const uint4 *>(a0);
-                    uint4 *d4 = reinterpret_cast<uint4 *>(dp);
-                    const uint32_t n4 = static_cast<uint32_t>(a1 - a0) / 16u;
-                    for (uint32_t j = lane; j < n4; j += 32) d4[j] = s4[j];
+                    copy_host16(reinterpret_cast<uint4 *>(dp), reinterpret_cast<const uint4 *>(a0),
+                                static_cast<uint32_t>(a1 - a0) / 16u, lane);
                 } else {
                     // 4-byte words when the source allows, else 2-byte units;
                     // both keep the copy inside [sp, sp + bytes)

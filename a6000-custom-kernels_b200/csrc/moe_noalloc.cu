@@ -240,10 +240,14 @@ extern "C" int moe_b200_noalloc_device_error(moe_stream_t stream, int32_t *code)
     std::lock_guard<std::mutex> lock(g_na_mu);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOE_ERR_CUDA;
-    if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return MOE_ERR_CUDA;
-    if (!g_na_ptr[dev]) return MOE_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (!g_na_ptr[dev]) return cudaStreamSynchronize(st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+    // read on the caller's stream (after its work), not on the legacy stream,
+    // which would wait for every other stream of the device too
     int v = 0;
-    if (cudaMemcpy(&v, g_na_ptr[dev] + NA_ERR, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return MOE_ERR_CUDA;
+    if (cudaMemcpyAsync(&v, g_na_ptr[dev] + NA_ERR, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return MOE_ERR_CUDA;
     if (code) *code = v;
     return MOE_OK;
 }
