@@ -857,8 +857,36 @@ def run_other_config(args):
             step(i)
     torch.cuda.synchronize()
     G = 64 if n_layers_step > 1 else 512
-    stack_mode = args.config != 1 and B == 1 and args.launch == "stack"
-    if stack_mode:
+    stack_mode = B == 1 and args.launch == "stack"
+    if stack_mode and args.config == 1:
+        # batch 1: 512 independent layer steps (the 32 copies cycled) in one
+        # persistent launch of the stack kernel
+        st = pkg.Stack([layers[j % R] for j in range(G)], [xs[j % P] for j in range(G)],
+                       [lgs[j % P] for j in range(G)], [outs[j % P] for j in range(G)], stream=stream)
+        st.run(stream)
+        torch.cuda.synchronize()
+        assert mc.device_error(stream) == 0
+        # in-run check: the stack's outputs equal the per-step layer decode
+        first = outs[:8].clone()
+        with torch.cuda.stream(stream):
+            for i in range(8):
+                step(i)
+        torch.cuda.synchronize()
+        stack_diff = float((first - outs[:8]).abs().max())
+        reps = max(1, K // G)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(reps):
+                st.run(stream)
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        K = reps * G
+        launches = 1.0 / G
+        extra = {"timing": f"persistent launches of {G} layer steps (stack kernel), device events",
+                 "stack_vs_per_layer_max_abs_diff": stack_diff}
+    elif stack_mode:
         # batch 1: G steps x n_layers layers in one persistent launch of the
         # mixed-type stack kernel (each layer its own gate/up and down types);
         # within a step the layers chain through x_next, a step starts from

@@ -122,3 +122,25 @@ def test_stack_512_experts_equals_layer_by_layer(pkg, cuda, pairs):
         diffs.append((l, float((outs[l] - ref).abs().max()), float(ref.abs().max())))
         x = x + ref
     assert all(d == 0.0 for _, d, _ in diffs), diffs
+
+
+def test_stack_without_shared_expert(pkg, cuda):
+    """Config-1 layers (H=2048, F=512, 64 experts, Q4_0, no shared expert) as
+    a residual chain: equal to the layer decode bit for bit."""
+    H, F, E, k, t = 2048, 512, 64, 8, O.Q4_0
+    n = 5
+    layers = [pkg.MoELayer(H, F, E, k, {"gate": t, "up": t, "down": t}, shared=False, seed=140 + l) for l in range(n)]
+    xs = [torch.zeros((1, H), device=cuda) for _ in range(n + 1)]
+    xs[0].copy_(torch.from_numpy(activations((1, H), seed=8)))
+    lgs = [torch.from_numpy(activations((1, E), seed=60 + l)).to(cuda) for l in range(n)]
+    outs = [torch.zeros((1, H), device=cuda) for _ in range(n)]
+    st = pkg.Stack(layers, xs[:n], lgs, outs, x_nexts=xs[1:])
+    st.run()
+    torch.cuda.synchronize()
+    assert pkg.moe_cache.device_error() == 0
+    x = xs[0].clone()
+    for l in range(n):
+        ref = layers[l].decode(x, lgs[l])
+        assert torch.equal(outs[l], ref), l
+        x = x + ref
+        assert torch.equal(xs[l + 1], x), l
