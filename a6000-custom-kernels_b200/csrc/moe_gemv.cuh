@@ -240,7 +240,11 @@ __device__ __forceinline__ void stage_f32_block(const float *xv, uint8_t *slot, 
         stage_q80_block<TYPE, CG>(xv, q, bs, sc, b, lane, K / CE);
 }
 
-// Q8_1 block (36 bytes) as given: copy qs, scale = d, per-16 sums.
+// Q8_1 block (36 bytes) as given: copy qs, scale = d, per-16 sums. For
+// Q4_0 / Q5_0 weights the per-16 sums are not needed: the sum area holds the
+// block's stored s instead (one f32 per block, the same K / 8 bytes), which
+// llama.cpp's vec_dot_q4_0_q8_1 / vec_dot_q5_0_q8_1 use for the weights'
+// offset.
 template <int TYPE>
 __device__ __forceinline__ void stage_q81_block(const uint8_t *yb, int8_t *q, int16_t *bs, float *sc, int b, int lane,
                                                 int NC) {
@@ -253,8 +257,12 @@ __device__ __forceinline__ void stage_q81_block(const uint8_t *yb, int8_t *q, in
     }
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
-    if (lane == 0) bs[b * 2] = static_cast<int16_t>(s);
-    if (lane == 4) bs[b * 2 + 1] = static_cast<int16_t>(s);
+    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q5_0) {
+        if (lane == 0) reinterpret_cast<float *>(bs)[b] = ld_half(blk + 2);
+    } else {
+        if (lane == 0) bs[b * 2] = static_cast<int16_t>(s);
+        if (lane == 4) bs[b * 2 + 1] = static_cast<int16_t>(s);
+    }
     if (lane == 0) sc[b] = ld_half(blk);
 }
 
@@ -266,7 +274,7 @@ __device__ __forceinline__ void stage_q81_block(const uint8_t *yb, int8_t *q, in
 // ---------------------------------------------------------------------------
 
 // Q4_0 / Q5_0 / Q8_0: task = one 32-element block
-template <int TYPE, int NMX, int RL>
+template <int TYPE, int ACT, int NMX, int RL>
 __device__ __forceinline__ void task_legacy(const uint8_t *const (&rows)[RL], int b, const Acts<NMX> &A,
                                             float (&acc)[RL][NMX]) {
     float dw[RL];
@@ -296,8 +304,11 @@ __device__ __forceinline__ void task_legacy(const uint8_t *const (&rows)[RL], in
     for (int m = 0; m < NMX; ++m) {
         if (m >= A.nm) break;
         const int4 a0 = A.q[m][b], a1 = A.q[m][A.NC + b];
+        // Q8_1 with Q4_0 / Q5_0: the block's stored s (see stage_q81_block)
+        constexpr bool S_OFF = ACT == ACT_Q8_1 && TYPE != T_Q8_0;
         const int bsw = *reinterpret_cast<const int *>(A.bs[m] + b * 2);
-        const int asum = bs_lo(bsw) + bs_hi(bsw);
+        const int asum = S_OFF ? 0 : bs_lo(bsw) + bs_hi(bsw);
+        const float s8 = S_OFF ? reinterpret_cast<const float *>(A.bs[m])[b] : 0.f;
         const float d8 = A.sc[m][b];
 #pragma unroll
         for (int r = 0; r < RL; ++r) {
@@ -320,9 +331,16 @@ __device__ __forceinline__ void task_legacy(const uint8_t *const (&rows)[RL], in
                 S = dp4a_us(hi[r][1], a1.y, S);
                 S = dp4a_us(hi[r][2], a1.z, S);
                 S = dp4a_us(hi[r][3], a1.w, S);
-                S -= (TYPE == T_Q4_0 ? 8 : 16) * asum;
+                if constexpr (!S_OFF) S -= (TYPE == T_Q4_0 ? 8 : 16) * asum;
             }
-            acc[r][m] += (dw[r] * d8) * static_cast<float>(S);
+            // Q8_0 / Q8_K activations (CPU semantics): the exact integer sum,
+            // offset taken off, times d_w d_a; Q8_1 activations with Q4_0 /
+            // Q5_0 (llama.cpp's CUDA vec_dot_q{4,5}_0_q8_1):
+            // d_w * (sumi * d_a - offset * s)
+            if constexpr (S_OFF)
+                acc[r][m] += dw[r] * (static_cast<float>(S) * d8 - (TYPE == T_Q4_0 ? 8.f : 16.f) * s8);
+            else
+                acc[r][m] += (dw[r] * d8) * static_cast<float>(S);
         }
     }
 }
@@ -609,7 +627,7 @@ __device__ __forceinline__ void task_q6_K(const uint8_t *const (&rows)[RL], int 
 template <int TYPE, int ACT, int NMX, int RL>
 __device__ __forceinline__ void task_dot(const uint8_t *const (&rows)[RL], int t, const Acts<NMX> &A,
                                          float (&acc)[RL][NMX]) {
-    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q5_0 || TYPE == T_Q8_0) task_legacy<TYPE, NMX, RL>(rows, t, A, acc);
+    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q5_0 || TYPE == T_Q8_0) task_legacy<TYPE, ACT, NMX, RL>(rows, t, A, acc);
     else if constexpr (TYPE == T_Q2_K) task_q2_K<ACT, NMX, RL>(rows, t, A, acc);
     else if constexpr (TYPE == T_Q3_K) task_q3_K<ACT, NMX, RL>(rows, t, A, acc);
     else if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) task_q45_K<TYPE, ACT, NMX, RL>(rows, t, A, acc);

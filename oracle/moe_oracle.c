@@ -682,10 +682,30 @@ static double act_value(int act_type, const uint8_t *a, int64_t i) {
     }
 }
 
+/* Value of a row dot in double. With Q8_1 activations this is what
+ * llama.cpp's CUDA vec_dot_*_q8_1 computes (the functions the reference
+ * kernel dispatches to, kernels/moe-cache.cu:46-47 for Q4_0 / Q5_0): the
+ * integer dots are exact, and for Q4_0 / Q5_0 the weights' offset (8 or 16)
+ * is taken off with the Q8_1 block's stored sum s -- the f16-rounded sum of
+ * the UNquantized inputs that quantize_q8_1 writes -- as
+ * d_w * (d_a * sum(q_w * q_a) - offset * s), not with the quantized inputs.
+ * Every other pairing: sum(w * a) over the dequantized values. */
 static double dot_exact(int type, int act_type, int64_t n, const uint8_t *x, const uint8_t *a) {
     const int bs = orc_blck_size(type), ts = orc_type_size(type);
     double s = 0;
     int q[QK_K]; double sa[QK_K], sb[QK_K];
+    if (act_type == ORC_Q8_1 && (type == ORC_Q4_0 || type == ORC_Q5_0)) {
+        const int off = type == ORC_Q4_0 ? 8 : 16;
+        for (int64_t ib = 0; ib < n / 32; ++ib, x += ts) {
+            block_affine(type, x, q, sa, sb);
+            const uint8_t *ab = a + ib * 36;
+            const double d_a = rdh(ab), s_a = rdh(ab + 2);
+            int64_t sumi = 0;
+            for (int i = 0; i < 32; ++i) sumi += (int64_t)(q[i] + off) * (int8_t)ab[4 + i];
+            s += sa[0] * (d_a * (double)sumi - off * s_a);
+        }
+        return s;
+    }
     for (int64_t ib = 0; ib < n / bs; ++ib, x += ts) {
         block_affine(type, x, q, sa, sb);
         for (int i = 0; i < bs; ++i) {

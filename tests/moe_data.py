@@ -50,6 +50,11 @@ def act_quant_sigma(t, W, K, x, ids):
         (amax / 127): variance w_i^2 (d1_i^2 + dc_i^2) / 12;
       * the f16 block scales of Q8_1 and Q8_0 (relative error uniform in
         +-2^-11): variance (sum over the block of w_i x_i)^2 * 2^-22 / 3.
+    Q4_0 / Q5_0 with Q8_1 activations (llama.cpp's CUDA dot) compute
+    d_w (d_a sum(q_w q_a) - offset s), s the f16 sum of the unquantized x of
+    the block: the Q8_1 side's rounding then meets the unsigned weights
+    u_i = w_i + offset d_w (in both terms above), and s adds the variance
+    (offset d_w)^2 (sum over the block of x_i)^2 2^-22 / 3.
     No test assumes more than this model."""
     import oracle as O
     x = np.asarray(x, dtype=np.float64)
@@ -61,12 +66,25 @@ def act_quant_sigma(t, W, K, x, ids):
         step[name] = (np.repeat(d, blk, axis=1), blk)
     var_el = (step["q8_1"][0] ** 2 + step["cpu"][0] ** 2) / 12.0            # [n_tok][K]
     f16_cpu = O.vec_dot_type(t) == O.Q8_0
+    off = {O.Q4_0: 8, O.Q5_0: 16}.get(t, 0)
+    f16 = (2.0 ** -22) / 3.0
     out = np.zeros(ids.shape + (W.shape[1],))
     for ti in range(n_tok):
         for p in range(ids.shape[1]):
             w = O.dequantize(t, W[ids[ti, p]], K).astype(np.float64)          # [rows][K]
-            v = (w ** 2) @ var_el[ti]
-            wx = (w * x[ti][None, :]).reshape(w.shape[0], K // 32, 32).sum(axis=2)
-            v += (wx ** 2).sum(axis=1) * (2.0 ** -22) / 3.0 * (2 if f16_cpu else 1)
+            rows = w.shape[0]
+            wx = (w * x[ti][None, :]).reshape(rows, K // 32, 32).sum(axis=2)
+            if off:
+                blk = W[ids[ti, p]].reshape(rows, K // 32, -1)
+                dw = blk[:, :, :2].copy().view(np.float16)[..., 0].astype(np.float64)   # [rows][K/32]
+                u = w + off * np.repeat(dw, 32, axis=1)
+                ux = (u * x[ti][None, :]).reshape(rows, K // 32, 32).sum(axis=2)
+                xs = x[ti].reshape(K // 32, 32).sum(axis=1)
+                v = (u ** 2) @ (step["q8_1"][0][ti] ** 2 / 12.0) + (w ** 2) @ (step["cpu"][0][ti] ** 2 / 12.0)
+                v += ((ux ** 2).sum(axis=1) + (wx ** 2).sum(axis=1)) * f16
+                v += ((off * dw) ** 2 * xs[None, :] ** 2).sum(axis=1) * f16
+            else:
+                v = (w ** 2) @ var_el[ti]
+                v += (wx ** 2).sum(axis=1) * f16 * (2 if f16_cpu else 1)
             out[ti, p] = np.sqrt(v)
     return out

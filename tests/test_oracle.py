@@ -23,9 +23,14 @@ def test_generic_dot_close_to_exact(t):
 
 @pytest.mark.parametrize("t", O.WEIGHT_TYPES)
 def test_exact_dot_equals_dequantized_product(t):
+    """Exact mode = sum(w * a) of the dequantized values -- except Q4_0 / Q5_0
+    with Q8_1 activations, where llama.cpp's CUDA dot takes the weights'
+    offset off with the block's stored s (f16 sum of the unquantized x):
+    sum(w * a) + offset * sum over blocks of d_w (sum(a) - s)."""
     K = 256
     w = experts(t, 1, 4, K, seed=7)[0]
     x = activations((K,), seed=8)
+    off = {O.Q4_0: 8, O.Q5_0: 16}.get(t, 0)
     for at in (O.Q8_0, O.Q8_1, O.Q8_K):
         a = O.quantize_act(at, x)
         wd = O.dequantize(t, w, 4 * K).reshape(4, K).astype(np.float64)
@@ -33,6 +38,10 @@ def test_exact_dot_equals_dequantized_product(t):
         for r in range(4):
             e = O.vec_dot(t, at, 1, w[r], a, K)
             ref = float(wd[r] @ ad)
+            if at == O.Q8_1 and off:
+                dw = w[r].reshape(K // 32, -1)[:, :2].copy().view(np.float16)[:, 0].astype(np.float64)
+                s = a.reshape(K // 32, 36)[:, 2:4].copy().view(np.float16)[:, 0].astype(np.float64)
+                ref += off * float((dw * (ad.reshape(K // 32, 32).sum(axis=1) - s)).sum())
             assert abs(e - ref) <= 2e-4 * max(1.0, abs(ref))
 
 
