@@ -78,6 +78,9 @@ constexpr int STACK_MAX_K = 32;
 #define STACK_POLL_NS 100
 #endif
 constexpr int STACK_ROUTE_BUFS = 3;
+#ifndef STACK_COMBINE_W
+#define STACK_COMBINE_W 9        // terms a combining warp polls per round: top-8 + shared in one
+#endif
 
 // One layer's routing, written by the producer warp, read by the consumers.
 struct StackRoute {
@@ -372,20 +375,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             const uint64_t *xin = a.xtag + static_cast<int64_t>(l & 1) * H;
             const bool from_tags = l > 0 && Lr.chained;
             const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
-            // one warp watches the last row of every 32-row block (the rows a
-            // combining warp writes together) with a pause between rounds; the
-            // others wait at the barrier instead of polling L2 too
-            if (l > 0 && warp == 0) {
-                for (;;) {
-                    bool got = true;
-                    for (int r = 32 * lane + 31; r < H + 31; r += 32 * 32)
-                        got &= static_cast<uint32_t>(ld_relaxed_u64(xin + min(r, H - 1)) >> 32) == tag - 1u;
-                    if (__all_sync(0xffffffffu, got)) break;
-                    if (static_cast<uint64_t>(clock64()) - t0 > lim) break;   // the block loads below time out too
-                    __nanosleep(STACK_POLL_NS);
-                }
-            }
-            if (l > 0) consumer_sync();
+            // every warp polls its own blocks of x_l directly (a pause between
+            // rounds), so a block is staged one L2 round trip after its
+            // combining warp wrote it (a watcher warp and a CTA barrier before
+            // the loads cost a second round trip and the barrier per layer)
             // the activation layout is the gate/up type's
             auto stage_x = [&](auto tt) {
                 constexpr int T = decltype(tt)::value;
@@ -400,6 +393,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                                 }
                                 break;
                             }
+                            __nanosleep(2 * STACK_POLL_NS);
                         }
                     }
                     if (from_tags) {
@@ -537,12 +531,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
             const uint64_t t0 = clock64(), lim = timeout_cycles(a.timeout_ns);
             float acc = 0.f;
             bool fail = false;
-            for (int p0 = 0; p0 < np && !fail; p0 += 8) {
-                uint64_t w[8];
+            for (int p0 = 0; p0 < np && !fail; p0 += STACK_COMBINE_W) {
+                uint64_t w[STACK_COMBINE_W];
                 for (;;) {
                     bool got = true;
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
+                    for (int q = 0; q < STACK_COMBINE_W; ++q) {
                         const int p = p0 + q;
                         const uint64_t *yp = p < k ? a.ytag + static_cast<int64_t>(p) * a.ysc : a.ytag_s;
                         w[q] = p < np && ok ? ld_relaxed_u64(yp + r) : tagged(0.f, tag);
@@ -556,7 +550,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) moe_stack_kernel(const __grid
                     __nanosleep(STACK_POLL_NS);
                 }
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
+                for (int q = 0; q < STACK_COMBINE_W; ++q) {
                     const int p = p0 + q;
                     if (p >= np || fail) break;
                     const float v = __uint_as_float(static_cast<uint32_t>(w[q]));
