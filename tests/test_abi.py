@@ -55,3 +55,33 @@ def test_errors_are_status_codes_not_aborts(pkg):
     rc = L.moe_b200_prefill_mul_mat_id(None, None, 1, None, 8, 8, None, None, 0, None, None)
     assert rc == pkg._lib.MOE_ERR_INVALID
     assert L.moe_b200_prefill_workspace_size(None, 1, 8) == 0
+
+
+def test_stack_prepare_rejects_unsupported_type_mixes(pkg):
+    """The stack takes one type for every tensor of every layer, or per-layer
+    types when gate = up and every type is among Q2_K, Q3_K, Q4_K, Q6_K; any
+    other mix is refused with a status code before anything touches the GPU."""
+    from importlib import import_module
+    lm = import_module("a6000-custom-kernels_b200._lib")
+    L = pkg.lib()
+    H, F, E, k = 1024, 512, 16, 4
+
+    def desc(tg, tu, td):
+        d = lm.MoeLayerDesc()
+        for name, t, (rows, K) in (("gate", tg, (F, H)), ("up", tu, (F, H)), ("down", td, (H, F))):
+            m = getattr(d, name)
+            m.data, m.type = 0x1000, t
+            m.ne[0], m.ne[1], m.ne[2], m.ne[3] = K, rows, E, 1
+        d.shared_type, d.H, d.F, d.n_experts, d.k = -1, H, F, E, k
+        return d
+
+    Q4_0, Q2_K, Q3_K = 2, 10, 11
+    dummy = (ctypes.c_void_p * 2)(0x1000, 0x1000)
+    for pair in ((desc(Q2_K, Q2_K, Q2_K), desc(Q4_0, Q4_0, Q4_0)),     # a legacy type in a mixed stack
+                 (desc(Q2_K, Q2_K, Q3_K), desc(Q3_K, Q2_K, Q3_K))):    # gate and up of different types
+        arr = (lm.MoeLayerDesc * 2)(*pair)
+        need = L.moe_b200_stack_workspace_size(ctypes.byref(arr[0]), 2)
+        ws = ctypes.create_string_buffer(need)
+        rc = L.moe_b200_stack_prepare(arr, 2, dummy, dummy, dummy, None, ws, need, None)
+        assert rc == lm.MOE_ERR_UNSUPPORTED, rc
+        assert b"Q2_K, Q3_K, Q4_K, Q6_K" in L.moe_b200_last_error()
