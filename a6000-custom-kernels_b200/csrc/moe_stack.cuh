@@ -7,20 +7,22 @@
 // while the consumers still work on layer l. When a layer's input arrives,
 // its weights are already in shared memory (the ring holds about one layer of
 // a CTA's share), and what is left on the critical path per layer is the
-// arithmetic and two exchanges between CTAs: the h rows of each expert and
-// the 64-row output blocks. One launch for many layers also keeps the code
-// warm in the instruction cache and removes the launch gaps.
+// arithmetic and the exchanges between CTAs. One launch for many layers also
+// keeps the code warm in the instruction cache and removes the launch gaps.
 //
 // Per layer l (one token): the same static plan as moe_layer2_kernel at batch
 // 1 (unit u = pick u, the shared expert = unit k, CTA groups fixed), the same
 // picks and weights (route_select / route_weights: descending logit, ties to
-// the lower id), tiles, h exchange by (value, tag) pairs (tag = launch epoch
-// + 1 + l), down rows and combine by the CTA that completes a 64-row block.
-// The combining CTA writes out_l (and x_next_l = x_l + out_l when asked) and
-// counts the block done; every CTA waits until all of layer l's blocks are
-// done before it reads layer l + 1's input -- the layers may form a chain.
+// the lower id) and tiles. Three exchanges, all by 64-bit (value, tag) words
+// (tag = launch epoch + 1 + l; relaxed stores and loads, a reader that sees
+// the tag sees the value): the h rows of each unit among its CTAs; the down
+// rows of every unit (ytag), summed per 32-row block in pick order by the
+// warp that owns the block, which writes out_l (and x_next_l = x_l + out_l
+// when asked) and x_l + out_l tagged into xtag; and xtag, whose blocks every
+// warp of every CTA polls before it stages layer l + 1's input -- so the
+// layers may form a chain.
 //
-// Ring: tile i of layer l has ring index l * (tiles per layer) + i and is
+// Ring: tile i of layer l has ring index (tiles of layers 0..l-1) + i and is
 // consumed by warp (ring index) % nw. Routing: the producer writes layer j's
 // picks, weights and expert sources into buffer j % 3 and arrives on
 // rt_full[j % 3]; the consumers release the buffer (rt_empty) when layer j is
