@@ -161,7 +161,10 @@ class Stack:
     (moe_b200_stack_prepare / moe_b200_stack_run). Layer l reads xs[l] and
     logits[l] (device f32 [1, H] / [1, E]), writes outs[l] and, with
     x_nexts, x_nexts[l] = xs[l] + outs[l] (a residual chain when xs[l + 1]
-    is x_nexts[l]). run() may be repeated; every tensor must stay alive."""
+    is x_nexts[l]). The layers share one shape; their types are either one
+    type for every tensor or, per layer, gate = up with the gate/up and down
+    types among Q2_K, Q3_K, Q4_K, Q6_K (the mixed-type kernel). run() may be
+    repeated; every tensor must stay alive."""
 
     def __init__(self, layers, xs, logits, outs, x_nexts=None, stream=None):
         n = len(layers)
